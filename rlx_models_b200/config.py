@@ -1,0 +1,237 @@
+"""HF ``config.json`` -> typed model configs.
+
+Covers the keys the reference's config layer reads (rlx-models-core
+src/config.rs:181 `legacy_rope_keys`, :231 `from_hf_json`; rlx-qwen3
+src/config.rs:20-136; rlx-gpt-oss gpt_oss_ops.rs; rlx-flux1 src/config.rs:24-150):
+transformers-5 ``rope_parameters`` are folded back into the legacy
+``rope_theta`` / ``rope_scaling`` keys, a nested ``text_config`` (VLM wrappers)
+is merged into the top level, and family defaults fill missing keys.
+"""
+from __future__ import annotations
+
+import dataclasses
+import json
+import os
+from dataclasses import dataclass, field
+from typing import Any
+
+
+def legacy_rope_keys(cfg: dict) -> dict:
+    """Map transformers-5 ``rope_parameters`` onto ``rope_theta`` / ``rope_scaling``."""
+    cfg = dict(cfg)
+    rp = cfg.get("rope_parameters")
+    if isinstance(rp, dict):
+        if "rope_theta" in rp and "rope_theta" not in cfg:
+            cfg["rope_theta"] = rp["rope_theta"]
+        kind = rp.get("rope_type", rp.get("type", "default"))
+        if kind not in (None, "default") and not cfg.get("rope_scaling"):
+            cfg["rope_scaling"] = {k: v for k, v in rp.items() if k != "rope_theta"}
+    return cfg
+
+
+def merge_text_config(cfg: dict) -> dict:
+    tc = cfg.get("text_config")
+    if isinstance(tc, dict):
+        merged = dict(cfg)
+        for k, v in tc.items():
+            merged.setdefault(k, v) if k in ("model_type",) else merged.__setitem__(k, v)
+        return merged
+    return cfg
+
+
+@dataclass
+class DecoderConfig:
+    """Normalised decoder description shared by the dense and MoE families."""
+    model_type: str = "qwen3"
+    vocab_size: int = 151936
+    hidden_size: int = 1024
+    intermediate_size: int = 3072
+    num_hidden_layers: int = 28
+    num_attention_heads: int = 16
+    num_key_value_heads: int = 8
+    head_dim: int = 128
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1e6
+    rope_scaling: dict | None = None
+    max_position_embeddings: int = 40960
+    tie_word_embeddings: bool = False
+    qk_norm: bool = True
+    attention_bias: bool = False
+    mlp_bias: bool = False
+    # sliding window: per-layer list of "full_attention" / "sliding_attention"
+    sliding_window: int = 0
+    layer_types: list[str] | None = None
+    # learned attention sinks (gpt-oss)
+    attn_sinks: bool = False
+    # MoE
+    num_experts: int = 0
+    num_experts_per_tok: int = 0
+    moe_intermediate_size: int = 0
+    router_bias: bool = False
+    expert_bias: bool = False
+    swiglu_limit: float = 0.0   # clamped SwiGLU (gpt-oss: 7.0)
+    swiglu_alpha: float = 1.702
+    norm_topk_prob: bool = True
+    softmax_after_topk: bool = False  # gpt-oss: top-k on logits, softmax over the k
+    expert_quant: str = "bf16"  # "bf16" | "mxfp4"
+    torch_dtype: str = "bfloat16"
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def q_size(self) -> int:
+        return self.num_attention_heads * self.head_dim
+
+    @property
+    def kv_size(self) -> int:
+        return self.num_key_value_heads * self.head_dim
+
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
+    def layer_window(self, i: int) -> int:
+        if self.layer_types is not None and self.sliding_window:
+            return self.sliding_window if self.layer_types[i] == "sliding_attention" else 0
+        return 0
+
+    def num_params(self) -> int:
+        H, I, V, L = self.hidden_size, self.intermediate_size, self.vocab_size, self.num_hidden_layers
+        attn = H * (self.q_size + 2 * self.kv_size) + self.q_size * H
+        if self.is_moe:
+            mlp = self.num_experts * 3 * H * self.moe_intermediate_size + H * self.num_experts
+        else:
+            mlp = 3 * H * I
+        emb = V * H * (1 if self.tie_word_embeddings else 2)
+        return L * (attn + mlp + 2 * H) + emb + H
+
+    @classmethod
+    def from_hf_dict(cls, raw: dict) -> "DecoderConfig":
+        d = legacy_rope_keys(merge_text_config(raw))
+        mt = d.get("model_type", "qwen3")
+        kw: dict[str, Any] = {}
+        fields = {f.name for f in dataclasses.fields(cls)}
+        for k in fields:
+            if k in d and k != "extra":
+                kw[k] = d[k]
+        kw["model_type"] = mt
+        if "head_dim" not in d or d.get("head_dim") is None:
+            kw["head_dim"] = d["hidden_size"] // d["num_attention_heads"]
+        if "num_key_value_heads" not in d:
+            kw["num_key_value_heads"] = d["num_attention_heads"]
+        if mt in ("qwen3", "qwen3_moe"):
+            kw.setdefault("qk_norm", True)
+            if mt == "qwen3_moe":
+                kw["num_experts"] = d.get("num_experts", 0)
+                kw["moe_intermediate_size"] = d.get("moe_intermediate_size", 0)
+        elif mt in ("llama", "mistral", "qwen2"):
+            kw["qk_norm"] = False
+            kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-5))
+            if mt == "qwen2":
+                kw["attention_bias"] = True
+        elif mt == "gpt_oss":
+            kw["qk_norm"] = False
+            kw["attention_bias"] = True
+            kw["attn_sinks"] = True
+            kw["num_experts"] = d.get("num_local_experts", d.get("num_experts", 128))
+            kw["num_experts_per_tok"] = d.get("num_experts_per_tok", d.get("experts_per_token", 4))
+            kw["moe_intermediate_size"] = d.get("intermediate_size", 2880)
+            kw["router_bias"] = True
+            kw["expert_bias"] = True
+            kw["swiglu_limit"] = d.get("swiglu_limit", 7.0)
+            kw["softmax_after_topk"] = True
+            kw["sliding_window"] = d.get("sliding_window", 128)
+            if "layer_types" not in d:
+                kw["layer_types"] = ["sliding_attention" if i % 2 == 0 else "full_attention"
+                                     for i in range(d["num_hidden_layers"])]
+            q = d.get("quantization_config") or {}
+            kw["expert_quant"] = "mxfp4" if q.get("quant_method") == "mxfp4" else d.get("expert_quant", "bf16")
+        kw["extra"] = {k: v for k, v in d.items() if k not in fields}
+        return cls(**kw)
+
+    @classmethod
+    def from_file(cls, path: str) -> "DecoderConfig":
+        if os.path.isdir(path):
+            path = os.path.join(path, "config.json")
+        with open(path) as f:
+            return cls.from_hf_dict(json.load(f))
+
+    def to_hf_dict(self) -> dict:
+        d = {k: v for k, v in dataclasses.asdict(self).items() if k != "extra"}
+        d.update(self.extra)
+        if self.model_type == "gpt_oss":
+            d["num_local_experts"] = self.num_experts
+            d["intermediate_size"] = self.moe_intermediate_size
+        return d
+
+    def save(self, path: str):
+        os.makedirs(path, exist_ok=True)
+        with open(os.path.join(path, "config.json"), "w") as f:
+            json.dump(self.to_hf_dict(), f, indent=2)
+
+
+# ---------------------------------------------------------------------------
+# Named shapes used by the benchmarks and tests (random-init weights)
+# ---------------------------------------------------------------------------
+
+def qwen3_0_6b() -> DecoderConfig:
+    return DecoderConfig(model_type="qwen3", vocab_size=151936, hidden_size=1024, intermediate_size=3072,
+                         num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8, head_dim=128,
+                         rms_norm_eps=1e-6, rope_theta=1e6, tie_word_embeddings=True)
+
+
+def qwen3_1_7b() -> DecoderConfig:
+    return DecoderConfig(model_type="qwen3", vocab_size=151936, hidden_size=2048, intermediate_size=6144,
+                         num_hidden_layers=28, num_attention_heads=16, num_key_value_heads=8, head_dim=128,
+                         rms_norm_eps=1e-6, rope_theta=1e6, tie_word_embeddings=True)
+
+
+def qwen3_8b() -> DecoderConfig:
+    return DecoderConfig(model_type="qwen3", vocab_size=151936, hidden_size=4096, intermediate_size=12288,
+                         num_hidden_layers=36, num_attention_heads=32, num_key_value_heads=8, head_dim=128,
+                         rms_norm_eps=1e-6, rope_theta=1e6, tie_word_embeddings=False)
+
+
+def gpt_oss_120b() -> DecoderConfig:
+    L = 36
+    return DecoderConfig(model_type="gpt_oss", vocab_size=201088, hidden_size=2880, intermediate_size=2880,
+                         num_hidden_layers=L, num_attention_heads=64, num_key_value_heads=8, head_dim=64,
+                         rms_norm_eps=1e-5, rope_theta=150000.0,
+                         rope_scaling={"rope_type": "yarn", "factor": 32.0, "beta_fast": 32.0, "beta_slow": 1.0,
+                                       "original_max_position_embeddings": 4096, "truncate": False},
+                         max_position_embeddings=131072, tie_word_embeddings=False, qk_norm=False,
+                         attention_bias=True, sliding_window=128,
+                         layer_types=["sliding_attention" if i % 2 == 0 else "full_attention" for i in range(L)],
+                         attn_sinks=True, num_experts=128, num_experts_per_tok=4, moe_intermediate_size=2880,
+                         router_bias=True, expert_bias=True, swiglu_limit=7.0, softmax_after_topk=True,
+                         expert_quant="mxfp4")
+
+
+PRESETS = {
+    "qwen3-0.6b": qwen3_0_6b,
+    "qwen3-1.7b": qwen3_1_7b,
+    "qwen3-8b": qwen3_8b,
+    "gpt-oss-120b": gpt_oss_120b,
+}
+
+
+def preset(name: str) -> DecoderConfig:
+    key = name.lower().replace("_", "-")
+    for k, fn in PRESETS.items():
+        if key.endswith(k):
+            return fn()
+    raise KeyError(f"unknown preset {name!r}; known: {sorted(PRESETS)}")
+
+
+def tiny(model_type: str = "qwen3", **over) -> DecoderConfig:
+    """A small config with the same structure, for tests."""
+    base = dict(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                num_attention_heads=4, num_key_value_heads=2, head_dim=64, rms_norm_eps=1e-6, rope_theta=1e6)
+    if model_type == "gpt_oss":
+        cfg = gpt_oss_120b()
+        base.update(num_experts=8, num_experts_per_tok=2, moe_intermediate_size=256, intermediate_size=256,
+                    num_hidden_layers=2, sliding_window=16, layer_types=["sliding_attention", "full_attention"],
+                    rope_scaling=dict(cfg.rope_scaling), expert_quant="mxfp4")
+        base.update(over)
+        return dataclasses.replace(cfg, **base)
+    base.update(over)
+    return DecoderConfig(model_type=model_type, **base)

@@ -1,0 +1,599 @@
+// Paged attention for sm_100a ("K9" prefill, "K10" decode).
+//
+// KV cache layout: [num_blocks, Hkv, 16, D] bf16 (block size 16). One page of
+// one kv head is a contiguous [16, D] tile, which a TMA 2-D map over the cache
+// viewed as [num_blocks * Hkv * 16, D] fetches as D/64 boxes of [16, 64] with
+// 128-byte swizzle (conflict-free ldmatrix reads).
+//
+// GQA packing: all G = Hq / Hkv query heads that share a kv head are rows of
+// the same MMA tile, so each K/V page is read from HBM once per kv head.
+// Supports causal prefill over cached pages (chunked prefill), decode with
+// split-KV ("flash decoding"), sliding windows and learned per-head sink
+// logits (gpt-oss: an extra softmax column that is dropped after softmax).
+//
+// Reference behaviour: fused SDPA with causal / sliding-window / sink masks
+// (rlx-models-core src/standard_decoder.rs:11946-12079
+// `build_gpt_oss_attention_with_sinks`; rlx-qwen3 src/builder.rs:450 ragged
+// decode). The reference re-uploads host KV per step; here the KV is always
+// device resident in pages.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <stdexcept>
+
+#include "../common/b200.cuh"
+#include "../common/launch.h"
+#include "../common/tma_host.h"
+
+namespace b200 {
+namespace attn {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kNegInf = -INFINITY;
+
+// ---------------------------------------------------------------------------
+// Decode: grid (B * Hkv, splits), 4 compute warps + 1 TMA producer warp.
+// Warp w consumes pages w, w+4, ... of this split from an NST-deep ring.
+// ---------------------------------------------------------------------------
+template <int D, int NST>
+struct DecCfg {
+  static constexpr int PAGE_BYTES = 16 * D * 2;
+  static constexpr int STAGE_BYTES = 2 * PAGE_BYTES;  // K page + V page
+  static constexpr int MERGE_BYTES = 4 * 16 * (D + 2) * 4;
+  static constexpr int RING_BYTES = NST * STAGE_BYTES;
+  static constexpr int SMEM = 1024 + (RING_BYTES > MERGE_BYTES ? RING_BYTES : MERGE_BYTES) + 2 * NST * 8 + 64;
+};
+
+template <int D, int NST>
+__global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                          const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
+  using Cf = DecCfg<D, NST>;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  const int ring_or_merge = Cf::RING_BYTES > Cf::MERGE_BYTES ? Cf::RING_BYTES : Cf::MERGE_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring_or_merge);
+  uint64_t* empty = full + NST;
+
+  const int G = a.Hq / a.Hkv;
+  const int bh = blockIdx.x;
+  const int b = bh / a.Hkv;
+  const int hkv = bh % a.Hkv;
+  const int split = blockIdx.y;
+  const int nsplit = gridDim.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int ctx = a.ctx_lens[b];
+  int first_tok = 0;
+  if (a.window > 0) first_tok = max(0, ctx - a.window);
+  const int first_page = first_tok >> 4;
+  const int last_page = (ctx + 15) >> 4;  // exclusive
+  const int npages = max(0, last_page - first_page);
+  const int pps = (npages + nsplit - 1) / nsplit;
+  const int p0 = first_page + split * pps;
+  const int p1 = min(last_page, p0 + pps);
+  const int my_pages = max(0, p1 - p0);
+  const int32_t* btab = a.block_tables + (int64_t)b * a.max_blocks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+
+  const float scale_log2 = a.scale * kLog2e;
+  float m_r[2] = {kNegInf, kNegInf}, l_r[2] = {0.f, 0.f};
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      for (int j = 0; j < my_pages; ++j) {
+        if (!mbar_wait(&empty[s], ph ^ 1, a.status, kErrTimeoutEmpty)) break;
+        const int blk = btab[p0 + j];
+        const int row = (blk * a.Hkv + hkv) * 16;
+        uint8_t* st = smem + s * Cf::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[s], Cf::STAGE_BYTES);
+#pragma unroll
+        for (int bx = 0; bx < D / 64; ++bx) {
+          tma_load_2d(st + bx * 2048, &tmK, &full[s], bx * 64, row);
+          tma_load_2d(st + Cf::PAGE_BYTES + bx * 2048, &tmV, &full[s], bx * 64, row);
+        }
+        if (++s == NST) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+  } else {
+    // Q fragments: rows = heads of this kv group (row r < G valid), k = dims.
+    const int g = lane >> 2, t4 = lane & 3;
+    uint32_t qa[D / 16][4];
+    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) + ((int64_t)b * a.Hq + hkv * G) * D;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int r = g + ((h & 1) ? 8 : 0);
+        const int c = ks * 16 + 2 * t4 + ((h & 2) ? 8 : 0);
+        qa[ks][h] = (r < G) ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)r * D + c) : 0u;
+      }
+    }
+    int s = warp % NST;
+    uint32_t ph = 0;
+    // pages j = warp, warp+4, ...; stage of page j is j % NST, phase (j / NST) & 1
+    for (int j = warp; j < my_pages; j += 4) {
+      s = j % NST;
+      ph = (j / NST) & 1;
+      if (!mbar_wait(&full[s], ph, a.status, kErrTimeoutFull)) break;
+      const uint32_t kb = smem_u32(smem + s * Cf::STAGE_BYTES);
+      const uint32_t vb = kb + Cf::PAGE_BYTES;
+      float sc[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      const int mi = lane >> 3, rr = lane & 7;
+#pragma unroll
+      for (int ks = 0; ks < D / 16; ++ks) {
+        const int tok = (mi >> 1) * 8 + rr;
+        const int d0 = ks * 16 + (mi & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(kb + sw128_off(tok, d0, 16), b0, b1, b2, b3);
+        mma_bf16_16816(sc[0], qa[ks], b0, b1);
+        mma_bf16_16816(sc[1], qa[ks], b2, b3);
+      }
+      // mask + online softmax (rows g and g+8)
+      const int base_tok = (p0 + j) * 16;
+      float mx[2] = {kNegInf, kNegInf};
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const int tk = base_tok + nt * 8 + 2 * t4 + (h & 1);
+          const bool ok = tk < ctx && tk >= first_tok;
+          sc[nt][h] = ok ? sc[nt][h] * scale_log2 : kNegInf;
+          mx[h >> 1] = fmaxf(mx[h >> 1], sc[nt][h]);
+        }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      }
+      float corr[2];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const float mn = fmaxf(m_r[r], mx[r]);
+        corr[r] = (mn == kNegInf) ? 1.f : exp2f(m_r[r] - mn);
+        m_r[r] = mn;
+        l_r[r] *= corr[r];
+      }
+      uint32_t pa[4];
+      {
+        float p[2][4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float mm = m_r[h >> 1];
+            p[nt][h] = (mm == kNegInf) ? 0.f : exp2f(sc[nt][h] - mm);
+            l_r[h >> 1] += p[nt][h];
+          }
+        pa[0] = pack_bf16x2(p[0][0], p[0][1]);
+        pa[1] = pack_bf16x2(p[0][2], p[0][3]);
+        pa[2] = pack_bf16x2(p[1][0], p[1][1]);
+        pa[3] = pack_bf16x2(p[1][2], p[1][3]);
+      }
+#pragma unroll
+      for (int dn = 0; dn < D / 8; ++dn) {
+        o[dn][0] *= corr[0];
+        o[dn][1] *= corr[0];
+        o[dn][2] *= corr[1];
+        o[dn][3] *= corr[1];
+      }
+#pragma unroll
+      for (int dp = 0; dp < D / 16; ++dp) {
+        const int tok = (mi & 1) * 8 + rr;
+        const int d0 = (dp * 2 + (mi >> 1)) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(vb + sw128_off(tok, d0, 16), b0, b1, b2, b3);
+        mma_bf16_16816(o[dp * 2], pa, b0, b1);
+        mma_bf16_16816(o[dp * 2 + 1], pa, b2, b3);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    // finish row sums inside the quad
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      l_r[r] += __shfl_xor_sync(0xffffffffu, l_r[r], 1);
+      l_r[r] += __shfl_xor_sync(0xffffffffu, l_r[r], 2);
+    }
+  }
+  __syncthreads();  // ring no longer needed: reuse it for the cross-warp merge
+
+  float* sm_o = reinterpret_cast<float*>(smem);       // [4][16][D]
+  float* sm_ml = sm_o + 4 * 16 * D;                   // [4][16][2]
+  if (warp < 4) {
+    const int g = lane >> 2, t4 = lane & 3;
+#pragma unroll
+    for (int dn = 0; dn < D / 8; ++dn) {
+      const int c = dn * 8 + 2 * t4;
+      sm_o[(warp * 16 + g) * D + c] = o[dn][0];
+      sm_o[(warp * 16 + g) * D + c + 1] = o[dn][1];
+      sm_o[(warp * 16 + g + 8) * D + c] = o[dn][2];
+      sm_o[(warp * 16 + g + 8) * D + c + 1] = o[dn][3];
+    }
+    if (t4 == 0) {
+      sm_ml[(warp * 16 + g) * 2] = m_r[0];
+      sm_ml[(warp * 16 + g) * 2 + 1] = l_r[0];
+      sm_ml[(warp * 16 + g + 8) * 2] = m_r[1];
+      sm_ml[(warp * 16 + g + 8) * 2 + 1] = l_r[1];
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int r = idx / D, d = idx % D;
+    float M = kNegInf;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_ml[(w * 16 + r) * 2]);
+    float L = 0.f, O = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = sm_ml[(w * 16 + r) * 2];
+      const float f = (mw == kNegInf) ? 0.f : exp2f(mw - M);
+      L += sm_ml[(w * 16 + r) * 2 + 1] * f;
+      O += sm_o[(w * 16 + r) * D + d] * f;
+    }
+    const int head = hkv * G + r;
+    if (nsplit == 1) {
+      if (a.sinks != nullptr) {
+        const float sk = a.sinks[head] * kLog2e;
+        const float Mx = fmaxf(M, sk);
+        const float f = (M == kNegInf) ? 0.f : exp2f(M - Mx);
+        L = L * f + exp2f(sk - Mx);
+        O *= f;
+      }
+      const float inv = L > 0.f ? 1.f / L : 0.f;
+      reinterpret_cast<__nv_bfloat16*>(a.out)[((int64_t)b * a.Hq + head) * D + d] = __float2bfloat16(O * inv);
+    } else {
+      // workspace: [B, Hq, splits, D] partial O  followed by [B, Hq, splits, 2] (M, L)
+      const int64_t slot = ((int64_t)b * a.Hq + head) * nsplit + split;
+      a.ws[slot * D + d] = O;
+      if (d == 0) {
+        float* ml = a.ws + (int64_t)a.B * a.Hq * nsplit * D;
+        ml[slot * 2] = M;
+        ml[slot * 2 + 1] = L;
+      }
+    }
+  }
+}
+
+template <int D>
+__global__ void decode_merge_kernel(AttnArgs a, int nsplit) {
+  const int bh = blockIdx.x;  // b * Hq + head
+  const int head = bh % a.Hq;
+  const float* ml = a.ws + (int64_t)a.B * a.Hq * nsplit * D;
+  float M = kNegInf;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[((int64_t)bh * nsplit + s) * 2]);
+  float sk = kNegInf;
+  if (a.sinks != nullptr) {
+    sk = a.sinks[head] * kLog2e;
+  }
+  const float Mx = fmaxf(M, sk);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float L = (sk == kNegInf) ? 0.f : exp2f(sk - Mx), O = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float ms = ml[((int64_t)bh * nsplit + s) * 2];
+      const float f = (ms == kNegInf) ? 0.f : exp2f(ms - Mx);
+      L += ml[((int64_t)bh * nsplit + s) * 2 + 1] * f;
+      O += a.ws[((int64_t)bh * nsplit + s) * D + d] * f;
+    }
+    reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)bh * D + d] = __float2bfloat16(L > 0.f ? O / L : 0.f);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Prefill (causal, over cached pages): grid (B * q_tiles, Hkv), 8 compute
+// warps (16 MMA rows each; row = token * G + head) + 1 TMA producer warp.
+// K/V tiles of 64 keys (4 pages) in an NST-deep ring.
+// ---------------------------------------------------------------------------
+template <int D, int NST>
+struct PreCfg {
+  static constexpr int TILE_KEYS = 64;
+  static constexpr int HALF = TILE_KEYS * D * 2;  // K (or V) bytes per stage
+  static constexpr int STAGE_BYTES = 2 * HALF;
+  static constexpr int SMEM = 1024 + NST * STAGE_BYTES + 2 * NST * 8 + 64;
+};
+
+template <int D, int NST>
+__global__ void __launch_bounds__(288) prefill_attn_kernel(const __grid_constant__ CUtensorMap tmK,
+                                                           const __grid_constant__ CUtensorMap tmV, AttnArgs a,
+                                                           int q_tiles, int rows_tok) {
+  using Cf = PreCfg<D, NST>;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * Cf::STAGE_BYTES);
+  uint64_t* empty = full + NST;
+
+  const int G = a.Hq / a.Hkv;
+  const int b = blockIdx.x / q_tiles;
+  const int qt = blockIdx.x % q_tiles;
+  const int hkv = blockIdx.y;
+  const int q0 = a.cu_q[b];
+  const int q_len = a.cu_q[b + 1] - q0;
+  const int tok0 = qt * rows_tok;  // first query (within this sequence) of the tile
+  if (tok0 >= q_len) return;
+  const int ntok = min(rows_tok, q_len - tok0);
+  const int ctx = a.ctx_lens[b];
+  const int pos_base = ctx - q_len;  // position of query 0
+  const int pos_lo = pos_base + tok0, pos_hi = pos_base + tok0 + ntok - 1;
+  int k_begin = 0;
+  if (a.window > 0) k_begin = max(0, pos_lo - a.window + 1);
+  k_begin &= ~(Cf::TILE_KEYS - 1);
+  const int k_end = pos_hi + 1;
+  const int ntiles = (k_end - k_begin + Cf::TILE_KEYS - 1) / Cf::TILE_KEYS;
+  const int32_t* btab = a.block_tables + (int64_t)b * a.max_blocks;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 8);
+    }
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+
+  if (warp == 8) {
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      const int max_page = (ctx + 15) >> 4;
+      for (int it = 0; it < ntiles; ++it) {
+        if (!mbar_wait(&empty[s], ph ^ 1, a.status, kErrTimeoutEmpty)) break;
+        uint8_t* st = smem + s * Cf::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[s], Cf::STAGE_BYTES);
+        const int page0 = (k_begin >> 4) + it * 4;
+        for (int pg = 0; pg < 4; ++pg) {
+          const int page = page0 + pg;
+          // pages beyond the context reuse a valid page; their keys are masked
+          const int blk = btab[min(page, max_page - 1)];
+          const int row = (blk * a.Hkv + hkv) * 16;
+#pragma unroll
+          for (int bx = 0; bx < D / 64; ++bx) {
+            // box bx holds dims [64 bx, 64 bx + 64) of all 64 keys: [64 rows][128 B]
+            tma_load_2d(st + bx * (Cf::TILE_KEYS * 128) + pg * 16 * 128, &tmK, &full[s], bx * 64, row);
+            tma_load_2d(st + Cf::HALF + bx * (Cf::TILE_KEYS * 128) + pg * 16 * 128, &tmV, &full[s], bx * 64, row);
+          }
+        }
+        if (++s == NST) {
+          s = 0;
+          ph ^= 1;
+        }
+      }
+    }
+    return;
+  }
+
+  const int g = lane >> 2, t4 = lane & 3;
+  const float scale_log2 = a.scale * kLog2e;
+  // rows of this warp: warp*16 + {g, g+8}; row -> (token, head)
+  int r_tok[2], r_head[2], r_pos[2];
+  bool r_ok[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = warp * 16 + g + r * 8;
+    r_tok[r] = row / G;
+    r_head[r] = row % G;
+    r_ok[r] = r_tok[r] < ntok;
+    r_pos[r] = pos_base + tok0 + r_tok[r];
+  }
+  uint32_t qa[D / 16][4];
+  {
+    const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q);
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks)
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int r = h & 1;
+        const int c = ks * 16 + 2 * t4 + ((h & 2) ? 8 : 0);
+        qa[ks][h] = r_ok[r] ? *reinterpret_cast<const uint32_t*>(
+                                  qb + ((int64_t)(q0 + tok0 + r_tok[r]) * a.Hq + hkv * G + r_head[r]) * D + c)
+                            : 0u;
+      }
+  }
+  float m_r[2] = {kNegInf, kNegInf}, l_r[2] = {0.f, 0.f};
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+  const int mi = lane >> 3, rr = lane & 7;
+  int s = 0;
+  uint32_t ph = 0;
+  for (int it = 0; it < ntiles; ++it) {
+    if (!mbar_wait(&full[s], ph, a.status, kErrTimeoutFull)) break;
+    const uint32_t kb = smem_u32(smem + s * Cf::STAGE_BYTES);
+    const uint32_t vb = kb + Cf::HALF;
+    const int key0 = k_begin + it * Cf::TILE_KEYS;
+    float sc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        const int tok = np * 16 + (mi >> 1) * 8 + rr;
+        const int d0 = ks * 16 + (mi & 1) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(kb + sw128_off(tok, d0, Cf::TILE_KEYS), b0, b1, b2, b3);
+        mma_bf16_16816(sc[np * 2], qa[ks], b0, b1);
+        mma_bf16_16816(sc[np * 2 + 1], qa[ks], b2, b3);
+      }
+    }
+    float mx[2] = {kNegInf, kNegInf};
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int r = h >> 1;
+        const int kp = key0 + nt * 8 + 2 * t4 + (h & 1);
+        const bool ok = r_ok[r] && kp <= r_pos[r] && kp < ctx && (a.window <= 0 || kp > r_pos[r] - a.window);
+        sc[nt][h] = ok ? sc[nt][h] * scale_log2 : kNegInf;
+        mx[r] = fmaxf(mx[r], sc[nt][h]);
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+    }
+    float corr[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const float mn = fmaxf(m_r[r], mx[r]);
+      corr[r] = (mn == kNegInf) ? 1.f : exp2f(m_r[r] - mn);
+      m_r[r] = mn;
+      l_r[r] *= corr[r];
+    }
+#pragma unroll
+    for (int dn = 0; dn < D / 8; ++dn) {
+      o[dn][0] *= corr[0];
+      o[dn][1] *= corr[0];
+      o[dn][2] *= corr[1];
+      o[dn][3] *= corr[1];
+    }
+#pragma unroll
+    for (int kc = 0; kc < 4; ++kc) {  // 16 keys per P fragment
+      uint32_t pa[4];
+      float p[2][4];
+#pragma unroll
+      for (int q = 0; q < 2; ++q)
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float mm = m_r[h >> 1];
+          p[q][h] = (mm == kNegInf) ? 0.f : exp2f(sc[kc * 2 + q][h] - mm);
+          l_r[h >> 1] += p[q][h];
+        }
+      pa[0] = pack_bf16x2(p[0][0], p[0][1]);
+      pa[1] = pack_bf16x2(p[0][2], p[0][3]);
+      pa[2] = pack_bf16x2(p[1][0], p[1][1]);
+      pa[3] = pack_bf16x2(p[1][2], p[1][3]);
+#pragma unroll
+      for (int dp = 0; dp < D / 16; ++dp) {
+        const int tok = kc * 16 + (mi & 1) * 8 + rr;
+        const int d0 = (dp * 2 + (mi >> 1)) * 8;
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(vb + sw128_off(tok, d0, Cf::TILE_KEYS), b0, b1, b2, b3);
+        mma_bf16_16816(o[dp * 2], pa, b0, b1);
+        mma_bf16_16816(o[dp * 2 + 1], pa, b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if (++s == NST) {
+      s = 0;
+      ph ^= 1;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_r[r] += __shfl_xor_sync(0xffffffffu, l_r[r], 1);
+    l_r[r] += __shfl_xor_sync(0xffffffffu, l_r[r], 2);
+  }
+  __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(a.out);
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    if (!r_ok[r]) continue;
+    const int head = hkv * G + r_head[r];
+    float L = l_r[r], M = m_r[r], f = 1.f;
+    if (a.sinks != nullptr) {
+      const float sk = a.sinks[head] * kLog2e;
+      const float Mx = fmaxf(M, sk);
+      f = (M == kNegInf) ? 0.f : exp2f(M - Mx);
+      L = L * f + exp2f(sk - Mx);
+    }
+    const float inv = L > 0.f ? f / L : 0.f;
+    __nv_bfloat16* dst = ob + ((int64_t)(q0 + tok0 + r_tok[r]) * a.Hq + head) * D;
+#pragma unroll
+    for (int dn = 0; dn < D / 8; ++dn) {
+      const int c = dn * 8 + 2 * t4;
+      *reinterpret_cast<uint32_t*>(dst + c) = pack_bf16x2(o[dn][r * 2] * inv, o[dn][r * 2 + 1] * inv);
+    }
+  }
+}
+
+template <typename K>
+static void set_smem(K kern, int bytes, int device) {
+  (void)device;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+}  // namespace attn
+
+void decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
+  using namespace attn;
+  if (a.B == 0) return;
+  const int G = a.Hq / a.Hkv;
+  if (G > 16 || a.Hq % a.Hkv != 0) throw std::runtime_error("b200.decode_attention: G must divide and be <= 16");
+  if (a.D != 128 && a.D != 64) throw std::runtime_error("b200.decode_attention: D must be 64 or 128");
+  const int64_t rows = a.num_blocks * a.Hkv * 16;
+  CUtensorMap tk = make_tmap_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
+  CUtensorMap tv = make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
+  int splits = a.splits;
+  const int sms = num_sms(a.device);
+  if (splits <= 0) {
+    const int ctas = a.B * a.Hkv;
+    splits = std::max(1, std::min(16, (3 * sms + ctas - 1) / ctas));
+    if (ctas >= 2 * sms) splits = 1;
+  }
+  if (splits > 1 && a.ws_elems < (int64_t)a.B * a.Hq * splits * (a.D + 2))
+    throw std::runtime_error("b200.decode_attention: split workspace too small");
+  dim3 grid(a.B * a.Hkv, splits);
+  if (a.D == 128) {
+    constexpr int NST = 8;
+    auto k = decode_attn_kernel<128, NST>;
+    static bool once = false;
+    if (!once) { set_smem(k, DecCfg<128, NST>::SMEM, a.device); once = true; }
+    k<<<grid, 160, DecCfg<128, NST>::SMEM, st>>>(tk, tv, a);
+    if (splits > 1) decode_merge_kernel<128><<<a.B * a.Hq, 128, 0, st>>>(a, splits);
+  } else {
+    constexpr int NST = 8;
+    auto k = decode_attn_kernel<64, NST>;
+    static bool once = false;
+    if (!once) { set_smem(k, DecCfg<64, NST>::SMEM, a.device); once = true; }
+    k<<<grid, 160, DecCfg<64, NST>::SMEM, st>>>(tk, tv, a);
+    if (splits > 1) decode_merge_kernel<64><<<a.B * a.Hq, 64, 0, st>>>(a, splits);
+  }
+}
+
+void prefill_attention_launch(const AttnArgs& a, cudaStream_t st) {
+  using namespace attn;
+  if (a.B == 0) return;
+  const int G = a.Hq / a.Hkv;
+  if (a.Hq % a.Hkv != 0 || 128 % G != 0) throw std::runtime_error("b200.prefill_attention: G must divide 128");
+  if (a.D != 128 && a.D != 64) throw std::runtime_error("b200.prefill_attention: D must be 64 or 128");
+  const int64_t rows = a.num_blocks * a.Hkv * 16;
+  CUtensorMap tk = make_tmap_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
+  CUtensorMap tv = make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
+  const int rows_tok = 128 / G;
+  const int q_tiles = (a.max_q_len + rows_tok - 1) / rows_tok;
+  dim3 grid(a.B * q_tiles, a.Hkv);
+  if (a.D == 128) {
+    constexpr int NST = 2;
+    auto k = prefill_attn_kernel<128, NST>;
+    static bool once = false;
+    if (!once) { set_smem(k, PreCfg<128, NST>::SMEM, a.device); once = true; }
+    k<<<grid, 288, PreCfg<128, NST>::SMEM, st>>>(tk, tv, a, q_tiles, rows_tok);
+  } else {
+    constexpr int NST = 3;
+    auto k = prefill_attn_kernel<64, NST>;
+    static bool once = false;
+    if (!once) { set_smem(k, PreCfg<64, NST>::SMEM, a.device); once = true; }
+    k<<<grid, 288, PreCfg<64, NST>::SMEM, st>>>(tk, tv, a, q_tiles, rows_tok);
+  }
+}
+
+}  // namespace b200

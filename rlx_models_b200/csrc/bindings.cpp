@@ -1,0 +1,268 @@
+// torch bindings of the sm_100a kernels: tensor validation, then a call into
+// the plain-C++ launchers declared in common/launch.h on the current stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common/launch.h"
+
+using at::Tensor;
+using c10::optional;
+
+namespace {
+
+inline const void* opt_ptr(const optional<Tensor>& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr;
+}
+
+inline cudaStream_t cur_stream(const Tensor& t) { return at::cuda::getCurrentCUDAStream(t.get_device()); }
+
+void check_cuda(const Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), "b200: ", name, " must be a CUDA tensor");
+}
+
+}  // namespace
+
+void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const optional<Tensor>& residual,
+            const optional<Tensor>& bias, double alpha, Tensor& ws, Tensor& sem, Tensor& status, int64_t swap,
+            int64_t bn, int64_t splits) {
+  check_cuda(x, "x");
+  check_cuda(w, "w");
+  check_cuda(out, "out");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "b200.linear: bf16 inputs");
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && out.dim() == 2, "b200.linear: 2-D tensors");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && out.stride(1) == 1, "b200.linear: inner dim contiguous");
+  const int64_t M = x.size(0), K = x.size(1), N = w.size(0);
+  TORCH_CHECK(w.size(1) == K, "b200.linear: K mismatch ", w.size(1), " vs ", K);
+  TORCH_CHECK(K % 8 == 0 && x.stride(0) % 8 == 0 && w.stride(0) % 8 == 0, "b200.linear: K and row strides % 8");
+  if (mode == 2) {
+    TORCH_CHECK(N % 128 == 0 && out.size(0) == M && out.size(1) == N / 2, "b200.linear(swiglu): shapes");
+  } else {
+    TORCH_CHECK(out.size(0) == M && out.size(1) == N, "b200.linear: out shape");
+  }
+  TORCH_CHECK((mode == 1) == (out.scalar_type() == at::kFloat), "b200.linear: out dtype");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::LinearArgs a{};
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.w = w.data_ptr();
+  a.ldw = w.stride(0);
+  a.out = out.data_ptr();
+  a.ldo = out.stride(0);
+  a.residual = nullptr;
+  if (residual.has_value() && residual->defined()) {
+    TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1 && residual->size(0) == M &&
+                    residual->size(1) == out.size(1),
+                "b200.linear: residual");
+    a.residual = residual->data_ptr();
+    a.ldr = residual->stride(0);
+  }
+  if (bias.has_value() && bias->defined())
+    TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N, "b200.linear: bias");
+  a.bias = opt_ptr(bias);
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.mode = (int)mode;
+  a.alpha = (float)alpha;
+  a.swap = (int)swap;
+  a.bn = (int)bn;
+  a.splits = (int)splits;
+  a.ws = ws.numel() ? ws.data_ptr<float>() : nullptr;
+  a.ws_elems = ws.numel();
+  a.sem = sem.numel() ? sem.data_ptr<int>() : nullptr;
+  a.sem_elems = sem.numel();
+  a.status = status.data_ptr<int>();
+  a.device = x.get_device();
+  b200::linear_launch(a, cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void embedding(const Tensor& ids, const Tensor& table, Tensor& out) {
+  check_cuda(ids, "ids");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "b200.embedding: int32 ids");
+  TORCH_CHECK(table.scalar_type() == at::kBFloat16 && table.is_contiguous() && table.size(1) % 8 == 0,
+              "b200.embedding: table");
+  TORCH_CHECK(out.is_contiguous() && out.size(0) == ids.numel() && out.size(1) == table.size(1), "b200.embedding: out");
+  c10::cuda::CUDAGuard g(ids.device());
+  b200::embedding_launch(ids.data_ptr<int32_t>(), table.data_ptr(), out.data_ptr(), ids.numel(), table.size(1),
+                         table.size(0), cur_stream(ids));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rmsnorm(const Tensor& x, const Tensor& w, Tensor& out, double eps, const optional<Tensor>& residual_in,
+             const optional<Tensor>& residual_out) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "b200.rmsnorm: x");
+  const int64_t T = x.size(0), H = x.size(1);
+  TORCH_CHECK(H % 256 == 0, "b200.rmsnorm: hidden % 256");
+  TORCH_CHECK(w.numel() == H && w.scalar_type() == at::kBFloat16, "b200.rmsnorm: weight");
+  TORCH_CHECK(out.size(0) == T && out.size(1) == H && out.stride(1) == 1, "b200.rmsnorm: out");
+  if (residual_in.has_value() && residual_in->defined())
+    TORCH_CHECK(residual_in->is_contiguous() && residual_in->numel() == T * H, "b200.rmsnorm: residual_in");
+  if (residual_out.has_value() && residual_out->defined())
+    TORCH_CHECK(residual_out->is_contiguous() && residual_out->numel() == T * H, "b200.rmsnorm: residual_out");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::rmsnorm_launch(x.data_ptr(), x.stride(0), opt_ptr(residual_in),
+                       const_cast<void*>(opt_ptr(residual_out)), w.data_ptr(), out.data_ptr(), out.stride(0), T, H,
+                       (float)eps, cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void qkv_rope(const Tensor& qkv, const optional<Tensor>& q_norm, const optional<Tensor>& k_norm,
+              const Tensor& positions, const optional<Tensor>& slots, const Tensor& inv_freq, double rope_scale,
+              Tensor& q_out, const optional<Tensor>& k_cache, const optional<Tensor>& v_cache,
+              const optional<Tensor>& k_out, const optional<Tensor>& v_out, int64_t Hq, int64_t Hkv, int64_t D,
+              double eps) {
+  check_cuda(qkv, "qkv");
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1, "b200.qkv_rope: qkv");
+  TORCH_CHECK(qkv.size(1) == (Hq + 2 * Hkv) * D, "b200.qkv_rope: qkv width");
+  TORCH_CHECK(D == 64 || D == 128, "b200.qkv_rope: head_dim 64 or 128");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && positions.numel() == qkv.size(0), "b200.qkv_rope: positions");
+  TORCH_CHECK(inv_freq.scalar_type() == at::kFloat && inv_freq.numel() == D / 2, "b200.qkv_rope: inv_freq");
+  TORCH_CHECK(q_out.is_contiguous() && q_out.numel() == qkv.size(0) * Hq * D, "b200.qkv_rope: q_out");
+  if (slots.has_value() && slots->defined()) {
+    TORCH_CHECK(slots->scalar_type() == at::kLong && slots->numel() == qkv.size(0), "b200.qkv_rope: slots");
+    TORCH_CHECK(k_cache.has_value() && v_cache.has_value(), "b200.qkv_rope: caches");
+  }
+  c10::cuda::CUDAGuard g(qkv.device());
+  b200::QkvRopeArgs a{};
+  a.qkv = qkv.data_ptr();
+  a.ld_qkv = qkv.stride(0);
+  a.q_norm = opt_ptr(q_norm);
+  a.k_norm = opt_ptr(k_norm);
+  a.positions = positions.data_ptr<int32_t>();
+  a.slots = (slots.has_value() && slots->defined()) ? slots->data_ptr<int64_t>() : nullptr;
+  a.inv_freq = inv_freq.data_ptr<float>();
+  a.rope_scale = (float)rope_scale;
+  a.rot_dim = (int)D;
+  a.q_out = q_out.data_ptr();
+  a.k_cache = const_cast<void*>(opt_ptr(k_cache));
+  a.v_cache = const_cast<void*>(opt_ptr(v_cache));
+  a.k_out = const_cast<void*>(opt_ptr(k_out));
+  a.v_out = const_cast<void*>(opt_ptr(v_out));
+  a.T = qkv.size(0);
+  a.Hq = (int)Hq;
+  a.Hkv = (int)Hkv;
+  a.D = (int)D;
+  a.eps = (float)eps;
+  b200::qkv_rope_launch(a, cur_stream(qkv));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static b200::AttnArgs attn_args(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache,
+                                const Tensor& block_tables, const Tensor& ctx_lens, Tensor& out,
+                                const optional<Tensor>& sinks, int64_t window, double scale, Tensor& status) {
+  check_cuda(q, "q");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.is_contiguous(), "b200.attention: q [T,Hq,D]");
+  TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous(),
+              "b200.attention: caches [NB,Hkv,16,D]");
+  TORCH_CHECK(k_cache.size(2) == 16 && k_cache.size(3) == q.size(2), "b200.attention: cache block/head dim");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.dim() == 2 && block_tables.is_contiguous(),
+              "b200.attention: block_tables int32 [B, max_blocks]");
+  TORCH_CHECK(ctx_lens.scalar_type() == at::kInt && ctx_lens.numel() == block_tables.size(0),
+              "b200.attention: ctx_lens");
+  TORCH_CHECK(out.is_contiguous() && out.sizes() == q.sizes() && out.scalar_type() == at::kBFloat16,
+              "b200.attention: out");
+  if (sinks.has_value() && sinks->defined())
+    TORCH_CHECK(sinks->scalar_type() == at::kFloat && sinks->numel() == q.size(1), "b200.attention: sinks f32 [Hq]");
+  b200::AttnArgs a{};
+  a.q = q.data_ptr();
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.num_blocks = k_cache.size(0);
+  a.block_tables = block_tables.data_ptr<int32_t>();
+  a.max_blocks = (int)block_tables.size(1);
+  a.ctx_lens = ctx_lens.data_ptr<int32_t>();
+  a.out = out.data_ptr();
+  a.sinks = (sinks.has_value() && sinks->defined()) ? sinks->data_ptr<float>() : nullptr;
+  a.window = (int)window;
+  a.B = (int)block_tables.size(0);
+  a.Hq = (int)q.size(1);
+  a.Hkv = (int)k_cache.size(1);
+  a.D = (int)q.size(2);
+  a.scale = (float)scale;
+  a.status = status.data_ptr<int>();
+  a.device = q.get_device();
+  return a;
+}
+
+void decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& block_tables,
+                      const Tensor& ctx_lens, Tensor& out, const optional<Tensor>& sinks, int64_t window,
+                      double scale, int64_t splits, Tensor& ws, Tensor& status) {
+  c10::cuda::CUDAGuard g(q.device());
+  auto a = attn_args(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, window, scale, status);
+  TORCH_CHECK(q.size(0) == block_tables.size(0), "b200.decode_attention: one query per sequence");
+  a.cu_q = nullptr;
+  a.splits = (int)splits;
+  a.ws = ws.numel() ? ws.data_ptr<float>() : nullptr;
+  a.ws_elems = ws.numel();
+  b200::decode_attention_launch(a, cur_stream(q));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void prefill_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& block_tables,
+                       const Tensor& ctx_lens, const Tensor& cu_q, Tensor& out, const optional<Tensor>& sinks,
+                       int64_t window, double scale, int64_t max_q_len, Tensor& status) {
+  c10::cuda::CUDAGuard g(q.device());
+  auto a = attn_args(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, window, scale, status);
+  TORCH_CHECK(cu_q.scalar_type() == at::kInt && cu_q.numel() == block_tables.size(0) + 1, "b200.prefill: cu_q");
+  a.cu_q = cu_q.data_ptr<int32_t>();
+  a.max_q_len = (int)max_q_len;
+  b200::prefill_attention_launch(a, cur_stream(q));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void argmax(const Tensor& logits, Tensor& out) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1, "b200.argmax");
+  TORCH_CHECK(out.scalar_type() == at::kInt && out.numel() == logits.size(0), "b200.argmax: out");
+  c10::cuda::CUDAGuard g(logits.device());
+  b200::argmax_launch(logits.data_ptr<float>(), logits.stride(0), logits.size(0), logits.size(1),
+                      out.data_ptr<int32_t>(), cur_stream(logits));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k, const Tensor& top_p,
+            const Tensor& min_p, const Tensor& seeds, const Tensor& offsets, Tensor& out,
+            const optional<Tensor>& logprob) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1, "b200.sample");
+  const int64_t B = logits.size(0);
+  TORCH_CHECK(temperature.numel() == B && top_k.numel() == B && top_p.numel() == B && min_p.numel() == B &&
+                  seeds.numel() == B && offsets.numel() == B && out.numel() == B,
+              "b200.sample: per-row parameter sizes");
+  TORCH_CHECK(temperature.scalar_type() == at::kFloat && top_k.scalar_type() == at::kInt &&
+                  top_p.scalar_type() == at::kFloat && min_p.scalar_type() == at::kFloat &&
+                  seeds.scalar_type() == at::kLong && offsets.scalar_type() == at::kLong &&
+                  out.scalar_type() == at::kInt,
+              "b200.sample: parameter dtypes");
+  c10::cuda::CUDAGuard g(logits.device());
+  b200::SampleArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.ld = logits.stride(0);
+  a.B = B;
+  a.V = logits.size(1);
+  a.temperature = temperature.data_ptr<float>();
+  a.top_k = top_k.data_ptr<int32_t>();
+  a.top_p = top_p.data_ptr<float>();
+  a.min_p = min_p.data_ptr<float>();
+  a.seeds = reinterpret_cast<const uint64_t*>(seeds.data_ptr<int64_t>());
+  a.offsets = offsets.data_ptr<int64_t>();
+  a.out = out.data_ptr<int32_t>();
+  a.out_logprob = (logprob.has_value() && logprob->defined()) ? logprob->data_ptr<float>() : nullptr;
+  b200::sample_launch(a, cur_stream(logits));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "rlx_models_b200 sm_100a kernels";
+  m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues");
+  m.def("embedding", &embedding);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("qkv_rope", &qkv_rope);
+  m.def("decode_attention", &decode_attention);
+  m.def("prefill_attention", &prefill_attention);
+  m.def("argmax", &argmax);
+  m.def("sample", &sample);
+}

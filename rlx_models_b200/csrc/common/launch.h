@@ -1,0 +1,109 @@
+// Plain-C++ launch interfaces of the CUDA kernels. The .cu files implement
+// them without any torch headers (so they compile quickly with nvcc); the
+// torch bindings in bindings.cpp validate tensors and fill these structs.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace b200 {
+
+// ---------------- GEMM ----------------
+struct LinearArgs {
+  const void* x;
+  int64_t ldx;  // [M, K]
+  const void* w;
+  int64_t ldw;  // [N, K]
+  void* out;
+  int64_t ldo;  // [M, N] or [M, N/2] for SwiGLU
+  const void* residual;
+  int64_t ldr;  // optional [M, N] bf16 added in the epilogue
+  const void* bias;  // optional [N] bf16
+  int64_t M, N, K;
+  int mode;  // 0 bf16, 1 f32, 2 SwiGLU (interleaved gate/up groups of 64)
+  float alpha;
+  int swap, bn, splits;  // -1/0 = auto
+  float* ws;
+  int64_t ws_elems;
+  int* sem;
+  int64_t sem_elems;
+  int* status;
+  int device;
+};
+void linear_launch(const LinearArgs& a, cudaStream_t st);
+
+// ---------------- norms / rope / embedding ----------------
+void embedding_launch(const int32_t* ids, const void* table, void* out, int64_t T, int64_t H, int64_t V,
+                      cudaStream_t st);
+// out = rmsnorm(x (+ residual_in)) * w ; if residual_out: residual_out = x (+ residual_in)
+void rmsnorm_launch(const void* x, int64_t ldx, const void* residual_in, void* residual_out, const void* w,
+                    void* out, int64_t ldo, int64_t T, int64_t H, float eps, cudaStream_t st);
+
+struct QkvRopeArgs {
+  const void* qkv;  // [T, (Hq + 2 Hkv) * D] bf16
+  int64_t ld_qkv;
+  const void* q_norm;  // [D] or null
+  const void* k_norm;  // [D] or null
+  const int32_t* positions;  // [T]
+  const int64_t* slots;      // [T] cache slot (block * 16 + offset), -1 = skip
+  const float* inv_freq;     // [rot_dim / 2]
+  float rope_scale;          // multiplier on cos/sin (YaRN mscale), 1 otherwise
+  int rot_dim;               // rotary dims (<= D), half-split (NeoX) layout
+  void* q_out;               // [T, Hq, D]
+  void* k_cache;             // [NB, Hkv, 16, D]
+  void* v_cache;
+  void* k_out;               // optional [T, Hkv, D] (training / no cache)
+  void* v_out;
+  int64_t T;
+  int Hq, Hkv, D;
+  float eps;
+};
+void qkv_rope_launch(const QkvRopeArgs& a, cudaStream_t st);
+
+// ---------------- attention ----------------
+struct AttnArgs {
+  const void* q;  // [Tq, Hq, D] bf16
+  const void* k_cache;
+  const void* v_cache;  // [NB, Hkv, 16, D]
+  int64_t num_blocks;
+  const int32_t* block_tables;  // [B, max_blocks]
+  int max_blocks;
+  const int32_t* ctx_lens;   // [B] kv length incl. the new tokens
+  const int32_t* cu_q;       // [B+1] query offsets (prefill); null for decode (1 query / seq)
+  void* out;                 // [Tq, Hq, D] bf16
+  const float* sinks;        // [Hq] or null (learned sink logits)
+  int window;                // sliding window (0 = full)
+  int B, Hq, Hkv, D;
+  float scale;
+  int max_q_len;             // prefill: max query length per sequence
+  int splits;                // decode: KV splits (0 = auto)
+  float* ws;                 // decode split workspace
+  int64_t ws_elems;
+  int* status;
+  int device;
+};
+void decode_attention_launch(const AttnArgs& a, cudaStream_t st);
+void prefill_attention_launch(const AttnArgs& a, cudaStream_t st);
+
+// ---------------- sampling ----------------
+void argmax_launch(const float* logits, int64_t ld, int64_t B, int64_t V, int32_t* out, cudaStream_t st);
+
+struct SampleArgs {
+  const float* logits;  // [B, V]
+  int64_t ld;
+  int64_t B, V;
+  const float* temperature;  // [B] (<= 0 -> greedy)
+  const int32_t* top_k;      // [B] (0 -> disabled)
+  const float* top_p;        // [B] (1 -> disabled)
+  const float* min_p;        // [B] (0 -> disabled)
+  const uint64_t* seeds;     // [B] per-row RNG seed
+  const int64_t* offsets;    // [B] per-row RNG counter
+  int32_t* out;              // [B]
+  float* out_logprob;        // [B] or null
+  float* ws;                 // candidate workspace
+  int64_t ws_elems;
+};
+void sample_launch(const SampleArgs& a, cudaStream_t st);
+
+}  // namespace b200

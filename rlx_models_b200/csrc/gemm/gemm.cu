@@ -1,0 +1,121 @@
+// Host launcher for the tcgen05 BF16 GEMM (see gemm_sm100.cuh).
+//
+// linear(x[M,K], w[N,K]) -> out: picks the orientation, tile width and split-K
+// factor for the shape, builds the two TMA maps and launches the persistent
+// kernel on the current stream.
+//   * prefill / training shapes (M > 128): A = x, B = w, BN = 256.
+//   * decode shapes (M <= 128): "swap-AB" - A = w (weights fill the 128-row MMA
+//     M dimension), B = x (the few tokens are the MMA N dimension), and split-K
+//     so that every SM streams a slice of the weights.
+#include <algorithm>
+#include <stdexcept>
+#include <string>
+
+#include "../common/tma_host.h"
+#include "gemm_sm100.cuh"
+
+namespace b200 {
+namespace gemm {
+
+template <int BN, int EPI>
+static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid, cudaStream_t st,
+                     int device) {
+  auto kern = gemm_bf16_kernel<BN, EPI>;
+  static uint64_t attr_done = 0;  // one bit per device
+  if (!(attr_done & (1ull << device))) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM_BYTES);
+    attr_done |= (1ull << device);
+  }
+  kern<<<grid, kThreads, Cfg<BN>::SMEM_BYTES, st>>>(ta, tb, p);
+}
+
+template <int EPI>
+static void launch_bn(int BN, const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
+                      cudaStream_t st, int device) {
+  switch (BN) {
+    case 32: launch_t<32, EPI>(ta, tb, p, grid, st, device); break;
+    case 64: launch_t<64, EPI>(ta, tb, p, grid, st, device); break;
+    case 128: launch_t<128, EPI>(ta, tb, p, grid, st, device); break;
+    case 256: launch_t<256, EPI>(ta, tb, p, grid, st, device); break;
+    default: throw std::runtime_error("b200.linear: unsupported BN " + std::to_string(BN));
+  }
+}
+
+}  // namespace gemm
+}  // namespace b200
+
+#include "../common/launch.h"
+
+namespace b200 {
+
+// Raw-pointer GEMM entry used by the torch bindings and by the fused kernels'
+// host code. All tensors are row-major with unit inner stride.
+void linear_launch(const LinearArgs& a, cudaStream_t st) {
+  const int64_t M = a.M, K = a.K, N = a.N;
+  const int epi = a.mode;
+  if (M == 0 || N == 0) return;
+  const int sms = num_sms(a.device);
+  const bool sw = a.swap < 0 ? (M <= 128 && N >= 256) : (a.swap == 1);
+
+  gemm::Params p{};
+  const void* A = sw ? a.w : a.x;
+  const void* B = sw ? a.x : a.w;
+  const int64_t lda = sw ? a.ldw : a.ldx;
+  const int64_t ldb = sw ? a.ldx : a.ldw;
+  p.MA = (int)(sw ? N : M);
+  p.NB = (int)(sw ? M : N);
+  p.K = (int)K;
+  int BN = a.bn;
+  if (BN == 0) {
+    if (sw) BN = p.NB <= 32 ? 32 : (p.NB <= 64 ? 64 : 128);
+    else BN = p.NB >= 256 ? 256 : (p.NB > 64 ? 128 : (p.NB > 32 ? 64 : 32));
+    if (epi == gemm::EPI_SWIGLU && !sw && BN < 128) BN = 128;
+  }
+  p.k_tiles = (int)((K + gemm::kBK - 1) / gemm::kBK);
+  p.num_m = (p.MA + gemm::kBM - 1) / gemm::kBM;
+  p.num_n = (p.NB + BN - 1) / BN;
+  const int tiles = p.num_m * p.num_n;
+  int sp = a.splits;
+  if (sp <= 0) {
+    sp = 1;
+    if (tiles * 2 <= sms) {
+      sp = sms / tiles;
+      sp = std::min(sp, std::max(1, p.k_tiles / 4));
+      sp = std::min(sp, 32);
+    }
+  }
+  sp = std::max(1, std::min(sp, p.k_tiles));
+  p.kt_per_split = (p.k_tiles + sp - 1) / sp;
+  p.splits = (p.k_tiles + p.kt_per_split - 1) / p.kt_per_split;
+  p.num_units = tiles * p.splits;
+  if (p.splits > 1) {
+    if (a.ws_elems < (int64_t)p.num_units * gemm::kBM * BN || a.ws == nullptr)
+      throw std::runtime_error("b200.linear: split-K workspace too small");
+    if (a.sem_elems < tiles || a.sem == nullptr) throw std::runtime_error("b200.linear: semaphore buffer too small");
+  }
+  p.C = a.out;
+  p.ldc_i = sw ? 1 : a.ldo;
+  p.ldc_j = sw ? a.ldo : 1;
+  p.R = reinterpret_cast<const __nv_bfloat16*>(a.residual);
+  p.ldr_i = sw ? 1 : a.ldr;
+  p.ldr_j = sw ? a.ldr : 1;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
+  p.bias_on_i = sw ? 1 : 0;
+  p.alpha = a.alpha;
+  p.swiglu_on_i = sw ? 1 : 0;
+  p.ws = a.ws;
+  p.sem = a.sem;
+  p.status = a.status;
+
+  CUtensorMap ta = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.MA, K, lda, gemm::kBM, gemm::kBK);
+  CUtensorMap tb = make_tmap_2d(B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.NB, K, ldb, BN, gemm::kBK);
+  const int grid = std::min(p.num_units, sms);
+  switch (epi) {
+    case gemm::EPI_BF16: gemm::launch_bn<gemm::EPI_BF16>(BN, ta, tb, p, grid, st, a.device); break;
+    case gemm::EPI_F32: gemm::launch_bn<gemm::EPI_F32>(BN, ta, tb, p, grid, st, a.device); break;
+    case gemm::EPI_SWIGLU: gemm::launch_bn<gemm::EPI_SWIGLU>(BN, ta, tb, p, grid, st, a.device); break;
+    default: throw std::runtime_error("b200.linear: bad mode");
+  }
+}
+
+}  // namespace b200

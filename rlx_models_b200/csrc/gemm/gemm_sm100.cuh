@@ -1,0 +1,430 @@
+// Persistent, warp-specialized tcgen05 BF16 GEMM for sm_100a.
+//
+//   D[i, j] = alpha * sum_k A[i, k] * B[j, k]      (A: [MA, K], B: [NB, K], both K-major)
+//
+// followed by a fused epilogue (bias, residual add, SwiGLU pairing, bf16/f32
+// store, split-K reduction). This is the dense-linear kernel ("K1") behind every
+// projection of the decoder families; the reference emits the same op as a
+// graph MatMul lowered to a library GEMM (rlx-models-core
+// src/standard_decoder.rs:727 `emit_proj`).
+//
+// Roles (192 threads, one CTA per SM, grid = min(work units, #SMs)):
+//   warp 0      TMA producer: one elected lane streams A/B k-tiles into a
+//               STAGES-deep shared-memory ring (128-byte swizzle) using
+//               cp.async.bulk.tensor (no multicast) + mbarrier complete_tx.
+//   warp 1      MMA issuer: one elected lane issues tcgen05.mma (M=128, N=BN,
+//               K=16) into a double-buffered TMEM accumulator and releases each
+//               smem stage with tcgen05.commit.
+//   warps 2..5  epilogue: tcgen05.ld 32x32b from TMEM -> registers -> fused
+//               epilogue -> global, overlapping the next tile's MMAs.
+//
+// Split-K (used for skinny decode GEMMs so that all SMs stream weights): each
+// split writes an fp32 partial tile to a workspace; the last split of a tile
+// (per-tile semaphore) sums the partials and runs the real epilogue, then
+// resets the semaphore so the next launch (or graph replay) starts from zero.
+#pragma once
+
+#include "../common/b200.cuh"
+
+namespace b200 {
+namespace gemm {
+
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2 };
+
+struct Params {
+  int MA, NB, K;
+  int k_tiles, splits, kt_per_split;
+  int num_m, num_n, num_units;
+  void* C;
+  int64_t ldc_i, ldc_j;
+  const __nv_bfloat16* R;
+  int64_t ldr_i, ldr_j;
+  const __nv_bfloat16* bias;
+  int bias_on_i;
+  float alpha;
+  int swiglu_on_i;
+  float* ws;
+  int* sem;
+  int* status;
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kGroupM = 8;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct Cfg {
+  static constexpr uint32_t A_BYTES = kBM * kBK * 2;
+  static constexpr uint32_t B_BYTES = BN * kBK * 2;
+  static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
+  static constexpr uint32_t TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
+  static constexpr uint32_t XCHG_BYTES = 64 * 33 * 4;  // swap-SwiGLU gate/up exchange
+  static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + XCHG_BYTES + 256;
+};
+
+__device__ __forceinline__ void unit_to_tile(const Params& p, int u, int& m_tile, int& n_tile, int& ks, int& tile) {
+  ks = u % p.splits;
+  tile = u / p.splits;
+  const int group_size = kGroupM * p.num_n;
+  const int g = tile / group_size;
+  const int first_m = g * kGroupM;
+  const int gm = min(p.num_m - first_m, kGroupM);
+  const int r = tile % group_size;
+  m_tile = first_m + r % gm;
+  n_tile = r / gm;
+}
+
+template <int BN, int EPI>
+__device__ __forceinline__ void store_chunk(const Params& p, int i, int j0, float (&v)[32]) {
+  if (i >= p.MA) return;
+  // scalar-or-vector epilogue for one row i and 32 consecutive j
+  float bi = 0.f;
+  if (p.bias != nullptr && p.bias_on_i) bi = __bfloat162float(p.bias[i]);
+#pragma unroll
+  for (int t = 0; t < 32; ++t) {
+    float x = v[t] * p.alpha + bi;
+    v[t] = x;
+  }
+  if (p.bias != nullptr && !p.bias_on_i) {
+#pragma unroll
+    for (int t = 0; t < 32; ++t)
+      if (j0 + t < p.NB) v[t] += __bfloat162float(p.bias[j0 + t]);
+  }
+  const bool full = (j0 + 32 <= p.NB);
+  if (p.R != nullptr) {
+    const __nv_bfloat16* r = p.R + (int64_t)i * p.ldr_i;
+    if (p.ldr_j == 1 && full && ((reinterpret_cast<uintptr_t>(r + j0) & 15u) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w = *reinterpret_cast<const uint4*>(r + j0 + q * 8);
+        uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[q * 8 + 2 * h] += bf16_lo(ww[h]);
+          v[q * 8 + 2 * h + 1] += bf16_hi(ww[h]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        if (j0 + t < p.NB) v[t] += __bfloat162float(r[(int64_t)(j0 + t) * p.ldr_j]);
+    }
+  }
+  if (EPI == EPI_F32) {
+    float* c = reinterpret_cast<float*>(p.C) + (int64_t)i * p.ldc_i;
+    if (p.ldc_j == 1 && full && ((reinterpret_cast<uintptr_t>(c + j0) & 15u) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<float4*>(c + j0 + q * 4) = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        if (j0 + t < p.NB) c[(int64_t)(j0 + t) * p.ldc_j] = v[t];
+    }
+  } else {
+    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (int64_t)i * p.ldc_i;
+    if (p.ldc_j == 1 && full && ((reinterpret_cast<uintptr_t>(c + j0) & 15u) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+        w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+        w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+        w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+        *reinterpret_cast<uint4*>(c + j0 + q * 8) = w;
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        if (j0 + t < p.NB) c[(int64_t)(j0 + t) * p.ldc_j] = __float2bfloat16(v[t]);
+    }
+  }
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + __expf(-g)) * u; }
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const Params p) {
+  using C = Cfg<BN>;
+  constexpr int STAGES = C::STAGES;
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  float* xchg = reinterpret_cast<float*>(smem + STAGES * C::STAGE_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * C::STAGE_BYTES + C::XCHG_BYTES);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* accf = bars + 2 * STAGES;
+  uint64_t* acce = bars + 2 * STAGES + 2;
+  uint64_t* drain = bars + 2 * STAGES + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* s_last = reinterpret_cast<int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf[a], 1);
+      mbar_init(&acce[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one_sync()) {
+      // ---------------- TMA producer ----------------
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+        int m_tile, n_tile, ks, tile;
+        unit_to_tile(p, u, m_tile, n_tile, ks, tile);
+        const int kb = ks * p.kt_per_split;
+        const int ke = min(p.k_tiles, kb + p.kt_per_split);
+        for (int kt = kb; kt < ke; ++kt) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.status, kErrTimeoutEmpty) || *abort_flag) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          uint8_t* sa = ring + stage * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+          tma_load_2d(sa, &tmA, &full[stage], kt * kBK, m_tile * kBM);
+          tma_load_2d(sb, &tmB, &full[stage], kt * kBK, n_tile * BN);
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Error path: wait (bounded) for the loads this thread put in flight.
+        int s = stage;
+        uint32_t ph = phase;
+        const uint32_t n = issued < (uint32_t)STAGES ? issued : (uint32_t)STAGES;
+        for (uint32_t q = 0; q < n; ++q) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          mbar_wait(&full[s], ph, p.status, kErrTimeoutDrain);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one_sync()) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN, false, false);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x, ++it) {
+        int m_tile, n_tile, ks, tile;
+        unit_to_tile(p, u, m_tile, n_tile, ks, tile);
+        const int kb = ks * p.kt_per_split;
+        const int ke = min(p.k_tiles, kb + p.kt_per_split);
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&acce[acc], acc_phase ^ 1, p.status, kErrTimeoutAccEmpty) || *abort_flag) {
+          *abort_flag = 1;
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kt = kb; kt < ke; ++kt) {
+          if (!mbar_wait(&full[stage], phase, p.status, kErrTimeoutFull) || *abort_flag) {
+            *abort_flag = 1;
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(ring + stage * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint64_t ad = umma_desc_sw128(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = umma_desc_sw128(b_addr + kk * 32, 16, 1024);
+            umma_f16(d_tmem, ad, bd, idesc, (kt > kb || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) umma_commit(&accf[acc]);
+      }
+      if (!ok) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, p.status, kErrTimeoutDrain);
+      }
+    }
+  } else {
+    // ---------------- Epilogue (warps 2..5) ----------------
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const int ew = warp - 2;
+    int it = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++it) {
+      int m_tile, n_tile, ks, tile;
+      unit_to_tile(p, u, m_tile, n_tile, ks, tile);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&accf[acc], acc_phase, p.status, kErrTimeoutAccFull) || *abort_flag) {
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+      const int i = m_tile * kBM + row;
+      const int jt = n_tile * BN;
+
+      if (p.splits > 1) {
+        // Park this split's fp32 partial tile in the workspace.
+        float* wsp = p.ws + ((int64_t)tile * p.splits + ks) * (kBM * BN) + (int64_t)row * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(reinterpret_cast<float4*>(wsp + c * 32 + q * 4),
+                   make_float4(__uint_as_float(r[q * 4]), __uint_as_float(r[q * 4 + 1]),
+                               __uint_as_float(r[q * 4 + 2]), __uint_as_float(r[q * 4 + 3])));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[acc]);
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (ew == 0 && lane == 0) {
+          const int old = atomicAdd(&p.sem[tile], 1);
+          *s_last = (old == p.splits - 1) ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        if (*s_last == 0) continue;
+        __threadfence();
+      }
+
+      // Fetch 32 accumulator columns [c*32, c*32+32) of this thread's row.
+      auto fetch = [&](int c, float (&v)[32]) {
+        if (p.splits > 1) {
+          const float* base = p.ws + (int64_t)tile * p.splits * (kBM * BN) + (int64_t)row * BN + c * 32;
+#pragma unroll
+          for (int t = 0; t < 32; ++t) v[t] = 0.f;
+          for (int s = 0; s < p.splits; ++s) {
+            const float4* src = reinterpret_cast<const float4*>(base + (int64_t)s * (kBM * BN));
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              float4 w = __ldcg(src + q);
+              v[q * 4] += w.x;
+              v[q * 4 + 1] += w.y;
+              v[q * 4 + 2] += w.z;
+              v[q * 4 + 3] += w.w;
+            }
+          }
+        } else {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 32; ++t) v[t] = __uint_as_float(r[t]);
+        }
+      };
+
+      if (EPI == EPI_SWIGLU && !p.swiglu_on_i) {
+        // gate/up interleaved along j in groups of 64 columns: [g*128, g*128+64) gate, +64 up.
+#pragma unroll 1
+        for (int g = 0; g < BN / 128; ++g) {
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            float vg[32], vu[32];
+            fetch(g * 4 + h, vg);
+            fetch(g * 4 + h + 2, vu);
+#pragma unroll
+            for (int t = 0; t < 32; ++t) vg[t] = silu_mul(vg[t] * p.alpha, vu[t] * p.alpha);
+            Params q = p;
+            q.alpha = 1.f;
+            q.NB = p.NB / 2;
+            q.bias = nullptr;
+            store_chunk<BN, EPI_BF16>(q, i, (jt + g * 128) / 2 + h * 32, vg);
+          }
+        }
+      } else if (EPI == EPI_SWIGLU) {
+        // gate/up interleaved along i: tile rows [0,64) gate, [64,128) up of the same features.
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          fetch(c, v);
+          if (quad >= 2) {
+#pragma unroll
+            for (int t = 0; t < 32; ++t) xchg[((quad - 2) * 32 + lane) * 33 + t] = v[t];
+          }
+          named_bar_sync(2, 128);
+          if (quad < 2) {
+#pragma unroll
+            for (int t = 0; t < 32; ++t) v[t] = silu_mul(v[t] * p.alpha, xchg[(quad * 32 + lane) * 33 + t] * p.alpha);
+            Params q = p;
+            q.alpha = 1.f;
+            q.MA = p.MA / 2;
+            q.bias = nullptr;
+            store_chunk<BN, EPI_BF16>(q, m_tile * 64 + quad * 32 + lane, jt + c * 32, v);
+          }
+          named_bar_sync(2, 128);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          fetch(c, v);
+          store_chunk<BN, EPI>(p, i, jt + c * 32, v);
+        }
+      }
+
+      if (p.splits > 1) {
+        if (ew == 0 && lane == 0) p.sem[tile] = 0;
+      } else {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[acc]);
+      }
+    }
+  }
+
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+}  // namespace gemm
+}  // namespace b200

@@ -1,0 +1,180 @@
+"""Functional wrappers over the sm_100a kernels.
+
+Every function here launches one of this package's own CUDA kernels on the
+current stream; none falls back to a torch/cuBLAS implementation. The fp32
+CPU restatements used as test oracles live in :mod:`rlx_models_b200.ops.reference`.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ._ext import KernelError, available, check_errors, ext, scratch
+
+__all__ = [
+    "linear", "linear_swiglu", "rmsnorm", "qkv_rope", "embedding", "decode_attention",
+    "prefill_attention", "argmax", "sample", "interleave_gate_up", "rope_inv_freq",
+    "check_errors", "KernelError", "available",
+]
+
+SWIGLU_GROUP = 64  # gate/up rows interleaved in groups of 64 for the fused epilogue
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, *, out: torch.Tensor | None = None,
+           residual: torch.Tensor | None = None, bias: torch.Tensor | None = None,
+           alpha: float = 1.0, out_dtype: torch.dtype = torch.bfloat16,
+           swap: int = -1, bn: int = 0, splits: int = 0) -> torch.Tensor:
+    """``out = alpha * x @ w.T (+ bias) (+ residual)`` on the tcgen05 GEMM.
+
+    x: [M, K] bf16, w: [N, K] bf16 (nn.Linear layout). ``out_dtype`` bf16 or f32.
+    """
+    M, N = x.shape[0], w.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=out_dtype, device=x.device)
+    s = scratch(x.device)
+    mode = 1 if out.dtype == torch.float32 else 0
+    ext().linear(x, w, out, mode, residual, bias, float(alpha), s.gemm_ws, s.gemm_sem, s.status,
+                 swap, bn, splits)
+    return out
+
+
+def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, *, out: torch.Tensor | None = None,
+                  swap: int = -1, bn: int = 0, splits: int = 0) -> torch.Tensor:
+    """``silu(x @ Wg.T) * (x @ Wu.T)`` with ``w_gu = interleave_gate_up(Wg, Wu)``."""
+    M, N = x.shape[0], w_gu.shape[0]
+    if out is None:
+        out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
+    s = scratch(x.device)
+    ext().linear(x, w_gu, out, 2, None, None, 1.0, s.gemm_ws, s.gemm_sem, s.status, swap, bn, splits)
+    return out
+
+
+def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor, group: int = SWIGLU_GROUP) -> torch.Tensor:
+    """[I, K] x2 -> [2I, K] with rows [g*2G, g*2G+G) = gate, [g*2G+G, (g+1)*2G) = up."""
+    I, K = w_gate.shape
+    assert I % group == 0, "intermediate size must be a multiple of the SwiGLU group"
+    g = w_gate.reshape(I // group, group, K)
+    u = w_up.reshape(I // group, group, K)
+    return torch.stack([g, u], dim=1).reshape(2 * I, K).contiguous()
+
+
+def deinterleave_gate_up(w_gu: torch.Tensor, group: int = SWIGLU_GROUP):
+    two_i, K = w_gu.shape
+    v = w_gu.reshape(two_i // (2 * group), 2, group, K)
+    return v[:, 0].reshape(-1, K), v[:, 1].reshape(-1, K)
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, *, out: torch.Tensor | None = None,
+            residual: torch.Tensor | None = None, residual_out: torch.Tensor | None = None) -> torch.Tensor:
+    """``rmsnorm(x (+ residual)) * w``; with ``residual_out`` the sum is also stored."""
+    if out is None:
+        out = torch.empty_like(x)
+    ext().rmsnorm(x, w, out, float(eps), residual, residual_out)
+    return out
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    ext().embedding(ids, table, out)
+    return out
+
+
+def rope_inv_freq(head_dim: int, theta: float, scaling: dict | None = None,
+                  max_position: int | None = None) -> tuple[torch.Tensor, float]:
+    """fp32 inverse frequencies (HF formula) and the cos/sin multiplier.
+
+    Supports no scaling, ``linear``, ``llama3`` and ``yarn`` (returns mscale).
+    """
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
+    mult = 1.0
+    if scaling:
+        kind = scaling.get("rope_type", scaling.get("type", "default"))
+        if kind == "linear":
+            inv = inv / float(scaling["factor"])
+        elif kind == "llama3":
+            factor = float(scaling["factor"])
+            lo = float(scaling.get("low_freq_factor", 1.0))
+            hi = float(scaling.get("high_freq_factor", 4.0))
+            old = float(scaling.get("original_max_position_embeddings", 8192))
+            lo_wl, hi_wl = old / lo, old / hi
+            wl = 2 * math.pi / inv
+            smooth = (old / wl - lo) / (hi - lo)
+            scaled = torch.where(wl > lo_wl, inv / factor, inv)
+            mid = (1 - smooth) * scaled / factor + smooth * scaled
+            is_mid = (wl >= hi_wl) & (wl <= lo_wl)
+            inv = torch.where(is_mid, mid, scaled)
+        elif kind == "yarn":
+            factor = float(scaling["factor"])
+            old = float(scaling.get("original_max_position_embeddings", max_position or 4096))
+            beta_fast = float(scaling.get("beta_fast", 32.0))
+            beta_slow = float(scaling.get("beta_slow", 1.0))
+
+            def corr_dim(n_rot):
+                return (head_dim * math.log(old / (n_rot * 2 * math.pi))) / (2 * math.log(theta))
+
+            low = max(math.floor(corr_dim(beta_fast)), 0)
+            high = min(math.ceil(corr_dim(beta_slow)), head_dim - 1)
+            if scaling.get("truncate", True) is False:
+                low, high = corr_dim(beta_fast), corr_dim(beta_slow)
+            if low == high:
+                high += 0.001
+            ramp = (torch.arange(head_dim // 2, dtype=torch.float32) - low) / (high - low)
+            ramp = ramp.clamp(0, 1)
+            extrap = 1 - ramp
+            inv = (inv / factor) * (1 - extrap) + inv * extrap
+            ms = scaling.get("mscale")
+            mult = float(scaling.get("attention_factor") or (0.1 * math.log(factor) + 1.0 if factor > 1 else 1.0))
+            if ms is not None and scaling.get("attention_factor") is None:
+                mult = float(ms) if ms else mult
+    return inv.float(), mult
+
+
+def qkv_rope(qkv: torch.Tensor, *, num_q_heads: int, num_kv_heads: int, head_dim: int,
+             positions: torch.Tensor, inv_freq: torch.Tensor, rope_scale: float = 1.0,
+             q_norm: torch.Tensor | None = None, k_norm: torch.Tensor | None = None, eps: float = 1e-6,
+             slots: torch.Tensor | None = None, k_cache: torch.Tensor | None = None,
+             v_cache: torch.Tensor | None = None, q_out: torch.Tensor | None = None,
+             k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None) -> torch.Tensor:
+    """QK RMSNorm + RoPE on the fused qkv projection; K/V written to the paged cache."""
+    T = qkv.shape[0]
+    if q_out is None:
+        q_out = torch.empty(T, num_q_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
+    ext().qkv_rope(qkv, q_norm, k_norm, positions, slots, inv_freq, float(rope_scale), q_out, k_cache,
+                   v_cache, k_out, v_out, num_q_heads, num_kv_heads, head_dim, float(eps))
+    return q_out
+
+
+def decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, *, scale, sinks=None, window=0,
+                     splits=0, out=None):
+    if out is None:
+        out = torch.empty_like(q)
+    s = scratch(q.device)
+    ext().decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, int(window), float(scale),
+                           int(splits), s.attn_ws, s.status)
+    return out
+
+
+def prefill_attention(q, k_cache, v_cache, block_tables, ctx_lens, cu_q, max_q_len, *, scale, sinks=None,
+                      window=0, out=None):
+    if out is None:
+        out = torch.empty_like(q)
+    s = scratch(q.device)
+    ext().prefill_attention(q, k_cache, v_cache, block_tables, ctx_lens, cu_q, out, sinks, int(window),
+                            float(scale), int(max_q_len), s.status)
+    return out
+
+
+def argmax(logits: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    ext().argmax(logits, out)
+    return out
+
+
+def sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, *, out=None, logprob=None):
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    ext().sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out, logprob)
+    return out

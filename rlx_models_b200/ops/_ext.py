@@ -1,0 +1,97 @@
+"""Loader for the in-tree sm_100a extension and per-device scratch buffers.
+
+The kernels live in ``rlx_models_b200/_C*.so`` (built by ``setup.py
+build_ext --inplace``). There is no silent fallback: if a CUDA device is
+present and the extension is missing, the first op call raises.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+_C = None
+_ERR = None
+try:  # the .so imports fine on machines without a GPU
+    from rlx_models_b200 import _C as _C  # type: ignore
+except Exception as e:  # pragma: no cover - only when not built
+    _ERR = e
+
+
+def ext():
+    if _C is None:
+        raise RuntimeError(
+            "rlx_models_b200._C is not built; run `python setup.py build_ext --inplace` "
+            f"(import error: {_ERR})")
+    return _C
+
+
+def available() -> bool:
+    return _C is not None and torch.cuda.is_available()
+
+
+class DeviceScratch:
+    """Scratch memory shared by all kernel launches on one device/stream order.
+
+    * ``status``: int32[4] device error word written by bounded waits.
+    * ``gemm_ws`` / ``gemm_sem``: split-K partial tiles and per-tile semaphores
+      (semaphores are self-resetting, so they start and stay zero).
+    * ``attn_ws``: split-KV partial outputs of decode attention.
+    """
+
+    GEMM_WS_ELEMS = 12 * 1024 * 1024  # fp32, 48 MB
+    GEMM_SEM_ELEMS = 65536
+    ATTN_WS_ELEMS = 8 * 1024 * 1024  # fp32, 32 MB
+
+    def __init__(self, device: torch.device):
+        self.device = device
+        self.status = torch.zeros(4, dtype=torch.int32, device=device)
+        self.gemm_ws = torch.empty(self.GEMM_WS_ELEMS, dtype=torch.float32, device=device)
+        self.gemm_sem = torch.zeros(self.GEMM_SEM_ELEMS, dtype=torch.int32, device=device)
+        self.attn_ws = torch.empty(self.ATTN_WS_ELEMS, dtype=torch.float32, device=device)
+
+    def check(self):
+        """Raise if any kernel on this device recorded an error (syncs)."""
+        st = self.status.cpu().tolist()
+        if st[0] != 0:
+            self.status.zero_()
+            raise KernelError(st)
+
+
+class KernelError(RuntimeError):
+    CODES = {
+        1: "TMA stage wait timed out", 2: "free-stage wait timed out",
+        3: "accumulator wait timed out", 4: "accumulator release wait timed out",
+        5: "peer flag wait timed out", 6: "split-K wait timed out", 7: "bounds check failed",
+        8: "drain wait timed out", 9: "test timeout",
+    }
+
+    def __init__(self, st):
+        self.code, self.block, self.thread, self.detail = st
+        super().__init__(
+            f"b200 kernel error {self.code} ({self.CODES.get(self.code, '?')}) "
+            f"block={self.block} thread={self.thread} detail={self.detail}")
+
+
+_scratch: dict[int, DeviceScratch] = {}
+_lock = threading.Lock()
+
+
+def scratch(device: torch.device | int | None = None) -> DeviceScratch:
+    if device is None:
+        device = torch.cuda.current_device()
+    idx = device.index if isinstance(device, torch.device) else int(device)
+    if idx is None:
+        idx = torch.cuda.current_device()
+    s = _scratch.get(idx)
+    if s is None:
+        with _lock:
+            s = _scratch.get(idx)
+            if s is None:
+                s = DeviceScratch(torch.device("cuda", idx))
+                _scratch[idx] = s
+    return s
+
+
+def check_errors(device=None):
+    scratch(device).check()

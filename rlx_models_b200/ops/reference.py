@@ -1,0 +1,67 @@
+"""Plain-PyTorch fp32 restatements of every kernel (test oracles, CPU path).
+
+These follow the HF module semantics that the reference mirrors and are the
+spec the CUDA kernels are tested against.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    var = xf.pow(2).mean(-1, keepdim=True)
+    return (xf * torch.rsqrt(var + eps)) * w.float()
+
+
+def rmsnorm_hf_bf16(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """Exact HF order for bf16 activations: normalise fp32, cast, scale by weight."""
+    xf = x.float()
+    var = xf.pow(2).mean(-1, keepdim=True)
+    return w * (xf * torch.rsqrt(var + eps)).to(x.dtype)
+
+
+def rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor, scale: float = 1.0) -> torch.Tensor:
+    """Half-split rotary embedding. x: [T, H, D], positions: [T]."""
+    freqs = positions.float()[:, None] * inv_freq.float()[None, :]
+    emb = torch.cat([freqs, freqs], dim=-1)
+    cos, sin = emb.cos() * scale, emb.sin() * scale
+    xf = x.float()
+    half = xf.shape[-1] // 2
+    rot = torch.cat([-xf[..., half:], xf[..., :half]], dim=-1)
+    return xf * cos[:, None, :] + rot * sin[:, None, :]
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    return F.silu(gate.float()) * up.float()
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Tensor, k_pos: torch.Tensor,
+              scale: float, causal: bool = True, window: int = 0, sinks: torch.Tensor | None = None) -> torch.Tensor:
+    """Dense GQA attention. q: [Tq, Hq, D], k/v: [Tk, Hkv, D]; returns [Tq, Hq, D] fp32."""
+    Hq, Hkv = q.shape[1], k.shape[1]
+    G = Hq // Hkv
+    kf = k.float().repeat_interleave(G, dim=1)
+    vf = v.float().repeat_interleave(G, dim=1)
+    s = torch.einsum("qhd,khd->hqk", q.float(), kf) * scale
+    mask = torch.ones(q.shape[0], k.shape[0], dtype=torch.bool, device=q.device)
+    if causal:
+        mask &= k_pos[None, :] <= q_pos[:, None]
+    if window > 0:
+        mask &= k_pos[None, :] > (q_pos[:, None] - window)
+    s = s.masked_fill(~mask[None], float("-inf"))
+    if sinks is not None:
+        sk = sinks.float()[:, None, None].expand(Hq, q.shape[0], 1)
+        s = torch.cat([s, sk], dim=-1)
+        p = torch.softmax(s, dim=-1)[..., :-1]
+    else:
+        p = torch.softmax(s, dim=-1)
+    return torch.einsum("hqk,khd->qhd", p, vf)
+
+
+def gather_paged(cache: torch.Tensor, block_table: torch.Tensor, length: int) -> torch.Tensor:
+    """cache [NB, Hkv, 16, D] + block list -> [length, Hkv, D]."""
+    nblk = (length + 15) // 16
+    pages = cache[block_table[:nblk].long()]  # [nblk, Hkv, 16, D]
+    return pages.permute(0, 2, 1, 3).reshape(nblk * 16, cache.shape[1], cache.shape[3])[:length]

@@ -1,0 +1,218 @@
+"""Numerics of every sm_100a kernel against the fp32 PyTorch oracle.
+
+Small and odd shapes (M, N, K not multiples of the tile) exercise the TMA
+out-of-bounds fill and the epilogue masks; split-K and both GEMM orientations
+are forced explicitly.
+"""
+import math
+
+import pytest
+import torch
+
+from rlx_models_b200 import ops
+from rlx_models_b200.ops import reference as ref
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm().clamp_min(1e-6)).item()
+
+
+def _mk(shape, dev, scale=1.0, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(dev, torch.bfloat16)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 256, 64), (7, 384, 192), (64, 4096, 4096), (129, 512, 320),
+                                   (300, 768, 1024), (512, 2048, 512), (1000, 1280, 2048)])
+@pytest.mark.parametrize("swap", [-1, 0, 1])
+def test_linear_bf16(cuda, M, N, K, swap):
+    if swap == 1 and M > 256:
+        pytest.skip("swap-AB only for skinny M")
+    x, w = _mk((M, K), cuda, 1.0, 1), _mk((N, K), cuda, 0.05, 2)
+    y = ops.linear(x, w, swap=swap)
+    ops.check_errors(cuda)
+    r = x.float() @ w.float().T
+    assert rel_err(y, r) < 1e-2
+
+
+@pytest.mark.parametrize("splits", [1, 2, 5])
+@pytest.mark.parametrize("M", [16, 200])
+def test_linear_splitk_residual_bias_f32(cuda, splits, M):
+    N, K = 640, 1536
+    x, w = _mk((M, K), cuda, 1.0, 3), _mk((N, K), cuda, 0.05, 4)
+    res, b = _mk((M, N), cuda, 1.0, 5), _mk((N,), cuda, 1.0, 6)
+    y = ops.linear(x, w, residual=res, bias=b, splits=splits)
+    r = x.float() @ w.float().T + b.float() + res.float()
+    assert rel_err(y, r) < 1e-2
+    y32 = ops.linear(x, w, out_dtype=torch.float32, alpha=0.5, splits=splits)
+    assert rel_err(y32, 0.5 * (x.float() @ w.float().T)) < 5e-3
+    ops.check_errors(cuda)
+    # semaphores must be self-resetting: a second identical call gives the same result
+    y2 = ops.linear(x, w, residual=res, bias=b, splits=splits)
+    assert torch.equal(y, y2)
+
+
+@pytest.mark.parametrize("M", [1, 33, 64, 128, 257, 1024])
+def test_linear_swiglu(cuda, M):
+    I, K = 768, 1024
+    x = _mk((M, K), cuda, 1.0, 7)
+    wg, wu = _mk((I, K), cuda, 0.05, 8), _mk((I, K), cuda, 0.05, 9)
+    wgu = ops.interleave_gate_up(wg, wu)
+    y = ops.linear_swiglu(x, wgu)
+    r = ref.swiglu(x.float() @ wg.float().T, x.float() @ wu.float().T)
+    assert rel_err(y, r) < 1.5e-2
+    ops.check_errors(cuda)
+
+
+def test_rmsnorm_residual(cuda):
+    T, H = 37, 4096
+    x, res, w = _mk((T, H), cuda, 1.0, 10), _mk((T, H), cuda, 1.0, 11), _mk((H,), cuda, 1.0, 12)
+    res_out = torch.empty_like(res)
+    y = ops.rmsnorm(x, w, 1e-6, residual=res, residual_out=res_out)
+    s = (x.float() + res.float()).bfloat16()
+    assert torch.equal(res_out, s)
+    assert rel_err(y, ref.rmsnorm(s, w, 1e-6)) < 1e-2
+    y2 = ops.rmsnorm(x, w, 1e-6)
+    assert rel_err(y2, ref.rmsnorm(x, w, 1e-6)) < 1e-2
+
+
+def test_embedding(cuda):
+    V, H = 1000, 512
+    tab = _mk((V, H), cuda, 1.0, 13)
+    ids = torch.randint(0, V, (77,), dtype=torch.int32, device=cuda)
+    assert torch.equal(ops.embedding(ids, tab), tab[ids.long()])
+
+
+@pytest.mark.parametrize("D,Hq,Hkv", [(128, 32, 8), (64, 8, 1)])
+def test_qkv_rope_cache_write(cuda, D, Hq, Hkv):
+    T = 40
+    qkv = _mk((T, (Hq + 2 * Hkv) * D), cuda, 1.0, 14)
+    qn, kn = _mk((D,), cuda, 1.0, 15), _mk((D,), cuda, 1.0, 16)
+    pos = torch.randint(0, 3000, (T,), dtype=torch.int32, device=cuda)
+    inv, _ = ops.rope_inv_freq(D, 1e6)
+    inv = inv.to(cuda)
+    NB = 16
+    kc = torch.zeros(NB, Hkv, 16, D, dtype=torch.bfloat16, device=cuda)
+    vc = torch.zeros_like(kc)
+    slots = torch.randperm(NB * 16, device=cuda)[:T].long()
+    q = ops.qkv_rope(qkv, num_q_heads=Hq, num_kv_heads=Hkv, head_dim=D, positions=pos, inv_freq=inv,
+                     q_norm=qn, k_norm=kn, eps=1e-6, slots=slots, k_cache=kc, v_cache=vc)
+    qr = qkv[:, :Hq * D].view(T, Hq, D)
+    kr = qkv[:, Hq * D:(Hq + Hkv) * D].view(T, Hkv, D)
+    vr = qkv[:, (Hq + Hkv) * D:].view(T, Hkv, D)
+    q_ref = ref.rope(ref.rmsnorm_hf_bf16(qr, qn, 1e-6), pos, inv)
+    k_ref = ref.rope(ref.rmsnorm_hf_bf16(kr, kn, 1e-6), pos, inv)
+    assert rel_err(q, q_ref) < 1e-2
+    blk, off = slots // 16, slots % 16
+    kg = kc[blk, :, off]  # [T, Hkv, D]
+    vg = vc[blk, :, off]
+    assert rel_err(kg, k_ref) < 1e-2
+    assert torch.equal(vg, vr)
+
+
+def _paged_setup(dev, B, Hkv, D, lens, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    maxb = max((l + 15) // 16 for l in lens)
+    NB = sum((l + 15) // 16 for l in lens) + 3
+    perm = torch.randperm(NB, generator=g)
+    tables = torch.zeros(B, maxb, dtype=torch.int32)
+    c = 0
+    for b, l in enumerate(lens):
+        n = (l + 15) // 16
+        tables[b, :n] = perm[c:c + n].int()
+        c += n
+    kc = (torch.randn(NB, Hkv, 16, D, generator=g)).to(dev, torch.bfloat16)
+    vc = (torch.randn(NB, Hkv, 16, D, generator=g)).to(dev, torch.bfloat16)
+    return tables.to(dev), kc, vc
+
+
+@pytest.mark.parametrize("D,Hq,Hkv", [(128, 32, 8), (128, 4, 1), (64, 64, 8)])
+@pytest.mark.parametrize("splits", [0, 1, 3])
+@pytest.mark.parametrize("window,use_sinks", [(0, False), (128, True)])
+def test_decode_attention(cuda, D, Hq, Hkv, splits, window, use_sinks):
+    lens = [1, 15, 16, 17, 100, 513, 2047]
+    B = len(lens)
+    tables, kc, vc = _paged_setup(cuda, B, Hkv, D, lens)
+    q = _mk((B, Hq, D), cuda, 1.0, 20)
+    ctx = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    sinks = torch.randn(Hq, device=cuda) if use_sinks else None
+    scale = 1 / math.sqrt(D)
+    out = ops.decode_attention(q, kc, vc, tables, ctx, scale=scale, sinks=sinks, window=window, splits=splits)
+    ops.check_errors(cuda)
+    for b, l in enumerate(lens):
+        k = ref.gather_paged(kc, tables[b], l)
+        v = ref.gather_paged(vc, tables[b], l)
+        pos = torch.arange(l, device=cuda)
+        r = ref.attention(q[b:b + 1], k, v, pos[-1:], pos, scale, causal=True, window=window, sinks=sinks)
+        assert rel_err(out[b:b + 1], r) < 2e-2, (b, l)
+
+
+@pytest.mark.parametrize("D,Hq,Hkv", [(128, 32, 8), (128, 16, 8), (64, 64, 8), (128, 24, 24)])
+@pytest.mark.parametrize("window,use_sinks", [(0, False), (128, True)])
+def test_prefill_attention_chunked(cuda, D, Hq, Hkv, window, use_sinks):
+    # (q_len, ctx_len): ctx > q_len means earlier tokens are already cached
+    cfg = [(1, 1), (17, 17), (70, 300), (257, 257), (33, 1000)]
+    B = len(cfg)
+    lens = [c for _, c in cfg]
+    tables, kc, vc = _paged_setup(cuda, B, Hkv, D, lens, seed=3)
+    qlens = [q for q, _ in cfg]
+    cu = torch.tensor([0] + list(torch.tensor(qlens).cumsum(0)), dtype=torch.int32, device=cuda)
+    q = _mk((sum(qlens), Hq, D), cuda, 1.0, 21)
+    ctx = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    sinks = torch.randn(Hq, device=cuda) if use_sinks else None
+    scale = 1 / math.sqrt(D)
+    out = ops.prefill_attention(q, kc, vc, tables, ctx, cu, max(qlens), scale=scale, sinks=sinks, window=window)
+    ops.check_errors(cuda)
+    for b, (ql, l) in enumerate(cfg):
+        k = ref.gather_paged(kc, tables[b], l)
+        v = ref.gather_paged(vc, tables[b], l)
+        kpos = torch.arange(l, device=cuda)
+        qpos = kpos[l - ql:]
+        r = ref.attention(q[cu[b]:cu[b + 1]], k, v, qpos, kpos, scale, causal=True, window=window, sinks=sinks)
+        assert rel_err(out[cu[b]:cu[b + 1]], r) < 2e-2, (b, ql, l)
+
+
+def test_argmax_and_greedy_sample(cuda):
+    B, V = 9, 151936
+    logits = torch.randn(B, V, device=cuda)
+    logits[3, 777] = 100.0
+    am = ops.argmax(logits)
+    assert torch.equal(am.long(), logits.argmax(-1))
+    z = torch.zeros(B, device=cuda)
+    one = torch.ones(B, device=cuda)
+    k0 = torch.zeros(B, dtype=torch.int32, device=cuda)
+    seeds = torch.arange(B, dtype=torch.int64, device=cuda)
+    offs = torch.zeros(B, dtype=torch.int64, device=cuda)
+    s = ops.sample(logits, z, k0, one, z, seeds, offs)
+    assert torch.equal(s.long(), logits.argmax(-1))
+    # top-k = 1 at any temperature is greedy
+    s1 = ops.sample(logits, one, torch.ones(B, dtype=torch.int32, device=cuda), one, z, seeds, offs)
+    assert torch.equal(s1.long(), logits.argmax(-1))
+
+
+def test_sampling_distribution(cuda):
+    V, N = 64, 4000
+    base = torch.randn(V) * 2
+    logits = base[None].repeat(N, 1).to(cuda)
+    T = torch.full((N,), 0.7, device=cuda)
+    k0 = torch.zeros(N, dtype=torch.int32, device=cuda)
+    one = torch.ones(N, device=cuda)
+    z = torch.zeros(N, device=cuda)
+    seeds = torch.arange(N, dtype=torch.int64, device=cuda) * 7919
+    offs = torch.zeros(N, dtype=torch.int64, device=cuda)
+    s = ops.sample(logits, T, k0, one, z, seeds, offs).long().cpu()
+    emp = torch.bincount(s, minlength=V).float() / N
+    p = torch.softmax(base / 0.7, -1)
+    assert (emp - p).abs().max() < 0.04
+    # top-p: every draw must come from the nucleus
+    tp = torch.full((N,), 0.5, device=cuda)
+    s2 = ops.sample(logits, T, k0, tp, z, seeds, offs).long().cpu()
+    srt, idx = p.sort(descending=True)
+    n_keep = int((srt.cumsum(0) < 0.5).sum()) + 1
+    assert set(s2.tolist()) <= set(idx[:n_keep].tolist())
+    # top-k = 3
+    s3 = ops.sample(logits, T, torch.full((N,), 3, dtype=torch.int32, device=cuda), one, z, seeds, offs)
+    assert set(s3.long().cpu().tolist()) <= set(idx[:3].tolist())
