@@ -1,0 +1,120 @@
+"""High-level API: ``load(model)`` -> :class:`LLM` with generate / stream / logits.
+
+The B200 counterpart of the reference's runner builders and `auto_runner`
+(rlx-qwen3 src/high_level_runner.rs:90-181 `Qwen3Runner::builder()...build()`,
+:515-970 `generate` / `predict_logits` / `cache_prefix`; rlx-models
+src/run.rs:76-175 `auto_runner`, which sniffs the architecture from the
+checkpoint). ``model`` may be
+
+* a local directory with ``config.json`` + safetensors (HF layout, same tensor
+  names as the reference's loaders),
+* an HF repo id resolved offline from the local HF cache (``org/name``), or
+* a named shape (``qwen3-0.6b``, ``qwen3-8b``, ``gpt-oss-120b`` ...) with seeded
+  random weights, which is what the benchmarks use.
+"""
+from __future__ import annotations
+
+import os
+from typing import Iterator
+
+import torch
+
+from . import config as C
+from .registry import build_model
+from .runtime.engine import EngineConfig, LLMEngine, RequestOutput, SamplingParams
+from .weights.weight_map import WeightMap
+
+
+def resolve_model_path(model: str) -> str | None:
+    """Local dir, or an HF id found in the offline HF cache (snapshots/<rev>)."""
+    if os.path.isdir(model):
+        return model
+    if "/" in model:
+        name, _, rev = model.partition("@")
+        root = os.environ.get("HF_HUB_CACHE") or os.path.join(
+            os.environ.get("HF_HOME", os.path.expanduser("~/.cache/huggingface")), "hub")
+        d = os.path.join(root, "models--" + name.replace("/", "--"), "snapshots")
+        if os.path.isdir(d):
+            snaps = sorted(os.listdir(d))
+            if rev and rev in snaps:
+                return os.path.join(d, rev)
+            if snaps:
+                return os.path.join(d, snaps[-1])
+    return None
+
+
+class LLM:
+    """A loaded language model plus its serving engine (one process, TP rank)."""
+
+    def __init__(self, model, engine_config: EngineConfig | None = None, tokenizer=None):
+        self.model = model
+        self.engine = LLMEngine(model, engine_config)
+        self.tokenizer = tokenizer
+
+    @property
+    def config(self):
+        return self.model.cfg
+
+    def _encode(self, p):
+        if isinstance(p, str):
+            if self.tokenizer is None:
+                raise ValueError("string prompts need a tokenizer")
+            return self.tokenizer.encode(p)
+        return list(p)
+
+    def generate(self, prompts, params: SamplingParams | list[SamplingParams] | None = None) -> list[RequestOutput]:
+        single = isinstance(prompts, str) or (prompts and isinstance(prompts[0], int))
+        plist = [prompts] if single else list(prompts)
+        outs = self.engine.generate([self._encode(p) for p in plist], params)
+        return outs[:1] if single else outs
+
+    def stream(self, prompt, params: SamplingParams | None = None) -> Iterator[int]:
+        """Yield tokens of one request as they are produced."""
+        sid = self.engine.add_request(self._encode(prompt), params)
+        seen = 0
+        while True:
+            done = {o.seq_id: o for o in self.engine.step()}
+            st = self.engine.requests.get(sid)
+            toks = done[sid].token_ids if sid in done else (st.tokens if st else [])
+            for t in toks[seen:]:
+                yield t
+            seen = len(toks)
+            if sid in done or not self.engine.has_unfinished():
+                return
+
+    @torch.no_grad()
+    def logits(self, prompt) -> torch.Tensor:
+        """fp32 next-token logits for every prompt position (prefill only)."""
+        from .models.decoder import ForwardBatch
+        ids = self._encode(prompt)
+        T = len(ids)
+        dev = self.model.device
+        kv = self.model.make_kv_cache((T + 15) // 16)
+        nb = (T + 15) // 16
+        fb = ForwardBatch(input_ids=torch.tensor(ids, dtype=torch.int32, device=dev),
+                          positions=torch.arange(T, dtype=torch.int32, device=dev),
+                          slots=torch.arange(T, dtype=torch.int64, device=dev), num_decode=0,
+                          pre_block_tables=torch.arange(nb, dtype=torch.int32, device=dev).view(1, -1),
+                          pre_ctx_lens=torch.tensor([T], dtype=torch.int32, device=dev),
+                          pre_cu_q=torch.tensor([0, T], dtype=torch.int32, device=dev), pre_max_q=T)
+        return self.model.forward(fb, kv)
+
+
+def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, tp_size: int = 1, comm=None,
+         seed: int = 0, engine_config: EngineConfig | None = None, config: C.DecoderConfig | None = None) -> LLM:
+    """Load a model by path, HF id (offline cache) or named shape (random init)."""
+    path = resolve_model_path(model)
+    tok = None
+    if path is not None:
+        cfg = config or C.DecoderConfig.from_file(path)
+        weights = WeightMap.from_dir(path)
+        try:
+            from .tokenizer import load_tokenizer
+            tok = load_tokenizer(path)
+        except Exception:
+            tok = None
+    else:
+        cfg = config or C.preset(model)
+        weights = None  # random init on the device, per rank
+    m = build_model(cfg, weights, device=device, tp_rank=tp_rank, tp_size=tp_size, comm=comm, seed=seed)
+    return LLM(m, engine_config, tok)

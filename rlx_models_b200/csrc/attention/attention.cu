@@ -533,9 +533,9 @@ static void set_smem(K kern, int bytes, int device) {
 
 }  // namespace attn
 
-void decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
+int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
   using namespace attn;
-  if (a.B == 0) return;
+  if (a.B == 0) return 0;
   const int G = a.Hq / a.Hkv;
   if (G > 16 || a.Hq % a.Hkv != 0) throw std::runtime_error("b200.decode_attention: G must divide and be <= 16");
   if (a.D != 128 && a.D != 64) throw std::runtime_error("b200.decode_attention: D must be 64 or 128");
@@ -567,6 +567,7 @@ void decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
     k<<<grid, 160, DecCfg<64, NST>::SMEM, st>>>(tk, tv, a);
     if (splits > 1) decode_merge_kernel<64><<<a.B * a.Hq, 64, 0, st>>>(a, splits);
   }
+  return splits > 1 ? 2 : 1;
 }
 
 void prefill_attention_launch(const AttnArgs& a, cudaStream_t st) {

@@ -187,9 +187,9 @@ static b200::AttnArgs attn_args(const Tensor& q, const Tensor& k_cache, const Te
   return a;
 }
 
-void decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& block_tables,
-                      const Tensor& ctx_lens, Tensor& out, const optional<Tensor>& sinks, int64_t window,
-                      double scale, int64_t splits, Tensor& ws, Tensor& status) {
+int64_t decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& block_tables,
+                         const Tensor& ctx_lens, Tensor& out, const optional<Tensor>& sinks, int64_t window,
+                         double scale, int64_t splits, Tensor& ws, Tensor& status) {
   c10::cuda::CUDAGuard g(q.device());
   auto a = attn_args(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, window, scale, status);
   TORCH_CHECK(q.size(0) == block_tables.size(0), "b200.decode_attention: one query per sequence");
@@ -197,8 +197,9 @@ void decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_ca
   a.splits = (int)splits;
   a.ws = ws.numel() ? ws.data_ptr<float>() : nullptr;
   a.ws_elems = ws.numel();
-  b200::decode_attention_launch(a, cur_stream(q));
+  const int n = b200::decode_attention_launch(a, cur_stream(q));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  return n;
 }
 
 void prefill_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& block_tables,

@@ -83,7 +83,7 @@ struct AttnArgs {
   int* status;
   int device;
 };
-void decode_attention_launch(const AttnArgs& a, cudaStream_t st);
+int decode_attention_launch(const AttnArgs& a, cudaStream_t st);  // returns #launches
 void prefill_attention_launch(const AttnArgs& a, cudaStream_t st);
 
 // ---------------- sampling ----------------

@@ -89,8 +89,8 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
   p.splits = (p.k_tiles + p.kt_per_split - 1) / p.kt_per_split;
   p.num_units = tiles * p.splits;
   if (p.splits > 1) {
-    if (a.ws_elems < (int64_t)p.num_units * gemm::kBM * BN || a.ws == nullptr)
-      throw std::runtime_error("b200.linear: split-K workspace too small");
+    if (a.ws_elems < (int64_t)tiles * gemm::kBM * BN || a.ws == nullptr)
+      throw std::runtime_error("b200.linear: split-K accumulator too small");
     if (a.sem_elems < tiles || a.sem == nullptr) throw std::runtime_error("b200.linear: semaphore buffer too small");
   }
   p.C = a.out;

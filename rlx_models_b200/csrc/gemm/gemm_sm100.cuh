@@ -19,9 +19,10 @@
 //               epilogue -> global, overlapping the next tile's MMAs.
 //
 // Split-K (used for skinny decode GEMMs so that all SMs stream weights): each
-// split writes an fp32 partial tile to a workspace; the last split of a tile
-// (per-tile semaphore) sums the partials and runs the real epilogue, then
-// resets the semaphore so the next launch (or graph replay) starts from zero.
+// split adds its fp32 partial tile into a per-tile L2 accumulator with vector
+// red.global.add; the last split of a tile (per-tile semaphore) reads the sum
+// once, zeroes the accumulator, runs the real epilogue and resets the
+// semaphore, so the next launch (or graph replay) starts from zero.
 #pragma once
 
 #include "../common/b200.cuh"
@@ -60,7 +61,7 @@ struct Cfg {
   static constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN >= 256) ? 4 : (BN >= 128 ? 6 : 8);
   static constexpr uint32_t TMEM_COLS = (2 * BN < 32) ? 32 : 2 * BN;
-  static constexpr uint32_t XCHG_BYTES = 64 * 33 * 4;  // swap-SwiGLU gate/up exchange
+  static constexpr uint32_t XCHG_BYTES = 32 * 132 * 4;  // swap-AB transpose stage [32 tok][128 feat]
   static constexpr uint32_t SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + XCHG_BYTES + 256;
 };
 
@@ -144,6 +145,80 @@ __device__ __forceinline__ void store_chunk(const Params& p, int i, int j0, floa
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + __expf(-g)) * u; }
+
+// Swap-AB output row: token j, features [fo, fo+32) (contiguous in C / R / bias).
+template <int EPI>
+__device__ __forceinline__ void store_row32(const Params& p, int j, int fo, int nfeat, float (&o)[32]) {
+  const bool full = fo + 32 <= nfeat;
+  if (p.bias != nullptr) {
+    if (full && ((reinterpret_cast<uintptr_t>(p.bias + fo) & 15u) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 w = *reinterpret_cast<const uint4*>(p.bias + fo + q * 8);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          o[q * 8 + 2 * h] += bf16_lo(ww[h]);
+          o[q * 8 + 2 * h + 1] += bf16_hi(ww[h]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        if (fo + t < nfeat) o[t] += __bfloat162float(p.bias[fo + t]);
+    }
+  }
+  if (p.R != nullptr) {
+    const __nv_bfloat16* r = p.R + (int64_t)j * p.ldr_j + fo;
+    if (full && ((reinterpret_cast<uintptr_t>(r) & 15u) == 0)) {
+      uint4 w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) w[q] = *reinterpret_cast<const uint4*>(r + q * 8);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint32_t ww[4] = {w[q].x, w[q].y, w[q].z, w[q].w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          o[q * 8 + 2 * h] += bf16_lo(ww[h]);
+          o[q * 8 + 2 * h + 1] += bf16_hi(ww[h]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        if (fo + t < nfeat) o[t] += __bfloat162float(r[t]);
+    }
+  }
+  if (EPI == EPI_F32) {
+    float* c = reinterpret_cast<float*>(p.C) + (int64_t)j * p.ldc_j + fo;
+    if (full && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        *reinterpret_cast<float4*>(c + q * 4) = make_float4(o[q * 4], o[q * 4 + 1], o[q * 4 + 2], o[q * 4 + 3]);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        if (fo + t < nfeat) c[t] = o[t];
+    }
+  } else {
+    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (int64_t)j * p.ldc_j + fo;
+    if (full && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        w.x = pack_bf16x2(o[q * 8 + 0], o[q * 8 + 1]);
+        w.y = pack_bf16x2(o[q * 8 + 2], o[q * 8 + 3]);
+        w.z = pack_bf16x2(o[q * 8 + 4], o[q * 8 + 5]);
+        w.w = pack_bf16x2(o[q * 8 + 6], o[q * 8 + 7]);
+        *reinterpret_cast<uint4*>(c + q * 8) = w;
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        if (fo + t < nfeat) c[t] = __float2bfloat16(o[t]);
+    }
+  }
+}
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -291,6 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const int ew = warp - 2;
+    const int et = ew * 32 + lane;  // 0..127 epilogue thread id
+    const bool swap_out = (p.ldc_i == 1);
     int it = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++it) {
       int m_tile, n_tile, ks, tile;
@@ -305,10 +382,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
       const int i = m_tile * kBM + row;
       const int jt = n_tile * BN;
+      // fp32 accumulator of this tile in L2 (split-K); zero between uses
+      float* acc_row = p.ws + (int64_t)tile * (kBM * BN) + (int64_t)row * BN;
 
       if (p.splits > 1) {
-        // Park this split's fp32 partial tile in the workspace.
-        float* wsp = p.ws + ((int64_t)tile * p.splits + ks) * (kBM * BN) + (int64_t)row * BN;
+        // Add this split's partial into the shared fp32 tile (fire-and-forget
+        // vector reductions in L2), release TMEM, then count arrivals.
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -316,16 +395,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld();
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            __stcg(reinterpret_cast<float4*>(wsp + c * 32 + q * 4),
-                   make_float4(__uint_as_float(r[q * 4]), __uint_as_float(r[q * 4 + 1]),
-                               __uint_as_float(r[q * 4 + 2]), __uint_as_float(r[q * 4 + 3])));
+            red_add_v4(acc_row + c * 32 + q * 4, __uint_as_float(r[q * 4]), __uint_as_float(r[q * 4 + 1]),
+                       __uint_as_float(r[q * 4 + 2]), __uint_as_float(r[q * 4 + 3]));
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&acce[acc]);
         __threadfence();
         named_bar_sync(1, 128);
-        if (ew == 0 && lane == 0) {
+        if (et == 0) {
           const int old = atomicAdd(&p.sem[tile], 1);
           *s_last = (old == p.splits - 1) ? 1 : 0;
         }
@@ -337,19 +415,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Fetch 32 accumulator columns [c*32, c*32+32) of this thread's row.
       auto fetch = [&](int c, float (&v)[32]) {
         if (p.splits > 1) {
-          const float* base = p.ws + (int64_t)tile * p.splits * (kBM * BN) + (int64_t)row * BN + c * 32;
+          float4 w[8];
 #pragma unroll
-          for (int t = 0; t < 32; ++t) v[t] = 0.f;
-          for (int s = 0; s < p.splits; ++s) {
-            const float4* src = reinterpret_cast<const float4*>(base + (int64_t)s * (kBM * BN));
+          for (int q = 0; q < 8; ++q) w[q] = __ldcg(reinterpret_cast<const float4*>(acc_row + c * 32) + q);
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              float4 w = __ldcg(src + q);
-              v[q * 4] += w.x;
-              v[q * 4 + 1] += w.y;
-              v[q * 4 + 2] += w.z;
-              v[q * 4 + 3] += w.w;
-            }
+          for (int q = 0; q < 8; ++q) {
+            v[q * 4] = w[q].x;
+            v[q * 4 + 1] = w[q].y;
+            v[q * 4 + 2] = w[q].z;
+            v[q * 4 + 3] = w[q].w;
+            __stcg(reinterpret_cast<float4*>(acc_row + c * 32) + q, make_float4(0.f, 0.f, 0.f, 0.f));
           }
         } else {
           uint32_t r[32];
@@ -360,7 +435,43 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       };
 
-      if (EPI == EPI_SWIGLU && !p.swiglu_on_i) {
+      if (swap_out) {
+        // A rows are output features, B rows are tokens: stage [32 tokens][128
+        // features] in smem, then write each token's features as 16B vectors.
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          fetch(c, v);
+#pragma unroll
+          for (int t = 0; t < 32; ++t) xchg[t * 132 + row] = v[t];
+          named_bar_sync(2, 128);
+          const int tl = et >> 2, seg = et & 3;  // token within chunk, 32-feature segment
+          const int j = jt + c * 32 + tl;
+          float o[32];
+          int fo;       // first output feature of this segment
+          bool active;
+          if (EPI == EPI_SWIGLU) {
+            active = seg < 2;
+            fo = m_tile * 64 + seg * 32;
+#pragma unroll
+            for (int t = 0; t < 32; ++t) {
+              const float g = xchg[tl * 132 + seg * 32 + t] * p.alpha;
+              const float uu = xchg[tl * 132 + 64 + seg * 32 + t] * p.alpha;
+              o[t] = silu_mul(g, uu);
+            }
+          } else {
+            active = true;
+            fo = m_tile * kBM + seg * 32;
+#pragma unroll
+            for (int t = 0; t < 32; ++t) o[t] = xchg[tl * 132 + seg * 32 + t] * p.alpha;
+          }
+          named_bar_sync(2, 128);
+          const int nfeat = (EPI == EPI_SWIGLU) ? p.MA / 2 : p.MA;
+          if (active && j < p.NB && fo < nfeat) {
+            store_row32<EPI>(p, j, fo, nfeat, o);
+          }
+        }
+      } else if (EPI == EPI_SWIGLU) {
         // gate/up interleaved along j in groups of 64 columns: [g*128, g*128+64) gate, +64 up.
 #pragma unroll 1
         for (int g = 0; g < BN / 128; ++g) {
@@ -378,28 +489,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             store_chunk<BN, EPI_BF16>(q, i, (jt + g * 128) / 2 + h * 32, vg);
           }
         }
-      } else if (EPI == EPI_SWIGLU) {
-        // gate/up interleaved along i: tile rows [0,64) gate, [64,128) up of the same features.
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          fetch(c, v);
-          if (quad >= 2) {
-#pragma unroll
-            for (int t = 0; t < 32; ++t) xchg[((quad - 2) * 32 + lane) * 33 + t] = v[t];
-          }
-          named_bar_sync(2, 128);
-          if (quad < 2) {
-#pragma unroll
-            for (int t = 0; t < 32; ++t) v[t] = silu_mul(v[t] * p.alpha, xchg[(quad * 32 + lane) * 33 + t] * p.alpha);
-            Params q = p;
-            q.alpha = 1.f;
-            q.MA = p.MA / 2;
-            q.bias = nullptr;
-            store_chunk<BN, EPI_BF16>(q, m_tile * 64 + quad * 32 + lane, jt + c * 32, v);
-          }
-          named_bar_sync(2, 128);
-        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -410,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       if (p.splits > 1) {
-        if (ew == 0 && lane == 0) p.sem[tile] = 0;
+        if (et == 0) p.sem[tile] = 0;
       } else {
         tc_fence_before();
         __syncwarp();

@@ -1,0 +1,190 @@
+"""GPU decoder (Qwen3 / Llama / Qwen2 dense families) on the sm_100a kernels.
+
+One generic decoder driven by :class:`~rlx_models_b200.config.DecoderConfig`,
+the B200 counterpart of the reference's `DecoderSpec` builder
+(rlx-models-core src/standard_decoder.rs:172-312, `build_standard_decoder_packed`
+:12210) and the Qwen3 flow (rlx-qwen3 src/flow.rs:310-434 prefill,
+:558-690 decode). Weights are re-laid out once at load for the kernels:
+
+* q/k/v fused into one [q + 2kv, H] matrix (one GEMM, one TMA stream),
+* gate/up interleaved in groups of 64 rows so the GEMM epilogue applies SwiGLU,
+* o_proj / down_proj GEMMs add the residual in their epilogue (in place).
+
+A forward step works on a flat token batch: ``num_decode`` single-token decode
+sequences first, then chunked-prefill segments, all sharing the GEMMs; the
+attention kernels read/write the paged cache. Tensor parallelism shards heads
+and the MLP intermediate dimension; the partial o/down outputs are combined by
+the communicator (``comm``) — by the fused GEMM+reduce kernels over NVLink
+peer memory, or NCCL as the baseline.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .. import ops
+from ..config import DecoderConfig
+from ..ops import interleave_gate_up, rope_inv_freq
+from ..runtime.kv_cache import PagedKVCache
+
+
+@dataclass
+class ForwardBatch:
+    """Device tensors describing one engine step."""
+    input_ids: torch.Tensor        # [T] int32
+    positions: torch.Tensor        # [T] int32
+    slots: torch.Tensor            # [T] int64 cache slot per token
+    num_decode: int                # first num_decode tokens are decode tokens (1 per sequence)
+    dec_block_tables: torch.Tensor | None = None  # [Bd, maxb] int32
+    dec_ctx_lens: torch.Tensor | None = None      # [Bd] int32 (incl. the new token)
+    pre_block_tables: torch.Tensor | None = None  # [Bp, maxb] int32
+    pre_ctx_lens: torch.Tensor | None = None      # [Bp] int32
+    pre_cu_q: torch.Tensor | None = None          # [Bp + 1] int32 offsets into the prefill tokens
+    pre_max_q: int = 0
+    logit_rows: torch.Tensor | None = None        # [R] int64 rows needing logits
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.input_ids.shape[0])
+
+
+class LayerWeights:
+    __slots__ = ("ln1", "ln2", "wqkv", "bqkv", "q_norm", "k_norm", "wo", "bo", "w_gu", "wd", "sinks", "window")
+
+
+class DecoderLM:
+    def __init__(self, cfg: DecoderConfig, weights, device: torch.device | str = "cuda",
+                 tp_rank: int = 0, tp_size: int = 1, comm=None):
+        assert not cfg.is_moe, "MoE families use models.moe.MoEDecoderLM"
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.tp_rank, self.tp_size, self.comm = tp_rank, tp_size, comm
+        c = cfg
+        assert c.num_attention_heads % tp_size == 0 and c.num_key_value_heads % tp_size == 0
+        self.hq = c.num_attention_heads // tp_size
+        self.hkv = c.num_key_value_heads // tp_size
+        self.D = c.head_dim
+        self.inter = c.intermediate_size // tp_size
+        assert self.inter % ops.SWIGLU_GROUP == 0
+        inv, mult = rope_inv_freq(c.head_dim, c.rope_theta, c.rope_scaling, c.max_position_embeddings)
+        self.inv_freq = inv.to(self.device)
+        self.rope_mult = mult
+        self.scale = 1.0 / math.sqrt(c.head_dim)
+        self._load(weights)
+
+    # -- weights ---------------------------------------------------------------
+    def _get(self, w, name):
+        t = w.take(name) if hasattr(w, "take") else w[name]
+        return t
+
+    def _rows(self, t: torch.Tensor, per_rank: int, rank_parts: int = 1) -> torch.Tensor:
+        """Rank slice of dim 0 (column-parallel)."""
+        return t.narrow(0, self.tp_rank * per_rank, per_rank)
+
+    def _cols(self, t: torch.Tensor, per_rank: int) -> torch.Tensor:
+        """Rank slice of dim 1 (row-parallel)."""
+        return t.narrow(1, self.tp_rank * per_rank, per_rank)
+
+    def _load(self, w):
+        c, dev, bf = self.cfg, self.device, torch.bfloat16
+        D = self.D
+
+        def g(name):
+            return self._get(w, name)
+
+        def dv(t):
+            return t.to(device=dev, dtype=bf).contiguous()
+
+        self.embed = dv(g("model.embed_tokens.weight"))
+        self.norm = dv(g("model.norm.weight"))
+        if c.tie_word_embeddings:
+            head = self.embed
+        else:
+            head = dv(g("lm_head.weight"))
+        V = c.vocab_size
+        if self.tp_size > 1:
+            assert V % self.tp_size == 0
+            self.lm_head = head.narrow(0, self.tp_rank * (V // self.tp_size), V // self.tp_size).contiguous()
+        else:
+            self.lm_head = head
+        self.layers: list[LayerWeights] = []
+        for i in range(c.num_hidden_layers):
+            p = f"model.layers.{i}."
+            L = LayerWeights()
+            L.ln1 = dv(g(p + "input_layernorm.weight"))
+            L.ln2 = dv(g(p + "post_attention_layernorm.weight"))
+            q = self._rows(g(p + "self_attn.q_proj.weight"), self.hq * D)
+            k = self._rows(g(p + "self_attn.k_proj.weight"), self.hkv * D)
+            v = self._rows(g(p + "self_attn.v_proj.weight"), self.hkv * D)
+            L.wqkv = dv(torch.cat([q.to(dev), k.to(dev), v.to(dev)], 0))
+            L.bqkv = None
+            if c.attention_bias:
+                qb = self._rows(g(p + "self_attn.q_proj.bias"), self.hq * D)
+                kb = self._rows(g(p + "self_attn.k_proj.bias"), self.hkv * D)
+                vb = self._rows(g(p + "self_attn.v_proj.bias"), self.hkv * D)
+                L.bqkv = dv(torch.cat([qb.to(dev), kb.to(dev), vb.to(dev)]))
+            L.q_norm = dv(g(p + "self_attn.q_norm.weight")) if c.qk_norm else None
+            L.k_norm = dv(g(p + "self_attn.k_norm.weight")) if c.qk_norm else None
+            L.wo = dv(self._cols(g(p + "self_attn.o_proj.weight"), self.hq * D))
+            L.bo = None
+            gt = self._rows(g(p + "mlp.gate_proj.weight"), self.inter)
+            up = self._rows(g(p + "mlp.up_proj.weight"), self.inter)
+            L.w_gu = interleave_gate_up(gt.to(dev, bf), up.to(dev, bf))
+            L.wd = dv(self._cols(g(p + "mlp.down_proj.weight"), self.inter))
+            L.sinks = None
+            L.window = c.layer_window(i)
+            self.layers.append(L)
+
+    def make_kv_cache(self, num_blocks: int) -> PagedKVCache:
+        return PagedKVCache(self.cfg.num_hidden_layers, num_blocks, self.hkv, self.D, self.device)
+
+    # -- forward ---------------------------------------------------------------
+    def _attention(self, i: int, L: LayerWeights, x: torch.Tensor, fb: ForwardBatch, kv: PagedKVCache):
+        T = x.shape[0]
+        kc, vc = kv.layer(i)
+        qkv = ops.linear(x, L.wqkv, bias=L.bqkv)
+        q = ops.qkv_rope(qkv, num_q_heads=self.hq, num_kv_heads=self.hkv, head_dim=self.D,
+                         positions=fb.positions, inv_freq=self.inv_freq, rope_scale=self.rope_mult,
+                         q_norm=L.q_norm, k_norm=L.k_norm, eps=self.cfg.rms_norm_eps, slots=fb.slots,
+                         k_cache=kc, v_cache=vc)
+        o = torch.empty_like(q)
+        nd = fb.num_decode
+        if nd > 0:
+            ops.decode_attention(q[:nd], kc, vc, fb.dec_block_tables, fb.dec_ctx_lens, scale=self.scale,
+                                 sinks=L.sinks, window=L.window, out=o[:nd])
+        if T > nd:
+            ops.prefill_attention(q[nd:], kc, vc, fb.pre_block_tables, fb.pre_ctx_lens, fb.pre_cu_q,
+                                  fb.pre_max_q, scale=self.scale, sinks=L.sinks, window=L.window, out=o[nd:])
+        return o.view(T, self.hq * self.D)
+
+    def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, h: torch.Tensor, bias=None):
+        """h += x @ w.T (+ bias), reduced over the TP group."""
+        if self.tp_size == 1:
+            ops.linear(x, w, bias=bias, residual=h, out=h)
+        else:
+            self.comm.linear_allreduce_residual(x, w, h, bias=bias if self.tp_rank == 0 else None)
+
+    def forward_hidden(self, fb: ForwardBatch, kv: PagedKVCache) -> torch.Tensor:
+        c = self.cfg
+        h = ops.embedding(fb.input_ids, self.embed)
+        for i, L in enumerate(self.layers):
+            x = ops.rmsnorm(h, L.ln1, c.rms_norm_eps)
+            a = self._attention(i, L, x, fb, kv)
+            self._row_parallel(a, L.wo, h, L.bo)
+            x = ops.rmsnorm(h, L.ln2, c.rms_norm_eps)
+            gu = ops.linear_swiglu(x, L.w_gu)
+            self._row_parallel(gu, L.wd, h)
+        return h
+
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        """Final norm + lm_head (fp32 logits; vocab-sharded under TP)."""
+        x = ops.rmsnorm(h, self.norm, self.cfg.rms_norm_eps)
+        return ops.linear(x, self.lm_head, out_dtype=torch.float32)
+
+    def forward(self, fb: ForwardBatch, kv: PagedKVCache) -> torch.Tensor:
+        h = self.forward_hidden(fb, kv)
+        if fb.logit_rows is not None:
+            h = h.index_select(0, fb.logit_rows)
+        return self.logits(h)

@@ -1,0 +1,170 @@
+"""fp32 CPU oracle for the decoder families (the numerical spec).
+
+A direct PyTorch restatement of the HF modules for Qwen3 (dense), Llama /
+Qwen2 (no QK-norm, optional qkv bias) and gpt-oss (q/k/v/o biases, learned
+sinks, alternating sliding/full attention, YaRN RoPE, top-k-then-softmax
+router, MXFP4 experts with biases, clamped SwiGLU). Used as the reference for
+the GPU model and as the CPU execution path of config 1 (Qwen3-0.6B shape,
+fp32, prefill + greedy decode).
+
+Reference behaviour: rlx-models-core src/standard_decoder.rs (`DecoderSpec`
+:172-312, `build_gpt_oss_moe_ffn` :1040-1205, gpt-oss attention :11946-12079,
+prefill :12081); rlx-qwen3 src/generator.rs (`prefill_get_last_logits` :4303,
+`decode_get_logits` :4391). Unlike the reference gpt-oss builder (prefill
+only, all layers treated as full attention), this oracle applies the sliding
+window for sequences longer than the window and supports decode.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from ..config import DecoderConfig
+from ..ops import reference as R
+from ..ops import rope_inv_freq
+from ..quant.mxfp4 import dequantize_mxfp4
+
+
+class OracleKV:
+    def __init__(self, n_layers: int):
+        self.k = [None] * n_layers
+        self.v = [None] * n_layers
+
+    @property
+    def length(self) -> int:
+        return 0 if self.k[0] is None else self.k[0].shape[0]
+
+
+class DecoderOracle:
+    """fp32 decoder over a ``{hf_name: tensor}`` dict."""
+
+    def __init__(self, cfg: DecoderConfig, weights: dict[str, torch.Tensor], device="cpu"):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.w = {k: v.to(self.device) for k, v in weights.items()}
+        self.inv_freq, self.rope_mult = rope_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling,
+                                                      cfg.max_position_embeddings)
+        self._experts: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+
+    def W(self, name: str) -> torch.Tensor:
+        return self.w[name].float()
+
+    def _experts_fp32(self, i: int):
+        if i not in self._experts:
+            p = f"model.layers.{i}.mlp.experts."
+            if self.cfg.expert_quant == "mxfp4":
+                gu = dequantize_mxfp4(self.w[p + "gate_up_proj_blocks"], self.w[p + "gate_up_proj_scales"])
+                dn = dequantize_mxfp4(self.w[p + "down_proj_blocks"], self.w[p + "down_proj_scales"])
+                # stored [E, out, in]; HF bf16 layout is [E, in, out]
+                self._experts[i] = (gu.transpose(1, 2).contiguous(), dn.transpose(1, 2).contiguous())
+            else:
+                self._experts[i] = (self.W(p + "gate_up_proj"), self.W(p + "down_proj"))
+        return self._experts[i]
+
+    def _attn(self, i: int, x: torch.Tensor, pos: torch.Tensor, kv: OracleKV) -> torch.Tensor:
+        c = self.cfg
+        p = f"model.layers.{i}.self_attn."
+        T = x.shape[0]
+
+        def proj(n):
+            y = x @ self.W(p + n + ".weight").T
+            if (p + n + ".bias") in self.w:
+                y = y + self.W(p + n + ".bias")
+            return y
+
+        q = proj("q_proj").view(T, c.num_attention_heads, c.head_dim)
+        k = proj("k_proj").view(T, c.num_key_value_heads, c.head_dim)
+        v = proj("v_proj").view(T, c.num_key_value_heads, c.head_dim)
+        if c.qk_norm:
+            q = R.rmsnorm(q, self.W(p + "q_norm.weight"), c.rms_norm_eps)
+            k = R.rmsnorm(k, self.W(p + "k_norm.weight"), c.rms_norm_eps)
+        q = R.rope(q, pos, self.inv_freq, self.rope_mult)
+        k = R.rope(k, pos, self.inv_freq, self.rope_mult)
+        if kv.k[i] is None:
+            kv.k[i], kv.v[i] = k, v
+        else:
+            kv.k[i] = torch.cat([kv.k[i], k])
+            kv.v[i] = torch.cat([kv.v[i], v])
+        kpos = torch.arange(kv.k[i].shape[0], device=x.device)
+        sinks = self.W(p + "sinks") if c.attn_sinks else None
+        o = R.attention(q, kv.k[i], kv.v[i], pos, kpos, 1.0 / math.sqrt(c.head_dim), causal=True,
+                        window=c.layer_window(i), sinks=sinks)
+        y = o.reshape(T, -1) @ self.W(p + "o_proj.weight").T
+        if (p + "o_proj.bias") in self.w:
+            y = y + self.W(p + "o_proj.bias")
+        return y
+
+    def _mlp(self, i: int, x: torch.Tensor) -> torch.Tensor:
+        c = self.cfg
+        p = f"model.layers.{i}.mlp."
+        if not c.is_moe:
+            g = x @ self.W(p + "gate_proj.weight").T
+            u = x @ self.W(p + "up_proj.weight").T
+            return (F.silu(g) * u) @ self.W(p + "down_proj.weight").T
+        if c.model_type == "gpt_oss":
+            logits = x @ self.W(p + "router.weight").T + self.W(p + "router.bias")
+            topv, topi = logits.topk(c.num_experts_per_tok, dim=-1)
+            probs = torch.softmax(topv, dim=-1)
+            gu_w, dn_w = self._experts_fp32(i)
+            gu_b = self.W(p + "experts.gate_up_proj_bias")
+            dn_b = self.W(p + "experts.down_proj_bias")
+            out = torch.zeros_like(x)
+            for slot in range(c.num_experts_per_tok):
+                e = topi[:, slot]
+                gu = torch.einsum("th,thn->tn", x, gu_w[e]) + gu_b[e]
+                gate, up = gu[:, ::2], gu[:, 1::2]
+                gate = gate.clamp(max=c.swiglu_limit)
+                up = up.clamp(-c.swiglu_limit, c.swiglu_limit)
+                act = (up + 1) * gate * torch.sigmoid(gate * c.swiglu_alpha)
+                y = torch.einsum("tn,tnh->th", act, dn_w[e]) + dn_b[e]
+                out += probs[:, slot:slot + 1] * y
+            return out
+        # qwen3-moe style (softmax over all experts, top-k, optional renorm)
+        logits = x @ self.W(p + "gate.weight").T
+        probs = torch.softmax(logits, dim=-1)
+        topv, topi = probs.topk(c.num_experts_per_tok, dim=-1)
+        if c.norm_topk_prob:
+            topv = topv / topv.sum(-1, keepdim=True)
+        out = torch.zeros_like(x)
+        for t in range(x.shape[0]):
+            for s in range(c.num_experts_per_tok):
+                e = int(topi[t, s])
+                pe = p + f"experts.{e}."
+                g = x[t] @ self.W(pe + "gate_proj.weight").T
+                u = x[t] @ self.W(pe + "up_proj.weight").T
+                out[t] += topv[t, s] * ((F.silu(g) * u) @ self.W(pe + "down_proj.weight").T)
+        return out
+
+    @torch.no_grad()
+    def forward(self, ids: torch.Tensor, kv: OracleKV | None = None) -> tuple[torch.Tensor, OracleKV]:
+        """ids: [T] new tokens continuing ``kv``. Returns fp32 logits [T, V]."""
+        c = self.cfg
+        if kv is None:
+            kv = OracleKV(c.num_hidden_layers)
+        start = kv.length
+        pos = torch.arange(start, start + ids.shape[0], device=self.device)
+        h = self.W("model.embed_tokens.weight")[ids.to(self.device).long()]
+        for i in range(c.num_hidden_layers):
+            p = f"model.layers.{i}."
+            h = h + self._attn(i, R.rmsnorm(h, self.W(p + "input_layernorm.weight"), c.rms_norm_eps), pos, kv)
+            h = h + self._mlp(i, R.rmsnorm(h, self.W(p + "post_attention_layernorm.weight"), c.rms_norm_eps))
+        h = R.rmsnorm(h, self.W("model.norm.weight"), c.rms_norm_eps)
+        head = self.W("model.embed_tokens.weight") if c.tie_word_embeddings else self.W("lm_head.weight")
+        return h @ head.T, kv
+
+    @torch.no_grad()
+    def generate(self, prompt: torch.Tensor, max_new_tokens: int) -> tuple[list[int], list[torch.Tensor]]:
+        """Greedy decode. Returns new token ids and the logits at each step."""
+        logits, kv = self.forward(prompt)
+        out, all_logits = [], [logits[-1]]
+        nxt = int(logits[-1].argmax())
+        for _ in range(max_new_tokens):
+            out.append(nxt)
+            if len(out) == max_new_tokens:
+                break
+            logits, kv = self.forward(torch.tensor([nxt]), kv)
+            all_logits.append(logits[-1])
+            nxt = int(logits[-1].argmax())
+        return out, all_logits

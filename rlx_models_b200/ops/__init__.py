@@ -10,7 +10,8 @@ import math
 
 import torch
 
-from ._ext import KernelError, available, check_errors, ext, scratch
+from ._ext import KernelError, available, check_errors, ext, launch_count, scratch
+from ._ext import count_launches as _count
 
 __all__ = [
     "linear", "linear_swiglu", "rmsnorm", "qkv_rope", "embedding", "decode_attention",
@@ -34,6 +35,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, out: torch.Tensor | None = None,
         out = torch.empty(M, N, dtype=out_dtype, device=x.device)
     s = scratch(x.device)
     mode = 1 if out.dtype == torch.float32 else 0
+    _count(1)
     ext().linear(x, w, out, mode, residual, bias, float(alpha), s.gemm_ws, s.gemm_sem, s.status,
                  swap, bn, splits)
     return out
@@ -46,6 +48,7 @@ def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, *, out: torch.Tensor | No
     if out is None:
         out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
     s = scratch(x.device)
+    _count(1)
     ext().linear(x, w_gu, out, 2, None, None, 1.0, s.gemm_ws, s.gemm_sem, s.status, swap, bn, splits)
     return out
 
@@ -70,6 +73,7 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, *, out: torch.Tensor |
     """``rmsnorm(x (+ residual)) * w``; with ``residual_out`` the sum is also stored."""
     if out is None:
         out = torch.empty_like(x)
+    _count(1)
     ext().rmsnorm(x, w, out, float(eps), residual, residual_out)
     return out
 
@@ -77,6 +81,7 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, *, out: torch.Tensor |
 def embedding(ids: torch.Tensor, table: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    _count(1)
     ext().embedding(ids, table, out)
     return out
 
@@ -141,6 +146,7 @@ def qkv_rope(qkv: torch.Tensor, *, num_q_heads: int, num_kv_heads: int, head_dim
     T = qkv.shape[0]
     if q_out is None:
         q_out = torch.empty(T, num_q_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
+    _count(1)
     ext().qkv_rope(qkv, q_norm, k_norm, positions, slots, inv_freq, float(rope_scale), q_out, k_cache,
                    v_cache, k_out, v_out, num_q_heads, num_kv_heads, head_dim, float(eps))
     return q_out
@@ -151,8 +157,8 @@ def decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, *, scale, sink
     if out is None:
         out = torch.empty_like(q)
     s = scratch(q.device)
-    ext().decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, int(window), float(scale),
-                           int(splits), s.attn_ws, s.status)
+    _count(ext().decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, int(window), float(scale),
+                           int(splits), s.attn_ws, s.status))
     return out
 
 
@@ -161,6 +167,7 @@ def prefill_attention(q, k_cache, v_cache, block_tables, ctx_lens, cu_q, max_q_l
     if out is None:
         out = torch.empty_like(q)
     s = scratch(q.device)
+    _count(1)
     ext().prefill_attention(q, k_cache, v_cache, block_tables, ctx_lens, cu_q, out, sinks, int(window),
                             float(scale), int(max_q_len), s.status)
     return out
@@ -169,6 +176,7 @@ def prefill_attention(q, k_cache, v_cache, block_tables, ctx_lens, cu_q, max_q_l
 def argmax(logits: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Tensor:
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    _count(1)
     ext().argmax(logits, out)
     return out
 
@@ -176,5 +184,6 @@ def argmax(logits: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Te
 def sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, *, out=None, logprob=None):
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    _count(1)
     ext().sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out, logprob)
     return out

@@ -46,7 +46,8 @@ class DeviceScratch:
     def __init__(self, device: torch.device):
         self.device = device
         self.status = torch.zeros(4, dtype=torch.int32, device=device)
-        self.gemm_ws = torch.empty(self.GEMM_WS_ELEMS, dtype=torch.float32, device=device)
+        # split-K fp32 tile accumulators: zero at rest (each tile's last split re-zeroes it)
+        self.gemm_ws = torch.zeros(self.GEMM_WS_ELEMS, dtype=torch.float32, device=device)
         self.gemm_sem = torch.zeros(self.GEMM_SEM_ELEMS, dtype=torch.int32, device=device)
         self.attn_ws = torch.empty(self.ATTN_WS_ELEMS, dtype=torch.float32, device=device)
 
@@ -71,6 +72,19 @@ class KernelError(RuntimeError):
         super().__init__(
             f"b200 kernel error {self.code} ({self.CODES.get(self.code, '?')}) "
             f"block={self.block} thread={self.thread} detail={self.detail}")
+
+
+_LAUNCHES = [0]
+
+
+def count_launches(n: int = 1) -> None:
+    """Host-side tally of this package's kernel launches (eager calls and
+    graph captures); graph replays are added by the engine."""
+    _LAUNCHES[0] += int(n)
+
+
+def launch_count() -> int:
+    return _LAUNCHES[0]
 
 
 _scratch: dict[int, DeviceScratch] = {}

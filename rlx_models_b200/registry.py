@@ -1,0 +1,72 @@
+"""Model-type -> builder registry and lazy random weight source.
+
+The reference keeps an LM runner registry keyed by architecture
+(rlx-models-core src/lm_registry.rs:75-320 `LmBuildOptions`,
+`build_lm_runner`; src/model_registry.rs:35-116; `classify_config`
+src/standard_decoder.rs:13388). Here ``model_type`` from config.json selects a
+builder; families register themselves with :func:`register`.
+"""
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+
+from .config import DecoderConfig
+from .weights.init import decoder_tensor_specs, init_tensor
+
+_BUILDERS: dict[str, Callable] = {}
+
+
+def register(*model_types: str):
+    def deco(fn):
+        for mt in model_types:
+            _BUILDERS[mt] = fn
+        return fn
+    return deco
+
+
+def registered() -> list[str]:
+    return sorted(_BUILDERS)
+
+
+class RandomWeights:
+    """WeightMap-compatible source that generates each tensor on first take()."""
+
+    def __init__(self, cfg: DecoderConfig, seed: int, device, dtype=torch.bfloat16):
+        self.specs = {s.name: s for s in decoder_tensor_specs(cfg)}
+        self.seed, self.device, self.dtype = seed, torch.device(device), dtype
+
+    def __contains__(self, name):
+        return name in self.specs
+
+    def take(self, name, **kw):
+        return init_tensor(self.specs[name], self.seed, self.device, self.dtype)
+
+    def __getitem__(self, name):
+        return self.take(name)
+
+    def keys(self):
+        return list(self.specs)
+
+
+@register("qwen3", "llama", "mistral", "qwen2")
+def _dense(cfg, weights, device, tp_rank, tp_size, comm):
+    from .models.decoder import DecoderLM
+    return DecoderLM(cfg, weights, device=device, tp_rank=tp_rank, tp_size=tp_size, comm=comm)
+
+
+@register("gpt_oss", "qwen3_moe")
+def _moe(cfg, weights, device, tp_rank, tp_size, comm):
+    from .models.moe import MoEDecoderLM
+    return MoEDecoderLM(cfg, weights, device=device, ep_rank=tp_rank, ep_size=tp_size, comm=comm)
+
+
+def build_model(cfg: DecoderConfig, weights=None, *, device="cuda", tp_rank=0, tp_size=1, comm=None, seed=0):
+    fn = _BUILDERS.get(cfg.model_type)
+    if fn is None:
+        raise KeyError(f"no builder for model_type={cfg.model_type!r}; registered: {registered()}")
+    if weights is None:
+        weights = RandomWeights(cfg, seed, device)
+    with torch.no_grad():
+        return fn(cfg, weights, device, tp_rank, tp_size, comm)

@@ -1,0 +1,321 @@
+"""LLM engine: native scheduler + paged KV + model runner with CUDA graphs.
+
+Step loop (the B200 counterpart of rlx-serve's `BatchedEngine` /
+`scheduler_loop`, src/batch.rs:567-640, and `FusedBatchRunner::forward_batch`,
+src/batch.rs:262-360):
+
+1. the C++ scheduler (``_runtime.Scheduler``) picks decode tokens and prefill
+   chunks under the token budget and writes the flat batch into pinned host
+   staging buffers;
+2. one non-blocking host->device copy per field;
+3. decode-only steps replay a CUDA graph captured for the padded batch size
+   (model forward + on-GPU sampling in one graph); mixed / prefill steps run
+   eagerly;
+4. only the sampled token ids come back to the host; the scheduler appends
+   them and retires finished sequences.
+
+Every launch in a step is one of this package's kernels (GEMM, attention,
+norm/RoPE, sampling) except for small torch copies/index ops.
+"""
+from __future__ import annotations
+
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from .. import ops
+from ..models.decoder import ForwardBatch
+from .kv_cache import BLOCK_SIZE
+
+try:
+    from .. import _runtime  # type: ignore
+except Exception as e:  # pragma: no cover
+    _runtime = None
+    _RT_ERR = e
+
+
+@dataclass
+class SamplingParams:
+    max_new_tokens: int = 16
+    temperature: float = 0.0
+    top_k: int = 0
+    top_p: float = 1.0
+    min_p: float = 0.0
+    seed: int = 0
+    ignore_eos: bool = False
+    stop_token_ids: list[int] = field(default_factory=list)
+    logprobs: bool = False
+
+
+@dataclass
+class EngineConfig:
+    max_num_seqs: int = 256
+    max_batched_tokens: int = 8192
+    chunk_size: int = 0
+    max_model_len: int = 4096
+    num_blocks: int = 0            # 0: size from kv_memory_gb
+    kv_memory_gb: float = 16.0
+    prefix_caching: bool = True
+    cuda_graphs: bool = True
+    graph_batch_sizes: tuple = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
+    eos_token_id: int = -1
+
+
+@dataclass
+class RequestState:
+    seq_id: int
+    prompt_len: int
+    params: SamplingParams
+    arrival: float
+    first_token: float | None = None
+    finish: float | None = None
+    token_times: list[float] = field(default_factory=list)
+    tokens: list[int] = field(default_factory=list)
+    logprobs: list[float] = field(default_factory=list)
+    finish_reason: str | None = None
+
+
+@dataclass
+class RequestOutput:
+    seq_id: int
+    prompt_len: int
+    token_ids: list[int]
+    finish_reason: str
+    ttft: float
+    tpot: float
+    latency: float
+    cached_prompt_tokens: int = 0
+    logprobs: list[float] | None = None
+
+
+_REASONS = {1: "length", 2: "stop", 3: "abort"}
+
+
+class LLMEngine:
+    def __init__(self, model, config: EngineConfig | None = None):
+        if _runtime is None:
+            raise RuntimeError(f"rlx_models_b200._runtime not built: {_RT_ERR}")
+        self.model = model
+        self.cfg = cfg = config or EngineConfig()
+        self.device = model.device
+        mc = model.cfg
+        self.max_blocks_per_seq = (cfg.max_model_len + BLOCK_SIZE - 1) // BLOCK_SIZE
+        nb = cfg.num_blocks
+        if nb <= 0:
+            per = 2 * mc.num_hidden_layers * model.hkv * BLOCK_SIZE * model.D * 2
+            nb = max(self.max_blocks_per_seq + 1, int(cfg.kv_memory_gb * (1 << 30)) // per)
+        self.kv = model.make_kv_cache(nb + 1)
+        self.dummy_block = nb  # never handed out by the scheduler; padding rows write here
+        self.sched = _runtime.Scheduler(nb, cfg.max_num_seqs, cfg.max_batched_tokens, self.max_blocks_per_seq,
+                                        cfg.prefix_caching, cfg.chunk_size)
+        T, S, W = cfg.max_batched_tokens, cfg.max_num_seqs, self.max_blocks_per_seq
+        pin = dict(pin_memory=True)
+        i32, i64 = torch.int32, torch.int64
+        self.h = dict(
+            input_ids=torch.zeros(T, dtype=i32, **pin), positions=torch.zeros(T, dtype=i32, **pin),
+            slots=torch.zeros(T, dtype=i64, **pin), dec_tables=torch.zeros(S, W, dtype=i32, **pin),
+            dec_ctx=torch.zeros(S, dtype=i32, **pin), pre_tables=torch.zeros(S, W, dtype=i32, **pin),
+            pre_ctx=torch.zeros(S, dtype=i32, **pin), pre_cu=torch.zeros(S + 1, dtype=i32, **pin),
+            logit_rows=torch.zeros(T, dtype=i64, **pin), sample_ids=torch.zeros(T, dtype=i64, **pin))
+        dev = self.device
+        self.d = {k: torch.zeros_like(v, device=dev) for k, v in self.h.items() if k != "sample_ids"}
+        # per-row sampling parameters (host pinned -> device)
+        self.hp = dict(temp=torch.zeros(T, **pin), top_k=torch.zeros(T, dtype=i32, **pin),
+                       top_p=torch.ones(T, **pin), min_p=torch.zeros(T, **pin),
+                       seed=torch.zeros(T, dtype=i64, **pin), offset=torch.zeros(T, dtype=i64, **pin))
+        self.dp = {k: torch.zeros_like(v, device=dev) for k, v in self.hp.items()}
+        self.tok_out = torch.zeros(T, dtype=i32, device=dev)
+        self.logprob_out = torch.zeros(T, dtype=torch.float32, device=dev)
+        self.tok_host = torch.zeros(T, dtype=i32, pin_memory=True)
+        self.requests: dict[int, RequestState] = {}
+        self.graphs: dict[int, tuple] = {}
+        self._graph_pool = None
+        self.stats = dict(steps=0, graph_steps=0, eager_steps=0, tokens=0, h2d_bytes=0, d2h_bytes=0)
+        self.copy_stream = torch.cuda.current_stream(dev)
+
+    # -- requests --------------------------------------------------------------
+    def add_request(self, prompt: list[int], params: SamplingParams | None = None) -> int:
+        params = params or SamplingParams()
+        sid = self.sched.add_request(list(map(int, prompt)), int(params.max_new_tokens), bool(params.ignore_eos),
+                                     list(params.stop_token_ids))
+        self.requests[sid] = RequestState(sid, len(prompt), params, time.perf_counter())
+        return sid
+
+    def abort(self, sid: int):
+        self.sched.abort(sid)
+
+    def has_unfinished(self) -> bool:
+        return self.sched.has_work()
+
+    # -- model step ------------------------------------------------------------
+    def _params_rows(self, sids: list[int]) -> bool:
+        """Fill per-row sampling params; returns True if every row is greedy without logprobs."""
+        greedy = True
+        hp = self.hp
+        for r, sid in enumerate(sids):
+            st = self.requests[sid]
+            p = st.params
+            hp["temp"][r] = p.temperature
+            hp["top_k"][r] = p.top_k
+            hp["top_p"][r] = p.top_p
+            hp["min_p"][r] = p.min_p
+            hp["seed"][r] = p.seed * 1000003 + sid
+            hp["offset"][r] = len(st.tokens)
+            if p.temperature > 0 or p.logprobs:
+                greedy = False
+        return greedy
+
+    def _sample(self, logits: torch.Tensor, R: int, greedy: bool):
+        out = self.tok_out[:R]
+        if greedy:
+            ops.argmax(logits, out=out)
+        else:
+            for k in self.hp:
+                self.dp[k][:R].copy_(self.hp[k][:R], non_blocking=True)
+            ops.sample(logits, self.dp["temp"][:R], self.dp["top_k"][:R], self.dp["top_p"][:R],
+                       self.dp["min_p"][:R], self.dp["seed"][:R], self.dp["offset"][:R], out=out,
+                       logprob=self.logprob_out[:R])
+        return out
+
+    def _copy_in(self, keys_rows: dict[str, int]):
+        for k, n in keys_rows.items():
+            if n > 0:
+                src = self.h[k][:n]
+                self.d[k][:n].copy_(src, non_blocking=True)
+                self.stats["h2d_bytes"] += src.numel() * src.element_size()
+
+    def _eager_forward(self, T: int, nd: int, npf: int, max_q: int, R: int) -> torch.Tensor:
+        d = self.d
+        self._copy_in(dict(input_ids=T, positions=T, slots=T, dec_tables=nd, dec_ctx=nd, pre_tables=npf,
+                           pre_ctx=npf, pre_cu=npf + 1 if npf else 0, logit_rows=R))
+        fb = ForwardBatch(
+            input_ids=d["input_ids"][:T], positions=d["positions"][:T], slots=d["slots"][:T], num_decode=nd,
+            dec_block_tables=d["dec_tables"][:nd] if nd else None, dec_ctx_lens=d["dec_ctx"][:nd] if nd else None,
+            pre_block_tables=d["pre_tables"][:npf] if npf else None,
+            pre_ctx_lens=d["pre_ctx"][:npf] if npf else None, pre_cu_q=d["pre_cu"][:npf + 1] if npf else None,
+            pre_max_q=max_q, logit_rows=d["logit_rows"][:R])
+        return self.model.forward(fb, self.kv)
+
+    def _bucket(self, n: int) -> int | None:
+        for b in self.cfg.graph_batch_sizes:
+            if b >= n and b <= self.cfg.max_num_seqs:
+                return b
+        return None
+
+    def _pad_decode_rows(self, nd: int, B: int):
+        h = self.h
+        db = self.dummy_block
+        h["input_ids"][nd:B] = 0
+        h["positions"][nd:B] = 0
+        h["slots"][nd:B] = db * BLOCK_SIZE
+        h["dec_tables"][nd:B] = db
+        h["dec_ctx"][nd:B] = 1
+
+    def _capture(self, B: int, greedy: bool):
+        d = self.d
+        fb = ForwardBatch(input_ids=d["input_ids"][:B], positions=d["positions"][:B], slots=d["slots"][:B],
+                          num_decode=B, dec_block_tables=d["dec_tables"][:B], dec_ctx_lens=d["dec_ctx"][:B],
+                          logit_rows=None)
+        # warm up (allocations, kernel attributes) outside the graph on dummy
+        # rows written straight into the device buffers: the host staging
+        # buffers may already hold the step being scheduled.
+        db = self.dummy_block
+        d["input_ids"][:B].zero_()
+        d["positions"][:B].zero_()
+        d["slots"][:B].fill_(db * BLOCK_SIZE)
+        d["dec_tables"][:B].fill_(db)
+        d["dec_ctx"][:B].fill_(1)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                logits = self.model.forward(fb, self.kv)
+                self._sample(logits, B, greedy)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        if self._graph_pool is None:
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        n0 = ops.launch_count()
+        with torch.cuda.graph(g, pool=self._graph_pool):
+            logits = self.model.forward(fb, self.kv)
+            out = self._sample(logits, B, greedy)
+        n_launch = ops.launch_count() - n0
+        ops._count(-n_launch)  # capture does not execute; replays are counted
+        self.graphs[(B, greedy)] = (g, out, n_launch)
+        return g, out, n_launch
+
+    def capture_graphs(self, sizes=None, greedy: bool = True):
+        sizes = sizes or [b for b in self.cfg.graph_batch_sizes if b <= self.cfg.max_num_seqs]
+        for B in sorted(sizes, reverse=True):
+            if (B, greedy) not in self.graphs:
+                self._capture(B, greedy)
+
+    def step(self) -> list[RequestOutput]:
+        h = self.h
+        info = self.sched.schedule(h["input_ids"], h["positions"], h["slots"], h["dec_tables"], h["dec_ctx"],
+                                   h["pre_tables"], h["pre_ctx"], h["pre_cu"], h["logit_rows"], h["sample_ids"])
+        T, nd, npf = info["num_tokens"], info["num_decode"], info["num_prefill"]
+        R, max_q = info["num_logits"], info["max_q_len"]
+        self.stats["steps"] += 1
+        if T == 0:
+            return []
+        sids = h["sample_ids"][:R].tolist()
+        greedy = self._params_rows(sids)
+        B = self._bucket(nd) if (npf == 0 and self.cfg.cuda_graphs) else None
+        if B is not None:
+            key = (B, greedy)
+            if key not in self.graphs:
+                self._capture(B, greedy)
+            g, out, n_launch = self.graphs[key]
+            self._pad_decode_rows(nd, B)
+            self._copy_in(dict(input_ids=B, positions=B, slots=B, dec_tables=B, dec_ctx=B))
+            g.replay()
+            ops._count(n_launch)
+            toks = out[:nd]
+            self.stats["graph_steps"] += 1
+        else:
+            logits = self._eager_forward(T, nd, npf, max_q, R)
+            toks = self._sample(logits, R, greedy)
+            self.stats["eager_steps"] += 1
+        self.tok_host[:R].copy_(toks[:R])
+        self.stats["d2h_bytes"] += 4 * R
+        tl = self.tok_host[:R].tolist()
+        lps = self.logprob_out[:R].tolist() if not greedy else None
+        now = time.perf_counter()
+        for r, sid in enumerate(sids):
+            st = self.requests[sid]
+            st.tokens.append(tl[r])
+            st.token_times.append(now)
+            if st.first_token is None:
+                st.first_token = now
+            if lps is not None and st.params.logprobs:
+                st.logprobs.append(lps[r])
+        self.stats["tokens"] += R
+        done = self.sched.update(sids, tl, int(self.cfg.eos_token_id))
+        outs = []
+        for sid in done:
+            st = self.requests.pop(sid)
+            st.finish = now
+            reason = _REASONS.get(self.sched.finish_reason(sid), "length")
+            cached = self.sched.num_cached_prompt_tokens(sid)
+            self.sched.release(sid)
+            n = len(st.tokens)
+            tpot = (st.finish - st.first_token) / max(1, n - 1)
+            outs.append(RequestOutput(sid, st.prompt_len, st.tokens, reason, st.first_token - st.arrival, tpot,
+                                      st.finish - st.arrival, cached, st.logprobs or None))
+        return outs
+
+    def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None
+                 ) -> list[RequestOutput]:
+        if not isinstance(params, list):
+            params = [params or SamplingParams()] * len(prompts)
+        ids = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
+        order = {sid: i for i, sid in enumerate(ids)}
+        results: list[RequestOutput | None] = [None] * len(ids)
+        while self.has_unfinished():
+            for o in self.step():
+                if o.seq_id in order:
+                    results[order[o.seq_id]] = o
+        return results  # type: ignore

@@ -50,9 +50,10 @@ def test_linear_splitk_residual_bias_f32(cuda, splits, M):
     y32 = ops.linear(x, w, out_dtype=torch.float32, alpha=0.5, splits=splits)
     assert rel_err(y32, 0.5 * (x.float() @ w.float().T)) < 5e-3
     ops.check_errors(cuda)
-    # semaphores must be self-resetting: a second identical call gives the same result
+    # split-K accumulators / semaphores must be self-resetting: a second call
+    # matches (fp32 atomics make the summation order, hence the last bit, vary)
     y2 = ops.linear(x, w, residual=res, bias=b, splits=splits)
-    assert torch.equal(y, y2)
+    assert rel_err(y2, y) < 2e-3
 
 
 @pytest.mark.parametrize("M", [1, 33, 64, 128, 257, 1024])

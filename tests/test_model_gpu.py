@@ -1,0 +1,118 @@
+"""GPU decoder + engine against the fp32 oracle.
+
+Synthetic seeded weights (distinct per layer), bf16 on the GPU vs fp32 on the
+CPU oracle with the same bf16-rounded weights. Checks logits (teacher forced)
+and greedy tokens through the engine: chunked prefill, decode CUDA graphs,
+prefix caching and eager/graph equivalence.
+"""
+import pytest
+import torch
+
+from rlx_models_b200 import config as C
+from rlx_models_b200.models.decoder import DecoderLM
+from rlx_models_b200.models.oracle import DecoderOracle
+from rlx_models_b200.runtime.engine import EngineConfig, LLMEngine, SamplingParams
+from rlx_models_b200.weights.init import random_weights
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+
+def _setup(cfg, seed=0):
+    w = random_weights(cfg, seed=seed, dtype=torch.bfloat16)
+    oracle = DecoderOracle(cfg, {k: v.float() for k, v in w.items()})
+    model = DecoderLM(cfg, w, device="cuda")
+    return model, oracle
+
+
+@pytest.fixture(scope="module")
+def tiny_model():
+    cfg = C.tiny(num_hidden_layers=3, hidden_size=512, intermediate_size=1024, num_attention_heads=8,
+                 num_key_value_heads=2, head_dim=128, vocab_size=1024)
+    return (cfg,) + _setup(cfg, seed=11)
+
+
+def test_teacher_forced_logits(tiny_model):
+    cfg, model, oracle = tiny_model
+    eng = LLMEngine(model, EngineConfig(max_num_seqs=8, max_batched_tokens=512, max_model_len=512,
+                                        num_blocks=64, cuda_graphs=False, prefix_caching=False))
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab_size, (100,), generator=g)
+    out = eng.generate([prompt.tolist()], SamplingParams(max_new_tokens=12, ignore_eos=True))[0]
+    # oracle on the same token sequence
+    ref_logits, _ = oracle.forward(torch.tensor(prompt.tolist() + out.token_ids[:-1]))
+    ref_tokens = ref_logits[len(prompt) - 1:].argmax(-1).tolist()
+    assert ref_tokens[0] == out.token_ids[0]
+    agree = sum(int(a == b) for a, b in zip(ref_tokens, out.token_ids))
+    assert agree >= len(out.token_ids) - 1
+    # direct logits check through the model forward (prefill of the prompt)
+    from rlx_models_b200.models.decoder import ForwardBatch
+    kv = model.make_kv_cache(16)
+    T = len(prompt)
+    nb = (T + 15) // 16
+    fb = ForwardBatch(input_ids=prompt.int().cuda(), positions=torch.arange(T, dtype=torch.int32).cuda(),
+                      slots=torch.arange(T, dtype=torch.int64).cuda(), num_decode=0,
+                      pre_block_tables=torch.arange(nb, dtype=torch.int32).view(1, -1).cuda(),
+                      pre_ctx_lens=torch.tensor([T], dtype=torch.int32).cuda(),
+                      pre_cu_q=torch.tensor([0, T], dtype=torch.int32).cuda(), pre_max_q=T,
+                      logit_rows=None)
+    lg = model.forward(fb, kv)
+    ref_prefill, _ = oracle.forward(prompt)
+    assert rel(lg.cpu(), ref_prefill) < 3e-2
+
+
+def test_engine_graphs_chunking_prefix(tiny_model):
+    cfg, model, _ = tiny_model
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (5, 40, 77, 130, 16, 1)]
+    sp = SamplingParams(max_new_tokens=20, ignore_eos=True)
+
+    def run(**kw):
+        e = LLMEngine(model, EngineConfig(max_num_seqs=8, max_model_len=512, num_blocks=128, **kw))
+        return [o.token_ids for o in e.generate(prompts, sp)], e
+
+    base, e0 = run(max_batched_tokens=1024, cuda_graphs=False, prefix_caching=False)
+    graphs, e1 = run(max_batched_tokens=1024, cuda_graphs=True, prefix_caching=False)
+    assert e1.stats["graph_steps"] > 0
+    assert graphs == base
+    chunked, _ = run(max_batched_tokens=48, cuda_graphs=True, prefix_caching=False)
+    agree = sum(a == b for a, b in zip(chunked, base))
+    assert agree >= len(base) - 1
+    # prefix cache: same prompts twice through one engine
+    e = LLMEngine(model, EngineConfig(max_num_seqs=8, max_model_len=512, num_blocks=128, prefix_caching=True))
+    first = [o.token_ids for o in e.generate(prompts, sp)]
+    second = e.generate(prompts, sp)
+    assert sum(o.cached_prompt_tokens for o in second) > 0
+    assert sum(a == o.token_ids for a, o in zip(first, second)) >= len(prompts) - 1
+
+
+def test_sampling_through_engine(tiny_model):
+    cfg, model, _ = tiny_model
+    e = LLMEngine(model, EngineConfig(max_num_seqs=8, max_model_len=256, num_blocks=64))
+    p = [[1, 2, 3, 4, 5]] * 4
+    sp = SamplingParams(max_new_tokens=16, temperature=0.8, top_k=50, top_p=0.9, seed=7, ignore_eos=True,
+                        logprobs=True)
+    a = e.generate(p, sp)
+    assert all(len(o.token_ids) == 16 for o in a)
+    assert all(o.logprobs is not None and all(lp <= 0 for lp in o.logprobs) for o in a)
+    # different sequences (different seq ids in the seed) should not all coincide
+    assert len({tuple(o.token_ids) for o in a}) > 1
+
+
+def test_qwen3_0_6b_shape_vs_cpu_oracle():
+    """Config 1 shape (28 layers, 1024 hidden, 16/8 heads, vocab 151936, tied):
+    128-token prompt, GPU bf16 greedy vs fp32 CPU oracle, teacher-forced."""
+    cfg = C.qwen3_0_6b()
+    w = random_weights(cfg, seed=0, dtype=torch.bfloat16)
+    model = DecoderLM(cfg, w, device="cuda")
+    e = LLMEngine(model, EngineConfig(max_num_seqs=4, max_model_len=512, num_blocks=64))
+    prompt = torch.randint(0, cfg.vocab_size, (128,), generator=torch.Generator().manual_seed(1)).tolist()
+    out = e.generate([prompt], SamplingParams(max_new_tokens=8, ignore_eos=True))[0]
+    oracle = DecoderOracle(cfg, {k: v.float() for k, v in w.items()})
+    ref_logits, _ = oracle.forward(torch.tensor(prompt + out.token_ids[:-1]))
+    ref_tok = ref_logits[127:].argmax(-1).tolist()
+    assert ref_tok[0] == out.token_ids[0]
+    assert sum(int(a == b) for a, b in zip(ref_tok, out.token_ids)) >= 7
