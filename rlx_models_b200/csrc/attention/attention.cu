@@ -598,3 +598,111 @@ void prefill_attention_launch(const AttnArgs& a, cudaStream_t st) {
 }
 
 }  // namespace b200
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of decode attention (see decode_attention_noalloc.h).
+// Launches the same split-KV and merge kernels as decode_attention_launch, but
+// the split partials go to a file-scope device array instead of a caller- or
+// torch-allocated workspace.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+#include "decode_attention_noalloc.h"
+
+namespace b200 {
+namespace attn_noalloc {
+
+// Per-split partial outputs and (max, sum) pairs of every call on this device.
+static __device__ __align__(256) float g_decode_scratch[B200_NOALLOC_SCRATCH_FLOATS];
+
+constexpr int kMaxDevices = 64;
+static float* g_scratch_ptr[kMaxDevices] = {nullptr};
+static bool g_attr_done[kMaxDevices] = {false};
+static std::mutex g_setup_mu;
+
+// Once per device, with that device current: resolve the array's device
+// address (host code must not use the symbol itself) and raise the kernels'
+// dynamic shared-memory limit.
+static int setup(int dev, float** ptr) {
+  if (dev < 0 || dev >= kMaxDevices) return B200_NOALLOC_ERR_SETUP;
+  std::lock_guard<std::mutex> lk(g_setup_mu);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_decode_scratch) != cudaSuccess || p == nullptr) return B200_NOALLOC_ERR_SETUP;
+    g_scratch_ptr[dev] = static_cast<float*>(p);
+  }
+  if (!g_attr_done[dev]) {
+    using namespace attn;
+    if (cudaFuncSetAttribute(decode_attn_kernel<128, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             DecCfg<128, 8>::SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(decode_attn_kernel<64, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             DecCfg<64, 8>::SMEM) != cudaSuccess)
+      return B200_NOALLOC_ERR_SETUP;
+    g_attr_done[dev] = true;
+  }
+  *ptr = g_scratch_ptr[dev];
+  return B200_NOALLOC_OK;
+}
+
+}  // namespace attn_noalloc
+}  // namespace b200
+
+extern "C" int b200_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                             int64_t num_blocks, const int32_t* block_tables, int max_blocks,
+                                             const int32_t* ctx_lens, void* out, const float* sinks, int window,
+                                             int B, int Hq, int Hkv, int D, float scale, int splits, int* status,
+                                             void* stream) {
+  using namespace b200;
+  using namespace b200::attn;
+  if (q == nullptr || k_cache == nullptr || v_cache == nullptr || block_tables == nullptr || ctx_lens == nullptr ||
+      out == nullptr || B <= 0 || Hq <= 0 || Hkv <= 0 || num_blocks <= 0 || max_blocks <= 0 || splits < 1)
+    return B200_NOALLOC_ERR_ARGS;
+  if (Hq % Hkv != 0 || Hq / Hkv > 16 || (D != 64 && D != 128)) return B200_NOALLOC_ERR_ARGS;
+  if ((int64_t)B * Hq * splits * (D + 2) > (int64_t)B200_NOALLOC_SCRATCH_FLOATS) return B200_NOALLOC_ERR_SCRATCH;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return B200_NOALLOC_ERR_SETUP;
+  float* scratch = nullptr;
+  const int rc = attn_noalloc::setup(dev, &scratch);
+  if (rc != B200_NOALLOC_OK) return rc;
+
+  AttnArgs a{};
+  a.q = q;
+  a.k_cache = k_cache;
+  a.v_cache = v_cache;
+  a.num_blocks = num_blocks;
+  a.block_tables = block_tables;
+  a.max_blocks = max_blocks;
+  a.ctx_lens = ctx_lens;
+  a.cu_q = nullptr;
+  a.out = out;
+  a.sinks = sinks;
+  a.window = window;
+  a.B = B;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.D = D;
+  a.scale = scale;
+  a.splits = splits;
+  a.ws = scratch;
+  a.ws_elems = B200_NOALLOC_SCRATCH_FLOATS;
+  a.status = status;
+  a.device = dev;
+  CUtensorMap tk, tv;
+  try {
+    const int64_t rows = num_blocks * Hkv * 16;
+    tk = make_tmap_2d(k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, D, D, 16, 64);
+    tv = make_tmap_2d(v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, D, D, 16, 64);
+  } catch (...) {
+    return B200_NOALLOC_ERR_TMA;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  dim3 grid(B * Hkv, splits);
+  if (D == 128) {
+    decode_attn_kernel<128, 8><<<grid, 160, DecCfg<128, 8>::SMEM, st>>>(tk, tv, a);
+    if (splits > 1) decode_merge_kernel<128><<<B * Hq, 128, 0, st>>>(a, splits);
+  } else {
+    decode_attn_kernel<64, 8><<<grid, 160, DecCfg<64, 8>::SMEM, st>>>(tk, tv, a);
+    if (splits > 1) decode_merge_kernel<64><<<B * Hq, 64, 0, st>>>(a, splits);
+  }
+  return cudaGetLastError() == cudaSuccess ? B200_NOALLOC_OK : B200_NOALLOC_ERR_LAUNCH;
+}
