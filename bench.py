@@ -71,11 +71,10 @@ def serve(args):
 
     rank, ws, local = init_dist(args)
     dev = torch.device("cuda", local)
-    comm = None
-    if ws > 1:
-        from rlx_models_b200.parallel.tp import TPComm
-        comm = TPComm(rank, ws, dev, max_tokens=args.max_batched_tokens, hidden=4096)
     cfg = qwen3_8b()
+    from rlx_models_b200.parallel.tp import make_tp_comm
+    comm = make_tp_comm(args.tp_comm, rank, ws, dev, cfg.rms_norm_eps, max_tokens=args.max_batched_tokens,
+                        hidden=cfg.hidden_size)
     ecfg = EngineConfig(max_num_seqs=max(64, args.num_requests), max_batched_tokens=args.max_batched_tokens,
                         max_model_len=args.max_prompt + args.output_len + 16, kv_memory_gb=args.kv_gb,
                         prefix_caching=False, cuda_graphs=True)
@@ -150,7 +149,7 @@ def serve(args):
         "data": "synthetic: uniform-random token ids (seeded, fresh per pass), random-init N(0,0.02) weights",
         "config": {"model": "Qwen3-8B-shape (36L, h4096, 32q/8kv x128, I12288, V151936)",
                    "global_batch": args.num_requests, "seq_len": f"prompt U[{args.min_prompt},{args.max_prompt}]"
-                   f" + {args.output_len} out", "parallelism": f"tp{ws}", "kv_block": 16,
+                   f" + {args.output_len} out", "parallelism": f"tp{ws}", "tp_comm": args.tp_comm if ws > 1 else None, "kv_block": 16,
                    "max_batched_tokens": args.max_batched_tokens,
                    "l2": "inputs larger than L2: every step streams 16 GB of weights + the KV cache",
                    "step": "one full 64-request serving pass"},
@@ -185,6 +184,8 @@ def main():
     ap.add_argument("--output-len", type=int, default=256)
     ap.add_argument("--max-batched-tokens", type=int, default=8192)
     ap.add_argument("--kv-gb", type=float, default=40.0)
+    ap.add_argument("--tp-comm", default="nccl", choices=["nccl", "fused"],
+                    help="nccl: NCCL all-reduce baseline; fused: GEMM->reduce-scatter + norm + all-gather over NVLink")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1,0 +1,84 @@
+"""Time one decode step (CUDA-graph replay) of a model at a given batch/context.
+
+    python -m rlx_models_b200.bench.decode_step [--model qwen3-8b] [--batch 64] [--ctx 1400] [--iters 20]
+
+Prefills ``batch`` random prompts of ``ctx`` tokens through the engine, then
+times ``iters`` replays of the captured decode graph with CUDA events (device
+time per step), and reports the weight + KV bytes per step and the achieved
+fraction of measured HBM bandwidth. With ``--replays N`` it only replays N
+times (for an ncu launch list of one step).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="qwen3-8b")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--ctx", type=int, default=1400)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--replays", type=int, default=0)
+    args = ap.parse_args()
+    from .. import ops
+    from ..api import load
+    from ..config import preset
+    from ..runtime.engine import EngineConfig, SamplingParams
+    from .bench_ops import peaks
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = preset(args.model)
+    ecfg = EngineConfig(max_num_seqs=max(64, args.batch), max_batched_tokens=8192, max_model_len=args.ctx + 64,
+                        kv_memory_gb=40, prefix_caching=False)
+    llm = load(args.model, device=dev, engine_config=ecfg, config=cfg)
+    eng = llm.engine
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, cfg.vocab_size, (args.ctx,), generator=g).tolist() for _ in range(args.batch)]
+    sp = SamplingParams(max_new_tokens=48, ignore_eos=True)
+    for p in prompts:
+        eng.add_request(p, sp)
+    # run until every sequence is decoding
+    while True:
+        eng.step()
+        if eng.stats["graph_steps"] > 0:
+            break
+    key = next(k for k in eng.graphs if k[1])
+    g_, out, n_launch = eng.graphs[key]
+    torch.cuda.synchronize(dev)
+    if args.replays:
+        torch.cuda.nvtx.range_push("decode_replay")
+        for _ in range(args.replays):
+            g_.replay()
+        torch.cuda.synchronize(dev)
+        torch.cuda.nvtx.range_pop()
+        print("replayed", args.replays, "launches/step", n_launch)
+        return
+    for _ in range(3):
+        g_.replay()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record()
+    for _ in range(args.iters):
+        g_.replay()
+    ev[1].record()
+    torch.cuda.synchronize(dev)
+    ms = ev[0].elapsed_time(ev[1]) / args.iters
+    ops.check_errors(dev)
+    nparam = cfg.num_params()
+    wbytes = 2 * nparam - (2 * cfg.vocab_size * cfg.hidden_size)  # embedding rows are gathered, not streamed
+    kv_bytes = 2 * 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_dim * args.batch * (args.ctx + 1)
+    hbm, _, src = peaks()
+    ach = (wbytes + kv_bytes) / (ms * 1e-3) / 1e12
+    print(json.dumps({"model": args.model, "batch": key[0], "ctx": args.ctx, "ms_per_step": round(ms, 3),
+                      "launches_per_step": n_launch, "weight_gb": round(wbytes / 1e9, 2),
+                      "kv_gb": round(kv_bytes / 1e9, 2), "achieved_tbs": round(ach, 2),
+                      "frac_hbm": round(ach / hbm, 3), "peak_source": src}))
+
+
+if __name__ == "__main__":
+    main()

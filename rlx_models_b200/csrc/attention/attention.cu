@@ -23,6 +23,7 @@
 
 #include "../common/b200.cuh"
 #include "../common/launch.h"
+#include "../common/pdl_launch.h"
 #include "../common/tma_host.h"
 
 namespace b200 {
@@ -54,6 +55,7 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring_or_merge);
   uint64_t* empty = full + NST;
 
+  pdl_wait();
   const int G = a.Hq / a.Hkv;
   const int bh = blockIdx.x;
   const int b = bh / a.Hkv;
@@ -82,6 +84,8 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
     fence_mbarrier_init();
   }
   __syncthreads();
+  pdl_wait();
+  pdl_trigger();
 
   const float scale_log2 = a.scale * kLog2e;
   float m_r[2] = {kNegInf, kNegInf}, l_r[2] = {0.f, 0.f};
@@ -274,6 +278,8 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
 
 template <int D>
 __global__ void decode_merge_kernel(AttnArgs a, int nsplit) {
+  pdl_wait();
+  pdl_trigger();
   const int bh = blockIdx.x;  // b * Hq + head
   const int head = bh % a.Hq;
   const float* ml = a.ws + (int64_t)a.B * a.Hq * nsplit * D;
@@ -319,6 +325,8 @@ __global__ void __launch_bounds__(288) prefill_attn_kernel(const __grid_constant
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + NST * Cf::STAGE_BYTES);
   uint64_t* empty = full + NST;
 
+  pdl_wait();
+  pdl_trigger();
   const int G = a.Hq / a.Hkv;
   const int b = blockIdx.x / q_tiles;
   const int qt = blockIdx.x % q_tiles;
@@ -557,15 +565,15 @@ int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
     auto k = decode_attn_kernel<128, NST>;
     static bool once = false;
     if (!once) { set_smem(k, DecCfg<128, NST>::SMEM, a.device); once = true; }
-    k<<<grid, 160, DecCfg<128, NST>::SMEM, st>>>(tk, tv, a);
-    if (splits > 1) decode_merge_kernel<128><<<a.B * a.Hq, 128, 0, st>>>(a, splits);
+    launch_pdl(k, grid, dim3(160), DecCfg<128, NST>::SMEM, st, tk, tv, a);
+    if (splits > 1) launch_pdl(decode_merge_kernel<128>, dim3(a.B * a.Hq), dim3(128), 0, st, a, splits);
   } else {
     constexpr int NST = 8;
     auto k = decode_attn_kernel<64, NST>;
     static bool once = false;
     if (!once) { set_smem(k, DecCfg<64, NST>::SMEM, a.device); once = true; }
-    k<<<grid, 160, DecCfg<64, NST>::SMEM, st>>>(tk, tv, a);
-    if (splits > 1) decode_merge_kernel<64><<<a.B * a.Hq, 64, 0, st>>>(a, splits);
+    launch_pdl(k, grid, dim3(160), DecCfg<64, NST>::SMEM, st, tk, tv, a);
+    if (splits > 1) launch_pdl(decode_merge_kernel<64>, dim3(a.B * a.Hq), dim3(64), 0, st, a, splits);
   }
   return splits > 1 ? 2 : 1;
 }
@@ -587,13 +595,13 @@ void prefill_attention_launch(const AttnArgs& a, cudaStream_t st) {
     auto k = prefill_attn_kernel<128, NST>;
     static bool once = false;
     if (!once) { set_smem(k, PreCfg<128, NST>::SMEM, a.device); once = true; }
-    k<<<grid, 288, PreCfg<128, NST>::SMEM, st>>>(tk, tv, a, q_tiles, rows_tok);
+    launch_pdl(k, grid, dim3(288), PreCfg<128, NST>::SMEM, st, tk, tv, a, q_tiles, rows_tok);
   } else {
     constexpr int NST = 3;
     auto k = prefill_attn_kernel<64, NST>;
     static bool once = false;
     if (!once) { set_smem(k, PreCfg<64, NST>::SMEM, a.device); once = true; }
-    k<<<grid, 288, PreCfg<64, NST>::SMEM, st>>>(tk, tv, a, q_tiles, rows_tok);
+    launch_pdl(k, grid, dim3(288), PreCfg<64, NST>::SMEM, st, tk, tv, a, q_tiles, rows_tok);
   }
 }
 

@@ -25,7 +25,7 @@ void check_cuda(const Tensor& t, const char* name) {
 
 void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const optional<Tensor>& residual,
             const optional<Tensor>& bias, double alpha, Tensor& ws, Tensor& sem, Tensor& status, int64_t swap,
-            int64_t bn, int64_t splits) {
+            int64_t bn, int64_t splits, const optional<Tensor>& trace) {
   check_cuda(x, "x");
   check_cuda(w, "w");
   check_cuda(out, "out");
@@ -40,7 +40,8 @@ void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const o
   } else {
     TORCH_CHECK(out.size(0) == M && out.size(1) == N, "b200.linear: out shape");
   }
-  TORCH_CHECK((mode == 1) == (out.scalar_type() == at::kFloat), "b200.linear: out dtype");
+  TORCH_CHECK((mode == 1 || mode == 3) == (out.scalar_type() == at::kFloat), "b200.linear: out dtype");
+  TORCH_CHECK(mode != 3 || (M <= 128 && out.is_contiguous() && N % 4 == 0), "b200.linear(acc): M <= 128, N % 4");
   c10::cuda::CUDAGuard g(x.device());
   b200::LinearArgs a{};
   a.x = x.data_ptr();
@@ -74,6 +75,8 @@ void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const o
   a.sem_elems = sem.numel();
   a.status = status.data_ptr<int>();
   a.device = x.get_device();
+  if (trace.has_value() && trace->defined())
+    a.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
   b200::linear_launch(a, cur_stream(x));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -95,7 +98,7 @@ void rmsnorm(const Tensor& x, const Tensor& w, Tensor& out, double eps, const op
   check_cuda(x, "x");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "b200.rmsnorm: x");
   const int64_t T = x.size(0), H = x.size(1);
-  TORCH_CHECK(H % 256 == 0, "b200.rmsnorm: hidden % 256");
+  TORCH_CHECK(H % 8 == 0, "b200.rmsnorm: hidden % 8");
   TORCH_CHECK(w.numel() == H && w.scalar_type() == at::kBFloat16, "b200.rmsnorm: weight");
   TORCH_CHECK(out.size(0) == T && out.size(1) == H && out.stride(1) == 1, "b200.rmsnorm: out");
   if (residual_in.has_value() && residual_in->defined())
@@ -115,7 +118,9 @@ void qkv_rope(const Tensor& qkv, const optional<Tensor>& q_norm, const optional<
               const optional<Tensor>& k_out, const optional<Tensor>& v_out, int64_t Hq, int64_t Hkv, int64_t D,
               double eps) {
   check_cuda(qkv, "qkv");
-  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.dim() == 2 && qkv.stride(1) == 1, "b200.qkv_rope: qkv");
+  TORCH_CHECK((qkv.scalar_type() == at::kBFloat16 || qkv.scalar_type() == at::kFloat) && qkv.dim() == 2 &&
+                  qkv.stride(1) == 1,
+              "b200.qkv_rope: qkv");
   TORCH_CHECK(qkv.size(1) == (Hq + 2 * Hkv) * D, "b200.qkv_rope: qkv width");
   TORCH_CHECK(D == 64 || D == 128, "b200.qkv_rope: head_dim 64 or 128");
   TORCH_CHECK(positions.scalar_type() == at::kInt && positions.numel() == qkv.size(0), "b200.qkv_rope: positions");
@@ -128,6 +133,7 @@ void qkv_rope(const Tensor& qkv, const optional<Tensor>& q_norm, const optional<
   c10::cuda::CUDAGuard g(qkv.device());
   b200::QkvRopeArgs a{};
   a.qkv = qkv.data_ptr();
+  if (qkv.scalar_type() == at::kFloat) a.qkv_f32 = qkv.data_ptr<float>();
   a.ld_qkv = qkv.stride(0);
   a.q_norm = opt_ptr(q_norm);
   a.k_norm = opt_ptr(k_norm);
@@ -256,9 +262,152 @@ void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ---------------------------------------------------------------------------
+// Symmetric memory: raw device buffers shared between ranks by CUDA IPC.
+// ---------------------------------------------------------------------------
+int64_t symm_malloc(int64_t bytes, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaMalloc(&p, (size_t)bytes));
+  C10_CUDA_CHECK(cudaMemset(p, 0, (size_t)bytes));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_free(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  C10_CUDA_CHECK(cudaFree(reinterpret_cast<void*>(ptr)));
+}
+
+py::bytes ipc_handle(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  cudaIpcMemHandle_t h;
+  C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(ptr)));
+  return py::bytes(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+
+int64_t ipc_open(py::bytes handle, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  std::string s = handle;
+  TORCH_CHECK(s.size() == sizeof(cudaIpcMemHandle_t), "b200.ipc_open: bad handle size");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, s.data(), sizeof(h));
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  C10_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)));
+}
+
+Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> sizes, at::ScalarType dtype, int64_t device) {
+  auto opts = at::TensorOptions().dtype(dtype).device(at::kCUDA, (c10::DeviceIndex)device);
+  return torch::from_blob(reinterpret_cast<void*>(ptr), sizes, opts);
+}
+
+// GEMM in reduce-scatter push mode (see gemm_sm100.cuh). peer_out / peer_flags
+// are device int64 arrays of peer pointers; epoch / done_ctr are local uint32.
+void linear_push(const Tensor& x, const Tensor& w, const optional<Tensor>& bias, int64_t rpr, int64_t ld_out,
+                 int64_t slot_elems, int64_t my_rank, int64_t world, const Tensor& peer_out,
+                 const Tensor& peer_flags, const Tensor& epoch, const Tensor& done_ctr, Tensor& ws, Tensor& sem,
+                 Tensor& status) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && x.dim() == 2 && w.dim() == 2,
+              "b200.linear_push: bf16 2-D");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && x.size(1) == w.size(1), "b200.linear_push: shapes");
+  TORCH_CHECK(peer_out.scalar_type() == at::kLong && peer_out.numel() == world && peer_flags.numel() == world,
+              "b200.linear_push: peer arrays");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::LinearArgs a{};
+  a.x = x.data_ptr();
+  a.ldx = x.stride(0);
+  a.w = w.data_ptr();
+  a.ldw = w.stride(0);
+  a.out = nullptr;
+  a.ldo = ld_out;
+  a.residual = nullptr;
+  a.bias = opt_ptr(bias);
+  a.M = x.size(0);
+  a.N = w.size(0);
+  a.K = x.size(1);
+  a.mode = 0;
+  a.alpha = 1.f;
+  a.swap = -1;
+  a.bn = 0;
+  a.splits = 0;
+  a.ws = ws.data_ptr<float>();
+  a.ws_elems = ws.numel();
+  a.sem = sem.data_ptr<int>();
+  a.sem_elems = sem.numel();
+  a.status = status.data_ptr<int>();
+  a.device = x.get_device();
+  a.peer_out = reinterpret_cast<void* const*>(peer_out.data_ptr<int64_t>());
+  a.rpr = (int)rpr;
+  a.slot_elems = slot_elems;
+  a.my_rank = (int)my_rank;
+  a.world = (int)world;
+  a.epoch = reinterpret_cast<const unsigned*>(epoch.data_ptr<int>());
+  a.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr<int>());
+  a.peer_flags = reinterpret_cast<unsigned* const*>(peer_flags.data_ptr<int64_t>());
+  b200::linear_launch(a, cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rs_norm_ag(const optional<Tensor>& recv, Tensor& h, const Tensor& norm_w, const Tensor& peer_gath,
+                const Tensor& rs_flags, const Tensor& ag_flags, const Tensor& peer_ag_flags, Tensor& epoch,
+                Tensor& cta_ctr, int64_t M, int64_t rpr, int64_t world, int64_t rank, int64_t slot_elems,
+                double eps, Tensor& status) {
+  check_cuda(h, "h");
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous(), "b200.rs_norm_ag: h");
+  c10::cuda::CUDAGuard g(h.device());
+  b200::RsNormAgArgs a{};
+  a.recv = opt_ptr(recv);
+  a.h = h.data_ptr();
+  a.norm_w = norm_w.data_ptr();
+  a.peer_gath = reinterpret_cast<void* const*>(peer_gath.data_ptr<int64_t>());
+  a.rs_flags = reinterpret_cast<const unsigned*>(rs_flags.data_ptr<int>());
+  a.ag_flags = reinterpret_cast<const unsigned*>(ag_flags.data_ptr<int>());
+  a.peer_ag_flags = reinterpret_cast<unsigned* const*>(peer_ag_flags.data_ptr<int64_t>());
+  a.epoch = reinterpret_cast<unsigned*>(epoch.data_ptr<int>());
+  a.cta_ctr = reinterpret_cast<unsigned*>(cta_ctr.data_ptr<int>());
+  a.M = (int)M;
+  a.H = (int)h.size(1);
+  a.rpr = (int)rpr;
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.do_reduce = a.recv != nullptr;
+  a.slot_elems = slot_elems;
+  a.eps = (float)eps;
+  a.status = status.data_ptr<int>();
+  b200::rs_norm_ag_launch(a, cur_stream(h));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void add_rmsnorm_acc(Tensor& acc, Tensor& h, const Tensor& w, Tensor& out, double eps) {
+  check_cuda(acc, "acc");
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && h.is_contiguous() &&
+                  h.scalar_type() == at::kBFloat16 && acc.sizes() == h.sizes() && h.size(1) % 8 == 0,
+              "b200.add_rmsnorm_acc: shapes");
+  c10::cuda::CUDAGuard g(acc.device());
+  b200::add_rmsnorm_acc_launch(acc.data_ptr<float>(), h.data_ptr(), w.data_ptr(), out.data_ptr(), out.stride(0),
+                               h.size(0), h.size(1), (float)eps, cur_stream(acc));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void swiglu_acc(Tensor& acc, Tensor& out) {
+  check_cuda(acc, "acc");
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && out.is_contiguous() &&
+                  acc.size(1) == 2 * out.size(1) && out.size(1) % 64 == 0 && acc.size(0) == out.size(0),
+              "b200.swiglu_acc: shapes");
+  c10::cuda::CUDAGuard g(acc.device());
+  b200::swiglu_acc_launch(acc.data_ptr<float>(), out.data_ptr(), out.size(0), out.size(1), cur_stream(acc));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
-  m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues");
+  m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none());
   m.def("embedding", &embedding);
   m.def("rmsnorm", &rmsnorm);
   m.def("qkv_rope", &qkv_rope);
@@ -266,4 +415,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prefill_attention", &prefill_attention);
   m.def("argmax", &argmax);
   m.def("sample", &sample);
+  m.def("symm_malloc", &symm_malloc);
+  m.def("symm_free", &symm_free);
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("tensor_from_ptr", &tensor_from_ptr);
+  m.def("linear_push", &linear_push);
+  m.def("rs_norm_ag", &rs_norm_ag);
+  m.def("add_rmsnorm_acc", &add_rmsnorm_acc);
+  m.def("swiglu_acc", &swiglu_acc);
 }

@@ -1,0 +1,158 @@
+// Tensor-parallel residual-stream collective fused with RMSNorm, over NVLink
+// peer memory (no NCCL, no multicast loads).
+//
+// One row-parallel op of the sequence-parallel TP decoder is two kernels:
+//   1. the tcgen05 GEMM in push mode: every output row (token) of this rank's
+//      partial product is stored straight into slot `rank` of the row
+//      owner's receive buffer over NVLink, tile by tile as the MMAs finish
+//      (reduce-scatter fused into the GEMM epilogue); the GEMM's last CTA
+//      raises this op's epoch in every rank's rs_flags[rank];
+//   2. rs_norm_ag (this file): each rank waits for all rs flags, sums the
+//      `world` partial slots of the rows it owns, adds its residual-stream
+//      shard (h = h + sum, bf16 like HF), computes RMSNorm(h) * w and writes the
+//      normalised row into every rank's gather buffer (all-gather by P2P
+//      stores). The last CTA raises ag flags on every rank and waits for all
+//      ranks' ag flags, then advances the local epoch.
+// After (2) every rank holds the full normalised activation [M, H] locally, the
+// input of the next column-parallel GEMM; the residual stream itself stays
+// sharded by rows (sequence parallel).
+//
+// Ordering: a rank reuses its receive / gather buffers only after an epoch
+// barrier that every peer passes after its last read of them (see
+// parallel/fused_tp.py). All waits are bounded (kWaitTimeoutNs) and report
+// kErrTimeoutPeer in the status word instead of hanging.
+#include <cuda_bf16.h>
+
+#include <algorithm>
+#include <stdexcept>
+
+#include "../common/b200.cuh"
+#include "../common/launch.h"
+#include "../common/pdl_launch.h"
+
+namespace b200 {
+
+
+constexpr int kRsThreads = 256;
+constexpr int kRsMaxChunks = 4;  // H <= 256 * 8 * 4 = 8192
+
+__global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgArgs a) {
+  __shared__ float red[kRsThreads / 32];
+  pdl_wait();
+  pdl_trigger();
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(a.epoch) + 1u;
+  const __nv_bfloat16* recv = reinterpret_cast<const __nv_bfloat16*>(a.recv);
+  __nv_bfloat16* hbuf = reinterpret_cast<__nv_bfloat16*>(a.h);
+  const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
+  __nv_bfloat16* const* pg = reinterpret_cast<__nv_bfloat16* const*>(a.peer_gath);
+  const int n_my = max(0, min(a.rpr, a.M - a.rank * a.rpr));
+  if (a.do_reduce) {
+    if (threadIdx.x < (unsigned)a.world) wait_flag_geq(a.rs_flags + threadIdx.x, e, a.status, 100 + threadIdx.x);
+    __syncthreads();
+  }
+  const int r = blockIdx.x;
+  if (r < n_my) {
+    const int nch = a.H / (kRsThreads * 8);
+    float v[kRsMaxChunks][8];
+#pragma unroll
+    for (int c = 0; c < kRsMaxChunks; ++c) {
+      if (c >= nch) break;
+      const int col = (c * kRsThreads + threadIdx.x) * 8;
+      const uint4 hv = *reinterpret_cast<const uint4*>(hbuf + (int64_t)r * a.H + col);
+      const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+      float s[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        s[2 * k] = 0.f;
+        s[2 * k + 1] = 0.f;
+      }
+      if (a.do_reduce) {
+        for (int q = 0; q < a.world; ++q) {
+          const uint4 pv = __ldcg(reinterpret_cast<const uint4*>(recv + q * a.slot_elems + (int64_t)r * a.H + col));
+          const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            s[2 * k] += bf16_lo(pw[k]);
+            s[2 * k + 1] += bf16_hi(pw[k]);
+          }
+        }
+        // residual stream in bf16: h = bf16(h + bf16(sum))
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float lo = __bfloat162float(__float2bfloat16(s[2 * k]));
+          const float hi = __bfloat162float(__float2bfloat16(s[2 * k + 1]));
+          o[k] = pack_bf16x2(bf16_lo(hw[k]) + lo, bf16_hi(hw[k]) + hi);
+          v[c][2 * k] = bf16_lo(o[k]);
+          v[c][2 * k + 1] = bf16_hi(o[k]);
+        }
+        *reinterpret_cast<uint4*>(hbuf + (int64_t)r * a.H + col) = make_uint4(o[0], o[1], o[2], o[3]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          v[c][2 * k] = bf16_lo(hw[k]);
+          v[c][2 * k + 1] = bf16_hi(hw[k]);
+        }
+      }
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < kRsMaxChunks; ++c) {
+      if (c >= nch) break;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss += v[c][k] * v[c][k];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < kRsThreads / 32 ? red[threadIdx.x] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = rsqrtf(red[0] / (float)a.H + a.eps);
+    const int64_t grow = (int64_t)(a.rank * a.rpr + r) * a.H;
+#pragma unroll
+    for (int c = 0; c < kRsMaxChunks; ++c) {
+      if (c >= nch) break;
+      const int col = (c * kRsThreads + threadIdx.x) * 8;
+      const uint4 wv = *reinterpret_cast<const uint4*>(nw + col);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float lo = __bfloat162float(__float2bfloat16(v[c][2 * k] * inv)) * bf16_lo(ww[k]);
+        const float hi = __bfloat162float(__float2bfloat16(v[c][2 * k + 1] * inv)) * bf16_hi(ww[k]);
+        o[k] = pack_bf16x2(lo, hi);
+      }
+      const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+      // all-gather: the same normalised row into every rank's gather buffer
+      for (int q = 0; q < a.world; ++q) *reinterpret_cast<uint4*>(pg[q] + grow + col) = ov;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned old = atomicAdd(a.cta_ctr, 1u);
+    if (old == gridDim.x - 1) {
+      __threadfence_system();
+      for (int q = 0; q < a.world; ++q) st_release_sys_u32(a.peer_ag_flags[q] + a.rank, e);
+      for (int q = 0; q < a.world; ++q) wait_flag_geq(a.ag_flags + q, e, a.status, 200 + q);
+      *a.cta_ctr = 0;
+      __threadfence();
+      *reinterpret_cast<volatile unsigned*>(a.epoch) = e;
+    }
+  }
+}
+
+void rs_norm_ag_launch(const RsNormAgArgs& a, cudaStream_t st) {
+  if (a.H % (kRsThreads * 8) != 0 || a.H > kRsThreads * 8 * kRsMaxChunks)
+    throw std::runtime_error("b200.rs_norm_ag: hidden must be a multiple of 2048 and <= 8192");
+  const int n_my = std::max(0, std::min(a.rpr, a.M - a.rank * a.rpr));
+  launch_pdl(rs_norm_ag_kernel, dim3(std::max(1, n_my)), dim3(kRsThreads), 0, st, a);
+}
+
+}  // namespace b200

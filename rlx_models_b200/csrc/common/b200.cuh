@@ -44,7 +44,7 @@ constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)::"memory");
   return t;
 }
 
@@ -304,6 +304,33 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// System-scope release store / acquire load of a 32-bit flag (peer memory).
+__device__ __forceinline__ void st_release_sys_u32(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until *flag >= target (wrap-safe compare). Returns false and
+// records kErrTimeoutPeer after kWaitTimeoutNs.
+__device__ __forceinline__ bool wait_flag_geq(const unsigned* flag, unsigned target, int* status, int detail) {
+  if ((int)(ld_acquire_sys_u32(flag) - target) >= 0) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t i = 0;; ++i) {
+    if ((int)(ld_acquire_sys_u32(flag) - target) >= 0) return true;
+    if ((i & 63u) == 63u) {
+      __nanosleep(64);
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        report_error(status, kErrTimeoutPeer, detail);
+        return false;
+      }
+    }
+  }
+}
+
 // Vector fp32 reduction into global memory (no return value, sm_90+).
 __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
@@ -314,4 +341,18 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+}  // namespace b200
+
+namespace b200 {
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch (PDL). Kernels are launched with
+// programmatic stream serialization, so the next kernel on the stream may
+// start its prologue (barrier init, TMEM alloc, weight-tile prefetch) while
+// this one finishes. pdl_wait() blocks until the previous grid has completed
+// and its memory is visible; every kernel calls it before touching data a
+// previous kernel produced. pdl_trigger() lets the dependent grid launch.
+// Both are no-ops when the kernel was launched without the attribute.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 }  // namespace b200

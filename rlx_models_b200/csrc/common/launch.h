@@ -30,8 +30,35 @@ struct LinearArgs {
   int64_t sem_elems;
   int* status;
   int device;
+  // tensor-parallel reduce-scatter push mode (see gemm_sm100.cuh); null = off
+  void* const* peer_out = nullptr;
+  int rpr = 0;
+  int64_t slot_elems = 0;
+  int my_rank = 0, world = 1;
+  const unsigned* epoch = nullptr;
+  unsigned* done_ctr = nullptr;
+  unsigned* const* peer_flags = nullptr;
+  unsigned long long* trace = nullptr;  // debug timeline
 };
 void linear_launch(const LinearArgs& a, cudaStream_t st);
+
+// ---------------- tensor-parallel fused collective ----------------
+struct RsNormAgArgs {
+  const void* recv;           // local [world][rpr][H] (reduce inputs), unused if !do_reduce
+  void* h;                    // local residual shard [rpr][H]
+  const void* norm_w;         // [H]
+  void* const* peer_gath;     // [world] gather buffers [M][H]
+  const unsigned* rs_flags;            // local [world]
+  const unsigned* ag_flags;            // local [world]
+  unsigned* const* peer_ag_flags;      // [world] -> each rank's ag_flags
+  unsigned* epoch;                     // local op counter
+  unsigned* cta_ctr;                   // local arrival counter (self-resetting)
+  int M, H, rpr, world, rank, do_reduce;
+  int64_t slot_elems;                  // rpr_max * H
+  float eps;
+  int* status;
+};
+void rs_norm_ag_launch(const RsNormAgArgs& a, cudaStream_t st);
 
 // ---------------- norms / rope / embedding ----------------
 void embedding_launch(const int32_t* ids, const void* table, void* out, int64_t T, int64_t H, int64_t V,
@@ -42,6 +69,7 @@ void rmsnorm_launch(const void* x, int64_t ldx, const void* residual_in, void* r
 
 struct QkvRopeArgs {
   const void* qkv;  // [T, (Hq + 2 Hkv) * D] bf16
+  float* qkv_f32 = nullptr;  // or: fp32 sums from the accumulate-only GEMM (zeroed after use)
   int64_t ld_qkv;
   const void* q_norm;  // [D] or null
   const void* k_norm;  // [D] or null
@@ -60,6 +88,9 @@ struct QkvRopeArgs {
   float eps;
 };
 void qkv_rope_launch(const QkvRopeArgs& a, cudaStream_t st);
+void add_rmsnorm_acc_launch(float* acc, void* h, const void* w, void* out, int64_t ldo, int64_t T, int64_t H,
+                            float eps, cudaStream_t st);
+void swiglu_acc_launch(float* acc, void* out, int64_t T, int64_t I, cudaStream_t st);
 
 // ---------------- attention ----------------
 struct AttnArgs {

@@ -11,6 +11,7 @@
 #include <stdexcept>
 #include <string>
 
+#include "../common/pdl_launch.h"
 #include "../common/tma_host.h"
 #include "gemm_sm100.cuh"
 
@@ -26,7 +27,7 @@ static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params&
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM_BYTES);
     attr_done |= (1ull << device);
   }
-  kern<<<grid, kThreads, Cfg<BN>::SMEM_BYTES, st>>>(ta, tb, p);
+  launch_pdl(kern, dim3(grid), dim3(kThreads), Cfg<BN>::SMEM_BYTES, st, ta, tb, p);
 }
 
 template <int EPI>
@@ -77,18 +78,30 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
   const int tiles = p.num_m * p.num_n;
   int sp = a.splits;
   if (sp <= 0) {
+    // Split-K only to fill the machine: pick the factor minimising
+    // waves * k-tiles-per-unit plus a per-split reduction cost (in k-tiles).
     sp = 1;
-    if (tiles * 2 <= sms) {
-      sp = sms / tiles;
-      sp = std::min(sp, std::max(1, p.k_tiles / 4));
-      sp = std::min(sp, 32);
+    double best = 1e30;
+    // large tile counts already fill the machine; their partial tiles would
+    // also outgrow the accumulator
+    const int max_sp = (tiles >= 2 * sms) ? 1 : std::max(1, std::min(16, p.k_tiles / 4));
+    for (int s = 1; s <= max_sp; ++s) {
+      const int kts = (p.k_tiles + s - 1) / s;
+      const int waves = (tiles * s + sms - 1) / sms;
+      const double cost = (double)waves * kts + (s > 1 ? (epi == gemm::EPI_ACC ? 0.5 : 2.0) * s : 0.0);
+      if (cost < best - 1e-9) {
+        best = cost;
+        sp = s;
+      }
     }
   }
   sp = std::max(1, std::min(sp, p.k_tiles));
+  if (sp > 1 && epi != gemm::EPI_ACC && (int64_t)tiles * gemm::kBM * BN > a.ws_elems) sp = 1;
   p.kt_per_split = (p.k_tiles + sp - 1) / sp;
   p.splits = (p.k_tiles + p.kt_per_split - 1) / p.kt_per_split;
   p.num_units = tiles * p.splits;
-  if (p.splits > 1) {
+  if (epi == gemm::EPI_ACC && !sw) throw std::runtime_error("b200.linear: accumulate mode needs swap-AB (M <= 128)");
+  if (p.splits > 1 && epi != gemm::EPI_ACC) {
     if (a.ws_elems < (int64_t)tiles * gemm::kBM * BN || a.ws == nullptr)
       throw std::runtime_error("b200.linear: split-K accumulator too small");
     if (a.sem_elems < tiles || a.sem == nullptr) throw std::runtime_error("b200.linear: semaphore buffer too small");
@@ -103,9 +116,21 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
   p.bias_on_i = sw ? 1 : 0;
   p.alpha = a.alpha;
   p.swiglu_on_i = sw ? 1 : 0;
+  p.w_is_a = sw ? 1 : 0;
   p.ws = a.ws;
   p.sem = a.sem;
   p.status = a.status;
+  p.peer_out = a.peer_out;
+  p.rpr = a.rpr;
+  p.slot_elems = a.slot_elems;
+  p.my_rank = a.my_rank;
+  p.world = a.world;
+  p.epoch = a.epoch;
+  p.done_ctr = a.done_ctr;
+  p.peer_flags = a.peer_flags;
+  p.trace = a.trace;
+  if (p.peer_out != nullptr && (p.rpr <= 0 || p.done_ctr == nullptr || p.peer_flags == nullptr || p.epoch == nullptr))
+    throw std::runtime_error("b200.linear: incomplete push-mode arguments");
 
   CUtensorMap ta = make_tmap_2d(A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.MA, K, lda, gemm::kBM, gemm::kBK);
   CUtensorMap tb = make_tmap_2d(B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.NB, K, ldb, BN, gemm::kBK);
@@ -114,6 +139,7 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
     case gemm::EPI_BF16: gemm::launch_bn<gemm::EPI_BF16>(BN, ta, tb, p, grid, st, a.device); break;
     case gemm::EPI_F32: gemm::launch_bn<gemm::EPI_F32>(BN, ta, tb, p, grid, st, a.device); break;
     case gemm::EPI_SWIGLU: gemm::launch_bn<gemm::EPI_SWIGLU>(BN, ta, tb, p, grid, st, a.device); break;
+    case gemm::EPI_ACC: gemm::launch_bn<gemm::EPI_ACC>(BN, ta, tb, p, grid, st, a.device); break;
     default: throw std::runtime_error("b200.linear: bad mode");
   }
 }

@@ -30,7 +30,11 @@
 namespace b200 {
 namespace gemm {
 
-enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2 };
+// EPI_ACC (swap-AB only): accumulate-only split-K. Every unit adds its fp32
+// partial into the caller's [tokens][features] buffer with vector red.add and
+// leaves; there is no semaphore and no last-CTA tail. The consumer kernel
+// (add+RMSNorm, QK-norm/RoPE, SwiGLU) reads the sum and writes zeros back.
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU = 2, EPI_ACC = 3 };
 
 struct Params {
   int MA, NB, K;
@@ -44,10 +48,36 @@ struct Params {
   int bias_on_i;
   float alpha;
   int swiglu_on_i;
+  int w_is_a;  // 1: A is the weight operand (swap-AB), 0: B is
   float* ws;
   int* sem;
   int* status;
+  // Reduce-scatter push mode (tensor parallel). When peer_out != nullptr,
+  // output row `t` (a token) is written to rank owner = t / rpr, into slot
+  // `my_rank` of that rank's receive buffer: peer_out[owner] + my_rank *
+  // slot_elems + (t % rpr) * ldc. After the last tile, the last CTA writes
+  // epoch+1 into peer_flags[q][my_rank] of every rank q (release, system
+  // scope), so owners know when all partials for this op have landed.
+  void* const* peer_out;
+  int rpr;
+  int64_t slot_elems;
+  int my_rank, world;
+  const unsigned* epoch;
+  unsigned* done_ctr;
+  unsigned* const* peer_flags;
+  unsigned long long* trace;  // optional per-CTA timeline ([grid][16] globaltimer ns), debug only
 };
+
+// Base pointer of output row `t` (a token index), local or pushed to its owner.
+template <typename T>
+__device__ __forceinline__ T* out_row(const Params& p, int t, int64_t ld) {
+  if (p.peer_out == nullptr) return reinterpret_cast<T*>(p.C) + (int64_t)t * ld;
+  const int owner = t / p.rpr;
+  return reinterpret_cast<T*>(p.peer_out[owner]) + (int64_t)p.my_rank * p.slot_elems + (int64_t)(t - owner * p.rpr) * ld;
+}
+
+#define B200_GEMM_TRACE(i) \
+  if (p.trace != nullptr) p.trace[blockIdx.x * 16 + (i)] = globaltimer_ns();
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
@@ -114,7 +144,7 @@ __device__ __forceinline__ void store_chunk(const Params& p, int i, int j0, floa
     }
   }
   if (EPI == EPI_F32) {
-    float* c = reinterpret_cast<float*>(p.C) + (int64_t)i * p.ldc_i;
+    float* c = out_row<float>(p, i, p.ldc_i);
     if (p.ldc_j == 1 && full && ((reinterpret_cast<uintptr_t>(c + j0) & 15u) == 0)) {
 #pragma unroll
       for (int q = 0; q < 8; ++q)
@@ -125,7 +155,7 @@ __device__ __forceinline__ void store_chunk(const Params& p, int i, int j0, floa
         if (j0 + t < p.NB) c[(int64_t)(j0 + t) * p.ldc_j] = v[t];
     }
   } else {
-    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (int64_t)i * p.ldc_i;
+    __nv_bfloat16* c = out_row<__nv_bfloat16>(p, i, p.ldc_i);
     if (p.ldc_j == 1 && full && ((reinterpret_cast<uintptr_t>(c + j0) & 15u) == 0)) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -190,7 +220,7 @@ __device__ __forceinline__ void store_row32(const Params& p, int j, int fo, int 
     }
   }
   if (EPI == EPI_F32) {
-    float* c = reinterpret_cast<float*>(p.C) + (int64_t)j * p.ldc_j + fo;
+    float* c = out_row<float>(p, j, p.ldc_j) + fo;
     if (full && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0)) {
 #pragma unroll
       for (int q = 0; q < 8; ++q)
@@ -201,7 +231,7 @@ __device__ __forceinline__ void store_row32(const Params& p, int j, int fo, int 
         if (fo + t < nfeat) c[t] = o[t];
     }
   } else {
-    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (int64_t)j * p.ldc_j + fo;
+    __nv_bfloat16* c = out_row<__nv_bfloat16>(p, j, p.ldc_j) + fo;
     if (full && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0)) {
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -242,6 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) B200_GEMM_TRACE(0);
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -266,6 +297,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_trigger();
+  if (threadIdx.x == 0) B200_GEMM_TRACE(1);
 
   if (warp == 0) {
     if (elect_one_sync()) {
@@ -274,28 +307,55 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       uint32_t issued = 0;
       bool ok = true;
+      // PDL prologue: the weight operand does not depend on the previous
+      // kernel, so the first ring's worth of weight tiles is requested before
+      // griddepcontrol.wait; the activation halves of those stages follow it.
+      int npre = 0;
+      if ((int)blockIdx.x < p.num_units) {
+        int m_tile, n_tile, ks, tile;
+        unit_to_tile(p, blockIdx.x, m_tile, n_tile, ks, tile);
+        const int kb = ks * p.kt_per_split;
+        npre = min(STAGES, min(p.k_tiles, kb + p.kt_per_split) - kb);
+        for (int q = 0; q < npre; ++q) {
+          uint8_t* sa = ring + q * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[q], C::STAGE_BYTES);
+          if (p.w_is_a) tma_load_2d(sa, &tmA, &full[q], (kb + q) * kBK, m_tile * kBM);
+          else tma_load_2d(sa + C::A_BYTES, &tmB, &full[q], (kb + q) * kBK, n_tile * BN);
+        }
+      }
+      B200_GEMM_TRACE(2);
+      pdl_wait();
+      B200_GEMM_TRACE(3);
+      bool first = true;
       for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
         int m_tile, n_tile, ks, tile;
         unit_to_tile(p, u, m_tile, n_tile, ks, tile);
         const int kb = ks * p.kt_per_split;
         const int ke = min(p.k_tiles, kb + p.kt_per_split);
         for (int kt = kb; kt < ke; ++kt) {
-          if (!mbar_wait(&empty[stage], phase ^ 1, p.status, kErrTimeoutEmpty) || *abort_flag) {
-            *abort_flag = 1;
-            ok = false;
-            break;
-          }
           uint8_t* sa = ring + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
-          mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-          tma_load_2d(sa, &tmA, &full[stage], kt * kBK, m_tile * kBM);
-          tma_load_2d(sb, &tmB, &full[stage], kt * kBK, n_tile * BN);
+          if (first && kt - kb < npre) {
+            // weight half already in flight; issue the activation half
+            if (p.w_is_a) tma_load_2d(sb, &tmB, &full[stage], kt * kBK, n_tile * BN);
+            else tma_load_2d(sa, &tmA, &full[stage], kt * kBK, m_tile * kBM);
+          } else {
+            if (!mbar_wait(&empty[stage], phase ^ 1, p.status, kErrTimeoutEmpty) || *abort_flag) {
+              *abort_flag = 1;
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
+            tma_load_2d(sa, &tmA, &full[stage], kt * kBK, m_tile * kBM);
+            tma_load_2d(sb, &tmB, &full[stage], kt * kBK, n_tile * BN);
+          }
           ++issued;
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
+        first = false;
       }
       if (!ok) {
         // Error path: wait (bounded) for the loads this thread put in flight.
@@ -339,6 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          if (it == 0 && kt == kb) B200_GEMM_TRACE(4);
           tc_fence_after();
           const uint32_t a_addr = smem_u32(ring + stage * C::STAGE_BYTES);
           const uint32_t b_addr = a_addr + C::A_BYTES;
@@ -356,6 +417,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok) umma_commit(&accf[acc]);
       }
+      B200_GEMM_TRACE(5);
       if (!ok) {
         umma_commit(drain);
         mbar_wait(drain, 0, p.status, kErrTimeoutDrain);
@@ -367,6 +429,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quad * 32 + lane;
     const int ew = warp - 2;
     const int et = ew * 32 + lane;  // 0..127 epilogue thread id
+    pdl_wait();  // residual / workspace / outputs may belong to the previous kernel
     const bool swap_out = (p.ldc_i == 1);
     int it = 0;
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x, ++it) {
@@ -378,12 +441,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort_flag = 1;
         break;
       }
+      if (et == 0 && it == 0) B200_GEMM_TRACE(6);
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
       const int i = m_tile * kBM + row;
       const int jt = n_tile * BN;
       // fp32 accumulator of this tile in L2 (split-K); zero between uses
       float* acc_row = p.ws + (int64_t)tile * (kBM * BN) + (int64_t)row * BN;
+
+      if (EPI == EPI_ACC) {
+        float* dst = reinterpret_cast<float*>(p.C);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int t = 0; t < 32; ++t) xchg[t * 132 + row] = __uint_as_float(r[t]);
+          named_bar_sync(2, 128);
+          const int tl = et >> 2, seg = et & 3;
+          const int j = jt + c * 32 + tl;
+          const int f0 = m_tile * kBM + seg * 32;
+          if (j < p.NB && f0 < p.MA) {
+            float* drow = dst + (int64_t)j * p.ldc_j + f0;
+            const float* src = xchg + tl * 132 + seg * 32;
+            if (f0 + 32 <= p.MA) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                red_add_v4(drow + q * 4, src[q * 4] * p.alpha, src[q * 4 + 1] * p.alpha, src[q * 4 + 2] * p.alpha,
+                           src[q * 4 + 3] * p.alpha);
+            } else {
+              for (int t = 0; f0 + t < p.MA && t < 32; ++t) atomicAdd(drow + t, src[t] * p.alpha);
+            }
+          }
+          named_bar_sync(2, 128);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acce[acc]);
+        continue;
+      }
 
       if (p.splits > 1) {
         // Add this split's partial into the shared fp32 tile (fire-and-forget
@@ -408,6 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           *s_last = (old == p.splits - 1) ? 1 : 0;
         }
         named_bar_sync(1, 128);
+        if (et == 0 && it == 0) B200_GEMM_TRACE(7);
         if (*s_last == 0) continue;
         __threadfence();
       }
@@ -506,9 +604,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&acce[acc]);
       }
     }
+    if (et == 0) B200_GEMM_TRACE(8);
+    if (p.peer_out != nullptr) {
+      // Reduce-scatter completion: this CTA's pushes are issued; make them
+      // visible at system scope, count CTAs, and let the last one signal
+      // every rank (itself included) with this op's epoch.
+      __threadfence_system();
+      named_bar_sync(1, 128);
+      if (et == 0) {
+        const unsigned old = atomicAdd(p.done_ctr, 1u);
+        if (old == gridDim.x - 1) {
+          __threadfence_system();
+          const unsigned e = *reinterpret_cast<const volatile unsigned*>(p.epoch) + 1u;
+          for (int q = 0; q < p.world; ++q) st_release_sys_u32(p.peer_flags[q] + p.my_rank, e);
+          *p.done_ctr = 0;
+        }
+      }
+    }
   }
 
   __syncthreads();
+  if (threadIdx.x == 0) B200_GEMM_TRACE(9);
   if (warp == 2) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);

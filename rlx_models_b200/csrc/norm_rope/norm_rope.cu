@@ -16,11 +16,17 @@
 
 #include "../common/b200.cuh"
 #include "../common/launch.h"
+#include "../common/pdl_launch.h"
+
+#include <algorithm>
+#include <stdexcept>
 
 namespace b200 {
 
 __global__ void embedding_kernel(const int32_t* __restrict__ ids, const uint4* __restrict__ table,
                                  uint4* __restrict__ out, int64_t H8, int64_t V) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t t = blockIdx.x;
   int64_t id = ids[t];
   if (id < 0 || id >= V) id = 0;  // out-of-range ids read row 0 rather than faulting
@@ -32,79 +38,91 @@ __global__ void embedding_kernel(const int32_t* __restrict__ ids, const uint4* _
 void embedding_launch(const int32_t* ids, const void* table, void* out, int64_t T, int64_t H, int64_t V,
                       cudaStream_t st) {
   if (T == 0) return;
-  embedding_kernel<<<(unsigned)T, 256, 0, st>>>(ids, reinterpret_cast<const uint4*>(table),
-                                                 reinterpret_cast<uint4*>(out), H / 8, V);
+  launch_pdl(embedding_kernel, dim3((unsigned)T), dim3(256), 0, st, ids, reinterpret_cast<const uint4*>(table),
+             reinterpret_cast<uint4*>(out), H / 8, V);
 }
 
-// One warp per row. H % 256 == 0 (8 bf16 per lane per step).
+// One CTA per row, one 8-element vector (16 B) per thread and pass; the row
+// stays in registers between the sum-of-squares and the scaling pass.
+template <int VPT>
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
                                const __nv_bfloat16* __restrict__ res_in, __nv_bfloat16* __restrict__ res_out,
                                const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int64_t ldo,
-                               int64_t T, int H, float eps) {
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x & 31;
-  if (row >= T) return;
-  const __nv_bfloat16* xr = x + row * ldx;
+                               int H, float eps) {
+  __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
+  const int64_t row = blockIdx.x;
+  const int nv = H / 8;
+  float v[VPT][8];
   float ss = 0.f;
-  for (int c = lane * 8; c < H; c += 256) {
-    uint4 v = *reinterpret_cast<const uint4*>(xr + c);
-    uint32_t a[4] = {v.x, v.y, v.z, v.w};
-    if (res_in != nullptr) {
-      uint4 r = *reinterpret_cast<const uint4*>(res_in + row * (int64_t)H + c);
-      uint32_t b[4] = {r.x, r.y, r.z, r.w};
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        // residual stream is kept in bf16 (HF semantics): round the sum once
+  for (int k = 0; k < VPT; ++k) {
+    const int vi = threadIdx.x + k * blockDim.x;
+    if (vi >= nv) break;
+    const uint4 xv = *reinterpret_cast<const uint4*>(x + row * ldx + vi * 8);
+    uint32_t a[4] = {xv.x, xv.y, xv.z, xv.w};
+    if (res_in != nullptr) {
+      const uint4 r = *reinterpret_cast<const uint4*>(res_in + row * (int64_t)H + vi * 8);
+      const uint32_t b[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h)  // residual stream stays bf16 (HF): round the sum once
         a[h] = pack_bf16x2(bf16_lo(a[h]) + bf16_lo(b[h]), bf16_hi(a[h]) + bf16_hi(b[h]));
-      }
       if (res_out != nullptr)
-        *reinterpret_cast<uint4*>(res_out + row * (int64_t)H + c) = make_uint4(a[0], a[1], a[2], a[3]);
+        *reinterpret_cast<uint4*>(res_out + row * (int64_t)H + vi * 8) = make_uint4(a[0], a[1], a[2], a[3]);
     }
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      const float lo = bf16_lo(a[h]), hi = bf16_hi(a[h]);
-      ss += lo * lo + hi * hi;
+      v[k][2 * h] = bf16_lo(a[h]);
+      v[k][2 * h + 1] = bf16_hi(a[h]);
+      ss += v[k][2 * h] * v[k][2 * h] + v[k][2 * h + 1] * v[k][2 * h + 1];
     }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float inv = rsqrtf(ss / (float)H + eps);
-  const __nv_bfloat16* src = (res_in != nullptr && res_out != nullptr) ? res_out + row * (int64_t)H : xr;
-  for (int c = lane * 8; c < H; c += 256) {
-    uint4 v;
-    if (res_in != nullptr && res_out == nullptr) {
-      uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
-      uint4 r = *reinterpret_cast<const uint4*>(res_in + row * (int64_t)H + c);
-      uint32_t a[4] = {xv.x, xv.y, xv.z, xv.w}, b[4] = {r.x, r.y, r.z, r.w};
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
 #pragma unroll
-      for (int h = 0; h < 4; ++h)
-        a[h] = pack_bf16x2(bf16_lo(a[h]) + bf16_lo(b[h]), bf16_hi(a[h]) + bf16_hi(b[h]));
-      v = make_uint4(a[0], a[1], a[2], a[3]);
-    } else {
-      v = *reinterpret_cast<const uint4*>(src + c);
-    }
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
-    uint32_t a[4] = {v.x, v.y, v.z, v.w}, ww[4] = {wv.x, wv.y, wv.z, wv.w}, o[4];
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)H + eps);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int vi = threadIdx.x + k * blockDim.x;
+    if (vi >= nv) break;
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + vi * 8);
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
       // normalise in fp32, round to bf16, then scale by the bf16 weight
-      const float lo = __bfloat162float(__float2bfloat16(bf16_lo(a[h]) * inv)) * bf16_lo(ww[h]);
-      const float hi = __bfloat162float(__float2bfloat16(bf16_hi(a[h]) * inv)) * bf16_hi(ww[h]);
+      const float lo = __bfloat162float(__float2bfloat16(v[k][2 * h] * inv)) * bf16_lo(ww[h]);
+      const float hi = __bfloat162float(__float2bfloat16(v[k][2 * h + 1] * inv)) * bf16_hi(ww[h]);
       o[h] = pack_bf16x2(lo, hi);
     }
-    *reinterpret_cast<uint4*>(out + row * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(out + row * ldo + vi * 8) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
 void rmsnorm_launch(const void* x, int64_t ldx, const void* residual_in, void* residual_out, const void* w,
                     void* out, int64_t ldo, int64_t T, int64_t H, float eps, cudaStream_t st) {
   if (T == 0) return;
-  const int rows_per_block = 8;
-  const unsigned grid = (unsigned)((T + rows_per_block - 1) / rows_per_block);
-  rmsnorm_kernel<<<grid, rows_per_block * 32, 0, st>>>(
-      reinterpret_cast<const __nv_bfloat16*>(x), ldx, reinterpret_cast<const __nv_bfloat16*>(residual_in),
-      reinterpret_cast<__nv_bfloat16*>(residual_out), reinterpret_cast<const __nv_bfloat16*>(w),
-      reinterpret_cast<__nv_bfloat16*>(out), ldo, T, (int)H, eps);
+  const int nv = (int)(H / 8);
+  int threads = std::min(1024, (nv + 31) / 32 * 32);
+  const int vpt = (nv + threads - 1) / threads;
+  auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto rb = reinterpret_cast<const __nv_bfloat16*>(residual_in);
+  auto ro = reinterpret_cast<__nv_bfloat16*>(residual_out);
+  auto wb = reinterpret_cast<const __nv_bfloat16*>(w);
+  auto ob = reinterpret_cast<__nv_bfloat16*>(out);
+  if (vpt <= 1) launch_pdl(rmsnorm_kernel<1>, dim3((unsigned)T), dim3(threads), 0, st, xb, ldx, rb, ro, wb, ob, ldo, (int)H, eps);
+  else if (vpt <= 2) launch_pdl(rmsnorm_kernel<2>, dim3((unsigned)T), dim3(threads), 0, st, xb, ldx, rb, ro, wb, ob, ldo, (int)H, eps);
+  else if (vpt <= 4) launch_pdl(rmsnorm_kernel<4>, dim3((unsigned)T), dim3(threads), 0, st, xb, ldx, rb, ro, wb, ob, ldo, (int)H, eps);
+  else throw std::runtime_error("b200.rmsnorm: hidden size too large (max 32768)");
 }
 
 // One warp per (token, head) over q heads, k heads and v heads.
@@ -112,6 +130,8 @@ void rmsnorm_launch(const void* x, int64_t ldx, const void* residual_in, void* r
 // element d (< D/2) is d + D/2, held by lane (lane ^ 16).
 template <int E>
 __global__ void qkv_rope_kernel(QkvRopeArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int nh = a.Hq + 2 * a.Hkv;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -119,10 +139,21 @@ __global__ void qkv_rope_kernel(QkvRopeArgs a) {
   const int64_t t = gw / nh;
   const int h = (int)(gw % nh);
   const int D = 32 * E;
-  const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + t * a.ld_qkv + (int64_t)h * D;
   float x[E];
+  if (a.qkv_f32 != nullptr) {
+    // accumulate-only GEMM output: round the fp32 sum to bf16 (as the bf16
+    // GEMM epilogue would) and zero it for the next use
+    float* src = a.qkv_f32 + t * a.ld_qkv + (int64_t)h * D;
 #pragma unroll
-  for (int e = 0; e < E; ++e) x[e] = __bfloat162float(src[lane * E + e]);
+    for (int e = 0; e < E; ++e) {
+      x[e] = __bfloat162float(__float2bfloat16(__ldcg(src + lane * E + e)));
+      __stcg(src + lane * E + e, 0.f);
+    }
+  } else {
+    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.qkv) + t * a.ld_qkv + (int64_t)h * D;
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = __bfloat162float(src[lane * E + e]);
+  }
 
   const bool is_q = h < a.Hq;
   const bool is_k = !is_q && h < a.Hq + a.Hkv;
@@ -189,8 +220,129 @@ void qkv_rope_launch(const QkvRopeArgs& a, cudaStream_t st) {
   const int64_t warps = a.T * (a.Hq + 2 * a.Hkv);
   const int wpb = 8;
   const unsigned grid = (unsigned)((warps + wpb - 1) / wpb);
-  if (a.D == 128) qkv_rope_kernel<4><<<grid, wpb * 32, 0, st>>>(a);
-  else qkv_rope_kernel<2><<<grid, wpb * 32, 0, st>>>(a);
+  if (a.D == 128) launch_pdl(qkv_rope_kernel<4>, dim3(grid), dim3(wpb * 32), 0, st, a);
+  else launch_pdl(qkv_rope_kernel<2>, dim3(grid), dim3(wpb * 32), 0, st, a);
+}
+
+// ---------------------------------------------------------------------------
+// Consumers of the accumulate-only GEMM (fp32 [T, N] sums, zeroed after use).
+// ---------------------------------------------------------------------------
+
+// h = bf16(h + bf16(acc)); out = rmsnorm(h) * w; acc = 0.   One CTA per row.
+template <int VPT>
+__global__ void add_rmsnorm_acc_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ h,
+                                       const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
+                                       int64_t ldo, int H, float eps) {
+  __shared__ float red[32];
+  pdl_wait();
+  pdl_trigger();
+  const int64_t row = blockIdx.x;
+  const int nv = H / 8;
+  float v[VPT][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int vi = threadIdx.x + k * blockDim.x;
+    if (vi >= nv) break;
+    float4* ap = reinterpret_cast<float4*>(acc + row * (int64_t)H + vi * 8);
+    const float4 a0 = __ldcg(ap), a1 = __ldcg(ap + 1);
+    __stcg(ap, make_float4(0.f, 0.f, 0.f, 0.f));
+    __stcg(ap + 1, make_float4(0.f, 0.f, 0.f, 0.f));
+    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    uint4* hp = reinterpret_cast<uint4*>(h + row * (int64_t)H + vi * 8);
+    const uint4 hv = *hp;
+    const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float lo = __bfloat162float(__float2bfloat16(av[2 * q]));
+      const float hi = __bfloat162float(__float2bfloat16(av[2 * q + 1]));
+      o[q] = pack_bf16x2(bf16_lo(hw[q]) + lo, bf16_hi(hw[q]) + hi);
+      v[k][2 * q] = bf16_lo(o[q]);
+      v[k][2 * q + 1] = bf16_hi(o[q]);
+      ss += v[k][2 * q] * v[k][2 * q] + v[k][2 * q + 1] * v[k][2 * q + 1];
+    }
+    *hp = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)H + eps);
+#pragma unroll
+  for (int k = 0; k < VPT; ++k) {
+    const int vi = threadIdx.x + k * blockDim.x;
+    if (vi >= nv) break;
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + vi * 8);
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float lo = __bfloat162float(__float2bfloat16(v[k][2 * q] * inv)) * bf16_lo(ww[q]);
+      const float hi = __bfloat162float(__float2bfloat16(v[k][2 * q + 1] * inv)) * bf16_hi(ww[q]);
+      o[q] = pack_bf16x2(lo, hi);
+    }
+    *reinterpret_cast<uint4*>(out + row * ldo + vi * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+void add_rmsnorm_acc_launch(float* acc, void* h, const void* w, void* out, int64_t ldo, int64_t T, int64_t H,
+                            float eps, cudaStream_t st) {
+  if (T == 0) return;
+  const int nv = (int)(H / 8);
+  const int threads = std::min(1024, (nv + 31) / 32 * 32);
+  const int vpt = (nv + threads - 1) / threads;
+  auto hb = reinterpret_cast<__nv_bfloat16*>(h);
+  auto wb = reinterpret_cast<const __nv_bfloat16*>(w);
+  auto ob = reinterpret_cast<__nv_bfloat16*>(out);
+  if (vpt <= 1) launch_pdl(add_rmsnorm_acc_kernel<1>, dim3((unsigned)T), dim3(threads), 0, st, acc, hb, wb, ob, ldo, (int)H, eps);
+  else if (vpt <= 2) launch_pdl(add_rmsnorm_acc_kernel<2>, dim3((unsigned)T), dim3(threads), 0, st, acc, hb, wb, ob, ldo, (int)H, eps);
+  else if (vpt <= 4) launch_pdl(add_rmsnorm_acc_kernel<4>, dim3((unsigned)T), dim3(threads), 0, st, acc, hb, wb, ob, ldo, (int)H, eps);
+  else throw std::runtime_error("b200.add_rmsnorm_acc: hidden size too large");
+}
+
+// out[t, f] = silu(acc[t, g(f)]) * acc[t, g(f) + 64], g(f) = (f / 64) * 128 + f % 64
+// (gate/up interleaved in groups of 64 features); the consumed sums are zeroed.
+__global__ void swiglu_acc_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ out, int64_t I, int64_t T) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t idx = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;  // 8 outputs per thread
+  if (idx >= T * I) return;
+  const int64_t t = idx / I, f = idx % I;
+  float* row = acc + t * 2 * I;
+  const int64_t g = (f / 64) * 128 + (f % 64);
+  float4* gp = reinterpret_cast<float4*>(row + g);
+  float4* up = reinterpret_cast<float4*>(row + g + 64);
+  const float4 g0 = __ldcg(gp), g1 = __ldcg(gp + 1), u0 = __ldcg(up), u1 = __ldcg(up + 1);
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  __stcg(gp, z);
+  __stcg(gp + 1, z);
+  __stcg(up, z);
+  __stcg(up + 1, z);
+  const float gv[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+  const float uv[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float a = gv[2 * q] / (1.f + __expf(-gv[2 * q])) * uv[2 * q];
+    const float b = gv[2 * q + 1] / (1.f + __expf(-gv[2 * q + 1])) * uv[2 * q + 1];
+    o[q] = pack_bf16x2(a, b);
+  }
+  *reinterpret_cast<uint4*>(out + t * I + f) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+void swiglu_acc_launch(float* acc, void* out, int64_t T, int64_t I, cudaStream_t st) {
+  if (T == 0) return;
+  const int64_t n = T * I / 8;
+  launch_pdl(swiglu_acc_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, acc,
+             reinterpret_cast<__nv_bfloat16*>(out), I, T);
 }
 
 }  // namespace b200

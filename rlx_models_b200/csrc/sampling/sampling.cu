@@ -21,7 +21,9 @@
 #include <cfloat>
 #include <cstdint>
 
+#include "../common/b200.cuh"
 #include "../common/launch.h"
+#include "../common/pdl_launch.h"
 
 namespace b200 {
 namespace smp {
@@ -119,6 +121,8 @@ __global__ void __launch_bounds__(kThreads) argmax_kernel(const float* __restric
                                                           int32_t* __restrict__ out) {
   __shared__ float shv[32];
   __shared__ int shi[32];
+  pdl_wait();
+  pdl_trigger();
   const float* x = logits + (int64_t)blockIdx.x * ld;
   float best = -FLT_MAX;
   int bi = 0x7fffffff;
@@ -182,6 +186,8 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   __shared__ float sh[32];
   __shared__ int shi[32];
   __shared__ float hist[256];
+  pdl_wait();
+  pdl_trigger();
   const int64_t row = blockIdx.x;
   const float* x = a.logits + row * a.ld;
   const float temp = a.temperature ? a.temperature[row] : 0.f;
@@ -260,12 +266,12 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
 
 void argmax_launch(const float* logits, int64_t ld, int64_t B, int64_t V, int32_t* out, cudaStream_t st) {
   if (B == 0) return;
-  smp::argmax_kernel<<<(unsigned)B, smp::kThreads, 0, st>>>(logits, ld, V, out);
+  launch_pdl(smp::argmax_kernel, dim3((unsigned)B), dim3(smp::kThreads), 0, st, logits, ld, V, out);
 }
 
 void sample_launch(const SampleArgs& a, cudaStream_t st) {
   if (a.B == 0) return;
-  smp::sample_kernel<<<(unsigned)a.B, smp::kThreads, 0, st>>>(a);
+  launch_pdl(smp::sample_kernel, dim3((unsigned)a.B), dim3(smp::kThreads), 0, st, a);
 }
 
 }  // namespace b200

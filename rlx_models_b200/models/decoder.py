@@ -144,7 +144,10 @@ class DecoderLM:
     def _attention(self, i: int, L: LayerWeights, x: torch.Tensor, fb: ForwardBatch, kv: PagedKVCache):
         T = x.shape[0]
         kc, vc = kv.layer(i)
-        qkv = ops.linear(x, L.wqkv, bias=L.bqkv)
+        if T <= ops.ACC_MAX_M and L.bqkv is None:
+            qkv = ops.linear_acc(x, L.wqkv)  # fp32 sums, consumed (and zeroed) by qkv_rope
+        else:
+            qkv = ops.linear(x, L.wqkv, bias=L.bqkv)
         q = ops.qkv_rope(qkv, num_q_heads=self.hq, num_kv_heads=self.hkv, head_dim=self.D,
                          positions=fb.positions, inv_freq=self.inv_freq, rope_scale=self.rope_mult,
                          q_norm=L.q_norm, k_norm=L.k_norm, eps=self.cfg.rms_norm_eps, slots=fb.slots,
@@ -159,32 +162,51 @@ class DecoderLM:
                                   fb.pre_max_q, scale=self.scale, sinks=L.sinks, window=L.window, out=o[nd:])
         return o.view(T, self.hq * self.D)
 
-    def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, h: torch.Tensor, bias=None):
-        """h += x @ w.T (+ bias), reduced over the TP group."""
-        if self.tp_size == 1:
-            ops.linear(x, w, bias=bias, residual=h, out=h)
-        else:
-            self.comm.linear_allreduce_residual(x, w, h, bias=bias if self.tp_rank == 0 else None)
-
     def forward_hidden(self, fb: ForwardBatch, kv: PagedKVCache) -> torch.Tensor:
-        c = self.cfg
-        h = ops.embedding(fb.input_ids, self.embed)
+        """Returns the final-normed hidden states of every token ([T, H])."""
+        comm = self.comm or LocalComm(self.cfg.rms_norm_eps)
+        h = comm.embed(fb.input_ids, self.embed)
+        x = comm.norm_in(h, self.layers[0].ln1)
+        n = len(self.layers)
         for i, L in enumerate(self.layers):
-            x = ops.rmsnorm(h, L.ln1, c.rms_norm_eps)
             a = self._attention(i, L, x, fb, kv)
-            self._row_parallel(a, L.wo, h, L.bo)
-            x = ops.rmsnorm(h, L.ln2, c.rms_norm_eps)
-            gu = ops.linear_swiglu(x, L.w_gu)
-            self._row_parallel(gu, L.wd, h)
-        return h
+            x = comm.rowpar_add_norm(a, L.wo, h, L.ln2, bias=L.bo)
+            if x.shape[0] <= ops.ACC_MAX_M:
+                gu = ops.swiglu_acc(ops.linear_acc(x, L.w_gu))
+            else:
+                gu = ops.linear_swiglu(x, L.w_gu)
+            x = comm.rowpar_add_norm(gu, L.wd, h, self.layers[i + 1].ln1 if i + 1 < n else self.norm)
+        return x
 
-    def logits(self, h: torch.Tensor) -> torch.Tensor:
-        """Final norm + lm_head (fp32 logits; vocab-sharded under TP)."""
-        x = ops.rmsnorm(h, self.norm, self.cfg.rms_norm_eps)
+    def logits(self, x: torch.Tensor) -> torch.Tensor:
+        """lm_head on final-normed rows (fp32; vocab-sharded under TP)."""
         return ops.linear(x, self.lm_head, out_dtype=torch.float32)
 
     def forward(self, fb: ForwardBatch, kv: PagedKVCache) -> torch.Tensor:
-        h = self.forward_hidden(fb, kv)
+        x = self.forward_hidden(fb, kv)
         if fb.logit_rows is not None:
-            h = h.index_select(0, fb.logit_rows)
-        return self.logits(h)
+            x = x.index_select(0, fb.logit_rows)
+        return self.logits(x)
+
+
+class LocalComm:
+    """Single-GPU residual-stream ops (no communication)."""
+
+    def __init__(self, eps: float):
+        self.eps = eps
+
+    def embed(self, ids, table):
+        return ops.embedding(ids, table)
+
+    def norm_in(self, h, w):
+        return ops.rmsnorm(h, w, self.eps)
+
+    def rowpar_add_norm(self, x, w, h, norm_w, bias=None):
+        """h += x @ w.T (+ bias); returns rmsnorm(h) * norm_w.
+
+        Decode-sized batches: accumulate-only GEMM + one add+RMSNorm kernel that
+        consumes the fp32 sums; larger batches: residual add in the GEMM epilogue."""
+        if x.shape[0] <= ops.ACC_MAX_M and bias is None:
+            return ops.add_rmsnorm_acc(ops.linear_acc(x, w), h, norm_w, self.eps)
+        ops.linear(x, w, bias=bias, residual=h, out=h)
+        return ops.rmsnorm(h, norm_w, self.eps)

@@ -53,6 +53,40 @@ def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, *, out: torch.Tensor | No
     return out
 
 
+ACC_MAX_M = 128  # accumulate-only GEMM mode applies to decode-sized batches
+
+
+def linear_acc(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor | None = None) -> torch.Tensor:
+    """Accumulate-only GEMM: ``acc += x @ w.T`` in fp32 (split-K partials are
+    added with red.add, no reduction tail). ``acc`` must be zero on entry
+    unless a running sum is intended; consumers zero it after reading."""
+    s = scratch(x.device)
+    if acc is None:
+        acc = s.acc_view(x.shape[0], w.shape[0])
+    _count(1)
+    ext().linear(x, w, acc, 3, None, None, 1.0, s.gemm_ws, s.gemm_sem, s.status, -1, 0, 0)
+    return acc
+
+
+def add_rmsnorm_acc(acc: torch.Tensor, h: torch.Tensor, w: torch.Tensor, eps: float,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """h = bf16(h + bf16(acc)); returns rmsnorm(h) * w; zeroes acc."""
+    if out is None:
+        out = torch.empty_like(h)
+    _count(1)
+    ext().add_rmsnorm_acc(acc, h, w, out, float(eps))
+    return out
+
+
+def swiglu_acc(acc: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """SwiGLU of interleaved gate/up fp32 sums [M, 2I] -> bf16 [M, I]; zeroes acc."""
+    if out is None:
+        out = torch.empty(acc.shape[0], acc.shape[1] // 2, dtype=torch.bfloat16, device=acc.device)
+    _count(1)
+    ext().swiglu_acc(acc, out)
+    return out
+
+
 def interleave_gate_up(w_gate: torch.Tensor, w_up: torch.Tensor, group: int = SWIGLU_GROUP) -> torch.Tensor:
     """[I, K] x2 -> [2I, K] with rows [g*2G, g*2G+G) = gate, [g*2G+G, (g+1)*2G) = up."""
     I, K = w_gate.shape
@@ -145,7 +179,7 @@ def qkv_rope(qkv: torch.Tensor, *, num_q_heads: int, num_kv_heads: int, head_dim
     """QK RMSNorm + RoPE on the fused qkv projection; K/V written to the paged cache."""
     T = qkv.shape[0]
     if q_out is None:
-        q_out = torch.empty(T, num_q_heads, head_dim, dtype=qkv.dtype, device=qkv.device)
+        q_out = torch.empty(T, num_q_heads, head_dim, dtype=torch.bfloat16, device=qkv.device)
     _count(1)
     ext().qkv_rope(qkv, q_norm, k_norm, positions, slots, inv_freq, float(rope_scale), q_out, k_cache,
                    v_cache, k_out, v_out, num_q_heads, num_kv_heads, head_dim, float(eps))

@@ -42,6 +42,7 @@ class DeviceScratch:
     GEMM_WS_ELEMS = 12 * 1024 * 1024  # fp32, 48 MB
     GEMM_SEM_ELEMS = 65536
     ATTN_WS_ELEMS = 8 * 1024 * 1024  # fp32, 32 MB
+    ACC_ELEMS = 128 * 32768  # fp32, 16 MB: [tokens <= 128, features <= 32768]
 
     def __init__(self, device: torch.device):
         self.device = device
@@ -50,6 +51,13 @@ class DeviceScratch:
         self.gemm_ws = torch.zeros(self.GEMM_WS_ELEMS, dtype=torch.float32, device=device)
         self.gemm_sem = torch.zeros(self.GEMM_SEM_ELEMS, dtype=torch.int32, device=device)
         self.attn_ws = torch.empty(self.ATTN_WS_ELEMS, dtype=torch.float32, device=device)
+        # fp32 sums of the accumulate-only (decode) GEMMs: zero at rest, every
+        # consumer kernel zeroes what it reads; one GEMM uses it at a time
+        self.acc = torch.zeros(self.ACC_ELEMS, dtype=torch.float32, device=device)
+
+    def acc_view(self, m: int, n: int) -> torch.Tensor:
+        assert m * n <= self.ACC_ELEMS, "decode accumulator too small"
+        return self.acc[:m * n].view(m, n)
 
     def check(self):
         """Raise if any kernel on this device recorded an error (syncs)."""

@@ -168,6 +168,12 @@ class LLMEngine:
 
     def _sample(self, logits: torch.Tensor, R: int, greedy: bool):
         out = self.tok_out[:R]
+        comm = getattr(self.model, "comm", None)
+        if comm is not None and getattr(self.model, "tp_size", 1) > 1:
+            # vocab-parallel logits: every rank must pick the same tokens
+            if greedy:
+                return comm.greedy(logits, out)
+            logits = comm.gather_logits(logits)
         if greedy:
             ops.argmax(logits, out=out)
         else:

@@ -217,3 +217,25 @@ def test_sampling_distribution(cuda):
     # top-k = 3
     s3 = ops.sample(logits, T, torch.full((N,), 3, dtype=torch.int32, device=cuda), one, z, seeds, offs)
     assert set(s3.long().cpu().tolist()) <= set(idx[:3].tolist())
+
+
+@pytest.mark.parametrize("M", [1, 17, 64, 128])
+def test_accumulate_gemm_and_consumers(cuda, M):
+    """Accumulate-only GEMM (split-K partials via red.add) + the three
+    consumers that read the fp32 sums and zero them."""
+    H, I = 1024, 768
+    x = _mk((M, H), cuda, 1.0, 31)
+    w = _mk((H, H), cuda, 0.05, 32)
+    acc = ops.linear_acc(x, w)
+    assert rel_err(acc, x.float() @ w.float().T) < 5e-3
+    h = _mk((M, H), cuda, 1.0, 33)
+    nw = _mk((H,), cuda, 1.0, 34)
+    h_ref = (h.float() + acc.bfloat16().float()).bfloat16()
+    y = ops.add_rmsnorm_acc(acc, h, nw, 1e-6)
+    assert torch.equal(h, h_ref)
+    assert rel_err(y, ref.rmsnorm(h_ref, nw, 1e-6)) < 1e-2
+    assert torch.count_nonzero(acc) == 0
+    wg, wu = _mk((I, H), cuda, 0.05, 35), _mk((I, H), cuda, 0.05, 36)
+    g = ops.swiglu_acc(ops.linear_acc(x, ops.interleave_gate_up(wg, wu)))
+    assert rel_err(g, ref.swiglu(x.float() @ wg.float().T, x.float() @ wu.float().T)) < 1.5e-2
+    assert torch.count_nonzero(ops.scratch(cuda).acc) == 0
