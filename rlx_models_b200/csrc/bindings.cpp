@@ -308,8 +308,8 @@ Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> sizes, at::ScalarType d
 
 // GEMM in reduce-scatter push mode (see gemm_sm100.cuh). peer_out / peer_flags
 // are device int64 arrays of peer pointers; epoch / done_ctr are local uint32.
-void linear_push(const Tensor& x, const Tensor& w, const optional<Tensor>& bias, int64_t rpr, int64_t ld_out,
-                 int64_t slot_elems, int64_t my_rank, int64_t world, const Tensor& peer_out,
+void linear_push(const Tensor& x, const Tensor& w, const optional<Tensor>& bias, int64_t mode, int64_t rpr,
+                 int64_t ld_out, int64_t slot_elems, int64_t my_rank, int64_t world, const Tensor& peer_out,
                  const Tensor& peer_flags, const Tensor& epoch, const Tensor& done_ctr, Tensor& ws, Tensor& sem,
                  Tensor& status) {
   check_cuda(x, "x");
@@ -331,7 +331,9 @@ void linear_push(const Tensor& x, const Tensor& w, const optional<Tensor>& bias,
   a.M = x.size(0);
   a.N = w.size(0);
   a.K = x.size(1);
-  a.mode = 0;
+  TORCH_CHECK(mode == 0 || (mode == 3 && x.size(0) <= 128 && !(bias.has_value() && bias->defined())),
+              "b200.linear_push: mode 0 (bf16 slots) or 3 (fp32 accumulate, M <= 128, no bias)");
+  a.mode = (int)mode;
   a.alpha = 1.f;
   a.swap = -1;
   a.bn = 0;
@@ -354,7 +356,7 @@ void linear_push(const Tensor& x, const Tensor& w, const optional<Tensor>& bias,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void rs_norm_ag(const optional<Tensor>& recv, Tensor& h, const Tensor& norm_w, const Tensor& peer_gath,
+void rs_norm_ag(const optional<Tensor>& recv, const optional<Tensor>& racc, Tensor& h, const Tensor& norm_w, const Tensor& peer_gath,
                 const Tensor& rs_flags, const Tensor& ag_flags, const Tensor& peer_ag_flags, Tensor& epoch,
                 Tensor& cta_ctr, int64_t M, int64_t rpr, int64_t world, int64_t rank, int64_t slot_elems,
                 double eps, Tensor& status) {
@@ -376,7 +378,8 @@ void rs_norm_ag(const optional<Tensor>& recv, Tensor& h, const Tensor& norm_w, c
   a.rpr = (int)rpr;
   a.world = (int)world;
   a.rank = (int)rank;
-  a.do_reduce = a.recv != nullptr;
+  a.racc = (racc.has_value() && racc->defined()) ? racc->data_ptr<float>() : nullptr;
+  a.do_reduce = a.racc != nullptr ? 2 : (a.recv != nullptr ? 1 : 0);
   a.slot_elems = slot_elems;
   a.eps = (float)eps;
   a.status = status.data_ptr<int>();

@@ -66,7 +66,16 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgArgs a) 
         s[2 * k] = 0.f;
         s[2 * k + 1] = 0.f;
       }
-      if (a.do_reduce) {
+      if (a.do_reduce == 2) {
+        // fp32 sums that every rank's accumulate-mode GEMM added in place
+        float4* ap = reinterpret_cast<float4*>(a.racc + (int64_t)r * a.H + col);
+        const float4 a0 = __ldcg(ap), a1 = __ldcg(ap + 1);
+        __stcg(ap, make_float4(0.f, 0.f, 0.f, 0.f));
+        __stcg(ap + 1, make_float4(0.f, 0.f, 0.f, 0.f));
+        s[0] = a0.x; s[1] = a0.y; s[2] = a0.z; s[3] = a0.w;
+        s[4] = a1.x; s[5] = a1.y; s[6] = a1.z; s[7] = a1.w;
+      }
+      if (a.do_reduce == 1) {
         for (int q = 0; q < a.world; ++q) {
           const uint4 pv = __ldcg(reinterpret_cast<const uint4*>(recv + q * a.slot_elems + (int64_t)r * a.H + col));
           const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
@@ -76,6 +85,8 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgArgs a) 
             s[2 * k + 1] += bf16_hi(pw[k]);
           }
         }
+      }
+      if (a.do_reduce) {
         // residual stream in bf16: h = bf16(h + bf16(sum))
         uint32_t o[4];
 #pragma unroll

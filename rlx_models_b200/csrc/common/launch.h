@@ -53,7 +53,8 @@ struct RsNormAgArgs {
   unsigned* const* peer_ag_flags;      // [world] -> each rank's ag_flags
   unsigned* epoch;                     // local op counter
   unsigned* cta_ctr;                   // local arrival counter (self-resetting)
-  int M, H, rpr, world, rank, do_reduce;
+  float* racc;                         // local fp32 [rpr][H] accumulator (do_reduce == 2)
+  int M, H, rpr, world, rank, do_reduce;  // do_reduce: 0 none, 1 bf16 slots, 2 fp32 accumulator
   int64_t slot_elems;                  // rpr_max * H
   float eps;
   int* status;

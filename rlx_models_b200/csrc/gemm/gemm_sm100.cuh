@@ -463,7 +463,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int j = jt + c * 32 + tl;
           const int f0 = m_tile * kBM + seg * 32;
           if (j < p.NB && f0 < p.MA) {
-            float* drow = dst + (int64_t)j * p.ldc_j + f0;
+            // local accumulator, or (tensor parallel) the row owner's over NVLink
+            float* drow = (p.peer_out != nullptr ? out_row<float>(p, j, p.ldc_j) : dst + (int64_t)j * p.ldc_j) + f0;
             const float* src = xchg + tl * 132 + seg * 32;
             if (f0 + 32 <= p.MA) {
 #pragma unroll

@@ -46,11 +46,15 @@ class FusedTPComm(NcclTPComm):
         lay = Layout()
         self.o_recv = lay.add("recv", (world, self.rpr_max, hidden), torch.bfloat16)
         self.o_gath = lay.add("gath", (max_tokens, hidden), torch.bfloat16)
+        self.acc_rows = math.ceil(128 / world)  # decode steps (M <= 128) accumulate in fp32
+        self.o_racc = lay.add("racc", (self.acc_rows, hidden), torch.float32)
         self.o_rs = lay.add("rs_flags", (world,), torch.int32)
         self.o_ag = lay.add("ag_flags", (world,), torch.int32)
         self.heap = SymmetricHeap(lay.nbytes, device, group)
         self.recv = self.heap.view(self.o_recv, (world, self.rpr_max, hidden), torch.bfloat16)
         self.gath = self.heap.view(self.o_gath, (max_tokens, hidden), torch.bfloat16)
+        self.racc = self.heap.view(self.o_racc, (self.acc_rows, hidden), torch.float32)
+        self.peer_racc = self.heap.peer_ptr_table(self.o_racc)
         self.rs_flags = self.heap.view(self.o_rs, (world,), torch.int32)
         self.ag_flags = self.heap.view(self.o_ag, (world,), torch.int32)
         self.peer_recv = self.heap.peer_ptr_table(self.o_recv)
@@ -77,10 +81,10 @@ class FusedTPComm(NcclTPComm):
             ops.embedding(ids[lo:hi], table, out=h[:hi - lo])
         return h
 
-    def _rs_norm_ag(self, recv, h, norm_w):
+    def _rs_norm_ag(self, recv, h, norm_w, racc=None):
         s = scratch(h.device)
         ops._count(1)
-        ext().rs_norm_ag(recv, h, norm_w, self.peer_gath, self.rs_flags, self.ag_flags, self.peer_ag,
+        ext().rs_norm_ag(recv, racc, h, norm_w, self.peer_gath, self.rs_flags, self.ag_flags, self.peer_ag,
                          self.ctr[0:1], self.ctr[1:2], self.M, self.rpr, self.world, self.rank, self.slot_elems,
                          float(self.eps), s.status)
         return self.gath[:self.M]
@@ -91,7 +95,12 @@ class FusedTPComm(NcclTPComm):
     def rowpar_add_norm(self, x, w, h, norm_w, bias=None):
         s = scratch(x.device)
         ops._count(1)
-        ext().linear_push(x, w, bias if self.rank == 0 else None, self.rpr, self.H, self.slot_elems, self.rank,
+        if x.shape[0] <= 128 and bias is None:
+            # decode: split-K partials red.add'ed straight into the owner's fp32 accumulator
+            ext().linear_push(x, w, None, 3, self.rpr, self.H, 0, self.rank, self.world, self.peer_racc,
+                              self.peer_rs, self.ctr[0:1], self.ctr[2:3], s.gemm_ws, s.gemm_sem, s.status)
+            return self._rs_norm_ag(None, h, norm_w, racc=self.racc)
+        ext().linear_push(x, w, bias if self.rank == 0 else None, 0, self.rpr, self.H, self.slot_elems, self.rank,
                           self.world, self.peer_recv, self.peer_rs, self.ctr[0:1], self.ctr[2:3], s.gemm_ws,
                           s.gemm_sem, s.status)
         return self._rs_norm_ag(self.recv, h, norm_w)

@@ -45,6 +45,12 @@ class NcclTPComm:
         return ops.rmsnorm(h, w, self.eps)
 
     def rowpar_add_norm(self, x, w, h, norm_w, bias=None):
+        if x.shape[0] <= ops.ACC_MAX_M and bias is None:
+            # decode: fp32 partial from the accumulate-only GEMM, NCCL sum, then
+            # one kernel does h += sum, rmsnorm and re-zeroes the accumulator
+            part = ops.linear_acc(x, w)
+            dist.all_reduce(part, group=self.group)
+            return ops.add_rmsnorm_acc(part, h, norm_w, self.eps)
         part = ops.linear(x, w, bias=bias if self.rank == 0 else None)
         dist.all_reduce(part, group=self.group)
         # h = h + part ; return rmsnorm(h) * norm_w   (one fused kernel)
