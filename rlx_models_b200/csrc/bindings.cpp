@@ -408,9 +408,109 @@ void swiglu_acc(Tensor& acc, Tensor& out) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// out[M, N] = alpha * a[M, K] @ b[K, N] for any mix of row-major / transposed
+// views (the operand majors are read from the strides); bf16 inputs.
+void gemm(const Tensor& a, const Tensor& b, Tensor& out, bool accumulate, double alpha,
+          const optional<Tensor>& residual, const optional<Tensor>& bias, bool prefetch_b, Tensor& ws, Tensor& sem,
+          Tensor& status) {
+  check_cuda(a, "a");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && a.dim() == 2 && b.dim() == 2,
+              "b200.gemm: bf16 2-D operands");
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(1);
+  TORCH_CHECK(b.size(0) == K, "b200.gemm: inner dims");
+  TORCH_CHECK(out.dim() == 2 && out.size(0) == M && out.size(1) == N && out.stride(1) == 1, "b200.gemm: out");
+  b200::GemmArgs g{};
+  // A[i=m, k]: K-major if a is row-major, MN-major if a is a transposed view
+  if (a.stride(1) == 1) { g.a_mn = 0; g.lda = a.stride(0); }
+  else { TORCH_CHECK(a.stride(0) == 1, "b200.gemm: a must be row-major or a transposed view"); g.a_mn = 1; g.lda = a.stride(1); }
+  // B[j=n, k]: K-major if b is a transposed view of [N, K], MN-major if b is row-major [K, N]
+  if (b.stride(0) == 1) { g.b_mn = 0; g.ldb = b.stride(1); }
+  else { TORCH_CHECK(b.stride(1) == 1, "b200.gemm: b must be row-major or a transposed view"); g.b_mn = 1; g.ldb = b.stride(0); }
+  TORCH_CHECK(!(g.a_mn && !g.b_mn), "b200.gemm: transposed a needs row-major b");
+  TORCH_CHECK(g.lda % 8 == 0 && g.ldb % 8 == 0, "b200.gemm: strides % 8");
+  g.a = a.data_ptr();
+  g.b = b.data_ptr();
+  g.c = out.data_ptr();
+  g.ldc = out.stride(0);
+  g.MA = M;
+  g.NB = N;
+  g.K = K;
+  g.out_f32 = out.scalar_type() == at::kFloat;
+  TORCH_CHECK(g.out_f32 || out.scalar_type() == at::kBFloat16, "b200.gemm: out dtype");
+  TORCH_CHECK(!accumulate || g.out_f32, "b200.gemm: accumulate needs f32 out");
+  g.accumulate = accumulate;
+  g.alpha = (float)alpha;
+  g.residual = opt_ptr(residual);
+  g.ldr = (residual.has_value() && residual->defined()) ? residual->stride(0) : 0;
+  g.bias = opt_ptr(bias);
+  g.prefetch_b = prefetch_b;
+  g.ws = ws.data_ptr<float>();
+  g.ws_elems = ws.numel();
+  g.sem = sem.data_ptr<int>();
+  g.sem_elems = sem.numel();
+  g.status = status.data_ptr<int>();
+  g.device = a.get_device();
+  c10::cuda::CUDAGuard gd(a.device());
+  b200::gemm_launch(g, cur_stream(a));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void adamw(Tensor& master, const Tensor& grad, Tensor& m, Tensor& v, const optional<Tensor>& param_out, double lr,
+           double b1, double b2, double eps, double wd, int64_t step, const optional<Tensor>& scale_t,
+           double scale) {
+  check_cuda(master, "master");
+  const int64_t n = master.numel();
+  TORCH_CHECK(master.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat && v.scalar_type() == at::kFloat &&
+                  master.is_contiguous() && m.is_contiguous() && v.is_contiguous() && grad.is_contiguous() &&
+                  m.numel() == n && v.numel() == n && grad.numel() == n,
+              "b200.adamw: fp32 contiguous master/moments, matching grad");
+  TORCH_CHECK(grad.scalar_type() == at::kFloat || grad.scalar_type() == at::kBFloat16, "b200.adamw: grad dtype");
+  if (param_out.has_value() && param_out->defined())
+    TORCH_CHECK(param_out->scalar_type() == at::kBFloat16 && param_out->numel() == n && param_out->is_contiguous(),
+                "b200.adamw: param_out");
+  c10::cuda::CUDAGuard g(master.device());
+  b200::adamw_launch(master.data_ptr<float>(), grad.data_ptr(), grad.scalar_type() == at::kFloat,
+                     m.data_ptr<float>(), v.data_ptr<float>(), const_cast<void*>(opt_ptr(param_out)), n, (float)lr,
+                     (float)b1, (float)b2, (float)eps, (float)wd, step,
+                     (scale_t.has_value() && scale_t->defined()) ? scale_t->data_ptr<float>() : nullptr,
+                     (float)scale, cur_stream(master));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void sumsq(const Tensor& g, Tensor& out) {
+  check_cuda(g, "g");
+  TORCH_CHECK(g.is_contiguous() && (g.scalar_type() == at::kFloat || g.scalar_type() == at::kBFloat16) &&
+                  out.scalar_type() == at::kFloat,
+              "b200.sumsq");
+  c10::cuda::CUDAGuard gd(g.device());
+  b200::sumsq_launch(g.data_ptr(), g.scalar_type() == at::kFloat, g.numel(), out.data_ptr<float>(), cur_stream(g));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ce_fwd_bwd(const Tensor& logits, const Tensor& targets, Tensor& loss, const optional<Tensor>& dlogits,
+                double grad_scale) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1, "b200.ce: logits");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.numel() == logits.size(0), "b200.ce: targets int64");
+  if (dlogits.has_value() && dlogits->defined())
+    TORCH_CHECK(dlogits->scalar_type() == at::kBFloat16 && dlogits->stride(1) == 1 &&
+                    dlogits->size(0) == logits.size(0) && dlogits->size(1) == logits.size(1),
+                "b200.ce: dlogits");
+  c10::cuda::CUDAGuard g(logits.device());
+  b200::ce_fwd_bwd_launch(logits.data_ptr<float>(), logits.stride(0), logits.size(0), logits.size(1),
+                          targets.data_ptr<int64_t>(), loss.data_ptr<float>(), const_cast<void*>(opt_ptr(dlogits)),
+                          (dlogits.has_value() && dlogits->defined()) ? dlogits->stride(0) : 0, (float)grad_scale,
+                          cur_stream(logits));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
   m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none());
+  m.def("gemm", &gemm);
+  m.def("adamw", &adamw);
+  m.def("sumsq", &sumsq);
+  m.def("ce_fwd_bwd", &ce_fwd_bwd);
   m.def("embedding", &embedding);
   m.def("rmsnorm", &rmsnorm);
   m.def("qkv_rope", &qkv_rope);

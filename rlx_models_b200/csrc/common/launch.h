@@ -42,6 +42,34 @@ struct LinearArgs {
 };
 void linear_launch(const LinearArgs& a, cudaStream_t st);
 
+// General (training) GEMM: D[MA, NB] = alpha * A[MA, K] . B[NB, K]^T with
+// per-operand major (K-major rows, or MN-major = stored [K, rows]).
+struct GemmArgs {
+  const void* a;
+  int64_t lda;
+  int a_mn;
+  const void* b;
+  int64_t ldb;
+  int b_mn;
+  void* c;
+  int64_t ldc;
+  int64_t MA, NB, K;
+  int out_f32, accumulate;
+  float alpha;
+  const void* residual;
+  int64_t ldr;
+  const void* bias;
+  int prefetch_b;  // B may be read before the previous kernel finishes (static weights)
+  int bn, splits;
+  float* ws;
+  int64_t ws_elems;
+  int* sem;
+  int64_t sem_elems;
+  int* status;
+  int device;
+};
+void gemm_launch(const GemmArgs& a, cudaStream_t st);
+
 // ---------------- tensor-parallel fused collective ----------------
 struct RsNormAgArgs {
   const void* recv;           // local [world][rpr][H] (reduce inputs), unused if !do_reduce
@@ -117,6 +145,14 @@ struct AttnArgs {
 };
 int decode_attention_launch(const AttnArgs& a, cudaStream_t st);  // returns #launches
 void prefill_attention_launch(const AttnArgs& a, cudaStream_t st);
+
+// ---------------- training ----------------
+void adamw_launch(float* master, const void* grad, bool grad_f32, float* m, float* v, void* param_out, int64_t n,
+                  float lr, float b1, float b2, float eps, float wd, int64_t step, const float* scale_ptr,
+                  float scale, cudaStream_t st);
+void sumsq_launch(const void* g, bool f32, int64_t n, float* out, cudaStream_t st);
+void ce_fwd_bwd_launch(const float* logits, int64_t ld, int64_t T, int64_t V, const int64_t* targets, float* loss,
+                       void* dlogits, int64_t ldd, float grad_scale, cudaStream_t st);
 
 // ---------------- sampling ----------------
 void argmax_launch(const float* logits, int64_t ld, int64_t B, int64_t V, int32_t* out, cudaStream_t st);

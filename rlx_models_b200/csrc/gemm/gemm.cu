@@ -18,10 +18,10 @@
 namespace b200 {
 namespace gemm {
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool A_MN = false, bool B_MN = false>
 static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid, cudaStream_t st,
                      int device) {
-  auto kern = gemm_bf16_kernel<BN, EPI>;
+  auto kern = gemm_bf16_kernel<BN, EPI, A_MN, B_MN>;
   static uint64_t attr_done = 0;  // one bit per device
   if (!(attr_done & (1ull << device))) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM_BYTES);
@@ -117,6 +117,7 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
   p.alpha = a.alpha;
   p.swiglu_on_i = sw ? 1 : 0;
   p.w_is_a = sw ? 1 : 0;
+  p.prefetch_w = 1;
   p.ws = a.ws;
   p.sem = a.sem;
   p.status = a.status;
@@ -142,6 +143,87 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
     case gemm::EPI_ACC: gemm::launch_bn<gemm::EPI_ACC>(BN, ta, tb, p, grid, st, a.device); break;
     default: throw std::runtime_error("b200.linear: bad mode");
   }
+}
+
+}  // namespace b200
+
+namespace b200 {
+
+// General GEMM for training: D[i, j] = alpha * sum_k A[i, k] * B[j, k] with
+// either operand K-major or MN-major; bf16 or f32 (optionally accumulated)
+// output, optional residual / bias. No orientation swap, no TP push.
+void gemm_launch(const GemmArgs& a, cudaStream_t st) {
+  if (a.MA == 0 || a.NB == 0) return;
+  const int sms = num_sms(a.device);
+  const int epi = a.out_f32 ? gemm::EPI_F32 : gemm::EPI_BF16;
+  gemm::Params p{};
+  p.MA = (int)a.MA;
+  p.NB = (int)a.NB;
+  p.K = (int)a.K;
+  int BN = a.bn ? a.bn : (a.NB > 128 ? 256 : 128);
+  if (BN != 128 && BN != 256) throw std::runtime_error("b200.gemm: BN must be 128 or 256");
+  p.k_tiles = (int)((a.K + gemm::kBK - 1) / gemm::kBK);
+  p.num_m = (p.MA + gemm::kBM - 1) / gemm::kBM;
+  p.num_n = (p.NB + BN - 1) / BN;
+  const int tiles = p.num_m * p.num_n;
+  int sp = a.splits;
+  if (sp <= 0) {
+    sp = 1;
+    double best = 1e30;
+    const int max_sp = (tiles >= 2 * sms) ? 1 : std::max(1, std::min(16, p.k_tiles / 4));
+    for (int s = 1; s <= max_sp; ++s) {
+      const int kts = (p.k_tiles + s - 1) / s;
+      const int waves = (tiles * s + sms - 1) / sms;
+      const double cost = (double)waves * kts + (s > 1 ? 2.0 * s : 0.0);
+      if (cost < best - 1e-9) {
+        best = cost;
+        sp = s;
+      }
+    }
+  }
+  sp = std::max(1, std::min(sp, p.k_tiles));
+  if (sp > 1 && (int64_t)tiles * gemm::kBM * BN > a.ws_elems) sp = 1;
+  p.kt_per_split = (p.k_tiles + sp - 1) / sp;
+  p.splits = (p.k_tiles + p.kt_per_split - 1) / p.kt_per_split;
+  p.num_units = tiles * p.splits;
+  if (p.splits > 1 && (a.ws == nullptr || a.sem == nullptr || a.sem_elems < tiles))
+    throw std::runtime_error("b200.gemm: split-K buffers too small");
+  p.C = a.c;
+  p.ldc_i = a.ldc;
+  p.ldc_j = 1;
+  p.R = reinterpret_cast<const __nv_bfloat16*>(a.residual);
+  p.ldr_i = a.ldr;
+  p.ldr_j = 1;
+  p.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
+  p.bias_on_i = 0;
+  p.alpha = a.alpha;
+  p.swiglu_on_i = 0;
+  p.w_is_a = 0;
+  p.accumulate = a.accumulate;
+  p.prefetch_w = a.prefetch_b;
+  p.ws = a.ws;
+  p.sem = a.sem;
+  p.status = a.status;
+  // K-major operand: [rows, K] (ld = row stride); MN-major: stored [K, rows] (ld = stride of k)
+  CUtensorMap ta = a.a_mn ? make_tmap_2d(a.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.MA, a.lda, 64, 64)
+                          : make_tmap_2d(a.a, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.MA, a.K, a.lda, gemm::kBM, 64);
+  CUtensorMap tb = a.b_mn ? make_tmap_2d(a.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.K, a.NB, a.ldb, 64, 64)
+                          : make_tmap_2d(a.b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a.NB, a.K, a.ldb, BN, 64);
+  const int grid = std::min(p.num_units, sms);
+  const int code = (a.a_mn ? 2 : 0) + (a.b_mn ? 1 : 0);
+#define B200_GEMM_CASE(BNV, EPIV)                                                                      \
+  switch (code) {                                                                                      \
+    case 0: gemm::launch_t<BNV, EPIV, false, false>(ta, tb, p, grid, st, a.device); break;             \
+    case 1: gemm::launch_t<BNV, EPIV, false, true>(ta, tb, p, grid, st, a.device); break;              \
+    case 3: gemm::launch_t<BNV, EPIV, true, true>(ta, tb, p, grid, st, a.device); break;               \
+    default: throw std::runtime_error("b200.gemm: A MN-major with B K-major is not instantiated");     \
+  }
+  if (BN == 256) {
+    if (epi == gemm::EPI_F32) { B200_GEMM_CASE(256, gemm::EPI_F32) } else { B200_GEMM_CASE(256, gemm::EPI_BF16) }
+  } else {
+    if (epi == gemm::EPI_F32) { B200_GEMM_CASE(128, gemm::EPI_F32) } else { B200_GEMM_CASE(128, gemm::EPI_BF16) }
+  }
+#undef B200_GEMM_CASE
 }
 
 }  // namespace b200

@@ -49,6 +49,8 @@ struct Params {
   float alpha;
   int swiglu_on_i;
   int w_is_a;  // 1: A is the weight operand (swap-AB), 0: B is
+  int accumulate;  // EPI_F32: C += result (gradient accumulation)
+  int prefetch_w;  // 1: the weight operand may be loaded before griddepcontrol.wait
   float* ws;
   int* sem;
   int* status;
@@ -146,13 +148,28 @@ __device__ __forceinline__ void store_chunk(const Params& p, int i, int j0, floa
   if (EPI == EPI_F32) {
     float* c = out_row<float>(p, i, p.ldc_i);
     if (p.ldc_j == 1 && full && ((reinterpret_cast<uintptr_t>(c + j0) & 15u) == 0)) {
+      if (p.accumulate) {
+        float4 o[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) o[q] = *reinterpret_cast<const float4*>(c + j0 + q * 4);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          v[q * 4] += o[q].x;
+          v[q * 4 + 1] += o[q].y;
+          v[q * 4 + 2] += o[q].z;
+          v[q * 4 + 3] += o[q].w;
+        }
+      }
 #pragma unroll
       for (int q = 0; q < 8; ++q)
         *reinterpret_cast<float4*>(c + j0 + q * 4) = make_float4(v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
     } else {
 #pragma unroll
       for (int t = 0; t < 32; ++t)
-        if (j0 + t < p.NB) c[(int64_t)(j0 + t) * p.ldc_j] = v[t];
+        if (j0 + t < p.NB) {
+          float* cc = c + (int64_t)(j0 + t) * p.ldc_j;
+          *cc = p.accumulate ? *cc + v[t] : v[t];
+        }
     }
   } else {
     __nv_bfloat16* c = out_row<__nv_bfloat16>(p, i, p.ldc_i);
@@ -250,7 +267,26 @@ __device__ __forceinline__ void store_row32(const Params& p, int j, int fo, int 
   }
 }
 
-template <int BN, int EPI>
+// Operand tiles: K-major -> one TMA box [rows][64 k] (128-byte rows);
+// MN-major (the matrix is stored [K][rows], rows contiguous) -> rows/64 boxes
+// of [64 k][64 rows], each 8 KB, whose UMMA descriptor strides are LBO = 8 KB
+// (next 64 rows) and SBO = 1 KB (next 8 k), advancing 2 KB per K=16 step.
+template <bool MN, int ROWS>
+__device__ __forceinline__ void load_operand(uint8_t* dst, const CUtensorMap* tm, uint64_t* bar, int kt, int row0) {
+  if (!MN) {
+    tma_load_2d(dst, tm, bar, kt * kBK, row0);
+  } else {
+#pragma unroll
+    for (int c = 0; c < ROWS / 64; ++c) tma_load_2d(dst + c * 8192, tm, bar, row0 + c * 64, kt * kBK);
+  }
+}
+
+template <bool MN>
+__device__ __forceinline__ uint64_t operand_desc(uint32_t base, int kk) {
+  return MN ? umma_desc_sw128(base + kk * 2048, 8192, 1024) : umma_desc_sw128(base + kk * 32, 16, 1024);
+}
+
+template <int BN, int EPI, bool A_MN = false, bool B_MN = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const Params p) {
@@ -311,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // kernel, so the first ring's worth of weight tiles is requested before
       // griddepcontrol.wait; the activation halves of those stages follow it.
       int npre = 0;
-      if ((int)blockIdx.x < p.num_units) {
+      if (p.prefetch_w && (int)blockIdx.x < p.num_units) {
         int m_tile, n_tile, ks, tile;
         unit_to_tile(p, blockIdx.x, m_tile, n_tile, ks, tile);
         const int kb = ks * p.kt_per_split;
@@ -319,8 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int q = 0; q < npre; ++q) {
           uint8_t* sa = ring + q * C::STAGE_BYTES;
           mbar_arrive_expect_tx(&full[q], C::STAGE_BYTES);
-          if (p.w_is_a) tma_load_2d(sa, &tmA, &full[q], (kb + q) * kBK, m_tile * kBM);
-          else tma_load_2d(sa + C::A_BYTES, &tmB, &full[q], (kb + q) * kBK, n_tile * BN);
+          if (p.w_is_a) load_operand<A_MN, kBM>(sa, &tmA, &full[q], kb + q, m_tile * kBM);
+          else load_operand<B_MN, BN>(sa + C::A_BYTES, &tmB, &full[q], kb + q, n_tile * BN);
         }
       }
       B200_GEMM_TRACE(2);
@@ -337,8 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + C::A_BYTES;
           if (first && kt - kb < npre) {
             // weight half already in flight; issue the activation half
-            if (p.w_is_a) tma_load_2d(sb, &tmB, &full[stage], kt * kBK, n_tile * BN);
-            else tma_load_2d(sa, &tmA, &full[stage], kt * kBK, m_tile * kBM);
+            if (p.w_is_a) load_operand<B_MN, BN>(sb, &tmB, &full[stage], kt, n_tile * BN);
+            else load_operand<A_MN, kBM>(sa, &tmA, &full[stage], kt, m_tile * kBM);
           } else {
             if (!mbar_wait(&empty[stage], phase ^ 1, p.status, kErrTimeoutEmpty) || *abort_flag) {
               *abort_flag = 1;
@@ -346,8 +382,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               break;
             }
             mbar_arrive_expect_tx(&full[stage], C::STAGE_BYTES);
-            tma_load_2d(sa, &tmA, &full[stage], kt * kBK, m_tile * kBM);
-            tma_load_2d(sb, &tmB, &full[stage], kt * kBK, n_tile * BN);
+            load_operand<A_MN, kBM>(sa, &tmA, &full[stage], kt, m_tile * kBM);
+            load_operand<B_MN, BN>(sb, &tmB, &full[stage], kt, n_tile * BN);
           }
           ++issued;
           if (++stage == STAGES) {
@@ -374,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (elect_one_sync()) {
       // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN, false, false);
+      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN, A_MN, B_MN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -405,8 +441,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t b_addr = a_addr + C::A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t ad = umma_desc_sw128(a_addr + kk * 32, 16, 1024);
-            const uint64_t bd = umma_desc_sw128(b_addr + kk * 32, 16, 1024);
+            const uint64_t ad = operand_desc<A_MN>(a_addr, kk);
+            const uint64_t bd = operand_desc<B_MN>(b_addr, kk);
             umma_f16(d_tmem, ad, bd, idesc, (kt > kb || kk > 0) ? 1u : 0u);
           }
           umma_commit(&empty[stage]);

@@ -53,6 +53,21 @@ def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, *, out: torch.Tensor | No
     return out
 
 
+def matmul(a: torch.Tensor, b: torch.Tensor, *, out: torch.Tensor | None = None, out_dtype=torch.bfloat16,
+           accumulate: bool = False, alpha: float = 1.0, residual: torch.Tensor | None = None,
+           bias: torch.Tensor | None = None, static_b: bool = False) -> torch.Tensor:
+    """``out (+)= alpha * a @ b`` on the tcgen05 GEMM; ``a`` [M, K] and ``b`` [K, N]
+    may each be row-major or a transposed view (training: dX = dY @ W uses a
+    row-major ``b``; dW = dY.T @ X a transposed ``a``). ``static_b`` lets the
+    kernel prefetch ``b`` before the previous kernel finishes (weights only)."""
+    if out is None:
+        out = torch.empty(a.shape[0], b.shape[1], dtype=out_dtype, device=a.device)
+    s = scratch(a.device)
+    _count(1)
+    ext().gemm(a, b, out, accumulate, float(alpha), residual, bias, static_b, s.gemm_ws, s.gemm_sem, s.status)
+    return out
+
+
 ACC_MAX_M = 128  # accumulate-only GEMM mode applies to decode-sized batches
 
 

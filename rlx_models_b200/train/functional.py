@@ -1,0 +1,137 @@
+"""Differentiable building blocks of the training path.
+
+On CUDA every matmul (forward, dgrad, wgrad) runs on the tcgen05 GEMM and the
+loss runs on the fused chunked lm_head + cross-entropy kernels; on CPU the same
+functions fall back to plain fp32 torch so the host-side logic (FSDP sharding,
+checkpointing, schedules) is testable on gloo ranks without a GPU.
+
+Reference: the rlx-tune loss graph appends next-token CE to the LM graph
+(rlx-tune src/lm.rs:77-115, src/loss.rs:20) and differentiates it with the
+external autodiff crate; here autograd drives our kernels.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import ops
+
+
+def _cuda(t: torch.Tensor) -> bool:
+    return t.is_cuda
+
+
+class LinearFn(torch.autograd.Function):
+    """y = x @ w.T with bf16 operands; dW in fp32."""
+
+    @staticmethod
+    def forward(ctx, x, w):
+        ctx.save_for_backward(x, w)
+        x2 = x.reshape(-1, x.shape[-1])
+        if _cuda(x):
+            y = ops.matmul(x2, w.t(), static_b=False)
+        else:
+            y = (x2.float() @ w.float().t()).to(x.dtype)
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        x, w = ctx.saved_tensors
+        x2 = x.reshape(-1, x.shape[-1])
+        g2 = gy.reshape(-1, gy.shape[-1]).contiguous()
+        dx = dw = None
+        if _cuda(x):
+            if ctx.needs_input_grad[0]:
+                dx = ops.matmul(g2, w).view(x.shape)
+            if ctx.needs_input_grad[1]:
+                dw = torch.empty(w.shape, dtype=torch.float32, device=w.device)
+                ops.matmul(g2.t(), x2, out=dw)
+        else:
+            if ctx.needs_input_grad[0]:
+                dx = (g2.float() @ w.float()).to(x.dtype).view(x.shape)
+            if ctx.needs_input_grad[1]:
+                dw = g2.float().t() @ x2.float()
+        return dx, dw
+
+
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    return LinearFn.apply(x, w)
+
+
+class LMHeadCE(torch.autograd.Function):
+    """Mean next-token cross-entropy of ``x @ w.T`` without materialising all
+    logits: per chunk of rows, fp32 logits on the GEMM, one kernel for loss +
+    dlogits, then dX and dW from dlogits. Gradients are computed in forward
+    (the loss is the end of the graph) and scaled by grad_output in backward."""
+
+    @staticmethod
+    def forward(ctx, x, w, targets, chunk: int = 2048, denom: float | None = None):
+        T, H = x.shape
+        V = w.shape[0]
+        n_valid = int((targets >= 0).sum()) if denom is None else None
+        scale = 1.0 / (denom if denom is not None else max(1, n_valid))
+        total = torch.zeros((), dtype=torch.float32, device=x.device)
+        dx = torch.empty_like(x)
+        dw = torch.zeros(V, H, dtype=torch.float32, device=x.device)
+        for s in range(0, T, chunk):
+            e = min(T, s + chunk)
+            xc, tc = x[s:e], targets[s:e]
+            if _cuda(x):
+                logits = ops.matmul(xc, w.t(), out_dtype=torch.float32, static_b=False)
+                loss = torch.empty(e - s, dtype=torch.float32, device=x.device)
+                dlog = torch.empty(e - s, V, dtype=torch.bfloat16, device=x.device)
+                ops.ext().ce_fwd_bwd(logits, tc, loss, dlog, float(scale))
+                ops._count(1)
+                del logits
+                ops.matmul(dlog, w, out=dx[s:e])
+                ops.matmul(dlog.t(), xc, out=dw, accumulate=True)
+            else:
+                logits = xc.float() @ w.float().t()
+                valid = tc >= 0
+                lse = torch.logsumexp(logits, -1)
+                tgt = tc.clamp(min=0)
+                loss = torch.where(valid, lse - logits.gather(1, tgt[:, None]).squeeze(1), torch.zeros_like(lse))
+                p = torch.softmax(logits, -1)
+                p[torch.arange(e - s), tgt] -= 1.0
+                dlog = (p * valid[:, None].float() * scale).to(x.dtype)
+                dx[s:e] = (dlog.float() @ w.float()).to(x.dtype)
+                dw += dlog.float().t() @ xc.float()
+            total += loss.sum()
+        ctx.save_for_backward(dx, dw)
+        return total * scale
+
+    @staticmethod
+    def backward(ctx, g):
+        dx, dw = ctx.saved_tensors
+        return dx * g.to(dx.dtype), dw * g, None, None, None
+
+
+def lm_head_ce(x, w, targets, chunk: int = 2048, denom: float | None = None):
+    return LMHeadCE.apply(x, w, targets, chunk, denom)
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """HF RMSNorm semantics (normalise in fp32, cast, scale)."""
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return w * y.to(x.dtype)
+
+
+def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Half-split rotary embedding; x [B, S, H, D], cos/sin [S, D]."""
+    half = x.shape[-1] // 2
+    rot = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
+    return x * cos[None, :, None, :] + rot * sin[None, :, None, :]
+
+
+def attention(q, k, v, causal: bool = True):
+    """q [B, S, Hq, D], k/v [B, S, Hkv, D] -> [B, S, Hq, D] (GQA)."""
+    qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+    if not q.is_cuda:
+        g = q.shape[2] // k.shape[2]
+        kt = kt.repeat_interleave(g, dim=1)
+        vt = vt.repeat_interleave(g, dim=1)
+        o = torch.nn.functional.scaled_dot_product_attention(qt.float(), kt.float(), vt.float(), is_causal=causal)
+        return o.to(q.dtype).transpose(1, 2)
+    o = torch.nn.functional.scaled_dot_product_attention(qt, kt, vt, is_causal=causal,
+                                                         enable_gqa=q.shape[2] != k.shape[2])
+    return o.transpose(1, 2)

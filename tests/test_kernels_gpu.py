@@ -239,3 +239,20 @@ def test_accumulate_gemm_and_consumers(cuda, M):
     g = ops.swiglu_acc(ops.linear_acc(x, ops.interleave_gate_up(wg, wu)))
     assert rel_err(g, ref.swiglu(x.float() @ wg.float().T, x.float() @ wu.float().T)) < 1.5e-2
     assert torch.count_nonzero(ops.scratch(cuda).acc) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 384, 512), (1000, 2048, 640), (4096, 1024, 2048), (96, 1536, 4096)])
+def test_matmul_training_majors(cuda, M, N, K):
+    """Forward (x @ W.T), dgrad (dY @ W) and wgrad (dY.T @ X, f32 accumulate)."""
+    x = _mk((M, K), cuda, 1.0, 40)
+    w = _mk((N, K), cuda, 0.05, 41)
+    dy = _mk((M, N), cuda, 1.0, 42)
+    y = ops.matmul(x, w.t())
+    assert rel_err(y, x.float() @ w.float().T) < 1e-2
+    dx = ops.matmul(dy, w)
+    assert rel_err(dx, dy.float() @ w.float()) < 1e-2
+    dw = torch.zeros(N, K, dtype=torch.float32, device=cuda)
+    ops.matmul(dy.t(), x, out=dw, accumulate=True)
+    ops.matmul(dy.t(), x, out=dw, accumulate=True)
+    assert rel_err(dw, 2 * (dy.float().T @ x.float())) < 5e-3
+    ops.check_errors(cuda)
