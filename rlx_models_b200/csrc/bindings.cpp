@@ -308,7 +308,7 @@ Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> sizes, at::ScalarType d
 
 // GEMM in reduce-scatter push mode (see gemm_sm100.cuh). peer_out / peer_flags
 // are device int64 arrays of peer pointers; epoch / done_ctr are local uint32.
-void linear_push(const Tensor& x, const Tensor& w, const optional<Tensor>& bias, int64_t mode, int64_t rpr,
+void linear_push(const Tensor& x, const Tensor& w, const optional<Tensor>& bias, int64_t mode, bool bcast, int64_t rpr,
                  int64_t ld_out, int64_t slot_elems, int64_t my_rank, int64_t world, const Tensor& peer_out,
                  const Tensor& peer_flags, const Tensor& epoch, const Tensor& done_ctr, Tensor& ws, Tensor& sem,
                  Tensor& status) {
@@ -352,6 +352,7 @@ void linear_push(const Tensor& x, const Tensor& w, const optional<Tensor>& bias,
   a.epoch = reinterpret_cast<const unsigned*>(epoch.data_ptr<int>());
   a.done_ctr = reinterpret_cast<unsigned*>(done_ctr.data_ptr<int>());
   a.peer_flags = reinterpret_cast<unsigned* const*>(peer_flags.data_ptr<int64_t>());
+  a.bcast = bcast ? 1 : 0;
   b200::linear_launch(a, cur_stream(x));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -504,6 +505,30 @@ void ce_fwd_bwd(const Tensor& logits, const Tensor& targets, Tensor& loss, const
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void os_reduce_norm(const Tensor& slots, int64_t slot_elems, Tensor& h, const Tensor& norm_w, Tensor& out,
+                    const Tensor& flags, Tensor& epoch, Tensor& cta_ctr, int64_t M, int64_t world, double eps,
+                    Tensor& status) {
+  check_cuda(h, "h");
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous() && out.is_contiguous(), "b200.os_reduce_norm");
+  c10::cuda::CUDAGuard g(h.device());
+  b200::OsReduceArgs a{};
+  a.slots = slots.data_ptr();
+  a.slot_elems = slot_elems;
+  a.h = h.data_ptr();
+  a.norm_w = norm_w.data_ptr();
+  a.out = out.data_ptr();
+  a.flags = reinterpret_cast<const unsigned*>(flags.data_ptr<int>());
+  a.epoch = reinterpret_cast<unsigned*>(epoch.data_ptr<int>());
+  a.cta_ctr = reinterpret_cast<unsigned*>(cta_ctr.data_ptr<int>());
+  a.M = (int)M;
+  a.H = (int)h.size(1);
+  a.world = (int)world;
+  a.eps = (float)eps;
+  a.status = status.data_ptr<int>();
+  b200::os_reduce_norm_launch(a, cur_stream(h));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
   m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none());
@@ -526,6 +551,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("linear_push", &linear_push);
   m.def("rs_norm_ag", &rs_norm_ag);
+  m.def("os_reduce_norm", &os_reduce_norm);
   m.def("add_rmsnorm_acc", &add_rmsnorm_acc);
   m.def("swiglu_acc", &swiglu_acc);
 }

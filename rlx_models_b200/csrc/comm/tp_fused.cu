@@ -166,4 +166,93 @@ void rs_norm_ag_launch(const RsNormAgArgs& a, cudaStream_t st) {
   launch_pdl(rs_norm_ag_kernel, dim3(std::max(1, n_my)), dim3(kRsThreads), 0, st, a);
 }
 
+// ---------------------------------------------------------------------------
+// One-shot variant for decode-sized steps: the GEMM broadcast its bf16 partial
+// into slot `rank` of every rank; every rank sums all slots for all rows.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kRsThreads) os_reduce_norm_kernel(OsReduceArgs a) {
+  __shared__ float red[kRsThreads / 32];
+  pdl_wait();
+  pdl_trigger();
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(a.epoch) + 1u;
+  if (threadIdx.x < (unsigned)a.world) wait_flag_geq(a.flags + threadIdx.x, e, a.status, 300 + threadIdx.x);
+  __syncthreads();
+  const __nv_bfloat16* slots = reinterpret_cast<const __nv_bfloat16*>(a.slots);
+  __nv_bfloat16* hbuf = reinterpret_cast<__nv_bfloat16*>(a.h);
+  const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  const int r = blockIdx.x;
+  const int nch = a.H / (kRsThreads * 8);
+  float v[kRsMaxChunks][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < kRsMaxChunks; ++c) {
+    if (c >= nch) break;
+    const int col = (c * kRsThreads + threadIdx.x) * 8;
+    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int q = 0; q < a.world; ++q) {
+      const uint4 pv = __ldcg(reinterpret_cast<const uint4*>(slots + q * a.slot_elems + (int64_t)r * a.H + col));
+      const uint32_t pw[4] = {pv.x, pv.y, pv.z, pv.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        s[2 * k] += bf16_lo(pw[k]);
+        s[2 * k + 1] += bf16_hi(pw[k]);
+      }
+    }
+    const uint4 hv = *reinterpret_cast<const uint4*>(hbuf + (int64_t)r * a.H + col);
+    const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      o[k] = pack_bf16x2(bf16_lo(hw[k]) + __bfloat162float(__float2bfloat16(s[2 * k])),
+                         bf16_hi(hw[k]) + __bfloat162float(__float2bfloat16(s[2 * k + 1])));
+      v[c][2 * k] = bf16_lo(o[k]);
+      v[c][2 * k + 1] = bf16_hi(o[k]);
+      ss += v[c][2 * k] * v[c][2 * k] + v[c][2 * k + 1] * v[c][2 * k + 1];
+    }
+    *reinterpret_cast<uint4*>(hbuf + (int64_t)r * a.H + col) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < kRsThreads / 32 ? red[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(red[0] / (float)a.H + a.eps);
+#pragma unroll
+  for (int c = 0; c < kRsMaxChunks; ++c) {
+    if (c >= nch) break;
+    const int col = (c * kRsThreads + threadIdx.x) * 8;
+    const uint4 wv = *reinterpret_cast<const uint4*>(nw + col);
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      o[k] = pack_bf16x2(__bfloat162float(__float2bfloat16(v[c][2 * k] * inv)) * bf16_lo(ww[k]),
+                         __bfloat162float(__float2bfloat16(v[c][2 * k + 1] * inv)) * bf16_hi(ww[k]));
+    }
+    *reinterpret_cast<uint4*>(out + (int64_t)r * a.H + col) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned old = atomicAdd(a.cta_ctr, 1u);
+    if (old == gridDim.x - 1) {
+      *a.cta_ctr = 0;
+      __threadfence();
+      *reinterpret_cast<volatile unsigned*>(a.epoch) = e;
+    }
+  }
+}
+
+void os_reduce_norm_launch(const OsReduceArgs& a, cudaStream_t st) {
+  if (a.H % (kRsThreads * 8) != 0 || a.H > kRsThreads * 8 * kRsMaxChunks)
+    throw std::runtime_error("b200.os_reduce_norm: hidden must be a multiple of 2048 and <= 8192");
+  launch_pdl(os_reduce_norm_kernel, dim3(std::max(1, a.M)), dim3(kRsThreads), 0, st, a);
+}
+
 }  // namespace b200

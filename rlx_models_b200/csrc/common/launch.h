@@ -38,6 +38,7 @@ struct LinearArgs {
   const unsigned* epoch = nullptr;
   unsigned* done_ctr = nullptr;
   unsigned* const* peer_flags = nullptr;
+  int bcast = 0;  // one-shot: push rows to every rank's slot `my_rank`
   unsigned long long* trace = nullptr;  // debug timeline
 };
 void linear_launch(const LinearArgs& a, cudaStream_t st);
@@ -88,6 +89,24 @@ struct RsNormAgArgs {
   int* status;
 };
 void rs_norm_ag_launch(const RsNormAgArgs& a, cudaStream_t st);
+
+// One-shot all-reduce consumer: wait for every rank's epoch flag, then per row
+// h = bf16(h + bf16(sum_q slots[q][row])) (fixed rank order: identical on all
+// ranks), out = rmsnorm(h) * w; the last CTA advances the local epoch.
+struct OsReduceArgs {
+  const void* slots;        // local [world][M][H] bf16 (this op's parity buffer)
+  int64_t slot_elems;       // elements per slot
+  void* h;                  // [M][H] bf16 replicated residual stream (in/out)
+  const void* norm_w;
+  void* out;                // [M][H] bf16
+  const unsigned* flags;    // local [world]
+  unsigned* epoch;
+  unsigned* cta_ctr;
+  int M, H, world;
+  float eps;
+  int* status;
+};
+void os_reduce_norm_launch(const OsReduceArgs& a, cudaStream_t st);
 
 // ---------------- norms / rope / embedding ----------------
 void embedding_launch(const int32_t* ids, const void* table, void* out, int64_t T, int64_t H, int64_t V,

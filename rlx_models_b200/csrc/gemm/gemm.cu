@@ -129,6 +129,8 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
   p.epoch = a.epoch;
   p.done_ctr = a.done_ctr;
   p.peer_flags = a.peer_flags;
+  p.bcast = a.bcast;
+  if (p.bcast && !sw) throw std::runtime_error("b200.linear: broadcast push needs the swap-AB (decode) path");
   p.trace = a.trace;
   if (p.peer_out != nullptr && (p.rpr <= 0 || p.done_ctr == nullptr || p.peer_flags == nullptr || p.epoch == nullptr))
     throw std::runtime_error("b200.linear: incomplete push-mode arguments");

@@ -67,6 +67,7 @@ struct Params {
   const unsigned* epoch;
   unsigned* done_ctr;
   unsigned* const* peer_flags;
+  int bcast;  // push every output row to all ranks (one-shot all-reduce slots) instead of its owner
   unsigned long long* trace;  // optional per-CTA timeline ([grid][16] globaltimer ns), debug only
 };
 
@@ -193,76 +194,57 @@ __device__ __forceinline__ void store_chunk(const Params& p, int i, int j0, floa
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + __expf(-g)) * u; }
 
-// Swap-AB output row: token j, features [fo, fo+32) (contiguous in C / R / bias).
-template <int EPI>
-__device__ __forceinline__ void store_row32(const Params& p, int j, int fo, int nfeat, float (&o)[32]) {
-  const bool full = fo + 32 <= nfeat;
+// Swap-AB output: token j, NV consecutive features [fo, fo + NV) of one lane
+// (the lanes of a warp cover one token's features contiguously).
+template <int EPI, int NV>
+__device__ __forceinline__ void store_vec(const Params& p, int j, int fo, int nfeat, float (&o)[4]) {
+  if (fo >= nfeat) return;
+  const bool full = fo + NV <= nfeat;
   if (p.bias != nullptr) {
-    if (full && ((reinterpret_cast<uintptr_t>(p.bias + fo) & 15u) == 0)) {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 w = *reinterpret_cast<const uint4*>(p.bias + fo + q * 8);
-        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          o[q * 8 + 2 * h] += bf16_lo(ww[h]);
-          o[q * 8 + 2 * h + 1] += bf16_hi(ww[h]);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int t = 0; t < 32; ++t)
-        if (fo + t < nfeat) o[t] += __bfloat162float(p.bias[fo + t]);
-    }
+    for (int t = 0; t < NV; ++t)
+      if (fo + t < nfeat) o[t] += __bfloat162float(p.bias[fo + t]);
   }
   if (p.R != nullptr) {
     const __nv_bfloat16* r = p.R + (int64_t)j * p.ldr_j + fo;
-    if (full && ((reinterpret_cast<uintptr_t>(r) & 15u) == 0)) {
-      uint4 w[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) w[q] = *reinterpret_cast<const uint4*>(r + q * 8);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint32_t ww[4] = {w[q].x, w[q].y, w[q].z, w[q].w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          o[q * 8 + 2 * h] += bf16_lo(ww[h]);
-          o[q * 8 + 2 * h + 1] += bf16_hi(ww[h]);
-        }
-      }
+    if (NV == 4 && full && ((reinterpret_cast<uintptr_t>(r) & 7u) == 0)) {
+      const uint2 w = *reinterpret_cast<const uint2*>(r);
+      o[0] += bf16_lo(w.x);
+      o[1] += bf16_hi(w.x);
+      o[2] += bf16_lo(w.y);
+      o[3] += bf16_hi(w.y);
     } else {
 #pragma unroll
-      for (int t = 0; t < 32; ++t)
+      for (int t = 0; t < NV; ++t)
         if (fo + t < nfeat) o[t] += __bfloat162float(r[t]);
     }
   }
   if (EPI == EPI_F32) {
     float* c = out_row<float>(p, j, p.ldc_j) + fo;
-    if (full && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0)) {
-#pragma unroll
-      for (int q = 0; q < 8; ++q)
-        *reinterpret_cast<float4*>(c + q * 4) = make_float4(o[q * 4], o[q * 4 + 1], o[q * 4 + 2], o[q * 4 + 3]);
+    if (NV == 4 && full && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0)) {
+      *reinterpret_cast<float4*>(c) = make_float4(o[0], o[1], o[2], o[3]);
     } else {
 #pragma unroll
-      for (int t = 0; t < 32; ++t)
+      for (int t = 0; t < NV; ++t)
         if (fo + t < nfeat) c[t] = o[t];
     }
   } else {
-    __nv_bfloat16* c = out_row<__nv_bfloat16>(p, j, p.ldc_j) + fo;
-    if (full && ((reinterpret_cast<uintptr_t>(c) & 15u) == 0)) {
+    const int nq = p.bcast ? p.world : 1;
+    for (int q = 0; q < nq; ++q) {
+      __nv_bfloat16* c =
+          (p.bcast ? reinterpret_cast<__nv_bfloat16*>(p.peer_out[q]) + (int64_t)p.my_rank * p.slot_elems +
+                         (int64_t)j * p.ldc_j
+                   : out_row<__nv_bfloat16>(p, j, p.ldc_j)) +
+          fo;
+      if (full && NV == 4 && ((reinterpret_cast<uintptr_t>(c) & 7u) == 0)) {
+        *reinterpret_cast<uint2*>(c) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+      } else if (full && NV == 2 && ((reinterpret_cast<uintptr_t>(c) & 3u) == 0)) {
+        *reinterpret_cast<uint32_t*>(c) = pack_bf16x2(o[0], o[1]);
+      } else {
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 w;
-        w.x = pack_bf16x2(o[q * 8 + 0], o[q * 8 + 1]);
-        w.y = pack_bf16x2(o[q * 8 + 2], o[q * 8 + 3]);
-        w.z = pack_bf16x2(o[q * 8 + 4], o[q * 8 + 5]);
-        w.w = pack_bf16x2(o[q * 8 + 6], o[q * 8 + 7]);
-        *reinterpret_cast<uint4*>(c + q * 8) = w;
+        for (int t = 0; t < NV; ++t)
+          if (fo + t < nfeat) c[t] = __float2bfloat16(o[t]);
       }
-    } else {
-#pragma unroll
-      for (int t = 0; t < 32; ++t)
-        if (fo + t < nfeat) c[t] = __float2bfloat16(o[t]);
     }
   }
 }
@@ -495,20 +477,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int t = 0; t < 32; ++t) xchg[t * 132 + row] = __uint_as_float(r[t]);
           named_bar_sync(2, 128);
-          const int tl = et >> 2, seg = et & 3;
-          const int j = jt + c * 32 + tl;
-          const int f0 = m_tile * kBM + seg * 32;
-          if (j < p.NB && f0 < p.MA) {
-            // local accumulator, or (tensor parallel) the row owner's over NVLink
-            float* drow = (p.peer_out != nullptr ? out_row<float>(p, j, p.ldc_j) : dst + (int64_t)j * p.ldc_j) + f0;
-            const float* src = xchg + tl * 132 + seg * 32;
-            if (f0 + 32 <= p.MA) {
-#pragma unroll
-              for (int q = 0; q < 8; ++q)
-                red_add_v4(drow + q * 4, src[q * 4] * p.alpha, src[q * 4 + 1] * p.alpha, src[q * 4 + 2] * p.alpha,
-                           src[q * 4 + 3] * p.alpha);
-            } else {
-              for (int t = 0; f0 + t < p.MA && t < 32; ++t) atomicAdd(drow + t, src[t] * p.alpha);
+          // one token per warp-instruction: lane l adds features [4l, 4l+4) -> 512 B contiguous
+          const float4* xs = reinterpret_cast<const float4*>(xchg);
+          for (int tt = ew; tt < 32; tt += 4) {
+            const int j = jt + c * 32 + tt;
+            const int f = m_tile * kBM + lane * 4;
+            if (j < p.NB && f < p.MA) {
+              // local accumulator, or (tensor parallel) the row owner's over NVLink
+              float* drow = (p.peer_out != nullptr ? out_row<float>(p, j, p.ldc_j) : dst + (int64_t)j * p.ldc_j) + f;
+              const float4 v4 = xs[tt * 33 + lane];
+              if (f + 4 <= p.MA) {
+                red_add_v4(drow, v4.x * p.alpha, v4.y * p.alpha, v4.z * p.alpha, v4.w * p.alpha);
+              } else {
+                const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+                for (int t = 0; f + t < p.MA; ++t) atomicAdd(drow + t, vv[t] * p.alpha);
+              }
             }
           }
           named_bar_sync(2, 128);
@@ -580,31 +563,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int t = 0; t < 32; ++t) xchg[t * 132 + row] = v[t];
           named_bar_sync(2, 128);
-          const int tl = et >> 2, seg = et & 3;  // token within chunk, 32-feature segment
-          const int j = jt + c * 32 + tl;
-          float o[32];
-          int fo;       // first output feature of this segment
-          bool active;
-          if (EPI == EPI_SWIGLU) {
-            active = seg < 2;
-            fo = m_tile * 64 + seg * 32;
-#pragma unroll
-            for (int t = 0; t < 32; ++t) {
-              const float g = xchg[tl * 132 + seg * 32 + t] * p.alpha;
-              const float uu = xchg[tl * 132 + 64 + seg * 32 + t] * p.alpha;
-              o[t] = silu_mul(g, uu);
+          const int nfeat = (EPI == EPI_SWIGLU) ? p.MA / 2 : p.MA;
+          // one token per warp-instruction, contiguous features across the lanes
+          for (int tt = ew; tt < 32; tt += 4) {
+            const int j = jt + c * 32 + tt;
+            if (j >= p.NB) continue;
+            if (EPI == EPI_SWIGLU) {
+              const int fl = lane * 2;  // 64 outputs per tile: 2 per lane
+              const int fo = m_tile * 64 + fl;
+              float o[4] = {silu_mul(xchg[tt * 132 + fl] * p.alpha, xchg[tt * 132 + 64 + fl] * p.alpha),
+                            silu_mul(xchg[tt * 132 + fl + 1] * p.alpha, xchg[tt * 132 + 64 + fl + 1] * p.alpha),
+                            0.f, 0.f};
+              store_vec<EPI, 2>(p, j, fo, nfeat, o);
+            } else {
+              const int fl = lane * 4;
+              const int fo = m_tile * kBM + fl;
+              const float4 v4 = reinterpret_cast<const float4*>(xchg)[tt * 33 + lane];
+              float o[4] = {v4.x * p.alpha, v4.y * p.alpha, v4.z * p.alpha, v4.w * p.alpha};
+              store_vec<EPI, 4>(p, j, fo, nfeat, o);
             }
-          } else {
-            active = true;
-            fo = m_tile * kBM + seg * 32;
-#pragma unroll
-            for (int t = 0; t < 32; ++t) o[t] = xchg[tl * 132 + seg * 32 + t] * p.alpha;
           }
           named_bar_sync(2, 128);
-          const int nfeat = (EPI == EPI_SWIGLU) ? p.MA / 2 : p.MA;
-          if (active && j < p.NB && fo < nfeat) {
-            store_row32<EPI>(p, j, fo, nfeat, o);
-          }
         }
       } else if (EPI == EPI_SWIGLU) {
         // gate/up interleaved along j in groups of 64 columns: [g*128, g*128+64) gate, +64 up.
@@ -623,6 +602,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             q.bias = nullptr;
             store_chunk<BN, EPI_BF16>(q, i, (jt + g * 128) / 2 + h * 32, vg);
           }
+        }
+      } else if (EPI == EPI_BF16 && p.peer_out != nullptr) {
+        // Reduce-scatter push (remote rows): stage the [128 x 32] chunk in smem
+        // so that each store is a 64-byte row segment instead of one 16-byte
+        // piece per lane, then write 8 rows per warp instruction.
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          float v[32];
+          fetch(c, v);
+          const int j0 = jt + c * 32;
+#pragma unroll
+          for (int t = 0; t < 32; ++t) {
+            float x = v[t] * p.alpha;
+            if (p.bias != nullptr && j0 + t < p.NB) x += __bfloat162float(p.bias[j0 + t]);
+            xchg[row * 33 + t] = x;
+          }
+          named_bar_sync(2, 128);
+#pragma unroll
+          for (int st = 0; st < 4; ++st) {
+            const int rr = ew * 32 + st * 8 + (lane >> 2);
+            const int q = lane & 3;
+            const int ii = m_tile * kBM + rr;
+            const int jj = j0 + q * 8;
+            if (ii < p.MA && jj < p.NB) {
+              __nv_bfloat16* cptr = out_row<__nv_bfloat16>(p, ii, p.ldc_i) + jj;
+              const float* src = xchg + rr * 33 + q * 8;
+              if (jj + 8 <= p.NB && ((reinterpret_cast<uintptr_t>(cptr) & 15u) == 0)) {
+                *reinterpret_cast<uint4*>(cptr) = make_uint4(pack_bf16x2(src[0], src[1]), pack_bf16x2(src[2], src[3]),
+                                                             pack_bf16x2(src[4], src[5]), pack_bf16x2(src[6], src[7]));
+              } else {
+                for (int t = 0; t < 8 && jj + t < p.NB; ++t) cptr[t] = __float2bfloat16(src[t]);
+              }
+            }
+          }
+          named_bar_sync(2, 128);
         }
       } else {
 #pragma unroll 1

@@ -1,0 +1,165 @@
+"""Row-parallel op microbenchmark (launch with torchrun on N GPUs).
+
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 -m rlx_models_b200.parallel.comm_bench [--M 64]
+
+Times, per rank with CUDA events (max over ranks), the decoder's row-parallel
+step ``h += allreduce(x @ w_shard.T); x_next = rmsnorm(h)`` at the Qwen3-8B
+o_proj shape (K = 4096 / N) through each communicator, plus a bare NCCL
+all-reduce of the same partial. Reports us/op and, for the fused path, the
+fraction of its roofline max(GEMM at peak, HBM weight stream, NVLink bytes at
+the measured 770 GB/s per direction).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+from datetime import timedelta
+
+import torch
+import torch.distributed as dist
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--M", type=int, default=64)
+    ap.add_argument("--H", type=int, default=4096)
+    ap.add_argument("--K", type=int, default=4096)
+    ap.add_argument("--iters", type=int, default=100)
+    ap.add_argument("--graph", type=int, default=1)
+    args = ap.parse_args()
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    from .. import ops
+    from .tp import make_tp_comm
+
+    M, H, K = args.M, args.H, args.K // world
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.randn(M, K, device=dev, generator=g).bfloat16()
+    w = (torch.randn(H, K, device=dev, generator=g) * 0.02).bfloat16()
+    nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
+    res = {}
+    for kind in ("nccl", "fused"):
+        comm = make_tp_comm(kind, rank, world, dev, 1e-6, max_tokens=max(M, 128), hidden=H)
+        ids = torch.zeros(M, dtype=torch.int32, device=dev)
+        table = torch.randn(8, H, device=dev).bfloat16()
+        h = comm.embed(ids, table)
+        comm.norm_in(h, nw)
+
+        def op():
+            comm.rowpar_add_norm(x, w, h, nw)
+
+        for _ in range(5):
+            op()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        fn = op
+        if args.graph:
+            gr = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                op()
+            torch.cuda.current_stream(dev).wait_stream(s)
+            torch.cuda.synchronize(dev)
+            with torch.cuda.graph(gr):
+                for _ in range(args.iters):
+                    op()
+            fn = gr.replay
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        if args.graph:
+            fn()
+        else:
+            for _ in range(args.iters):
+                fn()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([e0.elapsed_time(e1) / args.iters * 1e3], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[kind] = round(float(t), 2)
+        ops.check_errors(dev)
+        if args.graph:
+            del gr
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        if hasattr(comm, "close"):
+            comm.close()
+    # per-kernel breakdown of the fused op (eager, events between launches)
+    from ..ops._ext import ext, scratch
+    comm = make_tp_comm("fused", rank, world, dev, 1e-6, max_tokens=max(M, 128), hidden=H)
+    h = comm.embed(torch.zeros(M, dtype=torch.int32, device=dev), torch.randn(8, H, device=dev).bfloat16())
+    comm.norm_in(h, nw)
+    sc = scratch(dev)
+    acc_mode = M <= 128
+    comm.one_shot = False  # breakdown of the two-shot kernels
+    comm.rpr = (M + world - 1) // world
+    h = torch.zeros(comm.rpr, H, device=dev, dtype=torch.bfloat16)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    tg = tn = 0.0
+    for it in range(args.iters + 5):
+        dist.barrier()
+        ev[0].record()
+        if acc_mode:
+            ext().linear_push(x, w, None, 3, False, comm.rpr, H, 0, rank, world, comm.peer_racc, comm.peer_rs,
+                              comm.ctr[0:1], comm.ctr[2:3], sc.gemm_ws, sc.gemm_sem, sc.status)
+        else:
+            ext().linear_push(x, w, None, 0, False, comm.rpr, H, comm.slot_elems, rank, world, comm.peer_recv, comm.peer_rs,
+                              comm.ctr[0:1], comm.ctr[2:3], sc.gemm_ws, sc.gemm_sem, sc.status)
+        ev[1].record()
+        comm._rs_norm_ag(None if acc_mode else comm.recv, h, nw, racc=comm.racc if acc_mode else None)
+        ev[2].record()
+        torch.cuda.synchronize(dev)
+        if it >= 5:
+            tg += ev[0].elapsed_time(ev[1])
+            tn += ev[1].elapsed_time(ev[2])
+    t = torch.tensor([tg / args.iters * 1e3, tn / args.iters * 1e3], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    res["fused_breakdown_us"] = {"gemm_push": round(float(t[0]), 2), "rs_norm_ag": round(float(t[1]), 2)}
+    # the same GEMM without the push (local output) for comparison
+    tl = 0.0
+    for it in range(args.iters + 5):
+        ev[0].record()
+        if acc_mode:
+            ops.linear_acc(x, w).zero_()
+        else:
+            ops.linear(x, w)
+        ev[1].record()
+        torch.cuda.synchronize(dev)
+        if it >= 5:
+            tl += ev[0].elapsed_time(ev[1])
+    res["local_gemm_us"] = round(tl / args.iters * 1e3, 2)
+    ops.check_errors(dev)
+    comm.close()
+    part = torch.randn(M, H, device=dev, dtype=torch.float32)
+    for _ in range(5):
+        dist.all_reduce(part)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.iters):
+        dist.all_reduce(part)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) / args.iters * 1e3], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    res["nccl_allreduce_only_f32"] = round(float(t), 2)
+    # roofline of one row-parallel op on this rank
+    flops = 2.0 * M * H * K
+    w_bytes = 2.0 * H * K
+    link = 2.0 * (world - 1) / world * M * H * 2  # reduce-scatter + all-gather, bf16
+    roof_us = max(flops / 1.6186e15, w_bytes / 6.449e12, link / 770e9) * 1e6
+    res.update(world=world, M=M, H=H, K_per_rank=K, roofline_us=round(roof_us, 2),
+               fused_frac_of_roofline=round(roof_us / res["fused"], 3))
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

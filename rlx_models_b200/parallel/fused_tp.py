@@ -48,6 +48,10 @@ class FusedTPComm(NcclTPComm):
         self.o_gath = lay.add("gath", (max_tokens, hidden), torch.bfloat16)
         self.acc_rows = math.ceil(128 / world)  # decode steps (M <= 128) accumulate in fp32
         self.o_racc = lay.add("racc", (self.acc_rows, hidden), torch.float32)
+        # one-shot (decode) path: double-buffered per-rank bf16 slots + flags
+        self.os_rows = 128
+        self.o_os = lay.add("os_slots", (2, world, self.os_rows, hidden), torch.bfloat16)
+        self.o_osf = lay.add("os_flags", (world,), torch.int32)
         self.o_rs = lay.add("rs_flags", (world,), torch.int32)
         self.o_ag = lay.add("ag_flags", (world,), torch.int32)
         self.heap = SymmetricHeap(lay.nbytes, device, group)
@@ -55,6 +59,13 @@ class FusedTPComm(NcclTPComm):
         self.gath = self.heap.view(self.o_gath, (max_tokens, hidden), torch.bfloat16)
         self.racc = self.heap.view(self.o_racc, (self.acc_rows, hidden), torch.float32)
         self.peer_racc = self.heap.peer_ptr_table(self.o_racc)
+        self.os_slots = self.heap.view(self.o_os, (2, world, self.os_rows, hidden), torch.bfloat16)
+        self.os_flags = self.heap.view(self.o_osf, (world,), torch.int32)
+        slot_bytes = world * self.os_rows * hidden * 2
+        self.peer_os = [self.heap.peer_ptr_table(self.o_os + par * slot_bytes) for par in (0, 1)]
+        self.peer_osf = self.heap.peer_ptr_table(self.o_osf)
+        self.parity = 0
+        self.one_shot = False
         self.rs_flags = self.heap.view(self.o_rs, (world,), torch.int32)
         self.ag_flags = self.heap.view(self.o_ag, (world,), torch.int32)
         self.peer_recv = self.heap.peer_ptr_table(self.o_recv)
@@ -73,6 +84,11 @@ class FusedTPComm(NcclTPComm):
         M = ids.shape[0]
         assert M <= self.max_tokens, f"step of {M} tokens exceeds the TP buffers ({self.max_tokens})"
         self.M = M
+        self.parity = 0
+        self.one_shot = M <= self.os_rows
+        if self.one_shot:
+            # decode-sized step: replicated residual stream, one-shot reductions
+            return ops.embedding(ids, table)
         self.rpr = math.ceil(M / self.world)
         lo = min(M, self.rank * self.rpr)
         hi = min(M, lo + self.rpr)
@@ -90,17 +106,33 @@ class FusedTPComm(NcclTPComm):
         return self.gath[:self.M]
 
     def norm_in(self, h, w):
+        if self.one_shot:
+            return ops.rmsnorm(h, w, self.eps)
         return self._rs_norm_ag(None, h, w)
 
     def rowpar_add_norm(self, x, w, h, norm_w, bias=None):
         s = scratch(x.device)
         ops._count(1)
+        if self.one_shot:
+            # GEMM epilogue broadcasts its bf16 partial rows into slot `rank` of
+            # every rank (this op's parity buffer); one kernel per rank waits for
+            # all ranks' epoch flags, sums the slots, adds the residual, RMSNorm.
+            par = self.parity
+            self.parity ^= 1
+            ext().linear_push(x, w, bias if self.rank == 0 else None, 0, True, self.M, self.H,
+                              self.os_rows * self.H, self.rank, self.world, self.peer_os[par], self.peer_osf,
+                              self.ctr[0:1], self.ctr[2:3], s.gemm_ws, s.gemm_sem, s.status)
+            out = torch.empty_like(h)
+            ops._count(1)
+            ext().os_reduce_norm(self.os_slots[par], self.os_rows * self.H, h, norm_w, out, self.os_flags,
+                                 self.ctr[0:1], self.ctr[1:2], self.M, self.world, float(self.eps), s.status)
+            return out
         if x.shape[0] <= 128 and bias is None:
             # decode: split-K partials red.add'ed straight into the owner's fp32 accumulator
-            ext().linear_push(x, w, None, 3, self.rpr, self.H, 0, self.rank, self.world, self.peer_racc,
+            ext().linear_push(x, w, None, 3, False, self.rpr, self.H, 0, self.rank, self.world, self.peer_racc,
                               self.peer_rs, self.ctr[0:1], self.ctr[2:3], s.gemm_ws, s.gemm_sem, s.status)
             return self._rs_norm_ag(None, h, norm_w, racc=self.racc)
-        ext().linear_push(x, w, bias if self.rank == 0 else None, 0, self.rpr, self.H, self.slot_elems, self.rank,
+        ext().linear_push(x, w, bias if self.rank == 0 else None, 0, False, self.rpr, self.H, self.slot_elems, self.rank,
                           self.world, self.peer_recv, self.peer_rs, self.ctr[0:1], self.ctr[2:3], s.gemm_ws,
                           s.gemm_sem, s.status)
         return self._rs_norm_ag(self.recv, h, norm_w)
