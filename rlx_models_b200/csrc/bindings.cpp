@@ -529,10 +529,90 @@ void os_reduce_norm(const Tensor& slots, int64_t slot_elems, Tensor& h, const Te
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void moe_route(const Tensor& logits, int64_t k, bool softmax_first, bool renorm, Tensor& experts, Tensor& weights) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.stride(1) == 1, "b200.moe_route: f32 logits");
+  c10::cuda::CUDAGuard g(logits.device());
+  b200::moe_route_launch(logits.data_ptr<float>(), logits.stride(0), (int)logits.size(0), (int)logits.size(1),
+                         (int)k, softmax_first, renorm, experts.data_ptr<int32_t>(), weights.data_ptr<float>(),
+                         cur_stream(logits));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void moe_align(const Tensor& experts, int64_t E, int64_t e_lo, int64_t e_cnt, Tensor& meta, Tensor& tiles,
+               Tensor& perm, Tensor& inv, Tensor& cursor) {
+  check_cuda(experts, "experts");
+  TORCH_CHECK(meta.numel() >= 2 * E + 2 && cursor.numel() >= E, "b200.moe_align: buffers");
+  c10::cuda::CUDAGuard g(experts.device());
+  b200::moe_align_launch(experts.data_ptr<int32_t>(), (int)experts.numel(), (int)E, (int)e_lo, (int)e_cnt,
+                         meta.data_ptr<int32_t>(), tiles.data_ptr<int32_t>(), (int)tiles.numel(),
+                         perm.data_ptr<int32_t>(), inv.data_ptr<int32_t>(), cursor.data_ptr<int32_t>(),
+                         cur_stream(experts));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void moe_gather(const Tensor& x, const Tensor& perm, const Tensor& meta, int64_t E, int64_t k, Tensor& out) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.is_contiguous() && out.is_contiguous() && x.size(1) % 8 == 0, "b200.moe_gather");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::moe_gather_launch(x.data_ptr(), x.size(1), perm.data_ptr<int32_t>(), meta.data_ptr<int32_t>(), (int)E,
+                          (int)k, (int)out.size(0), out.data_ptr(), cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void moe_combine(const Tensor& rows, const Tensor& inv, int64_t k, Tensor& out, bool accumulate) {
+  check_cuda(rows, "rows");
+  TORCH_CHECK(out.is_contiguous() && rows.is_contiguous() && out.size(1) % 8 == 0, "b200.moe_combine");
+  c10::cuda::CUDAGuard g(rows.device());
+  b200::moe_combine_launch(rows.data_ptr(), inv.data_ptr<int32_t>(), (int)out.size(0), (int)k, out.size(1),
+                           out.data_ptr(), accumulate, cur_stream(rows));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void moe_gemm(const Tensor& x, const Tensor& blocks, const Tensor& scales, const optional<Tensor>& bias,
+              const optional<Tensor>& row_weight, const Tensor& perm, const Tensor& meta, const Tensor& tiles,
+              Tensor& out, bool swiglu, double limit, double alpha, Tensor& status) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "b200.moe_gemm: x");
+  TORCH_CHECK(blocks.scalar_type() == at::kByte && scales.scalar_type() == at::kByte && blocks.is_contiguous() &&
+                  scales.is_contiguous(),
+              "b200.moe_gemm: uint8 blocks/scales");
+  const int64_t E = blocks.size(0), N = blocks.size(1);
+  const int64_t K = blocks.numel() / (E * N) * 2;
+  TORCH_CHECK(x.size(1) == K, "b200.moe_gemm: K mismatch");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::MoeGemmArgs a{};
+  a.x = x.data_ptr();
+  a.rows = x.size(0);
+  a.blocks = blocks.data_ptr();
+  a.scales = scales.data_ptr();
+  a.bias = opt_ptr(bias);
+  a.row_weight = (row_weight.has_value() && row_weight->defined()) ? row_weight->data_ptr<float>() : nullptr;
+  a.perm = perm.data_ptr<int32_t>();
+  a.meta = meta.data_ptr<int32_t>();
+  a.tiles = tiles.data_ptr<int32_t>();
+  a.out = out.data_ptr();
+  a.E = (int)E;
+  a.N = (int)N;
+  a.K = (int)K;
+  a.swiglu = swiglu;
+  a.limit = (float)limit;
+  a.alpha = (float)alpha;
+  a.status = status.data_ptr<int>();
+  a.device = x.get_device();
+  b200::moe_gemm_launch(a, cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
   m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none());
   m.def("gemm", &gemm);
+  m.def("moe_route", &moe_route);
+  m.def("moe_align", &moe_align);
+  m.def("moe_gather", &moe_gather);
+  m.def("moe_combine", &moe_combine);
+  m.def("moe_gemm", &moe_gemm);
   m.def("adamw", &adamw);
   m.def("sumsq", &sumsq);
   m.def("ce_fwd_bwd", &ce_fwd_bwd);

@@ -173,6 +173,34 @@ void sumsq_launch(const void* g, bool f32, int64_t n, float* out, cudaStream_t s
 void ce_fwd_bwd_launch(const float* logits, int64_t ld, int64_t T, int64_t V, const int64_t* targets, float* loss,
                        void* dlogits, int64_t ldd, float grad_scale, cudaStream_t st);
 
+// ---------------- mixture of experts ----------------
+void moe_route_launch(const float* logits, int64_t ld, int T, int E, int k, int softmax_first, int renorm,
+                      int32_t* experts, float* weights, cudaStream_t st);
+void moe_align_launch(const int32_t* experts, int n_assign, int E, int e_lo, int e_cnt, int32_t* meta,
+                      int32_t* tiles, int max_tiles, int32_t* perm, int32_t* inv, int32_t* cursor, cudaStream_t st);
+void moe_gather_launch(const void* x, int64_t H, const int32_t* perm, const int32_t* meta, int E, int k,
+                       int max_rows, void* out, cudaStream_t st);
+void moe_combine_launch(const void* rows, const int32_t* inv, int T, int k, int64_t H, void* out, int accumulate,
+                        cudaStream_t st);
+struct MoeGemmArgs {
+  const void* x;          // expert-sorted activations [rows, K] bf16
+  int64_t rows;
+  const void* blocks;     // [E, N, K/2] packed E2M1 (gate/up rows interleaved in groups of 64)
+  const void* scales;     // [E, N, K/32] E8M0
+  const void* bias;       // [E, N] bf16 or null
+  const float* row_weight;  // router weights per assignment (down) or null
+  const int32_t* perm;
+  const int32_t* meta;
+  const int32_t* tiles;
+  void* out;
+  int E, N, K;
+  int swiglu;
+  float limit, alpha;
+  int* status;
+  int device;
+};
+void moe_gemm_launch(const MoeGemmArgs& a, cudaStream_t st);
+
 // ---------------- sampling ----------------
 void argmax_launch(const float* logits, int64_t ld, int64_t B, int64_t V, int32_t* out, cudaStream_t st);
 

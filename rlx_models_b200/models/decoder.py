@@ -57,7 +57,6 @@ class LayerWeights:
 class DecoderLM:
     def __init__(self, cfg: DecoderConfig, weights, device: torch.device | str = "cuda",
                  tp_rank: int = 0, tp_size: int = 1, comm=None):
-        assert not cfg.is_moe, "MoE families use models.moe.MoEDecoderLM"
         self.cfg = cfg
         self.device = torch.device(device)
         self.tp_rank, self.tp_size, self.comm = tp_rank, tp_size, comm

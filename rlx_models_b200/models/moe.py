@@ -1,0 +1,164 @@
+"""GPU mixture-of-experts decoder (gpt-oss family) on the sm_100a kernels.
+
+Attention is the dense decoder's (q/k/v/o biases, learned sinks, alternating
+128-token sliding window / full attention, YaRN RoPE); the MLP is a routed
+expert block with MXFP4 expert weights kept packed in HBM:
+
+    router GEMM (f32 logits, bias) -> top-k, softmax over the k
+    -> moe_align (device counts / offsets / permutation / tile list)
+    -> gather rows -> grouped MXFP4 GEMM gate|up (bias, clamped SwiGLU)
+    -> grouped MXFP4 GEMM down (bias, x router weight) -> combine
+
+Expert parallelism: rank r holds experts [r E/ep, (r+1) E/ep). Every rank
+routes all tokens of the step (attention is replicated), runs only its own
+experts and the per-token partial outputs are summed across ranks; with top-4
+routing that sum moves ~2TH bytes per rank against ~7TH for an all-to-all
+dispatch + combine.
+
+Reference: rlx-models-core src/standard_decoder.rs:1040-1205
+(`build_gpt_oss_moe_ffn`), :11873-12208 (`GptOssSpec`, sinks attention,
+prefill); crates/rlx-gpt-oss/src/gpt_oss_ops.rs (clamped SwiGLU, alpha 1.702,
+limit 7). The reference has no decode path and treats every layer as full
+attention; both are implemented here.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..config import DecoderConfig
+from ..ops._ext import ext, scratch
+from ..quant.mxfp4 import quantize_mxfp4
+from .decoder import DecoderLM, LayerWeights, LocalComm
+
+GROUP = 64  # gate/up rows interleaved in groups of 64 for the fused epilogue
+
+
+def hf_interleaved_to_grouped(t: torch.Tensor, dim: int = 1) -> torch.Tensor:
+    """HF gpt-oss gate_up rows alternate (gate, up, gate, up, ...); the grouped
+    GEMM wants [64 gate rows][64 up rows] per 128-row tile."""
+    n = t.shape[dim]
+    idx = torch.arange(n, device=t.device).view(n // (2 * GROUP), GROUP, 2)  # [g, j, (gate, up)]
+    order = idx.permute(0, 2, 1).reshape(-1)  # g: gate_j..., up_j...
+    return t.index_select(dim, order)
+
+
+class MoELayer:
+    __slots__ = ("router_w", "router_b", "gu_blocks", "gu_scales", "gu_bias", "dn_blocks", "dn_scales", "dn_bias")
+
+
+class MoEDecoderLM(DecoderLM):
+    def __init__(self, cfg: DecoderConfig, weights, device="cuda", ep_rank: int = 0, ep_size: int = 1, comm=None):
+        assert cfg.is_moe
+        self.ep_rank, self.ep_size = ep_rank, ep_size
+        assert cfg.num_experts % ep_size == 0
+        self.e_local = cfg.num_experts // ep_size
+        self.e_lo = ep_rank * self.e_local
+        # attention / embeddings are replicated: build the dense parts with tp_size=1
+        self._moe_comm = comm
+        super().__init__(cfg, weights, device=device, tp_rank=0, tp_size=1, comm=None)
+
+    # -- weights ----------------------------------------------------------------
+    def _load(self, w):
+        c, dev, bf = self.cfg, self.device, torch.bfloat16
+
+        def g(name):
+            return self._get(w, name)
+
+        def dv(t):
+            return t.to(device=dev, dtype=bf).contiguous()
+
+        self.embed = dv(g("model.embed_tokens.weight"))
+        self.norm = dv(g("model.norm.weight"))
+        self.lm_head = self.embed if c.tie_word_embeddings else dv(g("lm_head.weight"))
+        D = c.head_dim
+        self.layers, self.moe = [], []
+        lo, hi = self.e_lo, self.e_lo + self.e_local
+        for i in range(c.num_hidden_layers):
+            p = f"model.layers.{i}."
+            L = LayerWeights()
+            L.ln1 = dv(g(p + "input_layernorm.weight"))
+            L.ln2 = dv(g(p + "post_attention_layernorm.weight"))
+            L.wqkv = dv(torch.cat([g(p + f"self_attn.{n}_proj.weight").to(dev) for n in "qkv"], 0))
+            L.bqkv = dv(torch.cat([g(p + f"self_attn.{n}_proj.bias").to(dev) for n in "qkv"])) \
+                if c.attention_bias else None
+            L.q_norm = L.k_norm = None
+            L.wo = dv(g(p + "self_attn.o_proj.weight"))
+            ob = p + "self_attn.o_proj.bias"
+            L.bo = dv(g(ob)) if (ob in w) else None
+            L.w_gu = L.wd = None
+            L.sinks = g(p + "self_attn.sinks").to(dev, torch.float32).contiguous() if c.attn_sinks else None
+            L.window = c.layer_window(i)
+            self.layers.append(L)
+            M = MoELayer()
+            M.router_w = dv(g(p + "mlp.router.weight"))
+            M.router_b = dv(g(p + "mlp.router.bias"))
+            pe = p + "mlp.experts."
+            if (pe + "gate_up_proj_blocks") in w:
+                gub = g(pe + "gate_up_proj_blocks")[lo:hi]
+                gus = g(pe + "gate_up_proj_scales")[lo:hi]
+                dnb = g(pe + "down_proj_blocks")[lo:hi]
+                dns = g(pe + "down_proj_scales")[lo:hi]
+            else:  # bf16 checkpoint: quantize to MXFP4 at load ([E, in, out] -> [E, out, in])
+                gub, gus = quantize_mxfp4(g(pe + "gate_up_proj")[lo:hi].to(dev).float().transpose(1, 2))
+                dnb, dns = quantize_mxfp4(g(pe + "down_proj")[lo:hi].to(dev).float().transpose(1, 2))
+            E_l = hi - lo
+            M.gu_blocks = hf_interleaved_to_grouped(gub.to(dev).reshape(E_l, gub.shape[1], -1)).contiguous()
+            M.gu_scales = hf_interleaved_to_grouped(gus.to(dev).reshape(E_l, gus.shape[1], -1)).contiguous()
+            M.gu_bias = hf_interleaved_to_grouped(dv(g(pe + "gate_up_proj_bias")[lo:hi]))
+            M.dn_blocks = dnb.to(dev).reshape(E_l, dnb.shape[1], -1).contiguous()
+            M.dn_scales = dns.to(dev).reshape(E_l, dns.shape[1], -1).contiguous()
+            M.dn_bias = dv(g(pe + "down_proj_bias")[lo:hi])  # each expert (and its bias) lives on one rank
+            self.moe.append(M)
+
+    # -- forward ---------------------------------------------------------------
+    def _moe(self, i: int, x: torch.Tensor) -> torch.Tensor:
+        c = self.cfg
+        M = self.moe[i]
+        T, H = x.shape
+        k = c.num_experts_per_tok
+        E_l = self.e_local
+        dev = x.device
+        logits = ops.linear(x, M.router_w, bias=M.router_b, out_dtype=torch.float32)
+        experts = torch.empty(T, k, dtype=torch.int32, device=dev)
+        weights = torch.empty(T, k, dtype=torch.float32, device=dev)
+        ext().moe_route(logits, k, not c.softmax_after_topk, c.norm_topk_prob, experts, weights)
+        n = T * k
+        meta = torch.empty(2 * E_l + 2, dtype=torch.int32, device=dev)
+        max_tiles = n // 128 + E_l + 1
+        tiles = torch.empty(max_tiles, dtype=torch.int32, device=dev)
+        perm = torch.empty(n, dtype=torch.int32, device=dev)
+        inv = torch.empty(n, dtype=torch.int32, device=dev)
+        cursor = torch.empty(E_l, dtype=torch.int32, device=dev)
+        ext().moe_align(experts, E_l, self.e_lo, E_l, meta, tiles, perm, inv, cursor)
+        a = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+        ext().moe_gather(x, perm, meta, E_l, k, a)
+        I = c.moe_intermediate_size
+        s = scratch(dev)
+        gu = torch.empty(n, I, dtype=torch.bfloat16, device=dev)
+        ext().moe_gemm(a, M.gu_blocks, M.gu_scales, M.gu_bias, None, perm, meta, tiles, gu, True,
+                       float(c.swiglu_limit or 1e30), float(c.swiglu_alpha), s.status)
+        dn = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+        ext().moe_gemm(gu, M.dn_blocks, M.dn_scales, M.dn_bias, weights.view(-1), perm, meta, tiles, dn, False,
+                       0.0, 0.0, s.status)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        ext().moe_combine(dn, inv, k, out, False)
+        ops._count(7)
+        if self.ep_size > 1:
+            dist.all_reduce(out)
+        return out
+
+    def forward_hidden(self, fb, kv) -> torch.Tensor:
+        c = self.cfg
+        h = ops.embedding(fb.input_ids, self.embed)
+        x = ops.rmsnorm(h, self.layers[0].ln1, c.rms_norm_eps)
+        n = len(self.layers)
+        for i, L in enumerate(self.layers):
+            a = self._attention(i, L, x, fb, kv)
+            ops.linear(a, L.wo, bias=L.bo, residual=h, out=h)  # h += o_proj (+ bias)
+            x = ops.rmsnorm(h, L.ln2, c.rms_norm_eps)
+            m = self._moe(i, x)
+            nw = self.layers[i + 1].ln1 if i + 1 < n else self.norm
+            x = ops.rmsnorm(m, nw, c.rms_norm_eps, residual=h, residual_out=h)  # h += moe; norm
+        return x
