@@ -2,6 +2,7 @@
 
     python bench.py --gpus N --steps K --warmup W           # serving, TP=N
     python bench.py --workload train --gpus N ...           # Qwen3-1.7B FSDP fine-tune step
+    python bench.py --workload moe --gpus N ...             # gpt-oss-120b serving, EP=N
     python bench.py --impl reference ...                    # the reference arm
 
 Serving workload: 64 concurrent requests, prompt lengths
@@ -28,6 +29,18 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "Qwen3-8B-shape TP8 output tok/s/box; p50 TTFT & TPOT; FSDP train tok/s"
+
+# serving workloads: BASELINE config 2 (dense, TP) and config 3 (MoE, EP)
+WORKLOADS = {
+    "serve": dict(model="qwen3-8b", num_requests=64, min_prompt=512, max_prompt=2048, output_len=256,
+                  desc="Qwen3-8B-shape (36L, h4096, 32q/8kv x128, I12288, V151936)", par="tp",
+                  l2="inputs larger than L2: every step streams 16 GB of weights + the KV cache"),
+    "moe": dict(model="gpt-oss-120b", num_requests=128, min_prompt=1024, max_prompt=1024, output_len=256,
+                desc="gpt-oss-120b-shape (36L, h2880, 64q/8kv x64, 128 experts top-4 MXFP4 I2880, SWA128 "
+                     "alternating, sinks, V201088)", par="ep",
+                l2="inputs larger than L2: every decode step streams ~5 GB of attention/lm_head weights, "
+                   "the routed MXFP4 experts and the KV cache"),
+}
 
 
 def reference_arm(args):
@@ -65,20 +78,27 @@ def serve(args):
 
     from rlx_models_b200 import ops
     from rlx_models_b200.api import LLM, load
-    from rlx_models_b200.config import qwen3_8b
     from rlx_models_b200.runtime.engine import EngineConfig, SamplingParams
     from rlx_models_b200.utils.clocks import ClockSampler
 
+    from rlx_models_b200.config import preset
+
+    W = WORKLOADS[args.workload]
+    for key in ("num_requests", "min_prompt", "max_prompt", "output_len"):
+        if getattr(args, key) is None:
+            setattr(args, key, W[key])
     rank, ws, local = init_dist(args)
     dev = torch.device("cuda", local)
-    cfg = qwen3_8b()
-    from rlx_models_b200.parallel.tp import make_tp_comm
-    comm = make_tp_comm(args.tp_comm, rank, ws, dev, cfg.rms_norm_eps, max_tokens=args.max_batched_tokens,
-                        hidden=cfg.hidden_size)
+    cfg = preset(W["model"])
+    comm = None
+    if W["par"] == "tp":
+        from rlx_models_b200.parallel.tp import make_tp_comm
+        comm = make_tp_comm(args.tp_comm, rank, ws, dev, cfg.rms_norm_eps, max_tokens=args.max_batched_tokens,
+                            hidden=cfg.hidden_size)
     ecfg = EngineConfig(max_num_seqs=max(64, args.num_requests), max_batched_tokens=args.max_batched_tokens,
                         max_model_len=args.max_prompt + args.output_len + 16, kv_memory_gb=args.kv_gb,
                         prefix_caching=False, cuda_graphs=True)
-    llm = load("qwen3-8b", device=dev, tp_rank=rank, tp_size=ws, comm=comm, seed=0, engine_config=ecfg,
+    llm = load(W["model"], device=dev, tp_rank=rank, tp_size=ws, comm=comm, seed=0, engine_config=ecfg,
                config=cfg)
     eng = llm.engine
     sp = SamplingParams(max_new_tokens=args.output_len, ignore_eos=True, temperature=0.0)
@@ -143,16 +163,17 @@ def serve(args):
     e2e_val = sum(len(o.token_ids) for o in e2e_outs) / e2e_s
     clocks = sampler.summary()
     res = {
-        "metric": METRIC, "value": round(value, 1), "unit": "output tok/s", "n_gpus": ws, "steps": args.steps,
+        "metric": METRIC if args.workload == "serve" else f"gpt-oss-120b-shape EP output tok/s (part of: {METRIC})",
+        "value": round(value, 1), "unit": "output tok/s", "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 2), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic: uniform-random token ids (seeded, fresh per pass), random-init N(0,0.02) weights",
-        "config": {"model": "Qwen3-8B-shape (36L, h4096, 32q/8kv x128, I12288, V151936)",
+        "config": {"model": W["desc"],
                    "global_batch": args.num_requests, "seq_len": f"prompt U[{args.min_prompt},{args.max_prompt}]"
-                   f" + {args.output_len} out", "parallelism": f"tp{ws}", "tp_comm": args.tp_comm if ws > 1 else None, "kv_block": 16,
-                   "max_batched_tokens": args.max_batched_tokens,
-                   "l2": "inputs larger than L2: every step streams 16 GB of weights + the KV cache",
-                   "step": "one full 64-request serving pass"},
+                   f" + {args.output_len} out", "parallelism": f"{W['par']}{ws}",
+                   "tp_comm": args.tp_comm if (ws > 1 and W["par"] == "tp") else None, "kv_block": 16,
+                   "max_batched_tokens": args.max_batched_tokens, "l2": W["l2"],
+                   "step": f"one full {args.num_requests}-request serving pass"},
         "ttft_p50_ms": round(ttft, 1), "tpot_p50_ms": round(tpot, 2),
         "clocks": clocks,
         "e2e": {"value": round(e2e_val, 1), "unit": "output tok/s via LLM.generate (wall clock)",
@@ -177,11 +198,11 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="serve", choices=["serve", "train"])
-    ap.add_argument("--num-requests", type=int, default=64)
-    ap.add_argument("--min-prompt", type=int, default=512)
-    ap.add_argument("--max-prompt", type=int, default=2048)
-    ap.add_argument("--output-len", type=int, default=256)
+    ap.add_argument("--workload", default="serve", choices=["serve", "moe", "train"])
+    ap.add_argument("--num-requests", type=int, default=None)
+    ap.add_argument("--min-prompt", type=int, default=None)
+    ap.add_argument("--max-prompt", type=int, default=None)
+    ap.add_argument("--output-len", type=int, default=None)
     ap.add_argument("--max-batched-tokens", type=int, default=8192)
     ap.add_argument("--kv-gb", type=float, default=40.0)
     ap.add_argument("--tp-comm", default="nccl", choices=["nccl", "fused"],

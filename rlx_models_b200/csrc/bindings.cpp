@@ -539,13 +539,14 @@ void moe_route(const Tensor& logits, int64_t k, bool softmax_first, bool renorm,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void moe_align(const Tensor& experts, int64_t E, int64_t e_lo, int64_t e_cnt, Tensor& meta, Tensor& tiles,
-               Tensor& perm, Tensor& inv, Tensor& cursor) {
+void moe_align(const Tensor& experts, int64_t E, int64_t e_lo, int64_t e_cnt, int64_t bt, Tensor& meta,
+               Tensor& tiles, Tensor& perm, Tensor& inv, Tensor& cursor) {
   check_cuda(experts, "experts");
   TORCH_CHECK(meta.numel() >= 2 * E + 2 && cursor.numel() >= E, "b200.moe_align: buffers");
   c10::cuda::CUDAGuard g(experts.device());
-  b200::moe_align_launch(experts.data_ptr<int32_t>(), (int)experts.numel(), (int)E, (int)e_lo, (int)e_cnt,
-                         meta.data_ptr<int32_t>(), tiles.data_ptr<int32_t>(), (int)tiles.numel(),
+  TORCH_CHECK(bt >= 1 && tiles.numel() >= 4 * (experts.numel() / bt + E + 1), "b200.moe_align: tile list too small");
+  b200::moe_align_launch(experts.data_ptr<int32_t>(), (int)experts.numel(), (int)E, (int)e_lo, (int)e_cnt, (int)bt,
+                         meta.data_ptr<int32_t>(), tiles.data_ptr<int32_t>(), (int)(tiles.numel() / 4),
                          perm.data_ptr<int32_t>(), inv.data_ptr<int32_t>(), cursor.data_ptr<int32_t>(),
                          cur_stream(experts));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -555,8 +556,11 @@ void moe_gather(const Tensor& x, const Tensor& perm, const Tensor& meta, int64_t
   check_cuda(x, "x");
   TORCH_CHECK(x.is_contiguous() && out.is_contiguous() && x.size(1) % 8 == 0, "b200.moe_gather");
   c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 &&
+                  (out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kHalf),
+              "b200.moe_gather: bf16 -> bf16/f16");
   b200::moe_gather_launch(x.data_ptr(), x.size(1), perm.data_ptr<int32_t>(), meta.data_ptr<int32_t>(), (int)E,
-                          (int)k, (int)out.size(0), out.data_ptr(), cur_stream(x));
+                          (int)k, (int)out.size(0), out.data_ptr(), out.scalar_type() == at::kHalf, cur_stream(x));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -569,23 +573,29 @@ void moe_combine(const Tensor& rows, const Tensor& inv, int64_t k, Tensor& out, 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void moe_gemm(const Tensor& x, const Tensor& blocks, const Tensor& scales, const optional<Tensor>& bias,
+// w, row_exp: tiled MXFP4 weights [E, ceil(N/128), K/64, 4352] and per-row exponents [E, ceil(N/128)*128]
+// (quant.mxfp4.tile_mxfp4); N: logical weight rows. x f16; out f16 (gate/up) or bf16 (down).
+void moe_gemm(const Tensor& x, const Tensor& w, const Tensor& row_exp, int64_t N, const optional<Tensor>& bias,
               const optional<Tensor>& row_weight, const Tensor& perm, const Tensor& meta, const Tensor& tiles,
-              Tensor& out, bool swiglu, double limit, double alpha, Tensor& status) {
+              Tensor& out, bool swiglu, double limit, double alpha, int64_t bt, Tensor& status) {
   check_cuda(x, "x");
-  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "b200.moe_gemm: x");
-  TORCH_CHECK(blocks.scalar_type() == at::kByte && scales.scalar_type() == at::kByte && blocks.is_contiguous() &&
-                  scales.is_contiguous(),
-              "b200.moe_gemm: uint8 blocks/scales");
-  const int64_t E = blocks.size(0), N = blocks.size(1);
-  const int64_t K = blocks.numel() / (E * N) * 2;
+  TORCH_CHECK(x.scalar_type() == at::kHalf && x.is_contiguous(), "b200.moe_gemm: x must be f16");
+  TORCH_CHECK(out.scalar_type() == (swiglu ? at::kHalf : at::kBFloat16), "b200.moe_gemm: out f16 (gate/up) / bf16");
+  TORCH_CHECK(w.scalar_type() == at::kByte && w.is_contiguous() && w.dim() == 4 && w.size(3) == 4352,
+              "b200.moe_gemm: tiled uint8 weights [E, NT, KT, 4352]");
+  const int64_t E = w.size(0);
+  const int64_t K = w.size(2) * 64;
+  TORCH_CHECK(w.size(1) == (N + 127) / 128, "b200.moe_gemm: weight n-tiles do not match N");
+  TORCH_CHECK(row_exp.scalar_type() == at::kByte && row_exp.numel() == E * w.size(1) * 128, "b200.moe_gemm: row_exp");
   TORCH_CHECK(x.size(1) == K, "b200.moe_gemm: K mismatch");
+  TORCH_CHECK(out.is_contiguous() && out.size(1) == (swiglu ? N / 2 : N), "b200.moe_gemm: out");
+  TORCH_CHECK(!bias.has_value() || !bias->defined() || bias->numel() == E * N, "b200.moe_gemm: bias [E, N]");
   c10::cuda::CUDAGuard g(x.device());
   b200::MoeGemmArgs a{};
   a.x = x.data_ptr();
   a.rows = x.size(0);
-  a.blocks = blocks.data_ptr();
-  a.scales = scales.data_ptr();
+  a.w = w.data_ptr();
+  a.row_exp = row_exp.data_ptr();
   a.bias = opt_ptr(bias);
   a.row_weight = (row_weight.has_value() && row_weight->defined()) ? row_weight->data_ptr<float>() : nullptr;
   a.perm = perm.data_ptr<int32_t>();
@@ -595,6 +605,8 @@ void moe_gemm(const Tensor& x, const Tensor& blocks, const Tensor& scales, const
   a.E = (int)E;
   a.N = (int)N;
   a.K = (int)K;
+  a.bt = (int)bt;
+  a.max_tiles = (int)(tiles.numel() / 4);
   a.swiglu = swiglu;
   a.limit = (float)limit;
   a.alpha = (float)alpha;

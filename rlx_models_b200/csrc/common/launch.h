@@ -176,17 +176,18 @@ void ce_fwd_bwd_launch(const float* logits, int64_t ld, int64_t T, int64_t V, co
 // ---------------- mixture of experts ----------------
 void moe_route_launch(const float* logits, int64_t ld, int T, int E, int k, int softmax_first, int renorm,
                       int32_t* experts, float* weights, cudaStream_t st);
-void moe_align_launch(const int32_t* experts, int n_assign, int E, int e_lo, int e_cnt, int32_t* meta,
+void moe_align_launch(const int32_t* experts, int n_assign, int E, int e_lo, int e_cnt, int bt, int32_t* meta,
                       int32_t* tiles, int max_tiles, int32_t* perm, int32_t* inv, int32_t* cursor, cudaStream_t st);
 void moe_gather_launch(const void* x, int64_t H, const int32_t* perm, const int32_t* meta, int E, int k,
-                       int max_rows, void* out, cudaStream_t st);
+                       int max_rows, void* out, int to_f16, cudaStream_t st);
 void moe_combine_launch(const void* rows, const int32_t* inv, int T, int k, int64_t H, void* out, int accumulate,
                         cudaStream_t st);
 struct MoeGemmArgs {
-  const void* x;          // expert-sorted activations [rows, K] bf16
+  const void* x;          // expert-sorted activations [rows, K] f16
   int64_t rows;
-  const void* blocks;     // [E, N, K/2] packed E2M1 (gate/up rows interleaved in groups of 64)
-  const void* scales;     // [E, N, K/32] E8M0
+  const void* w;          // tiled MXFP4 blocks [E, ceil(N/128), K/64, 4096 codes + 256 scales]
+                          // (gate/up rows interleaved in groups of 64); scales as offsets from row_exp
+  const void* row_exp;    // [E, ceil(N/128) * 128] uint8 largest E8M0 exponent per weight row
   const void* bias;       // [E, N] bf16 or null
   const float* row_weight;  // router weights per assignment (down) or null
   const int32_t* perm;
@@ -194,6 +195,8 @@ struct MoeGemmArgs {
   const int32_t* tiles;
   void* out;
   int E, N, K;
+  int bt;                 // token tile (32, 64, 128, 256)
+  int max_tiles;          // capacity of the tile list (grid bound)
   int swiglu;
   float limit, alpha;
   int* status;

@@ -29,7 +29,7 @@ import torch.distributed as dist
 from .. import ops
 from ..config import DecoderConfig
 from ..ops._ext import ext, scratch
-from ..quant.mxfp4 import quantize_mxfp4
+from ..quant.mxfp4 import quantize_mxfp4, tile_mxfp4
 from .decoder import DecoderLM, LayerWeights, LocalComm
 
 GROUP = 64  # gate/up rows interleaved in groups of 64 for the fused epilogue
@@ -44,8 +44,17 @@ def hf_interleaved_to_grouped(t: torch.Tensor, dim: int = 1) -> torch.Tensor:
     return t.index_select(dim, order)
 
 
+def token_tile(n_assign: int, num_experts: int) -> int:
+    """Token-tile width of the grouped GEMM from the mean rows per expert."""
+    avg = n_assign / max(1, num_experts)
+    for bt in (32, 64):
+        if avg <= bt:
+            return bt
+    return 128
+
+
 class MoELayer:
-    __slots__ = ("router_w", "router_b", "gu_blocks", "gu_scales", "gu_bias", "dn_blocks", "dn_scales", "dn_bias")
+    __slots__ = ("router_w", "router_b", "gu_w", "gu_exp", "gu_bias", "dn_w", "dn_exp", "dn_bias")
 
 
 class MoEDecoderLM(DecoderLM):
@@ -104,11 +113,10 @@ class MoEDecoderLM(DecoderLM):
                 gub, gus = quantize_mxfp4(g(pe + "gate_up_proj")[lo:hi].to(dev).float().transpose(1, 2))
                 dnb, dns = quantize_mxfp4(g(pe + "down_proj")[lo:hi].to(dev).float().transpose(1, 2))
             E_l = hi - lo
-            M.gu_blocks = hf_interleaved_to_grouped(gub.to(dev).reshape(E_l, gub.shape[1], -1)).contiguous()
-            M.gu_scales = hf_interleaved_to_grouped(gus.to(dev).reshape(E_l, gus.shape[1], -1)).contiguous()
+            M.gu_w, M.gu_exp = tile_mxfp4(hf_interleaved_to_grouped(gub.to(dev).reshape(E_l, gub.shape[1], -1)),
+                                hf_interleaved_to_grouped(gus.to(dev).reshape(E_l, gus.shape[1], -1)))
             M.gu_bias = hf_interleaved_to_grouped(dv(g(pe + "gate_up_proj_bias")[lo:hi]))
-            M.dn_blocks = dnb.to(dev).reshape(E_l, dnb.shape[1], -1).contiguous()
-            M.dn_scales = dns.to(dev).reshape(E_l, dns.shape[1], -1).contiguous()
+            M.dn_w, M.dn_exp = tile_mxfp4(dnb.to(dev), dns.to(dev).reshape(E_l, dns.shape[1], -1))
             M.dn_bias = dv(g(pe + "down_proj_bias")[lo:hi])  # each expert (and its bias) lives on one rank
             self.moe.append(M)
 
@@ -125,23 +133,24 @@ class MoEDecoderLM(DecoderLM):
         weights = torch.empty(T, k, dtype=torch.float32, device=dev)
         ext().moe_route(logits, k, not c.softmax_after_topk, c.norm_topk_prob, experts, weights)
         n = T * k
+        bt = token_tile(n, c.num_experts)
         meta = torch.empty(2 * E_l + 2, dtype=torch.int32, device=dev)
-        max_tiles = n // 128 + E_l + 1
-        tiles = torch.empty(max_tiles, dtype=torch.int32, device=dev)
+        max_tiles = n // bt + E_l + 1
+        tiles = torch.empty(4 * max_tiles, dtype=torch.int32, device=dev)
         perm = torch.empty(n, dtype=torch.int32, device=dev)
         inv = torch.empty(n, dtype=torch.int32, device=dev)
         cursor = torch.empty(E_l, dtype=torch.int32, device=dev)
-        ext().moe_align(experts, E_l, self.e_lo, E_l, meta, tiles, perm, inv, cursor)
-        a = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+        ext().moe_align(experts, E_l, self.e_lo, E_l, bt, meta, tiles, perm, inv, cursor)
+        a = torch.empty(n, H, dtype=torch.float16, device=dev)  # grouped GEMM operands are f16
         ext().moe_gather(x, perm, meta, E_l, k, a)
         I = c.moe_intermediate_size
         s = scratch(dev)
-        gu = torch.empty(n, I, dtype=torch.bfloat16, device=dev)
-        ext().moe_gemm(a, M.gu_blocks, M.gu_scales, M.gu_bias, None, perm, meta, tiles, gu, True,
-                       float(c.swiglu_limit or 1e30), float(c.swiglu_alpha), s.status)
+        gu = torch.empty(n, I, dtype=torch.float16, device=dev)
+        ext().moe_gemm(a, M.gu_w, M.gu_exp, 2 * I, M.gu_bias, None, perm, meta, tiles, gu, True,
+                       float(c.swiglu_limit or 1e30), float(c.swiglu_alpha), bt, s.status)
         dn = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
-        ext().moe_gemm(gu, M.dn_blocks, M.dn_scales, M.dn_bias, weights.view(-1), perm, meta, tiles, dn, False,
-                       0.0, 0.0, s.status)
+        ext().moe_gemm(gu, M.dn_w, M.dn_exp, H, M.dn_bias, weights.view(-1), perm, meta, tiles, dn, False,
+                       0.0, 0.0, bt, s.status)
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         ext().moe_combine(dn, inv, k, out, False)
         ops._count(7)

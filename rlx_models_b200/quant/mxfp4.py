@@ -55,3 +55,47 @@ def quantize_mxfp4(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
 def mxfp4_roundtrip(w: torch.Tensor) -> torch.Tensor:
     b, s = quantize_mxfp4(w)
     return dequantize_mxfp4(b, s)
+
+
+TILE_ROWS, TILE_K = 128, 64
+TILE_BYTES = TILE_ROWS * TILE_K // 2 + TILE_ROWS * TILE_K // GROUP  # 4096 code bytes + 256 scale bytes
+
+
+def tile_mxfp4(blocks: torch.Tensor, scales: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Grouped-GEMM weight layout: blocks [E, N, K/32, 16] (or [E, N, K/2]) and
+    scales [E, N, K/32] -> (tiles uint8 [E, ceil(N/128), K/64, 4352],
+    row_exp uint8 [E, ceil(N/128) * 128]).
+
+    Each (expert, 128-row tile, 64-wide k tile) is one contiguous block:
+    [2 k-halves][128 rows][16 code bytes] then [2 k-halves][128 rows] scale
+    offsets (a kernel thread owns one row and one half). A scale offset
+    is row_exp - s, with row_exp the largest E8M0 exponent of the weight row,
+    so the kernel multiplies codes by 2^-(offset) <= 1 and applies
+    2^(row_exp - 127) to the accumulator row. Rows past N are zero."""
+    E, N = blocks.shape[0], blocks.shape[1]
+    b = blocks.reshape(E, N, -1)
+    K = b.shape[2] * 2
+    assert K % TILE_K == 0 and scales.shape == (E, N, K // GROUP)
+    NT, KT = (N + TILE_ROWS - 1) // TILE_ROWS, K // TILE_K
+    pad = NT * TILE_ROWS - N
+    row_exp = scales.amax(-1)                                   # [E, N]
+    s = (row_exp[..., None] - scales).to(torch.uint8)           # offsets >= 0
+    if pad:
+        b = torch.cat([b, b.new_zeros(E, pad, b.shape[2])], 1)
+        s = torch.cat([s, s.new_zeros(E, pad, s.shape[2])], 1)
+        row_exp = torch.cat([row_exp, row_exp.new_zeros(E, pad)], 1)
+    # [E, NT, 128 rows, KT, 2 halves, 16 bytes] -> [E, NT, KT, half, row, 16]
+    bt = b.reshape(E, NT, TILE_ROWS, KT, 2, 16).permute(0, 1, 3, 4, 2, 5).reshape(E, NT, KT, TILE_ROWS * 32)
+    st = s.reshape(E, NT, TILE_ROWS, KT, 2).permute(0, 1, 3, 4, 2).reshape(E, NT, KT, TILE_ROWS * 2)
+    return torch.cat([bt, st], -1).contiguous(), row_exp.contiguous()
+
+
+def untile_mxfp4(t: torch.Tensor, row_exp: torch.Tensor, N: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """Inverse of ``tile_mxfp4``: -> (blocks [E, N, K/32, 16], scales [E, N, K/32])."""
+    E, NT, KT, _ = t.shape
+    b = t[..., :TILE_ROWS * 32].reshape(E, NT, KT, 2, TILE_ROWS, 16).permute(0, 1, 4, 2, 3, 5)
+    s = t[..., TILE_ROWS * 32:].reshape(E, NT, KT, 2, TILE_ROWS).permute(0, 1, 4, 2, 3)
+    b = b.reshape(E, NT * TILE_ROWS, KT * 32)[:, :N]
+    s = s.reshape(E, NT * TILE_ROWS, KT * 2)[:, :N]
+    s = (row_exp[:, :N, None].to(torch.int16) - s.to(torch.int16)).to(torch.uint8)
+    return b.reshape(E, N, KT * 2, 16).contiguous(), s.contiguous()

@@ -103,7 +103,7 @@ def init_tensor(spec: TensorSpec, seed: int, device="cpu", dtype: torch.dtype | 
     if spec.kind == "sinks":
         return torch.randn(spec.shape, generator=g, device=dev, dtype=torch.float32) * std
     if spec.kind == "mxfp4_blocks":
-        return torch.randint(0, 256, spec.shape, generator=g, device=dev, dtype=torch.int64).to(torch.uint8)
+        return torch.empty(spec.shape, dtype=torch.uint8, device=dev).random_(0, 256, generator=g)
     if spec.kind == "mxfp4_scales":
         # E8M0 exponents around 2^-8 give element magnitudes ~N(0, 0.02)-like
         return torch.randint(118, 121, spec.shape, generator=g, device=dev, dtype=torch.int64).to(torch.uint8)

@@ -231,3 +231,17 @@ def test_scheduler_stop_and_abort():
     _drive(s, bufs)
     assert s.output_tokens(a)[-1] == 6 and s.finish_reason(a) == 2
     assert s.finish_reason(b) == 3
+
+
+def test_mxfp4_tile_roundtrip():
+    from rlx_models_b200.quant.mxfp4 import quantize_mxfp4, tile_mxfp4, untile_mxfp4, dequantize_mxfp4
+    w = torch.randn(3, 200, 192) * torch.logspace(-3, 1, 200)[None, :, None]
+    b, s = quantize_mxfp4(w)
+    t, rexp = tile_mxfp4(b, s)
+    assert t.shape == (3, 2, 3, 4352) and rexp.shape == (3, 256)
+    b2, s2 = untile_mxfp4(t, rexp, 200)
+    assert torch.equal(b, b2) and torch.equal(s, s2)
+    # offsets are the distance below each row's largest exponent
+    offs = t[..., 4096:]
+    assert int(offs.max()) <= int((s.amax(-1, keepdim=True) - s).max())
+    assert torch.allclose(dequantize_mxfp4(b2, s2), dequantize_mxfp4(b, s))
