@@ -235,3 +235,71 @@ def tiny(model_type: str = "qwen3", **over) -> DecoderConfig:
         return dataclasses.replace(cfg, **base)
     base.update(over)
     return DecoderConfig(model_type=model_type, **base)
+
+
+# ---------------------------------------------------------------------------
+# FLUX.1 rectified-flow DiT (BFL checkpoint layout: double_blocks.* /
+# single_blocks.*), after rlx-flux1 src/config.rs:24-150
+# ---------------------------------------------------------------------------
+
+@dataclass
+class FluxConfig:
+    in_channels: int = 64          # 16 latent channels x 2x2 patch
+    out_channels: int = 64
+    vec_in_dim: int = 768          # CLIP pooled vector
+    context_in_dim: int = 4096     # T5 token embeddings
+    hidden_size: int = 3072
+    mlp_ratio: float = 4.0
+    num_heads: int = 24
+    depth: int = 19                # double-stream blocks
+    depth_single_blocks: int = 38
+    axes_dim: tuple = (16, 56, 56)
+    theta: float = 10000.0
+    qkv_bias: bool = True
+    guidance_embed: bool = True    # [dev]: distilled guidance input
+    eps: float = 1e-6
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_size // self.num_heads
+
+    @property
+    def mlp_hidden(self) -> int:
+        return int(self.hidden_size * self.mlp_ratio)
+
+    @classmethod
+    def from_shapes(cls, shape_of) -> "FluxConfig":
+        """Infer the config from checkpoint tensor shapes (``shape_of(name) -> tuple | None``)."""
+        img_in = shape_of("img_in.weight")
+        hidden, in_ch = img_in
+        head_dim = shape_of("double_blocks.0.img_attn.norm.query_norm.scale")[0]
+
+        def count(prefix):
+            n = 0
+            while shape_of(f"{prefix}.{n}.norm.key_norm.scale" if prefix == "single_blocks"
+                           else f"{prefix}.{n}.img_attn.norm.key_norm.scale") is not None:
+                n += 1
+            return n
+
+        return cls(in_channels=in_ch, out_channels=shape_of("final_layer.linear.weight")[0],
+                   vec_in_dim=shape_of("vector_in.in_layer.weight")[1],
+                   context_in_dim=shape_of("txt_in.weight")[1], hidden_size=hidden,
+                   mlp_ratio=shape_of("double_blocks.0.img_mlp.0.weight")[0] / hidden,
+                   num_heads=hidden // head_dim, depth=count("double_blocks"),
+                   depth_single_blocks=count("single_blocks"),
+                   guidance_embed=shape_of("guidance_in.in_layer.weight") is not None)
+
+
+def flux1_dev() -> FluxConfig:
+    return FluxConfig()
+
+
+def flux1_schnell() -> FluxConfig:
+    return FluxConfig(guidance_embed=False)
+
+
+def flux_tiny(**over) -> FluxConfig:
+    base = dict(in_channels=16, out_channels=16, vec_in_dim=32, context_in_dim=64, hidden_size=256,
+                num_heads=2, depth=2, depth_single_blocks=2, axes_dim=(16, 56, 56))
+    base.update(over)
+    return FluxConfig(**base)

@@ -303,7 +303,8 @@ __global__ void decode_merge_kernel(AttnArgs a, int nsplit) {
 }
 
 // ---------------------------------------------------------------------------
-// Prefill (causal, over cached pages): grid (B * q_tiles, Hkv), 8 compute
+// Prefill (causal over cached pages, or non-causal joint attention with
+// paged query rows for the DiT): grid (B * q_tiles, Hkv), 8 compute
 // warps (16 MMA rows each; row = token * G + head) + 1 TMA producer warp.
 // K/V tiles of 64 keys (4 pages) in an NST-deep ring.
 // ---------------------------------------------------------------------------
@@ -339,10 +340,11 @@ __global__ void __launch_bounds__(288) prefill_attn_kernel(const __grid_constant
   const int ctx = a.ctx_lens[b];
   const int pos_base = ctx - q_len;  // position of query 0
   const int pos_lo = pos_base + tok0, pos_hi = pos_base + tok0 + ntok - 1;
+  const bool causal = a.causal != 0;
   int k_begin = 0;
-  if (a.window > 0) k_begin = max(0, pos_lo - a.window + 1);
+  if (causal && a.window > 0) k_begin = max(0, pos_lo - a.window + 1);
   k_begin &= ~(Cf::TILE_KEYS - 1);
-  const int k_end = pos_hi + 1;
+  const int k_end = causal ? pos_hi + 1 : ctx;
   const int ntiles = (k_end - k_begin + Cf::TILE_KEYS - 1) / Cf::TILE_KEYS;
   const int32_t* btab = a.block_tables + (int64_t)b * a.max_blocks;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -400,6 +402,10 @@ __global__ void __launch_bounds__(288) prefill_attn_kernel(const __grid_constant
     r_ok[r] = r_tok[r] < ntok;
     r_pos[r] = pos_base + tok0 + r_tok[r];
   }
+  // query / output row of the sequence's token t
+  auto q_row = [&](int t) -> int64_t {
+    return a.q_paged ? (int64_t)btab[t >> 4] * 16 + (t & 15) : (int64_t)(q0 + t);
+  };
   uint32_t qa[D / 16][4];
   {
     const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q);
@@ -410,7 +416,7 @@ __global__ void __launch_bounds__(288) prefill_attn_kernel(const __grid_constant
         const int r = h & 1;
         const int c = ks * 16 + 2 * t4 + ((h & 2) ? 8 : 0);
         qa[ks][h] = r_ok[r] ? *reinterpret_cast<const uint32_t*>(
-                                  qb + ((int64_t)(q0 + tok0 + r_tok[r]) * a.Hq + hkv * G + r_head[r]) * D + c)
+                                  qb + (q_row(tok0 + r_tok[r]) * a.Hq + hkv * G + r_head[r]) * D + c)
                             : 0u;
       }
   }
@@ -449,7 +455,8 @@ __global__ void __launch_bounds__(288) prefill_attn_kernel(const __grid_constant
       for (int h = 0; h < 4; ++h) {
         const int r = h >> 1;
         const int kp = key0 + nt * 8 + 2 * t4 + (h & 1);
-        const bool ok = r_ok[r] && kp <= r_pos[r] && kp < ctx && (a.window <= 0 || kp > r_pos[r] - a.window);
+        const bool ok = r_ok[r] && kp < ctx &&
+                        (!causal || (kp <= r_pos[r] && (a.window <= 0 || kp > r_pos[r] - a.window)));
         sc[nt][h] = ok ? sc[nt][h] * scale_log2 : kNegInf;
         mx[r] = fmaxf(mx[r], sc[nt][h]);
       }
@@ -524,7 +531,7 @@ __global__ void __launch_bounds__(288) prefill_attn_kernel(const __grid_constant
       L = L * f + exp2f(sk - Mx);
     }
     const float inv = L > 0.f ? f / L : 0.f;
-    __nv_bfloat16* dst = ob + ((int64_t)(q0 + tok0 + r_tok[r]) * a.Hq + head) * D;
+    __nv_bfloat16* dst = ob + q_row(tok0 + r_tok[r]) * (a.out_ld ? a.out_ld : (int64_t)a.Hq * D) + (int64_t)head * D;
 #pragma unroll
     for (int dn = 0; dn < D / 8; ++dn) {
       const int c = dn * 8 + 2 * t4;

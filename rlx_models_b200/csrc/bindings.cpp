@@ -25,7 +25,8 @@ void check_cuda(const Tensor& t, const char* name) {
 
 void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const optional<Tensor>& residual,
             const optional<Tensor>& bias, double alpha, Tensor& ws, Tensor& sem, Tensor& status, int64_t swap,
-            int64_t bn, int64_t splits, const optional<Tensor>& trace) {
+            int64_t bn, int64_t splits, const optional<Tensor>& trace, int64_t act_from, const optional<Tensor>& gate,
+            int64_t gate_split, int64_t gate_r1, int64_t gate_r2) {
   check_cuda(x, "x");
   check_cuda(w, "w");
   check_cuda(out, "out");
@@ -77,6 +78,20 @@ void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const o
   a.device = x.get_device();
   if (trace.has_value() && trace->defined())
     a.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  if (act_from >= 0) {
+    a.act = 1;
+    a.act_from = (int)act_from;
+  }
+  if (gate.has_value() && gate->defined()) {
+    TORCH_CHECK(gate->scalar_type() == at::kBFloat16 && gate->dim() == 2 && gate->stride(1) == 1 &&
+                    gate->size(1) == N,
+                "b200.linear: gate [batches, N] bf16 with unit inner stride");
+    a.gate = gate->data_ptr();
+    a.gate_ld = gate->stride(0);
+    a.gate_split = (int)gate_split;
+    a.gate_r1 = (int)gate_r1;
+    a.gate_r2 = (int)gate_r2;
+  }
   b200::linear_launch(a, cur_stream(x));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -168,8 +183,10 @@ static b200::AttnArgs attn_args(const Tensor& q, const Tensor& k_cache, const Te
               "b200.attention: block_tables int32 [B, max_blocks]");
   TORCH_CHECK(ctx_lens.scalar_type() == at::kInt && ctx_lens.numel() == block_tables.size(0),
               "b200.attention: ctx_lens");
-  TORCH_CHECK(out.is_contiguous() && out.sizes() == q.sizes() && out.scalar_type() == at::kBFloat16,
-              "b200.attention: out");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 &&
+                  ((out.is_contiguous() && out.sizes() == q.sizes()) ||
+                   (out.dim() == 2 && out.size(0) == q.size(0) && out.stride(1) == 1)),
+              "b200.attention: out [Tq, Hq, D] (or a row-strided [Tq, Hq * D] view for prefill)");
   if (sinks.has_value() && sinks->defined())
     TORCH_CHECK(sinks->scalar_type() == at::kFloat && sinks->numel() == q.size(1), "b200.attention: sinks f32 [Hq]");
   b200::AttnArgs a{};
@@ -210,12 +227,19 @@ int64_t decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v
 
 void prefill_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& block_tables,
                        const Tensor& ctx_lens, const Tensor& cu_q, Tensor& out, const optional<Tensor>& sinks,
-                       int64_t window, double scale, int64_t max_q_len, Tensor& status) {
+                       int64_t window, double scale, int64_t max_q_len, Tensor& status, bool causal, bool q_paged) {
   c10::cuda::CUDAGuard g(q.device());
   auto a = attn_args(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, window, scale, status);
   TORCH_CHECK(cu_q.scalar_type() == at::kInt && cu_q.numel() == block_tables.size(0) + 1, "b200.prefill: cu_q");
   a.cu_q = cu_q.data_ptr<int32_t>();
   a.max_q_len = (int)max_q_len;
+  a.causal = causal ? 1 : 0;
+  a.q_paged = q_paged ? 1 : 0;
+  if (out.dim() == 2) {  // [rows, Hq * D] view with a row stride (DiT: a column slice of a wider buffer)
+    TORCH_CHECK(out.stride(1) == 1 && out.size(1) == a.Hq * a.D && out.stride(0) % 8 == 0,
+                "b200.prefill: 2-D out must be [rows, Hq * D] with unit inner stride");
+    a.out_ld = out.stride(0);
+  }
   b200::prefill_attention_launch(a, cur_stream(q));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -616,10 +640,61 @@ void moe_gemm(const Tensor& x, const Tensor& w, const Tensor& row_exp, int64_t N
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// x [rows, H] (row stride), mod [B, *] bf16: out = LN(x) * (1 + mod[b][scale_off:]) + mod[b][shift_off:]
+void ln_modulate(const Tensor& x, Tensor& out, const Tensor& mod, int64_t shift_off, int64_t scale_off, double eps,
+                 int64_t split, int64_t r1, int64_t r2) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16 &&
+                  mod.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1 &&
+                  mod.stride(1) == 1,
+              "b200.ln_modulate: bf16, unit inner stride");
+  const int64_t H = x.size(1);
+  TORCH_CHECK(out.size(0) == x.size(0) && out.size(1) == H && x.stride(0) % 8 == 0 && out.stride(0) % 8 == 0 &&
+                  mod.stride(0) % 8 == 0 && shift_off % 8 == 0 && scale_off % 8 == 0 &&
+                  shift_off + H <= mod.size(1) && scale_off + H <= mod.size(1),
+              "b200.ln_modulate: shapes / 16-byte alignment");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::ln_modulate_launch(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0), mod.data_ptr(), mod.stride(0),
+                           (int)shift_off, (int)scale_off, (int)x.size(0), (int)H, (float)eps, (int)split, (int)r1,
+                           (int)r2, cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// qkv [rows, 3 H] (row stride) -> q [rows, heads, 128], k/v pages [rows/16, heads, 16, 128]
+void dit_qk_rope(const Tensor& qkv, int64_t heads, const Tensor& scales_txt, const Tensor& scales_img,
+                 const Tensor& cos_t, const Tensor& sin_t, int64_t split, int64_t Lt, int64_t Li, double eps,
+                 Tensor& q_out, Tensor& k_pages, Tensor& v_pages) {
+  check_cuda(qkv, "qkv");
+  const int64_t rows = qkv.size(0);
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.stride(1) == 1 && qkv.size(1) >= 3 * heads * 128 &&
+                  qkv.stride(0) % 4 == 0,
+              "b200.dit_qk_rope: qkv [rows, 3 * heads * 128]");
+  TORCH_CHECK(rows % 16 == 0 && q_out.is_contiguous() && k_pages.is_contiguous() && v_pages.is_contiguous() &&
+                  q_out.numel() == rows * heads * 128 && k_pages.numel() == rows * heads * 128 &&
+                  v_pages.numel() == rows * heads * 128,
+              "b200.dit_qk_rope: outputs");
+  TORCH_CHECK(cos_t.scalar_type() == at::kFloat && sin_t.scalar_type() == at::kFloat && cos_t.is_contiguous() &&
+                  sin_t.is_contiguous() && cos_t.size(1) == 64 && cos_t.size(0) >= Lt + Li,
+              "b200.dit_qk_rope: f32 tables [Lt + Li, 64]");
+  TORCH_CHECK(scales_txt.numel() == 256 && scales_img.numel() == 256 && scales_txt.scalar_type() == at::kBFloat16 &&
+                  scales_img.scalar_type() == at::kBFloat16,
+              "b200.dit_qk_rope: scales [2, 128] bf16 (q, k)");
+  c10::cuda::CUDAGuard g(qkv.device());
+  b200::dit_qk_rope_launch(qkv.data_ptr(), qkv.stride(0), (int)rows, (int)heads, scales_txt.data_ptr(),
+                           scales_img.data_ptr(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), (int)split,
+                           (int)Lt, (int)Li, (float)eps, q_out.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(),
+                           cur_stream(qkv));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
-  m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none());
+  m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none(),
+        py::arg("act_from") = -1, py::arg("gate") = py::none(), py::arg("gate_split") = 0, py::arg("gate_r1") = 1,
+        py::arg("gate_r2") = 1);
   m.def("gemm", &gemm);
+  m.def("ln_modulate", &ln_modulate);
+  m.def("dit_qk_rope", &dit_qk_rope);
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);

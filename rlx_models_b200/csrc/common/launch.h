@@ -40,6 +40,12 @@ struct LinearArgs {
   unsigned* const* peer_flags = nullptr;
   int bcast = 0;  // one-shot: push rows to every rank's slot `my_rank`
   unsigned long long* trace = nullptr;  // debug timeline
+  // adaLN DiT epilogues (normal orientation): GELU-tanh on columns >= act_from;
+  // y *= gate[batch(row)][col] before the residual (batch(row) as in gemm::Params)
+  int act = 0, act_from = 0;
+  const void* gate = nullptr;
+  int64_t gate_ld = 0;
+  int gate_split = 0, gate_r1 = 1, gate_r2 = 1;
 };
 void linear_launch(const LinearArgs& a, cudaStream_t st);
 
@@ -157,6 +163,9 @@ struct AttnArgs {
   float scale;
   int max_q_len;             // prefill: max query length per sequence
   int splits;                // decode: KV splits (0 = auto)
+  int causal = 1;            // prefill: 0 = every query sees the whole context (DiT joint attention)
+  int q_paged = 0;           // prefill: query / output row of token t = block_tables[b][t / 16] * 16 + t % 16
+  int64_t out_ld = 0;        // prefill: output row stride in elements (0 = Hq * D)
   float* ws;                 // decode split workspace
   int64_t ws_elems;
   int* status;
@@ -203,6 +212,14 @@ struct MoeGemmArgs {
   int device;
 };
 void moe_gemm_launch(const MoeGemmArgs& a, cudaStream_t st);
+
+// ---------------- DiT (FLUX) ----------------
+void ln_modulate_launch(const void* x, int64_t ldx, void* out, int64_t ldo, const void* mod, int64_t ld_mod,
+                        int shift_off, int scale_off, int rows, int H, float eps, int split, int r1, int r2,
+                        cudaStream_t st);
+void dit_qk_rope_launch(const void* qkv, int64_t ld, int rows, int heads, const void* scales_txt,
+                        const void* scales_img, const float* cos_t, const float* sin_t, int split, int Lt, int Li,
+                        float eps, void* q_out, void* k_pages, void* v_pages, cudaStream_t st);
 
 // ---------------- sampling ----------------
 void argmax_launch(const float* logits, int64_t ld, int64_t B, int64_t V, int32_t* out, cudaStream_t st);

@@ -56,7 +56,8 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
   const int epi = a.mode;
   if (M == 0 || N == 0) return;
   const int sms = num_sms(a.device);
-  const bool sw = a.swap < 0 ? (M <= 128 && N >= 256) : (a.swap == 1);
+  const bool dit_epi = a.act != 0 || a.gate != nullptr;
+  const bool sw = dit_epi ? false : (a.swap < 0 ? (M <= 128 && N >= 256) : (a.swap == 1));
 
   gemm::Params p{};
   const void* A = sw ? a.w : a.x;
@@ -97,6 +98,7 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
   }
   sp = std::max(1, std::min(sp, p.k_tiles));
   if (sp > 1 && epi != gemm::EPI_ACC && (int64_t)tiles * gemm::kBM * BN > a.ws_elems) sp = 1;
+  if (dit_epi) sp = 1;  // the activation / gate must see the full sum
   p.kt_per_split = (p.k_tiles + sp - 1) / sp;
   p.splits = (p.k_tiles + p.kt_per_split - 1) / p.kt_per_split;
   p.num_units = tiles * p.splits;
@@ -132,6 +134,15 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
   p.bcast = a.bcast;
   if (p.bcast && !sw) throw std::runtime_error("b200.linear: broadcast push needs the swap-AB (decode) path");
   p.trace = a.trace;
+  p.act = a.act;
+  p.act_from = a.act_from;
+  p.gate = reinterpret_cast<const __nv_bfloat16*>(a.gate);
+  p.gate_ld = a.gate_ld;
+  p.gate_split = a.gate_split;
+  p.gate_r1 = std::max(1, a.gate_r1);
+  p.gate_r2 = std::max(1, a.gate_r2);
+  if (dit_epi && (epi != gemm::EPI_BF16 || p.splits > 1))
+    throw std::runtime_error("b200.linear: GELU / gate epilogues need bf16 output without split-K");
   if (p.peer_out != nullptr && (p.rpr <= 0 || p.done_ctr == nullptr || p.peer_flags == nullptr || p.epoch == nullptr))
     throw std::runtime_error("b200.linear: incomplete push-mode arguments");
 

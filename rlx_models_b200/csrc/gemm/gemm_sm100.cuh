@@ -69,7 +69,23 @@ struct Params {
   unsigned* const* peer_flags;
   int bcast;  // push every output row to all ranks (one-shot all-reduce slots) instead of its owner
   unsigned long long* trace;  // optional per-CTA timeline ([grid][16] globaltimer ns), debug only
+  // Normal orientation only (adaLN DiT blocks):
+  //   act = 1: GELU (tanh form) on output columns j >= act_from, after the bias;
+  //   gate != null: y = gate[batch(i)][j] * y before the residual is added, with
+  //   batch(i) = i < gate_split ? i / gate_r1 : (i - gate_split) / gate_r2.
+  int act, act_from;
+  const __nv_bfloat16* gate;
+  int64_t gate_ld;
+  int gate_split, gate_r1, gate_r2;
 };
+
+__device__ __forceinline__ float gelu_tanh(float x) {
+  // 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), tanh from the SFU
+  const float u = 0.7978845608028654f * (x + 0.044715f * x * x * x);
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return 0.5f * x * (1.f + t);
+}
 
 // Base pointer of output row `t` (a token index), local or pushed to its owner.
 template <typename T>
@@ -127,6 +143,31 @@ __device__ __forceinline__ void store_chunk(const Params& p, int i, int j0, floa
       if (j0 + t < p.NB) v[t] += __bfloat162float(p.bias[j0 + t]);
   }
   const bool full = (j0 + 32 <= p.NB);
+  if (p.act == 1 && j0 + 32 > p.act_from) {
+#pragma unroll
+    for (int t = 0; t < 32; ++t)
+      if (j0 + t >= p.act_from) v[t] = gelu_tanh(v[t]);
+  }
+  if (p.gate != nullptr) {
+    const int gb = i < p.gate_split ? i / p.gate_r1 : (i - p.gate_split) / p.gate_r2;
+    const __nv_bfloat16* g = p.gate + (int64_t)gb * p.gate_ld;
+    if (full && ((reinterpret_cast<uintptr_t>(g + j0) & 15u) == 0)) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 w = *reinterpret_cast<const uint4*>(g + j0 + q * 8);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[q * 8 + 2 * h] *= bf16_lo(ww[h]);
+          v[q * 8 + 2 * h + 1] *= bf16_hi(ww[h]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        if (j0 + t < p.NB) v[t] *= __bfloat162float(g[j0 + t]);
+    }
+  }
   if (p.R != nullptr) {
     const __nv_bfloat16* r = p.R + (int64_t)i * p.ldr_i;
     if (p.ldr_j == 1 && full && ((reinterpret_cast<uintptr_t>(r + j0) & 15u) == 0)) {

@@ -25,10 +25,15 @@ SWIGLU_GROUP = 64  # gate/up rows interleaved in groups of 64 for the fused epil
 def linear(x: torch.Tensor, w: torch.Tensor, *, out: torch.Tensor | None = None,
            residual: torch.Tensor | None = None, bias: torch.Tensor | None = None,
            alpha: float = 1.0, out_dtype: torch.dtype = torch.bfloat16,
-           swap: int = -1, bn: int = 0, splits: int = 0) -> torch.Tensor:
+           swap: int = -1, bn: int = 0, splits: int = 0, gelu_from: int = -1,
+           gate: torch.Tensor | None = None, gate_rows: tuple = (0, 1, 1)) -> torch.Tensor:
     """``out = alpha * x @ w.T (+ bias) (+ residual)`` on the tcgen05 GEMM.
 
     x: [M, K] bf16, w: [N, K] bf16 (nn.Linear layout). ``out_dtype`` bf16 or f32.
+    DiT epilogues: ``gelu_from`` >= 0 applies GELU (tanh) to output columns
+    >= gelu_from; ``gate`` [batches, N] multiplies the (biased) product before
+    the residual add, row i using gate row ``i // r1`` below ``split`` and
+    ``(i - split) // r2`` above, with ``gate_rows = (split, r1, r2)``.
     """
     M, N = x.shape[0], w.shape[0]
     if out is None:
@@ -37,7 +42,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, out: torch.Tensor | None = None,
     mode = 1 if out.dtype == torch.float32 else 0
     _count(1)
     ext().linear(x, w, out, mode, residual, bias, float(alpha), s.gemm_ws, s.gemm_sem, s.status,
-                 swap, bn, splits)
+                 swap, bn, splits, None, int(gelu_from), gate, int(gate_rows[0]), int(gate_rows[1]),
+                 int(gate_rows[2]))
     return out
 
 
@@ -212,13 +218,16 @@ def decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, *, scale, sink
 
 
 def prefill_attention(q, k_cache, v_cache, block_tables, ctx_lens, cu_q, max_q_len, *, scale, sinks=None,
-                      window=0, out=None):
+                      window=0, out=None, causal=True, q_paged=False):
+    """Causal prefill over paged K/V; ``causal=False`` lets every query see the
+    whole context (DiT joint attention) and ``q_paged`` places query/output rows
+    through the same block table as the keys (row = table[t // 16] * 16 + t % 16)."""
     if out is None:
         out = torch.empty_like(q)
     s = scratch(q.device)
     _count(1)
     ext().prefill_attention(q, k_cache, v_cache, block_tables, ctx_lens, cu_q, out, sinks, int(window),
-                            float(scale), int(max_q_len), s.status)
+                            float(scale), int(max_q_len), s.status, bool(causal), bool(q_paged))
     return out
 
 

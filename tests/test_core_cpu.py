@@ -245,3 +245,34 @@ def test_mxfp4_tile_roundtrip():
     offs = t[..., 4096:]
     assert int(offs.max()) <= int((s.amax(-1, keepdim=True) - s).max())
     assert torch.allclose(dequantize_mxfp4(b2, s2), dequantize_mxfp4(b, s))
+
+
+def test_flux_oracle_deinterleaved_rope_matches():
+    """Half-split RoPE on de-interleaved q/k rows == BFL interleaved-pair RoPE."""
+    from rlx_models_b200.config import flux_tiny
+    from rlx_models_b200.models.flux_common import (apply_rope_interleaved, deinterleave_perm, position_ids,
+                                                     rope_tables)
+    D = 128
+    ids = position_ids(4, 3, 5)
+    cos, sin = rope_tables(ids)
+    q = torch.randn(2, 3, ids.shape[0], D, dtype=torch.float64)
+    k = torch.randn(2, 3, ids.shape[0], D, dtype=torch.float64)
+    ref = apply_rope_interleaved(q, cos.double(), sin.double()) @ apply_rope_interleaved(k, cos.double(), sin.double()).transpose(-1, -2)
+    p = deinterleave_perm(D)
+
+    def half(x):
+        x1, x2 = x[..., :D // 2], x[..., D // 2:]
+        c, s = cos.double(), sin.double()
+        return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], -1)
+
+    got = half(q[..., p]) @ half(k[..., p]).transpose(-1, -2)
+    assert torch.allclose(got, ref, atol=1e-9)
+
+
+def test_flux_schedule_and_pack():
+    from rlx_models_b200.models.flux_common import pack, schedule, unpack
+    ts = schedule(28, 4096)
+    assert ts[0] == 1.0 and ts[-1] == 0.0 and all(a > b for a, b in zip(ts, ts[1:]))
+    x = torch.randn(2, 16, 8, 6)
+    assert torch.equal(unpack(pack(x), 16, 8, 6), x)
+    assert schedule(4, 4096, shift=False) == [1.0, 0.75, 0.5, 0.25, 0.0]

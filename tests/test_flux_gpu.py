@@ -1,0 +1,82 @@
+"""FLUX.1 DiT on the GPU against the fp32 oracle (tiny config), plus the
+DiT-specific kernels (LayerNorm+modulate, QK-norm + 3-axis RoPE, gated /
+GELU GEMM epilogues, non-causal paged attention)."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from rlx_models_b200 import ops
+from rlx_models_b200.config import flux_tiny
+from rlx_models_b200.models.flux import FluxDiT, generate_latents
+from rlx_models_b200.models.flux_common import flux_random_weights, position_ids
+from rlx_models_b200.models.flux_oracle import FluxOracle
+from rlx_models_b200.ops._ext import ext
+
+pytestmark = pytest.mark.gpu
+
+
+def rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-9)).item()
+
+
+def test_ln_modulate(cuda):
+    R, H, B = 96, 512, 3
+    x = torch.randn(R, H, device=cuda).bfloat16()
+    mod = (torch.randn(B, 4 * H, device=cuda) * 0.3).bfloat16()
+    out = torch.empty_like(x)
+    split, r1, r2 = 30, 10, 22  # rows < 30: batch row // 10; else (row - 30) // 22
+    ext().ln_modulate(x, out, mod, H, 2 * H, 1e-6, split, r1, r2)
+    b = torch.tensor([r // r1 if r < split else (r - split) // r2 for r in range(R)], device=cuda)
+    ref = F.layer_norm(x.float(), (H,), eps=1e-6) * (1 + mod[b, 2 * H:3 * H].float()) + mod[b, H:2 * H].float()
+    assert rel(out, ref) < 1e-2
+
+
+def test_linear_gate_gelu(cuda):
+    M, N, K, B = 256, 384, 512, 2
+    x = torch.randn(M, K, device=cuda).bfloat16()
+    w = (torch.randn(N, K, device=cuda) * 0.05).bfloat16()
+    bias = (torch.randn(N, device=cuda) * 0.1).bfloat16()
+    res = torch.randn(M, N, device=cuda).bfloat16()
+    gate = torch.randn(B, N, device=cuda).bfloat16()
+    y = ops.linear(x, w, bias=bias, residual=res, gate=gate, gate_rows=(0, 1, M // B))
+    ref = res.float() + gate.float().repeat_interleave(M // B, 0) * (x.float() @ w.float().T + bias.float())
+    assert rel(y, ref) < 1e-2
+    y2 = ops.linear(x, w, bias=bias, gelu_from=128)
+    lin = x.float() @ w.float().T + bias.float()
+    ref2 = torch.cat([lin[:, :128], F.gelu(lin[:, 128:], approximate="tanh")], 1)
+    assert rel(y2, ref2) < 1e-2
+
+
+def test_flux_dit_vs_oracle(cuda):
+    cfg = flux_tiny()
+    w = flux_random_weights(cfg, seed=0, bias_std=0.02)
+    B, Lt, h, wd = 2, 16, 4, 8
+    Li = h * wd
+    g = torch.Generator().manual_seed(1)
+    img = torch.randn(B, Li, cfg.in_channels, generator=g)
+    txt = torch.randn(B, Lt, cfg.context_in_dim, generator=g)
+    y = torch.randn(B, cfg.vec_in_dim, generator=g)
+    t = torch.tensor([0.8, 0.3])
+    gd = torch.tensor([3.5, 2.0])
+    ids = position_ids(Lt, h, wd)
+    ref = FluxOracle(cfg, w).forward(img, ids[Lt:], txt, ids[:Lt], t, y, gd)
+    model = FluxDiT(cfg, w, device=cuda)
+    out = model.forward(img.to(cuda).bfloat16(), txt.to(cuda).bfloat16(), t, y.to(cuda).bfloat16(), gd, h, wd,
+                        graph=False).clone()
+    torch.cuda.synchronize()
+    ops.check_errors(cuda)
+    assert rel(out.cpu(), ref) < 3e-2, rel(out.cpu(), ref)
+    out_g = model.forward(img.to(cuda).bfloat16(), txt.to(cuda).bfloat16(), t, y.to(cuda).bfloat16(), gd, h, wd)
+    torch.cuda.synchronize()
+    assert torch.equal(out_g, out)
+
+
+def test_flux_generate_runs(cuda):
+    cfg = flux_tiny()
+    model = FluxDiT(cfg, flux_random_weights(cfg, seed=0), device=cuda)
+    txt = torch.randn(2, 16, cfg.context_in_dim, device=cuda).bfloat16()
+    pooled = torch.randn(2, cfg.vec_in_dim, device=cuda).bfloat16()
+    lat = generate_latents(model, txt, pooled, height=64, width=64, steps=4)
+    assert lat.shape == (2, 4, 8, 8) and torch.isfinite(lat).all()
