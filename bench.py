@@ -3,6 +3,7 @@
     python bench.py --gpus N --steps K --warmup W           # serving, TP=N
     python bench.py --workload train --gpus N ...           # Qwen3-1.7B FSDP fine-tune step
     python bench.py --workload moe --gpus N ...             # gpt-oss-120b serving, EP=N
+    python bench.py --workload flux ...                     # FLUX.1-dev DiT, batch 4, 28 steps
     python bench.py --impl reference ...                    # the reference arm
 
 Serving workload: 64 concurrent requests, prompt lengths
@@ -198,7 +199,7 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="serve", choices=["serve", "moe", "train"])
+    ap.add_argument("--workload", default="serve", choices=["serve", "moe", "train", "flux"])
     ap.add_argument("--num-requests", type=int, default=None)
     ap.add_argument("--min-prompt", type=int, default=None)
     ap.add_argument("--max-prompt", type=int, default=None)
@@ -212,6 +213,9 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         return reference_arm(args)
+    if args.workload == "flux":
+        from rlx_models_b200.bench.bench_flux import bench_flux
+        return bench_flux(args)
     if args.workload == "train":
         from rlx_models_b200.train.bench_train import bench_train
         return bench_train(args)

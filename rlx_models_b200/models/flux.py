@@ -225,10 +225,14 @@ class FluxDiT:
                 self._forward_static()  # warm-up (lazy allocations, attribute setup)
             torch.cuda.current_stream(self.device).wait_stream(s)
             g = torch.cuda.CUDAGraph()
+            n0 = ops.launch_count()
             with torch.cuda.graph(g):
                 self._forward_static()
+            self._graph_launches = ops.launch_count() - n0
+            ops._count(-self._graph_launches)  # capture does not execute; replays are counted
             self._graph = g
         self._graph.replay()
+        ops._count(self._graph_launches)
         return S["vel"].view(B, Li, -1)
 
 
