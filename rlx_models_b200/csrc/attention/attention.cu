@@ -588,6 +588,10 @@ int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
 void prefill_attention_launch(const AttnArgs& a, cudaStream_t st) {
   using namespace attn;
   if (a.B == 0) return;
+  if (fmha_supported(a)) {
+    fmha_launch(a, st);
+    return;
+  }
   const int G = a.Hq / a.Hkv;
   if (a.Hq % a.Hkv != 0 || 128 % G != 0) throw std::runtime_error("b200.prefill_attention: G must divide 128");
   if (a.D != 128 && a.D != 64) throw std::runtime_error("b200.prefill_attention: D must be 64 or 128");

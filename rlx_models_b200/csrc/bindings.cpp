@@ -235,6 +235,7 @@ void prefill_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_c
   a.max_q_len = (int)max_q_len;
   a.causal = causal ? 1 : 0;
   a.q_paged = q_paged ? 1 : 0;
+  a.q_rows = q.size(0);
   if (out.dim() == 2) {  // [rows, Hq * D] view with a row stride (DiT: a column slice of a wider buffer)
     TORCH_CHECK(out.stride(1) == 1 && out.size(1) == a.Hq * a.D && out.stride(0) % 8 == 0,
                 "b200.prefill: 2-D out must be [rows, Hq * D] with unit inner stride");

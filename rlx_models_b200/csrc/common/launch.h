@@ -166,6 +166,7 @@ struct AttnArgs {
   int causal = 1;            // prefill: 0 = every query sees the whole context (DiT joint attention)
   int q_paged = 0;           // prefill: query / output row of token t = block_tables[b][t / 16] * 16 + t % 16
   int64_t out_ld = 0;        // prefill: output row stride in elements (0 = Hq * D)
+  int64_t q_rows = 0;        // prefill: rows of q (bounds of its TMA map)
   float* ws;                 // decode split workspace
   int64_t ws_elems;
   int* status;
@@ -173,6 +174,10 @@ struct AttnArgs {
 };
 int decode_attention_launch(const AttnArgs& a, cudaStream_t st);  // returns #launches
 void prefill_attention_launch(const AttnArgs& a, cudaStream_t st);
+// tcgen05 flash attention (head_dim 128, G <= 8 query heads per kv head); used by
+// prefill_attention_launch when supported (B200_ATTN_LEGACY=1 forces the mma.sync kernel)
+bool fmha_supported(const AttnArgs& a);
+void fmha_launch(const AttnArgs& a, cudaStream_t st);
 
 // ---------------- training ----------------
 void adamw_launch(float* master, const void* grad, bool grad_f32, float* m, float* v, void* param_out, int64_t n,

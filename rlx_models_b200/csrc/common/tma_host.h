@@ -53,6 +53,26 @@ inline CUtensorMap make_tmap_2d(const void* base, CUtensorMapDataType dtype, int
   return m;
 }
 
+// 3-D tiled map over [d2][d1][d0] (d0 contiguous; strides in elements for d1
+// and d2) with box [b2][b1][b0] and 128-byte swizzle.
+inline CUtensorMap make_tmap_3d(const void* base, CUtensorMapDataType dtype, int elem_bytes, uint64_t d0, uint64_t d1,
+                                uint64_t d2, uint64_t stride1_elems, uint64_t stride2_elems, uint32_t b0, uint32_t b1,
+                                uint32_t b2, CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) throw std::runtime_error("b200: TMA base not 16B aligned");
+  if ((stride1_elems * elem_bytes) % 16 != 0 || (stride2_elems * elem_bytes) % 16 != 0)
+    throw std::runtime_error("b200: TMA strides not 16B multiples");
+  CUtensorMap m;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_elems * (uint64_t)elem_bytes, stride2_elems * (uint64_t)elem_bytes};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = get_encode_tiled()(&m, dtype, 3, const_cast<void*>(base), dims, strides, box, estr,
+                                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("b200: cuTensorMapEncodeTiled (3d) failed: " + std::to_string((int)r));
+  return m;
+}
+
 inline int num_sms(int device) {
   static int cache[64] = {0};
   if (device < 0 || device >= 64) device = 0;

@@ -256,3 +256,29 @@ def test_matmul_training_majors(cuda, M, N, K):
     ops.matmul(dy.t(), x, out=dw, accumulate=True)
     assert rel_err(dw, 2 * (dy.float().T @ x.float())) < 5e-3
     ops.check_errors(cuda)
+
+
+@pytest.mark.parametrize("qscale,causal", [(0.5, False), (3.0, False), (3.0, True)])
+def test_attention_noncausal_paged_rescale(cuda, qscale, causal):
+    """Joint (non-causal) attention with query rows through the page table, and
+    score ranges large enough that the running max grows by > 2^8 mid-row
+    (lazy O rescale in the tcgen05 kernel; rows of a warp disagree)."""
+    B, L, H, D = 2, 640, 2, 128
+    nb = B * L // 16
+    g = torch.Generator(device=cuda).manual_seed(5)
+    q = (torch.randn(B * L, H, D, device=cuda, generator=g) * qscale).bfloat16()
+    k = (torch.randn(nb, H, 16, D, device=cuda, generator=g) * qscale).bfloat16()
+    v = torch.randn(nb, H, 16, D, device=cuda, generator=g).bfloat16()
+    # batch b's pages interleaved with the other batch's: a non-identity table
+    bt = torch.arange(nb, dtype=torch.int32, device=cuda).view(L // 16, B).t().contiguous()
+    ctx = torch.full((B,), L, dtype=torch.int32, device=cuda)
+    cu = (torch.arange(B + 1, dtype=torch.int32) * L).to(cuda)
+    out = ops.prefill_attention(q, k, v, bt, ctx, cu, L, scale=1 / math.sqrt(D), causal=causal, q_paged=True)
+    ops.check_errors(cuda)
+    for b in range(B):
+        rows = (bt[b].long()[:, None] * 16 + torch.arange(16, device=cuda)[None]).reshape(-1)
+        kk = ref.gather_paged(k, bt[b], L)
+        vv = ref.gather_paged(v, bt[b], L)
+        pos = torch.arange(L, device=cuda)
+        r = ref.attention(q[rows], kk, vv, pos, pos, 1 / math.sqrt(D), causal=causal)
+        assert rel_err(out[rows], r) < 2e-2, b
