@@ -44,6 +44,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--json", default=None)
     ap.add_argument("--reps", type=int, default=5)
+    ap.add_argument("--only", default=None, help="run one case (name prefix) --iters times without timing (for ncu)")
+    ap.add_argument("--iters", type=int, default=2)
     args = ap.parse_args()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -56,6 +58,15 @@ def main():
         case("qwen3_8b_prefill_b8_l2048_g4", 8, 2048, 32, 8, 128, True, False, dev),
         case("gpt_oss_prefill_b4_l1024_d64", 4, 1024, 64, 8, 64, True, False, dev),
     ]:
+        if args.only:
+            if not name.startswith(args.only):
+                continue
+            for _ in range(args.iters):
+                fn()
+            torch.cuda.synchronize()
+            ops.check_errors(dev)
+            print("ran", name)
+            continue
         t = timer(fn, reps=args.reps)
         r = {"case": name, "kernel": kernel, "us": round(t * 1e6, 1), "tflops": round(flops / t / 1e12, 1),
              "frac_of_bf16_peak": round(flops / t / 1e12 / tf, 3)}

@@ -688,12 +688,22 @@ void dit_qk_rope(const Tensor& qkv, int64_t heads, const Tensor& scales_txt, con
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void flag_wait_probe(const Tensor& flag, int64_t target, Tensor& status, Tensor& ok) {
+  check_cuda(flag, "flag");
+  TORCH_CHECK(flag.scalar_type() == at::kInt && ok.scalar_type() == at::kInt, "b200.flag_wait_probe: int32");
+  c10::cuda::CUDAGuard g(flag.device());
+  b200::flag_wait_probe_launch(reinterpret_cast<const unsigned*>(flag.data_ptr<int32_t>()), (unsigned)target,
+                               status.data_ptr<int>(), ok.data_ptr<int32_t>(), cur_stream(flag));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
   m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none(),
         py::arg("act_from") = -1, py::arg("gate") = py::none(), py::arg("gate_split") = 0, py::arg("gate_r1") = 1,
         py::arg("gate_r2") = 1);
   m.def("gemm", &gemm);
+  m.def("flag_wait_probe", &flag_wait_probe);
   m.def("ln_modulate", &ln_modulate);
   m.def("dit_qk_rope", &dit_qk_rope);
   m.def("moe_route", &moe_route);

@@ -256,3 +256,19 @@ void os_reduce_norm_launch(const OsReduceArgs& a, cudaStream_t st) {
 }
 
 }  // namespace b200
+
+namespace b200 {
+namespace {
+// Failure-path probe: one bounded wait on a flag. A flag that nothing sets
+// makes the wait run out (kWaitTimeoutNs), record kErrTimeoutPeer with
+// detail kErrTimeoutTest in the status word and return, leaving the context
+// usable; tests use it to check the host-side error reporting.
+__global__ void flag_wait_probe_kernel(const unsigned* flag, unsigned target, int* status, int* ok) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *ok = wait_flag_geq(flag, target, status, kErrTimeoutTest) ? 1 : 0;
+}
+}  // namespace
+
+void flag_wait_probe_launch(const unsigned* flag, unsigned target, int* status, int* ok, cudaStream_t st) {
+  flag_wait_probe_kernel<<<1, 32, 0, st>>>(flag, target, status, ok);
+}
+}  // namespace b200

@@ -218,6 +218,9 @@ struct MoeGemmArgs {
 };
 void moe_gemm_launch(const MoeGemmArgs& a, cudaStream_t st);
 
+// bounded flag wait that reports a timeout in the status word (failure-path tests)
+void flag_wait_probe_launch(const unsigned* flag, unsigned target, int* status, int* ok, cudaStream_t st);
+
 // ---------------- DiT (FLUX) ----------------
 void ln_modulate_launch(const void* x, int64_t ldx, void* out, int64_t ldo, const void* mod, int64_t ld_mod,
                         int shift_off, int scale_off, int rows, int H, float eps, int split, int r1, int r2,
