@@ -1,0 +1,148 @@
+"""Command line: ``python -m rlx_models_b200 <command>``.
+
+    inspect PATH                  config + tensor table of a checkpoint directory (no GPU)
+    run --model M --prompt TEXT   load and generate (greedy unless --temperature)
+    serve --model M [--port P]    OpenAI-compatible HTTP server
+    bench [bench.py args]         the repository benchmark
+    train --model M --data F      fine-tune on a JSONL dataset (train.data)
+
+``M`` is a checkpoint directory, an HF id in the offline cache (``org/name``,
+optionally ``org/name:QUANT@rev``) or a named shape (``qwen3-0.6b``, ...).
+
+Reference: rlx-cli (`rlx-inspect`), the per-family ``bin/`` runners and
+rlx-serve's server binary.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+
+def cmd_inspect(a):
+    from .config import DecoderConfig
+    from .weights.safetensors_io import Checkpoint
+    path = a.path
+    out = {}
+    cfgp = os.path.join(path, "config.json")
+    if os.path.exists(cfgp):
+        with open(cfgp) as f:
+            raw = json.load(f)
+        out["model_type"] = raw.get("model_type")
+        try:
+            c = DecoderConfig.from_hf_dict(raw)
+            out["config"] = {k: getattr(c, k) for k in ("hidden_size", "num_hidden_layers", "num_attention_heads",
+                                                        "num_key_value_heads", "head_dim", "intermediate_size",
+                                                        "vocab_size", "num_experts")}
+        except Exception as e:  # non-decoder configs
+            out["config_error"] = str(e)
+    ck = Checkpoint(path)
+    names = sorted(ck.keys())
+    total = 0
+    rows = []
+    for n in names:
+        dtype, shape = ck.info(n)
+        cnt = 1
+        for s in shape:
+            cnt *= s
+        total += cnt
+        rows.append((n, dtype, list(shape)))
+    out["tensors"] = len(names)
+    out["parameters"] = total
+    print(json.dumps(out, indent=1, default=str))
+    if a.tensors:
+        for n, d, s in rows[:a.limit]:
+            print(f"{n:70s} {str(d):10s} {s}")
+    return 0
+
+
+def cmd_run(a):
+    from .api import load
+    from .runtime.engine import EngineConfig, SamplingParams
+    llm = load(a.model, engine_config=EngineConfig(max_num_seqs=8, max_model_len=a.max_model_len,
+                                                   kv_memory_gb=a.kv_gb))
+    tok = llm.tokenizer
+    if a.ids:
+        ids = [int(x) for x in a.ids.split(",")]
+    else:
+        from .tokenizer import ByteTokenizer
+        tok = tok or ByteTokenizer()
+        ids = tok.encode(a.prompt)
+    sp = SamplingParams(max_new_tokens=a.max_tokens, temperature=a.temperature, top_p=a.top_p, top_k=a.top_k,
+                        seed=a.seed, ignore_eos=a.ignore_eos)
+    out = llm.generate([ids], sp)[0]
+    res = {"token_ids": out.token_ids, "finish_reason": out.finish_reason, "ttft_ms": round(out.ttft * 1e3, 2),
+           "tpot_ms": round(out.tpot * 1e3, 3)}
+    if tok is not None:
+        res["text"] = tok.decode(out.token_ids)
+    print(json.dumps(res))
+    return 0
+
+
+def cmd_serve(a):
+    from .api import load
+    from .runtime.engine import EngineConfig
+    from .serve.openai_server import serve
+    llm = load(a.model, engine_config=EngineConfig(max_num_seqs=a.max_num_seqs, max_model_len=a.max_model_len,
+                                                   kv_memory_gb=a.kv_gb))
+    serve(llm, a.host, a.port, model_name=a.model)
+    return 0
+
+
+def cmd_bench(rest):
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    sys.argv = ["bench.py"] + rest
+    import bench
+    return bench.main()
+
+
+def cmd_train(a):
+    from .train.data import train_from_jsonl
+    return train_from_jsonl(a)
+
+
+def main(argv=None):
+    argv = list(sys.argv[1:] if argv is None else argv)
+    if argv and argv[0] == "bench":
+        return cmd_bench(argv[1:])
+    ap = argparse.ArgumentParser(prog="python -m rlx_models_b200")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    p = sub.add_parser("inspect")
+    p.add_argument("path")
+    p.add_argument("--tensors", action="store_true")
+    p.add_argument("--limit", type=int, default=100000)
+    for name in ("run", "serve"):
+        p = sub.add_parser(name)
+        p.add_argument("--model", required=True)
+        p.add_argument("--max-model-len", type=int, default=4096)
+        p.add_argument("--kv-gb", type=float, default=8.0)
+        if name == "run":
+            p.add_argument("--prompt", default="Hello")
+            p.add_argument("--ids", default=None, help="comma-separated token ids instead of --prompt")
+            p.add_argument("--max-tokens", type=int, default=32)
+            p.add_argument("--temperature", type=float, default=0.0)
+            p.add_argument("--top-p", type=float, default=1.0)
+            p.add_argument("--top-k", type=int, default=0)
+            p.add_argument("--seed", type=int, default=0)
+            p.add_argument("--ignore-eos", action="store_true")
+        else:
+            p.add_argument("--host", default="127.0.0.1")
+            p.add_argument("--port", type=int, default=8000)
+            p.add_argument("--max-num-seqs", type=int, default=64)
+    p = sub.add_parser("train")
+    p.add_argument("--model", required=True)
+    p.add_argument("--data", required=True, help="JSONL with 'text', 'prompt'/'completion' or 'input_ids'")
+    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--seq-len", type=int, default=2048)
+    p.add_argument("--batch", type=int, default=8)
+    p.add_argument("--lr", type=float, default=1e-4)
+    p.add_argument("--out", default=None)
+    p.add_argument("--lora-rank", type=int, default=0)
+    a = ap.parse_args(argv)
+    return {"inspect": cmd_inspect, "run": cmd_run, "serve": cmd_serve, "train": cmd_train}[a.cmd](a)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

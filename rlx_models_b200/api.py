@@ -25,12 +25,25 @@ from .runtime.engine import EngineConfig, LLMEngine, RequestOutput, SamplingPara
 from .weights.weight_map import WeightMap
 
 
+def parse_model_ref(ref: str) -> tuple[str, str | None, str | None]:
+    """``org/name[:QUANT][@rev]`` -> (org/name, quant, rev); local paths pass through.
+
+    The hub reference syntax of the reference's model hub (rlx-model-hub):
+    QUANT names a quantised variant (e.g. ``mxfp4``, ``fp8``), ``rev`` a
+    snapshot revision in the cache."""
+    if os.path.exists(ref):
+        return ref, None, None
+    name, _, rev = ref.partition("@")
+    name, _, quant = name.partition(":")
+    return name, (quant or None), (rev or None)
+
+
 def resolve_model_path(model: str) -> str | None:
     """Local dir, or an HF id found in the offline HF cache (snapshots/<rev>)."""
     if os.path.isdir(model):
         return model
     if "/" in model:
-        name, _, rev = model.partition("@")
+        name, _, rev = parse_model_ref(model)
         root = os.environ.get("HF_HUB_CACHE") or os.path.join(
             os.environ.get("HF_HOME", os.path.expanduser("~/.cache/huggingface")), "hub")
         d = os.path.join(root, "models--" + name.replace("/", "--"), "snapshots")

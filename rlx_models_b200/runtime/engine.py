@@ -144,6 +144,7 @@ class LLMEngine:
 
     def abort(self, sid: int):
         self.sched.abort(sid)
+        self.requests.pop(sid, None)
 
     def has_unfinished(self) -> bool:
         return self.sched.has_work()

@@ -1,0 +1,182 @@
+"""OpenAI-compatible HTTP server with continuous batching and SSE streaming.
+
+    python -m rlx_models_b200 serve --model qwen3-0.6b --port 8000
+
+Endpoints: ``GET /health``, ``GET /v1/models``, ``GET /metrics``
+(Prometheus text), ``POST /v1/completions``, ``POST /v1/chat/completions``.
+Prompts may be text (tokenised with the checkpoint's tokenizer, or bytes
+for random-weight shapes) or token-id arrays. Sampling fields: ``max_tokens``,
+``temperature``, ``top_p``, ``top_k``, ``min_p``, ``seed``, ``stop`` (strings),
+``stop_token_ids``, ``ignore_eos``, ``logprobs``; ``stream: true`` answers
+with ``text/event-stream`` chunks and a final ``data: [DONE]``. Every request
+joins the same continuous batch (``serve.runner.EngineRunner``).
+
+Reference: rlx-openai (OpenAI route shapes, SSE framing) and rlx-serve
+src/engine.rs, src/backend.rs:116-167 (stop strings).
+"""
+from __future__ import annotations
+
+import json
+import time
+import uuid
+
+from ..runtime.engine import SamplingParams
+from .runner import EngineRunner
+
+
+def _params(body: dict, eos: int | None) -> tuple[SamplingParams, list[str]]:
+    stop = body.get("stop") or []
+    if isinstance(stop, str):
+        stop = [stop]
+    stop_ids = list(body.get("stop_token_ids") or [])
+    if eos is not None and not body.get("ignore_eos", False):
+        stop_ids.append(int(eos))
+    sp = SamplingParams(max_new_tokens=int(body.get("max_tokens") or 16),
+                        temperature=float(body.get("temperature", 1.0) if body.get("temperature") is not None else 1.0),
+                        top_k=int(body.get("top_k") or 0), top_p=float(body.get("top_p") or 1.0),
+                        min_p=float(body.get("min_p") or 0.0), seed=int(body.get("seed") or 0),
+                        ignore_eos=bool(body.get("ignore_eos", False)), stop_token_ids=stop_ids,
+                        logprobs=bool(body.get("logprobs")))
+    return sp, list(stop)
+
+
+def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model"):
+    from fastapi import FastAPI, HTTPException
+    from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+    from prometheus_client import CollectorRegistry, Counter, Histogram, generate_latest
+
+    app = FastAPI(title="rlx_models_b200 OpenAI server")
+    reg = CollectorRegistry()
+    m_req = Counter("b200_requests_total", "requests", ["route"], registry=reg)
+    m_tok = Counter("b200_generated_tokens_total", "generated tokens", registry=reg)
+    m_ttft = Histogram("b200_ttft_seconds", "time to first token", registry=reg,
+                       buckets=(0.01, 0.05, 0.1, 0.25, 0.5, 1, 2, 5, 10, 30))
+    eos = getattr(tokenizer, "eos_token_id", None)
+
+    def encode_prompt(p):
+        if isinstance(p, list) and p and isinstance(p[0], int):
+            return list(p)
+        if isinstance(p, list):
+            p = p[0] if p else ""
+        if not isinstance(p, str):
+            raise HTTPException(400, "prompt must be a string or an array of token ids")
+        return tokenizer.encode(p)
+
+    def run(ids, body, kind, route_id, created):
+        sp, stop = _params(body, eos)
+        t0 = time.perf_counter()
+        h = runner.submit(ids, sp, stop)
+        first = [None]
+
+        def events():
+            toks = []
+            for ev in h.events():
+                if ev[0] == "token":
+                    if first[0] is None:
+                        first[0] = time.perf_counter()
+                        m_ttft.observe(first[0] - t0)
+                    toks.append(ev[1])
+                    m_tok.inc()
+                    yield "token", ev[1], toks
+                elif ev[0] == "error":
+                    raise HTTPException(500, ev[1])
+                else:
+                    out = ev[1]
+                    reason = h.finish_reason or (out.finish_reason if out is not None else "stop")
+                    yield "done", reason, toks
+        return events()
+
+    def text_of(toks, stop):
+        s = tokenizer.decode(toks)
+        for st in stop:
+            if st and st in s:
+                s = s[:s.index(st)]
+        return s
+
+    def choice(kind, text, reason, idx=0, delta=False):
+        if kind == "chat":
+            key = "delta" if delta else "message"
+            return {"index": idx, key: ({"role": "assistant", "content": text}), "finish_reason": reason}
+        return {"index": idx, "text": text, "finish_reason": reason, "logprobs": None}
+
+    def respond(body, ids, kind):
+        rid = ("chatcmpl-" if kind == "chat" else "cmpl-") + uuid.uuid4().hex[:24]
+        created = int(time.time())
+        obj = "chat.completion" if kind == "chat" else "text_completion"
+        stop = body.get("stop") or []
+        stop = [stop] if isinstance(stop, str) else list(stop)
+        evs = run(ids, body, kind, rid, created)
+        if body.get("stream"):
+            def sse():
+                sent = ""
+                for typ, val, toks in evs:
+                    if typ == "token":
+                        cur = text_of(toks, stop)
+                        piece, sent = cur[len(sent):], cur
+                        if piece:
+                            chunk = {"id": rid, "object": obj + ".chunk", "created": created, "model": model_name,
+                                     "choices": [choice(kind, piece, None, delta=True)]}
+                            yield f"data: {json.dumps(chunk)}\n\n"
+                    else:
+                        chunk = {"id": rid, "object": obj + ".chunk", "created": created, "model": model_name,
+                                 "choices": [choice(kind, "", val, delta=True)],
+                                 "usage": {"prompt_tokens": len(ids), "completion_tokens": len(toks),
+                                           "total_tokens": len(ids) + len(toks)}}
+                        yield f"data: {json.dumps(chunk)}\n\n"
+                yield "data: [DONE]\n\n"
+            return StreamingResponse(sse(), media_type="text/event-stream")
+        toks, reason = [], "stop"
+        for typ, val, tk in evs:
+            toks = tk
+            if typ == "done":
+                reason = val
+        res = {"id": rid, "object": obj, "created": created, "model": model_name,
+               "choices": [choice(kind, text_of(toks, stop), reason)],
+               "usage": {"prompt_tokens": len(ids), "completion_tokens": len(toks),
+                         "total_tokens": len(ids) + len(toks)}}
+        if kind != "chat":
+            res["choices"][0]["token_ids"] = toks
+        return JSONResponse(res)
+
+    @app.get("/health")
+    def health():
+        return {"status": "ok"}
+
+    @app.get("/v1/models")
+    def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "rlx_models_b200"}]}
+
+    @app.get("/metrics")
+    def metrics():
+        return PlainTextResponse(generate_latest(reg).decode())
+
+    @app.post("/v1/completions")
+    def completions(body: dict):
+        m_req.labels("completions").inc()
+        if int(body.get("n", 1)) != 1:
+            raise HTTPException(400, "n > 1 is not supported")
+        return respond(body, encode_prompt(body.get("prompt", "")), "text")
+
+    @app.post("/v1/chat/completions")
+    def chat(body: dict):
+        m_req.labels("chat").inc()
+        msgs = body.get("messages") or []
+        if not msgs:
+            raise HTTPException(400, "messages required")
+        text = tokenizer.apply_chat_template(msgs, add_generation_prompt=True, tokenize=False)
+        return respond(body, tokenizer.encode(text), "chat")
+
+    return app
+
+
+def serve(llm, host: str = "127.0.0.1", port: int = 8000, model_name: str = "b200-model"):
+    import uvicorn
+
+    from ..tokenizer import ByteTokenizer
+    tok = llm.tokenizer or ByteTokenizer()
+    runner = EngineRunner(llm.engine, tok)
+    app = create_app(runner, tok, model_name)
+    try:
+        uvicorn.run(app, host=host, port=port, log_level="info")
+    finally:
+        runner.shutdown()

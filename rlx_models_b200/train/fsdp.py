@@ -59,6 +59,7 @@ class FlatGroup:
         self.exp_avg_sq = torch.zeros_like(master)
         self.grad = torch.zeros_like(master)
         self.anchor = torch.zeros((), device=self.device, requires_grad=True)  # autograd hook for backward
+        self.frozen = False  # frozen groups are gathered without autograd (no weight gradients)
 
     # -- collective helpers ---------------------------------------------------
     def _gloo(self) -> bool:
@@ -126,4 +127,7 @@ class GatherParams(torch.autograd.Function):
 
 
 def gather_params(fg: FlatGroup) -> list[torch.Tensor]:
+    if fg.frozen:
+        with torch.no_grad():
+            return list(fg.views(fg.all_gather()))
     return list(GatherParams.apply(fg.anchor, fg))

@@ -86,6 +86,7 @@ class TrainableDecoder:
         emb = torch.cat([freqs, freqs], -1)
         self.cos = (emb.cos() * mult).to(self.device, torch.bfloat16)
         self.sin = (emb.sin() * mult).to(self.device, torch.bfloat16)
+        self.lora = None  # train.lora.LoraAdapters when fine-tuning with adapters
 
     @property
     def groups(self) -> list[FlatGroup]:
@@ -103,8 +104,13 @@ class TrainableDecoder:
             ln1, wqkv, wo, ln2, wgu, wd = w
             qn = kn = None
         B, S, H = h.shape
+        if self.lora is not None:
+            lp = self.lora.params()
+            lin = lambda t, x, w: self.lora.linear(lp, i, t, x, w)
+        else:
+            lin = lambda t, x, w: TF.linear(x, w)
         a = TF.rmsnorm(h, ln1, c.rms_norm_eps)
-        qkv = TF.linear(a, wqkv)
+        qkv = lin("qkv", a, wqkv)
         q, k, v = torch.split(qkv, [c.q_size, c.kv_size, c.kv_size], -1)
         q = q.reshape(B, S, c.num_attention_heads, c.head_dim)
         k = k.reshape(B, S, c.num_key_value_heads, c.head_dim)
@@ -115,11 +121,11 @@ class TrainableDecoder:
         cos, sin = self.cos[:S], self.sin[:S]
         q, k = TF.rope(q, cos, sin), TF.rope(k, cos, sin)
         o = TF.attention(q, k, v, causal=True).reshape(B, S, c.q_size)
-        h = h + TF.linear(o, wo)
+        h = h + lin("o", o, wo)
         m = TF.rmsnorm(h, ln2, c.rms_norm_eps)
-        gu = TF.linear(m, wgu)
+        gu = lin("gate_up", m, wgu)
         g, u = gu.chunk(2, dim=-1)
-        h = h + TF.linear(F.silu(g) * u, wd)
+        h = h + lin("down", F.silu(g) * u, wd)
         return h
 
     def loss(self, ids: torch.Tensor, targets: torch.Tensor, denom: float | None = None) -> torch.Tensor:

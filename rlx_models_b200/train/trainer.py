@@ -39,6 +39,10 @@ class TrainConfig:
     micro_batch: int = 1        # sequences per micro-step per rank
     activation_checkpointing: bool = True
     param_dtype: str = "bfloat16"  # float32 only for exactness tests
+    lora_rank: int = 0             # > 0: freeze the base, train LoRA adapters of this rank
+    lora_alpha: float = 32.0
+    lora_targets: tuple = ("qkv", "o", "gate_up", "down")
+    dora: bool = False
 
     def lr_at(self, step: int) -> float:
         if self.warmup_steps and step < self.warmup_steps:
@@ -75,19 +79,42 @@ class Trainer:
         self.model = TrainableDecoder(model_cfg, weights, rank, world, self.device, group,
                                       activation_checkpointing=train_cfg.activation_checkpointing,
                                       param_dtype=getattr(torch, train_cfg.param_dtype))
+        self.lora = None
+        if train_cfg.lora_rank > 0:
+            from .lora import LoraAdapters
+            self.lora = LoraAdapters(self.model, train_cfg.lora_rank, train_cfg.lora_alpha, train_cfg.lora_targets,
+                                     train_cfg.dora, group=group, world=world)
+            self.model.lora = self.lora
         self.step_num = 0
         self._sumsq = torch.zeros(1, dtype=torch.float32, device=self.device)
         self._coef = torch.ones(1, dtype=torch.float32, device=self.device)
 
+    @property
+    def all_groups(self) -> list[FlatGroup]:
+        return self.model.groups + ([self.lora.group_flat] if self.lora is not None else [])
+
+    @property
+    def opt_groups(self) -> list[FlatGroup]:
+        """Groups the optimizer updates: the adapters when fine-tuning with LoRA."""
+        return [self.lora.group_flat] if self.lora is not None else self.model.groups
+
     # -- one optimizer step ------------------------------------------------------
-    def step(self, batch: torch.Tensor) -> StepMetrics:
-        """``batch``: this rank's [B_local, S + 1] token ids (inputs + shifted targets)."""
+    def step(self, batch) -> StepMetrics:
+        """``batch``: this rank's [B_local, S + 1] token ids (inputs + shifted
+        targets), or a pair (ids [B, S], targets [B, S]) whose negative targets
+        are ignored (prompt masking, padding)."""
         t0 = time.perf_counter()
         c = self.cfg
-        batch = batch.to(self.device)
-        ids, tgt = batch[:, :-1].contiguous(), batch[:, 1:].contiguous()
+        if isinstance(batch, (tuple, list)):
+            ids, tgt = batch[0].to(self.device), batch[1].to(self.device)
+        else:
+            batch = batch.to(self.device)
+            ids, tgt = batch[:, :-1].contiguous(), batch[:, 1:].contiguous()
         B_local, S = ids.shape
-        global_tokens = float(B_local * S * self.world)  # mean over the global batch
+        n_valid = torch.tensor([float((tgt >= 0).sum())], device=self.device)
+        if self.world > 1:
+            dist.all_reduce(n_valid, group=self.group)
+        global_tokens = max(1.0, float(n_valid))  # mean over the global batch's valid targets
         total = torch.zeros((), dtype=torch.float32, device=self.device)
         mb = max(1, c.micro_batch)
         for s in range(0, B_local, mb):
@@ -96,25 +123,60 @@ class Trainer:
             total += loss.detach()
         if self.world > 1:
             dist.all_reduce(total, group=self.group)
+        if self.lora is not None:
+            self.lora.allreduce_grad()
         gnorm = self._clip_coef()
         lr = c.lr_at(self.step_num)
         self.step_num += 1
-        for g in self.model.groups:
+        for g in self.opt_groups:
             self._adamw(g, lr)
             g.grad.zero_()
         torch.cuda.synchronize(self.device) if self.device.type == "cuda" else None
         ms = (time.perf_counter() - t0) * 1e3
         return StepMetrics(self.step_num, float(total.item()), float(gnorm.item()), lr, int(global_tokens), ms)
 
+    def dpo_step(self, chosen, rejected, beta: float = 0.1, ref_logps=None) -> StepMetrics:
+        """One DPO optimizer step on preference pairs ((ids, targets) each, this
+        rank's rows). Reference log-probs default to the frozen base model
+        (adapters off) when training LoRA, else must be given."""
+        from .losses import dpo_loss, sequence_logprob
+        t0 = time.perf_counter()
+        c = self.cfg
+        (ci, ct), (ri, rt) = [(x.to(self.device), y.to(self.device)) for x, y in (chosen, rejected)]
+        if ref_logps is None:
+            assert self.lora is not None, "ref_logps are required when the full model is trained"
+            with torch.no_grad():
+                saved, self.model.lora = self.model.lora, None
+                ref_c, ref_r = sequence_logprob(self.model, ci, ct), sequence_logprob(self.model, ri, rt)
+                self.model.lora = saved
+        else:
+            ref_c, ref_r = (t.to(self.device) for t in ref_logps)
+        loss = dpo_loss(sequence_logprob(self.model, ci, ct), sequence_logprob(self.model, ri, rt), ref_c, ref_r,
+                        beta) / self.world
+        loss.backward()
+        total = loss.detach()
+        if self.world > 1:
+            dist.all_reduce(total, group=self.group)
+        if self.lora is not None:
+            self.lora.allreduce_grad()
+        gnorm = self._clip_coef()
+        lr = c.lr_at(self.step_num)
+        self.step_num += 1
+        for g in self.opt_groups:
+            self._adamw(g, lr)
+            g.grad.zero_()
+        ms = (time.perf_counter() - t0) * 1e3
+        return StepMetrics(self.step_num, float(total.item()), float(gnorm.item()), lr, int(ci.numel() + ri.numel()), ms)
+
     def _clip_coef(self) -> torch.Tensor:
         """Global L2 norm of the gradient shards; clip coefficient stays on the device."""
         self._sumsq.zero_()
-        for g in self.model.groups:
+        for g in self.opt_groups:
             if g.grad.is_cuda:
                 ops.ext().sumsq(g.grad, self._sumsq)
             else:
                 self._sumsq += g.grad.float().pow(2).sum()
-        if self.world > 1:
+        if self.world > 1 and self.lora is None:  # adapter gradients are already all-reduced
             dist.all_reduce(self._sumsq, group=self.group)
         norm = self._sumsq.sqrt()
         if self.cfg.grad_clip and self.cfg.grad_clip > 0:
@@ -144,7 +206,7 @@ class Trainer:
         """Each rank writes its shards; rank 0 writes the index (world-size agnostic)."""
         os.makedirs(directory, exist_ok=True)
         tensors = {}
-        for g in self.model.groups:
+        for g in self.all_groups:
             tensors[f"{g.name}.master"] = g.master.cpu()
             tensors[f"{g.name}.exp_avg"] = g.exp_avg.cpu()
             tensors[f"{g.name}.exp_avg_sq"] = g.exp_avg_sq.cpu()
@@ -152,7 +214,7 @@ class Trainer:
                   {"rank": self.rank, "world": self.world})
         if self.rank == 0:
             meta = {"world": self.world, "step": self.step_num, "train_config": asdict(self.cfg),
-                    "groups": {g.name: {"numel": g.numel, "padded": g.padded} for g in self.model.groups}}
+                    "groups": {g.name: {"numel": g.numel, "padded": g.padded} for g in self.all_groups}}
             with open(os.path.join(directory, "index.json"), "w") as f:
                 json.dump(meta, f, indent=1)
         if self.world > 1:
@@ -164,7 +226,7 @@ class Trainer:
             meta = json.load(f)
         old_w = meta["world"]
         ckpts = [Checkpoint(os.path.join(directory, f"shard-{r:05d}.safetensors")) for r in range(old_w)]
-        for g in self.model.groups:
+        for g in self.all_groups:
             for field_name in ("master", "exp_avg", "exp_avg_sq"):
                 full = torch.cat([ck.get(f"{g.name}.{field_name}") for ck in ckpts])[:g.numel]
                 shard = torch.zeros(g.shard_n, dtype=torch.float32)
@@ -182,6 +244,15 @@ class Trainer:
         """Consolidated HF-named safetensors (bf16) + config.json, from rank 0."""
         from ..weights.weight_map import WeightMap
         sd = self.model.hf_state_dict()
+        if self.lora is not None:  # fold the adapters into the exported weights
+            from .model import split_fused
+            fused = {}
+            for (i, t), W in self.lora.merged().items():
+                p = f"model.layers.{i}."
+                name = {"qkv": p + "self_attn.qkv_proj.weight", "o": p + "self_attn.o_proj.weight",
+                        "gate_up": p + "mlp.gate_up_proj.weight", "down": p + "mlp.down_proj.weight"}[t]
+                fused[name] = W
+            sd.update(split_fused(fused, self.model.cfg))
         if self.rank == 0:
             WeightMap({k: v.to(torch.bfloat16).cpu() for k, v in sd.items()}).save(directory)
             self.model.cfg.save(directory)

@@ -40,7 +40,7 @@ def _worker(rank, world, port, mode, q):
 def test_rank_failure_detected(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + (0 if mode == "exit" else 7)
+    port = 29950 + (0 if mode == "exit" else 7) + os.getpid() % 20
     procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, q)) for r in range(2)]
     for p in procs:
         p.start()

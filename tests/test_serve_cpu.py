@@ -1,0 +1,122 @@
+"""OpenAI server + engine thread against a fake engine (no GPU): routes,
+token-id and text prompts, SSE framing, stop strings aborting in the engine,
+concurrent requests sharing one batch, metrics."""
+import json
+import threading
+from dataclasses import dataclass, field
+
+import pytest
+
+fastapi = pytest.importorskip("fastapi")
+from fastapi.testclient import TestClient  # noqa: E402
+
+from rlx_models_b200.serve.openai_server import create_app  # noqa: E402
+from rlx_models_b200.serve.runner import EngineRunner  # noqa: E402
+from rlx_models_b200.tokenizer import ByteTokenizer  # noqa: E402
+
+
+@dataclass
+class _St:
+    tokens: list = field(default_factory=list)
+
+
+@dataclass
+class _Out:
+    seq_id: int
+    token_ids: list
+    finish_reason: str
+
+
+class FakeEngine:
+    """Emits prompt[-1] + 1, + 2, ... (bytes) one token per step for every live request."""
+
+    def __init__(self):
+        self.requests, self.params, self.max_batch, self.aborted = {}, {}, 0, []
+        self._n = 0
+        self.lock = threading.Lock()
+
+    def add_request(self, ids, params):
+        self._n += 1
+        self.requests[self._n] = _St()
+        self.params[self._n] = (ids, params)
+        return self._n
+
+    def abort(self, sid):
+        self.aborted.append(sid)
+        self.requests.pop(sid, None)
+
+    def has_unfinished(self):
+        return bool(self.requests)
+
+    def step(self):
+        self.max_batch = max(self.max_batch, len(self.requests))
+        done = []
+        for sid, st in list(self.requests.items()):
+            ids, p = self.params[sid]
+            t = (ids[-1] + len(st.tokens) + 1) % 256
+            st.tokens.append(t)
+            if t in p.stop_token_ids or len(st.tokens) >= p.max_new_tokens:
+                done.append(_Out(sid, list(st.tokens), "stop" if t in p.stop_token_ids else "length"))
+                del self.requests[sid]
+        return done
+
+
+@pytest.fixture()
+def client():
+    eng = FakeEngine()
+    tok = ByteTokenizer()
+    runner = EngineRunner(eng, tok)
+    app = create_app(runner, tok, "fake")
+    with TestClient(app) as c:
+        yield c, eng
+    runner.shutdown()
+
+
+def test_completion_token_ids(client):
+    c, _ = client
+    r = c.post("/v1/completions", json={"prompt": [10, 20], "max_tokens": 4, "temperature": 0})
+    assert r.status_code == 200
+    j = r.json()
+    assert j["choices"][0]["token_ids"] == [21, 22, 23, 24]
+    assert j["choices"][0]["finish_reason"] == "length"
+    assert j["usage"] == {"prompt_tokens": 2, "completion_tokens": 4, "total_tokens": 6}
+
+
+def test_text_prompt_stop_string_and_stream(client):
+    c, eng = client
+    # "a" = 97 -> generates "bcdef..." ; stop at "de"
+    r = c.post("/v1/completions", json={"prompt": "a", "max_tokens": 20, "stop": ["de"]})
+    assert r.json()["choices"][0]["text"] == "bc"
+    assert eng.aborted, "stop string must abort the request in the engine"
+    with c.stream("POST", "/v1/completions", json={"prompt": "a", "max_tokens": 5, "stream": True}) as s:
+        lines = [ln for ln in s.iter_lines() if ln]
+    assert lines[-1] == "data: [DONE]"
+    chunks = [json.loads(ln[6:]) for ln in lines[:-1]]
+    assert "".join(ch["choices"][0]["text"] for ch in chunks) == "bcdef"
+    assert chunks[-1]["choices"][0]["finish_reason"] == "length"
+
+
+def test_chat_and_models_and_metrics(client):
+    c, _ = client
+    r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "hi"}], "max_tokens": 3})
+    j = r.json()
+    assert j["object"] == "chat.completion" and j["choices"][0]["message"]["role"] == "assistant"
+    assert c.get("/v1/models").json()["data"][0]["id"] == "fake"
+    m = c.get("/metrics").text
+    assert "b200_requests_total" in m and "b200_generated_tokens_total" in m
+
+
+def test_concurrent_requests_share_a_batch(client):
+    c, eng = client
+    res = {}
+
+    def go(i):
+        res[i] = c.post("/v1/completions", json={"prompt": [i], "max_tokens": 30}).json()
+
+    th = [threading.Thread(target=go, args=(i,)) for i in range(6)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    assert all(len(res[i]["choices"][0]["token_ids"]) == 30 for i in range(6))
+    assert eng.max_batch >= 2
