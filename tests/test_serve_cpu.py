@@ -49,6 +49,8 @@ class FakeEngine:
         return bool(self.requests)
 
     def step(self):
+        import time
+        time.sleep(0.002)  # a device step takes time; lets concurrent clients join the batch
         self.max_batch = max(self.max_batch, len(self.requests))
         done = []
         for sid, st in list(self.requests.items()):
