@@ -602,7 +602,8 @@ void moe_combine(const Tensor& rows, const Tensor& inv, int64_t k, Tensor& out, 
 // (quant.mxfp4.tile_mxfp4); N: logical weight rows. x f16; out f16 (gate/up) or bf16 (down).
 void moe_gemm(const Tensor& x, const Tensor& w, const Tensor& row_exp, int64_t N, const optional<Tensor>& bias,
               const optional<Tensor>& row_weight, const Tensor& perm, const Tensor& meta, const Tensor& tiles,
-              Tensor& out, bool swiglu, double limit, double alpha, int64_t bt, Tensor& status) {
+              Tensor& out, bool swiglu, double limit, double alpha, int64_t bt, Tensor& status,
+              double up_offset) {
   check_cuda(x, "x");
   TORCH_CHECK(x.scalar_type() == at::kHalf && x.is_contiguous(), "b200.moe_gemm: x must be f16");
   TORCH_CHECK(out.scalar_type() == (swiglu ? at::kHalf : at::kBFloat16), "b200.moe_gemm: out f16 (gate/up) / bf16");
@@ -635,6 +636,7 @@ void moe_gemm(const Tensor& x, const Tensor& w, const Tensor& row_exp, int64_t N
   a.swiglu = swiglu;
   a.limit = (float)limit;
   a.alpha = (float)alpha;
+  a.up_offset = (float)up_offset;
   a.status = status.data_ptr<int>();
   a.device = x.get_device();
   b200::moe_gemm_launch(a, cur_stream(x));
@@ -710,7 +712,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);
   m.def("moe_combine", &moe_combine);
-  m.def("moe_gemm", &moe_gemm);
+  m.def("moe_gemm", &moe_gemm, py::arg("x"), py::arg("w"), py::arg("row_exp"), py::arg("N"), py::arg("bias"),
+        py::arg("row_weight"), py::arg("perm"), py::arg("meta"), py::arg("tiles"), py::arg("out"), py::arg("swiglu"),
+        py::arg("limit"), py::arg("alpha"), py::arg("bt"), py::arg("status"), py::arg("up_offset") = 1.0);
   m.def("adamw", &adamw);
   m.def("sumsq", &sumsq);
   m.def("ce_fwd_bwd", &ce_fwd_bwd);

@@ -213,6 +213,7 @@ struct MoeGemmArgs {
   int max_tiles;          // capacity of the tile list (grid bound)
   int swiglu;
   float limit, alpha;
+  float up_offset;        // (up + up_offset): gpt-oss 1, plain SwiGLU 0
   int* status;
   int device;
 };

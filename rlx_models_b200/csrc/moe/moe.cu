@@ -300,6 +300,7 @@ struct MoeParams {
   const int32_t* perm;        // sorted row -> assignment
   void* out;                  // [rows, N] bf16 (down) or [rows, N / 2] f16 (gate/up)
   float limit, alpha;         // clamped SwiGLU
+  float up_offset;            // act = (up + up_offset) * g * sigmoid(alpha g): gpt-oss 1, plain SwiGLU 0
   int* status;
   int debug;                  // B200_MOE_DEBUG (timing experiments only): bit 0 skips the dequant,
                               // bit 1 the MMAs, bit 2 the token-tile loads, bit 3 runs the copy
@@ -546,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float uu = xchg[fl * 33 + j];
                 g = fminf(g, p.limit);
                 uu = fmaxf(fminf(uu, p.limit), -p.limit);
-                const float a = (uu + 1.f) * g / (1.f + __expf(-p.alpha * g));
+                const float a = (uu + p.up_offset) * g / (1.f + __expf(-p.alpha * g));
                 reinterpret_cast<__half*>(p.out)[(int64_t)(row0 + col) * Nh + f] = __float2half_rn(a);
               }
             }
@@ -660,6 +661,7 @@ void moe_gemm_launch(const MoeGemmArgs& a, cudaStream_t st) {
   p.out = a.out;
   p.limit = a.limit;
   p.alpha = a.alpha;
+  p.up_offset = a.up_offset;
   p.status = a.status;
   static const int dbg = [] {
     const char* e = std::getenv("B200_MOE_DEBUG");

@@ -92,18 +92,45 @@ class MoEDecoderLM(DecoderLM):
             L.wqkv = dv(torch.cat([g(p + f"self_attn.{n}_proj.weight").to(dev) for n in "qkv"], 0))
             L.bqkv = dv(torch.cat([g(p + f"self_attn.{n}_proj.bias").to(dev) for n in "qkv"])) \
                 if c.attention_bias else None
-            L.q_norm = L.k_norm = None
+            if c.qk_norm:
+                L.q_norm = dv(g(p + "self_attn.q_norm.weight"))
+                L.k_norm = dv(g(p + "self_attn.k_norm.weight"))
+            else:
+                L.q_norm = L.k_norm = None
             L.wo = dv(g(p + "self_attn.o_proj.weight"))
             ob = p + "self_attn.o_proj.bias"
             L.bo = dv(g(ob)) if (ob in w) else None
+            L.bqkv = L.bqkv if c.attention_bias else None
             L.w_gu = L.wd = None
             L.sinks = g(p + "self_attn.sinks").to(dev, torch.float32).contiguous() if c.attn_sinks else None
             L.window = c.layer_window(i)
             self.layers.append(L)
             M = MoELayer()
+            pe = p + "mlp.experts."
+            E_l = hi - lo
+            if c.model_type != "gpt_oss":
+                # qwen3-moe: router "mlp.gate", per-expert gate/up/down, no biases; experts are
+                # packed to MXFP4 at load (the grouped GEMM streams 4-bit weights)
+                M.router_w = dv(g(p + "mlp.gate.weight"))
+                M.router_b = None
+                I = c.moe_intermediate_size
+                gu_l, dn_l = [], []
+                for e in range(lo, hi):
+                    gt = g(pe + f"{e}.gate_proj.weight").to(dev).float()
+                    up = g(pe + f"{e}.up_proj.weight").to(dev).float()
+                    # [64 gate rows][64 up rows] per 128-row tile, like hf_interleaved_to_grouped's output
+                    gu_l.append(torch.stack([gt.view(I // GROUP, GROUP, -1), up.view(I // GROUP, GROUP, -1)], 1)
+                                .reshape(2 * I, -1))
+                    dn_l.append(g(pe + f"{e}.down_proj.weight").to(dev).float())
+                gub, gus = quantize_mxfp4(torch.stack(gu_l))
+                dnb, dns = quantize_mxfp4(torch.stack(dn_l))
+                M.gu_w, M.gu_exp = tile_mxfp4(gub, gus)
+                M.dn_w, M.dn_exp = tile_mxfp4(dnb, dns)
+                M.gu_bias = M.dn_bias = None
+                self.moe.append(M)
+                continue
             M.router_w = dv(g(p + "mlp.router.weight"))
             M.router_b = dv(g(p + "mlp.router.bias"))
-            pe = p + "mlp.experts."
             if (pe + "gate_up_proj_blocks") in w:
                 gub = g(pe + "gate_up_proj_blocks")[lo:hi]
                 gus = g(pe + "gate_up_proj_scales")[lo:hi]
@@ -112,7 +139,6 @@ class MoEDecoderLM(DecoderLM):
             else:  # bf16 checkpoint: quantize to MXFP4 at load ([E, in, out] -> [E, out, in])
                 gub, gus = quantize_mxfp4(g(pe + "gate_up_proj")[lo:hi].to(dev).float().transpose(1, 2))
                 dnb, dns = quantize_mxfp4(g(pe + "down_proj")[lo:hi].to(dev).float().transpose(1, 2))
-            E_l = hi - lo
             M.gu_w, M.gu_exp = tile_mxfp4(hf_interleaved_to_grouped(gub.to(dev).reshape(E_l, gub.shape[1], -1)),
                                 hf_interleaved_to_grouped(gus.to(dev).reshape(E_l, gus.shape[1], -1)))
             M.gu_bias = hf_interleaved_to_grouped(dv(g(pe + "gate_up_proj_bias")[lo:hi]))
@@ -146,8 +172,10 @@ class MoEDecoderLM(DecoderLM):
         I = c.moe_intermediate_size
         s = scratch(dev)
         gu = torch.empty(n, I, dtype=torch.float16, device=dev)
+        gpt_oss = c.model_type == "gpt_oss"
         ext().moe_gemm(a, M.gu_w, M.gu_exp, 2 * I, M.gu_bias, None, perm, meta, tiles, gu, True,
-                       float(c.swiglu_limit or 1e30), float(c.swiglu_alpha), bt, s.status)
+                       float(c.swiglu_limit or 1e30), float(c.swiglu_alpha) if gpt_oss else 1.0, bt, s.status,
+                       1.0 if gpt_oss else 0.0)
         dn = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
         ext().moe_gemm(gu, M.dn_w, M.dn_exp, H, M.dn_bias, weights.view(-1), perm, meta, tiles, dn, False,
                        0.0, 0.0, bt, s.status)

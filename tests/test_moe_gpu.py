@@ -110,3 +110,32 @@ def test_gpt_oss_model_vs_oracle(cuda):
     eng = LLMEngine(model, EngineConfig(max_num_seqs=4, max_model_len=128, num_blocks=32))
     out = eng.generate([ids.tolist()], SamplingParams(max_new_tokens=6, ignore_eos=True))[0]
     assert out.token_ids[0] == int(lg[-1].argmax())
+
+
+def test_qwen3_moe_model_vs_oracle(cuda):
+    """Qwen3-MoE (softmax-first routing with renormalisation, plain SwiGLU,
+    QK-norm, no biases) through the grouped MXFP4 GEMM; the oracle uses the
+    same MXFP4-rounded expert weights."""
+    from rlx_models_b200.quant.mxfp4 import mxfp4_roundtrip
+    cfg = C.tiny("qwen3_moe", hidden_size=256, num_attention_heads=4, num_key_value_heads=2, head_dim=64,
+                 num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128, vocab_size=512)
+    w = random_weights(cfg, seed=4, dtype=torch.bfloat16)
+    for k in list(w):
+        if ".mlp.experts." in k:
+            w[k] = mxfp4_roundtrip(w[k].float()).bfloat16()
+    model = MoEDecoderLM(cfg, w, device=cuda)
+    oracle = DecoderOracle(cfg, {k: v.float() for k, v in w.items()})
+    from rlx_models_b200.models.decoder import ForwardBatch
+    T = 37
+    ids = torch.randint(0, cfg.vocab_size, (T,), generator=torch.Generator().manual_seed(2))
+    nb = (T + 15) // 16
+    fb = ForwardBatch(input_ids=ids.int().to(cuda), positions=torch.arange(T, dtype=torch.int32, device=cuda),
+                      slots=torch.arange(T, dtype=torch.int64, device=cuda), num_decode=0,
+                      pre_block_tables=torch.arange(nb, dtype=torch.int32, device=cuda).view(1, -1),
+                      pre_ctx_lens=torch.tensor([T], dtype=torch.int32, device=cuda),
+                      pre_cu_q=torch.tensor([0, T], dtype=torch.int32, device=cuda), pre_max_q=T)
+    lg = model.forward(fb, model.make_kv_cache(nb))
+    ref, _ = oracle.forward(ids)
+    row = ((lg.cpu().float() - ref).norm(dim=-1) / ref.norm(dim=-1))
+    assert row.median() < 2e-2, row
+    assert (row > 0.1).float().mean() <= 0.1, row

@@ -40,3 +40,18 @@ def test_fused_ce_matches_torch(cuda):
     assert abs(loss.item() - lr.item()) < 1e-2
     assert ((x.grad.float() - xr.grad).norm() / xr.grad.norm()) < 2e-2
     assert ((w.grad.float() - wr.grad).norm() / wr.grad.norm()) < 2e-2
+
+
+def test_lora_on_gpu_trains_adapters(cuda):
+    from rlx_models_b200 import config as C
+    from rlx_models_b200.train.trainer import TrainConfig, Trainer
+    from rlx_models_b200.weights.init import random_weights
+    cfg = C.tiny(num_hidden_layers=2, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=64, vocab_size=512)
+    t = Trainer(cfg, TrainConfig(lr=2e-2, micro_batch=2, lora_rank=16, lora_alpha=32.0),
+                random_weights(cfg, 0), device=cuda)
+    base = [g.master.clone() for g in t.model.groups]
+    b = torch.randint(0, 512, (4, 129), generator=torch.Generator().manual_seed(0))
+    losses = [t.step(b).loss for _ in range(5)]
+    assert losses[-1] < losses[0]
+    assert all(torch.equal(g.master, m) for g, m in zip(t.model.groups, base))
