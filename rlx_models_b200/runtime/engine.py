@@ -270,7 +270,8 @@ class LLMEngine:
             return []
         sids = h["sample_ids"][:R].tolist()
         greedy = self._params_rows(sids)
-        B = self._bucket(nd) if (npf == 0 and self.cfg.cuda_graphs) else None
+        B = self._bucket(nd) if (npf == 0 and self.cfg.cuda_graphs and not hasattr(self.model, "share_tokens")) \
+            else None
         if B is not None:
             key = (B, greedy)
             if key not in self.graphs:
@@ -284,7 +285,13 @@ class LLMEngine:
             self.stats["graph_steps"] += 1
         else:
             logits = self._eager_forward(T, nd, npf, max_q, R)
-            toks = self._sample(logits, R, greedy)
+            if logits is None:  # a non-final pipeline stage: tokens come from the last stage
+                toks = self.tok_out[:R]
+            else:
+                toks = self._sample(logits, R, greedy)
+            if hasattr(self.model, "share_tokens"):
+                self.model.share_tokens(self.tok_out[:R])
+                toks = self.tok_out[:R]
             self.stats["eager_steps"] += 1
         self.tok_host[:R].copy_(toks[:R])
         self.stats["d2h_bytes"] += 4 * R

@@ -1,0 +1,138 @@
+"""Speculative decoding: draft, then verify k tokens in one target pass.
+
+Greedy draft-and-verify: a proposer suggests ``k`` tokens after the last
+accepted one; the target runs the last accepted token plus the ``k``
+proposals as one causal chunk (k + 1 positions, logits at every position),
+accepts the longest prefix that equals its own argmax and appends its own
+token at the first disagreement (or a bonus token when all k match). The
+output is the target's greedy continuation; each target pass yields between
+1 and k + 1 tokens.
+
+Proposers:
+  * a draft model (any decoder with the same vocabulary) decoding greedily on
+    its own paged KV cache, rolled back by position after each verification;
+  * prompt lookup (no model): the tokens that followed the most recent earlier
+    occurrence of the current n-gram suffix (n = ngram .. 1).
+
+KV caches are positional (slot = position under an identity block table), so
+rolling back after a rejection is just moving the position: stale entries past
+it are overwritten by the next writes.
+
+Reference: rlx-qwen3 src/spec.rs (draft / verify loop), rlx-eagle3 and
+rlx-dflash (learned draft heads, not built here).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ..models.decoder import ForwardBatch
+
+
+@dataclass
+class SpecStats:
+    target_passes: int = 0
+    proposed: int = 0
+    accepted: int = 0
+
+    @property
+    def acceptance(self) -> float:
+        return self.accepted / max(1, self.proposed)
+
+    @property
+    def tokens_per_pass(self) -> float:
+        return (self.accepted + self.target_passes) / max(1, self.target_passes)
+
+
+class _Seq:
+    """A model plus its own paged cache for one sequence (identity block table)."""
+
+    def __init__(self, model, max_len: int):
+        self.model = model
+        self.nb = (max_len + 15) // 16 + 1
+        self.kv = model.make_kv_cache(self.nb)
+        dev = model.device
+        self.table = torch.arange(self.nb, dtype=torch.int32, device=dev).view(1, -1)
+        self.pos = 0  # positions [0, pos) hold valid K/V
+
+    @torch.no_grad()
+    def run(self, tokens: list[int], start: int) -> torch.Tensor:
+        """Feed ``tokens`` at positions start.. ; returns fp32 logits per token [n, V]."""
+        dev = self.model.device
+        n = len(tokens)
+        ctx = start + n
+        if ctx > self.nb * 16:
+            raise ValueError("sequence longer than the speculative decoder's max_len")
+        fb = ForwardBatch(input_ids=torch.tensor(tokens, dtype=torch.int32, device=dev),
+                          positions=torch.arange(start, ctx, dtype=torch.int32, device=dev),
+                          slots=torch.arange(start, ctx, dtype=torch.int64, device=dev), num_decode=0,
+                          pre_block_tables=self.table, pre_ctx_lens=torch.tensor([ctx], dtype=torch.int32, device=dev),
+                          pre_cu_q=torch.tensor([0, n], dtype=torch.int32, device=dev), pre_max_q=n)
+        out = self.model.forward(fb, self.kv)
+        self.pos = ctx
+        return out
+
+
+class SpeculativeDecoder:
+    def __init__(self, target, draft=None, k: int = 4, max_len: int = 4096, ngram: int = 3):
+        self.target = _Seq(target, max_len)
+        self.draft = _Seq(draft, max_len) if draft is not None else None
+        self.k, self.ngram = k, ngram
+        self.stats = SpecStats()
+
+    # -- proposers ---------------------------------------------------------------
+    def _propose_draft(self, seq: list[int], k: int) -> list[int]:
+        d = self.draft
+        # catch up: feed every accepted token the draft has not seen (the last one included)
+        pending = seq[d.pos:]
+        lg = d.run(pending, d.pos)
+        props = [int(lg[-1].argmax())]
+        for _ in range(k - 1):
+            lg = d.run([props[-1]], d.pos)
+            props.append(int(lg[-1].argmax()))
+        return props
+
+    def _propose_lookup(self, seq: list[int], k: int) -> list[int]:
+        for n in range(min(self.ngram, len(seq) - 1), 0, -1):
+            suf = seq[-n:]
+            for s in range(len(seq) - n - 1, -1, -1):
+                if seq[s:s + n] == suf:
+                    nxt = seq[s + n:s + n + k]
+                    if nxt:
+                        return nxt
+        return []
+
+    # -- generation --------------------------------------------------------------
+    @torch.no_grad()
+    def generate(self, prompt: list[int], max_new_tokens: int, eos_token_id: int | None = None) -> list[int]:
+        t = self.target
+        t.pos = 0
+        if self.draft is not None:
+            self.draft.pos = 0
+        lg = t.run(list(prompt), 0)
+        seq = list(prompt) + [int(lg[-1].argmax())]
+        out = [seq[-1]]
+        while len(out) < max_new_tokens and (eos_token_id is None or out[-1] != eos_token_id):
+            k = min(self.k, max_new_tokens - len(out))
+            props = self._propose_draft(seq, k) if self.draft is not None else self._propose_lookup(seq, k)
+            # verify: the last accepted token (not yet in the target cache) + proposals
+            start = len(seq) - 1
+            lv = t.run([seq[-1]] + props, start)
+            tgt = lv.argmax(-1).tolist()
+            n_acc = 0
+            while n_acc < len(props) and props[n_acc] == tgt[n_acc]:
+                n_acc += 1
+            new = props[:n_acc] + [tgt[n_acc]]
+            self.stats.target_passes += 1
+            self.stats.proposed += len(props)
+            self.stats.accepted += n_acc
+            if eos_token_id is not None and eos_token_id in new:
+                new = new[:new.index(eos_token_id) + 1]
+            new = new[:max_new_tokens - len(out)]
+            seq += new
+            out += new
+            t.pos = len(seq) - 1  # the newest token is not in the cache yet
+            if self.draft is not None:
+                self.draft.pos = min(self.draft.pos, len(seq) - 1)
+        return out

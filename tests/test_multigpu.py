@@ -1,0 +1,31 @@
+"""Multi-GPU checks through torchrun (skipped with fewer than 2 GPUs):
+tensor-parallel and pipeline-parallel generations equal the single-GPU ones."""
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _torchrun(module, n):
+    if torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={n}", "--master-addr=127.0.0.1", f"--master-port={29500 + os.getpid() % 400}",
+           "-m", module]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-3000:]
+    return r.stdout
+
+
+def test_pipeline_parallel_two_stages():
+    out = _torchrun("rlx_models_b200.parallel.pp_check", 2)
+    assert '"match": true' in out
+
+
+def test_tensor_parallel_two_ranks():
+    _torchrun("rlx_models_b200.parallel.tp_check", 2)
