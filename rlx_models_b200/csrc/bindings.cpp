@@ -78,9 +78,9 @@ void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const o
   a.device = x.get_device();
   if (trace.has_value() && trace->defined())
     a.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
-  if (act_from >= 0) {
-    a.act = 1;
-    a.act_from = (int)act_from;
+  if (act_from >= 0) {  // act_from >= (1 << 30): ReLU from column act_from - (1 << 30)
+    a.act = act_from >= (1LL << 30) ? 2 : 1;
+    a.act_from = (int)(act_from >= (1LL << 30) ? act_from - (1LL << 30) : act_from);
   }
   if (gate.has_value() && gate->defined()) {
     TORCH_CHECK(gate->scalar_type() == at::kBFloat16 && gate->dim() == 2 && gate->stride(1) == 1 &&

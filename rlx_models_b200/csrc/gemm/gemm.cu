@@ -57,7 +57,7 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
   if (M == 0 || N == 0) return;
   const int sms = num_sms(a.device);
   const bool dit_epi = a.act != 0 || a.gate != nullptr;
-  const bool sw = dit_epi ? false : (a.swap < 0 ? (M <= 128 && N >= 256) : (a.swap == 1));
+  const bool sw = a.swap < 0 ? (M <= 128 && N >= 256) : (a.swap == 1);
 
   gemm::Params p{};
   const void* A = sw ? a.w : a.x;
@@ -85,11 +85,14 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
     double best = 1e30;
     // large tile counts already fill the machine; their partial tiles would
     // also outgrow the accumulator
-    const int max_sp = (tiles >= 2 * sms) ? 1 : std::max(1, std::min(16, p.k_tiles / 4));
+    // non-accumulating split-K pays a partial-tile round trip through the workspace
+    // and a semaphore tail per tile: only worth it when the tiles leave most SMs idle
+    const int max_sp = (tiles >= (epi == gemm::EPI_ACC ? 2 * sms : sms)) ? 1
+                                                                         : std::max(1, std::min(16, p.k_tiles / 4));
     for (int s = 1; s <= max_sp; ++s) {
       const int kts = (p.k_tiles + s - 1) / s;
       const int waves = (tiles * s + sms - 1) / sms;
-      const double cost = (double)waves * kts + (s > 1 ? (epi == gemm::EPI_ACC ? 0.5 : 2.0) * s : 0.0);
+      const double cost = (double)waves * kts + (s > 1 ? (epi == gemm::EPI_ACC ? 0.5 : 6.0) * s : 0.0);
       if (cost < best - 1e-9) {
         best = cost;
         sp = s;
@@ -183,7 +186,10 @@ void gemm_launch(const GemmArgs& a, cudaStream_t st) {
   if (sp <= 0) {
     sp = 1;
     double best = 1e30;
-    const int max_sp = (tiles >= 2 * sms) ? 1 : std::max(1, std::min(16, p.k_tiles / 4));
+    // non-accumulating split-K pays a partial-tile round trip through the workspace
+    // and a semaphore tail per tile: only worth it when the tiles leave most SMs idle
+    const int max_sp = (tiles >= (epi == gemm::EPI_ACC ? 2 * sms : sms)) ? 1
+                                                                         : std::max(1, std::min(16, p.k_tiles / 4));
     for (int s = 1; s <= max_sp; ++s) {
       const int kts = (p.k_tiles + s - 1) / s;
       const int waves = (tiles * s + sms - 1) / sms;

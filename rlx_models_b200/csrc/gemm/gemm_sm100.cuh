@@ -70,7 +70,7 @@ struct Params {
   int bcast;  // push every output row to all ranks (one-shot all-reduce slots) instead of its owner
   unsigned long long* trace;  // optional per-CTA timeline ([grid][16] globaltimer ns), debug only
   // Normal orientation only (adaLN DiT blocks):
-  //   act = 1: GELU (tanh form) on output columns j >= act_from, after the bias;
+  //   act = 1: GELU (tanh form), 2: ReLU, on output columns j >= act_from, after the bias;
   //   gate != null: y = gate[batch(i)][j] * y before the residual is added, with
   //   batch(i) = i < gate_split ? i / gate_r1 : (i - gate_split) / gate_r2.
   int act, act_from;
@@ -143,10 +143,10 @@ __device__ __forceinline__ void store_chunk(const Params& p, int i, int j0, floa
       if (j0 + t < p.NB) v[t] += __bfloat162float(p.bias[j0 + t]);
   }
   const bool full = (j0 + 32 <= p.NB);
-  if (p.act == 1 && j0 + 32 > p.act_from) {
+  if (p.act != 0 && j0 + 32 > p.act_from) {
 #pragma unroll
     for (int t = 0; t < 32; ++t)
-      if (j0 + t >= p.act_from) v[t] = gelu_tanh(v[t]);
+      if (j0 + t >= p.act_from) v[t] = p.act == 1 ? gelu_tanh(v[t]) : fmaxf(v[t], 0.f);
   }
   if (p.gate != nullptr) {
     const int gb = i < p.gate_split ? i / p.gate_r1 : (i - p.gate_split) / p.gate_r2;
@@ -245,6 +245,17 @@ __device__ __forceinline__ void store_vec(const Params& p, int j, int fo, int nf
 #pragma unroll
     for (int t = 0; t < NV; ++t)
       if (fo + t < nfeat) o[t] += __bfloat162float(p.bias[fo + t]);
+  }
+  if (p.act != 0) {
+#pragma unroll
+    for (int t = 0; t < NV; ++t)
+      if (fo + t >= p.act_from) o[t] = p.act == 1 ? gelu_tanh(o[t]) : fmaxf(o[t], 0.f);
+  }
+  if (p.gate != nullptr) {
+    const int gb = j < p.gate_split ? j / p.gate_r1 : (j - p.gate_split) / p.gate_r2;
+#pragma unroll
+    for (int t = 0; t < NV; ++t)
+      if (fo + t < nfeat) o[t] *= __bfloat162float(p.gate[(int64_t)gb * p.gate_ld + fo + t]);
   }
   if (p.R != nullptr) {
     const __nv_bfloat16* r = p.R + (int64_t)j * p.ldr_j + fo;

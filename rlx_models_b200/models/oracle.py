@@ -51,6 +51,14 @@ class DecoderOracle:
     def W(self, name: str) -> torch.Tensor:
         return self.w[name].float()
 
+    def _mm(self, x: torch.Tensor, name: str) -> torch.Tensor:
+        """x @ W^T; with ``self.taps`` set, records the input rows per weight
+        name (calibration activations for quant.calib)."""
+        taps = getattr(self, "taps", None)
+        if taps is not None:
+            taps.setdefault(name, []).append(x.detach().reshape(-1, x.shape[-1]).cpu())
+        return x @ self.W(name).T
+
     def _experts_fp32(self, i: int):
         if i not in self._experts:
             p = f"model.layers.{i}.mlp.experts."
@@ -69,7 +77,7 @@ class DecoderOracle:
         T = x.shape[0]
 
         def proj(n):
-            y = x @ self.W(p + n + ".weight").T
+            y = self._mm(x, p + n + ".weight")
             if (p + n + ".bias") in self.w:
                 y = y + self.W(p + n + ".bias")
             return y
@@ -91,7 +99,7 @@ class DecoderOracle:
         sinks = self.W(p + "sinks") if c.attn_sinks else None
         o = R.attention(q, kv.k[i], kv.v[i], pos, kpos, 1.0 / math.sqrt(c.head_dim), causal=True,
                         window=c.layer_window(i), sinks=sinks)
-        y = o.reshape(T, -1) @ self.W(p + "o_proj.weight").T
+        y = self._mm(o.reshape(T, -1), p + "o_proj.weight")
         if (p + "o_proj.bias") in self.w:
             y = y + self.W(p + "o_proj.bias")
         return y
@@ -100,9 +108,9 @@ class DecoderOracle:
         c = self.cfg
         p = f"model.layers.{i}.mlp."
         if not c.is_moe:
-            g = x @ self.W(p + "gate_proj.weight").T
-            u = x @ self.W(p + "up_proj.weight").T
-            return (F.silu(g) * u) @ self.W(p + "down_proj.weight").T
+            g = self._mm(x, p + "gate_proj.weight")
+            u = self._mm(x, p + "up_proj.weight")
+            return self._mm(F.silu(g) * u, p + "down_proj.weight")
         if c.model_type == "gpt_oss":
             logits = x @ self.W(p + "router.weight").T + self.W(p + "router.bias")
             topv, topi = logits.topk(c.num_experts_per_tok, dim=-1)

@@ -25,7 +25,7 @@ SWIGLU_GROUP = 64  # gate/up rows interleaved in groups of 64 for the fused epil
 def linear(x: torch.Tensor, w: torch.Tensor, *, out: torch.Tensor | None = None,
            residual: torch.Tensor | None = None, bias: torch.Tensor | None = None,
            alpha: float = 1.0, out_dtype: torch.dtype = torch.bfloat16,
-           swap: int = -1, bn: int = 0, splits: int = 0, gelu_from: int = -1,
+           swap: int = -1, bn: int = 0, splits: int = 0, gelu_from: int = -1, relu: bool = False,
            gate: torch.Tensor | None = None, gate_rows: tuple = (0, 1, 1)) -> torch.Tensor:
     """``out = alpha * x @ w.T (+ bias) (+ residual)`` on the tcgen05 GEMM.
 
@@ -41,9 +41,42 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, out: torch.Tensor | None = None,
     s = scratch(x.device)
     mode = 1 if out.dtype == torch.float32 else 0
     _count(1)
+    act_from = (1 << 30) if relu else int(gelu_from)
     ext().linear(x, w, out, mode, residual, bias, float(alpha), s.gemm_ws, s.gemm_sem, s.status,
-                 swap, bn, splits, None, int(gelu_from), gate, int(gate_rows[0]), int(gate_rows[1]),
+                 swap, bn, splits, None, act_from, gate, int(gate_rows[0]), int(gate_rows[1]),
                  int(gate_rows[2]))
+    return out
+
+
+_DENSE_Q_CACHE: dict = {}
+
+
+def linear_mxfp4(x: torch.Tensor, w_tiled: torch.Tensor, row_exp: torch.Tensor, n_out: int,
+                 bias: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ dequant(W).T (+ bias)`` with W stored as MXFP4 in the grouped-GEMM
+    tile layout (``quant.mxfp4.tile_mxfp4`` of one expert, [1, NT, KT, 4352]):
+    the dense weight-only 4-bit linear runs on the grouped kernel with a single
+    expert (f16 operands, E2M1 expanded into TMEM). x [T, K] bf16 -> [T, N] bf16."""
+    T, K = x.shape
+    dev = x.device
+    bt = 32 if T <= 32 else (64 if T <= 64 else 128)
+    key = (dev, T, bt)
+    st = _DENSE_Q_CACHE.get(key)
+    if st is None:
+        ntile = (T + bt - 1) // bt
+        meta = torch.tensor([ntile, T, 0, T], dtype=torch.int32, device=dev)  # tiles, count[0], offs[0..1]
+        info = torch.tensor([[0, m, m * bt, min(bt, T - m * bt)] for m in range(ntile)], dtype=torch.int32,
+                            device=dev).reshape(-1)
+        perm = torch.arange(T, dtype=torch.int32, device=dev)
+        st = _DENSE_Q_CACHE[key] = (meta, info, perm)
+    meta, info, perm = st
+    a = torch.empty(T, K, dtype=torch.float16, device=dev)
+    ext().moe_gather(x, perm, meta, 1, 1, a)
+    if out is None:
+        out = torch.empty(T, n_out, dtype=torch.bfloat16, device=dev)
+    _count(2)
+    ext().moe_gemm(a, w_tiled, row_exp, n_out, bias, None, perm, meta, info, out, False, 0.0, 0.0, bt,
+                   scratch(dev).status)
     return out
 
 

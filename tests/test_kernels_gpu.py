@@ -282,3 +282,40 @@ def test_attention_noncausal_paged_rescale(cuda, qscale, causal):
         pos = torch.arange(L, device=cuda)
         r = ref.attention(q[rows], kk, vv, pos, pos, 1 / math.sqrt(D), causal=causal)
         assert rel_err(out[rows], r) < 2e-2, b
+
+
+@pytest.mark.parametrize("M", [1, 40, 200])
+def test_linear_mxfp4_dense_and_relu(cuda, M):
+    from rlx_models_b200.quant.mxfp4 import dequantize_mxfp4, quantize_mxfp4, tile_mxfp4
+    N, K = 320, 512
+    w = torch.randn(N, K, device=cuda) * 0.05
+    b = (torch.randn(N, device=cuda) * 0.1).bfloat16()
+    blocks, scales = quantize_mxfp4(w.view(1, N, K))
+    wt, rexp = tile_mxfp4(blocks, scales)
+    x = torch.randn(M, K, device=cuda).bfloat16()
+    y = ops.linear_mxfp4(x, wt, rexp, N, bias=b)
+    ops.check_errors(cuda)
+    wd = dequantize_mxfp4(blocks, scales)[0]
+    ref = x.half().float() @ wd.T + b.float()
+    assert rel_err(y, ref) < 1e-2
+    wb = w.bfloat16()
+    yr = ops.linear(x, wb, bias=b, relu=True)
+    assert rel_err(yr, torch.relu(x.float() @ wb.float().T + b.float())) < 1e-2
+
+
+@pytest.mark.parametrize("M", [3, 64])
+def test_linear_small_m_epilogues(cuda, M):
+    """Swap-AB (M <= 128) path: bias + ReLU / GELU and the adaLN gate with residual."""
+    import torch.nn.functional as F
+    N, K, B = 512, 256, 1
+    x = torch.randn(M, K, device=cuda).bfloat16()
+    w = (torch.randn(N, K, device=cuda) * 0.05).bfloat16()
+    b = (torch.randn(N, device=cuda) * 0.1).bfloat16()
+    lin = x.float() @ w.float().T + b.float()
+    assert rel_err(ops.linear(x, w, bias=b, relu=True), torch.relu(lin)) < 1e-2
+    g = ops.linear(x, w, bias=b, gelu_from=128)
+    assert rel_err(g, torch.cat([lin[:, :128], F.gelu(lin[:, 128:], approximate="tanh")], 1)) < 1e-2
+    res = torch.randn(M, N, device=cuda).bfloat16()
+    gate = torch.randn(B, N, device=cuda).bfloat16()
+    y = ops.linear(x, w, bias=b, residual=res, gate=gate, gate_rows=(0, 1, M))
+    assert rel_err(y, res.float() + gate.float() * lin) < 1e-2
