@@ -206,7 +206,7 @@ def main():
     ap.add_argument("--output-len", type=int, default=None)
     ap.add_argument("--max-batched-tokens", type=int, default=8192)
     ap.add_argument("--kv-gb", type=float, default=40.0)
-    ap.add_argument("--tp-comm", default="nccl", choices=["nccl", "fused"],
+    ap.add_argument("--tp-comm", default="nccl", choices=["nccl", "fused", "pull"],
                     help="nccl: NCCL all-reduce baseline; fused: GEMM->reduce-scatter + norm + all-gather over NVLink")
     args = ap.parse_args()
     if args.warmup < 3:

@@ -699,6 +699,37 @@ void flag_wait_probe(const Tensor& flag, int64_t target, Tensor& status, Tensor&
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void ar_pull_norm(const Tensor& peer_acc, const Tensor& peer_flags, const Tensor& flags, Tensor& zero_buf,
+                  int64_t zero_rows, Tensor& h, const Tensor& norm_w, Tensor& out, Tensor& epoch, Tensor& cta_ctr,
+                  int64_t rank, int64_t world, double eps, Tensor& status) {
+  check_cuda(h, "h");
+  TORCH_CHECK(peer_acc.scalar_type() == at::kLong && peer_acc.numel() == world && peer_flags.numel() == world,
+              "b200.ar_pull_norm: peer tables");
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous() && out.is_contiguous() &&
+                  zero_buf.scalar_type() == at::kFloat && zero_buf.size(0) >= zero_rows,
+              "b200.ar_pull_norm: buffers");
+  c10::cuda::CUDAGuard g(h.device());
+  b200::PullNormArgs a{};
+  a.peer_acc = reinterpret_cast<const float* const*>(peer_acc.data_ptr<int64_t>());
+  a.peer_flags = reinterpret_cast<unsigned* const*>(peer_flags.data_ptr<int64_t>());
+  a.flags = reinterpret_cast<const unsigned*>(flags.data_ptr<int32_t>());
+  a.zero_buf = zero_buf.data_ptr<float>();
+  a.zero_rows = (int)zero_rows;
+  a.h = h.data_ptr();
+  a.norm_w = norm_w.data_ptr();
+  a.out = out.data_ptr();
+  a.epoch = reinterpret_cast<unsigned*>(epoch.data_ptr<int32_t>());
+  a.cta_ctr = reinterpret_cast<unsigned*>(cta_ctr.data_ptr<int32_t>());
+  a.M = (int)h.size(0);
+  a.H = (int)h.size(1);
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.eps = (float)eps;
+  a.status = status.data_ptr<int>();
+  b200::ar_pull_norm_launch(a, cur_stream(h));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
   m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none(),
@@ -706,6 +737,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gate_r2") = 1);
   m.def("gemm", &gemm);
   m.def("flag_wait_probe", &flag_wait_probe);
+  m.def("ar_pull_norm", &ar_pull_norm);
   m.def("ln_modulate", &ln_modulate);
   m.def("dit_qk_rope", &dit_qk_rope);
   m.def("moe_route", &moe_route);

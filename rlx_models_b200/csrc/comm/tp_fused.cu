@@ -272,3 +272,111 @@ void flag_wait_probe_launch(const unsigned* flag, unsigned target, int* status, 
   flag_wait_probe_kernel<<<1, 32, 0, st>>>(flag, target, status, ok);
 }
 }  // namespace b200
+
+namespace b200 {
+namespace tpc {
+// Pull all-reduce + residual add + RMSNorm for decode-sized steps (M <= 128).
+//
+// Every rank's row-parallel GEMM accumulates its fp32 partial into its own
+// slot of the symmetric heap (local red.add, no NVLink traffic in the GEMM).
+// This kernel: CTA 0 announces "partial ready" by writing this op's epoch into
+// every rank's flag[my rank] (release, system scope); every CTA waits until all
+// ranks announced, then row r is reduced by reading the world partials
+// straight from peer memory (P2P loads over NVLink), the residual is added and
+// the row normalised. Finally the CTA zeroes row r of its own *previous*
+// parity accumulator, which every rank has finished reading (they all passed
+// this op's barrier, hence finished the previous op), so the next GEMM can
+// accumulate into it. One barrier per op; no NCCL call.
+constexpr int kPullThreads = 256;
+
+__global__ void __launch_bounds__(kPullThreads) ar_pull_norm_kernel(PullNormArgs a) {
+  __shared__ float red[kPullThreads / 32];
+  pdl_wait();
+  pdl_trigger();
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(a.epoch) + 1u;
+  if (blockIdx.x == 0 && threadIdx.x < (unsigned)a.world)
+    st_release_sys_u32(a.peer_flags[threadIdx.x] + a.rank, e);
+  if (threadIdx.x < (unsigned)a.world) wait_flag_geq(a.flags + threadIdx.x, e, a.status, 500 + threadIdx.x);
+  __syncthreads();
+  const int r = blockIdx.x;
+  const int H = a.H;
+  if (r < a.M) {
+    __nv_bfloat16* hbuf = reinterpret_cast<__nv_bfloat16*>(a.h);
+    const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+    constexpr int kMaxChunks = 4;  // H <= 256 * 8 * 4
+    const int nch = H / (kPullThreads * 8);
+    float v[kMaxChunks][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      if (c >= nch) break;
+      const int col = (c * kPullThreads + threadIdx.x) * 8;
+      float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int q = 0; q < a.world; ++q) {
+        const float4* src = reinterpret_cast<const float4*>(a.peer_acc[q] + (int64_t)r * H + col);
+        const float4 x0 = __ldcv(src), x1 = __ldcv(src + 1);  // peer memory: bypass stale cache lines
+        s[0] += x0.x; s[1] += x0.y; s[2] += x0.z; s[3] += x0.w;
+        s[4] += x1.x; s[5] += x1.y; s[6] += x1.z; s[7] += x1.w;
+      }
+      const uint4 hv = *reinterpret_cast<const uint4*>(hbuf + (int64_t)r * H + col);
+      const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        o[k] = pack_bf16x2(bf16_lo(hw[k]) + __bfloat162float(__float2bfloat16(s[2 * k])),
+                           bf16_hi(hw[k]) + __bfloat162float(__float2bfloat16(s[2 * k + 1])));
+        v[c][2 * k] = bf16_lo(o[k]);
+        v[c][2 * k + 1] = bf16_hi(o[k]);
+        ss += v[c][2 * k] * v[c][2 * k] + v[c][2 * k + 1] * v[c][2 * k + 1];
+      }
+      *reinterpret_cast<uint4*>(hbuf + (int64_t)r * H + col) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < kPullThreads / 32 ? red[threadIdx.x] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = rsqrtf(red[0] / (float)H + a.eps);
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      if (c >= nch) break;
+      const int col = (c * kPullThreads + threadIdx.x) * 8;
+      const uint4 wv = *reinterpret_cast<const uint4*>(nw + col);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        o[k] = pack_bf16x2(v[c][2 * k] * inv * bf16_lo(ww[k]), v[c][2 * k + 1] * inv * bf16_hi(ww[k]));
+      *reinterpret_cast<uint4*>(out + (int64_t)r * H + col) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  if (r < a.zero_rows) {
+    float4* z = reinterpret_cast<float4*>(a.zero_buf + (int64_t)r * H);
+    for (int i = threadIdx.x; i < H / 4; i += kPullThreads) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  // the last CTA publishes this op's epoch for the next op
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(a.cta_ctr, 1u) == gridDim.x - 1) {
+      *a.cta_ctr = 0;
+      *a.epoch = e;
+    }
+  }
+}
+}  // namespace tpc
+
+void ar_pull_norm_launch(const PullNormArgs& a, cudaStream_t st) {
+  if (a.H % (tpc::kPullThreads * 8) != 0 || a.H > tpc::kPullThreads * 8 * 4)
+    throw std::runtime_error("b200.ar_pull_norm: hidden must be a multiple of 2048 and <= 8192");
+  launch_pdl(tpc::ar_pull_norm_kernel, dim3(std::max(std::max(1, a.M), a.zero_rows)), dim3(tpc::kPullThreads), 0,
+             st, a);
+}
+}  // namespace b200

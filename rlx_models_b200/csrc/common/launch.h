@@ -114,6 +114,24 @@ struct OsReduceArgs {
 };
 void os_reduce_norm_launch(const OsReduceArgs& a, cudaStream_t st);
 
+// pull all-reduce + residual add + RMSNorm (decode steps): see tp_fused.cu
+struct PullNormArgs {
+  const float* const* peer_acc;  // [world] each rank's fp32 [rows][H] partial (this op's parity)
+  unsigned* const* peer_flags;   // [world] each rank's flag array [world]
+  const unsigned* flags;         // local flags [world]
+  float* zero_buf;               // own previous-parity accumulator
+  int zero_rows;
+  void* h;                       // [M][H] bf16 replicated residual (in/out)
+  const void* norm_w;
+  void* out;                     // [M][H] bf16
+  unsigned* epoch;
+  unsigned* cta_ctr;
+  int M, H, world, rank;
+  float eps;
+  int* status;
+};
+void ar_pull_norm_launch(const PullNormArgs& a, cudaStream_t st);
+
 // ---------------- norms / rope / embedding ----------------
 void embedding_launch(const int32_t* ids, const void* table, void* out, int64_t T, int64_t H, int64_t V,
                       cudaStream_t st);

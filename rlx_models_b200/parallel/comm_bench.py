@@ -42,7 +42,7 @@ def main():
     w = (torch.randn(H, K, device=dev, generator=g) * 0.02).bfloat16()
     nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
     res = {}
-    for kind in ("nccl", "fused"):
+    for kind in ("nccl", "fused", "pull"):
         comm = make_tp_comm(kind, rank, world, dev, 1e-6, max_tokens=max(M, 128), hidden=H)
         ids = torch.zeros(M, dtype=torch.int32, device=dev)
         table = torch.randn(8, H, device=dev).bfloat16()

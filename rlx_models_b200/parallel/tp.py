@@ -86,4 +86,7 @@ def make_tp_comm(kind: str, rank: int, world: int, device, eps: float = 1e-6, **
     if kind == "fused":
         from .fused_tp import FusedTPComm
         return FusedTPComm(rank, world, device, eps, **kw)
+    if kind == "pull":
+        from .pull_tp import PullTPComm
+        return PullTPComm(rank, world, device, eps, **kw)
     raise ValueError(kind)

@@ -57,7 +57,7 @@ def main():
 
     ref_logits = ref.forward(fb(), ref.make_kv_cache(nb))
     ok_all = True
-    for kind in ("nccl", "fused"):
+    for kind in ("nccl", "fused", "pull"):
         comm = make_tp_comm(kind, rank, world, dev, cfg.rms_norm_eps, max_tokens=512, hidden=cfg.hidden_size)
         m = DecoderLM(cfg, w, device=dev, tp_rank=rank, tp_size=world, comm=comm)
         lg_local = m.forward(fb(), m.make_kv_cache(nb))
