@@ -592,6 +592,7 @@ void prefill_attention_launch(const AttnArgs& a, cudaStream_t st) {
     fmha_launch(a, st);
     return;
   }
+  if (a.kv_dense) throw std::runtime_error("b200.prefill_attention: row-major K/V needs the tcgen05 kernel (D 128)");
   const int G = a.Hq / a.Hkv;
   if (a.Hq % a.Hkv != 0 || 128 % G != 0) throw std::runtime_error("b200.prefill_attention: G must divide 128");
   if (a.D != 128 && a.D != 64) throw std::runtime_error("b200.prefill_attention: D must be 64 or 128");

@@ -161,17 +161,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive_expect_tx(&k_full[s], kKV);
         for (int pg = 0; pg < kBN / 16; ++pg) {
           const int blk = btab[min(page0 + pg, max_page - 1)];  // pages past the context are masked
-          const int row = (blk * a.Hkv + hkv) * 16;
 #pragma unroll
-          for (int h = 0; h < 2; ++h) tma_load_2d(st + h * kHalf + pg * 2048, &tmK, &k_full[s], h * 64, row);
+          for (int h = 0; h < 2; ++h) {
+            if (a.kv_dense)
+              tma_load_3d(st + h * kHalf + pg * 2048, &tmK, &k_full[s], h * 64, hkv, blk * 16);
+            else
+              tma_load_2d(st + h * kHalf + pg * 2048, &tmK, &k_full[s], h * 64, (blk * a.Hkv + hkv) * 16);
+          }
         }
         mbar_arrive_expect_tx(&v_full[s], kKV);
         for (int pg = 0; pg < kBN / 16; ++pg) {
           const int blk = btab[min(page0 + pg, max_page - 1)];
-          const int row = (blk * a.Hkv + hkv) * 16;
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
-            tma_load_2d(st + kKV + h * kHalf + pg * 2048, &tmV, &v_full[s], h * 64, row);
+          for (int h = 0; h < 2; ++h) {
+            if (a.kv_dense)
+              tma_load_3d(st + kKV + h * kHalf + pg * 2048, &tmV, &v_full[s], h * 64, hkv, blk * 16);
+            else
+              tma_load_2d(st + kKV + h * kHalf + pg * 2048, &tmV, &v_full[s], h * 64, (blk * a.Hkv + hkv) * 16);
+          }
         }
         if (++s == kNST) {
           s = 0;
@@ -374,11 +381,19 @@ void fmha_launch(const AttnArgs& a, cudaStream_t st) {
   using namespace fmha;
   const int G = a.Hq / a.Hkv;
   const int rows_tok = 128 / G;
-  const int64_t kv_rows = a.num_blocks * a.Hkv * 16;
   CUtensorMap tq = make_tmap_3d(a.q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kD, a.Hq, a.q_rows, kD,
                                 (uint64_t)a.Hq * kD, 64, G, 16);
-  CUtensorMap tk = make_tmap_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv_rows, kD, kD, 16, 64);
-  CUtensorMap tv = make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv_rows, kD, kD, 16, 64);
+  CUtensorMap tk, tv;
+  if (a.kv_dense) {  // [rows, Hkv, D]: one 16-row page of one head = box [16][1][64]
+    tk = make_tmap_3d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kD, a.Hkv, a.kv_rows, kD,
+                      (uint64_t)a.Hkv * kD, 64, 1, 16);
+    tv = make_tmap_3d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kD, a.Hkv, a.kv_rows, kD,
+                      (uint64_t)a.Hkv * kD, 64, 1, 16);
+  } else {
+    const int64_t kv_rows = a.num_blocks * a.Hkv * 16;
+    tk = make_tmap_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv_rows, kD, kD, 16, 64);
+    tv = make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv_rows, kD, kD, 16, 64);
+  }
   const int q_tiles = (a.max_q_len + rows_tok - 1) / rows_tok;
   static bool once = false;
   if (!once) {

@@ -26,7 +26,7 @@ void check_cuda(const Tensor& t, const char* name) {
 void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const optional<Tensor>& residual,
             const optional<Tensor>& bias, double alpha, Tensor& ws, Tensor& sem, Tensor& status, int64_t swap,
             int64_t bn, int64_t splits, const optional<Tensor>& trace, int64_t act_from, const optional<Tensor>& gate,
-            int64_t gate_split, int64_t gate_r1, int64_t gate_r2) {
+            int64_t gate_split, int64_t gate_r1, int64_t gate_r2, int64_t gate_off) {
   check_cuda(x, "x");
   check_cuda(w, "w");
   check_cuda(out, "out");
@@ -91,6 +91,7 @@ void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const o
     a.gate_split = (int)gate_split;
     a.gate_r1 = (int)gate_r1;
     a.gate_r2 = (int)gate_r2;
+    a.gate_off = (int)gate_off;
   }
   b200::linear_launch(a, cur_stream(x));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -176,9 +177,13 @@ static b200::AttnArgs attn_args(const Tensor& q, const Tensor& k_cache, const Te
                                 const optional<Tensor>& sinks, int64_t window, double scale, Tensor& status) {
   check_cuda(q, "q");
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.dim() == 3 && q.is_contiguous(), "b200.attention: q [T,Hq,D]");
-  TORCH_CHECK(k_cache.dim() == 4 && v_cache.dim() == 4 && k_cache.is_contiguous() && v_cache.is_contiguous(),
-              "b200.attention: caches [NB,Hkv,16,D]");
-  TORCH_CHECK(k_cache.size(2) == 16 && k_cache.size(3) == q.size(2), "b200.attention: cache block/head dim");
+  const bool dense = k_cache.dim() == 3;  // prefill only: row-major [rows, Hkv, D] (pages of 16 rows)
+  TORCH_CHECK((k_cache.dim() == 4 || dense) && v_cache.dim() == k_cache.dim() && k_cache.is_contiguous() &&
+                  v_cache.is_contiguous(),
+              "b200.attention: caches [NB,Hkv,16,D] (or [rows,Hkv,D] for prefill)");
+  TORCH_CHECK(dense ? (k_cache.size(0) % 16 == 0 && k_cache.size(2) == q.size(2))
+                    : (k_cache.size(2) == 16 && k_cache.size(3) == q.size(2)),
+              "b200.attention: cache block/head dim");
   TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.dim() == 2 && block_tables.is_contiguous(),
               "b200.attention: block_tables int32 [B, max_blocks]");
   TORCH_CHECK(ctx_lens.scalar_type() == at::kInt && ctx_lens.numel() == block_tables.size(0),
@@ -193,7 +198,7 @@ static b200::AttnArgs attn_args(const Tensor& q, const Tensor& k_cache, const Te
   a.q = q.data_ptr();
   a.k_cache = k_cache.data_ptr();
   a.v_cache = v_cache.data_ptr();
-  a.num_blocks = k_cache.size(0);
+  a.num_blocks = dense ? k_cache.size(0) / 16 : k_cache.size(0);
   a.block_tables = block_tables.data_ptr<int32_t>();
   a.max_blocks = (int)block_tables.size(1);
   a.ctx_lens = ctx_lens.data_ptr<int32_t>();
@@ -236,6 +241,10 @@ void prefill_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_c
   a.causal = causal ? 1 : 0;
   a.q_paged = q_paged ? 1 : 0;
   a.q_rows = q.size(0);
+  if (k_cache.dim() == 3) {  // row-major [rows, Hkv, D] keys / values
+    a.kv_dense = 1;
+    a.kv_rows = k_cache.size(0);
+  }
   if (out.dim() == 2) {  // [rows, Hq * D] view with a row stride (DiT: a column slice of a wider buffer)
     TORCH_CHECK(out.stride(1) == 1 && out.size(1) == a.Hq * a.D && out.stride(0) % 8 == 0,
                 "b200.prefill: 2-D out must be [rows, Hq * D] with unit inner stride");
@@ -645,7 +654,7 @@ void moe_gemm(const Tensor& x, const Tensor& w, const Tensor& row_exp, int64_t N
 
 // x [rows, H] (row stride), mod [B, *] bf16: out = LN(x) * (1 + mod[b][scale_off:]) + mod[b][shift_off:]
 void ln_modulate(const Tensor& x, Tensor& out, const Tensor& mod, int64_t shift_off, int64_t scale_off, double eps,
-                 int64_t split, int64_t r1, int64_t r2) {
+                 int64_t split, int64_t r1, int64_t r2, int64_t row_off) {
   check_cuda(x, "x");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16 &&
                   mod.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1 &&
@@ -659,20 +668,20 @@ void ln_modulate(const Tensor& x, Tensor& out, const Tensor& mod, int64_t shift_
   c10::cuda::CUDAGuard g(x.device());
   b200::ln_modulate_launch(x.data_ptr(), x.stride(0), out.data_ptr(), out.stride(0), mod.data_ptr(), mod.stride(0),
                            (int)shift_off, (int)scale_off, (int)x.size(0), (int)H, (float)eps, (int)split, (int)r1,
-                           (int)r2, cur_stream(x));
+                           (int)r2, (int)row_off, cur_stream(x));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // qkv [rows, 3 H] (row stride) -> q [rows, heads, 128], k/v pages [rows/16, heads, 16, 128]
 void dit_qk_rope(const Tensor& qkv, int64_t heads, const Tensor& scales_txt, const Tensor& scales_img,
                  const Tensor& cos_t, const Tensor& sin_t, int64_t split, int64_t Lt, int64_t Li, double eps,
-                 Tensor& q_out, Tensor& k_pages, Tensor& v_pages) {
+                 Tensor& q_out, Tensor& k_pages, Tensor& v_pages, int64_t row_off, int64_t kv_groups) {
   check_cuda(qkv, "qkv");
   const int64_t rows = qkv.size(0);
   TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 && qkv.stride(1) == 1 && qkv.size(1) >= 3 * heads * 128 &&
                   qkv.stride(0) % 4 == 0,
               "b200.dit_qk_rope: qkv [rows, 3 * heads * 128]");
-  TORCH_CHECK(rows % 16 == 0 && q_out.is_contiguous() && k_pages.is_contiguous() && v_pages.is_contiguous() &&
+  TORCH_CHECK((rows % 16 == 0 || kv_groups > 0) && (kv_groups == 0 || heads % kv_groups == 0) && q_out.is_contiguous() && k_pages.is_contiguous() && v_pages.is_contiguous() &&
                   q_out.numel() == rows * heads * 128 && k_pages.numel() == rows * heads * 128 &&
                   v_pages.numel() == rows * heads * 128,
               "b200.dit_qk_rope: outputs");
@@ -686,7 +695,7 @@ void dit_qk_rope(const Tensor& qkv, int64_t heads, const Tensor& scales_txt, con
   b200::dit_qk_rope_launch(qkv.data_ptr(), qkv.stride(0), (int)rows, (int)heads, scales_txt.data_ptr(),
                            scales_img.data_ptr(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), (int)split,
                            (int)Lt, (int)Li, (float)eps, q_out.data_ptr(), k_pages.data_ptr(), v_pages.data_ptr(),
-                           cur_stream(qkv));
+                           (int)row_off, (int)kv_groups, cur_stream(qkv));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -734,12 +743,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
   m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none(),
         py::arg("act_from") = -1, py::arg("gate") = py::none(), py::arg("gate_split") = 0, py::arg("gate_r1") = 1,
-        py::arg("gate_r2") = 1);
+        py::arg("gate_r2") = 1, py::arg("gate_off") = 0);
   m.def("gemm", &gemm);
   m.def("flag_wait_probe", &flag_wait_probe);
   m.def("ar_pull_norm", &ar_pull_norm);
-  m.def("ln_modulate", &ln_modulate);
-  m.def("dit_qk_rope", &dit_qk_rope);
+  m.def("ln_modulate", &ln_modulate, py::arg("x"), py::arg("out"), py::arg("mod"), py::arg("shift_off"),
+        py::arg("scale_off"), py::arg("eps"), py::arg("split"), py::arg("r1"), py::arg("r2"), py::arg("row_off") = 0);
+  m.def("dit_qk_rope", &dit_qk_rope, py::arg("qkv"), py::arg("heads"), py::arg("scales_txt"), py::arg("scales_img"),
+        py::arg("cos_t"), py::arg("sin_t"), py::arg("split"), py::arg("Lt"), py::arg("Li"), py::arg("eps"),
+        py::arg("q_out"), py::arg("k_pages"), py::arg("v_pages"), py::arg("row_off") = 0, py::arg("kv_groups") = 0);
   m.def("moe_route", &moe_route);
   m.def("moe_align", &moe_align);
   m.def("moe_gather", &moe_gather);

@@ -45,7 +45,7 @@ struct LinearArgs {
   int act = 0, act_from = 0;
   const void* gate = nullptr;
   int64_t gate_ld = 0;
-  int gate_split = 0, gate_r1 = 1, gate_r2 = 1;
+  int gate_split = 0, gate_r1 = 1, gate_r2 = 1, gate_off = 0;
 };
 void linear_launch(const LinearArgs& a, cudaStream_t st);
 
@@ -185,6 +185,8 @@ struct AttnArgs {
   int q_paged = 0;           // prefill: query / output row of token t = block_tables[b][t / 16] * 16 + t % 16
   int64_t out_ld = 0;        // prefill: output row stride in elements (0 = Hq * D)
   int64_t q_rows = 0;        // prefill: rows of q (bounds of its TMA map)
+  int kv_dense = 0;          // prefill: k/v row-major [kv_rows, Hkv, D] (pages = 16 consecutive rows)
+  int64_t kv_rows = 0;
   float* ws;                 // decode split workspace
   int64_t ws_elems;
   int* status;
@@ -243,10 +245,13 @@ void flag_wait_probe_launch(const unsigned* flag, unsigned target, int* status, 
 // ---------------- DiT (FLUX) ----------------
 void ln_modulate_launch(const void* x, int64_t ldx, void* out, int64_t ldo, const void* mod, int64_t ld_mod,
                         int shift_off, int scale_off, int rows, int H, float eps, int split, int r1, int r2,
-                        cudaStream_t st);
+                        int row_off, cudaStream_t st);
+// kv_groups == 0: q row-major [rows, heads, 128], k/v in 16-row pages [rows/16, heads, 16, 128];
+// kv_groups  > 0: q, k, v all in head-group-major [groups][rows][heads/groups][128] (all-to-all ready)
 void dit_qk_rope_launch(const void* qkv, int64_t ld, int rows, int heads, const void* scales_txt,
                         const void* scales_img, const float* cos_t, const float* sin_t, int split, int Lt, int Li,
-                        float eps, void* q_out, void* k_pages, void* v_pages, cudaStream_t st);
+                        float eps, void* q_out, void* k_pages, void* v_pages, int row_off, int kv_groups,
+                        cudaStream_t st);
 
 // ---------------- sampling ----------------
 void argmax_launch(const float* logits, int64_t ld, int64_t B, int64_t V, int32_t* out, cudaStream_t st);

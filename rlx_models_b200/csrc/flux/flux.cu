@@ -49,7 +49,7 @@ __device__ __forceinline__ float block_sum(float s, float* red) {
 
 __global__ void ln_modulate_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, __nv_bfloat16* __restrict__ out,
                                    int64_t ldo, const __nv_bfloat16* __restrict__ mod, int64_t ld_mod, int shift_off,
-                                   int scale_off, int H, float eps, int split, int r1, int r2) {
+                                   int scale_off, int H, float eps, int split, int r1, int r2, int row_off) {
   pdl_wait();
   pdl_trigger();
   __shared__ float red[32];
@@ -83,7 +83,7 @@ __global__ void ln_modulate_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
   }
   const float rstd = rsqrtf(block_sum(q, red) / H + eps);
   if (!active) return;
-  const int b = batch_of(row, split, r1, r2);
+  const int b = batch_of(row + row_off, split, r1, r2);
   const __nv_bfloat16* m = mod + (int64_t)b * ld_mod;
   const uint4 sh = *reinterpret_cast<const uint4*>(m + shift_off + c0);
   const uint4 sc = *reinterpret_cast<const uint4*>(m + scale_off + c0);
@@ -105,7 +105,7 @@ __global__ void dit_qk_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_
                                    const __nv_bfloat16* __restrict__ scales_img, const float* __restrict__ cos_t,
                                    const float* __restrict__ sin_t, int split, int Lt, int Li, float eps,
                                    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_pages,
-                                   __nv_bfloat16* __restrict__ v_pages) {
+                                   __nv_bfloat16* __restrict__ v_pages, int row_off, int kv_groups) {
   pdl_wait();
   pdl_trigger();
   constexpr int D = 128;
@@ -113,8 +113,9 @@ __global__ void dit_qk_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_
   const int lane = threadIdx.x & 31;
   if (gw >= (int64_t)rows * heads) return;
   const int row = (int)(gw / heads), head = (int)(gw % heads);
-  const int pos = row < split ? row % Lt : Lt + (row - split) % Li;
-  const __nv_bfloat16* sc = row < split ? scales_txt : scales_img;
+  const int grow = row + row_off;  // row in the global stream-major order
+  const int pos = grow < split ? grow % Lt : Lt + (grow - split) % Li;
+  const __nv_bfloat16* sc = grow < split ? scales_txt : scales_img;
   const int d0 = lane * 4;
   // rope: dims d < 64 pair with d + 64 (lane ^ 16); angle index d % 64
   const float4 cs = *reinterpret_cast<const float4*>(cos_t + (int64_t)pos * (D / 2) + (d0 & 63));
@@ -123,7 +124,15 @@ __global__ void dit_qk_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_
   const bool lo = lane < 16;
   const __nv_bfloat16* src = qkv + (int64_t)row * ld + head * D + d0;
   const int H = heads * D;
-  const int64_t page = ((int64_t)(row >> 4) * heads + head) * 16 + (row & 15);
+  int64_t page, qoff;
+  if (kv_groups > 0) {  // [groups][rows][heads per group][D]
+    const int hpg = heads / kv_groups;
+    page = ((int64_t)(head / hpg) * rows + row) * hpg + head % hpg;
+    qoff = page;
+  } else {
+    page = ((int64_t)(row >> 4) * heads + head) * 16 + (row & 15);
+    qoff = (int64_t)row * heads + head;
+  }
 #pragma unroll
   for (int which = 0; which < 2; ++which) {  // q, k
     const uint2 w = *reinterpret_cast<const uint2*>(src + which * H);
@@ -145,7 +154,7 @@ __global__ void dit_qk_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_
     }
     const uint2 o = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
     if (which == 0)
-      *reinterpret_cast<uint2*>(q_out + ((int64_t)row * heads + head) * D + d0) = o;
+      *reinterpret_cast<uint2*>(q_out + qoff * D + d0) = o;
     else
       *reinterpret_cast<uint2*>(k_pages + page * D + d0) = o;
   }
@@ -156,25 +165,27 @@ __global__ void dit_qk_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_
 
 void ln_modulate_launch(const void* x, int64_t ldx, void* out, int64_t ldo, const void* mod, int64_t ld_mod,
                         int shift_off, int scale_off, int rows, int H, float eps, int split, int r1, int r2,
-                        cudaStream_t st) {
+                        int row_off, cudaStream_t st) {
   if (rows == 0) return;
   if (H % 8 != 0 || H / 8 > 1024) throw std::runtime_error("b200.ln_modulate: H % 8 == 0 and H <= 8192");
   const int threads = ((H / 8 + 31) / 32) * 32;
   launch_pdl(flux::ln_modulate_kernel, dim3(rows), dim3(threads), 0, st, reinterpret_cast<const __nv_bfloat16*>(x),
              ldx, reinterpret_cast<__nv_bfloat16*>(out), ldo, reinterpret_cast<const __nv_bfloat16*>(mod), ld_mod,
-             shift_off, scale_off, H, eps, split, std::max(1, r1), std::max(1, r2));
+             shift_off, scale_off, H, eps, split, std::max(1, r1), std::max(1, r2), row_off);
 }
 
 void dit_qk_rope_launch(const void* qkv, int64_t ld, int rows, int heads, const void* scales_txt,
                         const void* scales_img, const float* cos_t, const float* sin_t, int split, int Lt, int Li,
-                        float eps, void* q_out, void* k_pages, void* v_pages, cudaStream_t st) {
+                        float eps, void* q_out, void* k_pages, void* v_pages, int row_off, int kv_groups,
+                        cudaStream_t st) {
   if (rows == 0) return;
   const int64_t warps = (int64_t)rows * heads;
   launch_pdl(flux::dit_qk_rope_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, st,
              reinterpret_cast<const __nv_bfloat16*>(qkv), ld, rows, heads,
              reinterpret_cast<const __nv_bfloat16*>(scales_txt), reinterpret_cast<const __nv_bfloat16*>(scales_img),
              cos_t, sin_t, split, std::max(1, Lt), std::max(1, Li), eps, reinterpret_cast<__nv_bfloat16*>(q_out),
-             reinterpret_cast<__nv_bfloat16*>(k_pages), reinterpret_cast<__nv_bfloat16*>(v_pages));
+             reinterpret_cast<__nv_bfloat16*>(k_pages), reinterpret_cast<__nv_bfloat16*>(v_pages), row_off,
+             kv_groups);
 }
 
 }  // namespace b200

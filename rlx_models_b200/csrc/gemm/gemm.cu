@@ -144,6 +144,7 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
   p.gate_split = a.gate_split;
   p.gate_r1 = std::max(1, a.gate_r1);
   p.gate_r2 = std::max(1, a.gate_r2);
+  p.gate_off = a.gate_off;
   if (dit_epi && (epi != gemm::EPI_BF16 || p.splits > 1))
     throw std::runtime_error("b200.linear: GELU / gate epilogues need bf16 output without split-K");
   if (p.peer_out != nullptr && (p.rpr <= 0 || p.done_ctr == nullptr || p.peer_flags == nullptr || p.epoch == nullptr))

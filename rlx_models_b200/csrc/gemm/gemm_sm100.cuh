@@ -72,11 +72,11 @@ struct Params {
   // Normal orientation only (adaLN DiT blocks):
   //   act = 1: GELU (tanh form), 2: ReLU, on output columns j >= act_from, after the bias;
   //   gate != null: y = gate[batch(i)][j] * y before the residual is added, with
-  //   batch(i) = i < gate_split ? i / gate_r1 : (i - gate_split) / gate_r2.
+  //   batch(i) = g < gate_split ? g / gate_r1 : (g - gate_split) / gate_r2 with g = i + gate_off.
   int act, act_from;
   const __nv_bfloat16* gate;
   int64_t gate_ld;
-  int gate_split, gate_r1, gate_r2;
+  int gate_split, gate_r1, gate_r2, gate_off;
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -149,7 +149,8 @@ __device__ __forceinline__ void store_chunk(const Params& p, int i, int j0, floa
       if (j0 + t >= p.act_from) v[t] = p.act == 1 ? gelu_tanh(v[t]) : fmaxf(v[t], 0.f);
   }
   if (p.gate != nullptr) {
-    const int gb = i < p.gate_split ? i / p.gate_r1 : (i - p.gate_split) / p.gate_r2;
+    const int gi = i + p.gate_off;
+    const int gb = gi < p.gate_split ? gi / p.gate_r1 : (gi - p.gate_split) / p.gate_r2;
     const __nv_bfloat16* g = p.gate + (int64_t)gb * p.gate_ld;
     if (full && ((reinterpret_cast<uintptr_t>(g + j0) & 15u) == 0)) {
 #pragma unroll
@@ -252,7 +253,8 @@ __device__ __forceinline__ void store_vec(const Params& p, int j, int fo, int nf
       if (fo + t >= p.act_from) o[t] = p.act == 1 ? gelu_tanh(o[t]) : fmaxf(o[t], 0.f);
   }
   if (p.gate != nullptr) {
-    const int gb = j < p.gate_split ? j / p.gate_r1 : (j - p.gate_split) / p.gate_r2;
+    const int gj = j + p.gate_off;
+    const int gb = gj < p.gate_split ? gj / p.gate_r1 : (gj - p.gate_split) / p.gate_r2;
 #pragma unroll
     for (int t = 0; t < NV; ++t)
       if (fo + t < nfeat) o[t] *= __bfloat162float(p.gate[(int64_t)gb * p.gate_ld + fo + t]);

@@ -16,6 +16,15 @@ so the single block's linear2 input concat(attn, gelu(mlp)) is the slice
 Y[:, 3H:] once linear2's columns are stored in [mlp | attn] order, and its
 linear1 writes qkv and the GELU'd MLP hidden with one GEMM.
 
+Sequence parallelism (Ulysses): with ``sp_size`` ranks each holds a
+contiguous block of R / sp rows of the stream-major row space (weights are
+replicated) and runs every GEMM, norm and modulation on its rows only (row
+offsets map local rows to their batch and joint position). Around each joint
+attention, q/k/v are written head-group-major and exchanged with one NCCL
+all-to-all each, so every rank attends over all rows for heads / sp heads;
+a second all-to-all returns the output rows. The final layer's image rows are
+all-gathered so every rank holds the full velocity.
+
 Fused epilogues carry the adaLN residual algebra: ``x += gate[b] * (y W^T + bias)``
 (gated residual) and GELU-tanh; LayerNorm + modulate is one kernel. All
 modulation vectors of a step come from a single GEMM over the concatenated
@@ -29,6 +38,7 @@ from __future__ import annotations
 import math
 
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 
 from .. import ops
@@ -39,9 +49,10 @@ from .flux_common import (deinterleave_perm, euler, pack, position_ids, rope_tab
 
 
 class FluxDiT:
-    def __init__(self, cfg: FluxConfig, weights, device="cuda"):
+    def __init__(self, cfg: FluxConfig, weights, device="cuda", sp_rank: int = 0, sp_size: int = 1, sp_group=None):
         assert cfg.head_dim == 128, "the DiT QK-norm/RoPE kernel is written for head_dim 128"
         self.cfg = cfg
+        self.sp_rank, self.sp_size, self.sp_group = sp_rank, sp_size, sp_group
         self.device = torch.device(device)
         H, M = cfg.hidden_size, cfg.mlp_hidden
         dev, bf = self.device, torch.bfloat16
@@ -110,11 +121,16 @@ class FluxDiT:
         key = (B, Lt, Li, h, w)
         if self._bufs is not None and self._bufs["key"] == key:
             return self._bufs
-        c, dev = self.cfg, self.device
+        c, dev, sp = self.cfg, self.device, self.sp_size
         assert Lt % 16 == 0 and Li % 16 == 0, "text and image lengths must be multiples of 16"
         H, M = c.hidden_size, c.mlp_hidden
         R = B * (Lt + Li)
         Lj = Lt + Li
+        assert R % (16 * sp) == 0 and c.num_heads % sp == 0, "rows / heads must split evenly over the SP ranks"
+        Rl = R // sp
+        row0 = self.sp_rank * Rl
+        T = B * Lt
+        t_hi = min(max(T - row0, 0), Rl)  # local rows [0, t_hi) are text, [t_hi, Rl) image
         bt = torch.empty(B, Lj // 16, dtype=torch.int32)
         for b in range(B):
             bt[b, :Lt // 16] = torch.arange(Lt // 16) + b * Lt // 16
@@ -122,25 +138,33 @@ class FluxDiT:
         ids = position_ids(Lt, h, w)
         cos, sin = rope_tables(ids, c.axes_dim, c.theta)
         z = lambda *s, dt=torch.bfloat16: torch.zeros(*s, dtype=dt, device=dev)
-        self._bufs = dict(
-            key=key, B=B, Lt=Lt, Li=Li, R=R,
+        hpg = c.num_heads // sp
+        S = dict(
+            key=key, B=B, Lt=Lt, Li=Li, R=R, Rl=Rl, row0=row0, T=T, t_hi=t_hi, hpg=hpg,
             img=z(B * Li, c.in_channels), txt=z(B * Lt, c.context_in_dim), y=z(B, c.vec_in_dim),
-            temb=z(B, 256), gemb=z(B, 256), X=z(R, H), Xm=z(R, H), Y=z(R, 4 * H + M),
-            Q=z(R, c.num_heads, 128), K=z(R // 16, c.num_heads, 16, 128), V=z(R // 16, c.num_heads, 16, 128),
+            temb=z(B, 256), gemb=z(B, 256), X=z(Rl, H), Xm=z(Rl, H), Y=z(Rl, 4 * H + M),
             mods=z(B, self.n_mod), vel=z(B * Li, c.out_channels),
             btab=bt.to(dev), ctx=torch.full((B,), Lj, dtype=torch.int32, device=dev),
             cu=(torch.arange(B + 1, dtype=torch.int32) * Lj).to(dev),
             cos=cos.to(dev).contiguous(), sin=sin.to(dev).contiguous())
+        if sp == 1:
+            S.update(Q=z(R, c.num_heads, 128), K=z(R // 16, c.num_heads, 16, 128), V=z(R // 16, c.num_heads, 16, 128))
+        else:
+            # head-group-major per-rank q/k/v [sp][Rl][hpg][128] -> all-to-all -> [R][hpg][128]
+            S.update(Qg=z(sp, Rl, hpg, 128), Kg=z(sp, Rl, hpg, 128), Vg=z(sp, Rl, hpg, 128),
+                     Qa=z(R, hpg, 128), Ka=z(R, hpg, 128), Va=z(R, hpg, 128), Oa=z(R, hpg, 128),
+                     Ob=z(sp, Rl, hpg * 128), vel_all=z(R, c.out_channels), vel_loc=z(Rl, c.out_channels))
+        self._bufs = S
         self._graph = None
-        return self._bufs
+        return S
 
     # -- one velocity evaluation (reads the static input buffers) -----------------
     def _forward_static(self):
         c, S = self.cfg, self._bufs
-        B, Lt, Li, R = S["B"], S["Lt"], S["Li"], S["R"]
+        B, Lt, Li, Rl, row0, T, t_hi = S["B"], S["Lt"], S["Li"], S["Rl"], S["row0"], S["T"], S["t_hi"]
         H, M = c.hidden_size, c.mlp_hidden
         X, Xm, Y, mods = S["X"], S["Xm"], S["Y"], S["mods"]
-        T = B * Lt
+        sp = self.sp_size
 
         def lin(x, wb, **kw):
             return ops.linear(x, wb[0], bias=wb[1], **kw)
@@ -154,48 +178,75 @@ class FluxDiT:
             vec = vec + mlp_embed("guidance_in", S["gemb"])
         vec = vec + mlp_embed("vector_in", S["y"])
         lin(F.silu(vec), (self.mod_w, self.mod_b), out=mods)
-        lin(S["txt"], self.w["txt_in"], out=X[:T])
-        lin(S["img"], self.w["img_in"], out=X[T:])
-        rows = {"txt": (0, T, Lt), "img": (T, R, Li)}
+        # local rows: text rows [0, t_hi) = global text rows row0.., image rows [t_hi, Rl)
+        i0 = row0 + t_hi - T  # first global image row held here
+        if t_hi > 0:
+            lin(S["txt"][row0:row0 + t_hi], self.w["txt_in"], out=X[:t_hi])
+        if t_hi < Rl:
+            lin(S["img"][i0:i0 + Rl - t_hi], self.w["img_in"], out=X[t_hi:])
+        # per-stream local ranges: (r0, r1, stream length, global stream-row offset of r0)
+        rows = {"txt": (0, t_hi, Lt, row0), "img": (t_hi, Rl, Li, i0)}
         attn_out = Y[:, 3 * H + M:]
 
         def attention(scales_txt, scales_img):
+            ops._count(1)
+            if sp == 1:
+                ext().dit_qk_rope(Y[:, :3 * H], c.num_heads, scales_txt, scales_img, S["cos"], S["sin"], T, Lt, Li,
+                                  c.eps, S["Q"], S["K"], S["V"])
+                ops.prefill_attention(S["Q"], S["K"], S["V"], S["btab"], S["ctx"], S["cu"], Lt + Li,
+                                      scale=1.0 / math.sqrt(128), causal=False, q_paged=True, out=attn_out)
+                return
+            # Ulysses: rows -> heads all-to-all, joint attention over all rows for hpg heads, back
             ext().dit_qk_rope(Y[:, :3 * H], c.num_heads, scales_txt, scales_img, S["cos"], S["sin"], T, Lt, Li,
-                              c.eps, S["Q"], S["K"], S["V"])
-            ops._count(1)
-            ops.prefill_attention(S["Q"], S["K"], S["V"], S["btab"], S["ctx"], S["cu"], Lt + Li,
-                                  scale=1.0 / math.sqrt(128), causal=False, q_paged=True, out=attn_out)
+                              c.eps, S["Qg"], S["Kg"], S["Vg"], row_off=row0, kv_groups=sp)
+            for src, dst in (("Qg", "Qa"), ("Kg", "Ka"), ("Vg", "Va")):
+                dist.all_to_all_single(S[dst], S[src], group=self.sp_group)
+            ops.prefill_attention(S["Qa"], S["Ka"], S["Va"], S["btab"], S["ctx"], S["cu"], Lt + Li,
+                                  scale=1.0 / math.sqrt(128), causal=False, q_paged=True, out=S["Oa"])
+            dist.all_to_all_single(S["Ob"], S["Oa"], group=self.sp_group)
+            attn_out.copy_(S["Ob"].transpose(0, 1).reshape(Rl, H))
 
-        def ln_mod(r0, r1, off, split, ra, rb):
-            ext().ln_modulate(X[r0:r1], Xm[r0:r1], mods, off, off + H, c.eps, split, ra, rb)
-            ops._count(1)
+        def ln_mod(r0, r1, off, split, ra, rb, row_off):
+            if r1 > r0:
+                ext().ln_modulate(X[r0:r1], Xm[r0:r1], mods, off, off + H, c.eps, split, ra, rb, row_off)
+                ops._count(1)
 
         for i, blk in enumerate(self.double):
-            for s in ("txt", "img"):
-                r0, r1, L = rows[s]
-                o = self.mod_off[(i, s)]
-                ln_mod(r0, r1, o, 0, 1, L)
-                lin(Xm[r0:r1], blk[s]["qkv"], out=Y[r0:r1, :3 * H])
+            for st in ("txt", "img"):
+                r0, r1, L, goff = rows[st]
+                if r1 > r0:
+                    o = self.mod_off[(i, st)]
+                    ln_mod(r0, r1, o, 0, 1, L, goff)
+                    lin(Xm[r0:r1], blk[st]["qkv"], out=Y[r0:r1, :3 * H])
             attention(blk["txt"]["scales"], blk["img"]["scales"])
-            for s in ("txt", "img"):
-                r0, r1, L = rows[s]
-                o = self.mod_off[(i, s)]
-                lin(attn_out[r0:r1], blk[s]["proj"], out=X[r0:r1], residual=X[r0:r1],
-                    gate=mods[:, o + 2 * H:o + 3 * H], gate_rows=(0, 1, L))
-                ln_mod(r0, r1, o + 3 * H, 0, 1, L)
-                lin(Xm[r0:r1], blk[s]["mlp0"], out=Y[r0:r1, 3 * H:3 * H + M], gelu_from=0)
-                lin(Y[r0:r1, 3 * H:3 * H + M], blk[s]["mlp2"], out=X[r0:r1], residual=X[r0:r1],
-                    gate=mods[:, o + 5 * H:o + 6 * H], gate_rows=(0, 1, L))
+            for st in ("txt", "img"):
+                r0, r1, L, goff = rows[st]
+                if r1 <= r0:
+                    continue
+                o = self.mod_off[(i, st)]
+                lin(attn_out[r0:r1], blk[st]["proj"], out=X[r0:r1], residual=X[r0:r1],
+                    gate=mods[:, o + 2 * H:o + 3 * H], gate_rows=(0, 1, L, goff))
+                ln_mod(r0, r1, o + 3 * H, 0, 1, L, goff)
+                lin(Xm[r0:r1], blk[st]["mlp0"], out=Y[r0:r1, 3 * H:3 * H + M], gelu_from=0)
+                lin(Y[r0:r1, 3 * H:3 * H + M], blk[st]["mlp2"], out=X[r0:r1], residual=X[r0:r1],
+                    gate=mods[:, o + 5 * H:o + 6 * H], gate_rows=(0, 1, L, goff))
         for i, blk in enumerate(self.single):
             o = self.mod_off[("single", i)]
-            ln_mod(0, R, o, T, Lt, Li)
+            ln_mod(0, Rl, o, T, Lt, Li, row0)
             lin(Xm, blk["l1"], out=Y[:, :3 * H + M], gelu_from=3 * H)
             attention(blk["scales"], blk["scales"])
             lin(Y[:, 3 * H:], blk["l2"], out=X, residual=X, gate=mods[:, o + 2 * H:o + 3 * H],
-                gate_rows=(T, Lt, Li))
+                gate_rows=(T, Lt, Li, row0))
         o = self.mod_off["final"]
-        ln_mod(T, R, o, 0, 1, Li)
-        lin(Xm[T:], self.w["final_layer.linear"], out=S["vel"])
+        if sp == 1:
+            ln_mod(T, Rl, o, 0, 1, Li, 0)
+            lin(Xm[T:], self.w["final_layer.linear"], out=S["vel"])
+            return S["vel"]
+        # every local row through the final layer (text rows are discarded), then gather the image rows
+        ln_mod(0, Rl, o, T, Lt, Li, row0)
+        lin(Xm, self.w["final_layer.linear"], out=S["vel_loc"])
+        dist.all_gather_into_tensor(S["vel_all"], S["vel_loc"], group=self.sp_group)
+        S["vel"].copy_(S["vel_all"][T:])
         return S["vel"]
 
     # -- public ------------------------------------------------------------------

@@ -33,7 +33,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, out: torch.Tensor | None = None,
     DiT epilogues: ``gelu_from`` >= 0 applies GELU (tanh) to output columns
     >= gelu_from; ``gate`` [batches, N] multiplies the (biased) product before
     the residual add, row i using gate row ``i // r1`` below ``split`` and
-    ``(i - split) // r2`` above, with ``gate_rows = (split, r1, r2)``.
+    ``(i - split) // r2`` above, with ``gate_rows = (split, r1, r2[, row offset added to i])``.
     """
     M, N = x.shape[0], w.shape[0]
     if out is None:
@@ -44,7 +44,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, *, out: torch.Tensor | None = None,
     act_from = (1 << 30) if relu else int(gelu_from)
     ext().linear(x, w, out, mode, residual, bias, float(alpha), s.gemm_ws, s.gemm_sem, s.status,
                  swap, bn, splits, None, act_from, gate, int(gate_rows[0]), int(gate_rows[1]),
-                 int(gate_rows[2]))
+                 int(gate_rows[2]), int(gate_rows[3]) if len(gate_rows) > 3 else 0)
     return out
 
 

@@ -29,3 +29,8 @@ def test_pipeline_parallel_two_stages():
 
 def test_tensor_parallel_two_ranks():
     _torchrun("rlx_models_b200.parallel.tp_check", 2)
+
+
+def test_flux_sequence_parallel_two_ranks():
+    out = _torchrun("rlx_models_b200.parallel.flux_sp_check", 2)
+    assert '"ok": true' in out
