@@ -739,6 +739,43 @@ void ar_pull_norm(const Tensor& peer_acc, const Tensor& peer_flags, const Tensor
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void ep_combine_norm(const Tensor& peer_rows, const Tensor& peer_inv, const Tensor& peer_flags, const Tensor& flags,
+                     const Tensor& experts, int64_t e_local, Tensor& h, const Tensor& norm_w, Tensor& out,
+                     Tensor& epoch, Tensor& cta_ctr, int64_t rank, int64_t world, double eps, Tensor& status) {
+  check_cuda(h, "h");
+  TORCH_CHECK(peer_rows.scalar_type() == at::kLong && peer_rows.numel() == world && peer_inv.numel() == world &&
+                  peer_flags.numel() == world && flags.numel() >= world,
+              "b200.ep_combine_norm: peer tables");
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous() && out.is_contiguous() &&
+                  out.sizes() == h.sizes() && norm_w.numel() == h.size(1),
+              "b200.ep_combine_norm: h / out / norm_w");
+  TORCH_CHECK(experts.scalar_type() == at::kInt && experts.is_contiguous() && experts.dim() == 2 &&
+                  experts.size(0) == h.size(0),
+              "b200.ep_combine_norm: experts [T, k] int32");
+  c10::cuda::CUDAGuard g(h.device());
+  b200::EpCombineArgs a{};
+  a.peer_rows = reinterpret_cast<const void* const*>(peer_rows.data_ptr<int64_t>());
+  a.peer_inv = reinterpret_cast<const int32_t* const*>(peer_inv.data_ptr<int64_t>());
+  a.peer_flags = reinterpret_cast<unsigned* const*>(peer_flags.data_ptr<int64_t>());
+  a.flags = reinterpret_cast<const unsigned*>(flags.data_ptr<int32_t>());
+  a.experts = experts.data_ptr<int32_t>();
+  a.h = h.data_ptr();
+  a.norm_w = norm_w.data_ptr();
+  a.out = out.data_ptr();
+  a.epoch = reinterpret_cast<unsigned*>(epoch.data_ptr<int32_t>());
+  a.cta_ctr = reinterpret_cast<unsigned*>(cta_ctr.data_ptr<int32_t>());
+  a.T = (int)h.size(0);
+  a.k = (int)experts.size(1);
+  a.H = (int)h.size(1);
+  a.e_local = (int)e_local;
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.eps = (float)eps;
+  a.status = status.data_ptr<int>();
+  b200::ep_combine_norm_launch(a, cur_stream(h));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
   m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none(),
@@ -747,6 +784,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("flag_wait_probe", &flag_wait_probe);
   m.def("ar_pull_norm", &ar_pull_norm);
+  m.def("ep_combine_norm", &ep_combine_norm);
   m.def("ln_modulate", &ln_modulate, py::arg("x"), py::arg("out"), py::arg("mod"), py::arg("shift_off"),
         py::arg("scale_off"), py::arg("eps"), py::arg("split"), py::arg("r1"), py::arg("r2"), py::arg("row_off") = 0);
   m.def("dit_qk_rope", &dit_qk_rope, py::arg("qkv"), py::arg("heads"), py::arg("scales_txt"), py::arg("scales_img"),

@@ -132,6 +132,27 @@ struct PullNormArgs {
 };
 void ar_pull_norm_launch(const PullNormArgs& a, cudaStream_t st);
 
+// Expert-parallel combine over NVLink + residual add + RMSNorm: see
+// comm/ep_combine.cu. Every rank routed the same tokens; token t's slot s went
+// to expert experts[t, s], held by rank experts[t, s] / e_local, whose down
+// GEMM wrote the router-weighted row at position inv_q[t * k + s] of its rows.
+struct EpCombineArgs {
+  const void* const* peer_rows;     // [world] each rank's bf16 [rows][H] expert outputs (this op's slot)
+  const int32_t* const* peer_inv;   // [world] each rank's inverse permutation [T * k] (-1: not its expert)
+  unsigned* const* peer_flags;      // [world] each rank's flag array [world]
+  const unsigned* flags;            // local flags [world]
+  const int32_t* experts;           // [T][k] global expert ids (identical on every rank)
+  void* h;                          // [T][H] bf16 replicated residual stream (in/out)
+  const void* norm_w;               // [H] bf16
+  void* out;                        // [T][H] bf16 = rmsnorm(h + moe) * w
+  unsigned* epoch;
+  unsigned* cta_ctr;
+  int T, k, H, e_local, world, rank;
+  float eps;
+  int* status;
+};
+void ep_combine_norm_launch(const EpCombineArgs& a, cudaStream_t st);
+
 // ---------------- norms / rope / embedding ----------------
 void embedding_launch(const int32_t* ids, const void* table, void* out, int64_t T, int64_t H, int64_t V,
                       cudaStream_t st);

@@ -10,10 +10,11 @@ expert block with MXFP4 expert weights kept packed in HBM:
     -> grouped MXFP4 GEMM down (bias, x router weight) -> combine
 
 Expert parallelism: rank r holds experts [r E/ep, (r+1) E/ep). Every rank
-routes all tokens of the step (attention is replicated), runs only its own
-experts and the per-token partial outputs are summed across ranks; with top-4
-routing that sum moves ~2TH bytes per rank against ~7TH for an all-to-all
-dispatch + combine.
+routes all tokens of the step (attention is replicated), so dispatch is a
+local gather, and runs only its own experts. Combine: for decode-sized steps
+one kernel reads each token's k expert rows from the owning ranks' HBM over
+NVLink and fuses the residual add and the next RMSNorm (parallel/ep.py);
+larger steps sum per-rank partials with an NCCL all-reduce.
 
 Reference: rlx-models-core src/standard_decoder.rs:1040-1205
 (`build_gpt_oss_moe_ffn`), :11873-12208 (`GptOssSpec`, sinks attention,
@@ -58,7 +59,13 @@ class MoELayer:
 
 
 class MoEDecoderLM(DecoderLM):
-    def __init__(self, cfg: DecoderConfig, weights, device="cuda", ep_rank: int = 0, ep_size: int = 1, comm=None):
+    def __init__(self, cfg: DecoderConfig, weights, device="cuda", ep_rank: int = 0, ep_size: int = 1, comm=None,
+                 ep_combine: str = "fused", combine_max_tokens: int = 512):
+        """``ep_combine``: "fused" gathers each token's expert rows from the
+        owning ranks over NVLink and fuses the residual add and RMSNorm into the
+        same kernel (parallel/ep.py) for steps of up to ``combine_max_tokens``
+        tokens; larger steps, and "nccl", sum per-rank partials with an NCCL
+        all-reduce."""
         assert cfg.is_moe
         self.ep_rank, self.ep_size = ep_rank, ep_size
         assert cfg.num_experts % ep_size == 0
@@ -67,6 +74,13 @@ class MoEDecoderLM(DecoderLM):
         # attention / embeddings are replicated: build the dense parts with tp_size=1
         self._moe_comm = comm
         super().__init__(cfg, weights, device=device, tp_rank=0, tp_size=1, comm=None)
+        self.combiner = None
+        if ep_combine == "fused":
+            from ..parallel.ep import EPCombiner
+            self.combiner = EPCombiner(ep_rank, ep_size, self.device, hidden=cfg.hidden_size,
+                                       top_k=cfg.num_experts_per_tok, e_local=self.e_local,
+                                       max_tokens=combine_max_tokens, num_layers=cfg.num_hidden_layers,
+                                       eps=cfg.rms_norm_eps)
 
     # -- weights ----------------------------------------------------------------
     def _load(self, w):
@@ -147,7 +161,9 @@ class MoEDecoderLM(DecoderLM):
             self.moe.append(M)
 
     # -- forward ---------------------------------------------------------------
-    def _moe(self, i: int, x: torch.Tensor) -> torch.Tensor:
+    def _moe(self, i: int, x: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor) -> torch.Tensor:
+        """Routed expert block on the normalised input ``x``: ``h += moe(x)``;
+        returns ``rmsnorm(h) * norm_w`` for the next layer."""
         c = self.cfg
         M = self.moe[i]
         T, H = x.shape
@@ -166,6 +182,9 @@ class MoEDecoderLM(DecoderLM):
         perm = torch.empty(n, dtype=torch.int32, device=dev)
         inv = torch.empty(n, dtype=torch.int32, device=dev)
         cursor = torch.empty(E_l, dtype=torch.int32, device=dev)
+        fused = self.combiner is not None and self.combiner.fits(T)
+        if fused:
+            dn, inv = self.combiner.slots(n)  # symmetric slots the peers read
         ext().moe_align(experts, E_l, self.e_lo, E_l, bt, meta, tiles, perm, inv, cursor)
         a = torch.empty(n, H, dtype=torch.float16, device=dev)  # grouped GEMM operands are f16
         ext().moe_gather(x, perm, meta, E_l, k, a)
@@ -176,15 +195,19 @@ class MoEDecoderLM(DecoderLM):
         ext().moe_gemm(a, M.gu_w, M.gu_exp, 2 * I, M.gu_bias, None, perm, meta, tiles, gu, True,
                        float(c.swiglu_limit or 1e30), float(c.swiglu_alpha) if gpt_oss else 1.0, bt, s.status,
                        1.0 if gpt_oss else 0.0)
-        dn = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+        if not fused:
+            dn = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
         ext().moe_gemm(gu, M.dn_w, M.dn_exp, H, M.dn_bias, weights.view(-1), perm, meta, tiles, dn, False,
                        0.0, 0.0, bt, s.status)
+        ops._count(6)
+        if fused:
+            return self.combiner.combine_norm(experts, h, norm_w)
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         ext().moe_combine(dn, inv, k, out, False)
-        ops._count(7)
+        ops._count(1)
         if self.ep_size > 1:
             dist.all_reduce(out)
-        return out
+        return ops.rmsnorm(out, norm_w, c.rms_norm_eps, residual=h, residual_out=h)  # h += moe; norm
 
     def forward_hidden(self, fb, kv) -> torch.Tensor:
         c = self.cfg
@@ -195,7 +218,6 @@ class MoEDecoderLM(DecoderLM):
             a = self._attention(i, L, x, fb, kv)
             ops.linear(a, L.wo, bias=L.bo, residual=h, out=h)  # h += o_proj (+ bias)
             x = ops.rmsnorm(h, L.ln2, c.rms_norm_eps)
-            m = self._moe(i, x)
             nw = self.layers[i + 1].ln1 if i + 1 < n else self.norm
-            x = ops.rmsnorm(m, nw, c.rms_norm_eps, residual=h, residual_out=h)  # h += moe; norm
+            x = self._moe(i, x, h, nw)  # h += moe; x = rmsnorm(h) * nw
         return x
