@@ -206,6 +206,11 @@ def main():
     ap.add_argument("--output-len", type=int, default=None)
     ap.add_argument("--max-batched-tokens", type=int, default=8192)
     ap.add_argument("--kv-gb", type=float, default=40.0)
+    ap.add_argument("--micro-batch", type=int, default=4, help="train: sequences per micro-step per rank")
+    ap.add_argument("--act-ckpt", type=int, default=0,
+                    help="train: 1 = recompute each layer in backward (0 fits: activations of 4 x 4096 tokens ~70 GB)")
+    ap.add_argument("--grad-reduce", default="push", choices=["push", "nccl"],
+                    help="train: FSDP gradient reduce-scatter by NVLink push or NCCL")
     ap.add_argument("--tp-comm", default="nccl", choices=["nccl", "fused", "pull"],
                     help="nccl: NCCL all-reduce baseline; fused: GEMM->reduce-scatter + norm + all-gather over NVLink")
     args = ap.parse_args()

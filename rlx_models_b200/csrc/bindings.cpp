@@ -445,6 +445,54 @@ void swiglu_acc(Tensor& acc, Tensor& out) {
 
 // out[M, N] = alpha * a[M, K] @ b[K, N] for any mix of row-major / transposed
 // views (the operand majors are read from the strides); bf16 inputs.
+// Operand layouts of the training GEMM: A [M, K] and B [K, N], each row-major
+// or a transposed view.
+static void gemm_operands(const Tensor& a, const Tensor& b, b200::GemmArgs& g) {
+  check_cuda(a, "a");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16 && a.dim() == 2 && b.dim() == 2,
+              "b200.gemm: bf16 2-D operands");
+  TORCH_CHECK(b.size(0) == a.size(1), "b200.gemm: inner dims");
+  if (a.stride(1) == 1) { g.a_mn = 0; g.lda = a.stride(0); }
+  else { TORCH_CHECK(a.stride(0) == 1, "b200.gemm: a must be row-major or a transposed view"); g.a_mn = 1; g.lda = a.stride(1); }
+  if (b.stride(0) == 1) { g.b_mn = 0; g.ldb = b.stride(1); }
+  else { TORCH_CHECK(b.stride(1) == 1, "b200.gemm: b must be row-major or a transposed view"); g.b_mn = 1; g.ldb = b.stride(0); }
+  TORCH_CHECK(!(g.a_mn && !g.b_mn), "b200.gemm: transposed a needs row-major b");
+  TORCH_CHECK(g.lda % 8 == 0 && g.ldb % 8 == 0, "b200.gemm: strides % 8");
+  g.a = a.data_ptr();
+  g.b = b.data_ptr();
+  g.MA = a.size(0);
+  g.NB = b.size(1);
+  g.K = a.size(1);
+}
+
+// FSDP weight gradient pushed into the owners' gradient shards: element
+// (i, j) of a @ b is added to flat parameter base + i * N + j of the group
+// whose shard_n-element shards live at peer_shards[rank] (an int64 table of
+// device addresses, this GPU's own shard included).
+void gemm_push_shards(const Tensor& a, const Tensor& b, const Tensor& peer_shards, int64_t base, int64_t shard_n,
+                      double alpha, Tensor& ws, Tensor& sem, Tensor& status) {
+  b200::GemmArgs g{};
+  gemm_operands(a, b, g);
+  TORCH_CHECK(peer_shards.scalar_type() == at::kLong && peer_shards.is_cuda() && shard_n > 0 && base >= 0,
+              "b200.gemm_push_shards: peer table / shard size");
+  g.c = nullptr;
+  g.ldc = g.NB;
+  g.out_f32 = 1;
+  g.alpha = (float)alpha;
+  g.ws = ws.data_ptr<float>();
+  g.ws_elems = ws.numel();
+  g.sem = sem.data_ptr<int>();
+  g.sem_elems = sem.numel();
+  g.status = status.data_ptr<int>();
+  g.device = a.get_device();
+  g.shard_peer = reinterpret_cast<float* const*>(peer_shards.data_ptr<int64_t>());
+  g.shard_base = base;
+  g.shard_n = shard_n;
+  c10::cuda::CUDAGuard gd(a.device());
+  b200::gemm_launch(g, cur_stream(a));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void gemm(const Tensor& a, const Tensor& b, Tensor& out, bool accumulate, double alpha,
           const optional<Tensor>& residual, const optional<Tensor>& bias, bool prefetch_b, Tensor& ws, Tensor& sem,
           Tensor& status) {
@@ -776,12 +824,41 @@ void ep_combine_norm(const Tensor& peer_rows, const Tensor& peer_inv, const Tens
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void shard_push_add(const Tensor& src, const Tensor& peer_shards, int64_t base, int64_t shard_n, double scale) {
+  check_cuda(src, "src");
+  TORCH_CHECK(src.is_contiguous() && (src.scalar_type() == at::kFloat || src.scalar_type() == at::kBFloat16),
+              "b200.shard_push_add: contiguous fp32 / bf16 source");
+  TORCH_CHECK(peer_shards.scalar_type() == at::kLong && peer_shards.is_cuda() && base >= 0,
+              "b200.shard_push_add: peer table");
+  c10::cuda::CUDAGuard g(src.device());
+  b200::shard_push_add_launch(src.data_ptr(), src.scalar_type() == at::kFloat, src.numel(), base,
+                              reinterpret_cast<float* const*>(peer_shards.data_ptr<int64_t>()), shard_n, (float)scale,
+                              cur_stream(src));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void peer_barrier(const Tensor& peer_flags, const Tensor& flags, Tensor& epoch, int64_t rank, int64_t world,
+                  Tensor& status) {
+  check_cuda(flags, "flags");
+  TORCH_CHECK(peer_flags.scalar_type() == at::kLong && peer_flags.numel() == world && flags.numel() >= world,
+              "b200.peer_barrier: tables");
+  c10::cuda::CUDAGuard g(flags.device());
+  b200::peer_barrier_launch(reinterpret_cast<unsigned* const*>(peer_flags.data_ptr<int64_t>()),
+                            reinterpret_cast<const unsigned*>(flags.data_ptr<int32_t>()),
+                            reinterpret_cast<unsigned*>(epoch.data_ptr<int32_t>()), (int)rank, (int)world,
+                            status.data_ptr<int>(), cur_stream(flags));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
   m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none(),
         py::arg("act_from") = -1, py::arg("gate") = py::none(), py::arg("gate_split") = 0, py::arg("gate_r1") = 1,
         py::arg("gate_r2") = 1, py::arg("gate_off") = 0);
   m.def("gemm", &gemm);
+  m.def("gemm_push_shards", &gemm_push_shards);
+  m.def("shard_push_add", &shard_push_add);
+  m.def("peer_barrier", &peer_barrier);
   m.def("flag_wait_probe", &flag_wait_probe);
   m.def("ar_pull_norm", &ar_pull_norm);
   m.def("ep_combine_norm", &ep_combine_norm);

@@ -74,6 +74,8 @@ struct GemmArgs {
   int64_t sem_elems;
   int* status;
   int device;
+  float* const* shard_peer = nullptr;  // FSDP gradient push (see gemm::Params::shard_peer)
+  int64_t shard_base = 0, shard_n = 0;
 };
 void gemm_launch(const GemmArgs& a, cudaStream_t st);
 
@@ -152,6 +154,13 @@ struct EpCombineArgs {
   int* status;
 };
 void ep_combine_norm_launch(const EpCombineArgs& a, cudaStream_t st);
+
+// FSDP gradient push into the owners' fp32 shards + cross-rank barrier: see
+// comm/fsdp_comm.cu.
+void shard_push_add_launch(const void* src, bool f32, int64_t n, int64_t base, float* const* peers, int64_t shard_n,
+                           float scale, cudaStream_t st);
+void peer_barrier_launch(unsigned* const* peer_flags, const unsigned* flags, unsigned* epoch, int rank, int world,
+                         int* status, cudaStream_t st);
 
 // ---------------- norms / rope / embedding ----------------
 void embedding_launch(const int32_t* ids, const void* table, void* out, int64_t T, int64_t H, int64_t V,

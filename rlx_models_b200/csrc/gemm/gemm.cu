@@ -221,6 +221,12 @@ void gemm_launch(const GemmArgs& a, cudaStream_t st) {
   p.w_is_a = 0;
   p.accumulate = a.accumulate;
   p.prefetch_w = a.prefetch_b;
+  p.shard_peer = a.shard_peer;
+  p.shard_base = a.shard_base;
+  p.shard_n = a.shard_n;
+  if (a.shard_peer != nullptr && (!a.out_f32 || a.accumulate || a.residual != nullptr || a.bias != nullptr ||
+                                  a.shard_n <= 0))
+    throw std::runtime_error("b200.gemm: shard push needs f32 output, no accumulate / residual / bias");
   p.ws = a.ws;
   p.sem = a.sem;
   p.status = a.status;

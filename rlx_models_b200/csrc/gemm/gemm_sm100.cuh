@@ -77,6 +77,13 @@ struct Params {
   const __nv_bfloat16* gate;
   int64_t gate_ld;
   int gate_split, gate_r1, gate_r2, gate_off;
+  // FSDP gradient reduce-scatter push (EPI_F32, normal orientation). When
+  // shard_peer != nullptr, output element (i, j) is the gradient of flat
+  // parameter shard_base + i * ldc_i + j; it is added (red.add, fp32) into
+  // the owning rank's gradient shard shard_peer[idx / shard_n] at idx %
+  // shard_n, over NVLink for remote owners. C is not written.
+  float* const* shard_peer;
+  int64_t shard_base, shard_n;
 };
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -187,6 +194,24 @@ __device__ __forceinline__ void store_chunk(const Params& p, int i, int j0, floa
       for (int t = 0; t < 32; ++t)
         if (j0 + t < p.NB) v[t] += __bfloat162float(r[(int64_t)(j0 + t) * p.ldr_j]);
     }
+  }
+  if (EPI == EPI_F32 && p.shard_peer != nullptr) {
+    const int64_t base = p.shard_base + (int64_t)i * p.ldc_i + j0;
+    const int64_t own0 = base / p.shard_n;
+    if (full && (base & 3) == 0 && base + 31 < (own0 + 1) * p.shard_n) {
+      float* d = p.shard_peer[own0] + (base - own0 * p.shard_n);  // one owner for the whole chunk
+#pragma unroll
+      for (int q = 0; q < 8; ++q) red_add_v4(d + q * 4, v[q * 4], v[q * 4 + 1], v[q * 4 + 2], v[q * 4 + 3]);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 32; ++t)
+        if (j0 + t < p.NB) {
+          const int64_t idx = base + t;
+          const int64_t own = idx / p.shard_n;
+          atomicAdd(p.shard_peer[own] + (idx - own * p.shard_n), v[t]);
+        }
+    }
+    return;
   }
   if (EPI == EPI_F32) {
     float* c = out_row<float>(p, i, p.ldc_i);

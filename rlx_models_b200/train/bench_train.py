@@ -39,7 +39,9 @@ def bench_train(args) -> int:
     assert gbatch % ws == 0
     local_b = gbatch // ws
     tcfg = TrainConfig(lr=1e-4, betas=(0.9, 0.95), weight_decay=0.1, grad_clip=1.0,
-                       micro_batch=getattr(args, "micro_batch", 4), total_steps=20)
+                       micro_batch=getattr(args, "micro_batch", 4), total_steps=20,
+                       activation_checkpointing=bool(getattr(args, "act_ckpt", 0)),
+                       grad_reduce=getattr(args, "grad_reduce", "push"))
     trainer = Trainer(cfg, tcfg, RandomWeights(cfg, 0, dev), rank=rank, world=ws, device=dev)
     g = torch.Generator().manual_seed(1234 + rank)
     host = torch.empty(local_b, seq + 1, dtype=torch.int64).pin_memory()
@@ -82,6 +84,7 @@ def bench_train(args) -> int:
         "data": "synthetic uniform-random token ids, fresh per step; random-init weights",
         "config": {"model": "Qwen3-1.7B-shape", "global_batch": gbatch, "seq_len": seq,
                    "parallelism": f"fsdp{ws}", "micro_batch_per_rank": tcfg.micro_batch,
+                   "activation_checkpointing": tcfg.activation_checkpointing, "grad_reduce": tcfg.grad_reduce,
                    "l2": "inputs larger than L2 (every micro-step streams >1 GB of activations)"},
         "loss_first": metrics[0].loss, "loss_last": metrics[-1].loss,
         "clocks": sampler.summary(),

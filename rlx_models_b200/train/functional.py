@@ -43,8 +43,17 @@ class LinearFn(torch.autograd.Function):
             if ctx.needs_input_grad[0]:
                 dx = ops.matmul(g2, w).view(x.shape)
             if ctx.needs_input_grad[1]:
-                dw = torch.empty(w.shape, dtype=torch.float32, device=w.device)
-                ops.matmul(g2.t(), x2, out=dw)
+                from .fsdp import push_target
+                tgt = push_target(w)
+                if tgt is not None:  # FSDP push: the GEMM adds dW into the owners' shards
+                    fg, base = tgt
+                    s = ops.scratch(w.device)
+                    ops._count(1)
+                    ops.ext().gemm_push_shards(g2.t(), x2, fg.push_table, base, fg.shard_n, 1.0, s.gemm_ws,
+                                               s.gemm_sem, s.status)
+                else:
+                    dw = torch.empty(w.shape, dtype=torch.float32, device=w.device)
+                    ops.matmul(g2.t(), x2, out=dw)
         else:
             if ctx.needs_input_grad[0]:
                 dx = (g2.float() @ w.float()).to(x.dtype).view(x.shape)

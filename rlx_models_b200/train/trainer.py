@@ -43,6 +43,11 @@ class TrainConfig:
     lora_alpha: float = 32.0
     lora_targets: tuple = ("qkv", "o", "gate_up", "down")
     dora: bool = False
+    # gradient reduce-scatter on CUDA: "push" adds every gradient element into
+    # its owner's shard over NVLink (wgrad GEMM epilogue + push kernel, one
+    # device barrier per step); "nccl" materialises full gradients and calls
+    # reduce_scatter_tensor per group
+    grad_reduce: str = "push"
 
     def lr_at(self, step: int) -> float:
         if self.warmup_steps and step < self.warmup_steps:
@@ -85,6 +90,10 @@ class Trainer:
             self.lora = LoraAdapters(self.model, train_cfg.lora_rank, train_cfg.lora_alpha, train_cfg.lora_targets,
                                      train_cfg.dora, group=group, world=world)
             self.model.lora = self.lora
+        self.push = None
+        if train_cfg.grad_reduce == "push" and self.device.type == "cuda" and self.lora is None:
+            from .fsdp import GradPush
+            self.push = GradPush(self.model.groups, rank, world, self.device, group)
         self.step_num = 0
         self._sumsq = torch.zeros(1, dtype=torch.float32, device=self.device)
         self._coef = torch.ones(1, dtype=torch.float32, device=self.device)
@@ -121,6 +130,8 @@ class Trainer:
             loss = self.model.loss(ids[s:s + mb], tgt[s:s + mb], denom=global_tokens)
             loss.backward()
             total += loss.detach()
+        if self.push is not None:
+            self.push.barrier()  # every rank's gradient pushes of this step have landed
         if self.world > 1:
             dist.all_reduce(total, group=self.group)
         if self.lora is not None:
@@ -155,6 +166,8 @@ class Trainer:
                         beta) / self.world
         loss.backward()
         total = loss.detach()
+        if self.push is not None:
+            self.push.barrier()
         if self.world > 1:
             dist.all_reduce(total, group=self.group)
         if self.lora is not None:

@@ -39,3 +39,8 @@ def test_flux_sequence_parallel_two_ranks():
 def test_expert_parallel_fused_combine_two_ranks():
     out = _torchrun("rlx_models_b200.parallel.ep_check", 2)
     assert '"ok_all_ranks": false' not in out and out.count('"ok_all_ranks": true') == 2
+
+
+def test_fsdp_push_reduce_scatter_two_ranks():
+    out = _torchrun("rlx_models_b200.train.fsdp_check", 2)
+    assert '"ok_all_ranks": true' in out
