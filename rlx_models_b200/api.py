@@ -38,9 +38,29 @@ def parse_model_ref(ref: str) -> tuple[str, str | None, str | None]:
     return name, (quant or None), (rev or None)
 
 
+GGUF_QUANT_PREFERENCE = ("Q4_K_M", "Q4_K_S", "Q5_K_M", "Q6_K", "Q8_0", "Q4_0", "F16", "BF16")
+
+
+def pick_gguf(directory: str, quant: str | None = None) -> str | None:
+    """The GGUF file of ``directory`` whose name carries ``quant`` (case
+    insensitive), else the first match in the default quant preference order
+    (the hub's "QUANT" selection rule), else the only GGUF file."""
+    files = sorted(f for f in os.listdir(directory) if f.lower().endswith(".gguf"))
+    if not files:
+        return None
+    for q in ((quant,) if quant else ()) + GGUF_QUANT_PREFERENCE:
+        for f in files:
+            if q.lower() in f.lower():
+                return os.path.join(directory, f)
+    if quant:
+        raise FileNotFoundError(f"no GGUF file for quant {quant!r} in {directory}: {files}")
+    return os.path.join(directory, files[0])
+
+
 def resolve_model_path(model: str) -> str | None:
-    """Local dir, or an HF id found in the offline HF cache (snapshots/<rev>)."""
-    if os.path.isdir(model):
+    """Local dir or .gguf file, or an HF id found in the offline HF cache
+    (snapshots/<rev>)."""
+    if os.path.isdir(model) or (os.path.isfile(model) and model.lower().endswith(".gguf")):
         return model
     if "/" in model:
         name, _, rev = parse_model_ref(model)
@@ -118,7 +138,17 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
     """Load a model by path, HF id (offline cache) or named shape (random init)."""
     path = resolve_model_path(model)
     tok = None
+    gguf_file = None
     if path is not None:
+        if os.path.isfile(path):
+            gguf_file = path
+        elif not os.path.exists(os.path.join(path, "config.json")):
+            gguf_file = pick_gguf(path, parse_model_ref(model)[1])
+    if gguf_file is not None:
+        from .weights.gguf import GGUFWeights
+        weights = GGUFWeights(gguf_file, device=device)  # quantised blocks expand on the GPU
+        cfg = config or weights.config
+    elif path is not None:
         cfg = config or C.DecoderConfig.from_file(path)
         weights = WeightMap.from_dir(path)
         try:

@@ -850,6 +850,17 @@ void peer_barrier(const Tensor& peer_flags, const Tensor& flags, Tensor& epoch, 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void gguf_dequant(const Tensor& raw, int64_t ggml_type, Tensor& out) {
+  check_cuda(raw, "raw");
+  TORCH_CHECK(raw.scalar_type() == at::kByte && raw.is_contiguous() && out.is_contiguous() &&
+                  (out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kFloat),
+              "b200.gguf_dequant: contiguous uint8 blocks -> bf16 / fp32");
+  c10::cuda::CUDAGuard g(raw.device());
+  b200::gguf_dequant_launch(raw.data_ptr(), (int)ggml_type, out.numel(), out.data_ptr(),
+                            out.scalar_type() == at::kFloat, cur_stream(raw));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
   m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none(),
@@ -859,6 +870,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_push_shards", &gemm_push_shards);
   m.def("shard_push_add", &shard_push_add);
   m.def("peer_barrier", &peer_barrier);
+  m.def("gguf_dequant", &gguf_dequant);
   m.def("flag_wait_probe", &flag_wait_probe);
   m.def("ar_pull_norm", &ar_pull_norm);
   m.def("ep_combine_norm", &ep_combine_norm);

@@ -159,6 +159,9 @@ void ep_combine_norm_launch(const EpCombineArgs& a, cudaStream_t st);
 // comm/fsdp_comm.cu.
 void shard_push_add_launch(const void* src, bool f32, int64_t n, int64_t base, float* const* peers, int64_t shard_n,
                            float scale, cudaStream_t st);
+// GGUF block dequantisation (quant/gguf_dequant.cu): n output elements of
+// ggml type `ggml_type` from its raw blocks into bf16 (or fp32).
+void gguf_dequant_launch(const void* raw, int ggml_type, int64_t n, void* out, bool out_f32, cudaStream_t st);
 void peer_barrier_launch(unsigned* const* peer_flags, const unsigned* flags, unsigned* epoch, int rank, int world,
                          int* status, cudaStream_t st);
 

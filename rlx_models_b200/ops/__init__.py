@@ -278,3 +278,22 @@ def sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, *, out=None
     _count(1)
     ext().sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, out, logprob)
     return out
+
+
+def gguf_dequant(raw: torch.Tensor, kind: str, shape, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """GGUF blocks (device uint8) -> dequantised tensor of ``shape`` (bf16 or
+    fp32); F16 / BF16 payloads are converted with a cast."""
+    from ..weights.gguf import GGML_TYPES, TYPE_ID
+    tid = TYPE_ID[kind]
+    _, be, bb = GGML_TYPES[tid]
+    if kind in ("F16", "BF16"):
+        src = raw.view(torch.float16 if kind == "F16" else torch.bfloat16)
+        return src.to(dtype).view(*shape)
+    n = 1
+    for d in shape:
+        n *= int(d)
+    assert raw.numel() == n // be * bb, "gguf_dequant: byte count does not match the shape"
+    out = torch.empty(*shape, dtype=dtype, device=raw.device)
+    _count(1)
+    ext().gguf_dequant(raw.contiguous(), tid, out)
+    return out
