@@ -1,0 +1,145 @@
+"""CPU tests: evaluation metrics, serving guardrails, pipeline stage planner."""
+import math
+
+import pytest
+import torch
+
+from rlx_models_b200 import eval as E
+from rlx_models_b200.parallel import pp_plan as P
+from rlx_models_b200.serve import guardrails as GR
+
+
+# -- eval ----------------------------------------------------------------------
+
+def _uniform_logits(V):
+    return lambda ids: torch.zeros(len(ids), V)
+
+
+def test_perplexity_uniform_model_equals_vocab():
+    V = 50
+    r = E.perplexity(_uniform_logits(V), list(range(40)), window=16, stride=8)
+    assert r.tokens == 39 and abs(r.ppl - V) < 1e-3
+
+
+def test_perplexity_windows_score_each_token_once():
+    torch.manual_seed(0)
+    table = torch.randn(30, 30)
+
+    def bigram(ids):  # logits depend only on the current token
+        return table[torch.tensor(ids)]
+
+    ids = torch.randint(0, 30, (100,)).tolist()
+    full = E.perplexity(bigram, ids, window=1000)
+    for w, s in ((10, 10), (16, 5), (33, 11)):
+        r = E.perplexity(bigram, ids, window=w, stride=s)
+        assert r.tokens == 99 and abs(r.nll - full.nll) < 1e-5
+
+
+def test_multiple_choice_prefers_likely_continuation():
+    V = 10
+
+    def fn(ids):  # always predicts token 7 strongly
+        lg = torch.zeros(len(ids), V)
+        lg[:, 7] = 5.0
+        return lg
+
+    sc = E.multiple_choice(fn, [1, 2, 3], [[4, 4], [7, 7], [7]])
+    assert sc.best == 2 and sc.best_norm in (1, 2)
+    assert abs(sc.logprob_norm[1] - sc.logprob_norm[2]) < 1e-6
+    assert E.accuracy(fn, [([1], [[3], [7]], 1), ([2], [[7], [0]], 0)]) == 1.0
+
+
+def test_bleu_chrf():
+    assert E.bleu(["the cat sat on the mat"], ["the cat sat on the mat"]) == pytest.approx(100.0)
+    assert E.bleu(["a b c d"], ["e f g h"]) == 0.0
+    b = E.bleu(["the cat sat on a mat today"], [["the cat sat on the mat", "a cat sat on a mat"]])
+    assert 0 < b < 100
+    assert E.chrf(["hello world"], ["hello world"]) == pytest.approx(100.0)
+    c = E.chrf(["hello word"], ["hello world"])
+    assert 50 < c < 100
+
+
+# -- guardrails ----------------------------------------------------------------
+
+TOOLS = [{"type": "function", "function": {"name": "read_file", "parameters": {
+    "type": "object", "properties": {"path": {"type": "string"}, "n": {"type": "integer"},
+                                     "mode": {"enum": ["r", "rb"]}}, "required": ["path"]}}}]
+
+
+def test_validate_tool_call():
+    GR.validate_tool_call({"name": "read_file", "arguments": {"path": "a"}}, TOOLS)
+    GR.validate_tool_call({"function": {"name": "read_file", "arguments": '{"path": "a"}'}}, TOOLS)
+    with pytest.raises(GR.GuardrailError) as e:
+        GR.validate_tool_call({"name": "write_file", "arguments": {}}, TOOLS)
+    assert e.value.kind == "unknown_tool"
+    with pytest.raises(GR.GuardrailError) as e:
+        GR.validate_tool_call({"name": "read_file", "arguments": {"n": 3}}, TOOLS)
+    assert e.value.kind == "missing_required" and e.value.fields == ["path"]
+    with pytest.raises(GR.GuardrailError) as e:
+        GR.validate_tool_call({"name": GR.RESPOND_TOOL, "arguments": {"message": "x"}}, TOOLS)
+    assert e.value.kind == "reserved_tool"
+    GR.validate_tool_call({"name": GR.RESPOND_TOOL, "arguments": {"message": "x"}}, TOOLS + [GR.respond_tool()])
+    assert GR.collides_with_reserved([GR.respond_tool()]) and not GR.collides_with_reserved(TOOLS)
+
+
+def test_sanitize_and_wire():
+    args = GR.sanitize_tool_arguments({"name": "read_file", "arguments": {"path": "a", "n": "3", "mode": "w",
+                                                                          "junk": 1}}, TOOLS)
+    assert args == {"path": "a"}
+    with pytest.raises(GR.GuardrailError):
+        GR.sanitize_tool_arguments({"name": "read_file", "arguments": {"path": 5}}, TOOLS)
+    assert GR.arguments_wire_string({"a": 1}) == '{"a":1}'
+    assert GR.arguments_wire_string("[1, 2]") == "{}" and GR.arguments_wire_string('{"x": 2}') == '{"x": 2}'
+    assert GR.arguments_object(None) is None and GR.arguments_object(3) == {}
+
+
+def test_compaction_policy():
+    sys_m = {"role": "system", "content": "SYSTEM PROMPT"}
+    msgs = [sys_m, {"role": "user", "content": "a" * 400}, {"role": "tool", "content": "t" * 400},
+            {"role": "assistant", "content": "b" * 400}, {"role": "user", "content": "short"}]
+    assert GR.compact_messages(msgs, 10 ** 6) == msgs
+    budget = GR.message_tokens(sys_m) + GR.message_tokens(msgs[-1])
+    out = GR.compact_messages(msgs, budget)
+    assert out == [sys_m, msgs[-1]]
+    out2 = GR.compact_messages(msgs, GR.messages_tokens(msgs) - 50)
+    assert all(m["role"] != "tool" for m in out2) and len(out2) == 4  # tool result evicted first
+    assert GR.compact_messages([sys_m], 1) == [sys_m]  # system kept even over budget
+
+
+# -- pipeline planner ----------------------------------------------------------
+
+def test_plan_even_and_balanced_head():
+    from rlx_models_b200 import config as C
+    cfg = C.preset("qwen3-8b")
+    nodes = [P.NodeSpec(f"gpu{i}", 180 << 30) for i in range(4)]
+    pl = P.plan_decoder(cfg, nodes)
+    r = pl.ranges()
+    assert r[0][0] == 0 and r[-1][1] == 36 and all(a[1] == b[0] for a, b in zip(r, r[1:]))
+    assert pl.stages[0].roles == ["driver", "embedding"] and pl.stages[-1].roles == ["readout"]
+    # the end stages carry the embedding / head, so they get fewer layers
+    assert pl.stages[0].layer_count < pl.stages[1].layer_count
+    assert pl.stages[-1].layer_count < pl.stages[1].layer_count
+    util = [s.utilisation for s in pl.stages]
+    assert max(util) - min(util) < 0.25 * max(util)
+    assert [b.after_layer for b in pl.boundaries] == [s.layer_end - 1 for s in pl.stages[:-1]]
+
+
+def test_plan_memory_weighting_and_state():
+    G = 1 << 30
+    layers = [P.LayerSpec(i, 100 * G, has_attention=i % 2 == 0, has_recurrent=i % 2 == 1) for i in range(10)]
+    nodes = [P.NodeSpec("small", 300 * G), P.NodeSpec("big", 900 * G, cached_bytes=5 * G),
+             P.NodeSpec("far", 900 * G, rtt_ms=5)]
+    pl = P.plan(layers, nodes)
+    assert [s.node_id for s in pl.stages] == ["big", "far", "small"]  # best first: memory, cache, RTT
+    assert sum(s.layer_count for s in pl.stages) == 10
+    assert pl.stages[-1].layer_count <= 3  # the small node takes the fewest layers
+    assert pl.stages[0].state_affinity == "mixed" and pl.stages[0].migration_policy == "sticky_recurrent_owner"
+    assert "cache_locality_preferred" in pl.stages[0].reasons and "network_pipeline_cost" in pl.stages[1].reasons
+    pl2 = P.plan(layers, nodes, allow_state_transfer=True)
+    assert pl2.stages[0].migration_policy == "recurrent_state_transfer_allowed"
+    tiny = P.plan(layers[:2], nodes)
+    assert len(tiny.stages) == 2 and any("idle" in d for d in tiny.diagnostics)
+    with pytest.raises(P.PlanError):
+        P.plan([P.LayerSpec(0, 1), P.LayerSpec(2, 1)], nodes)
+    over = P.plan(layers, [P.NodeSpec("x", 10 * G)])
+    assert over.max_utilisation > 1 and over.diagnostics
