@@ -130,8 +130,22 @@ def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model"):
             toks = tk
             if typ == "done":
                 reason = val
+        text = text_of(toks, stop)
+        ch = choice(kind, text, reason)
+        tools = body.get("tools") or []
+        if kind == "chat" and tools:
+            # tool calls in the text: validated and sanitised against the request's tools
+            from .tool_calls import parse, to_openai
+            calls, rest = parse(text)
+            if calls:
+                good, errors = to_openai(calls, tools)
+                if good:
+                    ch["message"] = {"role": "assistant", "content": rest or None, "tool_calls": good}
+                    ch["finish_reason"] = "tool_calls"
+                if errors:
+                    ch["guardrail_errors"] = errors
         res = {"id": rid, "object": obj, "created": created, "model": model_name,
-               "choices": [choice(kind, text_of(toks, stop), reason)],
+               "choices": [ch],
                "usage": {"prompt_tokens": len(ids), "completion_tokens": len(toks),
                          "total_tokens": len(ids) + len(toks)}}
         if kind != "chat":
@@ -163,7 +177,15 @@ def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model"):
         msgs = body.get("messages") or []
         if not msgs:
             raise HTTPException(400, "messages required")
-        text = tokenizer.apply_chat_template(msgs, add_generation_prompt=True, tokenize=False)
+        budget = body.get("max_context_tokens")
+        if budget:  # keep the conversation inside a token budget (system messages stay)
+            from .guardrails import compact_messages
+            msgs = compact_messages(msgs, int(budget), tokenizer)
+        tools = body.get("tools") or None
+        try:
+            text = tokenizer.apply_chat_template(msgs, add_generation_prompt=True, tokenize=False, tools=tools)
+        except TypeError:  # a template helper without tool support
+            text = tokenizer.apply_chat_template(msgs, add_generation_prompt=True, tokenize=False)
         return respond(body, tokenizer.encode(text), "chat")
 
     return app

@@ -7,6 +7,7 @@ Reference: the runners load ``tokenizer.json`` next to the weights
 """
 from __future__ import annotations
 
+import json
 import os
 
 
@@ -21,8 +22,12 @@ class ByteTokenizer:
     def decode(self, ids) -> str:
         return bytes(i for i in ids if 0 <= i < 256).decode("utf-8", errors="replace")
 
-    def apply_chat_template(self, messages, add_generation_prompt=True, tokenize=False):
-        s = "".join(f"<|{m['role']}|>\n{m['content']}\n" for m in messages)
+    def apply_chat_template(self, messages, add_generation_prompt=True, tokenize=False, tools=None):
+        s = ""
+        if tools:  # tool catalog as a system block; calls come back as <tool_call>{json}</tool_call>
+            s += "<|system|>\n# Tools\n" + "\n".join(json.dumps(t) for t in tools) + \
+                 "\nCall a tool with <tool_call>{\"name\": ..., \"arguments\": {...}}</tool_call>\n"
+        s += "".join(f"<|{m['role']}|>\n{m.get('content') or ''}\n" for m in messages)
         return s + ("<|assistant|>\n" if add_generation_prompt else "")
 
 
@@ -39,11 +44,11 @@ class HFTokenizer:
     def decode(self, ids) -> str:
         return self.tok.decode(list(ids), skip_special_tokens=True)
 
-    def apply_chat_template(self, messages, add_generation_prompt=True, tokenize=False):
+    def apply_chat_template(self, messages, add_generation_prompt=True, tokenize=False, tools=None):
         if self.chat_template:
             return self.tok.apply_chat_template(messages, add_generation_prompt=add_generation_prompt,
-                                                tokenize=tokenize)
-        return ByteTokenizer().apply_chat_template(messages, add_generation_prompt)
+                                                tokenize=tokenize, tools=tools)
+        return ByteTokenizer().apply_chat_template(messages, add_generation_prompt, tools=tools)
 
 
 def load_tokenizer(path: str | None):

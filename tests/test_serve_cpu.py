@@ -122,3 +122,62 @@ def test_concurrent_requests_share_a_batch(client):
         t.join()
     assert all(len(res[i]["choices"][0]["token_ids"]) == 30 for i in range(6))
     assert eng.max_batch >= 2
+
+
+class ScriptedEngine(FakeEngine):
+    """Emits the bytes of a fixed reply, one per step."""
+
+    def __init__(self, reply: str):
+        super().__init__()
+        self.reply = list(reply.encode())
+
+    def step(self):
+        done = []
+        for sid, st in list(self.requests.items()):
+            ids, p = self.params[sid]
+            st.tokens.append(self.reply[len(st.tokens)])
+            if len(st.tokens) >= min(len(self.reply), p.max_new_tokens):
+                done.append(_Out(sid, list(st.tokens), "stop"))
+                del self.requests[sid]
+        return done
+
+
+TOOLS = [{"type": "function", "function": {"name": "get_weather", "parameters": {
+    "type": "object", "properties": {"city": {"type": "string"}}, "required": ["city"]}}}]
+
+
+@pytest.mark.parametrize("reply,expect", [
+    ('Checking.<tool_call>{"name": "get_weather", "arguments": {"city": "Oslo", "junk": 1}}</tool_call>', "call"),
+    ('<tool_call>{"name": "launch_rocket", "arguments": {}}</tool_call>', "rejected"),
+    ("It is sunny.", "text")])
+def test_chat_tool_calls_validated(reply, expect):
+    eng = ScriptedEngine(reply)
+    tok = ByteTokenizer()
+    runner = EngineRunner(eng, tok)
+    app = create_app(runner, tok, "fake")
+    with TestClient(app) as c:
+        r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "weather?"}],
+                                                 "tools": TOOLS, "max_tokens": 500, "ignore_eos": True})
+    runner.shutdown()
+    ch = r.json()["choices"][0]
+    if expect == "call":
+        assert ch["finish_reason"] == "tool_calls" and ch["message"]["content"] == "Checking."
+        fn = ch["message"]["tool_calls"][0]["function"]
+        assert fn["name"] == "get_weather" and json.loads(fn["arguments"]) == {"city": "Oslo"}
+    elif expect == "rejected":
+        assert "tool_calls" not in ch["message"] and "unknown tool" in ch["guardrail_errors"][0]
+    else:
+        assert ch["message"]["content"] == "It is sunny." and "tool_calls" not in ch["message"]
+    # the tool catalog reached the prompt
+    ids, _ = eng.params[1]
+    assert b"get_weather" in bytes(ids)
+
+
+def test_chat_compaction_budget(client):
+    c, eng = client
+    msgs = [{"role": "system", "content": "SYS"}] + [{"role": "user", "content": "x" * 400}] * 5 + \
+           [{"role": "user", "content": "last"}]
+    r = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 2, "max_context_tokens": 120})
+    assert r.status_code == 200
+    ids, _ = eng.params[1]
+    assert len(ids) < 300 and b"SYS" in bytes(ids) and b"last" in bytes(ids)
