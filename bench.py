@@ -211,8 +211,10 @@ def main():
                     help="train: 1 = recompute each layer in backward (0 fits: activations of 4 x 4096 tokens ~70 GB)")
     ap.add_argument("--grad-reduce", default="push", choices=["push", "nccl"],
                     help="train: FSDP gradient reduce-scatter by NVLink push or NCCL")
-    ap.add_argument("--tp-comm", default="nccl", choices=["nccl", "fused", "pull"],
-                    help="nccl: NCCL all-reduce baseline; fused: GEMM->reduce-scatter + norm + all-gather over NVLink")
+    ap.add_argument("--tp-comm", default="pull", choices=["nccl", "fused", "pull"],
+                    help="pull (default): decode steps read every rank's GEMM partial over NVLink in one kernel "
+                         "with the residual add + RMSNorm, prefill on NCCL; nccl: NCCL all-reduce baseline; "
+                         "fused: GEMM->reduce-scatter push + norm + all-gather over NVLink")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -150,7 +150,11 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
         cfg = config or weights.config
     elif path is not None:
         cfg = config or C.DecoderConfig.from_file(path)
-        weights = WeightMap.from_dir(path)
+        from .weights.mlx import MLXWeights
+        if MLXWeights.is_mlx_dir(path):  # MLX affine group-quantised checkpoint
+            weights = MLXWeights(path, device=device)
+        else:
+            weights = WeightMap.from_dir(path)
         try:
             from .tokenizer import load_tokenizer
             tok = load_tokenizer(path)

@@ -81,13 +81,51 @@ def gemm_rows(cfg, tp, M):
             ("lm_head(f32)", min(M, 64), V // tp, H, 3)]
 
 
+def wgrad(args, dev, timer, tf, hbm):
+    """FSDP weight gradient at the Qwen3-1.7B gate|up shape (dW [12288, 2048]
+    from T tokens): the dense fp32 GEMM, the same GEMM adding dW into a
+    gradient shard through the push epilogue (world 1, 8 emulated shards on
+    this GPU), and cuBLAS (bf16 out) for reference."""
+    T, N, K = args.M, 12288, 2048
+    dy = (torch.randn(T, N, device=dev) * 0.02).bfloat16()
+    x = torch.randn(T, K, device=dev).bfloat16()
+    W = 8
+    shard_n = (N * K + W - 1) // W
+    shard_n = (shard_n + 127) // 128 * 128
+    shards = torch.zeros(W, shard_n, dtype=torch.float32, device=dev)
+    table = torch.tensor([shards[i].data_ptr() for i in range(W)], dtype=torch.int64, device=dev)
+    s = ops.scratch(dev)
+    dw = torch.empty(N, K, dtype=torch.float32, device=dev)
+
+    def push():
+        ops.ext().gemm_push_shards(dy.t(), x, table, 0, shard_n, 1.0, s.gemm_ws, s.gemm_sem, s.status)
+
+    if args.only == "wgrad_push":
+        for _ in range(args.iters):
+            push()
+        torch.cuda.synchronize()
+        ops.check_errors(dev)
+        print("ran wgrad_push", T, N, K)
+        return
+    flops = 2.0 * T * N * K
+    for name, fn in (("wgrad_dense_f32", lambda: ops.matmul(dy.t(), x, out=dw)), ("wgrad_push_shards", push),
+                     ("wgrad_cublas_bf16", lambda: torch.matmul(dy.t(), x))):
+        t = timer(fn, args.reps)
+        row = dict(op=name, T=T, N=N, K=K, us=round(t * 1e6, 1), tflops=round(flops / t / 1e12, 1),
+                   frac_flops=round(flops / t / 1e12 / tf, 3))
+        print(json.dumps(row), flush=True)
+    ops.check_errors(dev)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="qwen3-8b")
     ap.add_argument("--tp", type=int, default=1)
     ap.add_argument("--json", default=None)
     ap.add_argument("--reps", type=int, default=10)
-    ap.add_argument("--only", default=None, help="run a single GEMM op (e.g. o_proj+res) at --M")
+    ap.add_argument("--only", default=None, help="run a single GEMM op (e.g. o_proj+res) at --M; 'wgrad' times "
+                    "the FSDP weight-gradient GEMM (dense / shard push / cuBLAS) with --M tokens, "
+                    "'wgrad_push' only launches the push GEMM --iters times (for ncu)")
     ap.add_argument("--M", type=int, default=64)
     ap.add_argument("--iters", type=int, default=3, help="with --only: plain launches (for ncu)")
     args = ap.parse_args()
@@ -97,6 +135,8 @@ def main():
     hbm, tf, src = peaks()
     timer = Timer(dev)
     rows = []
+    if args.only in ("wgrad", "wgrad_push"):
+        return wgrad(args, dev, timer, tf, hbm)
     if args.only:
         for name, m, n, k, mode in gemm_rows(cfg, args.tp, args.M):
             if name != args.only:

@@ -861,6 +861,29 @@ void gguf_dequant(const Tensor& raw, int64_t ggml_type, Tensor& out) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void apply_penalties(Tensor& logits, const Tensor& off, const Tensor& ids, const Tensor& counts, const Tensor& rep,
+                     const Tensor& freq, const Tensor& pres, const Tensor& boff, const Tensor& bias_ids,
+                     const Tensor& bias_vals) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
+              "b200.apply_penalties: fp32 [B, V] logits with unit column stride");
+  const int64_t B = logits.size(0);
+  TORCH_CHECK(off.numel() == B + 1 && boff.numel() == B + 1 && rep.numel() >= B && freq.numel() >= B &&
+                  pres.numel() >= B && ids.numel() == counts.numel() && bias_ids.numel() == bias_vals.numel(),
+              "b200.apply_penalties: table sizes");
+  TORCH_CHECK(off.scalar_type() == at::kInt && ids.scalar_type() == at::kInt && counts.scalar_type() == at::kInt &&
+                  boff.scalar_type() == at::kInt && bias_ids.scalar_type() == at::kInt &&
+                  rep.scalar_type() == at::kFloat && freq.scalar_type() == at::kFloat &&
+                  pres.scalar_type() == at::kFloat && bias_vals.scalar_type() == at::kFloat,
+              "b200.apply_penalties: dtypes");
+  c10::cuda::CUDAGuard g(logits.device());
+  b200::penalties_launch(logits.data_ptr<float>(), logits.stride(0), B, logits.size(1), off.data_ptr<int32_t>(),
+                         ids.data_ptr<int32_t>(), counts.data_ptr<int32_t>(), rep.data_ptr<float>(),
+                         freq.data_ptr<float>(), pres.data_ptr<float>(), boff.data_ptr<int32_t>(),
+                         bias_ids.data_ptr<int32_t>(), bias_vals.data_ptr<float>(), cur_stream(logits));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
   m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none(),
@@ -871,6 +894,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("shard_push_add", &shard_push_add);
   m.def("peer_barrier", &peer_barrier);
   m.def("gguf_dequant", &gguf_dequant);
+  m.def("apply_penalties", &apply_penalties);
   m.def("flag_wait_probe", &flag_wait_probe);
   m.def("ar_pull_norm", &ar_pull_norm);
   m.def("ep_combine_norm", &ep_combine_norm);

@@ -305,5 +305,9 @@ struct SampleArgs {
   int64_t ws_elems;
 };
 void sample_launch(const SampleArgs& a, cudaStream_t st);
+// repetition / frequency / presence penalties + logit bias, in place (CSR per row)
+void penalties_launch(float* logits, int64_t ld, int64_t B, int64_t V, const int32_t* off, const int32_t* ids,
+                      const int32_t* counts, const float* rep, const float* freq, const float* pres,
+                      const int32_t* boff, const int32_t* bias_ids, const float* bias_vals, cudaStream_t st);
 
 }  // namespace b200

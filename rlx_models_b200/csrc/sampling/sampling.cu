@@ -262,7 +262,49 @@ __global__ void __launch_bounds__(kThreads) sample_kernel(SampleArgs a) {
   }
 }
 
+// Penalties and logit bias, in place on fp32 logits before token selection.
+// Row r's distinct previously seen tokens are ids[off[r] .. off[r + 1]) with
+// their counts; its biases are bias_ids / bias_vals[boff[r] .. boff[r + 1]).
+//   repetition (CTRL, Keskar et al. 2019, as HF applies it): x / rep if x > 0
+//   else x * rep, for every listed token (prompt and output); frequency:
+//   x -= freq * count; presence: x -= pres, for tokens generated (count > 0).
+// Each (row, token) pair appears once, so threads never collide.
+__global__ void penalties_kernel(float* __restrict__ logits, int64_t ld, const int32_t* __restrict__ off,
+                                 const int32_t* __restrict__ ids, const int32_t* __restrict__ counts,
+                                 const float* __restrict__ rep, const float* __restrict__ freq,
+                                 const float* __restrict__ pres, const int32_t* __restrict__ boff,
+                                 const int32_t* __restrict__ bias_ids, const float* __restrict__ bias_vals,
+                                 int64_t V) {
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x;
+  float* x = logits + (int64_t)row * ld;
+  const float rp = rep[row], fq = freq[row], pr = pres[row];
+  for (int i = off[row] + threadIdx.x; i < off[row + 1]; i += blockDim.x) {
+    const int t = ids[i];
+    if (t < 0 || t >= V) continue;
+    float v = x[t];
+    if (rp != 1.f) v = v > 0.f ? v / rp : v * rp;
+    const int n = counts[i];  // 0: seen in the prompt only (repetition penalty applies, the others do not)
+    if (n > 0) v -= fq * (float)n + pr;
+    x[t] = v;
+  }
+  __syncthreads();
+  for (int i = boff[row] + threadIdx.x; i < boff[row + 1]; i += blockDim.x) {
+    const int t = bias_ids[i];
+    if (t >= 0 && t < V) x[t] += bias_vals[i];
+  }
+}
+
 }  // namespace smp
+
+void penalties_launch(float* logits, int64_t ld, int64_t B, int64_t V, const int32_t* off, const int32_t* ids,
+                      const int32_t* counts, const float* rep, const float* freq, const float* pres,
+                      const int32_t* boff, const int32_t* bias_ids, const float* bias_vals, cudaStream_t st) {
+  if (B == 0) return;
+  launch_pdl(smp::penalties_kernel, dim3((unsigned)B), dim3(128), 0, st, logits, ld, off, ids, counts, rep, freq,
+             pres, boff, bias_ids, bias_vals, V);
+}
 
 void argmax_launch(const float* logits, int64_t ld, int64_t B, int64_t V, int32_t* out, cudaStream_t st) {
   if (B == 0) return;

@@ -297,3 +297,37 @@ def gguf_dequant(raw: torch.Tensor, kind: str, shape, dtype: torch.dtype = torch
     _count(1)
     ext().gguf_dequant(raw.contiguous(), tid, out)
     return out
+
+
+def apply_penalties(logits: torch.Tensor, rows: list) -> torch.Tensor:
+    """In place on fp32 ``logits`` [B, V]: per row ``(counts: dict[token, n],
+    repetition, frequency, presence, bias: dict[token, value] | None)`` or
+    None for an untouched row. Repetition scales x by 1/rep (x > 0) or rep
+    for every listed token; frequency subtracts freq * n and presence pres
+    for tokens with n > 0; bias adds."""
+    B = logits.shape[0]
+    off, ids, cnt, boff, bids, bval = [0], [], [], [0], [], []
+    rep, freq, pres = [1.0] * B, [0.0] * B, [0.0] * B
+    for r in range(B):
+        row = rows[r] if r < len(rows) else None
+        if row is not None:
+            counts, rep[r], freq[r], pres[r], bias = row
+            for t, n in counts.items():
+                ids.append(int(t))
+                cnt.append(int(n))
+            for t, v in (bias or {}).items():
+                bids.append(int(t))
+                bval.append(float(v))
+        off.append(len(ids))
+        boff.append(len(bids))
+    dev = logits.device
+
+    def up(v, dt):
+        return torch.tensor(v if v else [0], dtype=dt).pin_memory().to(dev, non_blocking=True)
+
+    i32, f32 = torch.int32, torch.float32
+    _count(1)
+    ext().apply_penalties(logits, up(off, i32), up(ids, i32)[:len(ids)], up(cnt, i32)[:len(cnt)], up(rep, f32),
+                          up(freq, f32), up(pres, f32), up(boff, i32), up(bids, i32)[:len(bids)],
+                          up(bval, f32)[:len(bval)])
+    return logits

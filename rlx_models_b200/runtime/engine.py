@@ -46,6 +46,17 @@ class SamplingParams:
     ignore_eos: bool = False
     stop_token_ids: list[int] = field(default_factory=list)
     logprobs: bool = False
+    # penalties (applied on the GPU before selection; such rows take the eager path):
+    # repetition (HF / CTRL: over prompt + output), frequency and presence (OpenAI: output only)
+    repetition_penalty: float = 1.0
+    frequency_penalty: float = 0.0
+    presence_penalty: float = 0.0
+    logit_bias: dict | None = None
+
+    @property
+    def penalised(self) -> bool:
+        return (self.repetition_penalty != 1.0 or self.frequency_penalty != 0.0 or self.presence_penalty != 0.0
+                or bool(self.logit_bias))
 
 
 @dataclass
@@ -74,6 +85,8 @@ class RequestState:
     tokens: list[int] = field(default_factory=list)
     logprobs: list[float] = field(default_factory=list)
     finish_reason: str | None = None
+    prompt: list[int] | None = None     # kept for the repetition penalty
+    out_counts: dict | None = None      # token -> count of generated tokens (penalised requests)
 
 
 @dataclass
@@ -139,7 +152,12 @@ class LLMEngine:
         params = params or SamplingParams()
         sid = self.sched.add_request(list(map(int, prompt)), int(params.max_new_tokens), bool(params.ignore_eos),
                                      list(params.stop_token_ids))
-        self.requests[sid] = RequestState(sid, len(prompt), params, time.perf_counter())
+        st = RequestState(sid, len(prompt), params, time.perf_counter())
+        if params.penalised:
+            st.out_counts = {}
+            if params.repetition_penalty != 1.0:
+                st.prompt = list(map(int, prompt))
+        self.requests[sid] = st
         return sid
 
     def abort(self, sid: int):
@@ -167,14 +185,36 @@ class LLMEngine:
                 greedy = False
         return greedy
 
-    def _sample(self, logits: torch.Tensor, R: int, greedy: bool):
+    def _penalty_rows(self, sids: list[int]):
+        """Per-row penalty tables for ops.apply_penalties (None when no row of
+        the step is penalised): output tokens with their counts, plus prompt
+        tokens at count 0 when the repetition penalty is on."""
+        rows, any_pen = [], False
+        for sid in sids:
+            st = self.requests[sid]
+            p = st.params
+            if st.out_counts is None:
+                rows.append(None)
+                continue
+            any_pen = True
+            counts = st.out_counts
+            if st.prompt:
+                counts = dict.fromkeys(st.prompt, 0)
+                counts.update(st.out_counts)
+            rows.append((counts, p.repetition_penalty, p.frequency_penalty, p.presence_penalty, p.logit_bias))
+        return rows if any_pen else None
+
+    def _sample(self, logits: torch.Tensor, R: int, greedy: bool, pen=None):
         out = self.tok_out[:R]
         comm = getattr(self.model, "comm", None)
         if comm is not None and getattr(self.model, "tp_size", 1) > 1:
             # vocab-parallel logits: every rank must pick the same tokens
-            if greedy:
+            if greedy and pen is None:
                 return comm.greedy(logits, out)
             logits = comm.gather_logits(logits)
+        if pen is not None:
+            logits = logits.float() if logits.dtype != torch.float32 else logits
+            ops.apply_penalties(logits, pen)
         if greedy:
             ops.argmax(logits, out=out)
         else:
@@ -270,8 +310,9 @@ class LLMEngine:
             return []
         sids = h["sample_ids"][:R].tolist()
         greedy = self._params_rows(sids)
-        B = self._bucket(nd) if (npf == 0 and self.cfg.cuda_graphs and not hasattr(self.model, "share_tokens")) \
-            else None
+        pen = self._penalty_rows(sids)
+        B = self._bucket(nd) if (npf == 0 and self.cfg.cuda_graphs and not hasattr(self.model, "share_tokens")
+                                 and pen is None) else None
         if B is not None:
             key = (B, greedy)
             if key not in self.graphs:
@@ -288,7 +329,7 @@ class LLMEngine:
             if logits is None:  # a non-final pipeline stage: tokens come from the last stage
                 toks = self.tok_out[:R]
             else:
-                toks = self._sample(logits, R, greedy)
+                toks = self._sample(logits, R, greedy, pen)
             if hasattr(self.model, "share_tokens"):
                 self.model.share_tokens(self.tok_out[:R])
                 toks = self.tok_out[:R]
@@ -301,6 +342,8 @@ class LLMEngine:
         for r, sid in enumerate(sids):
             st = self.requests[sid]
             st.tokens.append(tl[r])
+            if st.out_counts is not None:
+                st.out_counts[tl[r]] = st.out_counts.get(tl[r], 0) + 1
             st.token_times.append(now)
             if st.first_token is None:
                 st.first_token = now

@@ -36,7 +36,11 @@ def _params(body: dict, eos: int | None) -> tuple[SamplingParams, list[str]]:
                         top_k=int(body.get("top_k") or 0), top_p=float(body.get("top_p") or 1.0),
                         min_p=float(body.get("min_p") or 0.0), seed=int(body.get("seed") or 0),
                         ignore_eos=bool(body.get("ignore_eos", False)), stop_token_ids=stop_ids,
-                        logprobs=bool(body.get("logprobs")))
+                        logprobs=bool(body.get("logprobs")),
+                        repetition_penalty=float(body.get("repetition_penalty") or 1.0),
+                        frequency_penalty=float(body.get("frequency_penalty") or 0.0),
+                        presence_penalty=float(body.get("presence_penalty") or 0.0),
+                        logit_bias={int(k): float(v) for k, v in (body.get("logit_bias") or {}).items()} or None)
     return sp, list(stop)
 
 

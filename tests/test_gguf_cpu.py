@@ -137,3 +137,44 @@ def test_model_from_gguf_matches_safetensors(tmp_path, model_type):
     gq = G.GGUFWeights(pq, dtype=torch.float32)
     c, _ = DecoderOracle(gq.config, {k: gq.take(k) for k in gq.keys()}).forward(ids)
     assert ((c - a).norm() / a.norm()) < 2e-2
+
+
+# -- MLX quantised checkpoints ---------------------------------------------------
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+def test_mlx_pack_roundtrip(bits):
+    from rlx_models_b200.weights import mlx as M
+    w = torch.randn(48, 256, generator=torch.Generator().manual_seed(bits))
+    wq, sc, bi = M.quantize(w, bits, 64)
+    assert wq.dtype == torch.int32 and wq.shape == (48, 256 * bits // 32) and sc.shape == (48, 4)
+    q = M.unpack_codes(wq, bits)
+    assert int(q.min()) >= 0 and int(q.max()) <= (1 << bits) - 1
+    # code j of a row sits at bits [(j % per) * bits, ...) of word j // per, least significant first
+    per = 32 // bits
+    word = (wq[3, 1].item() & 0xFFFFFFFF)
+    assert q[3, per + 2].item() == (word >> (2 * bits)) & ((1 << bits) - 1)
+    y = M.dequantize(wq, sc, bi, bits, 64)
+    err = ((y - w).norm() / w.norm()).item()
+    assert err < {2: 0.5, 4: 0.12, 8: 0.01}[bits]
+
+
+def test_mlx_checkpoint_loads_into_model(tmp_path):
+    from rlx_models_b200 import config as C
+    from rlx_models_b200.models.oracle import DecoderOracle
+    from rlx_models_b200.weights import mlx as M
+    from rlx_models_b200.weights.init import random_weights
+    cfg = C.tiny(num_hidden_layers=2, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=64, vocab_size=256)
+    w = random_weights(cfg, 0)
+    d = str(tmp_path / "mlx")
+    cfg.save(d)
+    import json
+    raw = json.load(open(tmp_path / "mlx" / "config.json"))
+    M.save_mlx(d, w, raw, bits=8, group_size=64)
+    assert M.MLXWeights.is_mlx_dir(d)
+    mw = M.MLXWeights(d, dtype=torch.float32)
+    assert set(mw.keys()) == set(w.keys())
+    ids = torch.randint(0, 256, (10,), generator=torch.Generator().manual_seed(0))
+    a, _ = DecoderOracle(cfg, {k: v.float() for k, v in w.items()}).forward(ids)
+    b, _ = DecoderOracle(cfg, {k: mw.take(k) for k in mw.keys()}).forward(ids)
+    assert ((b - a).norm() / a.norm()).item() < 3e-2
