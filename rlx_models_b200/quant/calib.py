@@ -72,10 +72,61 @@ def mxfp4_rtn(w: torch.Tensor) -> torch.Tensor:
     return dequantize_mxfp4(b, s)
 
 
+def quantize_int_group(w: torch.Tensor, bits: int = 4, group: int = 128):
+    """Group-wise symmetric integer RTN: per group of ``group`` input columns
+    scale = amax / (2^(bits-1) - 1), codes in [-(2^(bits-1) - 1), 2^(bits-1) - 1]
+    -> (int8 codes [out, in], fp32 scales [out, in / group])."""
+    out_f, in_f = w.shape
+    g = min(group, in_f)
+    qmax = (1 << (bits - 1)) - 1
+    wg = w.float().view(out_f, in_f // g, g)
+    scale = (wg.abs().amax(-1) / qmax).clamp_min(1e-12)
+    q = (wg / scale.unsqueeze(-1)).round().clamp(-qmax, qmax).to(torch.int8)
+    return q.view(out_f, in_f), scale
+
+
+def dequantize_int_group(q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    out_f, in_f = q.shape
+    g = in_f // scale.shape[1]
+    return (q.float().view(out_f, -1, g) * scale.unsqueeze(-1)).view(out_f, in_f)
+
+
+def quantize_bitnet(w: torch.Tensor):
+    """BitNet b1.58 weights (Ma et al. 2024): ternary codes round(W / mean|W|)
+    clipped to {-1, 0, 1} with the per-tensor absmean as the scale."""
+    scale = w.float().abs().mean().clamp_min(1e-8)
+    q = (w.float() / scale).round().clamp(-1, 1).to(torch.int8)
+    return q, scale
+
+
+def dequantize_bitnet(q: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    return q.float() * scale
+
+
+def pack_ternary(q: torch.Tensor) -> torch.Tensor:
+    """{-1, 0, 1} codes -> 2-bit fields (code + 1), four per byte, low bits first."""
+    u = (q.to(torch.int16) + 1).to(torch.uint8).view(q.shape[0], -1, 4)
+    return u[..., 0] | (u[..., 1] << 2) | (u[..., 2] << 4) | (u[..., 3] << 6)
+
+
+def unpack_ternary(p: torch.Tensor) -> torch.Tensor:
+    f = torch.stack([(p >> s) & 3 for s in (0, 2, 4, 6)], -1).to(torch.int8) - 1
+    return f.view(p.shape[0], -1)
+
+
+def bitnet_activation_quant(x: torch.Tensor):
+    """Per-token int8 absmax activations of BitNet b1.58: (int8 codes, fp32 scale [tokens, 1])."""
+    s = (x.float().abs().amax(-1, keepdim=True) / 127).clamp_min(1e-8)
+    return (x.float() / s).round().clamp(-128, 127).to(torch.int8), s
+
+
 FORMATS = {
     "mxfp4": mxfp4_rtn,
     "nvfp4": lambda w: dequantize_nvfp4(*quantize_nvfp4(w)),
     "fp8": lambda w: dequantize_fp8(*quantize_fp8(w)),
+    "int4": lambda w: dequantize_int_group(*quantize_int_group(w, 4)),
+    "int8": lambda w: dequantize_int_group(*quantize_int_group(w, 8)),
+    "bitnet": lambda w: dequantize_bitnet(*quantize_bitnet(w)),
 }
 
 
@@ -113,12 +164,17 @@ def _group_scale(fmt: str, grp: torch.Tensor) -> torch.Tensor:
         return (amax / 6.0).to(torch.float8_e4m3fn).float().clamp_min(1e-30)
     if fmt == "fp8":
         return amax / 448.0
+    if fmt in ("int4", "int8"):
+        return amax / ((1 << ((4 if fmt == "int4" else 8) - 1)) - 1)
     raise ValueError(fmt)
 
 
 def _quant_col(fmt: str, col: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
     if fmt == "fp8":
         return (col / scale).clamp(-448, 448).to(torch.float8_e4m3fn).float() * scale
+    if fmt in ("int4", "int8"):
+        qmax = (1 << ((4 if fmt == "int4" else 8) - 1)) - 1
+        return (col / scale).round().clamp(-qmax, qmax) * scale
     v = (col / scale).clamp(-6.0, 6.0)
     return E2M1.to(col.device)[_e2m1_round(v).long()] * scale
 
@@ -129,7 +185,10 @@ def gptq(w: torch.Tensor, x: torch.Tensor, fmt: str = "mxfp4", group: int | None
     with its group's scale (fixed at the group's first column from the
     error-corrected weights), the rounding error spread over the remaining
     columns through the upper Cholesky factor of the damped inverse Hessian."""
-    group = group or {"mxfp4": 32, "nvfp4": 16, "fp8": w.shape[1]}[fmt]
+    if fmt == "bitnet":
+        raise ValueError("GPTQ needs a group-wise format; BitNet ternary weights use RTN (per-tensor absmean)")
+    group = group or {"mxfp4": 32, "nvfp4": 16, "fp8": w.shape[1], "int4": 128, "int8": 128}[fmt]
+    group = min(group, w.shape[1])
     W = w.float().clone()
     out_f, in_f = W.shape
     H = x.float().t() @ x.float()

@@ -39,7 +39,17 @@ NORM_OF = {"self_attn.q_proj": "input_layernorm", "self_attn.k_proj": "input_lay
 
 
 def pack(name: str, w: torch.Tensor, fmt: str) -> dict[str, torch.Tensor]:
+    from .calib import pack_ternary, quantize_bitnet, quantize_int_group
     base = name[:-len(".weight")]
+    if fmt in ("int4", "int8"):
+        q, sc = quantize_int_group(w, 4 if fmt == "int4" else 8)
+        if fmt == "int4":  # two codes per byte, low nibble first (two's complement nibbles)
+            u = (q.to(torch.int16) & 0xF).to(torch.uint8)
+            q = (u[:, 0::2] | (u[:, 1::2] << 4))
+        return {base + f".weight_{fmt}": q, base + ".weight_group_scale": sc}
+    if fmt == "bitnet":
+        q, sc = quantize_bitnet(w)
+        return {base + ".weight_ternary": pack_ternary(q), base + ".weight_scale": sc.reshape(1)}
     if fmt == "mxfp4":
         b, s = quantize_mxfp4(w.float())
         return {base + ".weight_blocks": b, base + ".weight_scales": s}
@@ -69,7 +79,22 @@ def load_quantized(path: str) -> dict[str, torch.Tensor]:
             from .calib import dequantize_nvfp4
             out[base + ".weight"] = dequantize_nvfp4(c, get(base + ".weight_block_scale"),
                                                      get(base + ".weight_tensor_scale").float()).bfloat16()
-        elif n.endswith(("_scales", "_scale", ".weight_block_scale", ".weight_tensor_scale")):
+        elif n.endswith((".weight_int4", ".weight_int8")):
+            from .calib import dequantize_int_group
+            base, kind = n.rsplit(".weight_", 1)
+            q = get(n)
+            if kind == "int4":
+                lo = (q & 0xF).to(torch.int8)
+                hi = (q >> 4).to(torch.int8)
+                lo = torch.where(lo > 7, lo - 16, lo)
+                hi = torch.where(hi > 7, hi - 16, hi)
+                q = torch.stack([lo, hi], -1).reshape(q.shape[0], -1)
+            out[base + ".weight"] = dequantize_int_group(q, get(base + ".weight_group_scale").float()).bfloat16()
+        elif n.endswith(".weight_ternary"):
+            from .calib import unpack_ternary
+            base = n[:-len(".weight_ternary")]
+            out[base + ".weight"] = (unpack_ternary(get(n)).float() * get(base + ".weight_scale").float()).bfloat16()
+        elif n.endswith(("_scales", "_scale", ".weight_block_scale", ".weight_tensor_scale", ".weight_group_scale")):
             continue
         elif get(n).dtype == torch.float8_e4m3fn:
             out[n] = (get(n).float() * get(n[:-len(".weight")] + ".weight_scale")[:, None]).bfloat16()
@@ -83,6 +108,13 @@ def quantize_checkpoint(src: str, out: str, algo: str = "gptq", fmt: str = "mxfp
     """Quantise every dense decoder linear of ``src`` into ``out``; returns the
     per-linear relative output error on the calibration activations."""
     from .calib import output_error
+    gguf_kind = None
+    if fmt.startswith("gguf:"):  # e.g. gguf:Q4_K - GGUF output, RTN / AWQ on the ggml block format
+        gguf_kind = fmt.split(":", 1)[1]
+        from ..weights.gguf import dequantize, quantize
+        FORMATS[fmt] = lambda w, k=gguf_kind: dequantize(quantize(w, k), k, w.shape)
+        if algo == "gptq":
+            raise ValueError("GPTQ targets the group-wise formats; use rtn or awq with a GGUF output")
     cfg = DecoderConfig.from_file(src)
     wm = WeightMap.from_dir(src)
     weights = {n: wm.peek(n) for n in wm.keys()}
@@ -119,15 +151,21 @@ def quantize_checkpoint(src: str, out: str, algo: str = "gptq", fmt: str = "mxfp
                 else:
                     stored, eff = w, FORMATS[fmt](w)
                 report[n] = output_error(w, eff, x) if x is not None else None
-                result.update(pack(n, stored, fmt))
+                result.update({n: stored.to(weights[n].dtype)} if gguf_kind else pack(n, stored, fmt))
     for name, w in weights.items():
         if name not in result and not any(name.endswith(l + ".weight") for l in LINEARS):
             result[name] = w
     os.makedirs(out, exist_ok=True)
+    if gguf_kind is not None:
+        # GGUF sink: the (AWQ-scaled) weights quantised to a ggml block format in one .gguf file
+        from ..weights.gguf import save_gguf
+        save_gguf(os.path.join(out, f"model-{gguf_kind}.gguf"), result, cfg, kind=gguf_kind)
+        return report
     save_file(result, os.path.join(out, "model.safetensors"))
     hf = cfg.to_hf_dict()
     hf["quantization_config"] = {"quant_method": fmt, "algorithm": algo,
-                                 "group_size": {"mxfp4": 32, "nvfp4": 16, "fp8": -1}[fmt]}
+                                 "group_size": {"mxfp4": 32, "nvfp4": 16, "fp8": -1, "int4": 128, "int8": 128,
+                                                "bitnet": -1}[fmt]}
     with open(os.path.join(out, "config.json"), "w") as f:
         json.dump(hf, f, indent=1)
     return report
@@ -138,7 +176,8 @@ def main(argv=None):
     ap.add_argument("--model", required=True)
     ap.add_argument("--out", required=True)
     ap.add_argument("--algo", default="gptq", choices=["rtn", "awq", "gptq"])
-    ap.add_argument("--format", default="mxfp4", choices=["mxfp4", "nvfp4", "fp8"])
+    ap.add_argument("--format", default="mxfp4",
+                    help="mxfp4 | nvfp4 | fp8 | int4 | int8 | bitnet | gguf:<ggml type, e.g. Q4_K, Q8_0, Q6_K>")
     ap.add_argument("--calib-tokens", type=int, default=2048)
     ap.add_argument("--seed", type=int, default=0)
     a = ap.parse_args(argv)

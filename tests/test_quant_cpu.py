@@ -85,3 +85,53 @@ def test_quantize_checkpoint_roundtrip_and_algorithms():
                 errs[(algo, fmt)] = float((lg - ref).norm() / ref.norm())
         assert errs[("rtn", "fp8")] < errs[("rtn", "mxfp4")]
         assert all(e < 0.5 for e in errs.values()), errs
+
+
+def test_int_group_bitnet_formats():
+    from rlx_models_b200.quant import calib as Q
+    w = torch.randn(64, 256, generator=torch.Generator().manual_seed(0))
+    for fmt, tol in (("int8", 0.01), ("int4", 0.15)):
+        e = ((Q.FORMATS[fmt](w) - w).norm() / w.norm()).item()
+        assert e < tol, (fmt, e)
+    q, s = Q.quantize_bitnet(w)
+    assert set(q.unique().tolist()) <= {-1, 0, 1} and abs(float(s) - w.abs().mean().item()) < 1e-6
+    assert torch.equal(Q.unpack_ternary(Q.pack_ternary(q)), q)
+    x = torch.randn(5, 256)
+    xq, xs = Q.bitnet_activation_quant(x)
+    assert xq.dtype == torch.int8 and ((xq.float() * xs - x).abs().max() <= xs.max() / 2 + 1e-6)
+    xa = torch.randn(512, 256)
+    g = Q.gptq(w, xa, "int4")
+    assert Q.output_error(w, g, xa) < Q.output_error(w, Q.FORMATS["int4"](w), xa)
+
+
+def test_quantize_checkpoint_int_bitnet_and_gguf_sink(tmp_path):
+    from rlx_models_b200 import config as C
+    from rlx_models_b200.models.oracle import DecoderOracle
+    from rlx_models_b200.quant.tool import load_quantized, quantize_checkpoint
+    from rlx_models_b200.weights.gguf import GGUFWeights
+    from rlx_models_b200.weights.init import random_weights
+    from rlx_models_b200.weights.weight_map import WeightMap
+
+    cfg = C.tiny(num_hidden_layers=2, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=64, vocab_size=256)
+    w = random_weights(cfg, 0, dtype=torch.float32)
+    calib = [torch.randint(0, 256, (64,), generator=torch.Generator().manual_seed(s)) for s in range(2)]
+    ids = torch.randint(0, 256, (16,), generator=torch.Generator().manual_seed(9))
+    src = str(tmp_path / "src")
+    WeightMap(dict(w)).save(src)
+    cfg.save(src)
+    ref, _ = DecoderOracle(cfg, w).forward(ids)
+    errs = {}
+    for algo, fmt in (("rtn", "int8"), ("gptq", "int4"), ("rtn", "bitnet")):
+        out = str(tmp_path / f"{algo}_{fmt}")
+        quantize_checkpoint(src, out, algo, fmt, calib)
+        wq = load_quantized(out)
+        lg, _ = DecoderOracle(cfg, {k: v.float() for k, v in wq.items()}).forward(ids)
+        errs[fmt] = float((lg - ref).norm() / ref.norm())
+    assert errs["int8"] < errs["int4"] < errs["bitnet"] and errs["int8"] < 0.02, errs
+    for algo in ("rtn", "awq"):
+        out = str(tmp_path / f"gguf_{algo}")
+        quantize_checkpoint(src, out, algo, "gguf:Q8_0", calib)
+        gw = GGUFWeights(os.path.join(out, "model-Q8_0.gguf"), dtype=torch.float32)
+        lg, _ = DecoderOracle(gw.config, {k: gw.take(k) for k in gw.keys()}).forward(ids)
+        assert float((lg - ref).norm() / ref.norm()) < 0.03
