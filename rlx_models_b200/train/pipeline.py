@@ -80,8 +80,8 @@ class StageDecoder(TrainableDecoder):
         inv, mult = rope_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling, cfg.max_position_embeddings)
         freqs = torch.outer(torch.arange(max_seq, dtype=torch.float32), inv)
         emb = torch.cat([freqs, freqs], -1)
-        self.cos = (emb.cos() * mult).to(self.device, param_dtype)
-        self.sin = (emb.sin() * mult).to(self.device, param_dtype)
+        self.cos = (emb.cos() * mult).to(self.device, torch.bfloat16)  # the same tables as TrainableDecoder
+        self.sin = (emb.sin() * mult).to(self.device, torch.bfloat16)
 
     @property
     def groups(self) -> list[FlatGroup]:
@@ -186,7 +186,7 @@ class PipelineTrainer:
             h.wait()
         # loss lives on the last stage; share it
         dist.broadcast(total, src=self._peer(Sg - 1), group=self.group)
-        if self.tied:  # first and last stage hold copies of the tied embedding: sum their gradients
+        if self.tied and (m.first or m.last):  # both hold copies of the tied embedding: sum their gradients
             gr = m.embed_g.grad if m.first else m.head_g.grad
             dist.all_reduce(gr, group=self.tie_group)
         gnorm = self._clip_coef()
