@@ -116,6 +116,39 @@ class LLM:
                 return
 
     @torch.no_grad()
+    def embed(self, prompts, pooling: str = "last", normalize: bool = True) -> torch.Tensor:
+        """Sequence embeddings [N, H] (fp32) from the final-normed hidden states
+        of one batched prefill: ``pooling`` "last" (the last token, as
+        decoder embedding models such as Qwen3-Embedding use), "mean" or
+        "first"; L2-normalised unless ``normalize`` is False."""
+        from .models.decoder import ForwardBatch
+        single = isinstance(prompts, str) or (prompts and isinstance(prompts[0], int))
+        seqs = [self._encode(p) for p in ([prompts] if single else prompts)]
+        dev = self.model.device
+        nbs = [(len(s) + 15) // 16 for s in seqs]
+        W = max(nbs)
+        tables = torch.zeros(len(seqs), W, dtype=torch.int32)
+        slots, off = [], 0
+        for i, (s, nb) in enumerate(zip(seqs, nbs)):
+            tables[i, :nb] = torch.arange(off, off + nb, dtype=torch.int32)
+            slots.append(torch.arange(off * 16, off * 16 + len(s), dtype=torch.int64))
+            off += nb
+        lens = [len(s) for s in seqs]
+        cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0).tolist()), dtype=torch.int32)
+        kv = self.model.make_kv_cache(off)
+        fb = ForwardBatch(input_ids=torch.tensor([t for s in seqs for t in s], dtype=torch.int32, device=dev),
+                          positions=torch.cat([torch.arange(n, dtype=torch.int32) for n in lens]).to(dev),
+                          slots=torch.cat(slots).to(dev), num_decode=0, pre_block_tables=tables.to(dev),
+                          pre_ctx_lens=torch.tensor(lens, dtype=torch.int32, device=dev), pre_cu_q=cu.to(dev),
+                          pre_max_q=max(lens))
+        h = self.model.forward_hidden(fb, kv).float()
+        rows = []
+        for i in range(len(seqs)):
+            seg = h[int(cu[i]):int(cu[i + 1])]
+            rows.append(seg[-1] if pooling == "last" else seg.mean(0) if pooling == "mean" else seg[0])
+        e = torch.stack(rows)
+        return torch.nn.functional.normalize(e, dim=-1) if normalize else e
+
     def logits(self, prompt) -> torch.Tensor:
         """fp32 next-token logits for every prompt position (prefill only)."""
         from .models.decoder import ForwardBatch

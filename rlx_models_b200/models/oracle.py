@@ -148,6 +148,14 @@ class DecoderOracle:
     @torch.no_grad()
     def forward(self, ids: torch.Tensor, kv: OracleKV | None = None) -> tuple[torch.Tensor, OracleKV]:
         """ids: [T] new tokens continuing ``kv``. Returns fp32 logits [T, V]."""
+        h, kv = self.forward_hidden(ids, kv)
+        c = self.cfg
+        head = self.W("model.embed_tokens.weight") if c.tie_word_embeddings else self.W("lm_head.weight")
+        return h @ head.T, kv
+
+    @torch.no_grad()
+    def forward_hidden(self, ids: torch.Tensor, kv: OracleKV | None = None) -> tuple[torch.Tensor, OracleKV]:
+        """Final-normed hidden states [T, H] (the embedding models' last_hidden_state)."""
         c = self.cfg
         if kv is None:
             kv = OracleKV(c.num_hidden_layers)
@@ -158,9 +166,7 @@ class DecoderOracle:
             p = f"model.layers.{i}."
             h = h + self._attn(i, R.rmsnorm(h, self.W(p + "input_layernorm.weight"), c.rms_norm_eps), pos, kv)
             h = h + self._mlp(i, R.rmsnorm(h, self.W(p + "post_attention_layernorm.weight"), c.rms_norm_eps))
-        h = R.rmsnorm(h, self.W("model.norm.weight"), c.rms_norm_eps)
-        head = self.W("model.embed_tokens.weight") if c.tie_word_embeddings else self.W("lm_head.weight")
-        return h @ head.T, kv
+        return R.rmsnorm(h, self.W("model.norm.weight"), c.rms_norm_eps), kv
 
     @torch.no_grad()
     def generate(self, prompt: torch.Tensor, max_new_tokens: int) -> tuple[list[int], list[torch.Tensor]]:

@@ -1,0 +1,65 @@
+"""Dense decoder families beyond Qwen3 on the GPU against the fp32 oracle
+(Llama: no QK-norm, untied head; Qwen2: q/k/v biases; Mistral), and the
+``LLM.embed`` entry point against the oracle's final hidden states."""
+import pytest
+import torch
+
+from rlx_models_b200 import config as C
+from rlx_models_b200.models.decoder import DecoderLM, ForwardBatch
+from rlx_models_b200.models.oracle import DecoderOracle
+from rlx_models_b200.weights.init import random_weights
+
+pytestmark = pytest.mark.gpu
+
+
+def _prefill(model, ids, dev):
+    T = len(ids)
+    nb = (T + 15) // 16
+    fb = ForwardBatch(input_ids=torch.tensor(ids, dtype=torch.int32, device=dev),
+                      positions=torch.arange(T, dtype=torch.int32, device=dev),
+                      slots=torch.arange(T, dtype=torch.int64, device=dev), num_decode=0,
+                      pre_block_tables=torch.arange(nb, dtype=torch.int32, device=dev).view(1, -1),
+                      pre_ctx_lens=torch.tensor([T], dtype=torch.int32, device=dev),
+                      pre_cu_q=torch.tensor([0, T], dtype=torch.int32, device=dev), pre_max_q=T)
+    return model.forward(fb, model.make_kv_cache(nb))
+
+
+@pytest.mark.parametrize("family,over", [
+    ("llama", dict(qk_norm=False, tie_word_embeddings=False, rope_theta=5e5)),
+    ("qwen2", dict(qk_norm=False, attention_bias=True, tie_word_embeddings=True)),
+    ("mistral", dict(qk_norm=False, tie_word_embeddings=False, rope_theta=1e6)),
+])
+def test_family_vs_oracle(cuda, family, over):
+    cfg = C.tiny(family, num_hidden_layers=2, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=64, vocab_size=512, **over)
+    w = random_weights(cfg, 1, dtype=torch.bfloat16)
+    for k in list(w):
+        if k.endswith(".bias"):  # biases start at zero: make them matter
+            w[k] = (torch.randn(w[k].shape, generator=torch.Generator().manual_seed(7)) * 0.2).bfloat16()
+    model = DecoderLM(cfg, w, device=cuda)
+    ids = torch.randint(0, 512, (45,), generator=torch.Generator().manual_seed(2)).tolist()
+    lg = _prefill(model, ids, cuda).float().cpu()
+    ref, _ = DecoderOracle(cfg, {k: v.float() for k, v in w.items()}).forward(torch.tensor(ids))
+    rel = ((lg - ref).norm() / ref.norm()).item()
+    assert rel < 2e-2, rel
+    assert (lg.argmax(-1) == ref.argmax(-1)).float().mean() > 0.9
+
+
+def test_embed_matches_oracle_hidden(cuda):
+    from rlx_models_b200.api import LLM
+    from rlx_models_b200.runtime.engine import EngineConfig
+    cfg = C.tiny(num_hidden_layers=2, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=64, vocab_size=512)
+    w = random_weights(cfg, 3, dtype=torch.bfloat16)
+    llm = LLM(DecoderLM(cfg, w, device=cuda), EngineConfig(max_num_seqs=4, max_model_len=128, num_blocks=32))
+    g = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, 512, (n,), generator=g).tolist() for n in (5, 33, 17)]
+    oracle = DecoderOracle(cfg, {k: v.float() for k, v in w.items()})
+    for pooling in ("last", "mean"):
+        e = llm.embed(prompts, pooling=pooling).cpu()
+        for i, p in enumerate(prompts):
+            h, _ = oracle.forward_hidden(torch.tensor(p))
+            r = h[-1] if pooling == "last" else h.mean(0)
+            r = r / r.norm()
+            assert torch.nn.functional.cosine_similarity(e[i], r, dim=0) > 0.999
+    assert torch.allclose(e.norm(dim=-1), torch.ones(3), atol=1e-4)
