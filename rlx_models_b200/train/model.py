@@ -104,6 +104,9 @@ class TrainableDecoder:
             ln1, wqkv, wo, ln2, wgu, wd = w
             qn = kn = None
         B, S, H = h.shape
+        if getattr(self, "qat", None):  # quantisation-aware training: fake-quantised weights, STE gradients
+            from ..quant.dwq import fake_quant
+            wqkv, wo, wgu, wd = (fake_quant(t, self.qat) for t in (wqkv, wo, wgu, wd))
         if self.lora is not None:
             lp = self.lora.params()
             lin = lambda t, x, w: self.lora.linear(lp, i, t, x, w)

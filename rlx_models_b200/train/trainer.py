@@ -48,6 +48,9 @@ class TrainConfig:
     # device barrier per step); "nccl" materialises full gradients and calls
     # reduce_scatter_tensor per group
     grad_reduce: str = "push"
+    # quantisation-aware training: linear weights are fake-quantised to this
+    # format in the forward pass (quant/calib.py FORMATS), gradients straight-through
+    qat: str | None = None
 
     def lr_at(self, step: int) -> float:
         if self.warmup_steps and step < self.warmup_steps:
@@ -84,6 +87,7 @@ class Trainer:
         self.model = TrainableDecoder(model_cfg, weights, rank, world, self.device, group,
                                       activation_checkpointing=train_cfg.activation_checkpointing,
                                       param_dtype=getattr(torch, train_cfg.param_dtype))
+        self.model.qat = train_cfg.qat
         self.lora = None
         if train_cfg.lora_rank > 0:
             from .lora import LoraAdapters

@@ -135,3 +135,38 @@ def test_quantize_checkpoint_int_bitnet_and_gguf_sink(tmp_path):
         gw = GGUFWeights(os.path.join(out, "model-Q8_0.gguf"), dtype=torch.float32)
         lg, _ = DecoderOracle(gw.config, {k: gw.take(k) for k in gw.keys()}).forward(ids)
         assert float((lg - ref).norm() / ref.norm()) < 0.03
+
+
+def test_dwq_heals_quantised_layer():
+    from rlx_models_b200.quant.dwq import heal_linear
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(96, 128, generator=g) * 0.05
+    # activations occupy a low-dimensional subspace (as real layer inputs do), so the
+    # quantisation error they see has low rank and a rank-32 adapter can absorb it
+    x = torch.randn(512, 24, generator=g) @ torch.randn(24, 128, generator=g) + 0.01 * torch.randn(512, 128,
+                                                                                                     generator=g)
+    r = heal_linear(w, x, "int4", rank=32, steps=400)
+    assert r.healed_weight.shape == w.shape
+    assert r.dwq_error < 0.3 * r.quant_error, (r.quant_error, r.dwq_error)
+
+
+def test_qat_training_steps_and_ste():
+    from rlx_models_b200 import config as C
+    from rlx_models_b200.quant.dwq import fake_quant
+    from rlx_models_b200.train.trainer import TrainConfig, Trainer
+    from rlx_models_b200.weights.init import random_weights
+    w = torch.randn(8, 64, requires_grad=True)
+    y = fake_quant(w, "int4")
+    assert not torch.equal(y, w) and torch.allclose(y, w, atol=0.5 * w.abs().max().item() / 7 + 1e-6)  # half an int4 step
+    y.sum().backward()
+    assert torch.equal(w.grad, torch.ones_like(w))  # straight-through
+    cfg = C.tiny(num_hidden_layers=2, hidden_size=64, intermediate_size=128, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=16, vocab_size=96)
+    b = torch.randint(0, 96, (4, 17), generator=torch.Generator().manual_seed(1))
+    t = Trainer(cfg, TrainConfig(lr=1e-2, micro_batch=2, param_dtype="float32", qat="int4",
+                                 activation_checkpointing=False), random_weights(cfg, 0), device="cpu")
+    plain = Trainer(cfg, TrainConfig(lr=1e-2, micro_batch=2, param_dtype="float32",
+                                     activation_checkpointing=False), random_weights(cfg, 0), device="cpu")
+    lq = [t.step(b).loss for _ in range(4)]
+    lp = plain.step(b).loss
+    assert lq[-1] < lq[0] and abs(lq[0] - lp) > 1e-6  # trains, and the forward sees quantised weights
