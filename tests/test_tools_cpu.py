@@ -1,4 +1,5 @@
 """CPU tests: evaluation metrics, serving guardrails, pipeline stage planner."""
+import json
 import math
 
 import pytest
@@ -143,3 +144,54 @@ def test_plan_memory_weighting_and_state():
         P.plan([P.LayerSpec(0, 1), P.LayerSpec(2, 1)], nodes)
     over = P.plan(layers, [P.NodeSpec("x", 10 * G)])
     assert over.max_utilisation > 1 and over.diagnostics
+
+
+# -- llm bench -----------------------------------------------------------------
+
+def test_llm_bench_dimensions(tmp_path):
+    from rlx_models_b200 import config as C
+    from rlx_models_b200.bench import llm_bench as LB
+    from rlx_models_b200.weights.init import random_weights
+    mock = LB.MockModel()
+    sp = LB.speed(mock, 32, 8)
+    assert sp.fields["gen_toks"] == 8 and sp.line().startswith("LLMBENCH kind=speed model=mock")
+    # the mock predicts last + 1: the gold continuation " B" follows "Answer:" only by chance, but raw mode
+    # scores continuations, and the perplexity of the counting sequence is ~1
+    expect = 1 / (math.exp(4) / (math.exp(4) + 255 * math.exp(-4)))  # the mock's probability of the right token
+    assert abs(LB.perplexity(mock, list(range(10, 200))).fields["ppl"] - expect) < 1e-4
+    mc = LB.multiple_choice(mock, LB.synthetic_mc(4), mode="raw")
+    assert mc.fields["n"] == 4 and 0.0 <= mc.fields["accuracy"] <= 1.0
+    # parity: an oracle against its own dump and against a perturbed copy
+    cfg = C.tiny(num_hidden_layers=1, hidden_size=64, intermediate_size=128, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=16, vocab_size=96)
+    w = random_weights(cfg, 0)
+    a = LB.OracleModel(cfg, w, "a")
+    prompts = [[1, 2, 3, 4], [5, 6, 7, 8, 9]]
+    ref = str(tmp_path / "ref.pt")
+    LB.save_reference(a, prompts, ref)
+    p = LB.parity(a, ref)
+    assert p.fields["argmax_match"] and p.fields["cosine_min"] > 0.99999
+    w2 = {k: (v + 0.05 * torch.randn_like(v) if k.endswith("proj.weight") else v) for k, v in w.items()}
+    p2 = LB.parity(LB.OracleModel(cfg, w2, "b"), a, prompts)
+    assert p2.fields["cosine_mean"] < 0.99999
+    rep = str(tmp_path / "r.md")
+    LB.report([sp, mc, p], rep)
+    assert open(rep).read().count("\n") == 5
+
+
+def test_llm_bench_gsm8k_and_cli(tmp_path, capsys):
+    from rlx_models_b200.bench import llm_bench as LB
+
+    class Scripted(LB.MockModel):
+        def generate(self, ids, n):
+            return list(b"so the total is 1,234."), 0.0, 0.0
+
+    rows = [{"question": "q", "answer": "steps #### 1234"}, {"question": "q", "answer": "#### 7"}]
+    r = LB.gsm8k(Scripted(), rows)
+    assert r.fields["accuracy"] == 0.5
+    data = tmp_path / "mc.jsonl"
+    data.write_text("\n".join(json.dumps(x) for x in LB.synthetic_mc(3)))
+    assert LB.main(["all", "--dry-run", "--data", str(data), "--report", str(tmp_path / "rep.md"),
+                    "--save-ref", str(tmp_path / "ref.pt"), "--ref", str(tmp_path / "ref.pt")]) == 0
+    out = capsys.readouterr().out
+    assert out.count("LLMBENCH") == 4 and "argmax_match=yes" in out
