@@ -62,6 +62,9 @@ def resolve_model_path(model: str) -> str | None:
     (snapshots/<rev>)."""
     if os.path.isdir(model) or (os.path.isfile(model) and model.lower().endswith(".gguf")):
         return model
+    if os.path.isfile(model) and model.lower().endswith(".rlxp"):  # packed model: unpack once into the cache
+        from .weights.assets import materialize
+        return materialize(model)
     if "/" in model:
         name, _, rev = parse_model_ref(model)
         root = os.environ.get("HF_HUB_CACHE") or os.path.join(

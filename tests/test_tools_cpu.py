@@ -1,5 +1,6 @@
 """CPU tests: evaluation metrics, serving guardrails, pipeline stage planner."""
 import json
+import os
 import math
 
 import pytest
@@ -195,3 +196,93 @@ def test_llm_bench_gsm8k_and_cli(tmp_path, capsys):
                     "--save-ref", str(tmp_path / "ref.pt"), "--ref", str(tmp_path / "ref.pt")]) == 0
     out = capsys.readouterr().out
     assert out.count("LLMBENCH") == 4 and "argmax_match=yes" in out
+
+
+# -- plugin + assets -----------------------------------------------------------
+
+def test_plugin_registry_and_model_facade():
+    from rlx_models_b200 import plugin as PL
+
+    class FakeTok:
+        eos_token_id = 2
+
+        def encode(self, s):
+            return {"<|im_end|>": [7], "<|endoftext|>": [2]}.get(s, list(s.encode()))
+
+        def decode(self, t):
+            return bytes(t).decode()
+
+        def apply_chat_template(self, msgs, add_generation_prompt=True, tokenize=False, tools=None):
+            return "".join(m["content"] for m in msgs)
+
+    class Out:
+        def __init__(self, t):
+            self.token_ids = t
+
+    class FakeLLM:
+        tokenizer = FakeTok()
+        config = type("Cfg", (), dict(model_type="qwen3", num_hidden_layers=2, hidden_size=8, vocab_size=9))()
+
+        def generate(self, prompt, params):
+            self.params = params
+            return [Out(list(b"hi") + [7])]
+
+    class FakeProvider:
+        name = "fake"
+
+        def can_open(self, path, opts):
+            return path.startswith("fake://")
+
+        def open(self, path, opts):
+            return PL.PluginModel(FakeLLM(), path, self.name)
+
+    PL.register_provider(FakeProvider())
+    try:
+        m = PL.open_model("fake://x", {"device": "cpu"})
+        assert m.info()["provider"] == "fake" and "chat" in m.info()["tasks"]
+        assert m.generate_text("q", max_tokens=5) == "hi"  # the end-of-turn token is stripped
+        assert set(m.stop_ids) == {7, 2} and m.llm.params.max_new_tokens == 5
+        assert m.chat([{"role": "user", "content": "yo"}]) == "hi"
+        with pytest.raises(ValueError):
+            PL.open_model("fake://x", {"bogus": 1})
+        with pytest.raises(FileNotFoundError):
+            PL.open_model("/nonexistent/model")
+    finally:
+        PL._PROVIDERS.pop(0)
+    rp = PL.RlxModelsProvider()
+    assert rp.can_open("qwen3-8b", {}) and not rp.can_open("/nonexistent", {})
+
+
+def test_asset_pack_roundtrip(tmp_path):
+    from rlx_models_b200 import config as C
+    from rlx_models_b200.weights import assets as A
+    from rlx_models_b200.weights.init import random_weights
+    from rlx_models_b200.weights.weight_map import WeightMap
+    cfg = C.tiny(num_hidden_layers=1, hidden_size=64, intermediate_size=128, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=16, vocab_size=96)
+    w = random_weights(cfg, 0)
+    d = str(tmp_path / "model")
+    WeightMap(dict(w)).save(d)
+    cfg.save(d)
+    pk = A.pack_dir(d, str(tmp_path / "model.rlxp"), {"name": "tiny"})
+    src = A.open_source(pk)
+    assert isinstance(src, A.PackSource) and "config.json" in src.names() and src.manifest["meta"]["name"] == "tiny"
+    out = A.materialize(pk, str(tmp_path / "unpacked"))
+    wm = WeightMap.from_dir(out)
+    assert all(torch.equal(wm.take(k), w[k]) for k in w)
+    mem = A.open_source({n: src.read(n) for n in src.names()})
+    out2 = A.materialize(mem, str(tmp_path / "mem"))
+    assert sorted(os.listdir(out2)) == sorted(os.listdir(out))
+    raw = bytearray(open(pk, "rb").read())
+    i = raw.find(b'"model_type"')
+    raw[i + 1] = ord("M")  # corrupt config.json inside the archive
+    with pytest.raises(A.AssetError):
+        A.PackSource(bytes(raw)).read("config.json")
+    os.environ["RLX_B200_ASSET_CACHE"] = str(tmp_path / "cache")
+    try:
+        from rlx_models_b200.api import resolve_model_path
+        p = resolve_model_path(pk)
+        assert p.startswith(str(tmp_path / "cache")) and os.path.exists(os.path.join(p, "config.json"))
+        assert resolve_model_path(pk) == p  # cached
+    finally:
+        del os.environ["RLX_B200_ASSET_CACHE"]
