@@ -52,11 +52,27 @@ class SamplingParams:
     frequency_penalty: float = 0.0
     presence_penalty: float = 0.0
     logit_bias: dict | None = None
+    # host-side logit processors (runtime/samplers.py), also eager-path only
+    typical_p: float = 1.0
+    xtc_threshold: float = 0.1
+    xtc_probability: float = 0.0
+    dry_multiplier: float = 0.0
+    dry_base: float = 1.75
+    dry_allowed_length: int = 2
+    dry_penalty_last_n: int = -1
+    mirostat: int = 0          # 2: Mirostat v2
+    mirostat_tau: float = 5.0
+    mirostat_eta: float = 0.1
 
     @property
     def penalised(self) -> bool:
         return (self.repetition_penalty != 1.0 or self.frequency_penalty != 0.0 or self.presence_penalty != 0.0
                 or bool(self.logit_bias))
+
+    @property
+    def processed(self) -> bool:
+        from .samplers import needs_processing
+        return needs_processing(self)
 
 
 @dataclass
@@ -85,8 +101,11 @@ class RequestState:
     tokens: list[int] = field(default_factory=list)
     logprobs: list[float] = field(default_factory=list)
     finish_reason: str | None = None
-    prompt: list[int] | None = None     # kept for the repetition penalty
+    prompt: list[int] | None = None     # kept for the repetition penalty and DRY
     out_counts: dict | None = None      # token -> count of generated tokens (penalised requests)
+    rng: object = None                  # XTC coin flips
+    mirostat_mu: float | None = None
+    mirostat_lp2: object = None
 
 
 @dataclass
@@ -153,9 +172,9 @@ class LLMEngine:
         sid = self.sched.add_request(list(map(int, prompt)), int(params.max_new_tokens), bool(params.ignore_eos),
                                      list(params.stop_token_ids))
         st = RequestState(sid, len(prompt), params, time.perf_counter())
-        if params.penalised:
+        if params.penalised or params.processed:
             st.out_counts = {}
-            if params.repetition_penalty != 1.0:
+            if params.repetition_penalty != 1.0 or params.dry_multiplier > 0:
                 st.prompt = list(map(int, prompt))
         self.requests[sid] = st
         return sid
@@ -197,8 +216,11 @@ class LLMEngine:
                 rows.append(None)
                 continue
             any_pen = True
+            if not p.penalised:
+                rows.append(None)
+                continue
             counts = st.out_counts
-            if st.prompt:
+            if st.prompt and p.repetition_penalty != 1.0:
                 counts = dict.fromkeys(st.prompt, 0)
                 counts.update(st.out_counts)
             rows.append((counts, p.repetition_penalty, p.frequency_penalty, p.presence_penalty, p.logit_bias))
@@ -214,7 +236,13 @@ class LLMEngine:
             logits = comm.gather_logits(logits)
         if pen is not None:
             logits = logits.float() if logits.dtype != torch.float32 else logits
-            ops.apply_penalties(logits, pen)
+            if any(r is not None for r in pen):
+                ops.apply_penalties(logits, pen)
+            from .samplers import process_row
+            for r, sid in enumerate(self._step_sids[:R]):
+                st = self.requests[sid]
+                if st.params.processed:
+                    process_row(logits[r], st.params, st, (st.prompt or []) + st.tokens)
         if greedy:
             ops.argmax(logits, out=out)
         else:
@@ -309,6 +337,7 @@ class LLMEngine:
         if T == 0:
             return []
         sids = h["sample_ids"][:R].tolist()
+        self._step_sids = sids
         greedy = self._params_rows(sids)
         pen = self._penalty_rows(sids)
         B = self._bucket(nd) if (npf == 0 and self.cfg.cuda_graphs and not hasattr(self.model, "share_tokens")
@@ -344,6 +373,9 @@ class LLMEngine:
             st.tokens.append(tl[r])
             if st.out_counts is not None:
                 st.out_counts[tl[r]] = st.out_counts.get(tl[r], 0) + 1
+                if st.params.mirostat == 2:
+                    from .samplers import mirostat_update
+                    mirostat_update(st.params, st, tl[r])
             st.token_times.append(now)
             if st.first_token is None:
                 st.first_token = now

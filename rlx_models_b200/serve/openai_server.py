@@ -24,6 +24,11 @@ from ..runtime.engine import SamplingParams
 from .runner import EngineRunner
 
 
+# llama.cpp-style sampler fields accepted on the request body
+_EXTRA_SAMPLING = ("typical_p", "xtc_threshold", "xtc_probability", "dry_multiplier", "dry_base",
+                   "dry_allowed_length", "dry_penalty_last_n", "mirostat", "mirostat_tau", "mirostat_eta")
+
+
 def _params(body: dict, eos: int | None) -> tuple[SamplingParams, list[str]]:
     stop = body.get("stop") or []
     if isinstance(stop, str):
@@ -40,7 +45,8 @@ def _params(body: dict, eos: int | None) -> tuple[SamplingParams, list[str]]:
                         repetition_penalty=float(body.get("repetition_penalty") or 1.0),
                         frequency_penalty=float(body.get("frequency_penalty") or 0.0),
                         presence_penalty=float(body.get("presence_penalty") or 0.0),
-                        logit_bias={int(k): float(v) for k, v in (body.get("logit_bias") or {}).items()} or None)
+                        logit_bias={int(k): float(v) for k, v in (body.get("logit_bias") or {}).items()} or None,
+                        **{k: type(getattr(SamplingParams, k))(body[k]) for k in _EXTRA_SAMPLING if k in body})
     return sp, list(stop)
 
 

@@ -66,3 +66,27 @@ def test_engine_penalties(cuda):
                                                 repetition_penalty=1e6))[0].token_ids
     assert not (set(rep) & set(prompt))  # prompt tokens pushed below every unseen token
     ops.check_errors(cuda)
+
+
+def test_engine_logit_processors(cuda):
+    from rlx_models_b200 import config as C
+    from rlx_models_b200.models.decoder import DecoderLM
+    from rlx_models_b200.runtime.engine import EngineConfig, LLMEngine, SamplingParams
+    from rlx_models_b200.weights.init import random_weights
+    cfg = C.tiny(num_hidden_layers=2, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=64, vocab_size=512)
+    m = DecoderLM(cfg, random_weights(cfg, 0), device=cuda)
+    eng = LLMEngine(m, EngineConfig(max_num_seqs=8, max_model_len=256, num_blocks=64))
+    prompt = list(range(40, 60))
+    sp = dict(max_new_tokens=48, ignore_eos=True)
+    dry = eng.generate([prompt], SamplingParams(**sp, dry_multiplier=1e3, dry_allowed_length=2))[0].token_ids
+    seq = prompt + dry
+    trigrams = [tuple(seq[i:i + 3]) for i in range(len(prompt) - 2, len(seq) - 2)]
+    assert len(set(trigrams)) == len(trigrams)  # no repeated 3-gram is ever extended
+    typ = eng.generate([prompt], SamplingParams(**sp, temperature=1.0, typical_p=0.2, seed=1))[0].token_ids
+    miro = eng.generate([prompt], SamplingParams(**sp, temperature=1.0, mirostat=2, mirostat_tau=3.0,
+                                                 seed=2))[0].token_ids
+    xtc = eng.generate([prompt], SamplingParams(**sp, temperature=1.0, xtc_probability=1.0, xtc_threshold=0.0,
+                                                seed=3))[0].token_ids
+    assert len(typ) == len(miro) == len(xtc) == 48
+    ops.check_errors(cuda)

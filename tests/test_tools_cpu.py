@@ -286,3 +286,35 @@ def test_asset_pack_roundtrip(tmp_path):
         assert resolve_model_path(pk) == p  # cached
     finally:
         del os.environ["RLX_B200_ASSET_CACHE"]
+
+
+# -- logit processors ------------------------------------------------------------
+
+def test_samplers_processors():
+    import random as _r
+    from rlx_models_b200.runtime import samplers as SM
+    x = torch.tensor([4.0, 3.9, 1.0, 0.0, -2.0])
+    t = SM.typical_mask(x, 0.5)
+    assert torch.isinf(t).sum() >= 2 and not torch.isinf(t[:2]).any()
+    # XTC: both top tokens exceed the threshold; only the less likely one survives
+    y = SM.xtc(x, 0.2, 1.0, _r.Random(0))
+    assert torch.isinf(y[0]) and y[1] == x[1] and torch.equal(y[2:], x[2:])
+    assert torch.equal(SM.xtc(x, 0.2, 0.0, _r.Random(0)), x)
+    # DRY: context "a b c x a b" -> extending with "c" repeats "a b c" (length 2 match before it)
+    pen = SM.dry_penalties([1, 2, 3, 9, 1, 2], multiplier=0.8, base=1.75, allowed=2)
+    assert set(pen) == {3} and abs(pen[3] - 0.8) < 1e-9
+    pen3 = SM.dry_penalties([1, 2, 3, 9, 1, 2, 3, 7, 1, 2], 1.0, 2.0, 2)
+    assert abs(pen3[3] - 1.0) < 1e-9 and 7 not in pen3 or pen3.get(7, 0) <= pen3[3]
+    assert SM.dry_penalties([1, 2], 0.0, 1.75, 2) == {}
+    # Mirostat v2: truncation by surprise and the mu update moves toward tau
+    lg = torch.log(torch.tensor([0.5, 0.25, 0.125, 0.125]))
+    out, lp2 = SM.mirostat_v2(lg, mu=1.5)
+    assert not torch.isinf(out[0]) and torch.isinf(out[1:]).all()
+
+    class St:
+        mirostat_mu, mirostat_lp2 = 10.0, None
+    p = type("P", (), dict(mirostat=2, mirostat_tau=5.0, mirostat_eta=0.1))()
+    st = St()
+    st.mirostat_lp2 = lp2
+    SM.mirostat_update(p, st, 0)  # surprise 1 bit < tau: mu rises
+    assert abs(st.mirostat_mu - (10.0 - 0.1 * (1.0 - 5.0))) < 1e-6
