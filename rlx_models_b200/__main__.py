@@ -90,6 +90,33 @@ def cmd_serve(a):
     return 0
 
 
+def cmd_profile(a):
+    """Profile engine steps: prefill the requests, then ``--steps`` decode
+    steps under the torch profiler; prints the top kernels by device time and
+    writes a Chrome trace. Decode CUDA graphs are off by default so every
+    kernel shows up on its own."""
+    import torch
+
+    from .api import load
+    from .runtime.engine import EngineConfig, SamplingParams
+    from .utils.trace import enable_nvtx, profile
+    enable_nvtx(True)
+    llm = load(a.model, engine_config=EngineConfig(max_num_seqs=max(8, a.batch), max_model_len=a.prompt_len + 512,
+                                                   kv_memory_gb=a.kv_gb, cuda_graphs=a.graphs))
+    eng = llm.engine
+    g = torch.Generator().manual_seed(0)
+    V = llm.config.vocab_size
+    for _ in range(a.batch):
+        eng.add_request(torch.randint(0, V, (a.prompt_len,), generator=g).tolist(),
+                        SamplingParams(max_new_tokens=a.steps + 64, ignore_eos=True))
+    while eng.stats["steps"] < 1 or any(len(st.tokens) == 0 for st in eng.requests.values()):
+        eng.step()  # prefill
+    rows = profile(eng.step, steps=a.steps, warmup=2, trace_path=a.trace)
+    for r in rows:
+        print(json.dumps(r))
+    return 0
+
+
 def cmd_bench(rest):
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, root)
@@ -131,6 +158,14 @@ def main(argv=None):
             p.add_argument("--host", default="127.0.0.1")
             p.add_argument("--port", type=int, default=8000)
             p.add_argument("--max-num-seqs", type=int, default=64)
+    p = sub.add_parser("profile")
+    p.add_argument("--model", default="qwen3-0.6b")
+    p.add_argument("--batch", type=int, default=8)
+    p.add_argument("--prompt-len", type=int, default=256)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--kv-gb", type=float, default=4.0)
+    p.add_argument("--graphs", action="store_true", help="keep decode CUDA graphs (kernels then appear per graph)")
+    p.add_argument("--trace", default="b200_trace.json")
     p = sub.add_parser("train")
     p.add_argument("--model", required=True)
     p.add_argument("--data", required=True, help="JSONL with 'text', 'prompt'/'completion' or 'input_ids'")
@@ -141,7 +176,8 @@ def main(argv=None):
     p.add_argument("--out", default=None)
     p.add_argument("--lora-rank", type=int, default=0)
     a = ap.parse_args(argv)
-    return {"inspect": cmd_inspect, "run": cmd_run, "serve": cmd_serve, "train": cmd_train}[a.cmd](a)
+    return {"inspect": cmd_inspect, "run": cmd_run, "serve": cmd_serve, "train": cmd_train,
+            "profile": cmd_profile}[a.cmd](a)
 
 
 if __name__ == "__main__":

@@ -25,6 +25,7 @@ from dataclasses import dataclass
 import torch
 
 from .. import ops
+from ..utils.trace import inspect, inspecting, nvtx
 from ..config import DecoderConfig
 from ..ops import interleave_gate_up, rope_inv_freq
 from ..runtime.kv_cache import PagedKVCache
@@ -168,13 +169,18 @@ class DecoderLM:
         x = comm.norm_in(h, self.layers[0].ln1)
         n = len(self.layers)
         for i, L in enumerate(self.layers):
-            a = self._attention(i, L, x, fb, kv)
-            x = comm.rowpar_add_norm(a, L.wo, h, L.ln2, bias=L.bo)
-            if x.shape[0] <= ops.ACC_MAX_M:
-                gu = ops.swiglu_acc(ops.linear_acc(x, L.w_gu))
-            else:
-                gu = ops.linear_swiglu(x, L.w_gu)
-            x = comm.rowpar_add_norm(gu, L.wd, h, self.layers[i + 1].ln1 if i + 1 < n else self.norm)
+            with nvtx(f"layer{i}"):
+                a = self._attention(i, L, x, fb, kv)
+                x = comm.rowpar_add_norm(a, L.wo, h, L.ln2, bias=L.bo)
+                if x.shape[0] <= ops.ACC_MAX_M:
+                    gu = ops.swiglu_acc(ops.linear_acc(x, L.w_gu))
+                else:
+                    gu = ops.linear_swiglu(x, L.w_gu)
+                x = comm.rowpar_add_norm(gu, L.wd, h, self.layers[i + 1].ln1 if i + 1 < n else self.norm)
+            if inspecting():
+                inspect(f"layer{i}.residual", h)
+        if inspecting():
+            inspect("final_hidden", x)
         return x
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:

@@ -25,6 +25,7 @@ from dataclasses import dataclass, field
 import torch
 
 from .. import ops
+from ..utils.trace import nvtx
 from ..models.decoder import ForwardBatch
 from .kv_cache import BLOCK_SIZE
 
@@ -328,6 +329,10 @@ class LLMEngine:
                 self._capture(B, greedy)
 
     def step(self) -> list[RequestOutput]:
+        with nvtx("engine.step"):
+            return self._step()
+
+    def _step(self) -> list[RequestOutput]:
         h = self.h
         info = self.sched.schedule(h["input_ids"], h["positions"], h["slots"], h["dec_tables"], h["dec_ctx"],
                                    h["pre_tables"], h["pre_ctx"], h["pre_cu"], h["logit_rows"], h["sample_ids"])

@@ -20,6 +20,7 @@ import torch
 import torch.distributed as dist
 
 from .. import ops
+from ..utils.trace import nvtx
 from ..weights.safetensors_io import Checkpoint, save_file
 from .fsdp import FlatGroup
 from .model import TrainableDecoder
@@ -64,6 +65,27 @@ class TrainConfig:
         return self.lr - (self.lr - lo) * frac
 
 
+class _Marks:
+    """Phase boundaries of a step: CUDA events on the device, wall clock on CPU."""
+
+    def __init__(self, device):
+        self.cuda = device.type == "cuda"
+        self.t = []
+
+    def __call__(self):
+        if self.cuda:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self.t.append(e)
+        else:
+            self.t.append(time.perf_counter())
+
+    def spans(self) -> list[float]:
+        if self.cuda:
+            return [a.elapsed_time(b) for a, b in zip(self.t, self.t[1:])]
+        return [(b - a) * 1e3 for a, b in zip(self.t, self.t[1:])]
+
+
 @dataclass
 class StepMetrics:
     step: int
@@ -72,6 +94,14 @@ class StepMetrics:
     lr: float
     tokens: int
     step_ms: float
+    compute_ms: float = 0.0   # forward + backward (device time on CUDA)
+    comm_ms: float = 0.0      # gradient barrier / reductions after backward
+    optim_ms: float = 0.0     # clip + AdamW
+
+    @property
+    def compute_fraction(self) -> float:
+        tot = self.compute_ms + self.comm_ms + self.optim_ms
+        return self.compute_ms / tot if tot > 0 else 0.0
 
     def __str__(self):
         return (f"step {self.step} loss {self.loss:.4f} |g| {self.grad_norm:.3f} lr {self.lr:.2e} "
@@ -130,25 +160,35 @@ class Trainer:
         global_tokens = max(1.0, float(n_valid))  # mean over the global batch's valid targets
         total = torch.zeros((), dtype=torch.float32, device=self.device)
         mb = max(1, c.micro_batch)
-        for s in range(0, B_local, mb):
-            loss = self.model.loss(ids[s:s + mb], tgt[s:s + mb], denom=global_tokens)
-            loss.backward()
-            total += loss.detach()
-        if self.push is not None:
-            self.push.barrier()  # every rank's gradient pushes of this step have landed
-        if self.world > 1:
-            dist.all_reduce(total, group=self.group)
-        if self.lora is not None:
-            self.lora.allreduce_grad()
-        gnorm = self._clip_coef()
-        lr = c.lr_at(self.step_num)
-        self.step_num += 1
-        for g in self.opt_groups:
-            self._adamw(g, lr)
-            g.grad.zero_()
+        mark = _Marks(self.device)
+        mark()
+        with nvtx("train.forward_backward"):
+            for s in range(0, B_local, mb):
+                loss = self.model.loss(ids[s:s + mb], tgt[s:s + mb], denom=global_tokens)
+                loss.backward()
+                total += loss.detach()
+        mark()
+        with nvtx("train.reduce"):
+            if self.push is not None:
+                self.push.barrier()  # every rank's gradient pushes of this step have landed
+            if self.world > 1:
+                dist.all_reduce(total, group=self.group)
+            if self.lora is not None:
+                self.lora.allreduce_grad()
+        mark()
+        with nvtx("train.optimizer"):
+            gnorm = self._clip_coef()
+            lr = c.lr_at(self.step_num)
+            self.step_num += 1
+            for g in self.opt_groups:
+                self._adamw(g, lr)
+                g.grad.zero_()
+        mark()
         torch.cuda.synchronize(self.device) if self.device.type == "cuda" else None
         ms = (time.perf_counter() - t0) * 1e3
-        return StepMetrics(self.step_num, float(total.item()), float(gnorm.item()), lr, int(global_tokens), ms)
+        fb, red, opt = mark.spans()
+        return StepMetrics(self.step_num, float(total.item()), float(gnorm.item()), lr, int(global_tokens), ms,
+                           fb, red, opt)
 
     def dpo_step(self, chosen, rejected, beta: float = 0.1, ref_logps=None) -> StepMetrics:
         """One DPO optimizer step on preference pairs ((ids, targets) each, this

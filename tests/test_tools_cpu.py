@@ -318,3 +318,31 @@ def test_samplers_processors():
     st.mirostat_lp2 = lp2
     SM.mirostat_update(p, st, 0)  # surprise 1 bit < tau: mu rises
     assert abs(st.mirostat_mu - (10.0 - 0.1 * (1.0 - 5.0))) < 1e-6
+
+
+# -- tracing -----------------------------------------------------------------------
+
+def test_inspect_and_step_metrics():
+    from rlx_models_b200 import config as C
+    from rlx_models_b200.train.trainer import TrainConfig, Trainer
+    from rlx_models_b200.utils import trace as TR
+    from rlx_models_b200.weights.init import random_weights
+    TR.enable_inspect(True)
+    try:
+        TR.inspect("x", torch.tensor([1.0, float("nan"), -3.0, float("inf")]))
+        TR.inspect("y", torch.zeros(2, 3))
+    finally:
+        TR.enable_inspect(False)
+    TR.inspect("ignored", torch.ones(1))
+    log = TR.take_inspect_log()
+    assert [r["name"] for r in log] == ["x", "y"] and TR.take_inspect_log() == []
+    assert log[0]["nan"] == 1 and log[0]["inf"] == 1 and log[0]["min"] == -3.0 and log[0]["absmax"] == 3.0
+    assert sum(log[0]["hist"]) == 2 and log[1]["shape"] == (2, 3)
+    with TR.nvtx("noop"):  # no CUDA here: a no-op context
+        pass
+    cfg = C.tiny(num_hidden_layers=1, hidden_size=64, intermediate_size=128, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=16, vocab_size=96)
+    t = Trainer(cfg, TrainConfig(param_dtype="float32", micro_batch=2), random_weights(cfg, 0), device="cpu")
+    m = t.step(torch.randint(0, 96, (4, 9), generator=torch.Generator().manual_seed(0)))
+    assert m.compute_ms > 0 and m.optim_ms > 0 and 0 < m.compute_fraction < 1
+    assert abs(m.compute_ms + m.comm_ms + m.optim_ms - m.step_ms) < m.step_ms
