@@ -201,3 +201,21 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
         weights = None  # random init on the device, per rank
     m = build_model(cfg, weights, device=device, tp_rank=tp_rank, tp_size=tp_size, comm=comm, seed=seed)
     return LLM(m, engine_config, tok)
+
+
+def load_transcriber(model: str, *, device: str | torch.device = "cuda", language: str | None = "en",
+                     task: str = "transcribe"):
+    """Whisper checkpoint (local dir / offline HF id) -> object with
+    ``transcribe(audio, sample_rate)``."""
+    from .models.whisper import SpeechToText, WhisperConfig, WhisperModel
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local Whisper checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        import json
+        cfg = WhisperConfig.from_dict(json.load(f))
+    tok = None
+    if any(os.path.exists(os.path.join(path, f)) for f in ("tokenizer.json", "tokenizer_config.json", "vocab.json")):
+        from transformers import AutoTokenizer
+        tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+    return SpeechToText(WhisperModel(cfg, WeightMap.from_dir(path), device=device), tok, language, task)
