@@ -72,6 +72,7 @@ class DecoderConfig:
     swiglu_limit: float = 0.0   # clamped SwiGLU (gpt-oss: 7.0)
     swiglu_alpha: float = 1.702
     norm_topk_prob: bool = True
+    shared_expert_intermediate_size: int = 0  # qwen2-moe: a dense SwiGLU expert every token uses, sigmoid-gated
     softmax_after_topk: bool = False  # gpt-oss: top-k on logits, softmax over the k
     expert_quant: str = "bf16"  # "bf16" | "mxfp4"
     torch_dtype: str = "bfloat16"
@@ -123,6 +124,20 @@ class DecoderConfig:
             if mt == "qwen3_moe":
                 kw["num_experts"] = d.get("num_experts", 0)
                 kw["moe_intermediate_size"] = d.get("moe_intermediate_size", 0)
+        elif mt == "mixtral":
+            kw["qk_norm"] = False
+            kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-5))
+            kw["num_experts"] = d.get("num_local_experts", 8)
+            kw["num_experts_per_tok"] = d.get("num_experts_per_tok", 2)
+            kw["moe_intermediate_size"] = d.get("intermediate_size", 14336)
+            kw["norm_topk_prob"] = True
+        elif mt == "qwen2_moe":
+            kw["qk_norm"] = False
+            kw["attention_bias"] = True
+            kw["num_experts"] = d.get("num_experts", 60)
+            kw["moe_intermediate_size"] = d.get("moe_intermediate_size", 1408)
+            kw["shared_expert_intermediate_size"] = d.get("shared_expert_intermediate_size", 0)
+            kw["norm_topk_prob"] = bool(d.get("norm_topk_prob", False))
         elif mt in ("llama", "mistral", "qwen2"):
             kw["qk_norm"] = False
             kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-5))
@@ -158,7 +173,7 @@ class DecoderConfig:
     def to_hf_dict(self) -> dict:
         d = {k: v for k, v in dataclasses.asdict(self).items() if k != "extra"}
         d.update(self.extra)
-        if self.model_type == "gpt_oss":
+        if self.model_type in ("gpt_oss", "mixtral"):
             d["num_local_experts"] = self.num_experts
             d["intermediate_size"] = self.moe_intermediate_size
         return d

@@ -55,7 +55,8 @@ def token_tile(n_assign: int, num_experts: int) -> int:
 
 
 class MoELayer:
-    __slots__ = ("router_w", "router_b", "gu_w", "gu_exp", "gu_bias", "dn_w", "dn_exp", "dn_bias")
+    __slots__ = ("router_w", "router_b", "gu_w", "gu_exp", "gu_bias", "dn_w", "dn_exp", "dn_bias",
+                 "sh_gu", "sh_dn", "sh_gate")
 
 
 class MoEDecoderLM(DecoderLM):
@@ -85,6 +86,9 @@ class MoEDecoderLM(DecoderLM):
     # -- weights ----------------------------------------------------------------
     def _load(self, w):
         c, dev, bf = self.cfg, self.device, torch.bfloat16
+        if c.model_type == "mixtral":  # block_sparse_moe.* checkpoint names -> the canonical MoE names
+            from ..weights.aliases import CanonicalView
+            w = CanonicalView(w, c.model_type)
 
         def g(name):
             return self._get(w, name)
@@ -141,6 +145,12 @@ class MoEDecoderLM(DecoderLM):
                 M.gu_w, M.gu_exp = tile_mxfp4(gub, gus)
                 M.dn_w, M.dn_exp = tile_mxfp4(dnb, dns)
                 M.gu_bias = M.dn_bias = None
+                M.sh_gu = M.sh_dn = M.sh_gate = None
+                if c.shared_expert_intermediate_size:  # qwen2-moe shared expert (dense, sigmoid-gated)
+                    ps = p + "mlp.shared_expert."
+                    M.sh_gu = dv(ops.interleave_gate_up(g(ps + "gate_proj.weight"), g(ps + "up_proj.weight")))
+                    M.sh_dn = dv(g(ps + "down_proj.weight"))
+                    M.sh_gate = g(p + "mlp.shared_expert_gate.weight").to(dev, torch.float32)
                 self.moe.append(M)
                 continue
             M.router_w = dv(g(p + "mlp.router.weight"))
@@ -158,6 +168,7 @@ class MoEDecoderLM(DecoderLM):
             M.gu_bias = hf_interleaved_to_grouped(dv(g(pe + "gate_up_proj_bias")[lo:hi]))
             M.dn_w, M.dn_exp = tile_mxfp4(dnb.to(dev), dns.to(dev).reshape(E_l, dns.shape[1], -1))
             M.dn_bias = dv(g(pe + "down_proj_bias")[lo:hi])  # each expert (and its bias) lives on one rank
+            M.sh_gu = M.sh_dn = M.sh_gate = None
             self.moe.append(M)
 
     # -- forward ---------------------------------------------------------------
@@ -200,6 +211,10 @@ class MoEDecoderLM(DecoderLM):
         ext().moe_gemm(gu, M.dn_w, M.dn_exp, H, M.dn_bias, weights.view(-1), perm, meta, tiles, dn, False,
                        0.0, 0.0, bt, s.status)
         ops._count(6)
+        if M.sh_gu is not None:  # shared expert: every token; each rank adds it to its replicated residual
+            sh = ops.linear(ops.linear_swiglu(x, M.sh_gu), M.sh_dn)
+            gate = torch.sigmoid(x.float() @ M.sh_gate.t())
+            h.add_((sh.float() * gate).to(h.dtype))
         if fused:
             return self.combiner.combine_norm(experts, h, norm_w)
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)

@@ -43,7 +43,8 @@ class DecoderOracle:
     def __init__(self, cfg: DecoderConfig, weights: dict[str, torch.Tensor], device="cpu"):
         self.cfg = cfg
         self.device = torch.device(device)
-        self.w = {k: v.to(self.device) for k, v in weights.items()}
+        from ..weights.aliases import canonical_name
+        self.w = {canonical_name(cfg.model_type, k): v.to(self.device) for k, v in weights.items()}
         self.inv_freq, self.rope_mult = rope_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling,
                                                       cfg.max_position_embeddings)
         self._experts: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
@@ -143,6 +144,11 @@ class DecoderOracle:
                 g = x[t] @ self.W(pe + "gate_proj.weight").T
                 u = x[t] @ self.W(pe + "up_proj.weight").T
                 out[t] += topv[t, s] * ((F.silu(g) * u) @ self.W(pe + "down_proj.weight").T)
+        if c.shared_expert_intermediate_size:  # qwen2-moe: sigmoid-gated shared SwiGLU expert
+            ps = p + "shared_expert."
+            sh = (F.silu(x @ self.W(ps + "gate_proj.weight").T) * (x @ self.W(ps + "up_proj.weight").T)) \
+                @ self.W(ps + "down_proj.weight").T
+            out = out + torch.sigmoid(x @ self.W(p + "shared_expert_gate.weight").T) * sh
         return out
 
     @torch.no_grad()

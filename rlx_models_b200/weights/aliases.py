@@ -1,0 +1,44 @@
+"""Checkpoint tensor names of model families that differ only in naming from
+the canonical layout the builders read (Qwen3-MoE style MoE names).
+
+Mixtral: ``block_sparse_moe.gate`` is the router, ``block_sparse_moe.experts.{e}.w1 / w3 / w2``
+are gate / up / down. ``canonical_name`` maps a checkpoint name to the
+canonical one; ``CanonicalView`` presents a weight source under canonical names.
+"""
+from __future__ import annotations
+
+import re
+
+_MIXTRAL = [(re.compile(r"\.block_sparse_moe\.gate\."), ".mlp.gate."),
+            (re.compile(r"\.block_sparse_moe\.experts\.(\d+)\.w1\."), r".mlp.experts.\1.gate_proj."),
+            (re.compile(r"\.block_sparse_moe\.experts\.(\d+)\.w3\."), r".mlp.experts.\1.up_proj."),
+            (re.compile(r"\.block_sparse_moe\.experts\.(\d+)\.w2\."), r".mlp.experts.\1.down_proj.")]
+
+
+def canonical_name(model_type: str, name: str) -> str:
+    if model_type == "mixtral":
+        for pat, rep in _MIXTRAL:
+            name = pat.sub(rep, name)
+    return name
+
+
+class CanonicalView:
+    """Weight source (dict or WeightMap-like) seen under canonical names."""
+
+    def __init__(self, weights, model_type: str):
+        self.w = weights
+        names = list(weights.keys())
+        self.to_ckpt = {canonical_name(model_type, n): n for n in names}
+
+    def keys(self):
+        return list(self.to_ckpt)
+
+    def __contains__(self, name):
+        return name in self.to_ckpt
+
+    def take(self, name, **kw):
+        n = self.to_ckpt[name]
+        return self.w.take(n, **kw) if hasattr(self.w, "take") else self.w[n]
+
+    def __getitem__(self, name):
+        return self.take(name)

@@ -76,6 +76,13 @@ def decoder_tensor_specs(cfg: DecoderConfig) -> list[TensorSpec]:
                 specs += [TensorSpec(pe + "gate_proj.weight", (I, H), "matrix"),
                           TensorSpec(pe + "up_proj.weight", (I, H), "matrix"),
                           TensorSpec(pe + "down_proj.weight", (H, I), "matrix")]
+            Is = cfg.shared_expert_intermediate_size
+            if Is:
+                ps = p + "mlp.shared_expert."
+                specs += [TensorSpec(ps + "gate_proj.weight", (Is, H), "matrix"),
+                          TensorSpec(ps + "up_proj.weight", (Is, H), "matrix"),
+                          TensorSpec(ps + "down_proj.weight", (H, Is), "matrix"),
+                          TensorSpec(p + "mlp.shared_expert_gate.weight", (1, H), "matrix")]
         else:
             I = cfg.intermediate_size
             specs += [TensorSpec(p + "mlp.gate_proj.weight", (I, H), "matrix"),

@@ -276,3 +276,44 @@ def test_flux_schedule_and_pack():
     x = torch.randn(2, 16, 8, 6)
     assert torch.equal(unpack(pack(x), 16, 8, 6), x)
     assert schedule(4, 4096, shift=False) == [1.0, 0.75, 0.5, 0.25, 0.0]
+
+
+def test_mixtral_and_qwen2_moe_configs_and_names():
+    import json
+    import tempfile
+    from rlx_models_b200.config import DecoderConfig
+    from rlx_models_b200.models.oracle import DecoderOracle
+    from rlx_models_b200.weights.aliases import canonical_name
+    from rlx_models_b200.weights.init import random_weights
+    mx = DecoderConfig.from_hf_dict({"model_type": "mixtral", "hidden_size": 64, "intermediate_size": 128,
+                                     "num_hidden_layers": 1, "num_attention_heads": 4, "num_key_value_heads": 2,
+                                     "vocab_size": 50, "num_local_experts": 4, "num_experts_per_tok": 2})
+    assert (mx.num_experts, mx.moe_intermediate_size, mx.qk_norm, mx.is_moe) == (4, 128, False, True)
+    with tempfile.TemporaryDirectory() as d:
+        mx.save(d)
+        assert json.load(open(d + "/config.json"))["num_local_experts"] == 4
+    assert canonical_name("mixtral", "model.layers.3.block_sparse_moe.experts.7.w3.weight") == \
+        "model.layers.3.mlp.experts.7.up_proj.weight"
+    assert canonical_name("mixtral", "model.layers.0.block_sparse_moe.gate.weight") == "model.layers.0.mlp.gate.weight"
+    # a Mixtral-named checkpoint gives the same oracle logits as the canonical names
+    w = random_weights(mx, 0)
+    mixnames = {}
+    for k, v in w.items():
+        k2 = k.replace(".mlp.gate.", ".block_sparse_moe.gate.")
+        for a, b in (("gate_proj", "w1"), ("up_proj", "w3"), ("down_proj", "w2")):
+            k2 = k2.replace(f".mlp.experts.", ".block_sparse_moe.experts.").replace(f".{a}.", f".{b}.") \
+                if ".mlp.experts." in k2 or ".block_sparse_moe.experts." in k2 else k2
+        mixnames[k2] = v
+    ids = torch.randint(0, 50, (9,), generator=torch.Generator().manual_seed(0))
+    a, _ = DecoderOracle(mx, {k: v.float() for k, v in w.items()}).forward(ids)
+    b, _ = DecoderOracle(mx, {k: v.float() for k, v in mixnames.items()}).forward(ids)
+    assert torch.equal(a, b)
+    q2 = DecoderConfig.from_hf_dict({"model_type": "qwen2_moe", "hidden_size": 64, "num_hidden_layers": 1,
+                                     "num_attention_heads": 4, "num_key_value_heads": 2, "vocab_size": 50,
+                                     "num_experts": 4, "num_experts_per_tok": 2, "moe_intermediate_size": 64,
+                                     "shared_expert_intermediate_size": 128, "intermediate_size": 256})
+    assert q2.attention_bias and q2.shared_expert_intermediate_size == 128 and not q2.norm_topk_prob
+    w2 = random_weights(q2, 1)
+    assert "model.layers.0.mlp.shared_expert_gate.weight" in w2
+    lg, _ = DecoderOracle(q2, {k: v.float() for k, v in w2.items()}).forward(ids)
+    assert torch.isfinite(lg).all()

@@ -139,3 +139,48 @@ def test_qwen3_moe_model_vs_oracle(cuda):
     row = ((lg.cpu().float() - ref).norm(dim=-1) / ref.norm(dim=-1))
     assert row.median() < 2e-2, row
     assert (row > 0.1).float().mean() <= 0.1, row
+
+
+@pytest.mark.parametrize("family", ["mixtral", "qwen2_moe"])
+def test_mixtral_qwen2_moe_vs_oracle(cuda, family):
+    """Mixtral (block_sparse_moe checkpoint names) and Qwen2-MoE (q/k/v biases,
+    sigmoid-gated shared expert) through the grouped MXFP4 GEMM; the oracle
+    uses the same MXFP4-rounded expert weights."""
+    from rlx_models_b200.quant.mxfp4 import mxfp4_roundtrip
+    kw = dict(hidden_size=256, num_attention_heads=4, num_key_value_heads=2, head_dim=64, num_experts=8,
+              num_experts_per_tok=2, moe_intermediate_size=128, vocab_size=512, qk_norm=False)
+    if family == "qwen2_moe":
+        kw.update(attention_bias=True, shared_expert_intermediate_size=256, norm_topk_prob=False)
+    cfg = C.tiny(family, **kw)
+    w = random_weights(cfg, seed=6, dtype=torch.bfloat16)
+    for k in list(w):
+        if ".mlp.experts." in k:
+            w[k] = mxfp4_roundtrip(w[k].float()).bfloat16()
+        if k.endswith(".bias"):
+            w[k] = (torch.randn(w[k].shape, generator=torch.Generator().manual_seed(3)) * 0.1).bfloat16()
+    if family == "mixtral":  # serve the checkpoint under Mixtral's own tensor names
+        ren = {}
+        for k, v in w.items():
+            if ".mlp.gate." in k:
+                k = k.replace(".mlp.gate.", ".block_sparse_moe.gate.")
+            elif ".mlp.experts." in k:
+                k = k.replace(".mlp.experts.", ".block_sparse_moe.experts.")
+                k = k.replace(".gate_proj.", ".w1.").replace(".up_proj.", ".w3.").replace(".down_proj.", ".w2.")
+            ren[k] = v
+        w = ren
+    model = MoEDecoderLM(cfg, w, device=cuda)
+    oracle = DecoderOracle(cfg, {k: v.float() for k, v in w.items()})
+    from rlx_models_b200.models.decoder import ForwardBatch
+    T = 33
+    ids = torch.randint(0, cfg.vocab_size, (T,), generator=torch.Generator().manual_seed(4))
+    nb = (T + 15) // 16
+    fb = ForwardBatch(input_ids=ids.int().to(cuda), positions=torch.arange(T, dtype=torch.int32, device=cuda),
+                      slots=torch.arange(T, dtype=torch.int64, device=cuda), num_decode=0,
+                      pre_block_tables=torch.arange(nb, dtype=torch.int32, device=cuda).view(1, -1),
+                      pre_ctx_lens=torch.tensor([T], dtype=torch.int32, device=cuda),
+                      pre_cu_q=torch.tensor([0, T], dtype=torch.int32, device=cuda), pre_max_q=T)
+    lg = model.forward(fb, model.make_kv_cache(nb))
+    ref, _ = oracle.forward(ids)
+    row = ((lg.cpu().float() - ref).norm(dim=-1) / ref.norm(dim=-1))
+    assert row.median() < 2e-2, row
+    assert (row > 0.1).float().mean() <= 0.1, row
