@@ -127,7 +127,7 @@ def test_flux_pipeline_text_to_image(cuda):
     vcfg = VAEConfig(latent_channels=cfg.in_channels // 4, block_out_channels=[32, 32, 64, 64], norm_num_groups=8)
     pipe = FluxPipeline(FluxDiT(cfg, dw, device=cuda), VAEDecoder(vcfg, vae_random_weights(vcfg), device=cuda),
                         T5Encoder(tc, t5w, device=cuda), CLIPTextEncoder(cc, cw, device=cuda))
-    t5_ids = torch.randint(0, 100, (1, 24), generator=g)
+    t5_ids = torch.randint(0, 100, (1, 32), generator=g)  # text length: a multiple of 16
     clip_ids = torch.randint(3, 90, (1, 16), generator=g)
     img = pipe(t5_ids=t5_ids, clip_ids=clip_ids, height=64, width=64, steps=3, seed=1)
     torch.cuda.synchronize()
