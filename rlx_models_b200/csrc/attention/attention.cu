@@ -561,8 +561,10 @@ int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
   const int sms = num_sms(a.device);
   if (splits <= 0) {
     const int ctas = a.B * a.Hkv;
+    // split the KV range only when (sequence, kv-head) pairs leave SMs idle: measured on B200 at Hkv 8,
+    // ctx 1400, one split beats two at 256 pairs (42.4 vs 48.3 us) and at 512 (79.4 vs 90.8 us)
     splits = std::max(1, std::min(16, (3 * sms + ctas - 1) / ctas));
-    if (ctas >= 2 * sms) splits = 1;
+    if (ctas >= sms) splits = 1;
   }
   if (splits > 1 && a.ws_elems < (int64_t)a.B * a.Hq * splits * (a.D + 2))
     throw std::runtime_error("b200.decode_attention: split workspace too small");
