@@ -346,3 +346,54 @@ def test_inspect_and_step_metrics():
     m = t.step(torch.randint(0, 96, (4, 9), generator=torch.Generator().manual_seed(0)))
     assert m.compute_ms > 0 and m.optim_ms > 0 and 0 < m.compute_fraction < 1
     assert abs(m.compute_ms + m.comm_ms + m.optim_ms - m.step_ms) < m.step_ms
+
+
+# -- device + hub ----------------------------------------------------------------
+
+def test_parallelism_planner():
+    from rlx_models_b200 import config as C
+    from rlx_models_b200 import device as DV
+    q8 = C.preset("qwen3-8b")
+    w = DV.weight_bytes(q8)
+    assert 15e9 < w["total"] < 18e9  # ~8.2 B params in bf16
+    p1 = DV.plan_parallelism(q8, 8, 180e9, context_tokens=64 * 2304)
+    assert p1.tp == 1 and p1.fits and p1.reason == "fits on one GPU"
+    p2 = DV.plan_parallelism(q8, 8, 16e9, context_tokens=64 * 2304)
+    assert p2.tp > 1 and p2.fits and p2.tp <= 8
+    go = C.preset("gpt-oss-120b")
+    pm = DV.plan_parallelism(go, 8, 180e9, context_tokens=128 * 1280)
+    assert pm.ep == 8 and pm.fits and "experts" in pm.reason
+    assert abs(DV.expert_bytes_per_rank(go, 8) * 8 - DV.weight_bytes(go)["experts"]) < 1
+    assert DV.devices() == [] or isinstance(DV.devices(), list)
+
+
+def test_hub_file_selection_and_resolve(tmp_path):
+    from rlx_models_b200 import hub as HB
+    files = ["README.md", "config.json", "model-00001-of-00002.safetensors", "model-00002-of-00002.safetensors",
+             "model.safetensors.index.json", "tokenizer.json", "tokenizer_config.json", "pytorch_model.bin"]
+    sel = HB.select_files(files)
+    assert "pytorch_model.bin" not in sel and "README.md" not in sel and len(sel) == 6
+    g = ["qwen3-8b-Q8_0.gguf", "qwen3-8b-Q4_K_M.gguf", "qwen3-8b-Q6_K.gguf", "config.json"]
+    assert HB.select_files(g) == ["qwen3-8b-Q4_K_M.gguf"]
+    assert HB.select_files(g, "q6_k") == ["qwen3-8b-Q6_K.gguf"]
+    split = ["big-Q8_0-00001-of-00002.gguf", "big-Q8_0-00002-of-00002.gguf"]
+    assert HB.select_files(split, "Q8_0") == split
+    with pytest.raises(FileNotFoundError):
+        HB.select_files(g, "IQ2_XXS")
+
+    class FakeHub:
+        def list_repo_files(self, name, revision=None):
+            assert name == "org/model" and revision == "abc"
+            return g
+
+        def snapshot_download(self, name, revision=None, allow_patterns=None, cache_dir=None):
+            d = tmp_path / "snap"
+            d.mkdir(exist_ok=True)
+            for f in allow_patterns:
+                (d / f).write_text("x")
+            return str(d)
+
+    with pytest.raises(FileNotFoundError):
+        HB.resolve("org/model:Q6_K@abc")
+    p = HB.resolve("org/model:Q6_K@abc", download=True, api=FakeHub())
+    assert os.listdir(p) == ["qwen3-8b-Q6_K.gguf"]
