@@ -18,8 +18,12 @@ KV caches are positional (slot = position under an identity block table), so
 rolling back after a rejection is just moving the position: stale entries past
 it are overwritten by the next writes.
 
+  * a learned draft head (runtime/draft_head.py): the target's own final
+    features plus the newest token through one small layer, recurring on its
+    own features for the following drafts.
+
 Reference: rlx-qwen3 src/spec.rs (draft / verify loop), rlx-eagle3 and
-rlx-dflash (learned draft heads, not built here).
+rlx-dflash (learned draft heads).
 """
 from __future__ import annotations
 
@@ -55,9 +59,10 @@ class _Seq:
         dev = model.device
         self.table = torch.arange(self.nb, dtype=torch.int32, device=dev).view(1, -1)
         self.pos = 0  # positions [0, pos) hold valid K/V
+        self.hidden = None  # [max_len, H] final-normed features per position (draft-head proposers)
 
     @torch.no_grad()
-    def run(self, tokens: list[int], start: int) -> torch.Tensor:
+    def run(self, tokens: list[int], start: int, keep_hidden: bool = False) -> torch.Tensor:
         """Feed ``tokens`` at positions start.. ; returns fp32 logits per token [n, V]."""
         dev = self.model.device
         n = len(tokens)
@@ -69,17 +74,32 @@ class _Seq:
                           slots=torch.arange(start, ctx, dtype=torch.int64, device=dev), num_decode=0,
                           pre_block_tables=self.table, pre_ctx_lens=torch.tensor([ctx], dtype=torch.int32, device=dev),
                           pre_cu_q=torch.tensor([0, n], dtype=torch.int32, device=dev), pre_max_q=n)
-        out = self.model.forward(fb, self.kv)
+        if keep_hidden:
+            h = self.model.forward_hidden(fb, self.kv)
+            if self.hidden is None:
+                self.hidden = torch.zeros(self.nb * 16, h.shape[1], dtype=h.dtype, device=dev)
+            self.hidden[start:ctx] = h
+            out = self.model.logits(h)
+        else:
+            out = self.model.forward(fb, self.kv)
         self.pos = ctx
         return out
 
 
 class SpeculativeDecoder:
-    def __init__(self, target, draft=None, k: int = 4, max_len: int = 4096, ngram: int = 3):
+    def __init__(self, target, draft=None, k: int = 4, max_len: int = 4096, ngram: int = 3, draft_head=None,
+                 head_window: int = 16):
         self.target = _Seq(target, max_len)
         self.draft = _Seq(draft, max_len) if draft is not None else None
+        self.head, self.head_window = draft_head, head_window
         self.k, self.ngram = k, ngram
         self.stats = SpecStats()
+
+    def _propose_head(self, seq: list[int], k: int) -> list[int]:
+        """Learned draft head over the target's features of the last positions."""
+        last = len(seq) - 2  # feature that produced the newest token
+        a = max(0, last - self.head_window + 1)
+        return self.head.propose(self.target.hidden[a:last + 1], seq[a + 1:last + 2], k)
 
     # -- proposers ---------------------------------------------------------------
     def _propose_draft(self, seq: list[int], k: int) -> list[int]:
@@ -110,15 +130,21 @@ class SpeculativeDecoder:
         t.pos = 0
         if self.draft is not None:
             self.draft.pos = 0
-        lg = t.run(list(prompt), 0)
+        keep = self.head is not None
+        lg = t.run(list(prompt), 0, keep)
         seq = list(prompt) + [int(lg[-1].argmax())]
         out = [seq[-1]]
         while len(out) < max_new_tokens and (eos_token_id is None or out[-1] != eos_token_id):
             k = min(self.k, max_new_tokens - len(out))
-            props = self._propose_draft(seq, k) if self.draft is not None else self._propose_lookup(seq, k)
+            if self.head is not None:
+                props = self._propose_head(seq, k)
+            elif self.draft is not None:
+                props = self._propose_draft(seq, k)
+            else:
+                props = self._propose_lookup(seq, k)
             # verify: the last accepted token (not yet in the target cache) + proposals
             start = len(seq) - 1
-            lv = t.run([seq[-1]] + props, start)
+            lv = t.run([seq[-1]] + props, start, keep)
             tgt = lv.argmax(-1).tolist()
             n_acc = 0
             while n_acc < len(props) and props[n_acc] == tgt[n_acc]:
