@@ -181,7 +181,7 @@ def _nib(q: torch.Tensor):
 def _k4_scale_min(s: torch.Tensor):
     """12 packed bytes -> 8 six-bit scales and 8 six-bit mins (Q4_K / Q5_K)."""
     s = s.to(torch.int32)
-    sc = torch.empty(s.shape[0], 8, dtype=torch.int32)
+    sc = torch.empty(s.shape[0], 8, dtype=torch.int32, device=s.device)
     mn = torch.empty_like(sc)
     sc[:, :4] = s[:, 0:4] & 63
     mn[:, :4] = s[:, 4:8] & 63
@@ -194,7 +194,7 @@ def _q3k_scales(s: torch.Tensor) -> torch.Tensor:
     """12 packed bytes -> 16 six-bit scales minus 32 (Q3_K)."""
     s = s.to(torch.int32)
     lo, hi = s[:, 0:8], s[:, 8:12]
-    out = torch.empty(s.shape[0], 16, dtype=torch.int32)
+    out = torch.empty(s.shape[0], 16, dtype=torch.int32, device=s.device)
     out[:, 0:4] = (lo[:, 0:4] & 0xF) | ((hi & 3) << 4)
     out[:, 4:8] = (lo[:, 4:8] & 0xF) | (((hi >> 2) & 3) << 4)
     out[:, 8:12] = (lo[:, 0:4] >> 4) | (((hi >> 4) & 3) << 4)
@@ -231,7 +231,7 @@ def dequantize_blocks(raw: torch.Tensor, kind: str) -> torch.Tensor:
         d = _f16(b[:, 0:2])
         qh = b[:, off:off + 4].to(torch.int64)
         qh = qh[:, 0] | (qh[:, 1] << 8) | (qh[:, 2] << 16) | (qh[:, 3] << 24)
-        bits = ((qh[:, None] >> torch.arange(32)) & 1).to(torch.int32)
+        bits = ((qh[:, None] >> torch.arange(32, device=qh.device)) & 1).to(torch.int32)
         lo, hi = _nib(b[:, off + 4:off + 20])
         q = torch.cat([lo, hi], 1) | (bits << 4)
         if kind == "Q5_0":
@@ -332,12 +332,12 @@ def quantize(x: torch.Tensor, kind: str) -> torch.Tensor:
         sub = sb.view(nb, 16, 16)
         ls = sub.abs().amax(2) / 31  # per 16-element sub-block step, |q| <= 31
         d = (ls.amax(1) / 127).half()
-        dinv = torch.where(d.float() > 0, 1 / d.float(), torch.zeros(nb))
+        dinv = torch.where(d.float() > 0, 1 / d.float(), torch.zeros(nb, device=x.device))
         sc = (ls * dinv[:, None]).round().clamp(-128, 127).to(torch.int8)  # sub-block scales
         step = d.float()[:, None] * sc.float()
         q = torch.where(step[..., None] != 0, (sub / step[..., None]).round(), torch.zeros_like(sub))
         q = (q.clamp(-32, 31) + 32).to(torch.int32).view(nb, 2, 4, 32)  # [nb, half, quarter, 32]
-        ql = torch.empty(nb, 2, 64, dtype=torch.int32)
+        ql = torch.empty(nb, 2, 64, dtype=torch.int32, device=x.device)
         ql[:, :, :32] = (q[:, :, 0] & 0xF) | ((q[:, :, 2] & 0xF) << 4)
         ql[:, :, 32:] = (q[:, :, 1] & 0xF) | ((q[:, :, 3] & 0xF) << 4)
         qh = (q[:, :, 0] >> 4) | ((q[:, :, 1] >> 4) << 2) | ((q[:, :, 2] >> 4) << 4) | ((q[:, :, 3] >> 4) << 6)
@@ -352,15 +352,15 @@ def quantize(x: torch.Tensor, kind: str) -> torch.Tensor:
         scale = (hi - lo) / 15  # per sub-block step, min = -lo
         d = (scale.amax(1) / 63).half()
         dmin = ((-lo).amax(1) / 63).half()
-        dinv = torch.where(d.float() > 0, 1 / d.float(), torch.zeros(nb))
-        minv = torch.where(dmin.float() > 0, 1 / dmin.float(), torch.zeros(nb))
+        dinv = torch.where(d.float() > 0, 1 / d.float(), torch.zeros(nb, device=x.device))
+        minv = torch.where(dmin.float() > 0, 1 / dmin.float(), torch.zeros(nb, device=x.device))
         sc = (scale * dinv[:, None]).round().clamp(0, 63).to(torch.int32)
         mn = (-lo * minv[:, None]).round().clamp(0, 63).to(torch.int32)
         step = d.float()[:, None] * sc.float()
         off = dmin.float()[:, None] * mn.float()
         q = torch.where(step[..., None] > 0, ((sub + off[..., None]) / step[..., None]).round(),
                         torch.zeros_like(sub)).clamp(0, 15).to(torch.int32)  # [nb, 8, 32]
-        packed = torch.empty(nb, 12, dtype=torch.int32)
+        packed = torch.empty(nb, 12, dtype=torch.int32, device=x.device)
         packed[:, 0:4] = (sc[:, 0:4] & 63) | ((sc[:, 4:8] >> 4) << 6)
         packed[:, 4:8] = (mn[:, 0:4] & 63) | ((mn[:, 4:8] >> 4) << 6)
         packed[:, 8:12] = (sc[:, 4:8] & 0xF) | ((mn[:, 4:8] & 0xF) << 4)
@@ -400,7 +400,7 @@ class GGUFWriter:
 
     def add_tensor(self, name: str, x: torch.Tensor, kind: str = "F32"):
         shape = tuple(int(d) for d in x.shape)
-        self.tensors.append((name, shape, TYPE_ID[kind], quantize(x, kind).numpy().tobytes()))
+        self.tensors.append((name, shape, TYPE_ID[kind], quantize(x, kind).cpu().numpy().tobytes()))
 
     def add_raw(self, name: str, shape, kind: str, data: bytes):
         self.tensors.append((name, tuple(int(d) for d in shape), TYPE_ID[kind], bytes(data)))
