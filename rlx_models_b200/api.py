@@ -219,3 +219,44 @@ def load_transcriber(model: str, *, device: str | torch.device = "cuda", languag
         from transformers import AutoTokenizer
         tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
     return SpeechToText(WhisperModel(cfg, WeightMap.from_dir(path), device=device), tok, language, task)
+
+
+class Embedder:
+    """Sentence embeddings from an encoder checkpoint (BERT family)."""
+
+    def __init__(self, encoder, tokenizer=None, pooling: str = "mean"):
+        self.encoder, self.tokenizer, self.pooling = encoder, tokenizer, pooling
+
+    def embed(self, texts, normalize: bool = True) -> torch.Tensor:
+        if isinstance(texts, str):
+            texts = [texts]
+        if texts and isinstance(texts[0], str):
+            if self.tokenizer is None:
+                raise ValueError("string inputs need a tokenizer")
+            enc = self.tokenizer(list(texts), padding=True, truncation=True, return_tensors="pt")
+            ids, mask = enc["input_ids"], enc["attention_mask"]
+        else:
+            seqs = [list(t) for t in texts]
+            L = max(len(s) for s in seqs)
+            ids = torch.zeros(len(seqs), L, dtype=torch.long)
+            mask = torch.zeros(len(seqs), L, dtype=torch.long)
+            for i, s in enumerate(seqs):
+                ids[i, :len(s)] = torch.tensor(s)
+                mask[i, :len(s)] = 1
+        return self.encoder.embed(ids, mask, pooling=self.pooling, normalize=normalize)
+
+
+def load_embedder(model: str, *, device: str | torch.device = "cuda", pooling: str = "mean") -> Embedder:
+    """BERT-family checkpoint (local dir / offline HF id) -> ``Embedder``."""
+    import json
+    from .models.bert import BertConfig, BertEncoder
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local encoder checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        cfg = BertConfig.from_dict(json.load(f))
+    tok = None
+    if any(os.path.exists(os.path.join(path, f)) for f in ("tokenizer.json", "vocab.txt")):
+        from transformers import AutoTokenizer
+        tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+    return Embedder(BertEncoder(cfg, WeightMap.from_dir(path), device=device), tok, pooling)

@@ -1,0 +1,49 @@
+"""BERT encoder embeddings on CPU against transformers' BertModel."""
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+
+from rlx_models_b200.models.bert import BertConfig, BertEncoder  # noqa: E402
+
+
+def test_bert_matches_transformers():
+    from transformers import BertConfig as HC, BertModel
+    hc = HC(vocab_size=200, hidden_size=64, num_hidden_layers=2, num_attention_heads=4, intermediate_size=128,
+            max_position_embeddings=64, hidden_dropout_prob=0.0, attention_probs_dropout_prob=0.0)
+    torch.manual_seed(0)
+    ref = BertModel(hc).eval()
+    sd = {k: v.detach().clone() for k, v in ref.state_dict().items()}
+    enc = BertEncoder(BertConfig.from_dict(hc.to_dict()), sd)
+    ids = torch.randint(5, 200, (3, 20))
+    mask = torch.ones(3, 20, dtype=torch.long)
+    mask[1, 12:] = 0
+    mask[2, 5:] = 0
+    with torch.no_grad():
+        out = ref(input_ids=ids, attention_mask=mask)
+    h = enc(ids, mask)
+    valid = mask.bool()
+    assert torch.allclose(h[valid], out.last_hidden_state[valid], atol=1e-4)
+    pooled = enc.embed(ids, mask, pooling="pooler", normalize=False)
+    assert torch.allclose(pooled, out.pooler_output, atol=1e-4)
+    mean = enc.embed(ids, mask, pooling="mean")
+    want = (out.last_hidden_state * mask[..., None]).sum(1) / mask.sum(1, keepdim=True)
+    assert torch.allclose(mean, torch.nn.functional.normalize(want, dim=-1), atol=1e-4)
+    # prefixed task-model names ("bert.") load too
+    enc2 = BertEncoder(BertConfig.from_dict(hc.to_dict()), {"bert." + k: v for k, v in sd.items()})
+    assert torch.allclose(enc2(ids, mask)[valid], h[valid])
+
+
+def test_load_embedder_from_directory(tmp_path):
+    from transformers import BertConfig as HC, BertModel
+    from rlx_models_b200.api import load_embedder
+    from rlx_models_b200.weights.weight_map import WeightMap
+    hc = HC(vocab_size=100, hidden_size=32, num_hidden_layers=1, num_attention_heads=4, intermediate_size=64,
+            max_position_embeddings=32)
+    ref = BertModel(hc).eval()
+    d = tmp_path / "bert"
+    WeightMap({k: v.detach().clone() for k, v in ref.state_dict().items()}).save(str(d))
+    hc.save_pretrained(str(d))
+    emb = load_embedder(str(d), device="cpu")
+    e = emb.embed([[3, 4, 5], [6, 7, 8, 9, 10]])
+    assert e.shape == (2, 32) and torch.allclose(e.norm(dim=-1), torch.ones(2), atol=1e-5)
