@@ -185,6 +185,9 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
         weights = GGUFWeights(gguf_file, device=device)  # quantised blocks expand on the GPU
         cfg = config or weights.config
     elif path is not None:
+        from .models.deepseek import DeepseekConfig, is_deepseek_config
+        if config is None and is_deepseek_config(path):  # MLA + DeepSeekMoE family
+            config = DeepseekConfig.from_file(path)
         cfg = config or C.DecoderConfig.from_file(path)
         from .weights.mlx import MLXWeights
         if MLXWeights.is_mlx_dir(path):  # MLX affine group-quantised checkpoint

@@ -221,7 +221,23 @@ def gpt_oss_120b() -> DecoderConfig:
                          expert_quant="mxfp4")
 
 
+def deepseek_v2_lite():
+    """DeepSeek-V2-Lite shape (15.7B total, 2.4B active): MLA without q
+    compression, 64 routed experts (top-6, softmax) + 2 shared."""
+    from .models.deepseek import DeepseekConfig
+    return DeepseekConfig.from_dict(dict(
+        model_type="deepseek_v2", vocab_size=102400, hidden_size=2048, intermediate_size=10944,
+        moe_intermediate_size=1408, num_hidden_layers=27, num_attention_heads=16, n_shared_experts=2,
+        n_routed_experts=64, num_experts_per_tok=6, routed_scaling_factor=1.0, kv_lora_rank=512, q_lora_rank=None,
+        qk_rope_head_dim=64, v_head_dim=128, qk_nope_head_dim=128, n_group=1, topk_group=1, topk_method="greedy",
+        scoring_func="softmax", norm_topk_prob=False, first_k_dense_replace=1, max_position_embeddings=163840,
+        rope_theta=10000.0, rope_scaling={"rope_type": "yarn", "factor": 40.0, "original_max_position_embeddings": 4096,
+                                          "beta_fast": 32, "beta_slow": 1, "mscale": 0.707, "mscale_all_dim": 0.707},
+        bos_token_id=100000, eos_token_id=100001))
+
+
 PRESETS = {
+    "deepseek-v2-lite": deepseek_v2_lite,
     "qwen3-0.6b": qwen3_0_6b,
     "qwen3-1.7b": qwen3_1_7b,
     "qwen3-8b": qwen3_8b,

@@ -217,10 +217,16 @@ def rope_inv_freq(head_dim: int, theta: float, scaling: dict | None = None,
             ramp = ramp.clamp(0, 1)
             extrap = 1 - ramp
             inv = (inv / factor) * (1 - extrap) + inv * extrap
-            ms = scaling.get("mscale")
-            mult = float(scaling.get("attention_factor") or (0.1 * math.log(factor) + 1.0 if factor > 1 else 1.0))
-            if ms is not None and scaling.get("attention_factor") is None:
-                mult = float(ms) if ms else mult
+            def get_mscale(m=1.0):
+                return 0.1 * m * math.log(factor) + 1.0 if factor > 1 else 1.0
+
+            ms, ms_all = scaling.get("mscale"), scaling.get("mscale_all_dim")
+            if scaling.get("attention_factor") is not None:
+                mult = float(scaling["attention_factor"])
+            elif ms and ms_all:  # DeepSeek: ratio of the two magnitudes (1 when they are equal)
+                mult = get_mscale(float(ms)) / get_mscale(float(ms_all))
+            else:
+                mult = get_mscale()
     return inv.float(), mult
 
 

@@ -62,11 +62,22 @@ def _moe(cfg, weights, device, tp_rank, tp_size, comm):
     return MoEDecoderLM(cfg, weights, device=device, ep_rank=tp_rank, ep_size=tp_size, comm=comm)
 
 
+@register("deepseek_v3", "deepseek_v2", "kimi_k2")
+def _deepseek(cfg, weights, device, tp_rank, tp_size, comm):
+    from .models.deepseek import DeepseekLM
+    if tp_size != 1:
+        raise NotImplementedError("DeepSeek MLA models run on one GPU per replica")
+    return DeepseekLM(cfg, weights, device=device)
+
+
 def build_model(cfg: DecoderConfig, weights=None, *, device="cuda", tp_rank=0, tp_size=1, comm=None, seed=0):
     fn = _BUILDERS.get(cfg.model_type)
     if fn is None:
         raise KeyError(f"no builder for model_type={cfg.model_type!r}; registered: {registered()}")
-    if weights is None:
+    if weights is None and cfg.model_type in ("deepseek_v3", "deepseek_v2", "kimi_k2"):
+        from .models.deepseek import random_weights
+        weights = random_weights(cfg, seed, device)
+    elif weights is None:
         weights = RandomWeights(cfg, seed, device)
     with torch.no_grad():
         return fn(cfg, weights, device, tp_rank, tp_size, comm)

@@ -136,7 +136,8 @@ class LLMEngine:
         self.max_blocks_per_seq = (cfg.max_model_len + BLOCK_SIZE - 1) // BLOCK_SIZE
         nb = cfg.num_blocks
         if nb <= 0:
-            per = 2 * mc.num_hidden_layers * model.hkv * BLOCK_SIZE * model.D * 2
+            per = (model.kv_bytes_per_block() if hasattr(model, "kv_bytes_per_block")
+                   else 2 * mc.num_hidden_layers * model.hkv * BLOCK_SIZE * model.D * 2)
             nb = max(self.max_blocks_per_seq + 1, int(cfg.kv_memory_gb * (1 << 30)) // per)
         self.kv = model.make_kv_cache(nb + 1)
         self.dummy_block = nb  # never handed out by the scheduler; padding rows write here
