@@ -23,6 +23,8 @@ def legacy_rope_keys(cfg: dict) -> dict:
     if isinstance(rp, dict):
         if "rope_theta" in rp and "rope_theta" not in cfg:
             cfg["rope_theta"] = rp["rope_theta"]
+        if "partial_rotary_factor" in rp and "partial_rotary_factor" not in cfg:
+            cfg["partial_rotary_factor"] = rp["partial_rotary_factor"]
         kind = rp.get("rope_type", rp.get("type", "default"))
         if kind not in (None, "default") and not cfg.get("rope_scaling"):
             cfg["rope_scaling"] = {k: v for k, v in rp.items() if k != "rope_theta"}
@@ -53,6 +55,7 @@ class DecoderConfig:
     rms_norm_eps: float = 1e-6
     rope_theta: float = 1e6
     rope_scaling: dict | None = None
+    partial_rotary_factor: float = 1.0  # RoPE on the first head_dim * factor dims (GLM-4: 0.5)
     max_position_embeddings: int = 40960
     tie_word_embeddings: bool = False
     qk_norm: bool = True
@@ -74,6 +77,14 @@ class DecoderConfig:
     norm_topk_prob: bool = True
     shared_expert_intermediate_size: int = 0  # qwen2-moe: a dense SwiGLU expert every token uses, sigmoid-gated
     softmax_after_topk: bool = False  # gpt-oss: top-k on logits, softmax over the k
+    # DeepSeek-style routing (glm4_moe): sigmoid scores + e_score_correction_bias for the
+    # choice, group-limited top-k, routed scaling; always-on shared experts; dense first layers
+    router_scoring: str = "softmax"  # "softmax" | "sigmoid"
+    n_group: int = 1
+    topk_group: int = 1
+    routed_scaling_factor: float = 1.0
+    n_shared_experts: int = 0
+    first_k_dense_replace: int = 0
     expert_quant: str = "bf16"  # "bf16" | "mxfp4"
     torch_dtype: str = "bfloat16"
     extra: dict = field(default_factory=dict)
@@ -87,8 +98,15 @@ class DecoderConfig:
         return self.num_key_value_heads * self.head_dim
 
     @property
+    def rotary_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary_factor)
+
+    @property
     def is_moe(self) -> bool:
         return self.num_experts > 0
+
+    def is_moe_layer(self, i: int) -> bool:
+        return self.is_moe and i >= self.first_k_dense_replace
 
     def layer_window(self, i: int) -> int:
         if self.layer_types is not None and self.sliding_window:
@@ -143,6 +161,19 @@ class DecoderConfig:
             kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-5))
             if mt == "qwen2":
                 kw["attention_bias"] = True
+        elif mt == "glm4_moe":
+            kw["qk_norm"] = bool(d.get("use_qk_norm", False))
+            kw["attention_bias"] = bool(d.get("attention_bias", False))
+            kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-5))
+            kw["num_experts"] = d.get("n_routed_experts", 128)
+            kw["num_experts_per_tok"] = d.get("num_experts_per_tok", 8)
+            kw["moe_intermediate_size"] = d.get("moe_intermediate_size", 1408)
+            kw["router_scoring"] = "sigmoid"
+            for k, dflt in (("n_group", 1), ("topk_group", 1), ("routed_scaling_factor", 1.0),
+                            ("n_shared_experts", 1), ("first_k_dense_replace", 1)):
+                kw[k] = d[k] if d.get(k) is not None else dflt
+            kw["norm_topk_prob"] = bool(d.get("norm_topk_prob", True))
+            kw.setdefault("partial_rotary_factor", 0.5)
         elif mt == "gpt_oss":
             kw["qk_norm"] = False
             kw["attention_bias"] = True
@@ -176,6 +207,9 @@ class DecoderConfig:
         if self.model_type in ("gpt_oss", "mixtral"):
             d["num_local_experts"] = self.num_experts
             d["intermediate_size"] = self.moe_intermediate_size
+        if self.model_type == "glm4_moe":
+            d["n_routed_experts"] = self.num_experts
+            d["use_qk_norm"] = self.qk_norm
         return d
 
     def save(self, path: str):

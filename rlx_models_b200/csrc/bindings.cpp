@@ -132,15 +132,18 @@ void qkv_rope(const Tensor& qkv, const optional<Tensor>& q_norm, const optional<
               const Tensor& positions, const optional<Tensor>& slots, const Tensor& inv_freq, double rope_scale,
               Tensor& q_out, const optional<Tensor>& k_cache, const optional<Tensor>& v_cache,
               const optional<Tensor>& k_out, const optional<Tensor>& v_out, int64_t Hq, int64_t Hkv, int64_t D,
-              double eps) {
+              double eps, int64_t rot_dim) {
   check_cuda(qkv, "qkv");
+  if (rot_dim <= 0) rot_dim = D;
+  TORCH_CHECK(rot_dim <= D && rot_dim % (2 * (D / 32)) == 0, "b200.qkv_rope: rot_dim must be <= head_dim and a "
+              "multiple of 2 * head_dim / 32");
   TORCH_CHECK((qkv.scalar_type() == at::kBFloat16 || qkv.scalar_type() == at::kFloat) && qkv.dim() == 2 &&
                   qkv.stride(1) == 1,
               "b200.qkv_rope: qkv");
   TORCH_CHECK(qkv.size(1) == (Hq + 2 * Hkv) * D, "b200.qkv_rope: qkv width");
   TORCH_CHECK(D == 64 || D == 128, "b200.qkv_rope: head_dim 64 or 128");
   TORCH_CHECK(positions.scalar_type() == at::kInt && positions.numel() == qkv.size(0), "b200.qkv_rope: positions");
-  TORCH_CHECK(inv_freq.scalar_type() == at::kFloat && inv_freq.numel() == D / 2, "b200.qkv_rope: inv_freq");
+  TORCH_CHECK(inv_freq.scalar_type() == at::kFloat && inv_freq.numel() == rot_dim / 2, "b200.qkv_rope: inv_freq");
   TORCH_CHECK(q_out.is_contiguous() && q_out.numel() == qkv.size(0) * Hq * D, "b200.qkv_rope: q_out");
   if (slots.has_value() && slots->defined()) {
     TORCH_CHECK(slots->scalar_type() == at::kLong && slots->numel() == qkv.size(0), "b200.qkv_rope: slots");
@@ -157,7 +160,7 @@ void qkv_rope(const Tensor& qkv, const optional<Tensor>& q_norm, const optional<
   a.slots = (slots.has_value() && slots->defined()) ? slots->data_ptr<int64_t>() : nullptr;
   a.inv_freq = inv_freq.data_ptr<float>();
   a.rope_scale = (float)rope_scale;
-  a.rot_dim = (int)D;
+  a.rot_dim = (int)rot_dim;
   a.q_out = q_out.data_ptr();
   a.k_cache = const_cast<void*>(opt_ptr(k_cache));
   a.v_cache = const_cast<void*>(opt_ptr(v_cache));

@@ -173,21 +173,27 @@ __global__ void qkv_rope_kernel(QkvRopeArgs a) {
 #pragma unroll
       for (int e = 0; e < E; ++e) x[e] = __bfloat162float(__float2bfloat16(x[e]));
     }
-    // rotary embedding (full rotary dim, half-split layout)
+    // rotary embedding over the first rot_dim dims (half-split layout: dim d
+    // pairs with d + rot_dim/2); dims >= rot_dim pass through (partial RoPE)
     const float pos = (float)a.positions[t];
+    const int rh = a.rot_dim / 2;
+    const int base = lane * E;
+    const int off = rh / E;  // lanes between the two halves of a pair
+    const int src = base < rh ? lane + off : (base < a.rot_dim ? lane - off : lane);
     float y[E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) y[e] = __shfl_xor_sync(0xffffffffu, x[e], 16);
-    const int half = D / 2;
+    for (int e = 0; e < E; ++e) y[e] = __shfl_sync(0xffffffffu, x[e], src);
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      const int d = lane * E + e;
-      const int fi = d < half ? d : d - half;
-      float s, c;
-      sincosf(pos * a.inv_freq[fi], &s, &c);
-      c *= a.rope_scale;
-      s *= a.rope_scale;
-      x[e] = d < half ? (x[e] * c - y[e] * s) : (x[e] * c + y[e] * s);
+      const int d = base + e;
+      if (d < a.rot_dim) {
+        const int fi = d < rh ? d : d - rh;
+        float s, c;
+        sincosf(pos * a.inv_freq[fi], &s, &c);
+        c *= a.rope_scale;
+        s *= a.rope_scale;
+        x[e] = d < rh ? (x[e] * c - y[e] * s) : (x[e] * c + y[e] * s);
+      }
     }
   }
   if (is_q) {

@@ -68,7 +68,7 @@ class DecoderLM:
         self.D = c.head_dim
         self.inter = c.intermediate_size // tp_size
         assert self.inter % ops.SWIGLU_GROUP == 0
-        inv, mult = rope_inv_freq(c.head_dim, c.rope_theta, c.rope_scaling, c.max_position_embeddings)
+        inv, mult = rope_inv_freq(c.rotary_dim, c.rope_theta, c.rope_scaling, c.max_position_embeddings)
         self.inv_freq = inv.to(self.device)
         self.rope_mult = mult
         self.scale = 1.0 / math.sqrt(c.head_dim)
@@ -150,6 +150,7 @@ class DecoderLM:
             qkv = ops.linear(x, L.wqkv, bias=L.bqkv)
         q = ops.qkv_rope(qkv, num_q_heads=self.hq, num_kv_heads=self.hkv, head_dim=self.D,
                          positions=fb.positions, inv_freq=self.inv_freq, rope_scale=self.rope_mult,
+                         rot_dim=self.cfg.rotary_dim,
                          q_norm=L.q_norm, k_norm=L.k_norm, eps=self.cfg.rms_norm_eps, slots=fb.slots,
                          k_cache=kc, v_cache=vc)
         o = torch.empty_like(q)

@@ -1,4 +1,5 @@
-"""GPU mixture-of-experts decoder (gpt-oss family) on the sm_100a kernels.
+"""GPU mixture-of-experts decoder (gpt-oss, Qwen3-MoE, Mixtral, Qwen2-MoE,
+GLM-4.5 / glm4_moe) on the sm_100a kernels.
 
 Attention is the dense decoder's (q/k/v/o biases, learned sinks, alternating
 128-token sliding window / full attention, YaRN RoPE); the MLP is a routed
@@ -55,7 +56,7 @@ def token_tile(n_assign: int, num_experts: int) -> int:
 
 
 class MoELayer:
-    __slots__ = ("router_w", "router_b", "gu_w", "gu_exp", "gu_bias", "dn_w", "dn_exp", "dn_bias",
+    __slots__ = ("router_w", "router_b", "router_corr", "gu_w", "gu_exp", "gu_bias", "dn_w", "dn_exp", "dn_bias",
                  "sh_gu", "sh_dn", "sh_gate")
 
 
@@ -78,10 +79,18 @@ class MoEDecoderLM(DecoderLM):
         self.combiner = None
         if ep_combine == "fused":
             from ..parallel.ep import EPCombiner
+            n_moe = sum(cfg.is_moe_layer(i) for i in range(cfg.num_hidden_layers))
             self.combiner = EPCombiner(ep_rank, ep_size, self.device, hidden=cfg.hidden_size,
                                        top_k=cfg.num_experts_per_tok, e_local=self.e_local,
-                                       max_tokens=combine_max_tokens, num_layers=cfg.num_hidden_layers,
+                                       max_tokens=combine_max_tokens, num_layers=n_moe,
                                        eps=cfg.rms_norm_eps)
+        self._route_spec = None
+        if cfg.router_scoring == "sigmoid":  # DeepSeek-style group-limited routing (glm4_moe)
+            from types import SimpleNamespace
+            self._route_spec = SimpleNamespace(
+                scoring_func="sigmoid", topk_method="noaux_tc", n_group=cfg.n_group, topk_group=cfg.topk_group,
+                num_experts_per_tok=cfg.num_experts_per_tok, norm_topk_prob=cfg.norm_topk_prob,
+                routed_scaling_factor=cfg.routed_scaling_factor)
 
     # -- weights ----------------------------------------------------------------
     def _load(self, w):
@@ -123,7 +132,14 @@ class MoEDecoderLM(DecoderLM):
             L.sinks = g(p + "self_attn.sinks").to(dev, torch.float32).contiguous() if c.attn_sinks else None
             L.window = c.layer_window(i)
             self.layers.append(L)
+            if not c.is_moe_layer(i):  # dense layer of a mostly-MoE model (glm4_moe's first layers)
+                L.w_gu = dv(ops.interleave_gate_up(g(p + "mlp.gate_proj.weight").to(dev),
+                                                   g(p + "mlp.up_proj.weight").to(dev)))
+                L.wd = dv(g(p + "mlp.down_proj.weight"))
+                self.moe.append(None)
+                continue
             M = MoELayer()
+            M.router_corr = None
             pe = p + "mlp.experts."
             E_l = hi - lo
             if c.model_type != "gpt_oss":
@@ -131,6 +147,9 @@ class MoEDecoderLM(DecoderLM):
                 # packed to MXFP4 at load (the grouped GEMM streams 4-bit weights)
                 M.router_w = dv(g(p + "mlp.gate.weight"))
                 M.router_b = None
+                if c.router_scoring == "sigmoid":  # fp32 router (as HF) + the choice-only correction bias
+                    M.router_w = g(p + "mlp.gate.weight").to(dev, torch.float32).contiguous()
+                    M.router_corr = g(p + "mlp.gate.e_score_correction_bias").to(dev, torch.float32)
                 I = c.moe_intermediate_size
                 gu_l, dn_l = [], []
                 for e in range(lo, hi):
@@ -146,7 +165,11 @@ class MoEDecoderLM(DecoderLM):
                 M.dn_w, M.dn_exp = tile_mxfp4(dnb, dns)
                 M.gu_bias = M.dn_bias = None
                 M.sh_gu = M.sh_dn = M.sh_gate = None
-                if c.shared_expert_intermediate_size:  # qwen2-moe shared expert (dense, sigmoid-gated)
+                if c.n_shared_experts:  # glm4_moe / DeepSeek shared experts: dense, ungated, every token
+                    ps = p + "mlp.shared_experts."
+                    M.sh_gu = dv(ops.interleave_gate_up(g(ps + "gate_proj.weight"), g(ps + "up_proj.weight")))
+                    M.sh_dn = dv(g(ps + "down_proj.weight"))
+                elif c.shared_expert_intermediate_size:  # qwen2-moe shared expert (dense, sigmoid-gated)
                     ps = p + "mlp.shared_expert."
                     M.sh_gu = dv(ops.interleave_gate_up(g(ps + "gate_proj.weight"), g(ps + "up_proj.weight")))
                     M.sh_dn = dv(g(ps + "down_proj.weight"))
@@ -181,10 +204,15 @@ class MoEDecoderLM(DecoderLM):
         k = c.num_experts_per_tok
         E_l = self.e_local
         dev = x.device
-        logits = ops.linear(x, M.router_w, bias=M.router_b, out_dtype=torch.float32)
-        experts = torch.empty(T, k, dtype=torch.int32, device=dev)
-        weights = torch.empty(T, k, dtype=torch.float32, device=dev)
-        ext().moe_route(logits, k, not c.softmax_after_topk, c.norm_topk_prob, experts, weights)
+        if self._route_spec is not None:
+            from .deepseek import route
+            idx, wts = route(self._route_spec, x.float() @ M.router_w.t(), M.router_corr)
+            experts, weights = idx.to(torch.int32).contiguous(), wts.contiguous()
+        else:
+            logits = ops.linear(x, M.router_w, bias=M.router_b, out_dtype=torch.float32)
+            experts = torch.empty(T, k, dtype=torch.int32, device=dev)
+            weights = torch.empty(T, k, dtype=torch.float32, device=dev)
+            ext().moe_route(logits, k, not c.softmax_after_topk, c.norm_topk_prob, experts, weights)
         n = T * k
         bt = token_tile(n, c.num_experts)
         meta = torch.empty(2 * E_l + 2, dtype=torch.int32, device=dev)
@@ -211,7 +239,9 @@ class MoEDecoderLM(DecoderLM):
         ext().moe_gemm(gu, M.dn_w, M.dn_exp, H, M.dn_bias, weights.view(-1), perm, meta, tiles, dn, False,
                        0.0, 0.0, bt, s.status)
         ops._count(6)
-        if M.sh_gu is not None:  # shared expert: every token; each rank adds it to its replicated residual
+        if M.sh_gu is not None and M.sh_gate is None:  # ungated shared experts: h += shared(x)
+            ops.linear(ops.linear_swiglu(x, M.sh_gu), M.sh_dn, residual=h, out=h)
+        elif M.sh_gu is not None:  # shared expert: every token; each rank adds it to its replicated residual
             sh = ops.linear(ops.linear_swiglu(x, M.sh_gu), M.sh_dn)
             gate = torch.sigmoid(x.float() @ M.sh_gate.t())
             h.add_((sh.float() * gate).to(h.dtype))
@@ -234,5 +264,9 @@ class MoEDecoderLM(DecoderLM):
             ops.linear(a, L.wo, bias=L.bo, residual=h, out=h)  # h += o_proj (+ bias)
             x = ops.rmsnorm(h, L.ln2, c.rms_norm_eps)
             nw = self.layers[i + 1].ln1 if i + 1 < n else self.norm
-            x = self._moe(i, x, h, nw)  # h += moe; x = rmsnorm(h) * nw
+            if self.moe[i] is None:  # dense layer
+                ops.linear(ops.linear_swiglu(x, L.w_gu), L.wd, residual=h, out=h)
+                x = ops.rmsnorm(h, nw, c.rms_norm_eps)
+            else:
+                x = self._moe(i, x, h, nw)  # h += moe; x = rmsnorm(h) * nw
         return x

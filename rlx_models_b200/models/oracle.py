@@ -45,7 +45,7 @@ class DecoderOracle:
         self.device = torch.device(device)
         from ..weights.aliases import canonical_name
         self.w = {canonical_name(cfg.model_type, k): v.to(self.device) for k, v in weights.items()}
-        self.inv_freq, self.rope_mult = rope_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling,
+        self.inv_freq, self.rope_mult = rope_inv_freq(cfg.rotary_dim, cfg.rope_theta, cfg.rope_scaling,
                                                       cfg.max_position_embeddings)
         self._experts: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
 
@@ -108,7 +108,7 @@ class DecoderOracle:
     def _mlp(self, i: int, x: torch.Tensor) -> torch.Tensor:
         c = self.cfg
         p = f"model.layers.{i}.mlp."
-        if not c.is_moe:
+        if not c.is_moe_layer(i):
             g = self._mm(x, p + "gate_proj.weight")
             u = self._mm(x, p + "up_proj.weight")
             return self._mm(F.silu(g) * u, p + "down_proj.weight")
@@ -130,12 +130,19 @@ class DecoderOracle:
                 y = torch.einsum("tn,tnh->th", act, dn_w[e]) + dn_b[e]
                 out += probs[:, slot:slot + 1] * y
             return out
-        # qwen3-moe style (softmax over all experts, top-k, optional renorm)
         logits = x @ self.W(p + "gate.weight").T
-        probs = torch.softmax(logits, dim=-1)
-        topv, topi = probs.topk(c.num_experts_per_tok, dim=-1)
-        if c.norm_topk_prob:
-            topv = topv / topv.sum(-1, keepdim=True)
+        if c.router_scoring == "sigmoid":  # glm4_moe: DeepSeek's group-limited sigmoid routing
+            from types import SimpleNamespace
+            from .deepseek import route
+            spec = SimpleNamespace(scoring_func="sigmoid", topk_method="noaux_tc", n_group=c.n_group,
+                                   topk_group=c.topk_group, num_experts_per_tok=c.num_experts_per_tok,
+                                   norm_topk_prob=c.norm_topk_prob, routed_scaling_factor=c.routed_scaling_factor)
+            topi, topv = route(spec, logits, self.W(p + "gate.e_score_correction_bias"))
+        else:  # qwen3-moe style (softmax over all experts, top-k, optional renorm)
+            probs = torch.softmax(logits, dim=-1)
+            topv, topi = probs.topk(c.num_experts_per_tok, dim=-1)
+            if c.norm_topk_prob:
+                topv = topv / topv.sum(-1, keepdim=True)
         out = torch.zeros_like(x)
         for t in range(x.shape[0]):
             for s in range(c.num_experts_per_tok):
@@ -144,7 +151,11 @@ class DecoderOracle:
                 g = x[t] @ self.W(pe + "gate_proj.weight").T
                 u = x[t] @ self.W(pe + "up_proj.weight").T
                 out[t] += topv[t, s] * ((F.silu(g) * u) @ self.W(pe + "down_proj.weight").T)
-        if c.shared_expert_intermediate_size:  # qwen2-moe: sigmoid-gated shared SwiGLU expert
+        if c.n_shared_experts:  # glm4_moe: ungated shared experts
+            ps = p + "shared_experts."
+            out = out + (F.silu(x @ self.W(ps + "gate_proj.weight").T) * (x @ self.W(ps + "up_proj.weight").T)) \
+                @ self.W(ps + "down_proj.weight").T
+        elif c.shared_expert_intermediate_size:  # qwen2-moe: sigmoid-gated shared SwiGLU expert
             ps = p + "shared_expert."
             sh = (F.silu(x @ self.W(ps + "gate_proj.weight").T) * (x @ self.W(ps + "up_proj.weight").T)) \
                 @ self.W(ps + "down_proj.weight").T

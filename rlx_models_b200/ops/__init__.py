@@ -235,14 +235,16 @@ def qkv_rope(qkv: torch.Tensor, *, num_q_heads: int, num_kv_heads: int, head_dim
              q_norm: torch.Tensor | None = None, k_norm: torch.Tensor | None = None, eps: float = 1e-6,
              slots: torch.Tensor | None = None, k_cache: torch.Tensor | None = None,
              v_cache: torch.Tensor | None = None, q_out: torch.Tensor | None = None,
-             k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None) -> torch.Tensor:
-    """QK RMSNorm + RoPE on the fused qkv projection; K/V written to the paged cache."""
+             k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None,
+             rot_dim: int = 0) -> torch.Tensor:
+    """QK RMSNorm + RoPE on the fused qkv projection; K/V written to the paged cache.
+    ``rot_dim`` (0 = head_dim): rotate only the first rot_dim dims of each head."""
     T = qkv.shape[0]
     if q_out is None:
         q_out = torch.empty(T, num_q_heads, head_dim, dtype=torch.bfloat16, device=qkv.device)
     _count(1)
     ext().qkv_rope(qkv, q_norm, k_norm, positions, slots, inv_freq, float(rope_scale), q_out, k_cache,
-                   v_cache, k_out, v_out, num_q_heads, num_kv_heads, head_dim, float(eps))
+                   v_cache, k_out, v_out, num_q_heads, num_kv_heads, head_dim, float(eps), int(rot_dim))
     return q_out
 
 

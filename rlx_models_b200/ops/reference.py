@@ -23,7 +23,12 @@ def rmsnorm_hf_bf16(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tenso
 
 
 def rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor, scale: float = 1.0) -> torch.Tensor:
-    """Half-split rotary embedding. x: [T, H, D], positions: [T]."""
+    """Half-split rotary embedding. x: [T, H, D], positions: [T]. With fewer
+    than D/2 frequencies only the first 2 * len(inv_freq) dims rotate
+    (partial RoPE); the rest pass through."""
+    R = 2 * inv_freq.shape[0]
+    if R < x.shape[-1]:
+        return torch.cat([rope(x[..., :R], positions, inv_freq, scale), x[..., R:].float()], -1)
     freqs = positions.float()[:, None] * inv_freq.float()[None, :]
     emb = torch.cat([freqs, freqs], dim=-1)
     cos, sin = emb.cos() * scale, emb.sin() * scale

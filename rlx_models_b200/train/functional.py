@@ -126,7 +126,11 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
 
 
 def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-    """Half-split rotary embedding; x [B, S, H, D], cos/sin [S, D]."""
+    """Half-split rotary embedding; x [B, S, H, D], cos/sin [S, R] (R < D:
+    only the first R dims rotate)."""
+    R = cos.shape[-1]
+    if R < x.shape[-1]:
+        return torch.cat([rope(x[..., :R], cos, sin), x[..., R:]], -1)
     half = x.shape[-1] // 2
     rot = torch.cat([-x[..., half:], x[..., :half]], dim=-1)
     return x * cos[None, :, None, :] + rot * sin[None, :, None, :]

@@ -80,7 +80,7 @@ class TrainableDecoder:
         for i in range(cfg.num_hidden_layers):
             self.layers.append(FlatGroup(f"layer{i}", _layer_tensors(cfg, i, get), rank, world, self.device, group,
                                          param_dtype))
-        inv, mult = rope_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling, cfg.max_position_embeddings)
+        inv, mult = rope_inv_freq(cfg.rotary_dim, cfg.rope_theta, cfg.rope_scaling, cfg.max_position_embeddings)
         t = torch.arange(max_seq, dtype=torch.float32)
         freqs = torch.outer(t, inv)
         emb = torch.cat([freqs, freqs], -1)

@@ -77,7 +77,7 @@ class StageDecoder(TrainableDecoder):
             self.head_g = grp("head", [("lm_head.weight", head)])
             self.norm_g = grp("norm", [("model.norm.weight", get("model.norm.weight"))])
         self.layers = [grp(f"layer{i}", _layer_tensors(cfg, i, get)) for i in range(lo, hi)]
-        inv, mult = rope_inv_freq(cfg.head_dim, cfg.rope_theta, cfg.rope_scaling, cfg.max_position_embeddings)
+        inv, mult = rope_inv_freq(cfg.rotary_dim, cfg.rope_theta, cfg.rope_scaling, cfg.max_position_embeddings)
         freqs = torch.outer(torch.arange(max_seq, dtype=torch.float32), inv)
         emb = torch.cat([freqs, freqs], -1)
         self.cos = (emb.cos() * mult).to(self.device, torch.bfloat16)  # the same tables as TrainableDecoder

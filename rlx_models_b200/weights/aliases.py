@@ -42,3 +42,26 @@ class CanonicalView:
 
     def __getitem__(self, name):
         return self.take(name)
+
+
+def split_fused_experts(sd: dict, gate_up_order: str = "gate_first") -> dict:
+    """transformers' in-memory MoE layout (``mlp.experts.gate_up_proj`` [E, 2I, H],
+    ``mlp.experts.down_proj`` [E, H, I]) -> the released checkpoints' per-expert
+    names (``mlp.experts.{e}.gate_proj / up_proj / down_proj.weight``). Other
+    tensors pass through; 3-D tensors whose layout differs (gpt-oss's
+    [E, H, 2I] interleaved gate/up) are left to their own loaders."""
+    out = {}
+    for k, v in sd.items():
+        if k.endswith("mlp.experts.gate_up_proj") and v.dim() == 3 and v.shape[1] % 2 == 0:
+            pre = k[: -len("gate_up_proj")]
+            inter = v.shape[1] // 2
+            for e in range(v.shape[0]):
+                out[pre + f"{e}.gate_proj.weight"] = v[e, :inter]
+                out[pre + f"{e}.up_proj.weight"] = v[e, inter:]
+        elif k.endswith("mlp.experts.down_proj") and v.dim() == 3:
+            pre = k[: -len("down_proj")]
+            for e in range(v.shape[0]):
+                out[pre + f"{e}.down_proj.weight"] = v[e]
+        else:
+            out[k] = v
+    return out

@@ -68,9 +68,17 @@ def decoder_tensor_specs(cfg: DecoderConfig) -> list[TensorSpec]:
                           TensorSpec(p + "mlp.experts.down_proj", (E, I, H), "matrix")]
             specs += [TensorSpec(p + "mlp.experts.gate_up_proj_bias", (E, 2 * I), "bias"),
                       TensorSpec(p + "mlp.experts.down_proj_bias", (E, H), "bias")]
-        elif cfg.is_moe:
+        elif cfg.is_moe and cfg.is_moe_layer(i):
             E, I = cfg.num_experts, cfg.moe_intermediate_size
             specs.append(TensorSpec(p + "mlp.gate.weight", (E, H), "matrix"))
+            if cfg.router_scoring == "sigmoid":
+                specs.append(TensorSpec(p + "mlp.gate.e_score_correction_bias", (E,), "sinks", torch.float32))
+            if cfg.n_shared_experts:
+                Is = I * cfg.n_shared_experts
+                ps = p + "mlp.shared_experts."
+                specs += [TensorSpec(ps + "gate_proj.weight", (Is, H), "matrix"),
+                          TensorSpec(ps + "up_proj.weight", (Is, H), "matrix"),
+                          TensorSpec(ps + "down_proj.weight", (H, Is), "matrix")]
             for e in range(E):
                 pe = p + f"mlp.experts.{e}."
                 specs += [TensorSpec(pe + "gate_proj.weight", (I, H), "matrix"),

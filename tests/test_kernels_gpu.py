@@ -87,20 +87,22 @@ def test_embedding(cuda):
     assert torch.equal(ops.embedding(ids, tab), tab[ids.long()])
 
 
-@pytest.mark.parametrize("D,Hq,Hkv", [(128, 32, 8), (64, 8, 1)])
-def test_qkv_rope_cache_write(cuda, D, Hq, Hkv):
+@pytest.mark.parametrize("D,Hq,Hkv,rot", [(128, 32, 8, 128), (64, 8, 1, 64), (128, 8, 2, 64), (64, 4, 2, 32),
+                                           (128, 4, 1, 96)])
+def test_qkv_rope_cache_write(cuda, D, Hq, Hkv, rot):
+    """QK-norm + RoPE (full, or partial over the first ``rot`` dims) + paged cache write."""
     T = 40
     qkv = _mk((T, (Hq + 2 * Hkv) * D), cuda, 1.0, 14)
     qn, kn = _mk((D,), cuda, 1.0, 15), _mk((D,), cuda, 1.0, 16)
     pos = torch.randint(0, 3000, (T,), dtype=torch.int32, device=cuda)
-    inv, _ = ops.rope_inv_freq(D, 1e6)
+    inv, _ = ops.rope_inv_freq(rot, 1e6)
     inv = inv.to(cuda)
     NB = 16
     kc = torch.zeros(NB, Hkv, 16, D, dtype=torch.bfloat16, device=cuda)
     vc = torch.zeros_like(kc)
     slots = torch.randperm(NB * 16, device=cuda)[:T].long()
     q = ops.qkv_rope(qkv, num_q_heads=Hq, num_kv_heads=Hkv, head_dim=D, positions=pos, inv_freq=inv,
-                     q_norm=qn, k_norm=kn, eps=1e-6, slots=slots, k_cache=kc, v_cache=vc)
+                     q_norm=qn, k_norm=kn, eps=1e-6, slots=slots, k_cache=kc, v_cache=vc, rot_dim=rot)
     qr = qkv[:, :Hq * D].view(T, Hq, D)
     kr = qkv[:, Hq * D:(Hq + Hkv) * D].view(T, Hkv, D)
     vr = qkv[:, (Hq + Hkv) * D:].view(T, Hkv, D)
