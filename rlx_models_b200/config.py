@@ -56,6 +56,12 @@ class DecoderConfig:
     rope_theta: float = 1e6
     rope_scaling: dict | None = None
     partial_rotary_factor: float = 1.0  # RoPE on the first head_dim * factor dims (GLM-4: 0.5)
+    # Granite scalars: h = embed * embedding_multiplier; h += residual_multiplier * sublayer;
+    # attention scale = attention_multiplier (0: 1/sqrt(head_dim)); logits / logits_scaling
+    embedding_multiplier: float = 1.0
+    residual_multiplier: float = 1.0
+    attention_multiplier: float = 0.0
+    logits_scaling: float = 1.0
     max_position_embeddings: int = 40960
     tie_word_embeddings: bool = False
     qk_norm: bool = True
@@ -156,6 +162,14 @@ class DecoderConfig:
             kw["moe_intermediate_size"] = d.get("moe_intermediate_size", 1408)
             kw["shared_expert_intermediate_size"] = d.get("shared_expert_intermediate_size", 0)
             kw["norm_topk_prob"] = bool(d.get("norm_topk_prob", False))
+        elif mt in ("granite", "phi3"):
+            kw["qk_norm"] = False
+            kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-5))
+            rs = kw.get("rope_scaling")
+            if rs and rs.get("rope_type", rs.get("type")) in ("longrope", "su"):
+                rs = dict(rs)
+                rs.setdefault("original_max_position_embeddings", d.get("original_max_position_embeddings", 4096))
+                kw["rope_scaling"] = rs
         elif mt in ("llama", "mistral", "qwen2"):
             kw["qk_norm"] = False
             kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-5))

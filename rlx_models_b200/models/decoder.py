@@ -71,7 +71,7 @@ class DecoderLM:
         inv, mult = rope_inv_freq(c.rotary_dim, c.rope_theta, c.rope_scaling, c.max_position_embeddings)
         self.inv_freq = inv.to(self.device)
         self.rope_mult = mult
-        self.scale = 1.0 / math.sqrt(c.head_dim)
+        self.scale = c.attention_multiplier or 1.0 / math.sqrt(c.head_dim)
         self._load(weights)
 
     # -- weights ---------------------------------------------------------------
@@ -96,6 +96,14 @@ class DecoderLM:
 
         def dv(t):
             return t.to(device=dev, dtype=bf).contiguous()
+
+        from ..weights.aliases import FusedSplitView
+        if FusedSplitView.needed(w):  # Phi-3: fused qkv_proj / gate_up_proj
+            w = FusedSplitView(w, c.q_size, c.kv_size, c.intermediate_size)
+        rm = c.residual_multiplier
+
+        def dv_res(t):  # Granite: the residual multiplier folds into o_proj / down_proj
+            return dv(t.to(dev).float() * rm) if rm != 1.0 else dv(t)
 
         self.embed = dv(g("model.embed_tokens.weight"))
         self.norm = dv(g("model.norm.weight"))
@@ -127,12 +135,12 @@ class DecoderLM:
                 L.bqkv = dv(torch.cat([qb.to(dev), kb.to(dev), vb.to(dev)]))
             L.q_norm = dv(g(p + "self_attn.q_norm.weight")) if c.qk_norm else None
             L.k_norm = dv(g(p + "self_attn.k_norm.weight")) if c.qk_norm else None
-            L.wo = dv(self._cols(g(p + "self_attn.o_proj.weight"), self.hq * D))
+            L.wo = dv_res(self._cols(g(p + "self_attn.o_proj.weight"), self.hq * D))
             L.bo = None
             gt = self._rows(g(p + "mlp.gate_proj.weight"), self.inter)
             up = self._rows(g(p + "mlp.up_proj.weight"), self.inter)
             L.w_gu = interleave_gate_up(gt.to(dev, bf), up.to(dev, bf))
-            L.wd = dv(self._cols(g(p + "mlp.down_proj.weight"), self.inter))
+            L.wd = dv_res(self._cols(g(p + "mlp.down_proj.weight"), self.inter))
             L.sinks = None
             L.window = c.layer_window(i)
             self.layers.append(L)
@@ -167,6 +175,8 @@ class DecoderLM:
         """Returns the final-normed hidden states of every token ([T, H])."""
         comm = self.comm or LocalComm(self.cfg.rms_norm_eps)
         h = comm.embed(fb.input_ids, self.embed)
+        if self.cfg.embedding_multiplier != 1.0:
+            h.mul_(self.cfg.embedding_multiplier)
         x = comm.norm_in(h, self.layers[0].ln1)
         n = len(self.layers)
         for i, L in enumerate(self.layers):
@@ -186,7 +196,7 @@ class DecoderLM:
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
         """lm_head on final-normed rows (fp32; vocab-sharded under TP)."""
-        return ops.linear(x, self.lm_head, out_dtype=torch.float32)
+        return ops.linear(x, self.lm_head, out_dtype=torch.float32, alpha=1.0 / self.cfg.logits_scaling)
 
     def forward(self, fb: ForwardBatch, kv: PagedKVCache) -> torch.Tensor:
         x = self.forward_hidden(fb, kv)

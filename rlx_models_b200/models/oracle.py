@@ -43,7 +43,10 @@ class DecoderOracle:
     def __init__(self, cfg: DecoderConfig, weights: dict[str, torch.Tensor], device="cpu"):
         self.cfg = cfg
         self.device = torch.device(device)
-        from ..weights.aliases import canonical_name
+        from ..weights.aliases import FusedSplitView, canonical_name
+        if FusedSplitView.needed(weights):  # Phi-3 fused qkv / gate_up
+            v = FusedSplitView(weights, cfg.q_size, cfg.kv_size, cfg.intermediate_size)
+            weights = {k: v[k] for k in v.keys()}
         self.w = {canonical_name(cfg.model_type, k): v.to(self.device) for k, v in weights.items()}
         self.inv_freq, self.rope_mult = rope_inv_freq(cfg.rotary_dim, cfg.rope_theta, cfg.rope_scaling,
                                                       cfg.max_position_embeddings)
@@ -98,7 +101,8 @@ class DecoderOracle:
             kv.v[i] = torch.cat([kv.v[i], v])
         kpos = torch.arange(kv.k[i].shape[0], device=x.device)
         sinks = self.W(p + "sinks") if c.attn_sinks else None
-        o = R.attention(q, kv.k[i], kv.v[i], pos, kpos, 1.0 / math.sqrt(c.head_dim), causal=True,
+        o = R.attention(q, kv.k[i], kv.v[i], pos, kpos, c.attention_multiplier or 1.0 / math.sqrt(c.head_dim),
+                        causal=True,
                         window=c.layer_window(i), sinks=sinks)
         y = self._mm(o.reshape(T, -1), p + "o_proj.weight")
         if (p + "o_proj.bias") in self.w:
@@ -168,7 +172,7 @@ class DecoderOracle:
         h, kv = self.forward_hidden(ids, kv)
         c = self.cfg
         head = self.W("model.embed_tokens.weight") if c.tie_word_embeddings else self.W("lm_head.weight")
-        return h @ head.T, kv
+        return h @ head.T / c.logits_scaling, kv
 
     @torch.no_grad()
     def forward_hidden(self, ids: torch.Tensor, kv: OracleKV | None = None) -> tuple[torch.Tensor, OracleKV]:
@@ -178,11 +182,12 @@ class DecoderOracle:
             kv = OracleKV(c.num_hidden_layers)
         start = kv.length
         pos = torch.arange(start, start + ids.shape[0], device=self.device)
-        h = self.W("model.embed_tokens.weight")[ids.to(self.device).long()]
+        h = self.W("model.embed_tokens.weight")[ids.to(self.device).long()] * c.embedding_multiplier
+        rm = c.residual_multiplier
         for i in range(c.num_hidden_layers):
             p = f"model.layers.{i}."
-            h = h + self._attn(i, R.rmsnorm(h, self.W(p + "input_layernorm.weight"), c.rms_norm_eps), pos, kv)
-            h = h + self._mlp(i, R.rmsnorm(h, self.W(p + "post_attention_layernorm.weight"), c.rms_norm_eps))
+            h = h + rm * self._attn(i, R.rmsnorm(h, self.W(p + "input_layernorm.weight"), c.rms_norm_eps), pos, kv)
+            h = h + rm * self._mlp(i, R.rmsnorm(h, self.W(p + "post_attention_layernorm.weight"), c.rms_norm_eps))
         return R.rmsnorm(h, self.W("model.norm.weight"), c.rms_norm_eps), kv
 
     @torch.no_grad()

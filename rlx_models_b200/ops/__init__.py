@@ -178,7 +178,8 @@ def rope_inv_freq(head_dim: int, theta: float, scaling: dict | None = None,
                   max_position: int | None = None) -> tuple[torch.Tensor, float]:
     """fp32 inverse frequencies (HF formula) and the cos/sin multiplier.
 
-    Supports no scaling, ``linear``, ``llama3`` and ``yarn`` (returns mscale).
+    Supports no scaling, ``linear``, ``llama3``, ``longrope`` / ``su`` and
+    ``yarn`` (the last two return their attention factor).
     """
     inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).float() / head_dim))
     mult = 1.0
@@ -198,6 +199,17 @@ def rope_inv_freq(head_dim: int, theta: float, scaling: dict | None = None,
             mid = (1 - smooth) * scaled / factor + smooth * scaled
             is_mid = (wl >= hi_wl) & (wl <= lo_wl)
             inv = torch.where(is_mid, mid, scaled)
+        elif kind in ("longrope", "su"):
+            # per-dimension extension factors (Phi-3): the short factors; the long ones
+            # replace them when ``scaling["use_long_factor"]`` is set
+            old = float(scaling.get("original_max_position_embeddings", max_position or 4096))
+            ext = scaling["long_factor"] if scaling.get("use_long_factor") else scaling["short_factor"]
+            inv = inv / torch.tensor(ext, dtype=torch.float32)
+            factor = float(scaling.get("factor") or (max_position or old) / old)
+            if scaling.get("attention_factor") is not None:
+                mult = float(scaling["attention_factor"])
+            elif factor > 1.0:
+                mult = math.sqrt(1 + math.log(factor) / math.log(old))
         elif kind == "yarn":
             factor = float(scaling["factor"])
             old = float(scaling.get("original_max_position_embeddings", max_position or 4096))

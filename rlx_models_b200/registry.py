@@ -50,7 +50,7 @@ class RandomWeights:
         return list(self.specs)
 
 
-@register("qwen3", "llama", "mistral", "qwen2")
+@register("qwen3", "llama", "mistral", "qwen2", "granite", "phi3")
 def _dense(cfg, weights, device, tp_rank, tp_size, comm):
     from .models.decoder import DecoderLM
     return DecoderLM(cfg, weights, device=device, tp_rank=tp_rank, tp_size=tp_size, comm=comm)

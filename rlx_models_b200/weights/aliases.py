@@ -65,3 +65,42 @@ def split_fused_experts(sd: dict, gate_up_order: str = "gate_first") -> dict:
         else:
             out[k] = v
     return out
+
+
+class FusedSplitView:
+    """Weight source with fused dense projections presented as the separate
+    ones the builders read: ``self_attn.qkv_proj`` -> q / k / v rows and
+    ``mlp.gate_up_proj`` -> gate / up rows (Phi-3 layout)."""
+
+    def __init__(self, weights, q_size: int, kv_size: int, intermediate: int):
+        self.w = weights
+        self.map: dict[str, tuple[str, int | None, int | None]] = {}
+        for n in list(weights.keys()):
+            if n.endswith("self_attn.qkv_proj.weight") or n.endswith("self_attn.qkv_proj.bias"):
+                pre, suf = n.rsplit("qkv_proj.", 1)
+                for part, (a, ln) in zip("qkv", ((0, q_size), (q_size, kv_size), (q_size + kv_size, kv_size))):
+                    self.map[f"{pre}{part}_proj.{suf}"] = (n, a, ln)
+            elif n.endswith("mlp.gate_up_proj.weight"):
+                pre = n[: -len("gate_up_proj.weight")]
+                self.map[pre + "gate_proj.weight"] = (n, 0, intermediate)
+                self.map[pre + "up_proj.weight"] = (n, intermediate, intermediate)
+            else:
+                self.map[n] = (n, None, None)
+
+    @staticmethod
+    def needed(weights) -> bool:
+        return any(n.endswith("qkv_proj.weight") or n.endswith("mlp.gate_up_proj.weight") for n in weights.keys())
+
+    def keys(self):
+        return list(self.map)
+
+    def __contains__(self, name):
+        return name in self.map
+
+    def take(self, name, **kw):
+        n, a, ln = self.map[name]
+        t = self.w.take(n) if hasattr(self.w, "take") else self.w[n]
+        return t if a is None else t.narrow(0, a, ln)
+
+    def __getitem__(self, name):
+        return self.take(name)

@@ -28,6 +28,8 @@ def _prefill(model, ids, dev):
     ("llama", dict(qk_norm=False, tie_word_embeddings=False, rope_theta=5e5)),
     ("qwen2", dict(qk_norm=False, attention_bias=True, tie_word_embeddings=True)),
     ("mistral", dict(qk_norm=False, tie_word_embeddings=False, rope_theta=1e6)),
+    ("granite", dict(qk_norm=False, tie_word_embeddings=True, embedding_multiplier=12.0, residual_multiplier=0.22,
+                     attention_multiplier=0.0078125, logits_scaling=8.0)),
 ])
 def test_family_vs_oracle(cuda, family, over):
     cfg = C.tiny(family, num_hidden_layers=2, hidden_size=256, intermediate_size=512, num_attention_heads=4,
@@ -63,3 +65,32 @@ def test_embed_matches_oracle_hidden(cuda):
             r = r / r.norm()
             assert torch.nn.functional.cosine_similarity(e[i], r, dim=0) > 0.999
     assert torch.allclose(e.norm(dim=-1), torch.ones(3), atol=1e-4)
+
+
+def test_phi3_fused_longrope_partial_vs_oracle(cuda):
+    """Phi-3 layout (fused qkv_proj / gate_up_proj), LongRoPE short factors with
+    the attention factor, RoPE on 3/4 of each head."""
+    g = torch.Generator().manual_seed(9)
+    rot = 48
+    rs = {"rope_type": "longrope", "short_factor": (1 + 2 * torch.rand(rot // 2, generator=g)).tolist(),
+          "long_factor": (2 + 8 * torch.rand(rot // 2, generator=g)).tolist(), "original_max_position_embeddings": 256}
+    cfg = C.tiny("phi3", num_hidden_layers=2, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=64, vocab_size=512, qk_norm=False, tie_word_embeddings=False,
+                 partial_rotary_factor=0.75, rope_scaling=rs, max_position_embeddings=1024, rope_theta=1e4)
+    w = random_weights(cfg, 5, dtype=torch.bfloat16)
+    fused = {}
+    for k, v in w.items():
+        if ".self_attn.q_proj." in k:
+            p = k.replace("q_proj", "qkv_proj")
+            fused[p] = torch.cat([v, w[k.replace("q_proj", "k_proj")], w[k.replace("q_proj", "v_proj")]], 0)
+        elif ".mlp.gate_proj." in k:
+            fused[k.replace("gate_proj", "gate_up_proj")] = torch.cat([v, w[k.replace("gate_proj", "up_proj")]], 0)
+        elif not any(s in k for s in (".k_proj.", ".v_proj.", ".up_proj.")):
+            fused[k] = v
+    model = DecoderLM(cfg, fused, device=cuda)
+    ids = torch.randint(0, 512, (200,), generator=torch.Generator().manual_seed(2)).tolist()
+    lg = _prefill(model, ids, cuda).float().cpu()
+    ref, _ = DecoderOracle(cfg, {k: v.float() for k, v in fused.items()}).forward(torch.tensor(ids))
+    rel = ((lg - ref).norm() / ref.norm()).item()
+    assert rel < 2e-2, rel
+    assert (lg.argmax(-1) == ref.argmax(-1)).float().mean() > 0.9
