@@ -62,6 +62,15 @@ class DecoderConfig:
     residual_multiplier: float = 1.0
     attention_multiplier: float = 0.0
     logits_scaling: float = 1.0
+    # Gemma axes: GeGLU MLP, (1 + w) RMSNorm weights, sandwich norms (post-attention /
+    # pre- and post-feedforward), attention and final logit softcapping, a separate
+    # RoPE base for sliding-window layers
+    mlp_act: str = "silu"  # "silu" | "gelu_tanh"
+    norm_unit_offset: bool = False
+    sandwich_norm: bool = False
+    attn_softcap: float = 0.0
+    final_softcap: float = 0.0
+    rope_local_theta: float = 0.0
     max_position_embeddings: int = 40960
     tie_word_embeddings: bool = False
     qk_norm: bool = True
@@ -162,6 +171,35 @@ class DecoderConfig:
             kw["moe_intermediate_size"] = d.get("moe_intermediate_size", 1408)
             kw["shared_expert_intermediate_size"] = d.get("shared_expert_intermediate_size", 0)
             kw["norm_topk_prob"] = bool(d.get("norm_topk_prob", False))
+        elif mt in ("gemma", "gemma2", "gemma3_text", "gemma3"):
+            kw["qk_norm"] = mt.startswith("gemma3")
+            kw["norm_unit_offset"] = True
+            kw["sandwich_norm"] = mt != "gemma"
+            act = d.get("hidden_activation") or d.get("hidden_act") or "gelu_pytorch_tanh"
+            kw["mlp_act"] = "gelu_tanh" if "gelu" in act else "silu"
+            kw["embedding_multiplier"] = float(d["hidden_size"]) ** 0.5
+            if d.get("query_pre_attn_scalar"):
+                kw["attention_multiplier"] = float(d["query_pre_attn_scalar"]) ** -0.5
+            kw["attn_softcap"] = float(d.get("attn_logit_softcapping") or 0.0)
+            kw["final_softcap"] = float(d.get("final_logit_softcapping") or 0.0)
+            kw["tie_word_embeddings"] = d.get("tie_word_embeddings", True)
+            kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-6))
+            n = d["num_hidden_layers"]
+            if mt != "gemma" and not d.get("layer_types"):
+                period = 2 if mt == "gemma2" else int(d.get("sliding_window_pattern", 6))
+                kw["layer_types"] = ["full_attention" if (i + 1) % period == 0 else "sliding_attention"
+                                     for i in range(n)]
+            if mt == "gemma":
+                kw["sliding_window"] = 0
+            rp = raw.get("rope_parameters") or (merge_text_config(raw).get("rope_parameters"))
+            if isinstance(rp, dict) and "full_attention" in rp:  # per-layer-type RoPE (Gemma-3)
+                full, local = rp["full_attention"], rp.get("sliding_attention", {})
+                kw["rope_theta"] = float(full.get("rope_theta", 1e6))
+                kind = full.get("rope_type", "default")
+                kw["rope_scaling"] = None if kind == "default" else {k: v for k, v in full.items() if k != "rope_theta"}
+                kw["rope_local_theta"] = float(local.get("rope_theta", 1e4))
+            elif d.get("rope_local_base_freq"):
+                kw["rope_local_theta"] = float(d["rope_local_base_freq"])
         elif mt in ("granite", "phi3"):
             kw["qk_norm"] = False
             kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-5))

@@ -32,6 +32,11 @@ namespace attn {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kNegInf = -INFINITY;
 
+// Scaled score in log2 units; with logit softcapping, cap * tanh(scale * s / cap).
+__device__ __forceinline__ float score_log2(float s, const AttnArgs& a, float scale_log2) {
+  return a.softcap > 0.f ? a.softcap * tanhf(s * a.scale / a.softcap) * kLog2e : s * scale_log2;
+}
+
 // ---------------------------------------------------------------------------
 // Decode: grid (B * Hkv, splits), 4 compute warps + 1 TMA producer warp.
 // Warp w consumes pages w, w+4, ... of this split from an NST-deep ring.
@@ -159,7 +164,7 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
         for (int h = 0; h < 4; ++h) {
           const int tk = base_tok + nt * 8 + 2 * t4 + (h & 1);
           const bool ok = tk < ctx && tk >= first_tok;
-          sc[nt][h] = ok ? sc[nt][h] * scale_log2 : kNegInf;
+          sc[nt][h] = ok ? score_log2(sc[nt][h], a, scale_log2) : kNegInf;
           mx[h >> 1] = fmaxf(mx[h >> 1], sc[nt][h]);
         }
 #pragma unroll
@@ -457,7 +462,7 @@ __global__ void __launch_bounds__(288) prefill_attn_kernel(const __grid_constant
         const int kp = key0 + nt * 8 + 2 * t4 + (h & 1);
         const bool ok = r_ok[r] && kp < ctx &&
                         (!causal || (kp <= r_pos[r] && (a.window <= 0 || kp > r_pos[r] - a.window)));
-        sc[nt][h] = ok ? sc[nt][h] * scale_log2 : kNegInf;
+        sc[nt][h] = ok ? score_log2(sc[nt][h], a, scale_log2) : kNegInf;
         mx[r] = fmaxf(mx[r], sc[nt][h]);
       }
 #pragma unroll
@@ -553,7 +558,7 @@ int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
   if (a.B == 0) return 0;
   const int G = a.Hq / a.Hkv;
   if (G > 16 || a.Hq % a.Hkv != 0) throw std::runtime_error("b200.decode_attention: G must divide and be <= 16");
-  if (a.D != 128 && a.D != 64) throw std::runtime_error("b200.decode_attention: D must be 64 or 128");
+  if (a.D != 256 && a.D != 128 && a.D != 64) throw std::runtime_error("b200.decode_attention: D must be 64, 128 or 256");
   const int64_t rows = a.num_blocks * a.Hkv * 16;
   CUtensorMap tk = make_tmap_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
   CUtensorMap tv = make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
@@ -569,7 +574,14 @@ int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
   if (splits > 1 && a.ws_elems < (int64_t)a.B * a.Hq * splits * (a.D + 2))
     throw std::runtime_error("b200.decode_attention: split workspace too small");
   dim3 grid(a.B * a.Hkv, splits);
-  if (a.D == 128) {
+  if (a.D == 256) {
+    constexpr int NST = 4;
+    auto k = decode_attn_kernel<256, NST>;
+    static bool once = false;
+    if (!once) { set_smem(k, DecCfg<256, NST>::SMEM, a.device); once = true; }
+    launch_pdl(k, grid, dim3(160), DecCfg<256, NST>::SMEM, st, tk, tv, a);
+    if (splits > 1) launch_pdl(decode_merge_kernel<256>, dim3(a.B * a.Hq), dim3(256), 0, st, a, splits);
+  } else if (a.D == 128) {
     constexpr int NST = 8;
     auto k = decode_attn_kernel<128, NST>;
     static bool once = false;
@@ -597,14 +609,21 @@ void prefill_attention_launch(const AttnArgs& a, cudaStream_t st) {
   if (a.kv_dense) throw std::runtime_error("b200.prefill_attention: row-major K/V needs the tcgen05 kernel (D 128)");
   const int G = a.Hq / a.Hkv;
   if (a.Hq % a.Hkv != 0 || 128 % G != 0) throw std::runtime_error("b200.prefill_attention: G must divide 128");
-  if (a.D != 128 && a.D != 64) throw std::runtime_error("b200.prefill_attention: D must be 64 or 128");
+  if (a.D != 256 && a.D != 128 && a.D != 64)
+    throw std::runtime_error("b200.prefill_attention: D must be 64, 128 or 256");
   const int64_t rows = a.num_blocks * a.Hkv * 16;
   CUtensorMap tk = make_tmap_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
   CUtensorMap tv = make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
   const int rows_tok = 128 / G;
   const int q_tiles = (a.max_q_len + rows_tok - 1) / rows_tok;
   dim3 grid(a.B * q_tiles, a.Hkv);
-  if (a.D == 128) {
+  if (a.D == 256) {
+    constexpr int NST = 2;
+    auto k = prefill_attn_kernel<256, NST>;
+    static bool once = false;
+    if (!once) { set_smem(k, PreCfg<256, NST>::SMEM, a.device); once = true; }
+    launch_pdl(k, grid, dim3(288), PreCfg<256, NST>::SMEM, st, tk, tv, a, q_tiles, rows_tok);
+  } else if (a.D == 128) {
     constexpr int NST = 2;
     auto k = prefill_attn_kernel<128, NST>;
     static bool once = false;

@@ -374,7 +374,9 @@ bool fmha_supported(const AttnArgs& a) {
     return e != nullptr && e[0] == '1';
   }();
   const int G = a.Hq / a.Hkv;
-  return !legacy && a.D == 128 && a.Hq % a.Hkv == 0 && G >= 1 && G <= 8 && (G & (G - 1)) == 0 && a.q_rows > 0;
+  // logit softcapping runs on the mma.sync kernel
+  return !legacy && a.D == 128 && a.softcap <= 0.f && a.Hq % a.Hkv == 0 && G >= 1 && G <= 8 &&
+         (G & (G - 1)) == 0 && a.q_rows > 0;
 }
 
 void fmha_launch(const AttnArgs& a, cudaStream_t st) {

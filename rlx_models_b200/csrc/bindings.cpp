@@ -26,7 +26,7 @@ void check_cuda(const Tensor& t, const char* name) {
 void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const optional<Tensor>& residual,
             const optional<Tensor>& bias, double alpha, Tensor& ws, Tensor& sem, Tensor& status, int64_t swap,
             int64_t bn, int64_t splits, const optional<Tensor>& trace, int64_t act_from, const optional<Tensor>& gate,
-            int64_t gate_split, int64_t gate_r1, int64_t gate_r2, int64_t gate_off) {
+            int64_t gate_split, int64_t gate_r1, int64_t gate_r2, int64_t gate_off, int64_t glu_act) {
   check_cuda(x, "x");
   check_cuda(w, "w");
   check_cuda(out, "out");
@@ -93,6 +93,8 @@ void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const o
     a.gate_r2 = (int)gate_r2;
     a.gate_off = (int)gate_off;
   }
+  TORCH_CHECK(glu_act == 0 || mode == 2, "b200.linear: glu_act needs the gated (mode 2) epilogue");
+  a.glu_act = (int)glu_act;
   b200::linear_launch(a, cur_stream(x));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -141,7 +143,7 @@ void qkv_rope(const Tensor& qkv, const optional<Tensor>& q_norm, const optional<
                   qkv.stride(1) == 1,
               "b200.qkv_rope: qkv");
   TORCH_CHECK(qkv.size(1) == (Hq + 2 * Hkv) * D, "b200.qkv_rope: qkv width");
-  TORCH_CHECK(D == 64 || D == 128, "b200.qkv_rope: head_dim 64 or 128");
+  TORCH_CHECK(D == 64 || D == 128 || D == 256, "b200.qkv_rope: head_dim 64, 128 or 256");
   TORCH_CHECK(positions.scalar_type() == at::kInt && positions.numel() == qkv.size(0), "b200.qkv_rope: positions");
   TORCH_CHECK(inv_freq.scalar_type() == at::kFloat && inv_freq.numel() == rot_dim / 2, "b200.qkv_rope: inv_freq");
   TORCH_CHECK(q_out.is_contiguous() && q_out.numel() == qkv.size(0) * Hq * D, "b200.qkv_rope: q_out");
@@ -220,9 +222,10 @@ static b200::AttnArgs attn_args(const Tensor& q, const Tensor& k_cache, const Te
 
 int64_t decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& block_tables,
                          const Tensor& ctx_lens, Tensor& out, const optional<Tensor>& sinks, int64_t window,
-                         double scale, int64_t splits, Tensor& ws, Tensor& status) {
+                         double scale, int64_t splits, Tensor& ws, Tensor& status, double softcap) {
   c10::cuda::CUDAGuard g(q.device());
   auto a = attn_args(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, window, scale, status);
+  a.softcap = (float)softcap;
   TORCH_CHECK(q.size(0) == block_tables.size(0), "b200.decode_attention: one query per sequence");
   a.cu_q = nullptr;
   a.splits = (int)splits;
@@ -235,9 +238,11 @@ int64_t decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v
 
 void prefill_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& block_tables,
                        const Tensor& ctx_lens, const Tensor& cu_q, Tensor& out, const optional<Tensor>& sinks,
-                       int64_t window, double scale, int64_t max_q_len, Tensor& status, bool causal, bool q_paged) {
+                       int64_t window, double scale, int64_t max_q_len, Tensor& status, bool causal, bool q_paged,
+                       double softcap) {
   c10::cuda::CUDAGuard g(q.device());
   auto a = attn_args(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, window, scale, status);
+  a.softcap = (float)softcap;
   TORCH_CHECK(cu_q.scalar_type() == at::kInt && cu_q.numel() == block_tables.size(0) + 1, "b200.prefill: cu_q");
   a.cu_q = cu_q.data_ptr<int32_t>();
   a.max_q_len = (int)max_q_len;
@@ -436,13 +441,13 @@ void add_rmsnorm_acc(Tensor& acc, Tensor& h, const Tensor& w, Tensor& out, doubl
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void swiglu_acc(Tensor& acc, Tensor& out) {
+void swiglu_acc(Tensor& acc, Tensor& out, int64_t act) {
   check_cuda(acc, "acc");
   TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && out.is_contiguous() &&
                   acc.size(1) == 2 * out.size(1) && out.size(1) % 64 == 0 && acc.size(0) == out.size(0),
               "b200.swiglu_acc: shapes");
   c10::cuda::CUDAGuard g(acc.device());
-  b200::swiglu_acc_launch(acc.data_ptr<float>(), out.data_ptr(), out.size(0), out.size(1), cur_stream(acc));
+  b200::swiglu_acc_launch(acc.data_ptr<float>(), out.data_ptr(), out.size(0), out.size(1), (int)act, cur_stream(acc));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -891,7 +896,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rlx_models_b200 sm_100a kernels";
   m.def("linear", &linear, "tcgen05 bf16 GEMM with fused epilogues", py::arg("x"), py::arg("w"), py::arg("out"), py::arg("mode"), py::arg("residual"), py::arg("bias"), py::arg("alpha"), py::arg("ws"), py::arg("sem"), py::arg("status"), py::arg("swap"), py::arg("bn"), py::arg("splits"), py::arg("trace") = py::none(),
         py::arg("act_from") = -1, py::arg("gate") = py::none(), py::arg("gate_split") = 0, py::arg("gate_r1") = 1,
-        py::arg("gate_r2") = 1, py::arg("gate_off") = 0);
+        py::arg("gate_r2") = 1, py::arg("gate_off") = 0, py::arg("glu_act") = 0);
   m.def("gemm", &gemm);
   m.def("gemm_push_shards", &gemm_push_shards);
   m.def("shard_push_add", &shard_push_add);
@@ -919,8 +924,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &embedding);
   m.def("rmsnorm", &rmsnorm);
   m.def("qkv_rope", &qkv_rope);
-  m.def("decode_attention", &decode_attention);
-  m.def("prefill_attention", &prefill_attention);
+  m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("block_tables"), py::arg("ctx_lens"), py::arg("out"), py::arg("sinks"), py::arg("window"),
+        py::arg("scale"), py::arg("splits"), py::arg("ws"), py::arg("status"), py::arg("softcap") = 0.0);
+  m.def("prefill_attention", &prefill_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("block_tables"), py::arg("ctx_lens"), py::arg("cu_q"), py::arg("out"), py::arg("sinks"),
+        py::arg("window"), py::arg("scale"), py::arg("max_q_len"), py::arg("status"), py::arg("causal"),
+        py::arg("q_paged"), py::arg("softcap") = 0.0);
   m.def("argmax", &argmax);
   m.def("sample", &sample);
   m.def("symm_malloc", &symm_malloc);
@@ -933,5 +943,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rs_norm_ag", &rs_norm_ag);
   m.def("os_reduce_norm", &os_reduce_norm);
   m.def("add_rmsnorm_acc", &add_rmsnorm_acc);
-  m.def("swiglu_acc", &swiglu_acc);
+  m.def("swiglu_acc", &swiglu_acc, py::arg("acc"), py::arg("out"), py::arg("act") = 0);
 }

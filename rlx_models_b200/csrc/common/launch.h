@@ -43,6 +43,7 @@ struct LinearArgs {
   // adaLN DiT epilogues (normal orientation): GELU-tanh on columns >= act_from;
   // y *= gate[batch(row)][col] before the residual (batch(row) as in gemm::Params)
   int act = 0, act_from = 0;
+  int glu_act = 0;  // mode 2: 0 SwiGLU, 1 GeGLU (GELU tanh form)
   const void* gate = nullptr;
   int64_t gate_ld = 0;
   int gate_split = 0, gate_r1 = 1, gate_r2 = 1, gate_off = 0;
@@ -195,7 +196,7 @@ struct QkvRopeArgs {
 void qkv_rope_launch(const QkvRopeArgs& a, cudaStream_t st);
 void add_rmsnorm_acc_launch(float* acc, void* h, const void* w, void* out, int64_t ldo, int64_t T, int64_t H,
                             float eps, cudaStream_t st);
-void swiglu_acc_launch(float* acc, void* out, int64_t T, int64_t I, cudaStream_t st);
+void swiglu_acc_launch(float* acc, void* out, int64_t T, int64_t I, int act, cudaStream_t st);
 
 // ---------------- attention ----------------
 struct AttnArgs {
@@ -212,6 +213,7 @@ struct AttnArgs {
   int window;                // sliding window (0 = full)
   int B, Hq, Hkv, D;
   float scale;
+  float softcap = 0.f;       // > 0: scores = softcap * tanh(scale * q.k / softcap) (Gemma-2)
   int max_q_len;             // prefill: max query length per sequence
   int splits;                // decode: KV splits (0 = auto)
   int causal = 1;            // prefill: 0 = every query sees the whole context (DiT joint attention)

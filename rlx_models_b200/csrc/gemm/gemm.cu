@@ -138,6 +138,7 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
   if (p.bcast && !sw) throw std::runtime_error("b200.linear: broadcast push needs the swap-AB (decode) path");
   p.trace = a.trace;
   p.act = a.act;
+  p.glu_act = a.glu_act;
   p.act_from = a.act_from;
   p.gate = reinterpret_cast<const __nv_bfloat16*>(a.gate);
   p.gate_ld = a.gate_ld;

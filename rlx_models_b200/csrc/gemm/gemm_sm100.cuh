@@ -74,6 +74,7 @@ struct Params {
   //   gate != null: y = gate[batch(i)][j] * y before the residual is added, with
   //   batch(i) = g < gate_split ? g / gate_r1 : (g - gate_split) / gate_r2 with g = i + gate_off.
   int act, act_from;
+  int glu_act;  // EPI_SWIGLU gate activation: 0 SiLU (SwiGLU), 1 GELU tanh form (GeGLU)
   const __nv_bfloat16* gate;
   int64_t gate_ld;
   int gate_split, gate_r1, gate_r2, gate_off;
@@ -260,6 +261,7 @@ __device__ __forceinline__ void store_chunk(const Params& p, int i, int j0, floa
 }
 
 __device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.f + __expf(-g)) * u; }
+__device__ __forceinline__ float glu_mul(float g, float u, int act) { return act ? gelu_tanh(g) * u : silu_mul(g, u); }
 
 // Swap-AB output: token j, NV consecutive features [fo, fo + NV) of one lane
 // (the lanes of a warp cover one token's features contiguously).
@@ -650,8 +652,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (EPI == EPI_SWIGLU) {
               const int fl = lane * 2;  // 64 outputs per tile: 2 per lane
               const int fo = m_tile * 64 + fl;
-              float o[4] = {silu_mul(xchg[tt * 132 + fl] * p.alpha, xchg[tt * 132 + 64 + fl] * p.alpha),
-                            silu_mul(xchg[tt * 132 + fl + 1] * p.alpha, xchg[tt * 132 + 64 + fl + 1] * p.alpha),
+              float o[4] = {glu_mul(xchg[tt * 132 + fl] * p.alpha, xchg[tt * 132 + 64 + fl] * p.alpha, p.glu_act),
+                            glu_mul(xchg[tt * 132 + fl + 1] * p.alpha, xchg[tt * 132 + 64 + fl + 1] * p.alpha,
+                                    p.glu_act),
                             0.f, 0.f};
               store_vec<EPI, 2>(p, j, fo, nfeat, o);
             } else {
@@ -674,7 +677,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             fetch(g * 4 + h, vg);
             fetch(g * 4 + h + 2, vu);
 #pragma unroll
-            for (int t = 0; t < 32; ++t) vg[t] = silu_mul(vg[t] * p.alpha, vu[t] * p.alpha);
+            for (int t = 0; t < 32; ++t) vg[t] = glu_mul(vg[t] * p.alpha, vu[t] * p.alpha, p.glu_act);
             Params q = p;
             q.alpha = 1.f;
             q.NB = p.NB / 2;

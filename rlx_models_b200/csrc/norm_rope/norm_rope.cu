@@ -226,7 +226,8 @@ void qkv_rope_launch(const QkvRopeArgs& a, cudaStream_t st) {
   const int64_t warps = a.T * (a.Hq + 2 * a.Hkv);
   const int wpb = 8;
   const unsigned grid = (unsigned)((warps + wpb - 1) / wpb);
-  if (a.D == 128) launch_pdl(qkv_rope_kernel<4>, dim3(grid), dim3(wpb * 32), 0, st, a);
+  if (a.D == 256) launch_pdl(qkv_rope_kernel<8>, dim3(grid), dim3(wpb * 32), 0, st, a);
+  else if (a.D == 128) launch_pdl(qkv_rope_kernel<4>, dim3(grid), dim3(wpb * 32), 0, st, a);
   else launch_pdl(qkv_rope_kernel<2>, dim3(grid), dim3(wpb * 32), 0, st, a);
 }
 
@@ -316,7 +317,19 @@ void add_rmsnorm_acc_launch(float* acc, void* h, const void* w, void* out, int64
 
 // out[t, f] = silu(acc[t, g(f)]) * acc[t, g(f) + 64], g(f) = (f / 64) * 128 + f % 64
 // (gate/up interleaved in groups of 64 features); the consumed sums are zeroed.
-__global__ void swiglu_acc_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ out, int64_t I, int64_t T) {
+// act = 1: GELU (tanh form) on the gate instead of SiLU (GeGLU).
+__device__ __forceinline__ float glu_gate(float g, int act) {
+  if (act) {
+    const float u = 0.7978845608028654f * (g + 0.044715f * g * g * g);
+    float t;
+    asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+    return 0.5f * g * (1.f + t);
+  }
+  return g / (1.f + __expf(-g));
+}
+
+__global__ void swiglu_acc_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ out, int64_t I, int64_t T,
+                                  int act) {
   pdl_wait();
   pdl_trigger();
   const int64_t idx = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;  // 8 outputs per thread
@@ -337,18 +350,18 @@ __global__ void swiglu_acc_kernel(float* __restrict__ acc, __nv_bfloat16* __rest
   uint32_t o[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const float a = gv[2 * q] / (1.f + __expf(-gv[2 * q])) * uv[2 * q];
-    const float b = gv[2 * q + 1] / (1.f + __expf(-gv[2 * q + 1])) * uv[2 * q + 1];
+    const float a = glu_gate(gv[2 * q], act) * uv[2 * q];
+    const float b = glu_gate(gv[2 * q + 1], act) * uv[2 * q + 1];
     o[q] = pack_bf16x2(a, b);
   }
   *reinterpret_cast<uint4*>(out + t * I + f) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-void swiglu_acc_launch(float* acc, void* out, int64_t T, int64_t I, cudaStream_t st) {
+void swiglu_acc_launch(float* acc, void* out, int64_t T, int64_t I, int act, cudaStream_t st) {
   if (T == 0) return;
   const int64_t n = T * I / 8;
   launch_pdl(swiglu_acc_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, acc,
-             reinterpret_cast<__nv_bfloat16*>(out), I, T);
+             reinterpret_cast<__nv_bfloat16*>(out), I, T, act);
 }
 
 }  // namespace b200

@@ -52,7 +52,8 @@ class ForwardBatch:
 
 
 class LayerWeights:
-    __slots__ = ("ln1", "ln2", "wqkv", "bqkv", "q_norm", "k_norm", "wo", "bo", "w_gu", "wd", "sinks", "window")
+    __slots__ = ("ln1", "ln2", "wqkv", "bqkv", "q_norm", "k_norm", "wo", "bo", "w_gu", "wd", "sinks", "window",
+                 "ln_post_attn", "ln_post_ffn", "inv_freq", "rope_mult")
 
 
 class DecoderLM:
@@ -72,6 +73,13 @@ class DecoderLM:
         self.inv_freq = inv.to(self.device)
         self.rope_mult = mult
         self.scale = c.attention_multiplier or 1.0 / math.sqrt(c.head_dim)
+        self.glu_act = 1 if c.mlp_act == "gelu_tanh" else 0  # GeGLU (Gemma) in the gated GEMM epilogue
+        self.local_rope = None
+        if c.rope_local_theta:  # sliding-window layers with their own RoPE base (Gemma-3)
+            li, lm = rope_inv_freq(c.rotary_dim, c.rope_local_theta, None, c.max_position_embeddings)
+            self.local_rope = (li.to(self.device), lm)
+        if c.sandwich_norm and tp_size > 1:
+            raise NotImplementedError("sandwich-norm (Gemma-2/3) decoders run with tp_size 1")
         self._load(weights)
 
     # -- weights ---------------------------------------------------------------
@@ -105,8 +113,11 @@ class DecoderLM:
         def dv_res(t):  # Granite: the residual multiplier folds into o_proj / down_proj
             return dv(t.to(dev).float() * rm) if rm != 1.0 else dv(t)
 
+        def dv_norm(t):  # Gemma norms compute x * (1 + w): fold the offset at load
+            return dv(t.to(dev).float() + 1.0) if c.norm_unit_offset else dv(t)
+
         self.embed = dv(g("model.embed_tokens.weight"))
-        self.norm = dv(g("model.norm.weight"))
+        self.norm = dv_norm(g("model.norm.weight"))
         if c.tie_word_embeddings:
             head = self.embed
         else:
@@ -121,8 +132,14 @@ class DecoderLM:
         for i in range(c.num_hidden_layers):
             p = f"model.layers.{i}."
             L = LayerWeights()
-            L.ln1 = dv(g(p + "input_layernorm.weight"))
-            L.ln2 = dv(g(p + "post_attention_layernorm.weight"))
+            L.ln1 = dv_norm(g(p + "input_layernorm.weight"))
+            L.ln_post_attn = L.ln_post_ffn = None
+            if c.sandwich_norm:  # pre-MLP norm is pre_feedforward_layernorm; post_attention_layernorm follows attention
+                L.ln2 = dv_norm(g(p + "pre_feedforward_layernorm.weight"))
+                L.ln_post_attn = dv_norm(g(p + "post_attention_layernorm.weight"))
+                L.ln_post_ffn = dv_norm(g(p + "post_feedforward_layernorm.weight"))
+            else:
+                L.ln2 = dv_norm(g(p + "post_attention_layernorm.weight"))
             q = self._rows(g(p + "self_attn.q_proj.weight"), self.hq * D)
             k = self._rows(g(p + "self_attn.k_proj.weight"), self.hkv * D)
             v = self._rows(g(p + "self_attn.v_proj.weight"), self.hkv * D)
@@ -133,8 +150,8 @@ class DecoderLM:
                 kb = self._rows(g(p + "self_attn.k_proj.bias"), self.hkv * D)
                 vb = self._rows(g(p + "self_attn.v_proj.bias"), self.hkv * D)
                 L.bqkv = dv(torch.cat([qb.to(dev), kb.to(dev), vb.to(dev)]))
-            L.q_norm = dv(g(p + "self_attn.q_norm.weight")) if c.qk_norm else None
-            L.k_norm = dv(g(p + "self_attn.k_norm.weight")) if c.qk_norm else None
+            L.q_norm = dv_norm(g(p + "self_attn.q_norm.weight")) if c.qk_norm else None
+            L.k_norm = dv_norm(g(p + "self_attn.k_norm.weight")) if c.qk_norm else None
             L.wo = dv_res(self._cols(g(p + "self_attn.o_proj.weight"), self.hq * D))
             L.bo = None
             gt = self._rows(g(p + "mlp.gate_proj.weight"), self.inter)
@@ -143,6 +160,8 @@ class DecoderLM:
             L.wd = dv_res(self._cols(g(p + "mlp.down_proj.weight"), self.inter))
             L.sinks = None
             L.window = c.layer_window(i)
+            L.inv_freq, L.rope_mult = (self.local_rope if self.local_rope is not None and L.window > 0
+                                       else (self.inv_freq, self.rope_mult))
             self.layers.append(L)
 
     def make_kv_cache(self, num_blocks: int) -> PagedKVCache:
@@ -157,7 +176,7 @@ class DecoderLM:
         else:
             qkv = ops.linear(x, L.wqkv, bias=L.bqkv)
         q = ops.qkv_rope(qkv, num_q_heads=self.hq, num_kv_heads=self.hkv, head_dim=self.D,
-                         positions=fb.positions, inv_freq=self.inv_freq, rope_scale=self.rope_mult,
+                         positions=fb.positions, inv_freq=L.inv_freq, rope_scale=L.rope_mult,
                          rot_dim=self.cfg.rotary_dim,
                          q_norm=L.q_norm, k_norm=L.k_norm, eps=self.cfg.rms_norm_eps, slots=fb.slots,
                          k_cache=kc, v_cache=vc)
@@ -165,11 +184,30 @@ class DecoderLM:
         nd = fb.num_decode
         if nd > 0:
             ops.decode_attention(q[:nd], kc, vc, fb.dec_block_tables, fb.dec_ctx_lens, scale=self.scale,
-                                 sinks=L.sinks, window=L.window, out=o[:nd])
+                                 sinks=L.sinks, window=L.window, out=o[:nd], softcap=self.cfg.attn_softcap)
         if T > nd:
             ops.prefill_attention(q[nd:], kc, vc, fb.pre_block_tables, fb.pre_ctx_lens, fb.pre_cu_q,
-                                  fb.pre_max_q, scale=self.scale, sinks=L.sinks, window=L.window, out=o[nd:])
+                                  fb.pre_max_q, scale=self.scale, sinks=L.sinks, window=L.window, out=o[nd:],
+                                  softcap=self.cfg.attn_softcap)
         return o.view(T, self.hq * self.D)
+
+    def _layer(self, i: int, L: LayerWeights, x: torch.Tensor, h: torch.Tensor, fb: ForwardBatch, kv, comm,
+               nw: torch.Tensor) -> torch.Tensor:
+        """One decoder layer on the normed input ``x``; updates the residual
+        ``h`` in place and returns rmsnorm(h) * nw for the next layer."""
+        eps = self.cfg.rms_norm_eps
+        a = self._attention(i, L, x, fb, kv)
+        if L.ln_post_attn is not None:  # sandwich norms: h += norm(o_proj(a)); h += norm(mlp(norm(h)))
+            y = ops.rmsnorm(ops.linear(a, L.wo), L.ln_post_attn, eps)
+            x = ops.rmsnorm(y, L.ln2, eps, residual=h, residual_out=h)
+            m = ops.linear(ops.linear_swiglu(x, L.w_gu, act=self.glu_act), L.wd)
+            return ops.rmsnorm(ops.rmsnorm(m, L.ln_post_ffn, eps), nw, eps, residual=h, residual_out=h)
+        x = comm.rowpar_add_norm(a, L.wo, h, L.ln2, bias=L.bo)
+        if x.shape[0] <= ops.ACC_MAX_M:
+            gu = ops.swiglu_acc(ops.linear_acc(x, L.w_gu), act=self.glu_act)
+        else:
+            gu = ops.linear_swiglu(x, L.w_gu, act=self.glu_act)
+        return comm.rowpar_add_norm(gu, L.wd, h, nw)
 
     def forward_hidden(self, fb: ForwardBatch, kv: PagedKVCache) -> torch.Tensor:
         """Returns the final-normed hidden states of every token ([T, H])."""
@@ -181,13 +219,7 @@ class DecoderLM:
         n = len(self.layers)
         for i, L in enumerate(self.layers):
             with nvtx(f"layer{i}"):
-                a = self._attention(i, L, x, fb, kv)
-                x = comm.rowpar_add_norm(a, L.wo, h, L.ln2, bias=L.bo)
-                if x.shape[0] <= ops.ACC_MAX_M:
-                    gu = ops.swiglu_acc(ops.linear_acc(x, L.w_gu))
-                else:
-                    gu = ops.linear_swiglu(x, L.w_gu)
-                x = comm.rowpar_add_norm(gu, L.wd, h, self.layers[i + 1].ln1 if i + 1 < n else self.norm)
+                x = self._layer(i, L, x, h, fb, kv, comm, self.layers[i + 1].ln1 if i + 1 < n else self.norm)
             if inspecting():
                 inspect(f"layer{i}.residual", h)
         if inspecting():
@@ -196,7 +228,11 @@ class DecoderLM:
 
     def logits(self, x: torch.Tensor) -> torch.Tensor:
         """lm_head on final-normed rows (fp32; vocab-sharded under TP)."""
-        return ops.linear(x, self.lm_head, out_dtype=torch.float32, alpha=1.0 / self.cfg.logits_scaling)
+        logits = ops.linear(x, self.lm_head, out_dtype=torch.float32, alpha=1.0 / self.cfg.logits_scaling)
+        cap = self.cfg.final_softcap
+        if cap > 0:  # Gemma-2 final logit softcapping
+            logits.div_(cap).tanh_().mul_(cap)
+        return logits
 
     def forward(self, fb: ForwardBatch, kv: PagedKVCache) -> torch.Tensor:
         x = self.forward_hidden(fb, kv)

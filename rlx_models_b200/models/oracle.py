@@ -50,10 +50,17 @@ class DecoderOracle:
         self.w = {canonical_name(cfg.model_type, k): v.to(self.device) for k, v in weights.items()}
         self.inv_freq, self.rope_mult = rope_inv_freq(cfg.rotary_dim, cfg.rope_theta, cfg.rope_scaling,
                                                       cfg.max_position_embeddings)
+        # sliding-window layers with their own RoPE base (Gemma-3)
+        self.local_rope = (rope_inv_freq(cfg.rotary_dim, cfg.rope_local_theta, None, cfg.max_position_embeddings)
+                           if cfg.rope_local_theta else None)
         self._experts: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
 
     def W(self, name: str) -> torch.Tensor:
         return self.w[name].float()
+
+    def N(self, name: str) -> torch.Tensor:
+        """RMSNorm weight (Gemma stores w with the norm computing x * (1 + w))."""
+        return self.W(name) + 1.0 if self.cfg.norm_unit_offset else self.W(name)
 
     def _mm(self, x: torch.Tensor, name: str) -> torch.Tensor:
         """x @ W^T; with ``self.taps`` set, records the input rows per weight
@@ -90,10 +97,12 @@ class DecoderOracle:
         k = proj("k_proj").view(T, c.num_key_value_heads, c.head_dim)
         v = proj("v_proj").view(T, c.num_key_value_heads, c.head_dim)
         if c.qk_norm:
-            q = R.rmsnorm(q, self.W(p + "q_norm.weight"), c.rms_norm_eps)
-            k = R.rmsnorm(k, self.W(p + "k_norm.weight"), c.rms_norm_eps)
-        q = R.rope(q, pos, self.inv_freq, self.rope_mult)
-        k = R.rope(k, pos, self.inv_freq, self.rope_mult)
+            q = R.rmsnorm(q, self.N(p + "q_norm.weight"), c.rms_norm_eps)
+            k = R.rmsnorm(k, self.N(p + "k_norm.weight"), c.rms_norm_eps)
+        inv, mult = (self.local_rope if self.local_rope is not None and c.layer_window(i) > 0
+                     else (self.inv_freq, self.rope_mult))
+        q = R.rope(q, pos, inv, mult)
+        k = R.rope(k, pos, inv, mult)
         if kv.k[i] is None:
             kv.k[i], kv.v[i] = k, v
         else:
@@ -102,8 +111,7 @@ class DecoderOracle:
         kpos = torch.arange(kv.k[i].shape[0], device=x.device)
         sinks = self.W(p + "sinks") if c.attn_sinks else None
         o = R.attention(q, kv.k[i], kv.v[i], pos, kpos, c.attention_multiplier or 1.0 / math.sqrt(c.head_dim),
-                        causal=True,
-                        window=c.layer_window(i), sinks=sinks)
+                        causal=True, window=c.layer_window(i), sinks=sinks, softcap=c.attn_softcap)
         y = self._mm(o.reshape(T, -1), p + "o_proj.weight")
         if (p + "o_proj.bias") in self.w:
             y = y + self.W(p + "o_proj.bias")
@@ -115,7 +123,8 @@ class DecoderOracle:
         if not c.is_moe_layer(i):
             g = self._mm(x, p + "gate_proj.weight")
             u = self._mm(x, p + "up_proj.weight")
-            return self._mm(F.silu(g) * u, p + "down_proj.weight")
+            act = F.gelu(g, approximate="tanh") if c.mlp_act == "gelu_tanh" else F.silu(g)
+            return self._mm(act * u, p + "down_proj.weight")
         if c.model_type == "gpt_oss":
             logits = x @ self.W(p + "router.weight").T + self.W(p + "router.bias")
             topv, topi = logits.topk(c.num_experts_per_tok, dim=-1)
@@ -172,7 +181,10 @@ class DecoderOracle:
         h, kv = self.forward_hidden(ids, kv)
         c = self.cfg
         head = self.W("model.embed_tokens.weight") if c.tie_word_embeddings else self.W("lm_head.weight")
-        return h @ head.T / c.logits_scaling, kv
+        logits = h @ head.T / c.logits_scaling
+        if c.final_softcap > 0:
+            logits = torch.tanh(logits / c.final_softcap) * c.final_softcap
+        return logits, kv
 
     @torch.no_grad()
     def forward_hidden(self, ids: torch.Tensor, kv: OracleKV | None = None) -> tuple[torch.Tensor, OracleKV]:
@@ -184,11 +196,18 @@ class DecoderOracle:
         pos = torch.arange(start, start + ids.shape[0], device=self.device)
         h = self.W("model.embed_tokens.weight")[ids.to(self.device).long()] * c.embedding_multiplier
         rm = c.residual_multiplier
+        eps = c.rms_norm_eps
         for i in range(c.num_hidden_layers):
             p = f"model.layers.{i}."
-            h = h + rm * self._attn(i, R.rmsnorm(h, self.W(p + "input_layernorm.weight"), c.rms_norm_eps), pos, kv)
-            h = h + rm * self._mlp(i, R.rmsnorm(h, self.W(p + "post_attention_layernorm.weight"), c.rms_norm_eps))
-        return R.rmsnorm(h, self.W("model.norm.weight"), c.rms_norm_eps), kv
+            a = self._attn(i, R.rmsnorm(h, self.N(p + "input_layernorm.weight"), eps), pos, kv)
+            if c.sandwich_norm:  # Gemma-2/3: norms on both sides of each sublayer
+                h = h + R.rmsnorm(a, self.N(p + "post_attention_layernorm.weight"), eps)
+                m = self._mlp(i, R.rmsnorm(h, self.N(p + "pre_feedforward_layernorm.weight"), eps))
+                h = h + R.rmsnorm(m, self.N(p + "post_feedforward_layernorm.weight"), eps)
+                continue
+            h = h + rm * a
+            h = h + rm * self._mlp(i, R.rmsnorm(h, self.N(p + "post_attention_layernorm.weight"), eps))
+        return R.rmsnorm(h, self.N("model.norm.weight"), eps), kv
 
     @torch.no_grad()
     def generate(self, prompt: torch.Tensor, max_new_tokens: int) -> tuple[list[int], list[torch.Tensor]]:

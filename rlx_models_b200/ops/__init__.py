@@ -81,14 +81,16 @@ def linear_mxfp4(x: torch.Tensor, w_tiled: torch.Tensor, row_exp: torch.Tensor, 
 
 
 def linear_swiglu(x: torch.Tensor, w_gu: torch.Tensor, *, out: torch.Tensor | None = None,
-                  swap: int = -1, bn: int = 0, splits: int = 0) -> torch.Tensor:
-    """``silu(x @ Wg.T) * (x @ Wu.T)`` with ``w_gu = interleave_gate_up(Wg, Wu)``."""
+                  swap: int = -1, bn: int = 0, splits: int = 0, act: int = 0) -> torch.Tensor:
+    """``silu(x @ Wg.T) * (x @ Wu.T)`` with ``w_gu = interleave_gate_up(Wg, Wu)``;
+    ``act=1``: GELU (tanh form) on the gate instead (GeGLU)."""
     M, N = x.shape[0], w_gu.shape[0]
     if out is None:
         out = torch.empty(M, N // 2, dtype=torch.bfloat16, device=x.device)
     s = scratch(x.device)
     _count(1)
-    ext().linear(x, w_gu, out, 2, None, None, 1.0, s.gemm_ws, s.gemm_sem, s.status, swap, bn, splits)
+    ext().linear(x, w_gu, out, 2, None, None, 1.0, s.gemm_ws, s.gemm_sem, s.status, swap, bn, splits,
+                 glu_act=int(act))
     return out
 
 
@@ -132,12 +134,12 @@ def add_rmsnorm_acc(acc: torch.Tensor, h: torch.Tensor, w: torch.Tensor, eps: fl
     return out
 
 
-def swiglu_acc(acc: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """SwiGLU of interleaved gate/up fp32 sums [M, 2I] -> bf16 [M, I]; zeroes acc."""
+def swiglu_acc(acc: torch.Tensor, out: torch.Tensor | None = None, act: int = 0) -> torch.Tensor:
+    """SwiGLU (``act=1``: GeGLU) of interleaved gate/up fp32 sums [M, 2I] -> bf16 [M, I]; zeroes acc."""
     if out is None:
         out = torch.empty(acc.shape[0], acc.shape[1] // 2, dtype=torch.bfloat16, device=acc.device)
     _count(1)
-    ext().swiglu_acc(acc, out)
+    ext().swiglu_acc(acc, out, int(act))
     return out
 
 
@@ -261,17 +263,19 @@ def qkv_rope(qkv: torch.Tensor, *, num_q_heads: int, num_kv_heads: int, head_dim
 
 
 def decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, *, scale, sinks=None, window=0,
-                     splits=0, out=None):
+                     splits=0, out=None, softcap=0.0):
+    """Paged decode attention (one query per sequence); ``softcap`` > 0 caps
+    the scaled scores at softcap * tanh(s / softcap)."""
     if out is None:
         out = torch.empty_like(q)
     s = scratch(q.device)
     _count(ext().decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, int(window), float(scale),
-                           int(splits), s.attn_ws, s.status))
+                           int(splits), s.attn_ws, s.status, float(softcap)))
     return out
 
 
 def prefill_attention(q, k_cache, v_cache, block_tables, ctx_lens, cu_q, max_q_len, *, scale, sinks=None,
-                      window=0, out=None, causal=True, q_paged=False):
+                      window=0, out=None, causal=True, q_paged=False, softcap=0.0):
     """Causal prefill over paged K/V; ``causal=False`` lets every query see the
     whole context (DiT joint attention) and ``q_paged`` places query/output rows
     through the same block table as the keys (row = table[t // 16] * 16 + t % 16)."""
@@ -280,7 +284,7 @@ def prefill_attention(q, k_cache, v_cache, block_tables, ctx_lens, cu_q, max_q_l
     s = scratch(q.device)
     _count(1)
     ext().prefill_attention(q, k_cache, v_cache, block_tables, ctx_lens, cu_q, out, sinks, int(window),
-                            float(scale), int(max_q_len), s.status, bool(causal), bool(q_paged))
+                            float(scale), int(max_q_len), s.status, bool(causal), bool(q_paged), float(softcap))
     return out
 
 

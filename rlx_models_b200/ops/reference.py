@@ -43,13 +43,17 @@ def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Tensor, k_pos: torch.Tensor,
-              scale: float, causal: bool = True, window: int = 0, sinks: torch.Tensor | None = None) -> torch.Tensor:
-    """Dense GQA attention. q: [Tq, Hq, D], k/v: [Tk, Hkv, D]; returns [Tq, Hq, D] fp32."""
+              scale: float, causal: bool = True, window: int = 0, sinks: torch.Tensor | None = None,
+              softcap: float = 0.0) -> torch.Tensor:
+    """Dense GQA attention. q: [Tq, Hq, D], k/v: [Tk, Hkv, D]; returns [Tq, Hq, D] fp32.
+    ``softcap`` > 0: scaled scores become softcap * tanh(s / softcap)."""
     Hq, Hkv = q.shape[1], k.shape[1]
     G = Hq // Hkv
     kf = k.float().repeat_interleave(G, dim=1)
     vf = v.float().repeat_interleave(G, dim=1)
     s = torch.einsum("qhd,khd->hqk", q.float(), kf) * scale
+    if softcap > 0:
+        s = torch.tanh(s / softcap) * softcap
     mask = torch.ones(q.shape[0], k.shape[0], dtype=torch.bool, device=q.device)
     if causal:
         mask &= k_pos[None, :] <= q_pos[:, None]

@@ -19,7 +19,6 @@ import re
 import torch
 import torch.distributed as dist
 
-from .. import ops
 from ..models.decoder import DecoderLM, LocalComm
 
 _LAYER = re.compile(r"^model\.layers\.(\d+)\.")
@@ -78,19 +77,15 @@ class PipelineDecoderLM(DecoderLM):
         T = fb.num_tokens
         if self.pp_rank == 0:
             h = comm.embed(fb.input_ids, self.embed)
+            if self.cfg.embedding_multiplier != 1.0:
+                h.mul_(self.cfg.embedding_multiplier)
         else:
             h = torch.empty(T, self.cfg.hidden_size, dtype=torch.bfloat16, device=self.device)
             dist.recv(h, src=self.pp_ranks[self.pp_rank - 1], group=self.pp_group)
         x = comm.norm_in(h, self.layers[0].ln1)
         n = len(self.layers)
         for i, L in enumerate(self.layers):
-            a = self._attention(i, L, x, fb, kv)
-            x = comm.rowpar_add_norm(a, L.wo, h, L.ln2, bias=L.bo)
-            if x.shape[0] <= ops.ACC_MAX_M:
-                gu = ops.swiglu_acc(ops.linear_acc(x, L.w_gu))
-            else:
-                gu = ops.linear_swiglu(x, L.w_gu)
-            x = comm.rowpar_add_norm(gu, L.wd, h, self.layers[i + 1].ln1 if i + 1 < n else self.norm)
+            x = self._layer(i, L, x, h, fb, kv, comm, self.layers[i + 1].ln1 if i + 1 < n else self.norm)
         if not self.is_last:
             dist.send(h, dst=self.pp_ranks[self.pp_rank + 1], group=self.pp_group)
             return None

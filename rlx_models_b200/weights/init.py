@@ -39,6 +39,9 @@ def decoder_tensor_specs(cfg: DecoderConfig) -> list[TensorSpec]:
             TensorSpec(p + "self_attn.v_proj.weight", (kv, H), "matrix"),
             TensorSpec(p + "self_attn.o_proj.weight", (H, q), "matrix"),
         ]
+        if cfg.sandwich_norm:
+            specs += [TensorSpec(p + "pre_feedforward_layernorm.weight", (H,), "norm"),
+                      TensorSpec(p + "post_feedforward_layernorm.weight", (H,), "norm")]
         if cfg.qk_norm:
             specs += [TensorSpec(p + "self_attn.q_norm.weight", (D,), "norm"),
                       TensorSpec(p + "self_attn.k_norm.weight", (D,), "norm")]

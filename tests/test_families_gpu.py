@@ -94,3 +94,43 @@ def test_phi3_fused_longrope_partial_vs_oracle(cuda):
     rel = ((lg - ref).norm() / ref.norm()).item()
     assert rel < 2e-2, rel
     assert (lg.argmax(-1) == ref.argmax(-1)).float().mean() > 0.9
+
+
+@pytest.mark.parametrize("family,D", [("gemma", 256), ("gemma2", 256), ("gemma3_text", 128), ("gemma3_text", 256)])
+def test_gemma_vs_oracle(cuda, family, D):
+    """Gemma 1 / 2 / 3 on the GPU: GeGLU epilogue, (1 + w) norms, sandwich norms,
+    attention (Gemma-2) and final logit softcapping in the kernels, sliding
+    layers shorter than the prompt, Gemma-3 local RoPE base and QK-norm;
+    head_dim 256 through the QK-norm/RoPE, prefill and decode kernels."""
+    from rlx_models_b200.api import LLM
+    from rlx_models_b200.runtime.engine import EngineConfig, SamplingParams
+    over = dict(qk_norm=family == "gemma3_text", norm_unit_offset=True, sandwich_norm=family != "gemma",
+                mlp_act="gelu_tanh", embedding_multiplier=16.0, tie_word_embeddings=True, rms_norm_eps=1e-6)
+    if family != "gemma":
+        over.update(sliding_window=32, attention_multiplier=D ** -0.5,
+                    layer_types=["sliding_attention", "full_attention", "sliding_attention", "full_attention"])
+    if family == "gemma2":
+        over.update(attn_softcap=20.0, final_softcap=15.0)
+    if family == "gemma3_text":
+        over.update(rope_local_theta=1e4, rope_theta=1e6, rope_scaling={"rope_type": "linear", "factor": 4.0})
+    cfg = C.tiny(family, num_hidden_layers=4, hidden_size=256, intermediate_size=512, num_attention_heads=4,
+                 num_key_value_heads=2, head_dim=D, vocab_size=512, **over)
+    w = random_weights(cfg, 11, dtype=torch.bfloat16)
+    g = torch.Generator().manual_seed(12)
+    for k in list(w):
+        if k.endswith("norm.weight"):  # (1 + w) norms: weights around zero
+            w[k] = (torch.randn(w[k].shape, generator=g) * 0.2).bfloat16()
+    model = DecoderLM(cfg, w, device=cuda)
+    oracle = DecoderOracle(cfg, {k: v.float() for k, v in w.items()})
+    ids = torch.randint(0, 512, (70,), generator=torch.Generator().manual_seed(2)).tolist()
+    lg = _prefill(model, ids, cuda).float().cpu()
+    ref, _ = oracle.forward(torch.tensor(ids))
+    rel = ((lg - ref).norm() / ref.norm()).item()
+    assert rel < 3e-2, rel
+    assert (lg.argmax(-1) == ref.argmax(-1)).float().mean() > 0.85
+    llm = LLM(model, EngineConfig(max_num_seqs=4, max_model_len=256, num_blocks=64))
+    llm.engine.capture_graphs()
+    toks = llm.generate(ids, SamplingParams(max_new_tokens=6, ignore_eos=True))[0].token_ids
+    lg2, _ = oracle.forward(torch.tensor(ids + toks[:-1]))
+    for t, r in zip(toks, lg2[len(ids) - 1:]):
+        assert r[t] >= r.max() - 0.05 * (r.max() - r.min())

@@ -88,7 +88,7 @@ def test_embedding(cuda):
 
 
 @pytest.mark.parametrize("D,Hq,Hkv,rot", [(128, 32, 8, 128), (64, 8, 1, 64), (128, 8, 2, 64), (64, 4, 2, 32),
-                                           (128, 4, 1, 96)])
+                                           (128, 4, 1, 96), (256, 8, 4, 256)])
 def test_qkv_rope_cache_write(cuda, D, Hq, Hkv, rot):
     """QK-norm + RoPE (full, or partial over the first ``rot`` dims) + paged cache write."""
     T = 40
@@ -321,3 +321,48 @@ def test_linear_small_m_epilogues(cuda, M):
     gate = torch.randn(B, N, device=cuda).bfloat16()
     y = ops.linear(x, w, bias=b, residual=res, gate=gate, gate_rows=(0, 1, M))
     assert rel_err(y, res.float() + gate.float() * lin) < 1e-2
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,softcap", [(256, 8, 4, 0.0), (256, 16, 8, 30.0), (128, 16, 8, 20.0),
+                                               (64, 8, 2, 10.0)])
+def test_attention_head256_and_softcap(cuda, D, Hq, Hkv, softcap):
+    """Decode (1 and 3 KV splits) and prefill at head_dim 256 and with logit
+    softcapping (Gemma), against the fp32 reference."""
+    lens = [1, 17, 300, 1029]
+    B = len(lens)
+    tables, kc, vc = _paged_setup(cuda, B, Hkv, D, lens, seed=5)
+    scale = 1 / math.sqrt(D) * 4  # large scores so that the cap matters
+    ctx = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    q = _mk((B, Hq, D), cuda, 1.0, 40)
+    for splits in (1, 3):
+        out = ops.decode_attention(q, kc, vc, tables, ctx, scale=scale, splits=splits, softcap=softcap)
+        ops.check_errors(cuda)
+        for b, l in enumerate(lens):
+            k, v = ref.gather_paged(kc, tables[b], l), ref.gather_paged(vc, tables[b], l)
+            pos = torch.arange(l, device=cuda)
+            r = ref.attention(q[b:b + 1], k, v, pos[-1:], pos, scale, softcap=softcap)
+            assert rel_err(out[b:b + 1], r) < 2e-2, (splits, b, l)
+    qlens = [1, 17, 120, 29]
+    cu = torch.tensor([0] + list(torch.tensor(qlens).cumsum(0)), dtype=torch.int32, device=cuda)
+    qp = _mk((sum(qlens), Hq, D), cuda, 1.0, 41)
+    out = ops.prefill_attention(qp, kc, vc, tables, ctx, cu, max(qlens), scale=scale, softcap=softcap)
+    ops.check_errors(cuda)
+    for b, (ql, l) in enumerate(zip(qlens, lens)):
+        k, v = ref.gather_paged(kc, tables[b], l), ref.gather_paged(vc, tables[b], l)
+        kpos = torch.arange(l, device=cuda)
+        r = ref.attention(qp[cu[b]:cu[b + 1]], k, v, kpos[l - ql:], kpos, scale, softcap=softcap)
+        assert rel_err(out[cu[b]:cu[b + 1]], r) < 2e-2, (b, ql, l)
+
+
+def test_geglu_epilogues(cuda):
+    """GeGLU (GELU tanh form on the gate) in the gated GEMM epilogue (normal and
+    swap-AB) and in the accumulate-path consumer."""
+    H, I = 512, 384
+    wg, wu = _mk((I, H), cuda, 0.05, 42), _mk((I, H), cuda, 0.05, 43)
+    w_gu = ops.interleave_gate_up(wg, wu)
+    for M in (5, 300):
+        x = _mk((M, H), cuda, 1.0, 44)
+        r = torch.nn.functional.gelu(x.float() @ wg.float().t(), approximate="tanh") * (x.float() @ wu.float().t())
+        assert rel_err(ops.linear_swiglu(x, w_gu, act=1), r) < 1e-2
+        if M <= ops.ACC_MAX_M:
+            assert rel_err(ops.swiglu_acc(ops.linear_acc(x, w_gu), act=1), r) < 1e-2
