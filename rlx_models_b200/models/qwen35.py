@@ -1,0 +1,364 @@
+"""Qwen3.5 hybrid decoder (``qwen3_5_text``): Gated DeltaNet linear-attention
+layers interleaved with gated full-attention layers (every
+``full_attention_interval``-th layer, 4 by default).
+
+Gated DeltaNet layer (per value head h, key head h // (Hv / Hk)):
+
+    [q | k | v] = silu(causal_conv1d(in_proj_qkv(x)))      (kernel 4, per channel)
+    q, k        = l2norm(q), l2norm(k);  q *= dk^-1/2
+    g_t         = -exp(A_log) * softplus(in_proj_a(x) + dt_bias)   (log decay)
+    beta_t      = sigmoid(in_proj_b(x))
+    S_t         = exp(g_t) S_{t-1} + k_t u_t^T,
+    u_t         = beta_t (v_t - exp(g_t) S_{t-1}^T k_t)           (delta rule)
+    o_t         = S_t^T q_t
+    y           = out_proj(rmsnorm(o) * w * silu(in_proj_z(x)))
+
+Full-attention layers: q_proj emits [query | gate] per head; QK RMSNorm with
+(1 + w) weights; RoPE on the first quarter of each 256-wide head; the
+attention output is multiplied by sigmoid(gate) before o_proj. All RMSNorms
+except the gated one use (1 + w) weights. For text the three mRoPE position
+axes coincide, so the rotary embedding is the ordinary one.
+
+Prefill uses the chunked form of the recurrence (per chunk of C tokens, with
+G the in-chunk cumulative log decay and D_ij = exp(G_i - G_j) for j <= i):
+
+    A  = strictly-lower (K K^T * D)
+    (I + diag(beta) A) [W_v | W_k] = [beta * V | beta * exp(G) * K]
+    U  = W_v - W_k S0                      (the written values u_t)
+    O  = exp(G) * (Q S0) + lower(Q K^T * D) U
+    S1 = exp(G_C) S0 + (K * exp(G_C - G))^T U
+
+which is the sequential recurrence regrouped (the unit-lower-triangular
+system is solved with ``torch.linalg.solve_triangular``). Decode runs one
+fused sm_100a kernel per layer (``csrc/linear_attn/gdn.cu``): conv1d step,
+l2norm, gates, the delta-rule state update and the gated RMSNorm.
+
+B200 layout: the paged KV cache holds only the full-attention layers; each
+sequence owns a state slot with its conv window (double-buffered by position
+parity so that value heads sharing a key head never race) and its fp32
+recurrent state [Hv, dk, dv]. Prefix caching is off for this family (the
+recurrent state is not per block).
+
+Reference: crates/rlx-qwen35 (Gated DeltaNet + periodic attention + MTP:
+the largest family of the reference); transformers ``qwen3_5`` is the
+numerics oracle on CPU.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+from dataclasses import dataclass, field, fields
+
+import torch
+import torch.nn.functional as F
+
+from ..ops import rope_inv_freq
+from ..runtime.kv_cache import BLOCK_SIZE, PagedKVCache
+
+QWEN35_TYPES = ("qwen3_5_text", "qwen3_5", "qwen3_next")
+
+
+@dataclass
+class Qwen35Config:
+    model_type: str = "qwen3_5_text"
+    vocab_size: int = 248320
+    hidden_size: int = 4096
+    intermediate_size: int = 12288
+    num_hidden_layers: int = 32
+    num_attention_heads: int = 16
+    num_key_value_heads: int = 4
+    head_dim: int = 256
+    rms_norm_eps: float = 1e-6
+    rope_theta: float = 1e7
+    partial_rotary_factor: float = 0.25
+    max_position_embeddings: int = 32768
+    tie_word_embeddings: bool = False
+    attention_bias: bool = False
+    linear_conv_kernel_dim: int = 4
+    linear_key_head_dim: int = 128
+    linear_value_head_dim: int = 128
+    linear_num_key_heads: int = 16
+    linear_num_value_heads: int = 32
+    layer_types: list | None = None
+    bos_token_id: int | None = None
+    eos_token_id: int | list | None = None
+    extra: dict = field(default_factory=dict)
+
+    def __post_init__(self):
+        if self.layer_types is None:
+            self.layer_types = ["full_attention" if (i + 1) % 4 == 0 else "linear_attention"
+                                for i in range(self.num_hidden_layers)]
+
+    @property
+    def key_dim(self) -> int:
+        return self.linear_key_head_dim * self.linear_num_key_heads
+
+    @property
+    def value_dim(self) -> int:
+        return self.linear_value_head_dim * self.linear_num_value_heads
+
+    @property
+    def conv_dim(self) -> int:
+        return 2 * self.key_dim + self.value_dim
+
+    @property
+    def rotary_dim(self) -> int:
+        return int(self.head_dim * self.partial_rotary_factor)
+
+    def is_linear(self, i: int) -> bool:
+        return self.layer_types[i] == "linear_attention"
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "Qwen35Config":
+        d = dict(d)
+        if isinstance(d.get("text_config"), dict):  # the multimodal wrapper: the text model's config
+            d = dict(d["text_config"], model_type=d["text_config"].get("model_type", "qwen3_5_text"))
+        kw = {f.name: d[f.name] for f in fields(cls) if f.name in d and f.name != "extra"}
+        rp = d.get("rope_parameters") or d.get("rope_scaling") or {}
+        if "rope_theta" in rp:
+            kw["rope_theta"] = float(rp["rope_theta"])
+        if "partial_rotary_factor" in rp:
+            kw["partial_rotary_factor"] = float(rp["partial_rotary_factor"])
+        if kw.get("layer_types") is None:
+            n, every = d["num_hidden_layers"], int(d.get("full_attention_interval", 4))
+            kw["layer_types"] = ["full_attention" if (i + 1) % every == 0 else "linear_attention" for i in range(n)]
+        return cls(**kw)
+
+    @classmethod
+    def from_file(cls, path: str) -> "Qwen35Config":
+        with open(os.path.join(path, "config.json") if os.path.isdir(path) else path) as f:
+            return cls.from_dict(json.load(f))
+
+    def to_hf_dict(self) -> dict:
+        d = {f.name: getattr(self, f.name) for f in fields(self) if f.name != "extra"}
+        d["rope_parameters"] = {"rope_type": "default", "rope_theta": self.rope_theta,
+                                "partial_rotary_factor": self.partial_rotary_factor}
+        return d
+
+
+def is_qwen35_config(path: str) -> bool:
+    p = os.path.join(path, "config.json") if os.path.isdir(path) else path
+    try:
+        with open(p) as f:
+            d = json.load(f)
+    except (OSError, ValueError):
+        return False
+    return d.get("model_type") in QWEN35_TYPES and d.get("model_type") != "qwen3_next"
+
+
+# ---------------------------------------------------------------------------
+# shared math
+# ---------------------------------------------------------------------------
+
+def l2norm(x: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    return x * torch.rsqrt((x * x).sum(-1, keepdim=True) + eps)
+
+
+def gdn_gates(a: torch.Tensor, b: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor):
+    """(log decay g, write strength beta), both fp32 [..., Hv]."""
+    g = -A_log.float().exp() * F.softplus(a.float() + dt_bias.float())
+    return g, b.float().sigmoid()
+
+
+def causal_conv1d(x: torch.Tensor, w: torch.Tensor, window: torch.Tensor | None = None):
+    """x [C, L] (one sequence), w [C, K], window [C, K-1] (the inputs before x,
+    oldest first; None = zeros). Returns (silu(conv) [C, L], new window)."""
+    K = w.shape[1]
+    if window is None:
+        window = x.new_zeros(x.shape[0], K - 1)
+    full = torch.cat([window.to(x.dtype), x], 1)
+    y = F.conv1d(full[None].float(), w.float()[:, None, :], groups=x.shape[0])[0]
+    return F.silu(y).to(x.dtype), full[:, -(K - 1):]
+
+
+def gated_delta_recurrent(q, k, v, g, beta, state=None):
+    """Token-by-token gated delta rule. q, k [H, L, dk] (normalised, q scaled),
+    v [H, L, dv], g / beta [H, L]; state [H, dk, dv]. Returns (o [H, L, dv], state)."""
+    H, L, dk = k.shape
+    S = torch.zeros(H, dk, v.shape[-1], dtype=torch.float32, device=v.device) if state is None else state.float()
+    out = []
+    for t in range(L):
+        S = S * g[:, t].exp()[:, None, None]
+        u = beta[:, t, None] * (v[:, t].float() - torch.einsum("hkv,hk->hv", S, k[:, t].float()))
+        S = S + k[:, t].float()[:, :, None] * u[:, None, :]
+        out.append(torch.einsum("hkv,hk->hv", S, q[:, t].float()))
+    return torch.stack(out, 1), S
+
+
+def gated_delta_chunked(q, k, v, g, beta, state=None, chunk: int = 64):
+    """Chunked gated delta rule (same contract as ``gated_delta_recurrent``)."""
+    H, L, dk = k.shape
+    dv = v.shape[-1]
+    dev = v.device
+    S = torch.zeros(H, dk, dv, dtype=torch.float32, device=dev) if state is None else state.float()
+    pad = (-L) % chunk
+    q, k, v = (F.pad(t.float(), (0, 0, 0, pad)) for t in (q, k, v))
+    g, beta = F.pad(g.float(), (0, pad)), F.pad(beta.float(), (0, pad))
+    N = (L + pad) // chunk
+    q, k, v = (t.view(H, N, chunk, -1) for t in (q, k, v))
+    g, beta = g.view(H, N, chunk), beta.view(H, N, chunk)
+    G = g.cumsum(-1)
+    lower = torch.ones(chunk, chunk, dtype=torch.bool, device=dev).tril()
+    D = (G[..., :, None] - G[..., None, :]).masked_fill(~lower, float("-inf")).exp()  # [H, N, C, C]
+    eye = torch.eye(chunk, device=dev)
+    A = (k @ k.transpose(-1, -2)) * D * (1 - eye)
+    M = eye + beta[..., :, None] * A
+    rhs = torch.cat([beta[..., None] * v, (beta * G.exp())[..., None] * k], -1)
+    W = torch.linalg.solve_triangular(M, rhs, upper=False, unitriangular=True)
+    Wv, Wk = W[..., :dv], W[..., dv:]
+    QK = (q @ k.transpose(-1, -2)) * D
+    out = torch.empty(H, N, chunk, dv, dtype=torch.float32, device=dev)
+    for n in range(N):
+        U = Wv[:, n] - Wk[:, n] @ S
+        out[:, n] = G[:, n].exp()[..., None] * (q[:, n] @ S) + QK[:, n] @ U
+        gl = G[:, n, -1]
+        S = gl.exp()[:, None, None] * S + (k[:, n] * (gl[:, None] - G[:, n]).exp()[..., None]).transpose(-1, -2) @ U
+    return out.view(H, N * chunk, dv)[:, :L], S
+
+
+def gated_rmsnorm(o: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """rmsnorm over the last dim (plain weight) times silu(z); fp32."""
+    of = o.float()
+    return of * torch.rsqrt(of.pow(2).mean(-1, keepdim=True) + eps) * w.float() * F.silu(z.float())
+
+
+def _getter(weights):
+    return (lambda n: weights.take(n)) if hasattr(weights, "take") else (lambda n: weights[n])
+
+
+def canonical_weights(weights) -> dict:
+    """Released multimodal checkpoints keep the text model under
+    ``model.language_model.``; map those names to ``model.`` and drop the
+    vision tower and the MTP head."""
+    out = {}
+    for n in list(weights.keys()):
+        if n.startswith(("model.visual.", "mtp.")):
+            continue
+        out[n.replace("model.language_model.", "model.", 1)] = n
+    return out
+
+
+def random_weights(cfg: Qwen35Config, seed: int = 0, device="cpu", dtype=torch.bfloat16) -> dict:
+    gen = torch.Generator(device=device).manual_seed(seed)
+    H = cfg.hidden_size
+    w = {}
+
+    def lin(name, o, i, s=1.0):
+        w[name] = (torch.randn(o, i, generator=gen, device=device) * s / math.sqrt(i)).to(dtype)
+
+    def vec(name, n, s=0.1, base=0.0):
+        w[name] = (base + s * torch.randn(n, generator=gen, device=device)).to(dtype)
+
+    w["model.embed_tokens.weight"] = torch.randn(cfg.vocab_size, H, generator=gen, device=device).to(dtype)
+    vec("model.norm.weight", H)
+    if not cfg.tie_word_embeddings:
+        lin("lm_head.weight", cfg.vocab_size, H)
+    for i in range(cfg.num_hidden_layers):
+        p = f"model.layers.{i}."
+        vec(p + "input_layernorm.weight", H)
+        vec(p + "post_attention_layernorm.weight", H)
+        lin(p + "mlp.gate_proj.weight", cfg.intermediate_size, H)
+        lin(p + "mlp.up_proj.weight", cfg.intermediate_size, H)
+        lin(p + "mlp.down_proj.weight", H, cfg.intermediate_size)
+        if cfg.is_linear(i):
+            a = p + "linear_attn."
+            lin(a + "in_proj_qkv.weight", cfg.conv_dim, H)
+            lin(a + "in_proj_z.weight", cfg.value_dim, H)
+            lin(a + "in_proj_b.weight", cfg.linear_num_value_heads, H)
+            lin(a + "in_proj_a.weight", cfg.linear_num_value_heads, H)
+            w[a + "conv1d.weight"] = (torch.randn(cfg.conv_dim, 1, cfg.linear_conv_kernel_dim, generator=gen,
+                                                  device=device) * 0.5).to(dtype)
+            w[a + "A_log"] = torch.empty(cfg.linear_num_value_heads, device=device).uniform_(
+                0, 16, generator=gen).log().to(dtype)
+            w[a + "dt_bias"] = torch.ones(cfg.linear_num_value_heads, device=device, dtype=dtype)
+            vec(a + "norm.weight", cfg.linear_value_head_dim, base=1.0)
+            lin(a + "out_proj.weight", H, cfg.value_dim)
+        else:
+            a = p + "self_attn."
+            nh, nkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+            lin(a + "q_proj.weight", 2 * nh * D, H)
+            lin(a + "k_proj.weight", nkv * D, H)
+            lin(a + "v_proj.weight", nkv * D, H)
+            lin(a + "o_proj.weight", H, nh * D)
+            vec(a + "q_norm.weight", D)
+            vec(a + "k_norm.weight", D)
+    return w
+
+
+# ---------------------------------------------------------------------------
+# fp32 oracle
+# ---------------------------------------------------------------------------
+
+class Qwen35Oracle:
+    """fp32 full-sequence forward on any device (chunked delta rule)."""
+
+    def __init__(self, cfg: Qwen35Config, weights, device="cpu", chunk: int = 64):
+        self.cfg, self.device, self.chunk = cfg, torch.device(device), chunk
+        names = canonical_weights(weights)
+        g = _getter(weights)
+        self.w = {c: g(n) for c, n in names.items()}
+        self.inv, self.mult = rope_inv_freq(cfg.rotary_dim, cfg.rope_theta, None, cfg.max_position_embeddings)
+
+    def _t(self, n):
+        return self.w[n].to(self.device, torch.float32)
+
+    def _rms(self, x, n, offset=True):
+        w = self._t(n) + (1.0 if offset else 0.0)
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.cfg.rms_norm_eps) * w
+
+    def attention(self, i, x, pos):
+        from ..ops import reference as R
+        c = self.cfg
+        a = f"model.layers.{i}.self_attn."
+        S, nh, nkv, D = x.shape[0], c.num_attention_heads, c.num_key_value_heads, c.head_dim
+        qg = (x @ self._t(a + "q_proj.weight").t()).view(S, nh, 2 * D)
+        q, gate = qg[..., :D], qg[..., D:].reshape(S, nh * D)
+        k = (x @ self._t(a + "k_proj.weight").t()).view(S, nkv, D)
+        v = (x @ self._t(a + "v_proj.weight").t()).view(S, nkv, D)
+        q = R.rope(self._rms(q, a + "q_norm.weight"), pos, self.inv, self.mult)
+        k = R.rope(self._rms(k, a + "k_norm.weight"), pos, self.inv, self.mult)
+        o = R.attention(q, k, v, pos, pos, D ** -0.5, causal=True).reshape(S, nh * D)
+        return (o * gate.sigmoid()) @ self._t(a + "o_proj.weight").t()
+
+    def linear_attention(self, i, x, recurrent: bool = False):
+        c = self.cfg
+        a = f"model.layers.{i}.linear_attn."
+        L = x.shape[0]
+        Hv, Hk, dk, dv = c.linear_num_value_heads, c.linear_num_key_heads, c.linear_key_head_dim, \
+            c.linear_value_head_dim
+        mixed = x @ self._t(a + "in_proj_qkv.weight").t()
+        z = (x @ self._t(a + "in_proj_z.weight").t()).view(L, Hv, dv)
+        gl, beta = gdn_gates(x @ self._t(a + "in_proj_a.weight").t(), x @ self._t(a + "in_proj_b.weight").t(),
+                             self._t(a + "A_log"), self._t(a + "dt_bias"))
+        y, _ = causal_conv1d(mixed.t(), self._t(a + "conv1d.weight")[:, 0])
+        q, k, v = y.t().split([c.key_dim, c.key_dim, c.value_dim], -1)
+        rep = Hv // Hk
+        q = (l2norm(q.reshape(L, Hk, dk)) * dk ** -0.5).repeat_interleave(rep, 1).transpose(0, 1)
+        k = l2norm(k.reshape(L, Hk, dk)).repeat_interleave(rep, 1).transpose(0, 1)
+        v = v.reshape(L, Hv, dv).transpose(0, 1)
+        fn = gated_delta_recurrent if recurrent else (lambda *t: gated_delta_chunked(*t, chunk=self.chunk))
+        o, _ = fn(q, k, v, gl.t(), beta.t())
+        o = gated_rmsnorm(o.transpose(0, 1), z, self._t(a + "norm.weight"), c.rms_norm_eps)
+        return o.reshape(L, Hv * dv) @ self._t(a + "out_proj.weight").t()
+
+    @torch.no_grad()
+    def hidden(self, ids, recurrent: bool = False) -> torch.Tensor:
+        c = self.cfg
+        ids = torch.as_tensor(ids, device=self.device).long()
+        pos = torch.arange(ids.shape[0], device=self.device)
+        h = self._t("model.embed_tokens.weight")[ids]
+        for i in range(c.num_hidden_layers):
+            p = f"model.layers.{i}."
+            x = self._rms(h, p + "input_layernorm.weight")
+            h = h + (self.linear_attention(i, x, recurrent) if c.is_linear(i) else self.attention(i, x, pos))
+            x = self._rms(h, p + "post_attention_layernorm.weight")
+            m = p + "mlp."
+            h = h + (F.silu(x @ self._t(m + "gate_proj.weight").t()) * (x @ self._t(m + "up_proj.weight").t())) \
+                @ self._t(m + "down_proj.weight").t()
+        return self._rms(h, "model.norm.weight")
+
+    @torch.no_grad()
+    def logits(self, ids, recurrent: bool = False) -> torch.Tensor:
+        head = "model.embed_tokens.weight" if self.cfg.tie_word_embeddings else "lm_head.weight"
+        return self.hidden(ids, recurrent) @ self._t(head).t()
