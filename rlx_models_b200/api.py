@@ -186,8 +186,11 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
         cfg = config or weights.config
     elif path is not None:
         from .models.deepseek import DeepseekConfig, is_deepseek_config
+        from .models.qwen35 import Qwen35Config, is_qwen35_config
         if config is None and is_deepseek_config(path):  # MLA + DeepSeekMoE family
             config = DeepseekConfig.from_file(path)
+        elif config is None and is_qwen35_config(path):  # Gated DeltaNet hybrid
+            config = Qwen35Config.from_file(path)
         cfg = config or C.DecoderConfig.from_file(path)
         from .weights.mlx import MLXWeights
         if MLXWeights.is_mlx_dir(path):  # MLX affine group-quantised checkpoint

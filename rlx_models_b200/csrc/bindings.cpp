@@ -99,6 +99,59 @@ void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const o
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void gdn_decode(const Tensor& proj, const Tensor& conv_w, const Tensor& A_log, const Tensor& dt_bias,
+                const Tensor& norm_w, Tensor& conv_state, Tensor& rec_state, const Tensor& seq_slots,
+                const Tensor& positions, Tensor& out, int64_t Hk, int64_t Hv, int64_t D, double eps) {
+  check_cuda(proj, "proj");
+  const int64_t B = proj.size(0);
+  TORCH_CHECK(proj.scalar_type() == at::kBFloat16 && proj.dim() == 2 && proj.stride(1) == 1, "b200.gdn_decode: proj");
+  TORCH_CHECK(conv_w.scalar_type() == at::kFloat && conv_w.is_contiguous() && conv_w.dim() == 2, "b200.gdn_decode: conv_w");
+  const int64_t conv_dim = conv_w.size(0), K = conv_w.size(1);
+  const int64_t key_dim = Hk * D, value_dim = Hv * D;
+  TORCH_CHECK(conv_dim == 2 * key_dim + value_dim, "b200.gdn_decode: conv_dim != 2 key_dim + value_dim");
+  TORCH_CHECK(proj.size(1) >= conv_dim + value_dim + 2 * Hv, "b200.gdn_decode: proj width");
+  TORCH_CHECK(A_log.scalar_type() == at::kFloat && A_log.numel() == Hv && dt_bias.scalar_type() == at::kFloat &&
+                  dt_bias.numel() == Hv && norm_w.scalar_type() == at::kFloat && norm_w.numel() == D,
+              "b200.gdn_decode: A_log / dt_bias / norm_w fp32");
+  TORCH_CHECK(conv_state.scalar_type() == at::kBFloat16 && conv_state.is_contiguous() && conv_state.dim() == 4 &&
+                  conv_state.size(1) == 2 && conv_state.size(2) == conv_dim && conv_state.size(3) == K - 1,
+              "b200.gdn_decode: conv_state [slots, 2, conv_dim, K-1] bf16");
+  TORCH_CHECK(rec_state.scalar_type() == at::kFloat && rec_state.is_contiguous() && rec_state.dim() == 4 &&
+                  rec_state.size(0) == conv_state.size(0) && rec_state.size(1) == Hv && rec_state.size(2) == D &&
+                  rec_state.size(3) == D,
+              "b200.gdn_decode: rec_state [slots, Hv, D, D] fp32");
+  TORCH_CHECK(seq_slots.scalar_type() == at::kInt && seq_slots.numel() == B && positions.scalar_type() == at::kInt &&
+                  positions.numel() == B,
+              "b200.gdn_decode: seq_slots / positions int32 [B]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == B * value_dim,
+              "b200.gdn_decode: out [B, Hv*D] bf16");
+  c10::cuda::CUDAGuard g(proj.device());
+  b200::GdnDecodeArgs a{};
+  a.proj = reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr());
+  a.ld = proj.stride(0);
+  a.conv_w = conv_w.data_ptr<float>();
+  a.A_log = A_log.data_ptr<float>();
+  a.dt_bias = dt_bias.data_ptr<float>();
+  a.norm_w = norm_w.data_ptr<float>();
+  a.conv_state = reinterpret_cast<__nv_bfloat16*>(conv_state.data_ptr());
+  a.rec_state = rec_state.data_ptr<float>();
+  a.seq_slots = seq_slots.data_ptr<int32_t>();
+  a.positions = positions.data_ptr<int32_t>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.B = (int)B;
+  a.Hk = (int)Hk;
+  a.Hv = (int)Hv;
+  a.D = (int)D;
+  a.K = (int)K;
+  a.conv_dim = (int)conv_dim;
+  a.key_dim = (int)key_dim;
+  a.value_dim = (int)value_dim;
+  a.num_slots = conv_state.size(0);
+  a.eps = (float)eps;
+  b200::gdn_decode_launch(a, cur_stream(proj));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void embedding(const Tensor& ids, const Tensor& table, Tensor& out) {
   check_cuda(ids, "ids");
   TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "b200.embedding: int32 ids");
@@ -898,6 +951,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("act_from") = -1, py::arg("gate") = py::none(), py::arg("gate_split") = 0, py::arg("gate_r1") = 1,
         py::arg("gate_r2") = 1, py::arg("gate_off") = 0, py::arg("glu_act") = 0);
   m.def("gemm", &gemm);
+  m.def("gdn_decode", &gdn_decode);
   m.def("gemm_push_shards", &gemm_push_shards);
   m.def("shard_push_add", &shard_push_add);
   m.def("peer_barrier", &peer_barrier);

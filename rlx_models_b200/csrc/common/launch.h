@@ -3,6 +3,7 @@
 // torch bindings in bindings.cpp validate tensors and fill these structs.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -233,6 +234,26 @@ void prefill_attention_launch(const AttnArgs& a, cudaStream_t st);
 // prefill_attention_launch when supported (B200_ATTN_LEGACY=1 forces the mma.sync kernel)
 bool fmha_supported(const AttnArgs& a);
 void fmha_launch(const AttnArgs& a, cudaStream_t st);
+
+// ---------------- linear attention (Gated DeltaNet) ----------------
+struct GdnDecodeArgs {
+  const __nv_bfloat16* proj;  // [B, ld]: [q k v conv inputs (conv_dim) | z (Hv*D) | b (Hv) | a (Hv)]
+  int64_t ld;
+  const float* conv_w;        // [conv_dim, K]
+  const float* A_log;         // [Hv]
+  const float* dt_bias;       // [Hv]
+  const float* norm_w;        // [D]
+  __nv_bfloat16* conv_state;  // [num_slots, 2, conv_dim, K-1] (window before the token, by position parity)
+  float* rec_state;           // [num_slots, Hv, D, D]
+  const int32_t* seq_slots;   // [B] state slot per row (out of range: padding row)
+  const int32_t* positions;   // [B]
+  __nv_bfloat16* out;         // [B, Hv*D]
+  int B, Hk, Hv, D, K;
+  int conv_dim, key_dim, value_dim;
+  int64_t num_slots;
+  float eps;
+};
+void gdn_decode_launch(const GdnDecodeArgs& a, cudaStream_t st);
 
 // ---------------- training ----------------
 void adamw_launch(float* master, const void* grad, bool grad_f32, float* m, float* v, void* param_out, int64_t n,

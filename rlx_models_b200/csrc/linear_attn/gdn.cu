@@ -1,0 +1,139 @@
+// Gated DeltaNet decode step (Qwen3.5 linear-attention layers), one fused
+// kernel per layer and step:
+//
+//   conv1d step over the q / k / v channels (window of K-1 inputs per
+//   channel, double-buffered by position parity), SiLU, l2norm of q and k,
+//   q *= dk^-1/2, log decay g = -exp(A_log) * softplus(a + dt_bias),
+//   beta = sigmoid(b), the delta-rule update of the fp32 state
+//   S <- exp(g) S + k u^T with u = beta (v - exp(g) S^T k), o = S^T q, and the
+//   gated RMSNorm rmsnorm(o) * w * silu(z) that feeds out_proj.
+//
+// Grid (B, Hv), one CTA per (sequence, value head), DV threads: thread t owns
+// state column t (DK fp32 values kept in registers across the update), so the
+// state streams through HBM once per step (read + write of DK x DV fp32).
+// Value heads that share a key head compute the same q / k conv outputs; only
+// the first of them advances the q / k conv windows, and it writes them to the
+// other parity buffer, so the readers of this step never see a half-updated
+// window.
+//
+// Reference behaviour: transformers qwen3_5 Qwen3_5GatedDeltaNet (recurrent
+// path) and the family in crates/rlx-qwen35.
+#include <cuda_bf16.h>
+
+#include <cstdint>
+#include <stdexcept>
+
+#include "../common/b200.cuh"
+#include "../common/launch.h"
+#include "../common/pdl_launch.h"
+
+namespace b200 {
+namespace gdn {
+
+constexpr int kMaxK = 8;
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();  // red reuse across calls
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) s += red[i];
+  return s;
+}
+
+__device__ __forceinline__ float bf(const __nv_bfloat16 x) { return __bfloat162float(x); }
+__device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16(x)); }
+__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+
+// One conv1d step of channel c: window (K-1 previous inputs) + the new input.
+__device__ __forceinline__ float conv_step(const GdnDecodeArgs& a, const __nv_bfloat16* row, int64_t slot, int par,
+                                           int c, bool advance) {
+  const int W = a.K - 1;
+  const __nv_bfloat16* win = a.conv_state + ((slot * 2 + par) * a.conv_dim + c) * W;
+  __nv_bfloat16* nxt = a.conv_state + ((slot * 2 + (par ^ 1)) * a.conv_dim + c) * W;
+  float xs[kMaxK];
+#pragma unroll
+  for (int i = 0; i < kMaxK; ++i) xs[i] = 0.f;
+  for (int i = 0; i < W; ++i) xs[i] = bf(win[i]);
+  xs[W] = bf(row[c]);
+  float acc = 0.f;
+  for (int i = 0; i <= W; ++i) acc += a.conv_w[(int64_t)c * a.K + i] * xs[i];
+  if (advance)
+    for (int i = 0; i < W; ++i) nxt[i] = __float2bfloat16(xs[i + 1]);
+  return rbf(silu(acc));  // the conv output is a bf16 activation
+}
+
+template <int D>
+__global__ void __launch_bounds__(D) gdn_decode_kernel(GdnDecodeArgs a) {
+  __shared__ float qs[D], ks[D];
+  __shared__ float red[D / 32];
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x, hv = blockIdx.y, t = threadIdx.x;
+  const int64_t slot = a.seq_slots[b];
+  __nv_bfloat16* out = a.out + ((int64_t)b * a.Hv + hv) * D + t;
+  if (slot < 0 || slot >= a.num_slots) {  // a padding row without a state slot
+    *out = __float2bfloat16(0.f);
+    return;
+  }
+  const int par = a.positions[b] & 1;
+  const int rep = a.Hv / a.Hk;
+  const int kh = hv / rep;
+  const bool owner = (hv % rep) == 0;
+  const __nv_bfloat16* row = a.proj + (int64_t)b * a.ld;
+
+  float q = conv_step(a, row, slot, par, kh * D + t, owner);
+  float k = conv_step(a, row, slot, par, a.key_dim + kh * D + t, owner);
+  const float v = conv_step(a, row, slot, par, 2 * a.key_dim + hv * D + t, true);
+  const float qn = rsqrtf(block_sum<D>(q * q, red) + 1e-6f);
+  const float kn = rsqrtf(block_sum<D>(k * k, red) + 1e-6f);
+  qs[t] = q * qn * rsqrtf((float)D);
+  ks[t] = k * kn;
+  const float zb = bf(row[a.conv_dim + hv * D + t]);
+  const float bb = bf(row[a.conv_dim + a.value_dim + hv]);
+  const float ab = bf(row[a.conv_dim + a.value_dim + a.Hv + hv]);
+  const float xa = ab + a.dt_bias[hv];
+  const float softplus = xa > 20.f ? xa : log1pf(__expf(xa));
+  const float decay = __expf(-__expf(a.A_log[hv]) * softplus);
+  const float beta = 1.f / (1.f + __expf(-bb));
+  __syncthreads();
+
+  float* S = a.rec_state + ((slot * a.Hv + hv) * (int64_t)D) * D + t;  // column t of [D, D]
+  float s[D];
+  float kv = 0.f;
+#pragma unroll
+  for (int i = 0; i < D; ++i) {
+    s[i] = S[(int64_t)i * D] * decay;
+    kv += s[i] * ks[i];
+  }
+  const float u = beta * (v - kv);
+  float o = 0.f;
+#pragma unroll
+  for (int i = 0; i < D; ++i) {
+    s[i] += ks[i] * u;
+    o += s[i] * qs[i];
+    S[(int64_t)i * D] = s[i];
+  }
+  o = rbf(o);
+  const float inv = rsqrtf(block_sum<D>(o * o, red) / (float)D + a.eps);
+  *out = __float2bfloat16(rbf(o * inv) * a.norm_w[t] * silu(zb));
+}
+
+}  // namespace gdn
+
+void gdn_decode_launch(const GdnDecodeArgs& a, cudaStream_t st) {
+  if (a.B == 0) return;
+  if (a.K < 2 || a.K > gdn::kMaxK) throw std::runtime_error("b200.gdn_decode: conv kernel 2..8");
+  if (a.Hv % a.Hk != 0) throw std::runtime_error("b200.gdn_decode: value heads must be a multiple of key heads");
+  dim3 grid(a.B, a.Hv);
+  if (a.D == 128) launch_pdl(gdn::gdn_decode_kernel<128>, grid, dim3(128), 0, st, a);
+  else if (a.D == 64) launch_pdl(gdn::gdn_decode_kernel<64>, grid, dim3(64), 0, st, a);
+  else throw std::runtime_error("b200.gdn_decode: head dims 64 or 128 (key == value)");
+}
+
+}  // namespace b200

@@ -342,6 +342,14 @@ class Scheduler {
     return d;
   }
 
+  // Ids of every sequence in the last schedule() batch, in batch order
+  // (decode rows first, then prefill chunks): per-sequence state slots key on these.
+  std::vector<int64_t> step_seq_ids() const {
+    std::vector<int64_t> ids(step_decode_);
+    ids.insert(ids.end(), step_prefill_.begin(), step_prefill_.end());
+    return ids;
+  }
+
   // Append sampled tokens (one per logit row, in schedule() order). Returns
   // the ids of sequences that finished in this update.
   std::vector<int64_t> update(const std::vector<int64_t>& seq_ids, const std::vector<int32_t>& toks, int32_t eos) {
@@ -476,6 +484,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("num_running", &Scheduler::num_running)
       .def("num_free_blocks", &Scheduler::num_free_blocks)
       .def("schedule", &Scheduler::schedule)
+      .def("step_seq_ids", &Scheduler::step_seq_ids)
       .def("update", &Scheduler::update)
       .def("output_tokens", &Scheduler::output_tokens)
       .def("finish_reason", &Scheduler::finish_reason)

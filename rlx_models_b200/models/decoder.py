@@ -45,6 +45,7 @@ class ForwardBatch:
     pre_cu_q: torch.Tensor | None = None          # [Bp + 1] int32 offsets into the prefill tokens
     pre_max_q: int = 0
     logit_rows: torch.Tensor | None = None        # [R] int64 rows needing logits
+    seq_slots: torch.Tensor | None = None         # [Bd + Bp] int32 state slot per sequence (stateful models)
 
     @property
     def num_tokens(self) -> int:

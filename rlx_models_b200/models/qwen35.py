@@ -362,3 +362,202 @@ class Qwen35Oracle:
     def logits(self, ids, recurrent: bool = False) -> torch.Tensor:
         head = "model.embed_tokens.weight" if self.cfg.tie_word_embeddings else "lm_head.weight"
         return self.hidden(ids, recurrent) @ self._t(head).t()
+
+
+# ---------------------------------------------------------------------------
+# GPU model (engine interface)
+# ---------------------------------------------------------------------------
+
+class HybridCache:
+    """Paged KV for the full-attention layers plus per-sequence linear-attention
+    state: conv windows [n_lin, slots, 2 (position parity), conv_dim, K-1] bf16
+    and recurrent states [n_lin, slots, Hv, dk, dv] fp32."""
+
+    def __init__(self, cfg: Qwen35Config, num_blocks: int, num_slots: int, device):
+        n_full = sum(not cfg.is_linear(i) for i in range(cfg.num_hidden_layers))
+        n_lin = cfg.num_hidden_layers - n_full
+        self.paged = PagedKVCache(max(1, n_full), num_blocks, cfg.num_key_value_heads, cfg.head_dim, device)
+        self.k, self.v = self.paged.k, self.paged.v
+        self.num_slots = num_slots
+        self.conv = torch.zeros(n_lin, num_slots, 2, cfg.conv_dim, cfg.linear_conv_kernel_dim - 1,
+                                dtype=torch.bfloat16, device=device)
+        self.rec = torch.zeros(n_lin, num_slots, cfg.linear_num_value_heads, cfg.linear_key_head_dim,
+                               cfg.linear_value_head_dim, dtype=torch.float32, device=device)
+
+    def layer(self, i: int):
+        return self.paged.layer(i)
+
+
+class _Layer:
+    __slots__ = ("ln1", "ln2", "w_gu", "wd", "wo", "linear", "idx",
+                 "w_qkvg", "q_norm", "k_norm",
+                 "w_in", "conv_w", "A_log", "dt_bias", "norm_w")
+
+
+class Qwen35LM:
+    """Qwen3.5 hybrid decoder on the sm_100a kernels, driven by ``LLMEngine``."""
+
+    stateful = True
+
+    def __init__(self, cfg: Qwen35Config, weights, device="cuda"):
+        from .. import ops
+        self.cfg, self.device = cfg, torch.device(device)
+        c, dev, bf = cfg, self.device, torch.bfloat16
+        if c.linear_key_head_dim != c.linear_value_head_dim:
+            raise NotImplementedError("Gated DeltaNet decode kernel needs key head dim == value head dim")
+        self.hkv, self.D = c.num_key_value_heads, c.head_dim
+        self.scale = c.head_dim ** -0.5
+        inv, self.rope_mult = rope_inv_freq(c.rotary_dim, c.rope_theta, None, c.max_position_embeddings)
+        self.inv_freq = inv.to(dev)
+        names = canonical_weights(weights)
+        raw = _getter(weights)
+
+        def g(n):
+            return raw(names[n]).to(dev)
+
+        def dv(t):
+            return t.to(dev, bf).contiguous()
+
+        def dvn(t):  # (1 + w) RMSNorm weights
+            return dv(t.float() + 1.0)
+
+        self.embed = dv(g("model.embed_tokens.weight"))
+        self.norm = dvn(g("model.norm.weight"))
+        self.lm_head = self.embed if c.tie_word_embeddings else dv(g("lm_head.weight"))
+        nh, nkv, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
+        self.layers = []
+        n_full = n_lin = 0
+        for i in range(c.num_hidden_layers):
+            p = f"model.layers.{i}."
+            L = _Layer()
+            L.ln1, L.ln2 = dvn(g(p + "input_layernorm.weight")), dvn(g(p + "post_attention_layernorm.weight"))
+            L.w_gu = dv(ops.interleave_gate_up(g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")))
+            L.wd = dv(g(p + "mlp.down_proj.weight"))
+            L.linear = c.is_linear(i)
+            if L.linear:
+                a = p + "linear_attn."
+                L.idx, n_lin = n_lin, n_lin + 1
+                L.w_in = dv(torch.cat([g(a + "in_proj_qkv.weight"), g(a + "in_proj_z.weight"),
+                                       g(a + "in_proj_b.weight"), g(a + "in_proj_a.weight")], 0))
+                L.conv_w = g(a + "conv1d.weight").float().reshape(c.conv_dim, -1).contiguous()
+                L.A_log = g(a + "A_log").float().contiguous()
+                L.dt_bias = g(a + "dt_bias").float().contiguous()
+                L.norm_w = g(a + "norm.weight").float().contiguous()
+                L.wo = dv(g(a + "out_proj.weight"))
+            else:
+                a = p + "self_attn."
+                L.idx, n_full = n_full, n_full + 1
+                qg = g(a + "q_proj.weight").view(nh, 2, D, -1)  # per head: [query rows | gate rows]
+                L.w_qkvg = dv(torch.cat([qg[:, 0].reshape(nh * D, -1), g(a + "k_proj.weight"),
+                                         g(a + "v_proj.weight"), qg[:, 1].reshape(nh * D, -1)], 0))
+                L.q_norm, L.k_norm = dvn(g(a + "q_norm.weight")), dvn(g(a + "k_norm.weight"))
+                L.wo = dv(g(a + "o_proj.weight"))
+            self.layers.append(L)
+        self.n_full = n_full
+
+    # -- engine interface -------------------------------------------------------
+    def make_kv_cache(self, num_blocks: int, num_slots: int = 8) -> HybridCache:
+        return HybridCache(self.cfg, num_blocks, num_slots, self.device)
+
+    def kv_bytes_per_block(self) -> int:
+        return 2 * max(1, self.n_full) * self.hkv * BLOCK_SIZE * self.D * 2
+
+    def logits(self, x: torch.Tensor) -> torch.Tensor:
+        from .. import ops
+        return ops.linear(x, self.lm_head, out_dtype=torch.float32)
+
+    def forward(self, fb, kv: HybridCache) -> torch.Tensor:
+        x = self.forward_hidden(fb, kv)
+        if fb.logit_rows is not None:
+            x = x.index_select(0, fb.logit_rows)
+        return self.logits(x)
+
+    # -- layers ----------------------------------------------------------------
+    def _attention(self, L: _Layer, x: torch.Tensor, fb, kv: HybridCache) -> torch.Tensor:
+        from .. import ops
+        c = self.cfg
+        T = x.shape[0]
+        nh, nkv, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
+        qkvg = ops.linear(x, L.w_qkvg)
+        w_qkv = (nh + 2 * nkv) * D
+        kc, vc = kv.layer(L.idx)
+        q = ops.qkv_rope(qkvg[:, :w_qkv], num_q_heads=nh, num_kv_heads=nkv, head_dim=D, positions=fb.positions,
+                         inv_freq=self.inv_freq, rope_scale=self.rope_mult, q_norm=L.q_norm, k_norm=L.k_norm,
+                         eps=c.rms_norm_eps, slots=fb.slots, k_cache=kc, v_cache=vc, rot_dim=c.rotary_dim)
+        o = torch.empty_like(q)
+        nd = fb.num_decode
+        if nd > 0:
+            ops.decode_attention(q[:nd], kc, vc, fb.dec_block_tables, fb.dec_ctx_lens, scale=self.scale, out=o[:nd])
+        if T > nd:
+            ops.prefill_attention(q[nd:], kc, vc, fb.pre_block_tables, fb.pre_ctx_lens, fb.pre_cu_q, fb.pre_max_q,
+                                  scale=self.scale, out=o[nd:])
+        return (o.view(T, nh * D).float() * qkvg[:, w_qkv:].float().sigmoid()).to(torch.bfloat16)
+
+    def _gdn(self, L: _Layer, x: torch.Tensor, fb, kv: HybridCache, slots: torch.Tensor) -> torch.Tensor:
+        from .. import ops
+        from ..ops._ext import ext
+        c = self.cfg
+        T = x.shape[0]
+        p = ops.linear(x, L.w_in)  # [T, conv_dim | z | b | a]
+        out = torch.empty(T, c.value_dim, dtype=torch.bfloat16, device=x.device)
+        nd = fb.num_decode
+        if nd > 0:
+            ext().gdn_decode(p[:nd], L.conv_w, L.A_log, L.dt_bias, L.norm_w, kv.conv[L.idx], kv.rec[L.idx],
+                             slots[:nd], fb.positions[:nd], out[:nd], c.linear_num_key_heads,
+                             c.linear_num_value_heads, c.linear_value_head_dim, c.rms_norm_eps)
+            ops._count(1)
+        if T > nd:
+            self._gdn_prefill(L, p[nd:], fb, kv, slots[nd:], out[nd:])
+        return out
+
+    def _gdn_prefill(self, L: _Layer, p: torch.Tensor, fb, kv: HybridCache, slots: torch.Tensor, out: torch.Tensor):
+        """Chunked delta rule per prefill sequence; a chunk that starts at
+        position 0 starts from zero state, later chunks continue the slot's."""
+        c = self.cfg
+        Hv, Hk, dk, dv = c.linear_num_value_heads, c.linear_num_key_heads, c.linear_key_head_dim, \
+            c.linear_value_head_dim
+        C, vd = c.conv_dim, c.value_dim
+        cu, ctx, sl = fb.pre_cu_q.tolist(), fb.pre_ctx_lens.tolist(), slots.tolist()
+        rep = Hv // Hk
+        for s, n_ctx in enumerate(ctx):
+            a, b = cu[s], cu[s + 1]
+            n = b - a
+            start, slot = n_ctx - n, sl[s]
+            rows = p[a:b]
+            win = kv.conv[L.idx, slot, start & 1] if start > 0 else None
+            y, new_win = causal_conv1d(rows[:, :C].t(), L.conv_w, win)
+            kv.conv[L.idx, slot, (start + n) & 1] = new_win
+            q, k, v = y.t().split([c.key_dim, c.key_dim, vd], -1)
+            q = (l2norm(q.float().reshape(n, Hk, dk)) * dk ** -0.5).repeat_interleave(rep, 1).transpose(0, 1)
+            k = l2norm(k.float().reshape(n, Hk, dk)).repeat_interleave(rep, 1).transpose(0, 1)
+            v = v.float().reshape(n, Hv, dv).transpose(0, 1)
+            gl, beta = gdn_gates(rows[:, C + vd + Hv:C + vd + 2 * Hv], rows[:, C + vd:C + vd + Hv], L.A_log,
+                                 L.dt_bias)
+            state = kv.rec[L.idx, slot] if start > 0 else None
+            o, S = gated_delta_chunked(q, k, v, gl.t(), beta.t(), state)
+            kv.rec[L.idx, slot] = S
+            o = o.transpose(0, 1).to(torch.bfloat16)
+            z = rows[:, C:C + vd].reshape(n, Hv, dv)
+            out[a:b] = gated_rmsnorm(o, z, L.norm_w, c.rms_norm_eps).reshape(n, vd).to(torch.bfloat16)
+
+    def forward_hidden(self, fb, kv: HybridCache) -> torch.Tensor:
+        from .. import ops
+        from .decoder import LocalComm
+        c = self.cfg
+        comm = LocalComm(c.rms_norm_eps)
+        slots = fb.seq_slots
+        if slots is None:  # direct calls (LLM.logits): sequence i uses slot i
+            nseq = fb.num_decode + (0 if fb.pre_ctx_lens is None else fb.pre_ctx_lens.shape[0])
+            slots = torch.arange(nseq, dtype=torch.int32, device=self.device)
+        h = ops.embedding(fb.input_ids, self.embed)
+        x = ops.rmsnorm(h, self.layers[0].ln1, c.rms_norm_eps)
+        n = len(self.layers)
+        for i, L in enumerate(self.layers):
+            a = self._gdn(L, x, fb, kv, slots) if L.linear else self._attention(L, x, fb, kv)
+            x = comm.rowpar_add_norm(a, L.wo, h, L.ln2)
+            if x.shape[0] <= ops.ACC_MAX_M:
+                gu = ops.swiglu_acc(ops.linear_acc(x, L.w_gu))
+            else:
+                gu = ops.linear_swiglu(x, L.w_gu)
+            x = comm.rowpar_add_norm(gu, L.wd, h, self.layers[i + 1].ln1 if i + 1 < n else self.norm)
+        return x

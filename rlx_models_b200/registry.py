@@ -70,12 +70,23 @@ def _deepseek(cfg, weights, device, tp_rank, tp_size, comm):
     return DeepseekLM(cfg, weights, device=device)
 
 
+@register("qwen3_5_text", "qwen3_5")
+def _qwen35(cfg, weights, device, tp_rank, tp_size, comm):
+    from .models.qwen35 import Qwen35LM
+    if tp_size != 1:
+        raise NotImplementedError("Qwen3.5 hybrid models run on one GPU per replica")
+    return Qwen35LM(cfg, weights, device=device)
+
+
 def build_model(cfg: DecoderConfig, weights=None, *, device="cuda", tp_rank=0, tp_size=1, comm=None, seed=0):
     fn = _BUILDERS.get(cfg.model_type)
     if fn is None:
         raise KeyError(f"no builder for model_type={cfg.model_type!r}; registered: {registered()}")
     if weights is None and cfg.model_type in ("deepseek_v3", "deepseek_v2", "kimi_k2"):
         from .models.deepseek import random_weights
+        weights = random_weights(cfg, seed, device)
+    elif weights is None and cfg.model_type in ("qwen3_5_text", "qwen3_5"):
+        from .models.qwen35 import random_weights
         weights = random_weights(cfg, seed, device)
     elif weights is None:
         weights = RandomWeights(cfg, seed, device)

@@ -19,6 +19,8 @@ norm/RoPE, sampling) except for small torch copies/index ops.
 """
 from __future__ import annotations
 
+import dataclasses
+
 import time
 from dataclasses import dataclass, field
 
@@ -139,7 +141,16 @@ class LLMEngine:
             per = (model.kv_bytes_per_block() if hasattr(model, "kv_bytes_per_block")
                    else 2 * mc.num_hidden_layers * model.hkv * BLOCK_SIZE * model.D * 2)
             nb = max(self.max_blocks_per_seq + 1, int(cfg.kv_memory_gb * (1 << 30)) // per)
-        self.kv = model.make_kv_cache(nb + 1)
+        self.stateful = bool(getattr(model, "stateful", False))
+        if self.stateful:
+            # recurrent per-sequence state (hybrid linear-attention models): one slot per
+            # running sequence; a cached KV prefix would not restore that state
+            cfg = self.cfg = dataclasses.replace(cfg, prefix_caching=False)
+            self.kv = model.make_kv_cache(nb + 1, num_slots=cfg.max_num_seqs)
+            self.free_slots = list(range(cfg.max_num_seqs - 1, -1, -1))
+            self.slot_of: dict[int, int] = {}
+        else:
+            self.kv = model.make_kv_cache(nb + 1)
         self.dummy_block = nb  # never handed out by the scheduler; padding rows write here
         self.sched = _runtime.Scheduler(nb, cfg.max_num_seqs, cfg.max_batched_tokens, self.max_blocks_per_seq,
                                         cfg.prefix_caching, cfg.chunk_size)
@@ -151,7 +162,8 @@ class LLMEngine:
             slots=torch.zeros(T, dtype=i64, **pin), dec_tables=torch.zeros(S, W, dtype=i32, **pin),
             dec_ctx=torch.zeros(S, dtype=i32, **pin), pre_tables=torch.zeros(S, W, dtype=i32, **pin),
             pre_ctx=torch.zeros(S, dtype=i32, **pin), pre_cu=torch.zeros(S + 1, dtype=i32, **pin),
-            logit_rows=torch.zeros(T, dtype=i64, **pin), sample_ids=torch.zeros(T, dtype=i64, **pin))
+            logit_rows=torch.zeros(T, dtype=i64, **pin), sample_ids=torch.zeros(T, dtype=i64, **pin),
+            seq_slots=torch.full((S,), -1, dtype=i32, **pin))
         dev = self.device
         self.d = {k: torch.zeros_like(v, device=dev) for k, v in self.h.items() if k != "sample_ids"}
         # per-row sampling parameters (host pinned -> device)
@@ -184,6 +196,22 @@ class LLMEngine:
     def abort(self, sid: int):
         self.sched.abort(sid)
         self.requests.pop(sid, None)
+        self._free_slot(sid)
+
+    def _free_slot(self, sid: int):
+        if self.stateful and sid in self.slot_of:
+            self.free_slots.append(self.slot_of.pop(sid))
+
+    def _assign_slots(self) -> int:
+        """State slot of every sequence of the step (batch order) into the staging buffer."""
+        ids = self.sched.step_seq_ids()
+        hs = self.h["seq_slots"]
+        for i, sid in enumerate(ids):
+            slot = self.slot_of.get(sid)
+            if slot is None:
+                slot = self.slot_of[sid] = self.free_slots.pop()
+            hs[i] = slot
+        return len(ids)
 
     def has_unfinished(self) -> bool:
         return self.sched.has_work()
@@ -265,13 +293,15 @@ class LLMEngine:
     def _eager_forward(self, T: int, nd: int, npf: int, max_q: int, R: int) -> torch.Tensor:
         d = self.d
         self._copy_in(dict(input_ids=T, positions=T, slots=T, dec_tables=nd, dec_ctx=nd, pre_tables=npf,
-                           pre_ctx=npf, pre_cu=npf + 1 if npf else 0, logit_rows=R))
+                           pre_ctx=npf, pre_cu=npf + 1 if npf else 0, logit_rows=R,
+                           seq_slots=nd + npf if self.stateful else 0))
         fb = ForwardBatch(
             input_ids=d["input_ids"][:T], positions=d["positions"][:T], slots=d["slots"][:T], num_decode=nd,
             dec_block_tables=d["dec_tables"][:nd] if nd else None, dec_ctx_lens=d["dec_ctx"][:nd] if nd else None,
             pre_block_tables=d["pre_tables"][:npf] if npf else None,
             pre_ctx_lens=d["pre_ctx"][:npf] if npf else None, pre_cu_q=d["pre_cu"][:npf + 1] if npf else None,
-            pre_max_q=max_q, logit_rows=d["logit_rows"][:R])
+            pre_max_q=max_q, logit_rows=d["logit_rows"][:R],
+            seq_slots=d["seq_slots"][:nd + npf] if self.stateful else None)
         return self.model.forward(fb, self.kv)
 
     def _bucket(self, n: int) -> int | None:
@@ -288,12 +318,13 @@ class LLMEngine:
         h["slots"][nd:B] = db * BLOCK_SIZE
         h["dec_tables"][nd:B] = db
         h["dec_ctx"][nd:B] = 1
+        h["seq_slots"][nd:B] = -1  # no state slot: the recurrent kernels skip these rows
 
     def _capture(self, B: int, greedy: bool):
         d = self.d
         fb = ForwardBatch(input_ids=d["input_ids"][:B], positions=d["positions"][:B], slots=d["slots"][:B],
                           num_decode=B, dec_block_tables=d["dec_tables"][:B], dec_ctx_lens=d["dec_ctx"][:B],
-                          logit_rows=None)
+                          logit_rows=None, seq_slots=d["seq_slots"][:B] if self.stateful else None)
         # warm up (allocations, kernel attributes) outside the graph on dummy
         # rows written straight into the device buffers: the host staging
         # buffers may already hold the step being scheduled.
@@ -303,6 +334,7 @@ class LLMEngine:
         d["slots"][:B].fill_(db * BLOCK_SIZE)
         d["dec_tables"][:B].fill_(db)
         d["dec_ctx"][:B].fill_(1)
+        d["seq_slots"][:B].fill_(-1)
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
@@ -344,6 +376,8 @@ class LLMEngine:
             return []
         sids = h["sample_ids"][:R].tolist()
         self._step_sids = sids
+        if self.stateful:
+            self._assign_slots()
         greedy = self._params_rows(sids)
         pen = self._penalty_rows(sids)
         B = self._bucket(nd) if (npf == 0 and self.cfg.cuda_graphs and not hasattr(self.model, "share_tokens")
@@ -354,7 +388,8 @@ class LLMEngine:
                 self._capture(B, greedy)
             g, out, n_launch = self.graphs[key]
             self._pad_decode_rows(nd, B)
-            self._copy_in(dict(input_ids=B, positions=B, slots=B, dec_tables=B, dec_ctx=B))
+            self._copy_in(dict(input_ids=B, positions=B, slots=B, dec_tables=B, dec_ctx=B,
+                               seq_slots=B if self.stateful else 0))
             g.replay()
             ops._count(n_launch)
             toks = out[:nd]
@@ -392,6 +427,7 @@ class LLMEngine:
         outs = []
         for sid in done:
             st = self.requests.pop(sid)
+            self._free_slot(sid)
             st.finish = now
             reason = _REASONS.get(self.sched.finish_reason(sid), "length")
             cached = self.sched.num_cached_prompt_tokens(sid)

@@ -1,0 +1,97 @@
+"""Qwen3.5 hybrid on the GPU: the fused Gated DeltaNet decode kernel against
+the token recurrence, the model (chunked prefill, paged attention with
+output gate and head 256) against the fp32 oracle, and engine serving
+(graph decode, continuous batching with per-sequence state slots, chunked
+prefill continuing a slot's state)."""
+import json
+import os
+
+import pytest
+import torch
+
+from rlx_models_b200.models.qwen35 import (Qwen35Config, Qwen35LM, Qwen35Oracle, causal_conv1d, gated_delta_recurrent,
+                                           gated_rmsnorm, gdn_gates, l2norm, random_weights)
+
+pytestmark = pytest.mark.gpu
+
+
+def _cfg(**kw):
+    d = dict(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=4, num_attention_heads=4,
+             num_key_value_heads=2, head_dim=256, linear_key_head_dim=128, linear_value_head_dim=128,
+             linear_num_key_heads=2, linear_num_value_heads=4, linear_conv_kernel_dim=4, rope_theta=1e7,
+             max_position_embeddings=4096)
+    d.update(kw)
+    return Qwen35Config(**d)
+
+
+@pytest.mark.parametrize("D", [128, 64])
+def test_gdn_decode_kernel(cuda, D):
+    from rlx_models_b200.ops._ext import ext
+    g = torch.Generator().manual_seed(0)
+    B, Hk, Hv, K, slots = 5, 2, 4, 4, 8
+    C = 2 * Hk * D + Hv * D
+    proj = (torch.randn(B, C + Hv * D + 2 * Hv, generator=g)).bfloat16().to(cuda)
+    conv_w = (torch.randn(C, K, generator=g) * 0.5).to(cuda)
+    A_log = torch.rand(Hv, generator=g).mul(3).to(cuda)
+    dt_bias = torch.randn(Hv, generator=g).to(cuda)
+    norm_w = (1 + 0.1 * torch.randn(D, generator=g)).to(cuda)
+    conv = (torch.randn(slots, 2, C, K - 1, generator=g)).bfloat16().to(cuda)
+    rec = (torch.randn(slots, Hv, D, D, generator=g) * 0.1).to(cuda)
+    seq_slots = torch.tensor([3, 0, 6, -1, 5], dtype=torch.int32, device=cuda)
+    pos = torch.tensor([7, 10, 3, 0, 100], dtype=torch.int32, device=cuda)
+    conv0, rec0 = conv.clone(), rec.clone()
+    out = torch.empty(B, Hv * D, dtype=torch.bfloat16, device=cuda)
+    ext().gdn_decode(proj, conv_w, A_log, dt_bias, norm_w, conv, rec, seq_slots, pos, out, Hk, Hv, D, 1e-6)
+    torch.cuda.synchronize()
+    for b in range(B):
+        s, p = int(seq_slots[b]), int(pos[b])
+        if s < 0:
+            assert out[b].abs().max() == 0
+            continue
+        row = proj[b].float()
+        y, win = causal_conv1d(proj[b, :C, None], conv_w, conv0[s, p & 1])
+        assert torch.equal(conv[s, (p + 1) & 1], win), "conv window advanced into the other parity"
+        q, k, v = y[:, 0].float().split([Hk * D, Hk * D, Hv * D])
+        q = (l2norm(q.view(Hk, D)) * D ** -0.5).repeat_interleave(Hv // Hk, 0)
+        k = l2norm(k.view(Hk, D)).repeat_interleave(Hv // Hk, 0)
+        gl, beta = gdn_gates(row[C + Hv * D + Hv:], row[C + Hv * D:C + Hv * D + Hv], A_log, dt_bias)
+        o, S = gated_delta_recurrent(q[:, None], k[:, None], v.view(Hv, 1, D), gl[:, None], beta[:, None], rec0[s])
+        assert torch.allclose(rec[s], S, atol=1e-4, rtol=1e-3)
+        r = gated_rmsnorm(o[:, 0].bfloat16(), row[C:C + Hv * D].view(Hv, D), norm_w, 1e-6).reshape(-1)
+        assert ((out[b].float() - r).norm() / r.norm()) < 1e-2
+    untouched = [i for i in range(slots) if i not in seq_slots.tolist()]
+    assert torch.equal(rec[untouched], rec0[untouched])
+
+
+def test_qwen35_model_and_engine_vs_oracle(cuda, tmp_path):
+    from rlx_models_b200.api import load
+    from rlx_models_b200.runtime.engine import EngineConfig, SamplingParams
+    from rlx_models_b200.weights.safetensors_io import save_file
+    cfg = _cfg()
+    w = random_weights(cfg, seed=3)
+    d = tmp_path / "q35"
+    os.makedirs(d)
+    hf = cfg.to_hf_dict()
+    hf["model_type"] = "qwen3_5_text"
+    (d / "config.json").write_text(json.dumps(hf))
+    save_file({k: v.contiguous() for k, v in w.items()}, str(d / "model.safetensors"))
+    llm = load(str(d), device=cuda, engine_config=EngineConfig(max_num_seqs=4, max_model_len=512, num_blocks=96,
+                                                               chunk_size=48))
+    assert isinstance(llm.model, Qwen35LM) and not llm.engine.cfg.prefix_caching
+    oracle = Qwen35Oracle(cfg, {k: v.float() for k, v in w.items()})
+    g = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, 512, (70,), generator=g).tolist()
+    lg = llm.logits(ids).float().cpu()
+    ref = oracle.logits(ids)
+    row = (lg - ref).norm(dim=-1) / ref.norm(dim=-1)
+    assert row.median() < 3e-2 and (row > 0.1).float().mean() <= 0.1, row
+    llm.engine.capture_graphs()
+    prompts = [torch.randint(0, 512, (n,), generator=g).tolist() for n in (9, 100, 33)]  # 100 > chunk_size
+    sp = SamplingParams(max_new_tokens=10, ignore_eos=True)
+    singles = [llm.generate(p, sp)[0].token_ids for p in prompts]
+    for p, toks in zip(prompts, singles):
+        lg2 = oracle.logits(p + toks[:-1])[len(p) - 1:]
+        for t, r in zip(toks, lg2):
+            assert r[t] >= r.max() - 0.05 * (r.max() - r.min())
+    assert [o.token_ids for o in llm.generate(prompts, sp)] == singles
+    assert llm.engine.stats["graph_steps"] > 0 and not llm.engine.slot_of
