@@ -414,8 +414,7 @@ class DeepseekLM:
 
     def __init__(self, cfg: DeepseekConfig, weights, device="cuda"):
         from .. import ops
-        from ..quant.mxfp4 import quantize_mxfp4, tile_mxfp4
-        from .moe import GROUP
+        from .moe import pack_experts
         self.cfg, self.device = cfg, torch.device(device)
         self.hkv, self.D = 1, cfg.latent_dim  # one shared latent "head" per token
         c, dev, bf = cfg, self.device, torch.bfloat16
@@ -453,16 +452,9 @@ class DeepseekLM:
                 bn = m + "gate.e_score_correction_bias"
                 M.router_b = g(bn).to(dev, torch.float32) if bn in weights else None
                 I = c.moe_intermediate_size
-                gu_l, dn_l = [], []
-                for e in range(c.n_routed_experts):
-                    gt, up, down = (t.to(dev).float() for t in expert_weights(weights, p, e, I))
-                    # [64 gate rows][64 up rows] per 128-row tile for the fused SwiGLU epilogue
-                    gu_l.append(torch.stack([gt.reshape(I // GROUP, GROUP, -1), up.reshape(I // GROUP, GROUP, -1)],
-                                            1).reshape(2 * I, -1))
-                    dn_l.append(down)
-                M.gu_w, M.gu_exp = tile_mxfp4(*quantize_mxfp4(torch.stack(gu_l)))
-                M.dn_w, M.dn_exp = tile_mxfp4(*quantize_mxfp4(torch.stack(dn_l)))
-                del gu_l, dn_l
+                ws = [[t.to(dev).float() for t in expert_weights(weights, p, e, I)] for e in range(c.n_routed_experts)]
+                M.gu_w, M.gu_exp, M.dn_w, M.dn_exp = pack_experts(*zip(*ws))
+                del ws
                 M.sh_gu = M.sh_dn = None
                 if c.n_shared_experts:
                     s = m + "shared_experts."
@@ -545,35 +537,11 @@ class DeepseekLM:
     def _moe(self, M: _MoE, x: torch.Tensor, h: torch.Tensor, norm_w: torch.Tensor) -> torch.Tensor:
         """h += routed experts + shared expert; returns rmsnorm(h) * norm_w."""
         from .. import ops
-        from ..ops._ext import ext, scratch
-        from .moe import token_tile
+        from .moe import routed_experts
         c = self.cfg
-        T, H = x.shape
-        k, E, I = c.num_experts_per_tok, c.n_routed_experts, c.moe_intermediate_size
-        dev = x.device
         idx, wts = route(c, x.float() @ M.router_w.t(), M.router_b)
-        experts = idx.to(torch.int32).contiguous()
-        weights = wts.float().contiguous()
-        n = T * k
-        bt = token_tile(n, E)
-        meta = torch.empty(2 * E + 2, dtype=torch.int32, device=dev)
-        tiles = torch.empty(4 * (n // bt + E + 1), dtype=torch.int32, device=dev)
-        perm = torch.empty(n, dtype=torch.int32, device=dev)
-        inv = torch.empty(n, dtype=torch.int32, device=dev)
-        cursor = torch.empty(E, dtype=torch.int32, device=dev)
-        ext().moe_align(experts, E, 0, E, bt, meta, tiles, perm, inv, cursor)
-        xa = torch.empty(n, H, dtype=torch.float16, device=dev)
-        ext().moe_gather(x, perm, meta, E, k, xa)
-        s = scratch(dev)
-        gu = torch.empty(n, I, dtype=torch.float16, device=dev)
-        ext().moe_gemm(xa, M.gu_w, M.gu_exp, 2 * I, None, None, perm, meta, tiles, gu, True, 1e30, 1.0, bt,
-                       s.status, 0.0)
-        dn = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
-        ext().moe_gemm(gu, M.dn_w, M.dn_exp, H, None, weights.view(-1), perm, meta, tiles, dn, False, 0.0, 0.0, bt,
-                       s.status)
-        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
-        ext().moe_combine(dn, inv, k, out, False)
-        ops._count(5)
+        out = routed_experts(x, idx.to(torch.int32).contiguous(), wts.float().contiguous(), M.gu_w, M.gu_exp,
+                             M.dn_w, M.dn_exp, c.n_routed_experts, c.moe_intermediate_size)
         if M.sh_gu is not None:
             ops.linear(ops.linear_swiglu(x, M.sh_gu), M.sh_dn, residual=h, out=h)
         return ops.rmsnorm(out, norm_w, c.rms_norm_eps, residual=h, residual_out=h)

@@ -55,6 +55,61 @@ def token_tile(n_assign: int, num_experts: int) -> int:
     return 128
 
 
+def pack_experts(gates, ups, downs):
+    """Per-expert gate / up [I, H] and down [H, I] fp32 -> tiled MXFP4 banks
+    (gu_w, gu_exp, dn_w, dn_exp) for the grouped GEMM, gate / up rows in
+    [64 gate][64 up] groups for its fused SwiGLU epilogue."""
+    I = gates[0].shape[0]
+    gu = torch.stack([torch.stack([g.reshape(I // GROUP, GROUP, -1), u.reshape(I // GROUP, GROUP, -1)], 1)
+                      .reshape(2 * I, -1) for g, u in zip(gates, ups)])
+    gu_w, gu_exp = tile_mxfp4(*quantize_mxfp4(gu))
+    del gu
+    dn_w, dn_exp = tile_mxfp4(*quantize_mxfp4(torch.stack(list(downs))))
+    return gu_w, gu_exp, dn_w, dn_exp
+
+
+def routed_experts(x: torch.Tensor, experts: torch.Tensor, weights: torch.Tensor, gu_w, gu_exp, dn_w, dn_exp,
+                   num_experts: int, inter: int) -> torch.Tensor:
+    """sum_s weights[t, s] * expert_{experts[t, s]}(x[t]) on the grouped MXFP4
+    GEMM (SwiGLU experts, no biases, every expert local): align -> gather ->
+    gate/up GEMM with SwiGLU -> down GEMM scaled by the router weight -> combine."""
+    T, H = x.shape
+    k = experts.shape[1]
+    E = num_experts
+    dev = x.device
+    n = T * k
+    bt = token_tile(n, E)
+    meta = torch.empty(2 * E + 2, dtype=torch.int32, device=dev)
+    tiles = torch.empty(4 * (n // bt + E + 1), dtype=torch.int32, device=dev)
+    perm = torch.empty(n, dtype=torch.int32, device=dev)
+    inv = torch.empty(n, dtype=torch.int32, device=dev)
+    cursor = torch.empty(E, dtype=torch.int32, device=dev)
+    ext().moe_align(experts, E, 0, E, bt, meta, tiles, perm, inv, cursor)
+    xa = torch.empty(n, H, dtype=torch.float16, device=dev)
+    ext().moe_gather(x, perm, meta, E, k, xa)
+    s = scratch(dev)
+    gu = torch.empty(n, inter, dtype=torch.float16, device=dev)
+    ext().moe_gemm(xa, gu_w, gu_exp, 2 * inter, None, None, perm, meta, tiles, gu, True, 1e30, 1.0, bt, s.status, 0.0)
+    dn = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
+    ext().moe_gemm(gu, dn_w, dn_exp, H, None, weights.reshape(-1), perm, meta, tiles, dn, False, 0.0, 0.0, bt,
+                   s.status)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    ext().moe_combine(dn, inv, k, out, False)
+    ops._count(5)
+    return out
+
+
+def softmax_topk(logits: torch.Tensor, k: int, renorm: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """(expert ids int32 [T, k], weights fp32 [T, k]) of softmax-then-top-k
+    routing on the device (optionally renormalised over the k)."""
+    T = logits.shape[0]
+    experts = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+    weights = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+    ext().moe_route(logits, k, True, renorm, experts, weights)
+    ops._count(1)
+    return experts, weights
+
+
 class MoELayer:
     __slots__ = ("router_w", "router_b", "router_corr", "gu_w", "gu_exp", "gu_bias", "dn_w", "dn_exp", "dn_bias",
                  "sh_gu", "sh_dn", "sh_gate")

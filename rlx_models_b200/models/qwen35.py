@@ -56,7 +56,7 @@ import torch.nn.functional as F
 from ..ops import rope_inv_freq
 from ..runtime.kv_cache import BLOCK_SIZE, PagedKVCache
 
-QWEN35_TYPES = ("qwen3_5_text", "qwen3_5", "qwen3_next")
+QWEN35_TYPES = ("qwen3_5_text", "qwen3_5", "qwen3_5_moe_text", "qwen3_5_moe", "qwen3_next")
 
 
 @dataclass
@@ -81,6 +81,12 @@ class Qwen35Config:
     linear_num_key_heads: int = 16
     linear_num_value_heads: int = 32
     layer_types: list | None = None
+    # Qwen3.5-MoE (qwen3_5_moe_text): every MLP routed (softmax, top-k, renormalised)
+    # plus a sigmoid-gated shared expert
+    num_experts: int = 0
+    num_experts_per_tok: int = 8
+    moe_intermediate_size: int = 512
+    shared_expert_intermediate_size: int = 512
     bos_token_id: int | None = None
     eos_token_id: int | list | None = None
     extra: dict = field(default_factory=dict)
@@ -109,11 +115,17 @@ class Qwen35Config:
     def is_linear(self, i: int) -> bool:
         return self.layer_types[i] == "linear_attention"
 
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
     @classmethod
     def from_dict(cls, d: dict) -> "Qwen35Config":
         d = dict(d)
         if isinstance(d.get("text_config"), dict):  # the multimodal wrapper: the text model's config
-            d = dict(d["text_config"], model_type=d["text_config"].get("model_type", "qwen3_5_text"))
+            moe = "moe" in str(d.get("model_type", ""))
+            d = dict(d["text_config"], model_type=d["text_config"].get(
+                "model_type", "qwen3_5_moe_text" if moe else "qwen3_5_text"))
         kw = {f.name: d[f.name] for f in fields(cls) if f.name in d and f.name != "extra"}
         rp = d.get("rope_parameters") or d.get("rope_scaling") or {}
         if "rope_theta" in rp:
@@ -258,9 +270,21 @@ def random_weights(cfg: Qwen35Config, seed: int = 0, device="cpu", dtype=torch.b
         p = f"model.layers.{i}."
         vec(p + "input_layernorm.weight", H)
         vec(p + "post_attention_layernorm.weight", H)
-        lin(p + "mlp.gate_proj.weight", cfg.intermediate_size, H)
-        lin(p + "mlp.up_proj.weight", cfg.intermediate_size, H)
-        lin(p + "mlp.down_proj.weight", H, cfg.intermediate_size)
+        if cfg.is_moe:
+            m, I, Is = p + "mlp.", cfg.moe_intermediate_size, cfg.shared_expert_intermediate_size
+            lin(m + "gate.weight", cfg.num_experts, H)
+            for e in range(cfg.num_experts):
+                lin(m + f"experts.{e}.gate_proj.weight", I, H)
+                lin(m + f"experts.{e}.up_proj.weight", I, H)
+                lin(m + f"experts.{e}.down_proj.weight", H, I)
+            lin(m + "shared_expert.gate_proj.weight", Is, H)
+            lin(m + "shared_expert.up_proj.weight", Is, H)
+            lin(m + "shared_expert.down_proj.weight", H, Is)
+            lin(m + "shared_expert_gate.weight", 1, H)
+        else:
+            lin(p + "mlp.gate_proj.weight", cfg.intermediate_size, H)
+            lin(p + "mlp.up_proj.weight", cfg.intermediate_size, H)
+            lin(p + "mlp.down_proj.weight", H, cfg.intermediate_size)
         if cfg.is_linear(i):
             a = p + "linear_attn."
             lin(a + "in_proj_qkv.weight", cfg.conv_dim, H)
@@ -353,10 +377,29 @@ class Qwen35Oracle:
             x = self._rms(h, p + "input_layernorm.weight")
             h = h + (self.linear_attention(i, x, recurrent) if c.is_linear(i) else self.attention(i, x, pos))
             x = self._rms(h, p + "post_attention_layernorm.weight")
-            m = p + "mlp."
-            h = h + (F.silu(x @ self._t(m + "gate_proj.weight").t()) * (x @ self._t(m + "up_proj.weight").t())) \
-                @ self._t(m + "down_proj.weight").t()
+            h = h + (self.moe(i, x) if c.is_moe else self._swiglu(x, p + "mlp."))
         return self._rms(h, "model.norm.weight")
+
+    def _swiglu(self, x, m):
+        return (F.silu(x @ self._t(m + "gate_proj.weight").t()) * (x @ self._t(m + "up_proj.weight").t())) \
+            @ self._t(m + "down_proj.weight").t()
+
+    def moe(self, i, x):
+        from .deepseek import expert_weights
+        c = self.cfg
+        m = f"model.layers.{i}.mlp."
+        probs = (x @ self._t(m + "gate.weight").t()).softmax(-1)
+        top, idx = probs.topk(c.num_experts_per_tok, -1)
+        top = top / top.sum(-1, keepdim=True)
+        out = torch.zeros_like(x)
+        for e in idx.unique().tolist():
+            rows, slot = (idx == e).nonzero(as_tuple=True)
+            g, u, d = (t.to(self.device, torch.float32) for t in
+                       expert_weights(self.w, f"model.layers.{i}.", e, c.moe_intermediate_size))
+            xe = x[rows]
+            out.index_add_(0, rows, ((F.silu(xe @ g.t()) * (xe @ u.t())) @ d.t()) * top[rows, slot, None])
+        sh = self._swiglu(x, m + "shared_expert.")
+        return out + (x @ self._t(m + "shared_expert_gate.weight").t()).sigmoid() * sh
 
     @torch.no_grad()
     def logits(self, ids, recurrent: bool = False) -> torch.Tensor:
@@ -388,8 +431,24 @@ class HybridCache:
         return self.paged.layer(i)
 
 
+class _Renamed:
+    """Weight source seen under canonical names (``canonical_weights`` map)."""
+
+    def __init__(self, weights, names: dict):
+        self.w, self.names = weights, names
+
+    def __contains__(self, n):
+        return n in self.names
+
+    def keys(self):
+        return list(self.names)
+
+    def __getitem__(self, n):
+        return _getter(self.w)(self.names[n])
+
+
 class _Layer:
-    __slots__ = ("ln1", "ln2", "w_gu", "wd", "wo", "linear", "idx",
+    __slots__ = ("ln1", "ln2", "w_gu", "wd", "wo", "linear", "idx", "moe",
                  "w_qkvg", "q_norm", "k_norm",
                  "w_in", "conv_w", "A_log", "dt_bias", "norm_w")
 
@@ -431,8 +490,23 @@ class Qwen35LM:
             p = f"model.layers.{i}."
             L = _Layer()
             L.ln1, L.ln2 = dvn(g(p + "input_layernorm.weight")), dvn(g(p + "post_attention_layernorm.weight"))
-            L.w_gu = dv(ops.interleave_gate_up(g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")))
-            L.wd = dv(g(p + "mlp.down_proj.weight"))
+            L.moe = None
+            if c.is_moe:
+                from .deepseek import expert_weights
+                from .moe import pack_experts
+                m = p + "mlp."
+                ws = [[t.to(dev).float() for t in expert_weights(_Renamed(weights, names), p, e,
+                                                                   c.moe_intermediate_size)]
+                      for e in range(c.num_experts)]
+                L.moe = (g(m + "gate.weight").to(bf).contiguous(), *pack_experts(*zip(*ws)),
+                         g(m + "shared_expert_gate.weight").float().contiguous())
+                del ws
+                L.w_gu = dv(ops.interleave_gate_up(g(m + "shared_expert.gate_proj.weight"),
+                                                   g(m + "shared_expert.up_proj.weight")))
+                L.wd = dv(g(m + "shared_expert.down_proj.weight"))
+            else:
+                L.w_gu = dv(ops.interleave_gate_up(g(p + "mlp.gate_proj.weight"), g(p + "mlp.up_proj.weight")))
+                L.wd = dv(g(p + "mlp.down_proj.weight"))
             L.linear = c.is_linear(i)
             if L.linear:
                 a = p + "linear_attn."
@@ -555,9 +629,26 @@ class Qwen35LM:
         for i, L in enumerate(self.layers):
             a = self._gdn(L, x, fb, kv, slots) if L.linear else self._attention(L, x, fb, kv)
             x = comm.rowpar_add_norm(a, L.wo, h, L.ln2)
+            nw = self.layers[i + 1].ln1 if i + 1 < n else self.norm
+            if L.moe is not None:
+                x = self._moe(L, x, h, nw)
+                continue
             if x.shape[0] <= ops.ACC_MAX_M:
                 gu = ops.swiglu_acc(ops.linear_acc(x, L.w_gu))
             else:
                 gu = ops.linear_swiglu(x, L.w_gu)
-            x = comm.rowpar_add_norm(gu, L.wd, h, self.layers[i + 1].ln1 if i + 1 < n else self.norm)
+            x = comm.rowpar_add_norm(gu, L.wd, h, nw)
         return x
+
+    def _moe(self, L: _Layer, x: torch.Tensor, h: torch.Tensor, nw: torch.Tensor) -> torch.Tensor:
+        """h += routed experts (MXFP4 grouped GEMM) + sigmoid-gated shared expert;
+        returns rmsnorm(h) * nw."""
+        from .. import ops
+        from .moe import routed_experts, softmax_topk
+        c = self.cfg
+        router, gu_w, gu_exp, dn_w, dn_exp, sh_gate = L.moe
+        experts, weights = softmax_topk(ops.linear(x, router, out_dtype=torch.float32), c.num_experts_per_tok, True)
+        out = routed_experts(x, experts, weights, gu_w, gu_exp, dn_w, dn_exp, c.num_experts, c.moe_intermediate_size)
+        sh = ops.linear(ops.linear_swiglu(x, L.w_gu), L.wd)
+        h.add_((sh.float() * torch.sigmoid(x.float() @ sh_gate.t())).to(h.dtype))
+        return ops.rmsnorm(out, nw, c.rms_norm_eps, residual=h, residual_out=h)

@@ -71,3 +71,29 @@ def test_oracle_matches_transformers(recurrent):
     got = Qwen35Oracle(cfg, sd, chunk=32).logits(ids[0], recurrent=recurrent)
     err = (got - ref).abs().max() / ref.abs().max()
     assert err < 1e-4, err
+
+
+def test_moe_oracle_matches_transformers():
+    from transformers import Qwen3_5MoeForCausalLM, Qwen3_5MoeTextConfig
+    hc = Qwen3_5MoeTextConfig(vocab_size=128, hidden_size=64, num_hidden_layers=4, num_attention_heads=4,
+                              num_key_value_heads=2, head_dim=32, linear_key_head_dim=16, linear_value_head_dim=16,
+                              linear_num_key_heads=2, linear_num_value_heads=4, num_experts=8, num_experts_per_tok=2,
+                              moe_intermediate_size=32, shared_expert_intermediate_size=48, tie_word_embeddings=False)
+    torch.manual_seed(0)
+    m = Qwen3_5MoeForCausalLM(hc).eval()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if p.dim() >= 2 and "conv1d" not in n:
+                p.normal_(0, 1 / math.sqrt(p.shape[-1]))
+            elif n.endswith("norm.weight") and "linear_attn" not in n:
+                p.normal_(0, 0.1)
+    cfg = Qwen35Config.from_dict(hc.to_dict())
+    assert cfg.is_moe and cfg.num_experts == 8
+    sd = {k: v.detach() for k, v in m.state_dict().items()}
+    assert "model.layers.0.mlp.experts.gate_up_proj" in sd  # transformers' fused expert layout
+    ids = torch.randint(0, 128, (1, 41), generator=torch.Generator().manual_seed(3))
+    with torch.no_grad():
+        ref = m(ids).logits[0].float()
+    got = Qwen35Oracle(cfg, sd, chunk=16).logits(ids[0])
+    err = (got - ref).abs().max() / ref.abs().max()
+    assert err < 1e-4, err

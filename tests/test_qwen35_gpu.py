@@ -95,3 +95,28 @@ def test_qwen35_model_and_engine_vs_oracle(cuda, tmp_path):
             assert r[t] >= r.max() - 0.05 * (r.max() - r.min())
     assert [o.token_ids for o in llm.generate(prompts, sp)] == singles
     assert llm.engine.stats["graph_steps"] > 0 and not llm.engine.slot_of
+
+
+def test_qwen35_moe_vs_oracle(cuda):
+    """Qwen3.5-MoE: softmax top-k routed experts on the grouped MXFP4 GEMM and
+    the sigmoid-gated shared expert; oracle on the same MXFP4-rounded experts."""
+    from rlx_models_b200.api import LLM
+    from rlx_models_b200.quant.mxfp4 import mxfp4_roundtrip
+    from rlx_models_b200.runtime.engine import EngineConfig, SamplingParams
+    cfg = _cfg(model_type="qwen3_5_moe_text", num_experts=16, num_experts_per_tok=4, moe_intermediate_size=128,
+               shared_expert_intermediate_size=256)
+    w = random_weights(cfg, seed=8)
+    for k in list(w):
+        if ".mlp.experts." in k:
+            w[k] = mxfp4_roundtrip(w[k].float()).bfloat16()
+    llm = LLM(Qwen35LM(cfg, w, device=cuda), EngineConfig(max_num_seqs=4, max_model_len=256, num_blocks=64))
+    oracle = Qwen35Oracle(cfg, {k: v.float() for k, v in w.items()})
+    ids = torch.randint(0, 512, (45,), generator=torch.Generator().manual_seed(5)).tolist()
+    lg = llm.logits(ids).float().cpu()
+    ref = oracle.logits(ids)
+    row = (lg - ref).norm(dim=-1) / ref.norm(dim=-1)
+    assert row.median() < 3e-2 and (row > 0.1).float().mean() <= 0.1, row
+    toks = llm.generate(ids, SamplingParams(max_new_tokens=6, ignore_eos=True))[0].token_ids
+    lg2 = oracle.logits(ids + toks[:-1])[len(ids) - 1:]
+    for t, r in zip(toks, lg2):
+        assert r[t] >= r.max() - 0.05 * (r.max() - r.min())
