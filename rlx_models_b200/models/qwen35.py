@@ -87,6 +87,9 @@ class Qwen35Config:
     num_experts_per_tok: int = 8
     moe_intermediate_size: int = 512
     shared_expert_intermediate_size: int = 512
+    norm_topk_prob: bool = True
+    mlp_only_layers: list = field(default_factory=list)  # Qwen3-Next: dense layers of a MoE model
+    decoder_sparse_step: int = 1
     bos_token_id: int | None = None
     eos_token_id: int | list | None = None
     extra: dict = field(default_factory=dict)
@@ -118,6 +121,9 @@ class Qwen35Config:
     @property
     def is_moe(self) -> bool:
         return self.num_experts > 0
+
+    def is_moe_layer(self, i: int) -> bool:
+        return self.is_moe and i not in self.mlp_only_layers and (i + 1) % self.decoder_sparse_step == 0
 
     @classmethod
     def from_dict(cls, d: dict) -> "Qwen35Config":
@@ -156,7 +162,7 @@ def is_qwen35_config(path: str) -> bool:
             d = json.load(f)
     except (OSError, ValueError):
         return False
-    return d.get("model_type") in QWEN35_TYPES and d.get("model_type") != "qwen3_next"
+    return d.get("model_type") in QWEN35_TYPES
 
 
 # ---------------------------------------------------------------------------
@@ -239,16 +245,59 @@ def _getter(weights):
     return (lambda n: weights.take(n)) if hasattr(weights, "take") else (lambda n: weights[n])
 
 
-def canonical_weights(weights) -> dict:
-    """Released multimodal checkpoints keep the text model under
-    ``model.language_model.``; map those names to ``model.`` and drop the
-    vision tower and the MTP head."""
-    out = {}
-    for n in list(weights.keys()):
-        if n.startswith(("model.visual.", "mtp.")):
-            continue
-        out[n.replace("model.language_model.", "model.", 1)] = n
-    return out
+class CanonicalSource:
+    """Checkpoint tensors under the names the builders read.
+
+    * released multimodal checkpoints keep the text model under
+      ``model.language_model.``: mapped to ``model.``; the vision tower and the
+      MTP head are dropped;
+    * Qwen3-Next fuses the Gated DeltaNet input projections per key-head group
+      (``in_proj_qkvz`` rows [q | k | v of the group's value heads | z of
+      them] per group, ``in_proj_ba`` rows [b | a] per group): regrouped into
+      Qwen3.5's ``in_proj_qkv`` ([all q | all k | all v]), ``in_proj_z``,
+      ``in_proj_b`` and ``in_proj_a``."""
+
+    def __init__(self, weights, cfg: Qwen35Config):
+        self.get, self.cfg = _getter(weights), cfg
+        self.map: dict[str, tuple] = {}
+        for n in list(weights.keys()):
+            if n.startswith(("model.visual.", "mtp.")):
+                continue
+            c = n.replace("model.language_model.", "model.", 1)
+            if c.endswith("linear_attn.in_proj_qkvz.weight"):
+                pre = c[: -len("in_proj_qkvz.weight")]
+                for part in ("in_proj_qkv", "in_proj_z"):
+                    self.map[pre + part + ".weight"] = (n, part)
+            elif c.endswith("linear_attn.in_proj_ba.weight"):
+                pre = c[: -len("in_proj_ba.weight")]
+                for part in ("in_proj_b", "in_proj_a"):
+                    self.map[pre + part + ".weight"] = (n, part)
+            else:
+                self.map[c] = (n, None)
+
+    def keys(self):
+        return list(self.map)
+
+    def __contains__(self, name):
+        return name in self.map
+
+    def __getitem__(self, name):
+        n, part = self.map[name]
+        t = self.get(n)
+        if part is None:
+            return t
+        c = self.cfg
+        Hk, dk, dv = c.linear_num_key_heads, c.linear_key_head_dim, c.linear_value_head_dim
+        r = c.linear_num_value_heads // Hk
+        H = t.shape[-1]
+        if part in ("in_proj_qkv", "in_proj_z"):
+            t = t.view(Hk, 2 * dk + 2 * r * dv, H)
+            if part == "in_proj_z":
+                return t[:, 2 * dk + r * dv:].reshape(-1, H)
+            return torch.cat([t[:, :dk].reshape(-1, H), t[:, dk:2 * dk].reshape(-1, H),
+                              t[:, 2 * dk:2 * dk + r * dv].reshape(-1, H)], 0)
+        t = t.view(Hk, 2 * r, H)
+        return (t[:, :r] if part == "in_proj_b" else t[:, r:]).reshape(-1, H)
 
 
 def random_weights(cfg: Qwen35Config, seed: int = 0, device="cpu", dtype=torch.bfloat16) -> dict:
@@ -270,7 +319,7 @@ def random_weights(cfg: Qwen35Config, seed: int = 0, device="cpu", dtype=torch.b
         p = f"model.layers.{i}."
         vec(p + "input_layernorm.weight", H)
         vec(p + "post_attention_layernorm.weight", H)
-        if cfg.is_moe:
+        if cfg.is_moe_layer(i):
             m, I, Is = p + "mlp.", cfg.moe_intermediate_size, cfg.shared_expert_intermediate_size
             lin(m + "gate.weight", cfg.num_experts, H)
             for e in range(cfg.num_experts):
@@ -319,9 +368,7 @@ class Qwen35Oracle:
 
     def __init__(self, cfg: Qwen35Config, weights, device="cpu", chunk: int = 64):
         self.cfg, self.device, self.chunk = cfg, torch.device(device), chunk
-        names = canonical_weights(weights)
-        g = _getter(weights)
-        self.w = {c: g(n) for c, n in names.items()}
+        self.w = CanonicalSource(weights, cfg)
         self.inv, self.mult = rope_inv_freq(cfg.rotary_dim, cfg.rope_theta, None, cfg.max_position_embeddings)
 
     def _t(self, n):
@@ -377,7 +424,7 @@ class Qwen35Oracle:
             x = self._rms(h, p + "input_layernorm.weight")
             h = h + (self.linear_attention(i, x, recurrent) if c.is_linear(i) else self.attention(i, x, pos))
             x = self._rms(h, p + "post_attention_layernorm.weight")
-            h = h + (self.moe(i, x) if c.is_moe else self._swiglu(x, p + "mlp."))
+            h = h + (self.moe(i, x) if c.is_moe_layer(i) else self._swiglu(x, p + "mlp."))
         return self._rms(h, "model.norm.weight")
 
     def _swiglu(self, x, m):
@@ -390,7 +437,8 @@ class Qwen35Oracle:
         m = f"model.layers.{i}.mlp."
         probs = (x @ self._t(m + "gate.weight").t()).softmax(-1)
         top, idx = probs.topk(c.num_experts_per_tok, -1)
-        top = top / top.sum(-1, keepdim=True)
+        if c.norm_topk_prob:
+            top = top / top.sum(-1, keepdim=True)
         out = torch.zeros_like(x)
         for e in idx.unique().tolist():
             rows, slot = (idx == e).nonzero(as_tuple=True)
@@ -431,22 +479,6 @@ class HybridCache:
         return self.paged.layer(i)
 
 
-class _Renamed:
-    """Weight source seen under canonical names (``canonical_weights`` map)."""
-
-    def __init__(self, weights, names: dict):
-        self.w, self.names = weights, names
-
-    def __contains__(self, n):
-        return n in self.names
-
-    def keys(self):
-        return list(self.names)
-
-    def __getitem__(self, n):
-        return _getter(self.w)(self.names[n])
-
-
 class _Layer:
     __slots__ = ("ln1", "ln2", "w_gu", "wd", "wo", "linear", "idx", "moe",
                  "w_qkvg", "q_norm", "k_norm",
@@ -468,11 +500,10 @@ class Qwen35LM:
         self.scale = c.head_dim ** -0.5
         inv, self.rope_mult = rope_inv_freq(c.rotary_dim, c.rope_theta, None, c.max_position_embeddings)
         self.inv_freq = inv.to(dev)
-        names = canonical_weights(weights)
-        raw = _getter(weights)
+        src = CanonicalSource(weights, c)
 
         def g(n):
-            return raw(names[n]).to(dev)
+            return src[n].to(dev)
 
         def dv(t):
             return t.to(dev, bf).contiguous()
@@ -491,12 +522,11 @@ class Qwen35LM:
             L = _Layer()
             L.ln1, L.ln2 = dvn(g(p + "input_layernorm.weight")), dvn(g(p + "post_attention_layernorm.weight"))
             L.moe = None
-            if c.is_moe:
+            if c.is_moe_layer(i):
                 from .deepseek import expert_weights
                 from .moe import pack_experts
                 m = p + "mlp."
-                ws = [[t.to(dev).float() for t in expert_weights(_Renamed(weights, names), p, e,
-                                                                   c.moe_intermediate_size)]
+                ws = [[t.to(dev).float() for t in expert_weights(src, p, e, c.moe_intermediate_size)]
                       for e in range(c.num_experts)]
                 L.moe = (g(m + "gate.weight").to(bf).contiguous(), *pack_experts(*zip(*ws)),
                          g(m + "shared_expert_gate.weight").float().contiguous())
@@ -647,7 +677,8 @@ class Qwen35LM:
         from .moe import routed_experts, softmax_topk
         c = self.cfg
         router, gu_w, gu_exp, dn_w, dn_exp, sh_gate = L.moe
-        experts, weights = softmax_topk(ops.linear(x, router, out_dtype=torch.float32), c.num_experts_per_tok, True)
+        experts, weights = softmax_topk(ops.linear(x, router, out_dtype=torch.float32), c.num_experts_per_tok,
+                                        c.norm_topk_prob)
         out = routed_experts(x, experts, weights, gu_w, gu_exp, dn_w, dn_exp, c.num_experts, c.moe_intermediate_size)
         sh = ops.linear(ops.linear_swiglu(x, L.w_gu), L.wd)
         h.add_((sh.float() * torch.sigmoid(x.float() @ sh_gate.t())).to(h.dtype))

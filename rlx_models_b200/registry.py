@@ -70,7 +70,7 @@ def _deepseek(cfg, weights, device, tp_rank, tp_size, comm):
     return DeepseekLM(cfg, weights, device=device)
 
 
-@register("qwen3_5_text", "qwen3_5", "qwen3_5_moe_text", "qwen3_5_moe")
+@register("qwen3_5_text", "qwen3_5", "qwen3_5_moe_text", "qwen3_5_moe", "qwen3_next")
 def _qwen35(cfg, weights, device, tp_rank, tp_size, comm):
     from .models.qwen35 import Qwen35LM
     if tp_size != 1:
@@ -85,7 +85,8 @@ def build_model(cfg: DecoderConfig, weights=None, *, device="cuda", tp_rank=0, t
     if weights is None and cfg.model_type in ("deepseek_v3", "deepseek_v2", "kimi_k2"):
         from .models.deepseek import random_weights
         weights = random_weights(cfg, seed, device)
-    elif weights is None and cfg.model_type in ("qwen3_5_text", "qwen3_5", "qwen3_5_moe_text", "qwen3_5_moe"):
+    elif weights is None and cfg.model_type in ("qwen3_5_text", "qwen3_5", "qwen3_5_moe_text", "qwen3_5_moe",
+                                                "qwen3_next"):
         from .models.qwen35 import random_weights
         weights = random_weights(cfg, seed, device)
     elif weights is None:

@@ -97,3 +97,32 @@ def test_moe_oracle_matches_transformers():
     got = Qwen35Oracle(cfg, sd, chunk=16).logits(ids[0])
     err = (got - ref).abs().max() / ref.abs().max()
     assert err < 1e-4, err
+
+
+def test_qwen3_next_matches_transformers():
+    """Qwen3-Next: the per-group fused in_proj_qkvz / in_proj_ba regrouped into
+    the Qwen3.5 layout, MoE on all but the mlp_only_layers."""
+    from transformers import Qwen3NextConfig, Qwen3NextForCausalLM
+    hc = Qwen3NextConfig(vocab_size=128, hidden_size=64, intermediate_size=96, num_hidden_layers=4,
+                         num_attention_heads=4, num_key_value_heads=2, head_dim=32, linear_key_head_dim=16,
+                         linear_value_head_dim=16, linear_num_key_heads=2, linear_num_value_heads=4, num_experts=8,
+                         num_experts_per_tok=2, moe_intermediate_size=32, shared_expert_intermediate_size=48,
+                         mlp_only_layers=[1], norm_topk_prob=False, tie_word_embeddings=False)
+    torch.manual_seed(0)
+    m = Qwen3NextForCausalLM(hc).eval()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if p.dim() >= 2 and "conv1d" not in n:
+                p.normal_(0, 1 / math.sqrt(p.shape[-1]))
+            elif n.endswith("norm.weight") and "linear_attn" not in n:
+                p.normal_(0, 0.1)
+    cfg = Qwen35Config.from_dict(hc.to_dict())
+    assert cfg.is_moe_layer(0) and not cfg.is_moe_layer(1) and not cfg.norm_topk_prob
+    sd = {k: v.detach() for k, v in m.state_dict().items()}
+    assert "model.layers.0.linear_attn.in_proj_qkvz.weight" in sd
+    ids = torch.randint(0, 128, (1, 37), generator=torch.Generator().manual_seed(3))
+    with torch.no_grad():
+        ref = m(ids).logits[0].float()
+    got = Qwen35Oracle(cfg, sd, chunk=16).logits(ids[0])
+    err = (got - ref).abs().max() / ref.abs().max()
+    assert err < 1e-4, err
