@@ -191,6 +191,10 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
             config = DeepseekConfig.from_file(path)
         elif config is None and is_qwen35_config(path):  # Gated DeltaNet hybrid
             config = Qwen35Config.from_file(path)
+        else:
+            from .models.lfm2 import Lfm2Config, is_lfm2_config
+            if config is None and is_lfm2_config(path):  # short-conv hybrid
+                config = Lfm2Config.from_file(path)
         cfg = config or C.DecoderConfig.from_file(path)
         from .weights.mlx import MLXWeights
         if MLXWeights.is_mlx_dir(path):  # MLX affine group-quantised checkpoint

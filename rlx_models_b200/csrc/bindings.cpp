@@ -152,6 +152,41 @@ void gdn_decode(const Tensor& proj, const Tensor& conv_w, const Tensor& A_log, c
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void shortconv_decode(const Tensor& proj, const Tensor& w, const optional<Tensor>& bias, Tensor& conv_state,
+                      const Tensor& seq_slots, const Tensor& positions, Tensor& out) {
+  check_cuda(proj, "proj");
+  const int64_t B = proj.size(0), H = w.size(0), K = w.size(1);
+  TORCH_CHECK(proj.scalar_type() == at::kBFloat16 && proj.dim() == 2 && proj.stride(1) == 1 && proj.size(1) >= 3 * H,
+              "b200.shortconv_decode: proj [B, >= 3H] bf16");
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous() && w.dim() == 2, "b200.shortconv_decode: w [H, K]");
+  if (bias.has_value() && bias->defined())
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == H, "b200.shortconv_decode: bias [H] fp32");
+  TORCH_CHECK(conv_state.scalar_type() == at::kBFloat16 && conv_state.is_contiguous() && conv_state.dim() == 4 &&
+                  conv_state.size(1) == 2 && conv_state.size(2) == H && conv_state.size(3) == K - 1,
+              "b200.shortconv_decode: conv_state [slots, 2, H, K-1] bf16");
+  TORCH_CHECK(seq_slots.scalar_type() == at::kInt && seq_slots.numel() == B && positions.scalar_type() == at::kInt &&
+                  positions.numel() == B,
+              "b200.shortconv_decode: seq_slots / positions int32 [B]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == B * H,
+              "b200.shortconv_decode: out [B, H] bf16");
+  c10::cuda::CUDAGuard g(proj.device());
+  b200::ShortConvArgs a{};
+  a.proj = reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr());
+  a.ld = proj.stride(0);
+  a.w = w.data_ptr<float>();
+  a.bias = (bias.has_value() && bias->defined()) ? bias->data_ptr<float>() : nullptr;
+  a.conv_state = reinterpret_cast<__nv_bfloat16*>(conv_state.data_ptr());
+  a.seq_slots = seq_slots.data_ptr<int32_t>();
+  a.positions = positions.data_ptr<int32_t>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.B = (int)B;
+  a.H = (int)H;
+  a.K = (int)K;
+  a.num_slots = conv_state.size(0);
+  b200::shortconv_decode_launch(a, cur_stream(proj));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void embedding(const Tensor& ids, const Tensor& table, Tensor& out) {
   check_cuda(ids, "ids");
   TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "b200.embedding: int32 ids");
@@ -952,6 +987,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gate_r2") = 1, py::arg("gate_off") = 0, py::arg("glu_act") = 0);
   m.def("gemm", &gemm);
   m.def("gdn_decode", &gdn_decode);
+  m.def("shortconv_decode", &shortconv_decode);
   m.def("gemm_push_shards", &gemm_push_shards);
   m.def("shard_push_add", &shard_push_add);
   m.def("peer_barrier", &peer_barrier);

@@ -255,6 +255,21 @@ struct GdnDecodeArgs {
 };
 void gdn_decode_launch(const GdnDecodeArgs& a, cudaStream_t st);
 
+// LFM2 short convolution, decode step (see gdn.cu)
+struct ShortConvArgs {
+  const __nv_bfloat16* proj;  // [B, ld]: [B gate (H) | C gate (H) | x (H)]
+  int64_t ld;
+  const float* w;             // [H, K]
+  const float* bias;          // [H] or null
+  __nv_bfloat16* conv_state;  // [num_slots, 2, H, K-1] (window of B*x before the token, by position parity)
+  const int32_t* seq_slots;   // [B]
+  const int32_t* positions;   // [B]
+  __nv_bfloat16* out;         // [B, H]
+  int B, H, K;
+  int64_t num_slots;
+};
+void shortconv_decode_launch(const ShortConvArgs& a, cudaStream_t st);
+
 // ---------------- training ----------------
 void adamw_launch(float* master, const void* grad, bool grad_f32, float* m, float* v, void* param_out, int64_t n,
                   float lr, float b1, float b2, float eps, float wd, int64_t step, const float* scale_ptr,

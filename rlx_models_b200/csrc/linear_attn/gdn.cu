@@ -137,3 +137,54 @@ void gdn_decode_launch(const GdnDecodeArgs& a, cudaStream_t st) {
 }
 
 }  // namespace b200
+
+// ---------------------------------------------------------------------------
+// LFM2 short-convolution decode step: per (row, channel c)
+//   bx = B[c] * x[c];  y = C[c] * (sum_i w[c][i] * [window | bx][i] (+ bias[c]))
+// with the window (K-1 previous bx values) read from parity pos & 1 and the
+// advanced window written to the other parity (no activation).
+// ---------------------------------------------------------------------------
+namespace b200 {
+namespace shortconv {
+
+__global__ void shortconv_decode_kernel(ShortConvArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)a.B * a.H) return;
+  const int b = (int)(idx / a.H), c = (int)(idx % a.H);
+  const int64_t slot = a.seq_slots[b];
+  __nv_bfloat16* out = a.out + (int64_t)b * a.H + c;
+  if (slot < 0 || slot >= a.num_slots) {
+    *out = __float2bfloat16(0.f);
+    return;
+  }
+  const __nv_bfloat16* row = a.proj + (int64_t)b * a.ld;
+  const float bv = __bfloat162float(row[c]), cv = __bfloat162float(row[a.H + c]),
+              xv = __bfloat162float(row[2 * a.H + c]);
+  const float bx = __bfloat162float(__float2bfloat16(bv * xv));  // B * x is a bf16 activation
+  const int W = a.K - 1, par = a.positions[b] & 1;
+  const __nv_bfloat16* win = a.conv_state + ((slot * 2 + par) * a.H + c) * W;
+  __nv_bfloat16* nxt = a.conv_state + ((slot * 2 + (par ^ 1)) * a.H + c) * W;
+  float acc = a.bias != nullptr ? a.bias[c] : 0.f;
+  float prev[8];
+  for (int i = 0; i < W; ++i) {
+    prev[i] = __bfloat162float(win[i]);
+    acc += a.w[(int64_t)c * a.K + i] * prev[i];
+  }
+  acc += a.w[(int64_t)c * a.K + W] * bx;
+  for (int i = 0; i + 1 < W; ++i) nxt[i] = __float2bfloat16(prev[i + 1]);
+  nxt[W - 1] = __float2bfloat16(bx);
+  *out = __float2bfloat16(cv * __bfloat162float(__float2bfloat16(acc)));
+}
+
+}  // namespace shortconv
+
+void shortconv_decode_launch(const ShortConvArgs& a, cudaStream_t st) {
+  if (a.B == 0) return;
+  if (a.K < 2 || a.K > 9) throw std::runtime_error("b200.shortconv_decode: kernel size 2..9");
+  const int64_t n = (int64_t)a.B * a.H;
+  launch_pdl(shortconv::shortconv_decode_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, a);
+}
+
+}  // namespace b200

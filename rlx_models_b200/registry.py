@@ -78,6 +78,14 @@ def _qwen35(cfg, weights, device, tp_rank, tp_size, comm):
     return Qwen35LM(cfg, weights, device=device)
 
 
+@register("lfm2")
+def _lfm2(cfg, weights, device, tp_rank, tp_size, comm):
+    from .models.lfm2 import Lfm2LM
+    if tp_size != 1:
+        raise NotImplementedError("LFM2 runs on one GPU per replica")
+    return Lfm2LM(cfg, weights, device=device)
+
+
 def build_model(cfg: DecoderConfig, weights=None, *, device="cuda", tp_rank=0, tp_size=1, comm=None, seed=0):
     fn = _BUILDERS.get(cfg.model_type)
     if fn is None:
@@ -88,6 +96,9 @@ def build_model(cfg: DecoderConfig, weights=None, *, device="cuda", tp_rank=0, t
     elif weights is None and cfg.model_type in ("qwen3_5_text", "qwen3_5", "qwen3_5_moe_text", "qwen3_5_moe",
                                                 "qwen3_next"):
         from .models.qwen35 import random_weights
+        weights = random_weights(cfg, seed, device)
+    elif weights is None and cfg.model_type == "lfm2":
+        from .models.lfm2 import random_weights
         weights = random_weights(cfg, seed, device)
     elif weights is None:
         weights = RandomWeights(cfg, seed, device)
