@@ -187,6 +187,65 @@ void shortconv_decode(const Tensor& proj, const Tensor& w, const optional<Tensor
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void ssd_decode(const Tensor& proj, int64_t xbc_off, int64_t dt_off, const Tensor& conv_w,
+                const optional<Tensor>& conv_b, const Tensor& A_log, const Tensor& dt_bias, const Tensor& D,
+                double dt_min, double dt_max, Tensor& conv_state, Tensor& ssm_state, const Tensor& seq_slots,
+                const Tensor& positions, Tensor& out, int64_t G) {
+  check_cuda(proj, "proj");
+  const int64_t B = proj.size(0), H = A_log.numel();
+  TORCH_CHECK(proj.scalar_type() == at::kBFloat16 && proj.dim() == 2 && proj.stride(1) == 1, "b200.ssd_decode: proj");
+  TORCH_CHECK(conv_w.scalar_type() == at::kFloat && conv_w.is_contiguous() && conv_w.dim() == 2, "b200.ssd_decode: conv_w");
+  const int64_t conv_dim = conv_w.size(0), K = conv_w.size(1);
+  TORCH_CHECK(ssm_state.scalar_type() == at::kFloat && ssm_state.is_contiguous() && ssm_state.dim() == 4 &&
+                  ssm_state.size(1) == H,
+              "b200.ssd_decode: ssm_state [slots, H, N, P] fp32");
+  const int64_t N = ssm_state.size(2), P = ssm_state.size(3);
+  TORCH_CHECK(conv_dim == H * P + 2 * G * N, "b200.ssd_decode: conv_dim != H P + 2 G N");
+  TORCH_CHECK(xbc_off + conv_dim <= proj.size(1) && dt_off + H <= proj.size(1), "b200.ssd_decode: proj offsets");
+  if (conv_b.has_value() && conv_b->defined())
+    TORCH_CHECK(conv_b->scalar_type() == at::kFloat && conv_b->numel() == conv_dim, "b200.ssd_decode: conv_b");
+  TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat && dt_bias.numel() == H &&
+                  D.scalar_type() == at::kFloat && D.numel() == H,
+              "b200.ssd_decode: A_log / dt_bias / D fp32 [H]");
+  TORCH_CHECK(conv_state.scalar_type() == at::kBFloat16 && conv_state.is_contiguous() && conv_state.dim() == 4 &&
+                  conv_state.size(0) == ssm_state.size(0) && conv_state.size(1) == 2 &&
+                  conv_state.size(2) == conv_dim && conv_state.size(3) == K - 1,
+              "b200.ssd_decode: conv_state [slots, 2, conv_dim, K-1] bf16");
+  TORCH_CHECK(seq_slots.scalar_type() == at::kInt && seq_slots.numel() == B && positions.scalar_type() == at::kInt &&
+                  positions.numel() == B,
+              "b200.ssd_decode: seq_slots / positions int32 [B]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.numel() == B * H * P,
+              "b200.ssd_decode: out [B, H*P] bf16");
+  c10::cuda::CUDAGuard g(proj.device());
+  b200::SsdDecodeArgs a{};
+  a.proj = reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr());
+  a.ld = proj.stride(0);
+  a.xbc_off = (int)xbc_off;
+  a.dt_off = (int)dt_off;
+  a.conv_w = conv_w.data_ptr<float>();
+  a.conv_b = (conv_b.has_value() && conv_b->defined()) ? conv_b->data_ptr<float>() : nullptr;
+  a.A_log = A_log.data_ptr<float>();
+  a.dt_bias = dt_bias.data_ptr<float>();
+  a.D = D.data_ptr<float>();
+  a.dt_min = (float)dt_min;
+  a.dt_max = (float)dt_max;
+  a.conv_state = reinterpret_cast<__nv_bfloat16*>(conv_state.data_ptr());
+  a.ssm_state = ssm_state.data_ptr<float>();
+  a.seq_slots = seq_slots.data_ptr<int32_t>();
+  a.positions = positions.data_ptr<int32_t>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.B = (int)B;
+  a.H = (int)H;
+  a.G = (int)G;
+  a.N = (int)N;
+  a.P = (int)P;
+  a.K = (int)K;
+  a.conv_dim = (int)conv_dim;
+  a.num_slots = ssm_state.size(0);
+  b200::ssd_decode_launch(a, cur_stream(proj));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void embedding(const Tensor& ids, const Tensor& table, Tensor& out) {
   check_cuda(ids, "ids");
   TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "b200.embedding: int32 ids");
@@ -988,6 +1047,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("gdn_decode", &gdn_decode);
   m.def("shortconv_decode", &shortconv_decode);
+  m.def("ssd_decode", &ssd_decode);
   m.def("gemm_push_shards", &gemm_push_shards);
   m.def("shard_push_add", &shard_push_add);
   m.def("peer_barrier", &peer_barrier);

@@ -270,6 +270,27 @@ struct ShortConvArgs {
 };
 void shortconv_decode_launch(const ShortConvArgs& a, cudaStream_t st);
 
+// Mamba-2 SSD decode step (see gdn.cu)
+struct SsdDecodeArgs {
+  const __nv_bfloat16* proj;  // [B, ld]: x/B/C conv inputs at xbc_off (conv_dim), dt at dt_off (H)
+  int64_t ld;
+  int xbc_off, dt_off;
+  const float* conv_w;        // [conv_dim, K]
+  const float* conv_b;        // [conv_dim] or null
+  const float* A_log;         // [H]
+  const float* dt_bias;       // [H]
+  const float* D;             // [H]
+  float dt_min, dt_max;
+  __nv_bfloat16* conv_state;  // [num_slots, 2, conv_dim, K-1]
+  float* ssm_state;           // [num_slots, H, N, P]
+  const int32_t* seq_slots;   // [B]
+  const int32_t* positions;   // [B]
+  __nv_bfloat16* out;         // [B, H*P]: y + D x (before the gated norm)
+  int B, H, G, N, P, K, conv_dim;
+  int64_t num_slots;
+};
+void ssd_decode_launch(const SsdDecodeArgs& a, cudaStream_t st);
+
 // ---------------- training ----------------
 void adamw_launch(float* master, const void* grad, bool grad_f32, float* m, float* v, void* param_out, int64_t n,
                   float lr, float b1, float b2, float eps, float wd, int64_t step, const float* scale_ptr,

@@ -188,3 +188,90 @@ void shortconv_decode_launch(const ShortConvArgs& a, cudaStream_t st) {
 }
 
 }  // namespace b200
+
+// ---------------------------------------------------------------------------
+// Mamba-2 (SSD) decode step: per (sequence, head h of group g = h / (H / G)):
+//   conv1d step (+ bias, SiLU) over the head's P x channels and the group's
+//   N B and N C channels; dt = clamp(softplus(dt_raw + dt_bias)); dA = exp(dt A)
+//   S[n, p] <- dA S[n, p] + dt x[p] B[n];  y[p] = sum_n S[n, p] C[n] + D x[p]
+// One CTA of P threads per (sequence, head); thread p keeps state column p
+// (N fp32 values) in registers. The first head of a group advances the
+// group's B / C conv windows (written to the other parity buffer).
+// ---------------------------------------------------------------------------
+namespace b200 {
+namespace ssd {
+
+__device__ __forceinline__ float conv_ch(const SsdDecodeArgs& a, const __nv_bfloat16* row, int64_t slot, int par,
+                                         int c, bool advance) {
+  const int W = a.K - 1;
+  const __nv_bfloat16* win = a.conv_state + ((slot * 2 + par) * a.conv_dim + c) * W;
+  __nv_bfloat16* nxt = a.conv_state + ((slot * 2 + (par ^ 1)) * a.conv_dim + c) * W;
+  const float xin = __bfloat162float(row[a.xbc_off + c]);
+  float acc = a.conv_b != nullptr ? a.conv_b[c] : 0.f;
+  float prev[8];
+  for (int i = 0; i < W; ++i) {
+    prev[i] = __bfloat162float(win[i]);
+    acc += a.conv_w[(int64_t)c * a.K + i] * prev[i];
+  }
+  acc += a.conv_w[(int64_t)c * a.K + W] * xin;
+  if (advance) {
+    for (int i = 0; i + 1 < W; ++i) nxt[i] = __float2bfloat16(prev[i + 1]);
+    nxt[W - 1] = __float2bfloat16(xin);
+  }
+  return __bfloat162float(__float2bfloat16(acc / (1.f + __expf(-acc))));
+}
+
+template <int N, int P>
+__global__ void __launch_bounds__(P) ssd_decode_kernel(SsdDecodeArgs a) {
+  __shared__ float Bs[N], Cs[N];
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x, h = blockIdx.y, t = threadIdx.x;
+  const int64_t slot = a.seq_slots[b];
+  __nv_bfloat16* out = a.out + ((int64_t)b * a.H + h) * P + t;
+  if (slot < 0 || slot >= a.num_slots) {
+    *out = __float2bfloat16(0.f);
+    return;
+  }
+  const int par = a.positions[b] & 1;
+  const int hpg = a.H / a.G, g = h / hpg;
+  const bool owner = (h % hpg) == 0;
+  const __nv_bfloat16* row = a.proj + (int64_t)b * a.ld;
+  const int I = a.H * P;
+  const float x = conv_ch(a, row, slot, par, h * P + t, true);
+  for (int n = t; n < N; n += P) {
+    Bs[n] = conv_ch(a, row, slot, par, I + g * N + n, owner);
+    Cs[n] = conv_ch(a, row, slot, par, I + a.G * N + g * N + n, owner);
+  }
+  const float dr = __bfloat162float(row[a.dt_off + h]) + a.dt_bias[h];
+  float dt = dr > 20.f ? dr : log1pf(__expf(dr));
+  dt = fminf(fmaxf(dt, a.dt_min), a.dt_max);
+  const float dA = __expf(-__expf(a.A_log[h]) * dt);
+  __syncthreads();
+  float* S = a.ssm_state + ((slot * a.H + h) * (int64_t)N) * P + t;  // column t of [N, P]
+  const float dx = dt * x;
+  float y = 0.f;
+#pragma unroll
+  for (int n = 0; n < N; ++n) {
+    const float s = S[(int64_t)n * P] * dA + dx * Bs[n];
+    S[(int64_t)n * P] = s;
+    y += s * Cs[n];
+  }
+  *out = __float2bfloat16(y + a.D[h] * x);
+}
+
+}  // namespace ssd
+
+void ssd_decode_launch(const SsdDecodeArgs& a, cudaStream_t st) {
+  if (a.B == 0) return;
+  if (a.K < 2 || a.K > 9) throw std::runtime_error("b200.ssd_decode: conv kernel 2..9");
+  if (a.H % a.G != 0) throw std::runtime_error("b200.ssd_decode: heads must be a multiple of groups");
+  dim3 grid(a.B, a.H);
+  if (a.N == 128 && a.P == 64) launch_pdl(ssd::ssd_decode_kernel<128, 64>, grid, dim3(64), 0, st, a);
+  else if (a.N == 64 && a.P == 64) launch_pdl(ssd::ssd_decode_kernel<64, 64>, grid, dim3(64), 0, st, a);
+  else if (a.N == 128 && a.P == 128) launch_pdl(ssd::ssd_decode_kernel<128, 128>, grid, dim3(128), 0, st, a);
+  else if (a.N == 16 && a.P == 32) launch_pdl(ssd::ssd_decode_kernel<16, 32>, grid, dim3(32), 0, st, a);
+  else throw std::runtime_error("b200.ssd_decode: (state, head_dim) in {(128, 64), (64, 64), (128, 128), (16, 32)}");
+}
+
+}  // namespace b200

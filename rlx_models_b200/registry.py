@@ -78,6 +78,14 @@ def _qwen35(cfg, weights, device, tp_rank, tp_size, comm):
     return Qwen35LM(cfg, weights, device=device)
 
 
+@register("mamba2", "bamba")
+def _ssm(cfg, weights, device, tp_rank, tp_size, comm):
+    from .models.mamba2 import SSMHybridLM
+    if tp_size != 1:
+        raise NotImplementedError("Mamba-2 models run on one GPU per replica")
+    return SSMHybridLM(cfg, weights, device=device)
+
+
 @register("lfm2")
 def _lfm2(cfg, weights, device, tp_rank, tp_size, comm):
     from .models.lfm2 import Lfm2LM
@@ -96,6 +104,9 @@ def build_model(cfg: DecoderConfig, weights=None, *, device="cuda", tp_rank=0, t
     elif weights is None and cfg.model_type in ("qwen3_5_text", "qwen3_5", "qwen3_5_moe_text", "qwen3_5_moe",
                                                 "qwen3_next"):
         from .models.qwen35 import random_weights
+        weights = random_weights(cfg, seed, device)
+    elif weights is None and cfg.model_type in ("mamba2", "bamba"):
+        from .models.mamba2 import random_weights
         weights = random_weights(cfg, seed, device)
     elif weights is None and cfg.model_type == "lfm2":
         from .models.lfm2 import random_weights
