@@ -186,6 +186,8 @@ class MoEDecoderLM(DecoderLM):
             L.w_gu = L.wd = None
             L.sinks = g(p + "self_attn.sinks").to(dev, torch.float32).contiguous() if c.attn_sinks else None
             L.window = c.layer_window(i)
+            L.inv_freq, L.rope_mult = self.inv_freq, self.rope_mult
+            L.ln_post_attn = L.ln_post_ffn = None
             self.layers.append(L)
             if not c.is_moe_layer(i):  # dense layer of a mostly-MoE model (glm4_moe's first layers)
                 L.w_gu = dv(ops.interleave_gate_up(g(p + "mlp.gate_proj.weight").to(dev),
