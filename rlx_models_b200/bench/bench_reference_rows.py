@@ -14,6 +14,11 @@ bf16). Rows (reference value, hardware in parentheses):
      62 / 91 / 91 (M4 Pro)
   5. prefix-cache TTFT: time to the first token of a 2048-token prompt, cold
      vs with the 2048-token prefix cached: 9.2 s -> 1.2 s (M4 Pro)
+  7. long-context retrieval at 16k tokens of context: retrieval ~25 ms, decode
+     ~59 tok/s (M4 Pro, HNSW KV store); here single-stream decode at 16k with
+     KV-block retrieval (64 top-k + 16 recent + 1 sink blocks) and with full
+     attention, plus the device time of one retrieval selection over all
+     layers
 
 Each decode row times ``--tokens`` generated tokens per sequence with CUDA
 events around ``LLMEngine.generate`` (decode steps run as CUDA graphs),
@@ -31,7 +36,7 @@ import time
 import torch
 
 REF = {"single_stream_tok_s": 51.3, "batched_tok_s": {8: 62.0, 16: 91.0, 32: 91.0},
-       "ttft_2048_cold_s": 9.2, "ttft_2048_cached_s": 1.2}
+       "ttft_2048_cold_s": 9.2, "ttft_2048_cached_s": 1.2, "retrieval_16k_ms": 25.0, "decode_16k_tok_s": 59.0}
 
 
 def build_gguf(path: str, seed: int = 0):
@@ -54,6 +59,54 @@ def build_gguf(path: str, seed: int = 0):
         gw.add_tensor(hf_to_gguf_name(name), t.float(), kind)
     gw.write()
     return cfg
+
+
+def long_context_rows(gguf: str, tokens: int, ctx: int = 16384) -> list[dict]:
+    """Row 7: single-stream decode at ``ctx`` tokens of context with and
+    without KV-block retrieval, and one retrieval selection's device time."""
+    from ..api import load
+    from ..runtime.engine import EngineConfig, SamplingParams
+    out = []
+    g = torch.Generator().manual_seed(7)
+    for kvr in ({"topk_blocks": 64, "window_blocks": 16, "sink_blocks": 1}, None):
+        llm = load(gguf, device="cuda", engine_config=EngineConfig(max_num_seqs=2, max_model_len=ctx + tokens + 32,
+                                                                    kv_memory_gb=8, prefix_caching=False,
+                                                                    kv_retrieval=kvr, chunk_size=4096))
+        eng = llm.engine
+        V = llm.config.vocab_size
+        eng.capture_graphs(sizes=[1])
+        prompt = torch.randint(0, V, (ctx,), generator=g).tolist()
+        eng.generate([prompt[:64]], SamplingParams(max_new_tokens=4, ignore_eos=True))  # warm-up
+        torch.cuda.synchronize()
+        o = eng.generate([prompt], SamplingParams(max_new_tokens=tokens, ignore_eos=True))[0]
+        torch.cuda.synchronize()
+        name = "with KV-block retrieval" if kvr else "full attention"
+        out.append({"row": f"decode tok/s at {ctx} tokens of context, {name}", "value": round(1.0 / o.tpot, 1),
+                    "reference": REF["decode_16k_tok_s"], "ratio": round(1.0 / o.tpot / REF["decode_16k_tok_s"], 1)})
+        if kvr:
+            m = llm.model
+            r = m.retrieval
+            W = eng.max_blocks_per_seq
+            tables = torch.arange(W, dtype=torch.int32, device="cuda")[None]
+            ctx_t = torch.tensor([ctx], dtype=torch.int32, device="cuda")
+            q = torch.randn(1, m.hq, m.D, device="cuda").bfloat16()
+            for _ in range(3):
+                for layer in range(len(m.layers)):
+                    r.select(layer, q, tables, ctx_t)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record()
+            for layer in range(len(m.layers)):
+                r.select(layer, q, tables, ctx_t)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1)
+            out.append({"row": f"retrieval selection at {ctx} tokens, all {len(m.layers)} layers (ms)",
+                        "value": round(ms, 3), "reference": REF["retrieval_16k_ms"],
+                        "ratio": round(REF["retrieval_16k_ms"] / ms, 1)})
+        del llm, eng
+        torch.cuda.empty_cache()
+    return out
 
 
 def main(argv=None):
@@ -109,6 +162,7 @@ def main(argv=None):
                  "ratio": round(REF["ttft_2048_cold_s"] / cold, 1)})
     rows.append({"row": "TTFT, 2048-token prefix cached (s)", "value": round(cached, 4),
                  "reference": REF["ttft_2048_cached_s"], "ratio": round(REF["ttft_2048_cached_s"] / cached, 1)})
+    rows += long_context_rows(gguf, a.tokens)
     meta = {"device": torch.cuda.get_device_name(0), "gguf_build_s": round(t_build, 1),
             "note": "reference values are the reference's published Apple M4 Pro numbers; ratio > 1 = faster here"}
     for r in rows:

@@ -165,6 +165,14 @@ class DecoderLM:
                                        else (self.inv_freq, self.rope_mult))
             self.layers.append(L)
 
+    def enable_kv_retrieval(self, num_blocks: int, **kw):
+        """Long-context decode over a bounded set of retrieved KV blocks
+        (runtime/kv_retrieval.py); kw: topk_blocks, window_blocks, sink_blocks."""
+        from ..runtime.kv_retrieval import KVRetrieval
+        if any(L.window for L in self.layers) or any(L.sinks is not None for L in self.layers):
+            raise NotImplementedError("KV retrieval is for full-attention layers without sinks")
+        self.retrieval = KVRetrieval(self.cfg.num_hidden_layers, num_blocks, self.hkv, self.D, self.device, **kw)
+
     def make_kv_cache(self, num_blocks: int) -> PagedKVCache:
         return PagedKVCache(self.cfg.num_hidden_layers, num_blocks, self.hkv, self.D, self.device)
 
@@ -183,8 +191,14 @@ class DecoderLM:
                          k_cache=kc, v_cache=vc)
         o = torch.empty_like(q)
         nd = fb.num_decode
+        retrieval = getattr(self, "retrieval", None)
+        if retrieval is not None:
+            retrieval.update(i, kc, fb.slots)
         if nd > 0:
-            ops.decode_attention(q[:nd], kc, vc, fb.dec_block_tables, fb.dec_ctx_lens, scale=self.scale,
+            tables, ctx = fb.dec_block_tables, fb.dec_ctx_lens
+            if retrieval is not None:
+                tables, ctx = retrieval.select(i, q[:nd], tables, ctx)
+            ops.decode_attention(q[:nd], kc, vc, tables, ctx, scale=self.scale,
                                  sinks=L.sinks, window=L.window, out=o[:nd], softcap=self.cfg.attn_softcap)
         if T > nd:
             ops.prefill_attention(q[nd:], kc, vc, fb.pre_block_tables, fb.pre_ctx_lens, fb.pre_cu_q,

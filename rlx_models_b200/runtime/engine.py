@@ -90,6 +90,9 @@ class EngineConfig:
     cuda_graphs: bool = True
     graph_batch_sizes: tuple = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)
     eos_token_id: int = -1
+    # long-context decode over retrieved KV blocks, e.g. {"topk_blocks": 64,
+    # "window_blocks": 16, "sink_blocks": 1} (runtime/kv_retrieval.py); None = full attention
+    kv_retrieval: dict | None = None
 
 
 @dataclass
@@ -151,6 +154,10 @@ class LLMEngine:
             self.slot_of: dict[int, int] = {}
         else:
             self.kv = model.make_kv_cache(nb + 1)
+        if cfg.kv_retrieval:
+            if not hasattr(model, "enable_kv_retrieval"):
+                raise NotImplementedError(f"{type(model).__name__} has no KV retrieval")
+            model.enable_kv_retrieval(nb + 1, **cfg.kv_retrieval)
         self.dummy_block = nb  # never handed out by the scheduler; padding rows write here
         self.sched = _runtime.Scheduler(nb, cfg.max_num_seqs, cfg.max_batched_tokens, self.max_blocks_per_seq,
                                         cfg.prefix_caching, cfg.chunk_size)
