@@ -246,6 +246,43 @@ void ssd_decode(const Tensor& proj, int64_t xbc_off, int64_t dt_off, const Tenso
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void kv_select(const Tensor& q, const Tensor& summ, const Tensor& tables, const Tensor& ctx, Tensor& sel,
+               Tensor& sel_ctx, int64_t topk, int64_t window, int64_t sink) {
+  check_cuda(q, "q");
+  TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3, "b200.kv_select: q [B, Hq, D]");
+  TORCH_CHECK(summ.scalar_type() == at::kBFloat16 && summ.is_contiguous() && summ.dim() == 3 &&
+                  summ.size(2) == q.size(2),
+              "b200.kv_select: summ [blocks, Hkv, D] bf16");
+  TORCH_CHECK(tables.scalar_type() == at::kInt && tables.dim() == 2 && tables.is_contiguous() &&
+                  tables.size(0) == q.size(0),
+              "b200.kv_select: tables [B, W] int32");
+  TORCH_CHECK(ctx.scalar_type() == at::kInt && ctx.numel() == q.size(0), "b200.kv_select: ctx [B] int32");
+  const int64_t budget = topk + window + sink;
+  TORCH_CHECK(sel.scalar_type() == at::kInt && sel.is_contiguous() && sel.size(0) == q.size(0) &&
+                  sel.size(1) == budget && sel_ctx.scalar_type() == at::kInt && sel_ctx.numel() == q.size(0),
+              "b200.kv_select: sel [B, budget] / sel_ctx [B] int32");
+  TORCH_CHECK(q.size(1) % summ.size(1) == 0, "b200.kv_select: Hq must be a multiple of Hkv");
+  c10::cuda::CUDAGuard g(q.device());
+  b200::KvSelectArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.summ = reinterpret_cast<const __nv_bfloat16*>(summ.data_ptr());
+  a.tables = tables.data_ptr<int32_t>();
+  a.ctx = ctx.data_ptr<int32_t>();
+  a.sel = sel.data_ptr<int32_t>();
+  a.sel_ctx = sel_ctx.data_ptr<int32_t>();
+  a.B = (int)q.size(0);
+  a.W = (int)tables.size(1);
+  a.Hq = (int)q.size(1);
+  a.Hkv = (int)summ.size(1);
+  a.D = (int)q.size(2);
+  a.topk = (int)topk;
+  a.window = (int)window;
+  a.sink = (int)sink;
+  a.budget = (int)budget;
+  b200::kv_select_launch(a, cur_stream(q));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void embedding(const Tensor& ids, const Tensor& table, Tensor& out) {
   check_cuda(ids, "ids");
   TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "b200.embedding: int32 ids");
@@ -1048,6 +1085,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_decode", &gdn_decode);
   m.def("shortconv_decode", &shortconv_decode);
   m.def("ssd_decode", &ssd_decode);
+  m.def("kv_select", &kv_select);
   m.def("gemm_push_shards", &gemm_push_shards);
   m.def("shard_push_add", &shard_push_add);
   m.def("peer_barrier", &peer_barrier);

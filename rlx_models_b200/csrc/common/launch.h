@@ -291,6 +291,19 @@ struct SsdDecodeArgs {
 };
 void ssd_decode_launch(const SsdDecodeArgs& a, cudaStream_t st);
 
+// KV-block retrieval selection (attention/kv_select.cu)
+struct KvSelectArgs {
+  const __nv_bfloat16* q;     // [B, Hq, D]
+  const __nv_bfloat16* summ;  // [num_blocks, Hkv, D] block key summaries of the layer
+  const int32_t* tables;      // [B, W]
+  const int32_t* ctx;         // [B]
+  int32_t* sel;               // [B, budget] selected block ids in block order
+  int32_t* sel_ctx;           // [B]
+  int B, W, Hq, Hkv, D;
+  int topk, window, sink, budget;
+};
+void kv_select_launch(const KvSelectArgs& a, cudaStream_t st);
+
 // ---------------- training ----------------
 void adamw_launch(float* master, const void* grad, bool grad_f32, float* m, float* v, void* param_out, int64_t n,
                   float lr, float b1, float b2, float eps, float wd, int64_t step, const float* scale_ptr,

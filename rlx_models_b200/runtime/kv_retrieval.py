@@ -56,6 +56,21 @@ class KVRetrieval:
         Hkv, D = self.summ.shape[2], self.summ.shape[3]
         if self.budget >= W:
             return tables, ctx
+        if q.is_cuda:  # one kernel: scores, radix top-k, ordered table and context length
+            from .. import ops
+            from ..ops._ext import ext
+            sel = torch.empty(B, self.budget, dtype=torch.int32, device=q.device)
+            sctx = torch.empty(B, dtype=torch.int32, device=q.device)
+            ext().kv_select(q.contiguous(), self.summ[layer], tables.contiguous(), ctx, sel, sctx, self.topk,
+                            self.window, self.sink)
+            ops._count(1)
+            return sel, sctx
+        return self.select_reference(layer, q, tables, ctx)
+
+    def select_reference(self, layer: int, q: torch.Tensor, tables: torch.Tensor, ctx: torch.Tensor):
+        """torch restatement of the selection kernel (any device)."""
+        B, W = tables.shape
+        Hkv, D = self.summ.shape[2], self.summ.shape[3]
         s = self.summ[layer].index_select(0, tables.reshape(-1).long()).view(B, W, Hkv, D)
         qg = q.view(B, Hkv, -1, D).sum(2)  # sum over the query heads of each KV head
         score = torch.einsum("bhd,bwhd->bw", qg.float(), s.float())

@@ -56,3 +56,21 @@ def test_engine_with_retrieval_matches_full_within_budget(cuda):
         outs.append([o.token_ids for o in llm.generate(prompts, sp)])
         assert llm.engine.stats["graph_steps"] > 0
     assert outs[0] == outs[1]  # 7 blocks of budget cover these contexts (<= 6 blocks)
+
+
+@pytest.mark.parametrize("Hkv,D,W,lens", [(8, 128, 700, [700 * 16 - 5, 3000, 40, 1]), (2, 64, 90, [90 * 16, 500])])
+def test_select_kernel_matches_reference(cuda, Hkv, D, W, lens):
+    g = torch.Generator().manual_seed(W)
+    B, G, nb = len(lens), 4, W + 20
+    r = KVRetrieval(1, nb, Hkv, D, cuda, topk_blocks=24, window_blocks=6, sink_blocks=2)
+    r.summ[0] = torch.randn(nb, Hkv, D, generator=g).bfloat16().to(cuda)
+    q = torch.randn(B, Hkv * G, D, generator=g).bfloat16().to(cuda)
+    tables = torch.stack([torch.randperm(nb, generator=g)[:W] for _ in range(B)]).int().to(cuda)
+    ctx = torch.tensor(lens, dtype=torch.int32, device=cuda)
+    sel, sctx = r.select(0, q, tables, ctx)
+    ref_sel, ref_ctx = r.select_reference(0, q, tables, ctx)
+    torch.cuda.synchronize()
+    assert torch.equal(sctx, ref_ctx)
+    for b in range(B):
+        n = (int(sctx[b]) + 15) // 16
+        assert sel[b, :n].tolist() == ref_sel[b, :n].tolist(), b
