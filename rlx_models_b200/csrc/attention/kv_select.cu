@@ -5,8 +5,10 @@
 // radix select on the score bits, and writes the selected block ids in block
 // order plus the matching context length for the paged decode kernel.
 //
-// Scores live in shared memory (one float per block of the table), so a
-// sequence of W blocks needs 4 W bytes (W <= 49152, i.e. 786k tokens).
+// Two launches: kv_score_kernel spreads the block scores over many CTAs
+// (a GEMV-like pass over the summaries at HBM bandwidth), kv_select_kernel
+// (one CTA per sequence) stages them in shared memory (4 W bytes, W <= 49152
+// blocks, i.e. 786k tokens) for the selection.
 #include <cuda_bf16.h>
 
 #include <cstdint>
@@ -55,13 +57,13 @@ __device__ __forceinline__ int block_scan(int v, int* tot, int* warp_sums) {
   return before;
 }
 
-__global__ void __launch_bounds__(kThreads) kv_select_kernel(KvSelectArgs a) {
-  extern __shared__ float sc[];  // [W] scores
+// Block scores: grid (B, ceil(W / kBlocksPerCta)); each warp scores blocks of
+// the table (its query-sum vector staged in shared memory); blocks past the
+// context get -inf.
+constexpr int kBlocksPerCta = 32;
+
+__global__ void __launch_bounds__(kThreads) kv_score_kernel(KvSelectArgs a) {
   __shared__ float qs[kMaxQ];
-  __shared__ unsigned hist[256];
-  __shared__ int warp_sums[kThreads / 32];
-  __shared__ uint32_t s_prefix;
-  __shared__ int s_need;
   pdl_wait();
   pdl_trigger();
   const int b = blockIdx.x, t = threadIdx.x, lane = t & 31, warp = t >> 5;
@@ -74,13 +76,13 @@ __global__ void __launch_bounds__(kThreads) kv_select_kernel(KvSelectArgs a) {
     qs[i] = s;
   }
   __syncthreads();
-  const int ctx = a.ctx[b];
-  const int nblk = (ctx + 15) / 16;
+  const int nblk = (a.ctx[b] + 15) / 16;
   const int32_t* tab = a.tables + (int64_t)b * a.W;
-  // 1. scores of the candidate blocks (kept and invalid blocks are classified below)
-  for (int w = warp; w < a.W; w += kThreads / 32) {
-    float s = 0.f;
+  const int w0 = blockIdx.y * kBlocksPerCta;
+  for (int w = w0 + warp; w < min(a.W, w0 + kBlocksPerCta); w += kThreads / 32) {
+    float s = -INFINITY;
     if (w < nblk) {
+      s = 0.f;
       const __nv_bfloat16* sm = a.summ + (int64_t)tab[w] * HD;
       for (int i = lane * 8; i < HD; i += 256) {
         const uint4 v = *reinterpret_cast<const uint4*>(sm + i);
@@ -94,8 +96,43 @@ __global__ void __launch_bounds__(kThreads) kv_select_kernel(KvSelectArgs a) {
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
     }
-    if (lane == 0) sc[w] = s;
+    if (lane == 0) a.scores[(int64_t)b * a.W + w] = s;
   }
+}
+
+// Block key summaries of the blocks written this step: summ[blk] = mean of
+// the block's 16 key rows per KV head (grid: one CTA per token of the step;
+// tokens of the same block write the same values).
+__global__ void kv_summary_kernel(const __nv_bfloat16* __restrict__ k_cache, const int64_t* __restrict__ slots,
+                                  __nv_bfloat16* __restrict__ summ, int Hkv, int D) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t blk = slots[blockIdx.x] >> 4;
+  const __nv_bfloat16* src = k_cache + blk * Hkv * 16 * D;
+  __nv_bfloat16* dst = summ + blk * Hkv * D;
+  for (int i = threadIdx.x; i < Hkv * D; i += blockDim.x) {
+    const int h = i / D, d = i % D;
+    float s = 0.f;
+#pragma unroll
+    for (int r = 0; r < 16; ++r) s += __bfloat162float(src[(int64_t)(h * 16 + r) * D + d]);
+    dst[i] = __float2bfloat16(s * (1.f / 16.f));
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) kv_select_kernel(KvSelectArgs a) {
+  extern __shared__ float sc[];  // [W] scores
+  __shared__ unsigned hist[256];
+  __shared__ int warp_sums[kThreads / 32];
+  __shared__ uint32_t s_prefix;
+  __shared__ int s_need;
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x, t = threadIdx.x;
+  const int ctx = a.ctx[b];
+  const int nblk = (ctx + 15) / 16;
+  const int32_t* tab = a.tables + (int64_t)b * a.W;
+  // 1. the scores from kv_score_kernel
+  for (int w = t; w < nblk; w += kThreads) sc[w] = a.scores[(int64_t)b * a.W + w];
   __syncthreads();
   auto kept = [&](int w) { return w < nblk && (w < a.sink || w >= nblk - a.window); };
   auto cand = [&](int w) { return w < nblk && !(w < a.sink || w >= nblk - a.window); };
@@ -183,7 +220,17 @@ void kv_select_launch(const KvSelectArgs& a, cudaStream_t st) {
     cudaFuncSetAttribute(kvsel::kv_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 196608);
     once_smem = (int)smem;
   }
+  launch_pdl(kvsel::kv_score_kernel, dim3(a.B, (a.W + kvsel::kBlocksPerCta - 1) / kvsel::kBlocksPerCta),
+             dim3(kvsel::kThreads), 0, st, a);
   launch_pdl(kvsel::kv_select_kernel, dim3(a.B), dim3(kvsel::kThreads), smem, st, a);
+}
+
+void kv_summary_launch(const void* k_cache, const int64_t* slots, int64_t T, void* summ, int Hkv, int D,
+                       cudaStream_t st) {
+  if (T == 0) return;
+  launch_pdl(kvsel::kv_summary_kernel, dim3((unsigned)T), dim3(128), 0, st,
+             reinterpret_cast<const __nv_bfloat16*>(k_cache), slots, reinterpret_cast<__nv_bfloat16*>(summ), Hkv,
+             D);
 }
 
 }  // namespace b200

@@ -246,8 +246,23 @@ void ssd_decode(const Tensor& proj, int64_t xbc_off, int64_t dt_off, const Tenso
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void kv_select(const Tensor& q, const Tensor& summ, const Tensor& tables, const Tensor& ctx, Tensor& sel,
-               Tensor& sel_ctx, int64_t topk, int64_t window, int64_t sink) {
+void kv_summary(const Tensor& k_cache, const Tensor& slots, Tensor& summ) {
+  check_cuda(k_cache, "k_cache");
+  TORCH_CHECK(k_cache.scalar_type() == at::kBFloat16 && k_cache.is_contiguous() && k_cache.dim() == 4 &&
+                  k_cache.size(2) == 16,
+              "b200.kv_summary: k_cache [blocks, Hkv, 16, D] bf16");
+  TORCH_CHECK(summ.scalar_type() == at::kBFloat16 && summ.is_contiguous() && summ.size(0) >= k_cache.size(0) &&
+                  summ.size(1) == k_cache.size(1) && summ.size(2) == k_cache.size(3),
+              "b200.kv_summary: summ [blocks, Hkv, D] bf16");
+  TORCH_CHECK(slots.scalar_type() == at::kLong && slots.is_contiguous(), "b200.kv_summary: slots int64");
+  c10::cuda::CUDAGuard g(k_cache.device());
+  b200::kv_summary_launch(k_cache.data_ptr(), slots.data_ptr<int64_t>(), slots.numel(), summ.data_ptr(),
+                          (int)k_cache.size(1), (int)k_cache.size(3), cur_stream(k_cache));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void kv_select(const Tensor& q, const Tensor& summ, const Tensor& tables, const Tensor& ctx, Tensor& scores,
+               Tensor& sel, Tensor& sel_ctx, int64_t topk, int64_t window, int64_t sink) {
   check_cuda(q, "q");
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && q.is_contiguous() && q.dim() == 3, "b200.kv_select: q [B, Hq, D]");
   TORCH_CHECK(summ.scalar_type() == at::kBFloat16 && summ.is_contiguous() && summ.dim() == 3 &&
@@ -268,6 +283,9 @@ void kv_select(const Tensor& q, const Tensor& summ, const Tensor& tables, const 
   a.summ = reinterpret_cast<const __nv_bfloat16*>(summ.data_ptr());
   a.tables = tables.data_ptr<int32_t>();
   a.ctx = ctx.data_ptr<int32_t>();
+  TORCH_CHECK(scores.scalar_type() == at::kFloat && scores.is_contiguous() && scores.numel() >= tables.numel(),
+              "b200.kv_select: scores workspace [B, W] fp32");
+  a.scores = scores.data_ptr<float>();
   a.sel = sel.data_ptr<int32_t>();
   a.sel_ctx = sel_ctx.data_ptr<int32_t>();
   a.B = (int)q.size(0);
@@ -1086,6 +1104,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("shortconv_decode", &shortconv_decode);
   m.def("ssd_decode", &ssd_decode);
   m.def("kv_select", &kv_select);
+  m.def("kv_summary", &kv_summary);
   m.def("gemm_push_shards", &gemm_push_shards);
   m.def("shard_push_add", &shard_push_add);
   m.def("peer_barrier", &peer_barrier);

@@ -297,12 +297,15 @@ struct KvSelectArgs {
   const __nv_bfloat16* summ;  // [num_blocks, Hkv, D] block key summaries of the layer
   const int32_t* tables;      // [B, W]
   const int32_t* ctx;         // [B]
+  float* scores;              // [B, W] workspace
   int32_t* sel;               // [B, budget] selected block ids in block order
   int32_t* sel_ctx;           // [B]
   int B, W, Hq, Hkv, D;
   int topk, window, sink, budget;
 };
 void kv_select_launch(const KvSelectArgs& a, cudaStream_t st);
+void kv_summary_launch(const void* k_cache, const int64_t* slots, int64_t T, void* summ, int Hkv, int D,
+                       cudaStream_t st);
 
 // ---------------- training ----------------
 void adamw_launch(float* master, const void* grad, bool grad_f32, float* m, float* v, void* param_out, int64_t n,

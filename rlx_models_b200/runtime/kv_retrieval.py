@@ -43,9 +43,13 @@ class KVRetrieval:
     def update(self, layer: int, k_cache: torch.Tensor, slots: torch.Tensor):
         """Refresh the summaries of the blocks written this step (k_cache
         [blocks, Hkv, 16, D]; slots [T] token cache slots)."""
+        if k_cache.is_cuda:
+            from .. import ops
+            from ..ops._ext import ext
+            ext().kv_summary(k_cache, slots.contiguous(), self.summ[layer])
+            ops._count(1)
+            return
         blk = torch.div(slots, BLOCK_SIZE, rounding_mode="floor")
-        if blk.numel() > 256:  # prefill chunks: each block once (eager, so a dynamic shape is fine)
-            blk = torch.unique(blk)
         self.summ[layer].index_copy_(0, blk, k_cache.index_select(0, blk).float().mean(2).to(torch.bfloat16))
 
     def select(self, layer: int, q: torch.Tensor, tables: torch.Tensor, ctx: torch.Tensor):
@@ -56,14 +60,15 @@ class KVRetrieval:
         Hkv, D = self.summ.shape[2], self.summ.shape[3]
         if self.budget >= W:
             return tables, ctx
-        if q.is_cuda:  # one kernel: scores, radix top-k, ordered table and context length
+        if q.is_cuda:  # block scores (many CTAs), then radix top-k + ordered table + context length
             from .. import ops
             from ..ops._ext import ext
             sel = torch.empty(B, self.budget, dtype=torch.int32, device=q.device)
             sctx = torch.empty(B, dtype=torch.int32, device=q.device)
-            ext().kv_select(q.contiguous(), self.summ[layer], tables.contiguous(), ctx, sel, sctx, self.topk,
-                            self.window, self.sink)
-            ops._count(1)
+            scores = torch.empty(B, W, dtype=torch.float32, device=q.device)
+            ext().kv_select(q.contiguous(), self.summ[layer], tables.contiguous(), ctx, scores, sel, sctx,
+                            self.topk, self.window, self.sink)
+            ops._count(2)
             return sel, sctx
         return self.select_reference(layer, q, tables, ctx)
 
