@@ -69,8 +69,9 @@ def long_context_rows(gguf: str, tokens: int, ctx: int = 16384) -> list[dict]:
     out = []
     g = torch.Generator().manual_seed(7)
     for kvr in ({"topk_blocks": 64, "window_blocks": 16, "sink_blocks": 1}, None):
+        kv_gb = max(8.0, 2.5 * ctx * 28 * 8 * 128 * 4 / 2 ** 30)
         llm = load(gguf, device="cuda", engine_config=EngineConfig(max_num_seqs=2, max_model_len=ctx + tokens + 32,
-                                                                    kv_memory_gb=8, prefix_caching=False,
+                                                                    kv_memory_gb=kv_gb, prefix_caching=False,
                                                                     kv_retrieval=kvr, chunk_size=4096))
         eng = llm.engine
         V = llm.config.vocab_size
@@ -112,6 +113,8 @@ def long_context_rows(gguf: str, tokens: int, ctx: int = 16384) -> list[dict]:
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=128)
+    ap.add_argument("--long-ctx", type=int, nargs="*", default=[16384],
+                    help="contexts for the retrieval rows (row 7 is quoted at 16384)")
     ap.add_argument("--json", default=None)
     a = ap.parse_args(argv)
     from ..api import load
@@ -162,7 +165,8 @@ def main(argv=None):
                  "ratio": round(REF["ttft_2048_cold_s"] / cold, 1)})
     rows.append({"row": "TTFT, 2048-token prefix cached (s)", "value": round(cached, 4),
                  "reference": REF["ttft_2048_cached_s"], "ratio": round(REF["ttft_2048_cached_s"] / cached, 1)})
-    rows += long_context_rows(gguf, a.tokens)
+    for n in a.long_ctx:
+        rows += long_context_rows(gguf, a.tokens, n)
     meta = {"device": torch.cuda.get_device_name(0), "gguf_build_s": round(t_build, 1),
             "note": "reference values are the reference's published Apple M4 Pro numbers; ratio > 1 = faster here"}
     for r in rows:
