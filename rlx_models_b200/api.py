@@ -198,6 +198,10 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
                 config = Lfm2Config.from_file(path)
             elif config is None and is_ssm_config(path):  # Mamba-2 (SSD) and its attention hybrids
                 config = SSMConfig.from_file(path)
+            else:
+                from .models.mamba1 import Mamba1Config, is_mamba1_config
+                if config is None and is_mamba1_config(path):  # Mamba-1 selective scan, Jamba
+                    config = Mamba1Config.from_file(path)
         cfg = config or C.DecoderConfig.from_file(path)
         from .weights.mlx import MLXWeights
         if MLXWeights.is_mlx_dir(path):  # MLX affine group-quantised checkpoint

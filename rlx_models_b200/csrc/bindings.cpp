@@ -301,6 +301,90 @@ void kv_select(const Tensor& q, const Tensor& summ, const Tensor& tables, const 
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+static b200::MambaScanArgs mamba_args(const Tensor& cu, const Tensor& slots, const Tensor& positions, int64_t Di,
+                                      int64_t num_slots) {
+  TORCH_CHECK(cu.scalar_type() == at::kInt && cu.is_contiguous() && cu.dim() == 1 && cu.numel() >= 1,
+              "b200.mamba: cu int32 [nseq + 1]");
+  TORCH_CHECK(slots.scalar_type() == at::kLong && slots.is_contiguous() && slots.numel() == cu.numel() - 1,
+              "b200.mamba: slots int64 [nseq]");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && positions.is_contiguous(), "b200.mamba: positions int32");
+  b200::MambaScanArgs a{};
+  a.cu = cu.data_ptr<int32_t>();
+  a.slots = slots.data_ptr<int64_t>();
+  a.positions = positions.data_ptr<int32_t>();
+  a.nseq = (int)(cu.numel() - 1);
+  a.Di = (int)Di;
+  a.num_slots = num_slots;
+  return a;
+}
+
+void mamba_conv(const Tensor& cu, const Tensor& slots, const Tensor& positions, const Tensor& x_raw,
+                const Tensor& conv_w, const optional<Tensor>& conv_b, Tensor& conv_state, Tensor& x_out) {
+  check_cuda(x_raw, "x_raw");
+  const int64_t Di = conv_w.size(0), K = conv_w.size(1);
+  TORCH_CHECK(x_raw.scalar_type() == at::kBFloat16 && x_raw.dim() == 2 && x_raw.stride(1) == 1 &&
+                  x_raw.size(1) >= Di && x_raw.size(0) == positions.numel(),
+              "b200.mamba_conv: x_raw [T, >= Di] bf16");
+  TORCH_CHECK(conv_w.scalar_type() == at::kFloat && conv_w.is_contiguous(), "b200.mamba_conv: conv_w [Di, K] fp32");
+  if (conv_b.has_value() && conv_b->defined())
+    TORCH_CHECK(conv_b->scalar_type() == at::kFloat && conv_b->numel() == Di, "b200.mamba_conv: conv_b");
+  TORCH_CHECK(conv_state.scalar_type() == at::kBFloat16 && conv_state.is_contiguous() && conv_state.dim() == 3 &&
+                  conv_state.size(1) == Di && conv_state.size(2) == K - 1,
+              "b200.mamba_conv: conv_state [slots, Di, K-1] bf16");
+  TORCH_CHECK(x_out.scalar_type() == at::kBFloat16 && x_out.is_contiguous() && x_out.size(0) == x_raw.size(0) &&
+                  x_out.size(1) == Di,
+              "b200.mamba_conv: x_out [T, Di] bf16");
+  c10::cuda::CUDAGuard g(x_raw.device());
+  auto a = mamba_args(cu, slots, positions, Di, conv_state.size(0));
+  a.x_raw = reinterpret_cast<const __nv_bfloat16*>(x_raw.data_ptr());
+  a.ld_raw = x_raw.stride(0);
+  a.conv_w = conv_w.data_ptr<float>();
+  a.conv_b = (conv_b.has_value() && conv_b->defined()) ? conv_b->data_ptr<float>() : nullptr;
+  a.conv_state = reinterpret_cast<__nv_bfloat16*>(conv_state.data_ptr());
+  a.x_out = reinterpret_cast<__nv_bfloat16*>(x_out.data_ptr());
+  a.K = (int)K;
+  b200::mamba_conv_launch(a, cur_stream(x_raw));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void mamba_scan(const Tensor& cu, const Tensor& slots, const Tensor& positions, const Tensor& x, const Tensor& dt,
+                const Tensor& dt_bias, const Tensor& Bc, int64_t c_off, const Tensor& A_log, const Tensor& D,
+                const Tensor& z, Tensor& ssm_state, Tensor& y) {
+  check_cuda(x, "x");
+  const int64_t T = x.size(0), Di = x.size(1), N = A_log.size(1);
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "b200.mamba_scan: x [T, Di] bf16");
+  for (const Tensor* t : {&dt, &Bc, &z})
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->stride(1) == 1 && t->size(0) == T,
+                "b200.mamba_scan: dt / Bc / z [T, *] bf16 with unit inner stride");
+  TORCH_CHECK(dt.size(1) >= Di && z.size(1) >= Di && Bc.size(1) >= c_off + N, "b200.mamba_scan: widths");
+  TORCH_CHECK(A_log.scalar_type() == at::kFloat && A_log.is_contiguous() && A_log.size(0) == Di &&
+                  dt_bias.scalar_type() == at::kFloat && dt_bias.numel() == Di && D.scalar_type() == at::kFloat &&
+                  D.numel() == Di,
+              "b200.mamba_scan: A_log [Di, N] / dt_bias / D fp32");
+  TORCH_CHECK(ssm_state.scalar_type() == at::kFloat && ssm_state.is_contiguous() && ssm_state.dim() == 3 &&
+                  ssm_state.size(1) == Di && ssm_state.size(2) == N,
+              "b200.mamba_scan: ssm_state [slots, Di, N] fp32");
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && y.is_contiguous() && y.sizes() == x.sizes(), "b200.mamba_scan: y");
+  c10::cuda::CUDAGuard g(x.device());
+  auto a = mamba_args(cu, slots, positions, Di, ssm_state.size(0));
+  a.x_out = reinterpret_cast<__nv_bfloat16*>(const_cast<void*>(x.data_ptr()));
+  a.dt = reinterpret_cast<const __nv_bfloat16*>(dt.data_ptr());
+  a.ld_dt = dt.stride(0);
+  a.dt_bias = dt_bias.data_ptr<float>();
+  a.Bc = reinterpret_cast<const __nv_bfloat16*>(Bc.data_ptr());
+  a.ld_bc = Bc.stride(0);
+  a.c_off = (int)c_off;
+  a.A_log = A_log.data_ptr<float>();
+  a.D = D.data_ptr<float>();
+  a.z = reinterpret_cast<const __nv_bfloat16*>(z.data_ptr());
+  a.ld_z = z.stride(0);
+  a.ssm_state = ssm_state.data_ptr<float>();
+  a.y = reinterpret_cast<__nv_bfloat16*>(y.data_ptr());
+  a.N = (int)N;
+  b200::mamba_scan_launch(a, cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void embedding(const Tensor& ids, const Tensor& table, Tensor& out) {
   check_cuda(ids, "ids");
   TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "b200.embedding: int32 ids");
@@ -1105,6 +1189,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ssd_decode", &ssd_decode);
   m.def("kv_select", &kv_select);
   m.def("kv_summary", &kv_summary);
+  m.def("mamba_conv", &mamba_conv);
+  m.def("mamba_scan", &mamba_scan);
   m.def("gemm_push_shards", &gemm_push_shards);
   m.def("shard_push_add", &shard_push_add);
   m.def("peer_barrier", &peer_barrier);

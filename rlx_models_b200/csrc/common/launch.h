@@ -291,6 +291,35 @@ struct SsdDecodeArgs {
 };
 void ssd_decode_launch(const SsdDecodeArgs& a, cudaStream_t st);
 
+// Mamba-1 selective scan (see linear_attn/gdn.cu): conv kernel then scan kernel
+struct MambaScanArgs {
+  const int32_t* cu;          // [nseq + 1] token offsets of each sequence of the step
+  const int64_t* slots;       // [nseq] state slot (out of range: no state kept)
+  const int32_t* positions;   // [T]: a sequence starting at position 0 starts from zero state
+  const __nv_bfloat16* x_raw; // [T, ld_raw] conv input (channels 0..Di)
+  int64_t ld_raw;
+  const float* conv_w;        // [Di, K]
+  const float* conv_b;        // [Di] or null
+  __nv_bfloat16* conv_state;  // [num_slots, Di, K-1]
+  __nv_bfloat16* x_out;       // [T, Di] silu(conv)
+  const __nv_bfloat16* dt;    // [T, ld_dt] dt_proj output without its bias
+  int64_t ld_dt;
+  const float* dt_bias;       // [Di]
+  const __nv_bfloat16* Bc;    // [T, ld_bc]: B at 0, C at c_off
+  int64_t ld_bc;
+  int c_off;
+  const float* A_log;         // [Di, N]
+  const float* D;             // [Di]
+  const __nv_bfloat16* z;     // [T, ld_z] gate
+  int64_t ld_z;
+  float* ssm_state;           // [num_slots, Di, N]
+  __nv_bfloat16* y;           // [T, Di]
+  int nseq, Di, N, K;
+  int64_t num_slots;
+};
+void mamba_conv_launch(const MambaScanArgs& a, cudaStream_t st);
+void mamba_scan_launch(const MambaScanArgs& a, cudaStream_t st);
+
 // KV-block retrieval selection (attention/kv_select.cu)
 struct KvSelectArgs {
   const __nv_bfloat16* q;     // [B, Hq, D]

@@ -275,3 +275,104 @@ void ssd_decode_launch(const SsdDecodeArgs& a, cudaStream_t st) {
 }
 
 }  // namespace b200
+
+// ---------------------------------------------------------------------------
+// Mamba-1 (selective scan), prefill and decode in the same two kernels. The
+// step's tokens are grouped by sequence (cu offsets, decode sequences hold one
+// token); a sequence whose first token sits at position 0 starts from zero
+// state, otherwise from its slot's saved state. One thread per channel walks
+// its sequence in time order, so a channel's conv window and SSM state stay in
+// registers across the sequence and each slot row has exactly one writer.
+//   conv:  x = silu(conv1d(x_raw) + bias)          (window of K-1 raw inputs)
+//   scan:  dt = softplus(dt_raw + dt_bias); h[n] = exp(dt A[n]) h[n] + dt B[n] x
+//          y = (sum_n h[n] C[n] + D x) * silu(z)
+// ---------------------------------------------------------------------------
+namespace b200 {
+namespace mamba1 {
+
+__global__ void mamba_conv_kernel(MambaScanArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int s = blockIdx.x;
+  const int d = blockIdx.y * blockDim.x + threadIdx.x;
+  if (d >= a.Di) return;
+  const int t0 = a.cu[s], t1 = a.cu[s + 1];
+  if (t1 <= t0) return;
+  const int64_t slot = a.slots[s];
+  const bool fresh = a.positions[t0] == 0;
+  const int W = a.K - 1;
+  const bool has_slot = slot >= 0 && slot < a.num_slots;
+  __nv_bfloat16* win = has_slot ? a.conv_state + (slot * a.Di + d) * W : nullptr;
+  float w[8], prev[8];
+  for (int i = 0; i < a.K; ++i) w[i] = a.conv_w[(int64_t)d * a.K + i];
+  for (int i = 0; i < W; ++i) prev[i] = (fresh || !has_slot) ? 0.f : __bfloat162float(win[i]);
+  const float bias = a.conv_b != nullptr ? a.conv_b[d] : 0.f;
+  for (int t = t0; t < t1; ++t) {
+    const float xin = __bfloat162float(a.x_raw[(int64_t)t * a.ld_raw + d]);
+    float acc = bias + w[W] * xin;
+    for (int i = 0; i < W; ++i) acc += w[i] * prev[i];
+    for (int i = 0; i + 1 < W; ++i) prev[i] = prev[i + 1];
+    prev[W - 1] = xin;
+    a.x_out[(int64_t)t * a.Di + d] = __float2bfloat16(acc / (1.f + __expf(-acc)));
+  }
+  if (has_slot)
+    for (int i = 0; i < W; ++i) win[i] = __float2bfloat16(prev[i]);
+}
+
+template <int N>
+__global__ void mamba_scan_kernel(MambaScanArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int s = blockIdx.x;
+  const int d = blockIdx.y * blockDim.x + threadIdx.x;
+  if (d >= a.Di) return;
+  const int t0 = a.cu[s], t1 = a.cu[s + 1];
+  if (t1 <= t0) return;
+  const int64_t slot = a.slots[s];
+  const bool has_slot = slot >= 0 && slot < a.num_slots;
+  const bool fresh = a.positions[t0] == 0 || !has_slot;
+  float* st = has_slot ? a.ssm_state + (slot * a.Di + d) * N : nullptr;
+  float h[N], A[N];
+#pragma unroll
+  for (int n = 0; n < N; ++n) {
+    h[n] = fresh ? 0.f : st[n];
+    A[n] = -__expf(a.A_log[(int64_t)d * N + n]);
+  }
+  const float Dd = a.D[d], db = a.dt_bias[d];
+  for (int t = t0; t < t1; ++t) {
+    const float x = __bfloat162float(a.x_out[(int64_t)t * a.Di + d]);
+    const float r = __bfloat162float(a.dt[(int64_t)t * a.ld_dt + d]) + db;
+    const float dt = r > 20.f ? r : log1pf(__expf(r));
+    const __nv_bfloat16* Bt = a.Bc + (int64_t)t * a.ld_bc;
+    const __nv_bfloat16* Ct = Bt + a.c_off;
+    float y = 0.f;
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+      h[n] = __expf(dt * A[n]) * h[n] + dt * __bfloat162float(Bt[n]) * x;
+      y += h[n] * __bfloat162float(Ct[n]);
+    }
+    const float z = __bfloat162float(a.z[(int64_t)t * a.ld_z + d]);
+    a.y[(int64_t)t * a.Di + d] = __float2bfloat16((y + Dd * x) * (z / (1.f + __expf(-z))));
+  }
+  if (has_slot)
+#pragma unroll
+    for (int n = 0; n < N; ++n) st[n] = h[n];
+}
+
+}  // namespace mamba1
+
+void mamba_conv_launch(const MambaScanArgs& a, cudaStream_t st) {
+  if (a.nseq == 0) return;
+  if (a.K < 2 || a.K > 8) throw std::runtime_error("b200.mamba_conv: conv kernel 2..8");
+  launch_pdl(mamba1::mamba_conv_kernel, dim3(a.nseq, (a.Di + 127) / 128), dim3(128), 0, st, a);
+}
+
+void mamba_scan_launch(const MambaScanArgs& a, cudaStream_t st) {
+  if (a.nseq == 0) return;
+  dim3 grid(a.nseq, (a.Di + 127) / 128);
+  if (a.N == 16) launch_pdl(mamba1::mamba_scan_kernel<16>, grid, dim3(128), 0, st, a);
+  else if (a.N == 8) launch_pdl(mamba1::mamba_scan_kernel<8>, grid, dim3(128), 0, st, a);
+  else throw std::runtime_error("b200.mamba_scan: state size 8 or 16");
+}
+
+}  // namespace b200

@@ -86,6 +86,14 @@ def _ssm(cfg, weights, device, tp_rank, tp_size, comm):
     return SSMHybridLM(cfg, weights, device=device)
 
 
+@register("mamba", "falcon_mamba", "jamba")
+def _mamba1(cfg, weights, device, tp_rank, tp_size, comm):
+    from .models.mamba1 import Mamba1LM
+    if tp_size != 1:
+        raise NotImplementedError("Mamba-1 models run on one GPU per replica")
+    return Mamba1LM(cfg, weights, device=device)
+
+
 @register("lfm2")
 def _lfm2(cfg, weights, device, tp_rank, tp_size, comm):
     from .models.lfm2 import Lfm2LM
@@ -107,6 +115,9 @@ def build_model(cfg: DecoderConfig, weights=None, *, device="cuda", tp_rank=0, t
         weights = random_weights(cfg, seed, device)
     elif weights is None and cfg.model_type in ("mamba2", "bamba"):
         from .models.mamba2 import random_weights
+        weights = random_weights(cfg, seed, device)
+    elif weights is None and cfg.model_type in ("mamba", "falcon_mamba", "jamba"):
+        from .models.mamba1 import random_weights
         weights = random_weights(cfg, seed, device)
     elif weights is None and cfg.model_type == "lfm2":
         from .models.lfm2 import random_weights
