@@ -463,12 +463,12 @@ class Mamba1LM:
         comm = LocalComm(c.rms_norm_eps)
         nd = fb.num_decode
         dev = self.device
-        parts = [torch.arange(nd, dtype=torch.int32, device=dev)] if nd else []
-        if fb.pre_cu_q is not None:
-            parts.append(fb.pre_cu_q + nd)
+        if fb.pre_cu_q is None:  # decode only (also under CUDA-graph capture): one token per sequence
+            cu = torch.arange(nd + 1, dtype=torch.int32, device=dev)
+        elif nd:
+            cu = torch.cat([torch.arange(nd, dtype=torch.int32, device=dev), fb.pre_cu_q + nd])
         else:
-            parts.append(torch.tensor([nd], dtype=torch.int32, device=dev))
-        cu = torch.cat(parts) if len(parts) > 1 else parts[0]
+            cu = fb.pre_cu_q.contiguous()
         slots = fb.seq_slots
         if slots is None:
             slots = torch.arange(cu.numel() - 1, dtype=torch.int32, device=dev)
