@@ -271,9 +271,13 @@ def load_embedder(model: str, *, device: str | torch.device = "cuda", pooling: s
     if path is None:
         raise FileNotFoundError(f"no local encoder checkpoint for {model!r}")
     with open(os.path.join(path, "config.json")) as f:
-        cfg = BertConfig.from_dict(json.load(f))
+        raw = json.load(f)
     tok = None
     if any(os.path.exists(os.path.join(path, f)) for f in ("tokenizer.json", "vocab.txt")):
         from transformers import AutoTokenizer
         tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
-    return Embedder(BertEncoder(cfg, WeightMap.from_dir(path), device=device), tok, pooling)
+    if raw.get("model_type") == "nomic_bert":
+        from .models.bert import NomicBertConfig, NomicBertEncoder
+        return Embedder(NomicBertEncoder(NomicBertConfig.from_dict(raw), WeightMap.from_dir(path), device=device),
+                        tok, pooling)
+    return Embedder(BertEncoder(BertConfig.from_dict(raw), WeightMap.from_dir(path), device=device), tok, pooling)

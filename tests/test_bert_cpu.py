@@ -47,3 +47,33 @@ def test_load_embedder_from_directory(tmp_path):
     emb = load_embedder(str(d), device="cpu")
     e = emb.embed([[3, 4, 5], [6, 7, 8, 9, 10]])
     assert e.shape == (2, 32) and torch.allclose(e.norm(dim=-1), torch.ones(2), atol=1e-5)
+
+
+def test_nomic_bert_matches_transformers(tmp_path):
+    """NomicBERT (rotary, SwiGLU, post-norms) == transformers NomicBertModel on a
+    padded batch, and load_embedder picks it from config.json."""
+    import math
+    from transformers import NomicBertConfig as HFC, NomicBertModel
+    from rlx_models_b200.models.bert import NomicBertConfig, NomicBertEncoder
+    hc = HFC(vocab_size=100, hidden_size=64, num_hidden_layers=2, num_attention_heads=4, intermediate_size=96,
+             max_position_embeddings=64)
+    torch.manual_seed(0)
+    m = NomicBertModel(hc).eval()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if p.dim() >= 2:
+                p.normal_(0, 1 / math.sqrt(p.shape[-1]))
+            else:
+                p.normal_(1.0 if n.endswith("weight") else 0.0, 0.1)
+    ids = torch.randint(1, 100, (2, 11), generator=torch.Generator().manual_seed(1))
+    mask = torch.ones(2, 11, dtype=torch.long)
+    mask[1, 7:] = 0
+    with torch.no_grad():
+        ref = m(input_ids=ids, attention_mask=mask).last_hidden_state
+    sd = {k: v.detach() for k, v in m.state_dict().items()}
+    enc = NomicBertEncoder(NomicBertConfig.from_dict(hc.to_dict()), sd)
+    got = enc(ids, mask)
+    keep = mask.bool()
+    assert (got[keep] - ref[keep]).abs().max() < 1e-4
+    e = enc.embed(ids, mask, pooling="mean")
+    assert torch.allclose(e.norm(dim=-1), torch.ones(2), atol=1e-5)
