@@ -263,6 +263,62 @@ class Embedder:
         return self.encoder.embed(ids, mask, pooling=self.pooling, normalize=normalize)
 
 
+class DecoderEmbedder(Embedder):
+    """Sentence embeddings from a decoder-shaped trunk run over whole texts
+    (EuroBERT: bidirectional attention): final-normed hidden states pooled
+    over each text's tokens ("mean", "cls" = first token, "last")."""
+
+    def __init__(self, cfg, weights, device, tokenizer=None, pooling: str = "mean"):
+        from .weights.aliases import ModelPrefixView
+        self.cfg, self.device = cfg, torch.device(device)
+        weights = ModelPrefixView(weights)
+        if self.device.type == "cuda":
+            from .models.decoder import DecoderLM
+            self.trunk, self.oracle = DecoderLM(cfg, weights, device=self.device), None
+        else:
+            from .models.oracle import DecoderOracle
+            self.trunk, self.oracle = None, DecoderOracle(cfg, {k: weights[k] for k in weights.keys()})
+        super().__init__(self, tokenizer, pooling)
+
+    def hidden(self, ids: list[int]) -> torch.Tensor:
+        if self.oracle is not None:
+            return self.oracle.forward_hidden(torch.tensor(ids))[0]
+        from .models.decoder import ForwardBatch
+        T, dev = len(ids), self.device
+        nb = (T + 15) // 16
+        fb = ForwardBatch(input_ids=torch.tensor(ids, dtype=torch.int32, device=dev),
+                          positions=torch.arange(T, dtype=torch.int32, device=dev),
+                          slots=torch.arange(T, dtype=torch.int64, device=dev), num_decode=0,
+                          pre_block_tables=torch.arange(nb, dtype=torch.int32, device=dev).view(1, -1),
+                          pre_ctx_lens=torch.tensor([T], dtype=torch.int32, device=dev),
+                          pre_cu_q=torch.tensor([0, T], dtype=torch.int32, device=dev), pre_max_q=T)
+        return self.trunk.forward_hidden(fb, self.trunk.make_kv_cache(nb)).float()
+
+    def __call__(self, ids: torch.Tensor, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
+        """[B, L] padded ids -> [B, L, H] fp32 hidden states (zeros on padding)."""
+        B, L = ids.shape
+        out = torch.zeros(B, L, self.cfg.hidden_size)
+        for b in range(B):
+            keep = attention_mask[b].bool() if attention_mask is not None else torch.ones(L, dtype=torch.bool)
+            out[b, keep] = self.hidden(ids[b][keep].tolist()).cpu()
+        return out
+
+    def embed(self, ids, attention_mask=None, pooling: str | None = None, normalize: bool = True):
+        if isinstance(ids, (list, str)):  # texts / token lists through the Embedder front end
+            return Embedder.embed(self, ids, normalize)
+        h = self(ids, attention_mask)
+        m = attention_mask.float() if attention_mask is not None else torch.ones(h.shape[:2])
+        pooling = pooling or self.pooling
+        if pooling == "cls":
+            e = h[:, 0]
+        elif pooling == "last":  # the last non-padding token of each text
+            last = (m * torch.arange(m.shape[1])[None].float()).argmax(1)
+            e = h[torch.arange(h.shape[0]), last]
+        else:
+            e = (h * m[..., None]).sum(1) / m.sum(1, keepdim=True).clamp_min(1.0)
+        return torch.nn.functional.normalize(e, dim=-1) if normalize else e
+
+
 def load_embedder(model: str, *, device: str | torch.device = "cuda", pooling: str = "mean") -> Embedder:
     """BERT-family checkpoint (local dir / offline HF id) -> ``Embedder``."""
     import json
@@ -276,6 +332,8 @@ def load_embedder(model: str, *, device: str | torch.device = "cuda", pooling: s
     if any(os.path.exists(os.path.join(path, f)) for f in ("tokenizer.json", "vocab.txt")):
         from transformers import AutoTokenizer
         tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+    if raw.get("model_type") == "eurobert":  # bidirectional Llama-shaped trunk
+        return DecoderEmbedder(C.DecoderConfig.from_hf_dict(raw), WeightMap.from_dir(path), device, tok, pooling)
     if raw.get("model_type") == "nomic_bert":
         from .models.bert import NomicBertConfig, NomicBertEncoder
         return Embedder(NomicBertEncoder(NomicBertConfig.from_dict(raw), WeightMap.from_dir(path), device=device),

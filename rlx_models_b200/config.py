@@ -66,6 +66,7 @@ class DecoderConfig:
     # pre- and post-feedforward), attention and final logit softcapping, a separate
     # RoPE base for sliding-window layers
     mlp_act: str = "silu"  # "silu" | "gelu_tanh"
+    causal: bool = True  # False: a bidirectional encoder trunk (EuroBERT)
     norm_unit_offset: bool = False
     sandwich_norm: bool = False
     attn_softcap: float = 0.0
@@ -200,6 +201,10 @@ class DecoderConfig:
                 kw["rope_local_theta"] = float(local.get("rope_theta", 1e4))
             elif d.get("rope_local_base_freq"):
                 kw["rope_local_theta"] = float(d["rope_local_base_freq"])
+        elif mt == "eurobert":  # Llama-shaped bidirectional encoder
+            kw["qk_norm"] = False
+            kw["causal"] = False
+            kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-5))
         elif mt in ("granite", "phi3"):
             kw["qk_norm"] = False
             kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-5))

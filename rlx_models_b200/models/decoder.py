@@ -203,7 +203,7 @@ class DecoderLM:
         if T > nd:
             ops.prefill_attention(q[nd:], kc, vc, fb.pre_block_tables, fb.pre_ctx_lens, fb.pre_cu_q,
                                   fb.pre_max_q, scale=self.scale, sinks=L.sinks, window=L.window, out=o[nd:],
-                                  softcap=self.cfg.attn_softcap)
+                                  softcap=self.cfg.attn_softcap, causal=self.cfg.causal)
         return o.view(T, self.hq * self.D)
 
     def _layer(self, i: int, L: LayerWeights, x: torch.Tensor, h: torch.Tensor, fb: ForwardBatch, kv, comm,

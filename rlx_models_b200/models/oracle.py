@@ -111,7 +111,7 @@ class DecoderOracle:
         kpos = torch.arange(kv.k[i].shape[0], device=x.device)
         sinks = self.W(p + "sinks") if c.attn_sinks else None
         o = R.attention(q, kv.k[i], kv.v[i], pos, kpos, c.attention_multiplier or 1.0 / math.sqrt(c.head_dim),
-                        causal=True, window=c.layer_window(i), sinks=sinks, softcap=c.attn_softcap)
+                        causal=c.causal, window=c.layer_window(i), sinks=sinks, softcap=c.attn_softcap)
         y = self._mm(o.reshape(T, -1), p + "o_proj.weight")
         if (p + "o_proj.bias") in self.w:
             y = y + self.W(p + "o_proj.bias")

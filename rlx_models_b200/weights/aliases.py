@@ -104,3 +104,28 @@ class FusedSplitView:
 
     def __getitem__(self, name):
         return self.take(name)
+
+
+class ModelPrefixView:
+    """Weights of a bare base model (``embed_tokens.weight``, ``layers.N...``,
+    ``norm.weight``) seen under the ``model.``-prefixed names the decoder
+    builders read; names that already carry the prefix pass through."""
+
+    def __init__(self, weights):
+        self.w = weights
+        self.map = {}
+        for n in list(weights.keys()):
+            self.map[n if n.startswith(("model.", "lm_head.")) else "model." + n] = n
+
+    def keys(self):
+        return list(self.map)
+
+    def __contains__(self, name):
+        return name in self.map
+
+    def take(self, name, **kw):
+        n = self.map[name]
+        return self.w.take(n, **kw) if hasattr(self.w, "take") else self.w[n]
+
+    def __getitem__(self, name):
+        return self.take(name)

@@ -77,3 +77,41 @@ def test_nomic_bert_matches_transformers(tmp_path):
     assert (got[keep] - ref[keep]).abs().max() < 1e-4
     e = enc.embed(ids, mask, pooling="mean")
     assert torch.allclose(e.norm(dim=-1), torch.ones(2), atol=1e-5)
+
+
+def test_eurobert_bidirectional_trunk(tmp_path):
+    """EuroBERT (Llama-shaped trunk with bidirectional attention): the decoder
+    oracle with causal=False == transformers EuroBertModel, and
+    load_embedder builds a DecoderEmbedder over a saved checkpoint."""
+    import json
+    import math
+    from transformers import EuroBertConfig, EuroBertModel
+    from rlx_models_b200.api import DecoderEmbedder, load_embedder
+    from rlx_models_b200.weights.safetensors_io import save_file
+    hc = EuroBertConfig(vocab_size=128, hidden_size=64, num_hidden_layers=2, num_attention_heads=4,
+                        num_key_value_heads=2, intermediate_size=96, pad_token_id=0, bos_token_id=1, eos_token_id=2)
+    torch.manual_seed(0)
+    m = EuroBertModel(hc).eval()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if p.dim() >= 2:
+                p.normal_(0, 1 / math.sqrt(p.shape[-1]))
+            else:
+                p.normal_(1.0, 0.1)
+    d = tmp_path / "eb"
+    d.mkdir()
+    (d / "config.json").write_text(json.dumps(hc.to_dict()))
+    save_file({k: v.detach().contiguous() for k, v in m.state_dict().items()}, str(d / "model.safetensors"))
+    emb = load_embedder(str(d), device="cpu", pooling="mean")
+    assert isinstance(emb, DecoderEmbedder) and not emb.cfg.causal
+    ids = torch.randint(3, 128, (2, 13), generator=torch.Generator().manual_seed(1))
+    mask = torch.ones(2, 13, dtype=torch.long)
+    mask[1, 9:] = 0
+    with torch.no_grad():
+        ref = m(input_ids=ids, attention_mask=mask).last_hidden_state
+    got = emb(ids, mask)
+    keep = mask.bool()
+    assert (got[keep] - ref[keep]).abs().max() < 1e-4
+    e = emb.embed([ids[0].tolist(), ids[1, :9].tolist()])
+    r = torch.stack([ref[0].mean(0), ref[1, :9].mean(0)])
+    assert torch.allclose(e, torch.nn.functional.normalize(r, dim=-1), atol=1e-4)
