@@ -339,3 +339,37 @@ def load_embedder(model: str, *, device: str | torch.device = "cuda", pooling: s
         return Embedder(NomicBertEncoder(NomicBertConfig.from_dict(raw), WeightMap.from_dir(path), device=device),
                         tok, pooling)
     return Embedder(BertEncoder(BertConfig.from_dict(raw), WeightMap.from_dir(path), device=device), tok, pooling)
+
+
+class ImageEmbedder:
+    """Image embeddings from a CLIP / SigLIP vision tower."""
+
+    def __init__(self, encoder):
+        self.encoder = encoder
+
+    def pixels(self, images) -> torch.Tensor:
+        from .utils import preprocess as P
+        c = self.encoder.cfg
+        if c.family == "siglip":
+            return torch.stack([P.preprocess_image(im, size=(c.image_size, c.image_size), crop=None, mean=P.HALF,
+                                                   std=P.HALF) for im in images])
+        return torch.stack([P.preprocess_image(im, size=c.image_size, crop=c.image_size) for im in images])
+
+    def embed(self, images, normalize: bool = True) -> torch.Tensor:
+        """Paths, PIL images or HWC uint8 arrays -> [N, D] fp32 embeddings."""
+        if not isinstance(images, (list, tuple)):
+            images = [images]
+        return self.encoder.embed(self.pixels(images), normalize=normalize)
+
+
+def load_image_embedder(model: str, *, device: str | torch.device = "cuda") -> ImageEmbedder:
+    """CLIP / SigLIP checkpoint (vision model alone or the full dual encoder;
+    local dir / offline HF id) -> ``ImageEmbedder``."""
+    import json
+    from .models.vit import VisionConfig, VisionEncoder
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local vision checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        cfg = VisionConfig.from_dict(json.load(f))
+    return ImageEmbedder(VisionEncoder(cfg, WeightMap.from_dir(path), device=device))

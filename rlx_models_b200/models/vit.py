@@ -1,0 +1,142 @@
+"""Vision transformers for image embeddings: the CLIP and SigLIP vision towers
+(HF ``vision_model.*`` names, standalone or inside the full CLIP / SigLIP
+checkpoints).
+
+    patches  = patchify(pixels) @ W_patch^T (+ bias)      (the stride-p conv as a GEMM)
+    tokens   = [CLS] + patches (CLIP) | patches (SigLIP), + position embeddings
+    CLIP     : pre-LayerNorm, pre-norm blocks (quick-GELU MLP), pooled = LN(token 0),
+               image embedding = visual_projection(pooled)
+    SigLIP   : pre-norm blocks (GELU-tanh MLP), post-LayerNorm, pooled by the
+               attention-pooling head (a learned probe attends over the tokens,
+               then LayerNorm + MLP with a residual)
+
+Runs on the package's GEMM (``_linear``: bf16 on CUDA) or in fp32 on CPU;
+attention is non-causal SDPA. Images go through ``utils/preprocess.py``.
+
+Reference: crates/rlx-vision (NomicVision encoder graphs) and the vision
+towers of the reference's VLM families; transformers CLIP / SigLIP vision
+models are the CPU oracles.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from .flux_text import _linear
+
+
+@dataclass
+class VisionConfig:
+    family: str = "clip"  # "clip" | "siglip"
+    hidden_size: int = 768
+    intermediate_size: int = 3072
+    num_hidden_layers: int = 12
+    num_attention_heads: int = 12
+    image_size: int = 224
+    patch_size: int = 32
+    layer_norm_eps: float = 1e-5
+    projection_dim: int = 0
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "VisionConfig":
+        mt = d.get("model_type", "clip_vision_model")
+        vc = d.get("vision_config", d)
+        fam = "siglip" if "siglip" in mt else "clip"
+        kw = {k: vc[k] for k in cls.__dataclass_fields__ if k in vc and k != "family"}
+        kw["projection_dim"] = d.get("projection_dim", vc.get("projection_dim", 0)) if fam == "clip" else 0
+        return cls(family=fam, **kw)
+
+
+class VisionEncoder:
+    def __init__(self, cfg: VisionConfig, weights, device="cpu", dtype: torch.dtype | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else torch.float32)
+        get = (lambda n: weights.take(n)) if hasattr(weights, "take") else (lambda n: weights[n])
+        has = lambda n: n in weights  # noqa: E731
+        dv = lambda t: t.to(self.device, self.dtype).contiguous()  # noqa: E731
+        v = "vision_model."
+        e = v + "embeddings."
+        H = cfg.hidden_size
+        self.w_patch = dv(get(e + "patch_embedding.weight").reshape(H, -1))
+        self.b_patch = dv(get(e + "patch_embedding.bias")) if has(e + "patch_embedding.bias") else None
+        self.cls = dv(get(e + "class_embedding")) if has(e + "class_embedding") else None
+        self.pos = dv(get(e + "position_embedding.weight"))
+        ln = lambda p: (dv(get(p + ".weight")), dv(get(p + ".bias")))  # noqa: E731
+        self.pre_ln = ln(v + "pre_layrnorm") if has(v + "pre_layrnorm.weight") else None
+        self.post_ln = ln(v + "post_layernorm")
+        self.layers = []
+        for i in range(cfg.num_hidden_layers):
+            p = v + f"encoder.layers.{i}."
+            a = p + "self_attn."
+            self.layers.append(dict(
+                ln1=ln(p + "layer_norm1"), ln2=ln(p + "layer_norm2"),
+                qkv=dv(torch.cat([get(a + f"{n}_proj.weight") for n in "qkv"], 0)),
+                qkv_b=dv(torch.cat([get(a + f"{n}_proj.bias") for n in "qkv"], 0)),
+                o=(dv(get(a + "out_proj.weight")), dv(get(a + "out_proj.bias"))),
+                fc1=(dv(get(p + "mlp.fc1.weight")), dv(get(p + "mlp.fc1.bias"))),
+                fc2=(dv(get(p + "mlp.fc2.weight")), dv(get(p + "mlp.fc2.bias")))))
+        self.proj = dv(get("visual_projection.weight")) if has("visual_projection.weight") else None
+        self.head = None
+        h = v + "head."
+        if has(h + "probe"):
+            self.head = dict(probe=dv(get(h + "probe")), in_w=dv(get(h + "attention.in_proj_weight")),
+                             in_b=dv(get(h + "attention.in_proj_bias")),
+                             o=(dv(get(h + "attention.out_proj.weight")), dv(get(h + "attention.out_proj.bias"))),
+                             ln=ln(h + "layernorm"), fc1=(dv(get(h + "mlp.fc1.weight")), dv(get(h + "mlp.fc1.bias"))),
+                             fc2=(dv(get(h + "mlp.fc2.weight")), dv(get(h + "mlp.fc2.bias"))))
+
+    def _ln(self, x, p):
+        return F.layer_norm(x.float(), (x.shape[-1],), p[0].float(), p[1].float(),
+                            self.cfg.layer_norm_eps).to(x.dtype)
+
+    def _act(self, x):
+        x = x.float()
+        return x * torch.sigmoid(1.702 * x) if self.cfg.family == "clip" else F.gelu(x, approximate="tanh")
+
+    def _attend(self, q, k, v, nh):
+        B, Lq, H = q.shape
+        D = H // nh
+        q, k, v = (t.reshape(B, -1, nh, D).transpose(1, 2) for t in (q, k, v))
+        return F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(B, Lq, H)
+
+    @torch.no_grad()
+    def __call__(self, pixels: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """pixels [B, 3, S, S] (preprocessed) -> (last hidden [B, L, H], pooled [B, H])."""
+        from ..utils.preprocess import patchify
+        c = self.cfg
+        pixels = pixels.to(self.device, torch.float32)
+        B = pixels.shape[0]
+        H, nh = c.hidden_size, c.num_attention_heads
+        rows = torch.stack([patchify(p, c.patch_size) for p in pixels]).to(self.dtype)
+        x = _linear(rows, self.w_patch, self.b_patch)
+        if self.cls is not None:
+            x = torch.cat([self.cls.expand(B, 1, H), x], 1)
+        x = x + self.pos[None, :x.shape[1]]
+        if self.pre_ln is not None:
+            x = self._ln(x, self.pre_ln)
+        for ly in self.layers:
+            q, k, v = _linear(self._ln(x, ly["ln1"]), ly["qkv"], ly["qkv_b"]).split(H, -1)
+            x = x + _linear(self._attend(q, k, v, nh), *ly["o"])
+            x = x + _linear(self._act(_linear(self._ln(x, ly["ln2"]), *ly["fc1"])).to(x.dtype), *ly["fc2"])
+        if c.family == "clip":
+            return x, self._ln(x[:, 0], self.post_ln)
+        x = self._ln(x, self.post_ln)
+        if self.head is None:
+            return x, x.mean(1)
+        hd = self.head
+        wq, wk, wv = hd["in_w"].split(H, 0)
+        bq, bk, bv = hd["in_b"].split(H, 0)
+        probe = hd["probe"].expand(B, 1, H)
+        h = _linear(self._attend(_linear(probe, wq, bq), _linear(x, wk, bk), _linear(x, wv, bv), nh), *hd["o"])
+        h = h + _linear(self._act(_linear(self._ln(h, hd["ln"]), *hd["fc1"])).to(h.dtype), *hd["fc2"])
+        return x, h[:, 0]
+
+    def embed(self, pixels: torch.Tensor, normalize: bool = True) -> torch.Tensor:
+        """[B, D] fp32 image embeddings: CLIP's projected pooled token (when the
+        checkpoint has visual_projection), otherwise the pooled output."""
+        _, pooled = self(pixels)
+        e = _linear(pooled, self.proj).float() if self.proj is not None else pooled.float()
+        return F.normalize(e, dim=-1) if normalize else e

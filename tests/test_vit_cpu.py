@@ -1,0 +1,79 @@
+"""CLIP and SigLIP vision towers on CPU against transformers (last hidden
+state, pooled output, CLIP's projected image embedding), fed by the
+package's own image preprocessing."""
+import math
+
+import numpy as np
+import torch
+
+
+def _rand(m):
+    torch.manual_seed(0)
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if p.dim() >= 2:
+                p.normal_(0, 1 / math.sqrt(p[0].numel()))
+            else:
+                p.normal_(1.0 if ("norm" in n and n.endswith("weight")) else 0.0, 0.1)
+    return m.eval()
+
+
+def _pixels():
+    from PIL import Image
+    from rlx_models_b200.utils.preprocess import preprocess_image
+    rng = np.random.default_rng(0)
+    imgs = [Image.fromarray(rng.integers(0, 256, (50 + 7 * i, 61, 3), dtype=np.uint8)) for i in range(2)]
+    return torch.stack([preprocess_image(im, size=32, crop=32) for im in imgs])
+
+
+def test_clip_vision_matches_transformers():
+    from transformers import CLIPVisionConfig, CLIPVisionModelWithProjection
+    from rlx_models_b200.models.vit import VisionConfig, VisionEncoder
+    hc = CLIPVisionConfig(hidden_size=64, intermediate_size=96, num_hidden_layers=2, num_attention_heads=4,
+                          image_size=32, patch_size=8, projection_dim=48)
+    m = _rand(CLIPVisionModelWithProjection(hc))
+    px = _pixels()
+    with torch.no_grad():
+        ref = m(pixel_values=px)
+    enc = VisionEncoder(VisionConfig.from_dict(hc.to_dict()), {k: v.detach() for k, v in m.state_dict().items()})
+    last, _ = enc(px)
+    assert (last - ref.last_hidden_state).abs().max() < 1e-4
+    e = enc.embed(px, normalize=False)
+    assert (e - ref.image_embeds).abs().max() < 1e-4
+
+
+def test_siglip_vision_matches_transformers():
+    from transformers import SiglipVisionConfig, SiglipVisionModel
+    from rlx_models_b200.models.vit import VisionConfig, VisionEncoder
+    hc = SiglipVisionConfig(hidden_size=64, intermediate_size=96, num_hidden_layers=2, num_attention_heads=4,
+                            image_size=32, patch_size=8)
+    m = _rand(SiglipVisionModel(hc))
+    px = _pixels()
+    with torch.no_grad():
+        ref = m(pixel_values=px)
+    enc = VisionEncoder(VisionConfig.from_dict(hc.to_dict()), {k: v.detach() for k, v in m.state_dict().items()})
+    last, pooled = enc(px)
+    assert (last - ref.last_hidden_state).abs().max() < 1e-4
+    assert (pooled - ref.pooler_output).abs().max() < 1e-4
+
+
+def test_load_image_embedder(tmp_path):
+    import json
+    from PIL import Image
+    from transformers import CLIPVisionConfig, CLIPVisionModelWithProjection, CLIPImageProcessor
+    from rlx_models_b200.api import load_image_embedder
+    from rlx_models_b200.weights.safetensors_io import save_file
+    hc = CLIPVisionConfig(hidden_size=64, intermediate_size=96, num_hidden_layers=1, num_attention_heads=4,
+                          image_size=32, patch_size=8, projection_dim=48)
+    m = _rand(CLIPVisionModelWithProjection(hc))
+    d = tmp_path / "clipv"
+    d.mkdir()
+    (d / "config.json").write_text(json.dumps(hc.to_dict()))
+    save_file({k: v.detach().contiguous() for k, v in m.state_dict().items()}, str(d / "model.safetensors"))
+    img = Image.fromarray(np.random.default_rng(3).integers(0, 256, (40, 48, 3), dtype=np.uint8))
+    e = load_image_embedder(str(d), device="cpu").embed(img)
+    px = CLIPImageProcessor(size={"shortest_edge": 32}, crop_size={"height": 32, "width": 32})(
+        img, return_tensors="pt")["pixel_values"]
+    with torch.no_grad():
+        r = torch.nn.functional.normalize(m(pixel_values=px).image_embeds, dim=-1)
+    assert (e - r).abs().max() < 2e-2  # the resampler's 8-bit rounding on a few pixels
