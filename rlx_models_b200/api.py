@@ -273,8 +273,11 @@ class DecoderEmbedder(Embedder):
         self.cfg, self.device = cfg, torch.device(device)
         weights = ModelPrefixView(weights)
         if self.device.type == "cuda":
+            import dataclasses
             from .models.decoder import DecoderLM
-            self.trunk, self.oracle = DecoderLM(cfg, weights, device=self.device), None
+            # an encoder trunk has no LM head: point the (unused) head at the embedding table
+            trunk_cfg = dataclasses.replace(cfg, tie_word_embeddings=True)
+            self.trunk, self.oracle = DecoderLM(trunk_cfg, weights, device=self.device), None
         else:
             from .models.oracle import DecoderOracle
             self.trunk, self.oracle = None, DecoderOracle(cfg, {k: weights[k] for k in weights.keys()})

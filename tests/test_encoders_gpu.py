@@ -1,0 +1,54 @@
+"""Encoder families on the GPU (bf16 GEMMs) against their CPU fp32 paths:
+NomicBERT text embeddings and CLIP image embeddings."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _rand(m):
+    torch.manual_seed(0)
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if p.dim() >= 2:
+                p.normal_(0, 1 / math.sqrt(p[0].numel()))
+            else:
+                p.normal_(1.0 if n.endswith("weight") else 0.0, 0.1)
+    return m.eval()
+
+
+def _cos(a, b):
+    return torch.nn.functional.cosine_similarity(a.float().cpu(), b.float().cpu(), dim=-1)
+
+
+def test_nomic_bert_gpu_matches_cpu(cuda):
+    from transformers import NomicBertConfig as HFC, NomicBertModel
+    from rlx_models_b200.models.bert import NomicBertConfig, NomicBertEncoder
+    hc = HFC(vocab_size=128, hidden_size=256, num_hidden_layers=2, num_attention_heads=4, intermediate_size=512)
+    sd = {k: v.detach() for k, v in _rand(NomicBertModel(hc)).state_dict().items()}
+    cfg = NomicBertConfig.from_dict(hc.to_dict())
+    ids = torch.randint(1, 128, (3, 20), generator=torch.Generator().manual_seed(1))
+    mask = torch.ones(3, 20, dtype=torch.long)
+    mask[2, 11:] = 0
+    ref = NomicBertEncoder(cfg, sd).embed(ids, mask)
+    got = NomicBertEncoder(cfg, sd, device=cuda).embed(ids, mask)
+    assert _cos(got, ref).min() > 0.999
+
+
+def test_clip_vision_gpu_matches_cpu(cuda):
+    from transformers import CLIPVisionConfig, CLIPVisionModelWithProjection
+    from rlx_models_b200.models.vit import VisionConfig, VisionEncoder
+    from rlx_models_b200.utils.preprocess import preprocess_image
+    hc = CLIPVisionConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+                          image_size=64, patch_size=16, projection_dim=128)
+    sd = {k: v.detach() for k, v in _rand(CLIPVisionModelWithProjection(hc)).state_dict().items()}
+    cfg = VisionConfig.from_dict(hc.to_dict())
+    rng = np.random.default_rng(0)
+    px = torch.stack([preprocess_image(rng.integers(0, 256, (70, 90, 3), dtype=np.uint8), size=64, crop=64)
+                      for _ in range(2)])
+    ref = VisionEncoder(cfg, sd).embed(px)
+    got = VisionEncoder(cfg, sd, device=cuda).embed(px)
+    assert _cos(got, ref).min() > 0.999
