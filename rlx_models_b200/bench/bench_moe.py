@@ -21,7 +21,7 @@ import torch
 from ..config import gpt_oss_120b
 from ..ops._ext import ext, scratch
 from .. import ops
-from ..quant.mxfp4 import TILE_BYTES, tile_mxfp4
+from ..quant.mxfp4 import tile_mxfp4
 from .bench_ops import Timer, peaks
 from ..models.moe import token_tile
 

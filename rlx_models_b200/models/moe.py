@@ -32,7 +32,7 @@ from .. import ops
 from ..config import DecoderConfig
 from ..ops._ext import ext, scratch
 from ..quant.mxfp4 import quantize_mxfp4, tile_mxfp4
-from .decoder import DecoderLM, LayerWeights, LocalComm
+from .decoder import DecoderLM, LayerWeights
 
 GROUP = 64  # gate/up rows interleaved in groups of 64 for the fused epilogue
 

@@ -21,7 +21,6 @@ rlx-models-core src/mxfp4_pack.rs.
 """
 from __future__ import annotations
 
-import math
 
 import torch
 

@@ -12,7 +12,6 @@ checkpoints round-trip through :mod:`rlx_models_b200.weights`.
 """
 from __future__ import annotations
 
-import math
 
 import torch
 import torch.nn.functional as F

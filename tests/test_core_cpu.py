@@ -9,7 +9,7 @@ import torch
 from rlx_models_b200 import config as C
 from rlx_models_b200.models.oracle import DecoderOracle
 from rlx_models_b200.quant.mxfp4 import dequantize_mxfp4, quantize_mxfp4
-from rlx_models_b200.weights.init import decoder_tensor_specs, random_weights
+from rlx_models_b200.weights.init import random_weights
 from rlx_models_b200.weights.safetensors_io import Checkpoint, save_file, save_sharded
 from rlx_models_b200.weights.weight_map import UnusedWeights, WeightMap
 
@@ -249,7 +249,6 @@ def test_mxfp4_tile_roundtrip():
 
 def test_flux_oracle_deinterleaved_rope_matches():
     """Half-split RoPE on de-interleaved q/k rows == BFL interleaved-pair RoPE."""
-    from rlx_models_b200.config import flux_tiny
     from rlx_models_b200.models.flux_common import (apply_rope_interleaved, deinterleave_perm, position_ids,
                                                      rope_tables)
     D = 128

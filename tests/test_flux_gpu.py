@@ -1,7 +1,6 @@
 """FLUX.1 DiT on the GPU against the fp32 oracle (tiny config), plus the
 DiT-specific kernels (LayerNorm+modulate, QK-norm + 3-axis RoPE, gated /
 GELU GEMM epilogues, non-causal paged attention)."""
-import math
 
 import pytest
 import torch

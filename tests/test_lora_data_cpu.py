@@ -1,5 +1,4 @@
 """LoRA / DoRA fine-tuning, JSONL datasets and DPO on CPU (fp32, gloo)."""
-import json
 import os
 import tempfile
 

@@ -1,7 +1,6 @@
 """MoE (gpt-oss family) on the GPU: routing/permutation kernels, the grouped
 MXFP4 GEMM against a dequantized fp32 reference, and the full model against
 the fp32 oracle (sinks, sliding window beyond its length, YaRN, biases)."""
-import math
 
 import pytest
 import torch

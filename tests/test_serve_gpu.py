@@ -2,7 +2,6 @@
 import json
 
 import pytest
-import torch
 
 pytestmark = pytest.mark.gpu
 

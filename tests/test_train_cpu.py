@@ -3,7 +3,6 @@ schedules, sharded checkpoint resume across world sizes, HF export."""
 import os
 import tempfile
 
-import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
