@@ -376,3 +376,45 @@ def load_image_embedder(model: str, *, device: str | torch.device = "cuda") -> I
     with open(os.path.join(path, "config.json")) as f:
         cfg = VisionConfig.from_dict(json.load(f))
     return ImageEmbedder(VisionEncoder(cfg, WeightMap.from_dir(path), device=device))
+
+
+class CLIP:
+    """Text and image embeddings in one space, plus zero-shot labels."""
+
+    def __init__(self, model, tokenizer=None):
+        self.model, self.tokenizer = model, tokenizer
+        self.images = ImageEmbedder(model.vision)
+
+    def _ids(self, texts):
+        if texts and isinstance(texts[0], str):
+            if self.tokenizer is None:
+                raise ValueError("string inputs need a tokenizer")
+            return self.tokenizer(list(texts), padding="max_length", truncation=True, return_tensors="pt")["input_ids"]
+        return torch.tensor(texts)
+
+    def embed_text(self, texts) -> torch.Tensor:
+        return self.model.embed_text(self._ids(texts))
+
+    def embed_image(self, images) -> torch.Tensor:
+        return self.images.embed(images)
+
+    def zero_shot(self, images, labels) -> torch.Tensor:
+        """[images, labels] probabilities (softmax over the labels)."""
+        px = self.images.pixels(images if isinstance(images, (list, tuple)) else [images])
+        return self.model.logits_per_image(px, self._ids(labels)).softmax(-1)
+
+
+def load_clip(model: str, *, device: str | torch.device = "cuda") -> CLIP:
+    """Full CLIP checkpoint (text + vision towers, projections, logit scale)."""
+    import json
+    from .models.clip import CLIPDualEncoder
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local CLIP checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        cfg = json.load(f)
+    tok = None
+    if any(os.path.exists(os.path.join(path, f)) for f in ("tokenizer.json", "vocab.json")):
+        from transformers import AutoTokenizer
+        tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+    return CLIP(CLIPDualEncoder(cfg, WeightMap.from_dir(path), device=device), tok)

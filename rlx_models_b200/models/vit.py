@@ -42,7 +42,7 @@ class VisionConfig:
     @classmethod
     def from_dict(cls, d: dict) -> "VisionConfig":
         mt = d.get("model_type", "clip_vision_model")
-        vc = d.get("vision_config", d)
+        vc = d.get("vision_config") or d
         fam = "siglip" if "siglip" in mt else "clip"
         kw = {k: vc[k] for k in cls.__dataclass_fields__ if k in vc and k != "family"}
         kw["projection_dim"] = d.get("projection_dim", vc.get("projection_dim", 0)) if fam == "clip" else 0

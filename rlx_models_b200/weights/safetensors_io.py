@@ -147,8 +147,8 @@ def save_file(tensors: dict[str, torch.Tensor], path: str, metadata: dict[str, s
         f.write(hb)
         for t in items:
             if t.numel():
-                f.write(t.view(torch.uint8).reshape(-1).numpy().tobytes() if t.dtype != torch.uint8
-                        else t.reshape(-1).numpy().tobytes())
+                flat = t.reshape(-1)  # 0-dim scalars too (a byte view needs at least one dim)
+                f.write(flat.view(torch.uint8).numpy().tobytes() if t.dtype != torch.uint8 else flat.numpy().tobytes())
     os.replace(tmp, path)
 
 

@@ -77,3 +77,30 @@ def test_load_image_embedder(tmp_path):
     with torch.no_grad():
         r = torch.nn.functional.normalize(m(pixel_values=px).image_embeds, dim=-1)
     assert (e - r).abs().max() < 2e-2  # the resampler's 8-bit rounding on a few pixels
+
+
+def test_clip_dual_encoder_matches_transformers(tmp_path):
+    import json
+    from transformers import CLIPConfig, CLIPModel
+    from rlx_models_b200.api import load_clip
+    from rlx_models_b200.weights.safetensors_io import save_file
+    cfg = CLIPConfig(text_config=dict(vocab_size=99, hidden_size=64, intermediate_size=96, num_hidden_layers=2,
+                                      num_attention_heads=4, max_position_embeddings=16, eos_token_id=98),
+                     vision_config=dict(hidden_size=64, intermediate_size=96, num_hidden_layers=2,
+                                        num_attention_heads=4, image_size=32, patch_size=8),
+                     projection_dim=40)
+    m = _rand(CLIPModel(cfg))
+    with torch.no_grad():
+        m.logit_scale.fill_(2.0)
+    d = tmp_path / "clip"
+    d.mkdir()
+    (d / "config.json").write_text(json.dumps(cfg.to_dict()))
+    save_file({k: v.detach().contiguous() for k, v in m.state_dict().items()}, str(d / "model.safetensors"))
+    clip = load_clip(str(d), device="cpu")
+    ids = torch.randint(1, 98, (3, 16), generator=torch.Generator().manual_seed(4))
+    ids[:, 10] = 98  # end-of-text
+    px = _pixels()
+    with torch.no_grad():
+        ref = m(input_ids=ids, pixel_values=px).logits_per_image
+    got = clip.model.logits_per_image(px, ids)
+    assert (got - ref).abs().max() < 1e-3
