@@ -86,7 +86,11 @@ def cmd_serve(a):
     from .serve.openai_server import serve
     llm = load(a.model, engine_config=EngineConfig(max_num_seqs=a.max_num_seqs, max_model_len=a.max_model_len,
                                                    kv_memory_gb=a.kv_gb))
-    serve(llm, a.host, a.port, model_name=a.model)
+    embedder = None
+    if a.embed_model:  # an encoder checkpoint behind /v1/embeddings
+        from .api import load_embedder
+        embedder = load_embedder(a.embed_model)
+    serve(llm, a.host, a.port, model_name=a.model, embedder=embedder)
     return 0
 
 
@@ -158,6 +162,7 @@ def main(argv=None):
             p.add_argument("--host", default="127.0.0.1")
             p.add_argument("--port", type=int, default=8000)
             p.add_argument("--max-num-seqs", type=int, default=64)
+            p.add_argument("--embed-model", default=None, help="encoder checkpoint served at /v1/embeddings")
     p = sub.add_parser("profile")
     p.add_argument("--model", default="qwen3-0.6b")
     p.add_argument("--batch", type=int, default=8)

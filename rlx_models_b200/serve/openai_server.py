@@ -3,7 +3,8 @@
     python -m rlx_models_b200 serve --model qwen3-0.6b --port 8000
 
 Endpoints: ``GET /health``, ``GET /v1/models``, ``GET /metrics``
-(Prometheus text), ``POST /v1/completions``, ``POST /v1/chat/completions``.
+(Prometheus text), ``POST /v1/completions``, ``POST /v1/chat/completions``,
+``POST /v1/embeddings`` (when the server was given an embedder).
 Prompts may be text (tokenised with the checkpoint's tokenizer, or bytes
 for random-weight shapes) or token-id arrays. Sampling fields: ``max_tokens``,
 ``temperature``, ``top_p``, ``top_k``, ``min_p``, ``seed``, ``stop`` (strings),
@@ -50,7 +51,9 @@ def _params(body: dict, eos: int | None) -> tuple[SamplingParams, list[str]]:
     return sp, list(stop)
 
 
-def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model"):
+def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model", embedder=None):
+    """``embedder``: any object with ``embed(inputs) -> [N, D]`` over a list of
+    strings or of token-id lists (``api.load_embedder``, ``LLM.embed``)."""
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
     from prometheus_client import CollectorRegistry, Counter, Histogram, generate_latest
@@ -181,6 +184,23 @@ def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model"):
             raise HTTPException(400, "n > 1 is not supported")
         return respond(body, encode_prompt(body.get("prompt", "")), "text")
 
+    @app.post("/v1/embeddings")
+    def embeddings(body: dict):
+        m_req.labels("embeddings").inc()
+        if embedder is None:
+            raise HTTPException(404, "this server has no embedding model")
+        inp = body.get("input")
+        if inp is None or inp == [] or inp == "":
+            raise HTTPException(400, "input required")
+        if isinstance(inp, str) or (isinstance(inp, list) and inp and isinstance(inp[0], int)):
+            inp = [inp]  # one text or one token-id list
+        vecs = embedder.embed(list(inp))
+        n_tok = sum(len(x) if isinstance(x, list) else len(tokenizer.encode(x)) for x in inp)
+        data = [{"object": "embedding", "index": i, "embedding": [float(v) for v in vec]}
+                for i, vec in enumerate(vecs.float().cpu())]
+        return {"object": "list", "data": data, "model": body.get("model", model_name),
+                "usage": {"prompt_tokens": n_tok, "total_tokens": n_tok}}
+
     @app.post("/v1/chat/completions")
     def chat(body: dict):
         m_req.labels("chat").inc()
@@ -201,13 +221,13 @@ def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model"):
     return app
 
 
-def serve(llm, host: str = "127.0.0.1", port: int = 8000, model_name: str = "b200-model"):
+def serve(llm, host: str = "127.0.0.1", port: int = 8000, model_name: str = "b200-model", embedder=None):
     import uvicorn
 
     from ..tokenizer import ByteTokenizer
     tok = llm.tokenizer or ByteTokenizer()
     runner = EngineRunner(llm.engine, tok)
-    app = create_app(runner, tok, model_name)
+    app = create_app(runner, tok, model_name, embedder=embedder)
     try:
         uvicorn.run(app, host=host, port=port, log_level="info")
     finally:

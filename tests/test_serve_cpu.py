@@ -181,3 +181,28 @@ def test_chat_compaction_budget(client):
     assert r.status_code == 200
     ids, _ = eng.params[1]
     assert len(ids) < 300 and b"SYS" in bytes(ids) and b"last" in bytes(ids)
+
+
+class _FakeEmbedder:
+    def embed(self, inputs):
+        import torch
+        return torch.stack([torch.tensor([float(len(x)), 1.0, 0.5]) for x in inputs])
+
+
+def test_embeddings_endpoint():
+    eng = FakeEngine()
+    tok = ByteTokenizer()
+    runner = EngineRunner(eng, tok)
+    with TestClient(create_app(runner, tok, "fake", embedder=_FakeEmbedder())) as c:
+        r = c.post("/v1/embeddings", json={"input": ["abc", "hello"]}).json()
+        assert [d["index"] for d in r["data"]] == [0, 1]
+        assert r["data"][1]["embedding"] == [5.0, 1.0, 0.5]
+        assert r["usage"]["prompt_tokens"] == 8
+        r = c.post("/v1/embeddings", json={"input": [1, 2, 3, 4]}).json()
+        assert len(r["data"]) == 1 and r["data"][0]["embedding"][0] == 4.0
+        assert c.post("/v1/embeddings", json={"input": []}).status_code == 400
+    runner.shutdown()
+    runner = EngineRunner(FakeEngine(), tok)
+    with TestClient(create_app(runner, tok, "fake")) as c:
+        assert c.post("/v1/embeddings", json={"input": "x"}).status_code == 404
+    runner.shutdown()
