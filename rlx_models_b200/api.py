@@ -268,9 +268,10 @@ class DecoderEmbedder(Embedder):
     (EuroBERT: bidirectional attention): final-normed hidden states pooled
     over each text's tokens ("mean", "cls" = first token, "last")."""
 
-    def __init__(self, cfg, weights, device, tokenizer=None, pooling: str = "mean"):
+    def __init__(self, cfg, weights, device, tokenizer=None, pooling: str = "mean", dense=()):
         from .weights.aliases import ModelPrefixView
         self.cfg, self.device = cfg, torch.device(device)
+        self.dense = list(dense)  # sentence-transformers Dense layers after pooling: (W, b or None)
         weights = ModelPrefixView(weights)
         if self.device.type == "cuda":
             import dataclasses
@@ -286,6 +287,9 @@ class DecoderEmbedder(Embedder):
     def hidden(self, ids: list[int]) -> torch.Tensor:
         if self.oracle is not None:
             return self.oracle.forward_hidden(torch.tensor(ids))[0]
+        if any(L.window and len(ids) > L.window for L in self.trunk.layers):
+            # the prefill kernel's non-causal mode has no window
+            raise NotImplementedError("bidirectional sliding-window layers on the GPU: texts up to the window only")
         from .models.decoder import ForwardBatch
         T, dev = len(ids), self.device
         nb = (T + 15) // 16
@@ -319,7 +323,36 @@ class DecoderEmbedder(Embedder):
             e = h[torch.arange(h.shape[0]), last]
         else:
             e = (h * m[..., None]).sum(1) / m.sum(1, keepdim=True).clamp_min(1.0)
+        for w, b in self.dense:
+            e = e @ w.t() + (b if b is not None else 0.0)
         return torch.nn.functional.normalize(e, dim=-1) if normalize else e
+
+
+def _sentence_transformer_head(path: str):
+    """(pooling mode, [(W, b)]) from a sentence-transformers layout
+    (modules.json, N_Pooling/config.json, N_Dense/{config.json, weights});
+    ("mean", []) when the directory has none. Dense layers with an identity
+    activation only."""
+    import json
+    mf = os.path.join(path, "modules.json")
+    if not os.path.exists(mf):
+        return "mean", []
+    pooling, dense = "mean", []
+    for mod in json.load(open(mf)):
+        kind, sub = mod.get("type", ""), os.path.join(path, mod.get("path", ""))
+        if kind.endswith("Pooling"):
+            pc = json.load(open(os.path.join(sub, "config.json")))
+            pooling = "cls" if pc.get("pooling_mode_cls_token") else (
+                "last" if pc.get("pooling_mode_lasttoken") else "mean")
+        elif kind.endswith("Dense"):
+            dc = json.load(open(os.path.join(sub, "config.json")))
+            act = dc.get("activation_function", "torch.nn.modules.linear.Identity")
+            if not act.endswith("Identity"):
+                raise NotImplementedError(f"Dense activation {act}")
+            w = WeightMap.from_dir(sub)
+            dense.append((w.take("linear.weight").float(),
+                          w.take("linear.bias").float() if "linear.bias" in w else None))
+    return pooling, dense
 
 
 def load_embedder(model: str, *, device: str | torch.device = "cuda", pooling: str = "mean") -> Embedder:
@@ -335,8 +368,11 @@ def load_embedder(model: str, *, device: str | torch.device = "cuda", pooling: s
     if any(os.path.exists(os.path.join(path, f)) for f in ("tokenizer.json", "vocab.txt")):
         from transformers import AutoTokenizer
         tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
-    if raw.get("model_type") == "eurobert":  # bidirectional Llama-shaped trunk
-        return DecoderEmbedder(C.DecoderConfig.from_hf_dict(raw), WeightMap.from_dir(path), device, tok, pooling)
+    if raw.get("model_type") == "eurobert" or raw.get("use_bidirectional_attention"):
+        # bidirectional decoder trunks: EuroBERT, EmbeddingGemma (Gemma-3 + pooling + Dense head)
+        st_pool, dense = _sentence_transformer_head(path)
+        return DecoderEmbedder(C.DecoderConfig.from_hf_dict(raw), WeightMap.from_dir(path), device, tok,
+                               st_pool if dense else pooling, dense)
     if raw.get("model_type") == "nomic_bert":
         from .models.bert import NomicBertConfig, NomicBertEncoder
         return Embedder(NomicBertEncoder(NomicBertConfig.from_dict(raw), WeightMap.from_dir(path), device=device),

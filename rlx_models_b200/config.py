@@ -192,6 +192,10 @@ class DecoderConfig:
                                      for i in range(n)]
             if mt == "gemma":
                 kw["sliding_window"] = 0
+            if d.get("use_bidirectional_attention"):  # EmbeddingGemma: an encoder over the Gemma-3 trunk
+                kw["causal"] = False
+                # files keep the full window; attention spans |q - k| < window // 2 + 1
+                kw["sliding_window"] = int(d.get("sliding_window") or 0) // 2 + 1
             rp = raw.get("rope_parameters") or (merge_text_config(raw).get("rope_parameters"))
             if isinstance(rp, dict) and "full_attention" in rp:  # per-layer-type RoPE (Gemma-3)
                 full, local = rp["full_attention"], rp.get("sliding_attention", {})

@@ -59,6 +59,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Te
         mask &= k_pos[None, :] <= q_pos[:, None]
     if window > 0:
         mask &= k_pos[None, :] > (q_pos[:, None] - window)
+        if not causal:  # a bidirectional window: |q - k| < window
+            mask &= k_pos[None, :] < (q_pos[:, None] + window)
     s = s.masked_fill(~mask[None], float("-inf"))
     if sinks is not None:
         sk = sinks.float()[:, None, None].expand(Hq, q.shape[0], 1)

@@ -115,3 +115,53 @@ def test_eurobert_bidirectional_trunk(tmp_path):
     e = emb.embed([ids[0].tolist(), ids[1, :9].tolist()])
     r = torch.stack([ref[0].mean(0), ref[1, :9].mean(0)])
     assert torch.allclose(e, torch.nn.functional.normalize(r, dim=-1), atol=1e-4)
+
+
+def test_embeddinggemma_trunk_and_dense_head(tmp_path):
+    """EmbeddingGemma: the Gemma-3 trunk with bidirectional attention (sliding
+    layers see |q - k| < window // 2 + 1), mean pooling and the
+    sentence-transformers Dense stack, against transformers on CPU."""
+    import json
+    import math
+    from transformers import Gemma3TextConfig, Gemma3TextModel
+    from rlx_models_b200.api import DecoderEmbedder, load_embedder
+    from rlx_models_b200.weights.safetensors_io import save_file
+    kw = dict(vocab_size=128, hidden_size=64, intermediate_size=96, num_hidden_layers=3, num_attention_heads=4,
+              num_key_value_heads=1, head_dim=16, sliding_window=8, use_bidirectional_attention=True,
+              layer_types=["sliding_attention", "sliding_attention", "full_attention"], query_pre_attn_scalar=16)
+    m = Gemma3TextModel(Gemma3TextConfig(**kw)).eval()
+    torch.manual_seed(0)
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            p.normal_(0, 1 / math.sqrt(p.shape[-1])) if p.dim() >= 2 else p.normal_(0, 0.1)
+    d = tmp_path / "eg"
+    d.mkdir()
+    cfg = m.config.to_dict()
+    cfg["sliding_window"] = 8  # files keep the full window
+    (d / "config.json").write_text(json.dumps(cfg))
+    save_file({k: v.detach().contiguous() for k, v in m.state_dict().items()}, str(d / "model.safetensors"))
+    g = torch.Generator().manual_seed(2)
+    W1, W2 = torch.randn(96, 64, generator=g) / 8, torch.randn(32, 96, generator=g) / 10
+    (d / "modules.json").write_text(json.dumps([
+        {"idx": 0, "type": "sentence_transformers.models.Transformer", "path": ""},
+        {"idx": 1, "type": "sentence_transformers.models.Pooling", "path": "1_Pooling"},
+        {"idx": 2, "type": "sentence_transformers.models.Dense", "path": "2_Dense"},
+        {"idx": 3, "type": "sentence_transformers.models.Dense", "path": "3_Dense"}]))
+    for sub, W in (("2_Dense", W1), ("3_Dense", W2)):
+        (d / sub).mkdir()
+        (d / sub / "config.json").write_text(json.dumps({"in_features": W.shape[1], "out_features": W.shape[0],
+                                                         "bias": False, "activation_function":
+                                                         "torch.nn.modules.linear.Identity"}))
+        save_file({"linear.weight": W.contiguous()}, str(d / sub / "model.safetensors"))
+    (d / "1_Pooling").mkdir()
+    (d / "1_Pooling" / "config.json").write_text(json.dumps({"pooling_mode_mean_tokens": True}))
+    emb = load_embedder(str(d), device="cpu")
+    assert isinstance(emb, DecoderEmbedder) and not emb.cfg.causal and emb.cfg.layer_window(0) == 5
+    ids = torch.randint(1, 128, (1, 23), generator=g)
+    with torch.no_grad():
+        ref = m(input_ids=ids).last_hidden_state[0]
+    got = emb.hidden(ids[0].tolist())
+    assert (got - ref).abs().max() < 1e-4
+    e = emb.embed([ids[0].tolist()])
+    r = torch.nn.functional.normalize(ref.mean(0) @ W1.t() @ W2.t(), dim=-1)
+    assert torch.allclose(e[0], r, atol=1e-4)
