@@ -90,7 +90,11 @@ def cmd_serve(a):
     if a.embed_model:  # an encoder checkpoint behind /v1/embeddings
         from .api import load_embedder
         embedder = load_embedder(a.embed_model)
-    serve(llm, a.host, a.port, model_name=a.model, embedder=embedder)
+    transcriber = None
+    if a.asr_model:  # a Whisper checkpoint behind /v1/audio/transcriptions
+        from .api import load_transcriber
+        transcriber = load_transcriber(a.asr_model)
+    serve(llm, a.host, a.port, model_name=a.model, embedder=embedder, transcriber=transcriber)
     return 0
 
 
@@ -163,6 +167,7 @@ def main(argv=None):
             p.add_argument("--port", type=int, default=8000)
             p.add_argument("--max-num-seqs", type=int, default=64)
             p.add_argument("--embed-model", default=None, help="encoder checkpoint served at /v1/embeddings")
+            p.add_argument("--asr-model", default=None, help="Whisper checkpoint served at /v1/audio/transcriptions")
     p = sub.add_parser("profile")
     p.add_argument("--model", default="qwen3-0.6b")
     p.add_argument("--batch", type=int, default=8)

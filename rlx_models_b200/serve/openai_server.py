@@ -4,7 +4,9 @@
 
 Endpoints: ``GET /health``, ``GET /v1/models``, ``GET /metrics``
 (Prometheus text), ``POST /v1/completions``, ``POST /v1/chat/completions``,
-``POST /v1/embeddings`` (when the server was given an embedder).
+``POST /v1/embeddings`` (when the server was given an embedder),
+``POST /v1/audio/transcriptions`` (multipart WAV upload, when it was given a
+transcriber).
 Prompts may be text (tokenised with the checkpoint's tokenizer, or bytes
 for random-weight shapes) or token-id arrays. Sampling fields: ``max_tokens``,
 ``temperature``, ``top_p``, ``top_k``, ``min_p``, ``seed``, ``stop`` (strings),
@@ -16,6 +18,8 @@ Reference: rlx-openai (OpenAI route shapes, SSE framing) and rlx-serve
 src/engine.rs, src/backend.rs:116-167 (stop strings).
 """
 from __future__ import annotations
+
+import torch
 
 import json
 import time
@@ -51,9 +55,30 @@ def _params(body: dict, eos: int | None) -> tuple[SamplingParams, list[str]]:
     return sp, list(stop)
 
 
-def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model", embedder=None):
+def decode_wav(data: bytes) -> tuple[torch.Tensor, int]:
+    """PCM WAV bytes (8 / 16 / 32-bit integer, any channel count) -> (mono fp32
+    samples in [-1, 1], sample rate)."""
+    import io
+    import wave
+    with wave.open(io.BytesIO(data)) as w:
+        ch, width, sr, n = w.getnchannels(), w.getsampwidth(), w.getframerate(), w.getnframes()
+        raw = w.readframes(n)
+    if width == 1:
+        x = torch.frombuffer(bytearray(raw), dtype=torch.uint8).float().sub_(128.0).div_(128.0)
+    elif width == 2:
+        x = torch.frombuffer(bytearray(raw), dtype=torch.int16).float().div_(32768.0)
+    elif width == 4:
+        x = torch.frombuffer(bytearray(raw), dtype=torch.int32).float().div_(2147483648.0)
+    else:
+        raise ValueError(f"unsupported WAV sample width {width}")
+    return x.view(-1, ch).mean(1), sr
+
+
+def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model", embedder=None, transcriber=None):
     """``embedder``: any object with ``embed(inputs) -> [N, D]`` over a list of
-    strings or of token-id lists (``api.load_embedder``, ``LLM.embed``)."""
+    strings or of token-id lists (``api.load_embedder``, ``LLM.embed``);
+    ``transcriber``: any object with ``transcribe(samples, sample_rate) -> str``
+    (``api.load_transcriber``)."""
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
     from prometheus_client import CollectorRegistry, Counter, Histogram, generate_latest
@@ -201,6 +226,21 @@ def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model", 
         return {"object": "list", "data": data, "model": body.get("model", model_name),
                 "usage": {"prompt_tokens": n_tok, "total_tokens": n_tok}}
 
+    if transcriber is not None:
+        from fastapi import File, UploadFile
+
+        async def transcriptions(file=File(...)):
+            m_req.labels("transcriptions").inc()
+            try:
+                audio, sr = decode_wav(await file.read())
+            except Exception as e:  # not a PCM WAV file
+                raise HTTPException(400, f"could not read the audio: {e}")
+            return {"text": transcriber.transcribe(audio, sr)}
+
+        # a real type object (not a postponed string) so that FastAPI reads it as an upload
+        transcriptions.__annotations__ = {"file": UploadFile}
+        app.post("/v1/audio/transcriptions")(transcriptions)
+
     @app.post("/v1/chat/completions")
     def chat(body: dict):
         m_req.labels("chat").inc()
@@ -221,13 +261,14 @@ def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model", 
     return app
 
 
-def serve(llm, host: str = "127.0.0.1", port: int = 8000, model_name: str = "b200-model", embedder=None):
+def serve(llm, host: str = "127.0.0.1", port: int = 8000, model_name: str = "b200-model", embedder=None,
+          transcriber=None):
     import uvicorn
 
     from ..tokenizer import ByteTokenizer
     tok = llm.tokenizer or ByteTokenizer()
     runner = EngineRunner(llm.engine, tok)
-    app = create_app(runner, tok, model_name, embedder=embedder)
+    app = create_app(runner, tok, model_name, embedder=embedder, transcriber=transcriber)
     try:
         uvicorn.run(app, host=host, port=port, log_level="info")
     finally:

@@ -206,3 +206,28 @@ def test_embeddings_endpoint():
     with TestClient(create_app(runner, tok, "fake")) as c:
         assert c.post("/v1/embeddings", json={"input": "x"}).status_code == 404
     runner.shutdown()
+
+
+class _FakeTranscriber:
+    def transcribe(self, audio, sr):
+        return f"{audio.numel()} samples at {sr} Hz, peak {float(audio.abs().max()):.2f}"
+
+
+def test_transcriptions_endpoint():
+    import io
+    import struct
+    import wave
+    buf = io.BytesIO()
+    with wave.open(buf, "wb") as w:  # stereo 16-bit, 8 kHz
+        w.setnchannels(2)
+        w.setsampwidth(2)
+        w.setframerate(8000)
+        w.writeframes(b"".join(struct.pack("<hh", 16384, 16384) for _ in range(400)))
+    tok = ByteTokenizer()
+    runner = EngineRunner(FakeEngine(), tok)
+    with TestClient(create_app(runner, tok, "fake", transcriber=_FakeTranscriber())) as c:
+        r = c.post("/v1/audio/transcriptions", files={"file": ("a.wav", buf.getvalue(), "audio/wav")})
+        assert r.status_code == 200 and r.json()["text"] == "400 samples at 8000 Hz, peak 0.50"
+        bad = c.post("/v1/audio/transcriptions", files={"file": ("a.wav", b"not audio", "audio/wav")})
+        assert bad.status_code == 400
+    runner.shutdown()
