@@ -31,6 +31,14 @@ times ``routed_scaling_factor``. Routed experts run on the grouped MXFP4 GEMM
 SwiGLU on the tcgen05 GEMM; the first ``first_k_dense_replace`` layers are
 dense.
 
+GLM-4.7-Flash (``glm4_moe_lite``) is this architecture with GLM-4.5's router
+and per-layer ``mlp_layer_types``; GLM-5 (``glm_moe_dsa``) adds DeepSeek
+sparse attention: an indexer (its own small multi-head projections from the
+q_a latent and the hidden state, ReLU scores weighted per head) keeps the
+``index_topk`` best keys per query, and RoPE rotates split halves. The oracle
+applies the indexer; the served model attends densely, which is the same
+model while a sequence holds at most ``index_topk`` (2048) tokens.
+
 ``DeepseekOracle`` is the fp32 full-sequence restatement (expanded MLA, exact
 routing); it matches ``transformers``' DeepseekV3 / V2 on CPU and is the GPU
 model's numerics reference.
@@ -40,7 +48,8 @@ Reference: crates/rlx-deepseek/src/config.rs:35-150 (`DeepseekV3Config`,
 (`emit_mla_attention`: the same projections, expanded K/V with the value
 zero-padded to the qk width), src/moe.rs:16-40 and :133-279
 (`emit_deepseek_moe`: noaux_tc group-limited router, shared expert);
-rlx-models-core src/standard_decoder.rs:2045 (`build_deepseek_mla`).
+rlx-models-core src/standard_decoder.rs:2045 (`build_deepseek_mla`);
+crates/rlx-glm5next src/indexer.rs (DSA indexer), src/mla.rs.
 """
 from __future__ import annotations
 
@@ -55,7 +64,7 @@ import torch.nn.functional as F
 from ..ops import rope_inv_freq
 from ..runtime.kv_cache import BLOCK_SIZE
 
-DEEPSEEK_TYPES = ("deepseek_v3", "deepseek_v2", "kimi_k2")
+DEEPSEEK_TYPES = ("deepseek_v3", "deepseek_v2", "kimi_k2", "glm4_moe_lite", "glm_moe_dsa")
 _SUB_NORM_EPS = 1e-6  # q_a_layernorm / kv_a_layernorm use the RMSNorm default, not rms_norm_eps
 
 
@@ -93,6 +102,10 @@ class DeepseekConfig:
     attention_bias: bool = False
     bos_token_id: int | None = 0
     eos_token_id: int | list | None = 1
+    mlp_layer_types: list | None = None  # GLM: "dense" / "sparse" per layer (overrides first_k_dense_replace)
+    index_topk: int = 0  # GLM-5 DSA: keys kept per query by the indexer (0: dense attention)
+    index_n_heads: int = 32
+    index_head_dim: int = 128
     extra: dict = field(default_factory=dict)
 
     @property
@@ -104,6 +117,8 @@ class DeepseekConfig:
         return self.kv_lora_rank + self.qk_rope_head_dim
 
     def is_moe(self, i: int) -> bool:
+        if self.mlp_layer_types:
+            return bool(self.n_routed_experts) and self.mlp_layer_types[i] == "sparse"
         return bool(self.n_routed_experts) and i >= self.first_k_dense_replace and i % self.moe_layer_freq == 0
 
     @property
@@ -135,6 +150,20 @@ class DeepseekConfig:
             kw.setdefault("norm_topk_prob", False)
             kw.setdefault("routed_scaling_factor", 1.0)
             kw.setdefault("rope_interleave", True)
+        if mt in ("glm4_moe_lite", "glm_moe_dsa"):  # GLM-4.7-Flash / GLM-5: MLA + GLM-4.5's MoE
+            n = kw.get("num_hidden_layers", cls.num_hidden_layers)
+            if not kw.get("mlp_layer_types"):
+                k0 = 1 if mt == "glm4_moe_lite" else min(3, n)
+                kw["mlp_layer_types"] = ["dense"] * k0 + ["sparse"] * (n - k0)
+            kw.setdefault("rms_norm_eps", 1e-5)
+            kw.setdefault("routed_scaling_factor", 1.8 if mt == "glm4_moe_lite" else 2.5)
+            for k in ("n_group", "topk_group"):
+                kw.setdefault(k, 1)
+            if mt == "glm_moe_dsa":
+                kw["rope_interleave"] = False  # GLM-5 rotates split halves in MLA and the indexer
+                kw.setdefault("index_topk", 2048)
+            else:
+                kw["index_topk"] = 0
         for k in ("n_group", "topk_group"):
             if kw.get(k) is None:
                 kw[k] = 1
@@ -254,6 +283,13 @@ def random_weights(cfg: DeepseekConfig, seed: int = 0, device="cpu", dtype=torch
         ones(a + "kv_a_layernorm.weight", cfg.kv_lora_rank)
         lin(a + "kv_b_proj.weight", nh * (cfg.qk_nope_head_dim + cfg.v_head_dim), cfg.kv_lora_rank)
         lin(a + "o_proj.weight", H, nh * cfg.v_head_dim)
+        if cfg.index_topk and cfg.q_lora_rank:
+            x = a + "indexer."
+            lin(x + "wq_b.weight", cfg.index_n_heads * cfg.index_head_dim, cfg.q_lora_rank)
+            lin(x + "wk.weight", cfg.index_head_dim, H)
+            ones(x + "k_norm.weight", cfg.index_head_dim)
+            w[x + "k_norm.bias"] = torch.zeros(cfg.index_head_dim, device=device, dtype=dtype)
+            lin(x + "weights_proj.weight", cfg.index_n_heads, H)
         m = p + "mlp."
         if cfg.is_moe(i):
             I = cfg.moe_intermediate_size
@@ -308,9 +344,11 @@ class DeepseekOracle:
         S = x.shape[0]
         nh, dn, dr, dv, r = c.num_attention_heads, c.qk_nope_head_dim, c.qk_rope_head_dim, c.v_head_dim, c.kv_lora_rank
         a = f"model.layers.{i}.self_attn."
+        q_res = None
         if c.q_lora_rank:
-            q = self._rms(x @ self._t(a + "q_a_proj.weight").t(), self._t(a + "q_a_layernorm.weight"), _SUB_NORM_EPS)
-            q = q @ self._t(a + "q_b_proj.weight").t()
+            q_res = self._rms(x @ self._t(a + "q_a_proj.weight").t(), self._t(a + "q_a_layernorm.weight"),
+                              _SUB_NORM_EPS)
+            q = q_res @ self._t(a + "q_b_proj.weight").t()
         else:
             q = x @ self._t(a + "q_proj.weight").t()
         q = q.view(S, nh, dn + dr)
@@ -322,9 +360,33 @@ class DeepseekOracle:
         k_rot = apply_rope(ckv[:, None, r:], pos, self.inv, self.mult, c.rope_interleave).expand(S, nh, dr)
         qf = torch.cat([q[..., :dn], q_rot], -1).transpose(0, 1)
         kf = torch.cat([kv[..., :dn], k_rot], -1).transpose(0, 1)
-        o = F.scaled_dot_product_attention(qf, kf, kv[..., dn:].transpose(0, 1), is_causal=True,
-                                           scale=c.softmax_scale)
+        mask = None
+        if c.index_topk and q_res is not None and (a + "indexer.wq_b.weight") in self.w:
+            sel = self.dsa_select(i, x, q_res, pos)
+            mask = torch.zeros(S, S, dtype=torch.bool, device=x.device).scatter_(1, sel, True)
+            mask &= torch.ones(S, S, dtype=torch.bool, device=x.device).tril()
+        o = F.scaled_dot_product_attention(qf, kf, kv[..., dn:].transpose(0, 1), attn_mask=mask,
+                                           is_causal=mask is None, scale=c.softmax_scale)
         return o.transpose(0, 1).reshape(S, nh * dv)
+
+    def dsa_select(self, i: int, x: torch.Tensor, q_res: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """GLM-5 DSA indexer of layer ``i``: [S, min(index_topk, S)] key positions
+        per query. Index queries come from the normalised q_a latent, one index
+        key per token (LayerNorm of wk(x)); both carry RoPE on their first
+        qk_rope_head_dim values. score[s, t] = sum_h w[s, h] relu(q[s, h] . k[t] / sqrt(D)),
+        w = weights_proj(x) / sqrt(heads); future positions score -inf."""
+        c = self.cfg
+        a = f"model.layers.{i}.self_attn.indexer."
+        S, H, D, dr = x.shape[0], c.index_n_heads, c.index_head_dim, c.qk_rope_head_dim
+        q = (q_res @ self._t(a + "wq_b.weight").t()).view(S, H, D)
+        k = F.layer_norm(x @ self._t(a + "wk.weight").t(), (D,), self._t(a + "k_norm.weight"),
+                         self._t(a + "k_norm.bias"), 1e-6)
+        q = torch.cat([apply_rope(q[..., :dr], pos, self.inv, self.mult, False), q[..., dr:]], -1)
+        k = torch.cat([apply_rope(k[:, None, :dr], pos, self.inv, self.mult, False)[:, 0], k[:, dr:]], -1)
+        w = (x @ self._t(a + "weights_proj.weight").t()) * H ** -0.5
+        score = torch.einsum("sht,sh->st", torch.relu(torch.einsum("shd,td->sht", q, k) * D ** -0.5), w)
+        future = torch.ones(S, S, dtype=torch.bool, device=x.device).triu(1)
+        return score.masked_fill(future, float("-inf")).topk(min(c.index_topk, S), -1).indices
 
     def moe(self, i: int, x: torch.Tensor) -> torch.Tensor:
         c = self.cfg
@@ -415,6 +477,10 @@ class DeepseekLM:
     def __init__(self, cfg: DeepseekConfig, weights, device="cuda"):
         from .. import ops
         from .moe import pack_experts
+        if cfg.index_topk:
+            import warnings
+            warnings.warn(f"{cfg.model_type}: the served model attends densely; it equals the DSA model while a "
+                          f"sequence holds at most index_topk={cfg.index_topk} tokens")
         self.cfg, self.device = cfg, torch.device(device)
         self.hkv, self.D = 1, cfg.latent_dim  # one shared latent "head" per token
         c, dev, bf = cfg, self.device, torch.bfloat16

@@ -62,7 +62,7 @@ def _moe(cfg, weights, device, tp_rank, tp_size, comm):
     return MoEDecoderLM(cfg, weights, device=device, ep_rank=tp_rank, ep_size=tp_size, comm=comm)
 
 
-@register("deepseek_v3", "deepseek_v2", "kimi_k2")
+@register("deepseek_v3", "deepseek_v2", "kimi_k2", "glm4_moe_lite", "glm_moe_dsa")
 def _deepseek(cfg, weights, device, tp_rank, tp_size, comm):
     from .models.deepseek import DeepseekLM
     if tp_size != 1:
@@ -106,7 +106,7 @@ def build_model(cfg: DecoderConfig, weights=None, *, device="cuda", tp_rank=0, t
     fn = _BUILDERS.get(cfg.model_type)
     if fn is None:
         raise KeyError(f"no builder for model_type={cfg.model_type!r}; registered: {registered()}")
-    if weights is None and cfg.model_type in ("deepseek_v3", "deepseek_v2", "kimi_k2"):
+    if weights is None and cfg.model_type in ("deepseek_v3", "deepseek_v2", "kimi_k2", "glm4_moe_lite", "glm_moe_dsa"):
         from .models.deepseek import random_weights
         weights = random_weights(cfg, seed, device)
     elif weights is None and cfg.model_type in ("qwen3_5_text", "qwen3_5", "qwen3_5_moe_text", "qwen3_5_moe",
