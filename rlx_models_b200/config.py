@@ -75,6 +75,7 @@ class DecoderConfig:
     max_position_embeddings: int = 40960
     tie_word_embeddings: bool = False
     qk_norm: bool = True
+    qk_norm_full: bool = False  # one RMSNorm over all heads' q (and k) values (OLMo-2, MiniMax-M2)
     attention_bias: bool = False
     mlp_bias: bool = False
     # sliding window: per-layer list of "full_attention" / "sliding_attention"
@@ -165,6 +166,18 @@ class DecoderConfig:
             kw["num_experts_per_tok"] = d.get("num_experts_per_tok", 2)
             kw["moe_intermediate_size"] = d.get("intermediate_size", 14336)
             kw["norm_topk_prob"] = True
+        elif mt == "minimax_m2":  # full-width QK-norm, partial RoPE, sigmoid routing with a correction bias
+            kw["qk_norm"] = kw["qk_norm_full"] = True
+            kw["num_experts"] = d.get("num_local_experts", 256)
+            kw["num_experts_per_tok"] = d.get("num_experts_per_tok", 8)
+            kw["moe_intermediate_size"] = d.get("intermediate_size", 1536)
+            kw["router_scoring"] = "sigmoid"
+            kw["norm_topk_prob"] = True
+            for k, dflt in (("n_group", 1), ("topk_group", 1), ("routed_scaling_factor", 1.0),
+                            ("n_shared_experts", 0), ("first_k_dense_replace", 0)):
+                kw[k] = dflt
+            if d.get("rotary_dim") and not d.get("partial_rotary_factor"):
+                kw["partial_rotary_factor"] = d["rotary_dim"] / kw.get("head_dim", d.get("head_dim", 128))
         elif mt == "qwen2_moe":
             kw["qk_norm"] = False
             kw["attention_bias"] = True
@@ -265,7 +278,7 @@ class DecoderConfig:
     def to_hf_dict(self) -> dict:
         d = {k: v for k, v in dataclasses.asdict(self).items() if k != "extra"}
         d.update(self.extra)
-        if self.model_type in ("gpt_oss", "mixtral"):
+        if self.model_type in ("gpt_oss", "mixtral", "minimax_m2"):
             d["num_local_experts"] = self.num_experts
             d["intermediate_size"] = self.moe_intermediate_size
         if self.model_type == "glm4_moe":

@@ -96,7 +96,10 @@ class DecoderOracle:
         q = proj("q_proj").view(T, c.num_attention_heads, c.head_dim)
         k = proj("k_proj").view(T, c.num_key_value_heads, c.head_dim)
         v = proj("v_proj").view(T, c.num_key_value_heads, c.head_dim)
-        if c.qk_norm:
+        if c.qk_norm_full:  # one norm over all heads of the token
+            q = R.rmsnorm(q.reshape(T, -1), self.N(p + "q_norm.weight"), c.rms_norm_eps).view_as(q)
+            k = R.rmsnorm(k.reshape(T, -1), self.N(p + "k_norm.weight"), c.rms_norm_eps).view_as(k)
+        elif c.qk_norm:
             q = R.rmsnorm(q, self.N(p + "q_norm.weight"), c.rms_norm_eps)
             k = R.rmsnorm(k, self.N(p + "k_norm.weight"), c.rms_norm_eps)
         inv, mult = (self.local_rope if self.local_rope is not None and c.layer_window(i) > 0

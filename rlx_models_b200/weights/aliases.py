@@ -1,7 +1,7 @@
 """Checkpoint tensor names of model families that differ only in naming from
 the canonical layout the builders read (Qwen3-MoE style MoE names).
 
-Mixtral: ``block_sparse_moe.gate`` is the router, ``block_sparse_moe.experts.{e}.w1 / w3 / w2``
+Mixtral and MiniMax-M2: ``block_sparse_moe.gate`` is the router, ``block_sparse_moe.experts.{e}.w1 / w3 / w2``
 are gate / up / down. ``canonical_name`` maps a checkpoint name to the
 canonical one; ``CanonicalView`` presents a weight source under canonical names.
 """
@@ -15,10 +15,15 @@ _MIXTRAL = [(re.compile(r"\.block_sparse_moe\.gate\."), ".mlp.gate."),
             (re.compile(r"\.block_sparse_moe\.experts\.(\d+)\.w2\."), r".mlp.experts.\1.down_proj.")]
 
 
+# MiniMax-M2: Mixtral's expert names plus the routing correction bias, which
+# sits on the MoE block (``block_sparse_moe.`` in the release, ``mlp.`` in transformers)
+_MINIMAX = _MIXTRAL + [(re.compile(r"\.(?:block_sparse_moe|mlp)\.e_score_correction_bias$"),
+                        ".mlp.gate.e_score_correction_bias")]
+
+
 def canonical_name(model_type: str, name: str) -> str:
-    if model_type == "mixtral":
-        for pat, rep in _MIXTRAL:
-            name = pat.sub(rep, name)
+    for pat, rep in {"mixtral": _MIXTRAL, "minimax_m2": _MINIMAX}.get(model_type, ()):
+        name = pat.sub(rep, name)
     return name
 
 
