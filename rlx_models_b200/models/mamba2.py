@@ -71,6 +71,19 @@ class SSMConfig:
     max_position_embeddings: int = 262144
     bos_token_id: int | None = None
     eos_token_id: int | list | None = None
+    # nemotron_h: one mixer per block ("mamba" | "attention" | "moe"), NoPE
+    # attention, group-wise gated norm, squared-ReLU MoE (sigmoid group routing)
+    layer_types: list = field(default_factory=list)
+    norm_groups: int = 1
+    n_routed_experts: int = 0
+    num_experts_per_tok: int = 0
+    moe_intermediate_size: int = 0
+    moe_shared_expert_intermediate_size: int = 0
+    moe_latent_size: int | None = None
+    n_group: int = 1
+    topk_group: int = 1
+    norm_topk_prob: bool = True
+    routed_scaling_factor: float = 1.0
     extra: dict = field(default_factory=dict)
 
     @property
@@ -87,6 +100,9 @@ class SSMConfig:
 
     def is_attention(self, i: int) -> bool:
         return i in self.attn_layer_indices
+
+    def is_moe(self, i: int) -> bool:
+        return bool(self.layer_types) and self.layer_types[i] == "moe"
 
     @property
     def rotary_dim(self) -> int:
@@ -113,6 +129,25 @@ class SSMConfig:
             # partial_rotary_factor says; the oracle follows it
             kw["partial_rotary_factor"] = 1.0
             kw["rms_norm_eps"] = d.get("rms_norm_eps", 1e-5)
+        elif mt == "nemotron_h":
+            lt = d.get("layers_block_type") or d.get("layer_types")
+            if not lt:
+                code = {"M": "mamba", "*": "attention", "E": "moe", "-": "mlp"}
+                lt = [code[ch] for ch in d.get("hybrid_override_pattern", "ME*E")]
+            kw["layer_types"] = list(lt)
+            kw["num_hidden_layers"] = len(lt)
+            kw["attn_layer_indices"] = [i for i, t in enumerate(lt) if t == "attention"]
+            for src, dst in (("mamba_num_heads", "num_heads"), ("mamba_head_dim", "head_dim"),
+                             ("ssm_state_size", "state_size"), ("n_groups", "n_groups"), ("mamba_n_groups", "n_groups"),
+                             ("conv_kernel", "conv_kernel"), ("use_conv_bias", "use_conv_bias"),
+                             ("use_bias", "use_bias")):
+                if src in d:
+                    kw[dst] = d[src]
+            kw["attn_head_dim"] = d.get("head_dim") or d["hidden_size"] // d["num_attention_heads"]
+            kw["head_dim"] = d.get("mamba_head_dim", 64)
+            kw["norm_groups"] = kw.get("n_groups", 8)
+            kw["partial_rotary_factor"] = 0.0  # no positional encoding in the attention layers
+            kw["rms_norm_eps"] = d.get("layer_norm_epsilon", 1e-5)
         else:
             kw["rms_norm_eps"] = d.get("layer_norm_epsilon", d.get("rms_norm_eps", 1e-5))
         if "time_step_limit" in d:
@@ -196,15 +231,17 @@ def ssd_mixer_seq(cfg: SSMConfig, proj: torch.Tensor, conv_w, conv_b, A_log, dt_
     return y.reshape(L, I), z, win, S
 
 
-def gated_norm(y: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    """rmsnorm(y * silu(z)) * w over the last dim (fp32)."""
+def gated_norm(y: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float, groups: int = 1) -> torch.Tensor:
+    """rmsnorm(y * silu(z)) * w over the last dim (fp32), in ``groups`` equal
+    slices each with its own mean square (Nemotron-H) or over the whole width."""
     t = y.float() * F.silu(z.float())
-    return t * torch.rsqrt(t.pow(2).mean(-1, keepdim=True) + eps) * w.float()
+    g = t.view(*t.shape[:-1], groups, -1)
+    return (g * torch.rsqrt(g.pow(2).mean(-1, keepdim=True) + eps)).view_as(t) * w.float()
 
 
 def _names(cfg: SSMConfig):
     """(embed, final norm, layer prefix, block-norm, mixer prefix) names of the family."""
-    if cfg.model_type == "mamba2":
+    if cfg.model_type in ("mamba2", "nemotron_h"):
         return "backbone.embeddings.weight", "backbone.norm_f.weight", "backbone.layers.{i}.", "norm", "mixer."
     return "model.embed_tokens.weight", "model.final_layernorm.weight", "model.layers.{i}.", "input_layernorm", \
         "mamba."
@@ -259,9 +296,12 @@ class SSMOracle:
     """fp32 full-sequence forward."""
 
     def __init__(self, cfg: SSMConfig, weights, device="cpu", chunk: int = 64):
+        if cfg.model_type == "nemotron_h" and "backbone.embeddings.weight" not in weights and hasattr(weights, "items"):
+            # transformers keeps Nemotron-H under ``model.``; the released checkpoints use ``backbone.``
+            weights = {("backbone." + k[6:] if k.startswith("model.") else k): v for k, v in weights.items()}
         self.cfg, self.device, self.chunk, self.get = cfg, torch.device(device), chunk, _getter(weights)
         self.has = lambda n: n in weights  # noqa: E731
-        if cfg.attn_layer_indices:
+        if cfg.attn_layer_indices and cfg.rotary_dim:
             self.inv, self.mult = rope_inv_freq(cfg.rotary_dim, cfg.rope_theta, None, cfg.max_position_embeddings)
 
     def _t(self, n):
@@ -269,6 +309,33 @@ class SSMOracle:
 
     def _rms(self, x, n):
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.cfg.rms_norm_eps) * self._t(n)
+
+    def _expert(self, m: str, e: int, which: str) -> torch.Tensor:
+        fused = m + f"experts.{which}"
+        return self._t(fused)[e] if self.has(fused) else self._t(m + f"experts.{e}.{which}.weight")
+
+    def _moe(self, m: str, x: torch.Tensor) -> torch.Tensor:
+        """Nemotron-H MoE: sigmoid group-limited routing with the correction bias,
+        squared-ReLU experts (up -> relu^2 -> down, no gate), optionally in a
+        latent width (fc1 / fc2 latent projections around the routed experts),
+        plus a squared-ReLU shared expert on the block input."""
+        from types import SimpleNamespace
+        from .deepseek import route
+        c = self.cfg
+        spec = SimpleNamespace(scoring_func="sigmoid", topk_method="noaux_tc", n_group=c.n_group,
+                               topk_group=c.topk_group, num_experts_per_tok=c.num_experts_per_tok,
+                               norm_topk_prob=c.norm_topk_prob, routed_scaling_factor=c.routed_scaling_factor)
+        idx, wts = route(spec, x @ self._t(m + "gate.weight").t(), self._t(m + "gate.e_score_correction_bias"))
+        xl = x @ self._t(m + "fc1_latent_proj.weight").t() if self.has(m + "fc1_latent_proj.weight") else x
+        out = torch.zeros_like(xl)
+        for e in idx.unique().tolist():
+            rows, slot = (idx == e).nonzero(as_tuple=True)
+            y = torch.relu(xl[rows] @ self._expert(m, e, "up_proj").t()).square() @ self._expert(m, e, "down_proj").t()
+            out.index_add_(0, rows, y * wts[rows, slot, None])
+        if self.has(m + "fc2_latent_proj.weight"):
+            out = out @ self._t(m + "fc2_latent_proj.weight").t()
+        s = m + "shared_experts."
+        return out + torch.relu(x @ self._t(s + "up_proj.weight").t()).square() @ self._t(s + "down_proj.weight").t()
 
     @torch.no_grad()
     def logits(self, ids) -> torch.Tensor:
@@ -282,10 +349,14 @@ class SSMOracle:
         for i in range(c.num_hidden_layers):
             p = lay.format(i=i)
             x = self._rms(h, p + bn + ".weight")
-            if c.is_attention(i):
-                a, D, nh, nkv = p + "self_attn.", c.attn_head_dim, c.num_attention_heads, c.num_key_value_heads
-                q = R.rope((x @ self._t(a + "q_proj.weight").t()).view(S, nh, D), pos, self.inv, self.mult)
-                k = R.rope((x @ self._t(a + "k_proj.weight").t()).view(S, nkv, D), pos, self.inv, self.mult)
+            if c.is_moe(i):
+                h = h + self._moe(p + mix, x)
+            elif c.is_attention(i):
+                a, D, nh, nkv = p + ("mixer." if c.model_type == "nemotron_h" else "self_attn."), c.attn_head_dim, c.num_attention_heads, c.num_key_value_heads
+                q = (x @ self._t(a + "q_proj.weight").t()).view(S, nh, D)
+                k = (x @ self._t(a + "k_proj.weight").t()).view(S, nkv, D)
+                if c.rotary_dim:
+                    q, k = R.rope(q, pos, self.inv, self.mult), R.rope(k, pos, self.inv, self.mult)
                 v = (x @ self._t(a + "v_proj.weight").t()).view(S, nkv, D)
                 o = R.attention(q, k, v, pos, pos, D ** -0.5, causal=True).reshape(S, nh * D)
                 h = h + o @ self._t(a + "o_proj.weight").t()
@@ -295,7 +366,8 @@ class SSMOracle:
                 cb = self._t(m + "conv1d.bias") if self.has(m + "conv1d.bias") else None
                 y, z, _, _ = ssd_mixer_seq(c, proj, self._t(m + "conv1d.weight")[:, 0], cb, self._t(m + "A_log"),
                                            self._t(m + "dt_bias"), self._t(m + "D"), chunk=self.chunk)
-                h = h + gated_norm(y, z, self._t(m + "norm.weight"), c.rms_norm_eps) @ self._t(m + "out_proj.weight").t()
+                h = h + gated_norm(y, z, self._t(m + "norm.weight"), c.rms_norm_eps, c.norm_groups) @ \
+                    self._t(m + "out_proj.weight").t()
             if c.has_ffn:
                 x = self._rms(h, p + "pre_ff_layernorm.weight")
                 f = p + "feed_forward."
