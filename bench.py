@@ -46,7 +46,7 @@ WORKLOADS = {
 
 def reference_arm(args):
     why = ("reference is a Rust/cargo workspace whose engine crates (rlx, rlx-cuda, rlx-runtime ...) are not "
-           "in the tree; pip install of /root/reference fails (no setup.py/pyproject) and there is no cargo")
+           "in the tree; pip install of the reference tree fails (no setup.py/pyproject) and there is no cargo")
     print(json.dumps({"impl": "reference", "unavailable": why}))
     return 0
 
@@ -98,7 +98,8 @@ def serve(args):
                             hidden=cfg.hidden_size)
     ecfg = EngineConfig(max_num_seqs=max(64, args.num_requests), max_batched_tokens=args.max_batched_tokens,
                         max_model_len=args.max_prompt + args.output_len + 16, kv_memory_gb=args.kv_gb,
-                        prefix_caching=False, cuda_graphs=True)
+                        prefix_caching=False, cuda_graphs=True, async_scheduling=bool(args.async_sched),
+                        metrics_path=args.engine_metrics if rank == 0 else None)
     llm = load(W["model"], device=dev, tp_rank=rank, tp_size=ws, comm=comm, seed=0, engine_config=ecfg,
                config=cfg)
     eng = llm.engine
@@ -173,6 +174,7 @@ def serve(args):
                    "global_batch": args.num_requests, "seq_len": f"prompt U[{args.min_prompt},{args.max_prompt}]"
                    f" + {args.output_len} out", "parallelism": f"{W['par']}{ws}",
                    "tp_comm": args.tp_comm if (ws > 1 and W["par"] == "tp") else None, "kv_block": 16,
+                   "async_scheduling": bool(args.async_sched),
                    "max_batched_tokens": args.max_batched_tokens, "l2": W["l2"],
                    "step": f"one full {args.num_requests}-request serving pass"},
         "ttft_p50_ms": round(ttft, 1), "tpot_p50_ms": round(tpot, 2),
@@ -211,6 +213,9 @@ def main():
                     help="train: 1 = recompute each layer in backward (0 fits: activations of 4 x 4096 tokens ~70 GB)")
     ap.add_argument("--grad-reduce", default="push", choices=["push", "nccl"],
                     help="train: FSDP gradient reduce-scatter by NVLink push or NCCL")
+    ap.add_argument("--async-sched", type=int, default=1,
+                    help="serving: 1 = schedule / launch step n+1 while step n runs (default), 0 = synchronous loop")
+    ap.add_argument("--engine-metrics", default=None, help="serving: write per-step engine metrics (JSONL) here")
     ap.add_argument("--tp-comm", default="pull", choices=["nccl", "fused", "pull"],
                     help="pull (default): decode steps read every rank's GEMM partial over NVLink in one kernel "
                          "with the residual add + RMSNorm, prefill on NCCL; nccl: NCCL all-reduce baseline; "

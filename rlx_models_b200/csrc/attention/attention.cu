@@ -73,7 +73,11 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
   int first_tok = 0;
   if (a.window > 0) first_tok = max(0, ctx - a.window);
   const int first_page = first_tok >> 4;
-  const int last_page = (ctx + 15) >> 4;  // exclusive
+  int last_page = (ctx + 15) >> 4;  // exclusive
+  if (last_page > a.max_blocks) {  // ctx_lens[b] > 16 * max_blocks: never read past the table row
+    if (threadIdx.x == 0 && blockIdx.y == 0) report_error(a.status, kErrBounds, b);
+    last_page = a.max_blocks;
+  }
   const int npages = max(0, last_page - first_page);
   const int pps = (npages + nsplit - 1) / nsplit;
   const int p0 = first_page + split * pps;
@@ -545,11 +549,6 @@ __global__ void __launch_bounds__(288) prefill_attn_kernel(const __grid_constant
   }
 }
 
-template <typename K>
-static void set_smem(K kern, int bytes, int device) {
-  (void)device;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-}
 
 }  // namespace attn
 
@@ -577,22 +576,19 @@ int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
   if (a.D == 256) {
     constexpr int NST = 4;
     auto k = decode_attn_kernel<256, NST>;
-    static bool once = false;
-    if (!once) { set_smem(k, DecCfg<256, NST>::SMEM, a.device); once = true; }
+    ensure_smem(k, DecCfg<256, NST>::SMEM);
     launch_pdl(k, grid, dim3(160), DecCfg<256, NST>::SMEM, st, tk, tv, a);
     if (splits > 1) launch_pdl(decode_merge_kernel<256>, dim3(a.B * a.Hq), dim3(256), 0, st, a, splits);
   } else if (a.D == 128) {
     constexpr int NST = 8;
     auto k = decode_attn_kernel<128, NST>;
-    static bool once = false;
-    if (!once) { set_smem(k, DecCfg<128, NST>::SMEM, a.device); once = true; }
+    ensure_smem(k, DecCfg<128, NST>::SMEM);
     launch_pdl(k, grid, dim3(160), DecCfg<128, NST>::SMEM, st, tk, tv, a);
     if (splits > 1) launch_pdl(decode_merge_kernel<128>, dim3(a.B * a.Hq), dim3(128), 0, st, a, splits);
   } else {
     constexpr int NST = 8;
     auto k = decode_attn_kernel<64, NST>;
-    static bool once = false;
-    if (!once) { set_smem(k, DecCfg<64, NST>::SMEM, a.device); once = true; }
+    ensure_smem(k, DecCfg<64, NST>::SMEM);
     launch_pdl(k, grid, dim3(160), DecCfg<64, NST>::SMEM, st, tk, tv, a);
     if (splits > 1) launch_pdl(decode_merge_kernel<64>, dim3(a.B * a.Hq), dim3(64), 0, st, a, splits);
   }
@@ -620,20 +616,17 @@ void prefill_attention_launch(const AttnArgs& a, cudaStream_t st) {
   if (a.D == 256) {
     constexpr int NST = 2;
     auto k = prefill_attn_kernel<256, NST>;
-    static bool once = false;
-    if (!once) { set_smem(k, PreCfg<256, NST>::SMEM, a.device); once = true; }
+    ensure_smem(k, PreCfg<256, NST>::SMEM);
     launch_pdl(k, grid, dim3(288), PreCfg<256, NST>::SMEM, st, tk, tv, a, q_tiles, rows_tok);
   } else if (a.D == 128) {
     constexpr int NST = 2;
     auto k = prefill_attn_kernel<128, NST>;
-    static bool once = false;
-    if (!once) { set_smem(k, PreCfg<128, NST>::SMEM, a.device); once = true; }
+    ensure_smem(k, PreCfg<128, NST>::SMEM);
     launch_pdl(k, grid, dim3(288), PreCfg<128, NST>::SMEM, st, tk, tv, a, q_tiles, rows_tok);
   } else {
     constexpr int NST = 3;
     auto k = prefill_attn_kernel<64, NST>;
-    static bool once = false;
-    if (!once) { set_smem(k, PreCfg<64, NST>::SMEM, a.device); once = true; }
+    ensure_smem(k, PreCfg<64, NST>::SMEM);
     launch_pdl(k, grid, dim3(288), PreCfg<64, NST>::SMEM, st, tk, tv, a, q_tiles, rows_tok);
   }
 }
@@ -737,13 +730,24 @@ extern "C" int b200_decode_attention_noalloc(const void* q, const void* k_cache,
     return B200_NOALLOC_ERR_TMA;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  dim3 grid(B * Hkv, splits);
+  // cudaLaunchKernelEx returns this launch's own error; an error left pending
+  // by unrelated earlier work on the thread is neither reported nor cleared here
+  auto launch = [&](auto kern, dim3 grid, int threads, size_t smem, auto... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    return cudaLaunchKernelEx(&cfg, kern, args...) == cudaSuccess;
+  };
+  const dim3 grid(B * Hkv, splits);
+  bool ok;
   if (D == 128) {
-    decode_attn_kernel<128, 8><<<grid, 160, DecCfg<128, 8>::SMEM, st>>>(tk, tv, a);
-    if (splits > 1) decode_merge_kernel<128><<<B * Hq, 128, 0, st>>>(a, splits);
+    ok = launch(decode_attn_kernel<128, 8>, grid, 160, DecCfg<128, 8>::SMEM, tk, tv, a);
+    if (ok && splits > 1) ok = launch(decode_merge_kernel<128>, dim3(B * Hq), 128, 0, a, splits);
   } else {
-    decode_attn_kernel<64, 8><<<grid, 160, DecCfg<64, 8>::SMEM, st>>>(tk, tv, a);
-    if (splits > 1) decode_merge_kernel<64><<<B * Hq, 64, 0, st>>>(a, splits);
+    ok = launch(decode_attn_kernel<64, 8>, grid, 160, DecCfg<64, 8>::SMEM, tk, tv, a);
+    if (ok && splits > 1) ok = launch(decode_merge_kernel<64>, dim3(B * Hq), 64, 0, a, splits);
   }
-  return cudaGetLastError() == cudaSuccess ? B200_NOALLOC_OK : B200_NOALLOC_ERR_LAUNCH;
+  return ok ? B200_NOALLOC_OK : B200_NOALLOC_ERR_LAUNCH;
 }

@@ -22,7 +22,10 @@
 // Set-up: the first call on a device (with that device current) looks up the
 // device address of the scratch array with cudaGetSymbolAddress and sets the
 // kernel's shared-memory attribute; make that first call before any stream
-// capture. Later calls on the same device do no set-up.
+// capture. Later calls on the same device do no set-up. The looked-up address
+// is cached per device ordinal for the life of the process: a caller that
+// resets the device (cudaDeviceReset) or destroys and recreates its primary
+// context must not call this entry point afterwards in the same process.
 //
 // Sharing: all calls on a device share the one scratch array, which keeps the
 // previous call's contents. Every slot a call reads is written earlier in the
@@ -45,13 +48,14 @@ enum {
   B200_NOALLOC_ERR_SCRATCH = 2,  // B * Hq * splits * (D + 2) > B200_NOALLOC_SCRATCH_FLOATS
   B200_NOALLOC_ERR_SETUP = 3,    // cudaGetSymbolAddress / attribute set-up failed
   B200_NOALLOC_ERR_TMA = 4,      // tensor-map encoding failed
-  B200_NOALLOC_ERR_LAUNCH = 5,   // kernel launch reported an error
+  B200_NOALLOC_ERR_LAUNCH = 5,   // one of this call's own kernel launches failed
 };
 
 // q: [B, Hq, D] bf16; k_cache / v_cache: [num_blocks, Hkv, 16, D] bf16;
 // block_tables: [B, max_blocks] int32; ctx_lens: [B] int32 (kv length incl.
-// the new token); out: [B, Hq, D] bf16; sinks: [Hq] fp32 or NULL; window: 0
-// for full attention; splits >= 1 (the KV range of each sequence is cut into
+// the new token; each must be <= 16 * max_blocks: a longer one is clamped to
+// the table and flagged in `status` as a bounds error); out: [B, Hq, D] bf16;
+// sinks: [Hq] fp32 or NULL; window: 0 for full attention; splits >= 1 (the KV range of each sequence is cut into
 // `splits` parts whose partials meet in the scratch array); status: optional
 // device int32[4] error word (NULL to skip); stream: a cudaStream_t.
 // D must be 64 or 128 and Hq / Hkv <= 16. Returns a B200_NOALLOC_* code.

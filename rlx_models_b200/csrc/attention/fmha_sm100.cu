@@ -397,11 +397,7 @@ void fmha_launch(const AttnArgs& a, cudaStream_t st) {
     tv = make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv_rows, kD, kD, 16, 64);
   }
   const int q_tiles = (a.max_q_len + rows_tok - 1) / rows_tok;
-  static bool once = false;
-  if (!once) {
-    cudaFuncSetAttribute(fmha_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-    once = true;
-  }
+  ensure_smem(fmha_fwd_kernel, kSmem);
   launch_pdl(fmha_fwd_kernel, dim3(a.B * q_tiles, a.Hkv), dim3(kThreads), kSmem, st, tq, tk, tv, a, q_tiles,
              rows_tok);
 }

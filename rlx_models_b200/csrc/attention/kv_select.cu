@@ -215,11 +215,7 @@ void kv_select_launch(const KvSelectArgs& a, cudaStream_t st) {
   if (a.window < 1) throw std::runtime_error("b200.kv_select: the recent window must hold at least one block");
   const size_t smem = (size_t)a.W * sizeof(float);
   if (smem > 196608) throw std::runtime_error("b200.kv_select: block table too wide (W > 49152)");
-  static int once_smem = 0;
-  if ((int)smem > once_smem && smem > 48 * 1024) {
-    cudaFuncSetAttribute(kvsel::kv_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 196608);
-    once_smem = (int)smem;
-  }
+  ensure_smem(kvsel::kv_select_kernel, 196608);
   launch_pdl(kvsel::kv_score_kernel, dim3(a.B, (a.W + kvsel::kBlocksPerCta - 1) / kvsel::kBlocksPerCta),
              dim3(kvsel::kThreads), 0, st, a);
   launch_pdl(kvsel::kv_select_kernel, dim3(a.B), dim3(kvsel::kThreads), smem, st, a);

@@ -558,6 +558,17 @@ void argmax(const Tensor& logits, Tensor& out) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void forward_tokens(Tensor& ids, const Tensor& src, const Tensor& prev) {
+  check_cuda(ids, "ids");
+  TORCH_CHECK(ids.scalar_type() == at::kInt && src.scalar_type() == at::kInt && prev.scalar_type() == at::kInt &&
+                  ids.is_contiguous() && src.is_contiguous() && prev.is_contiguous() && src.numel() >= ids.numel(),
+              "b200.forward_tokens: int32 ids / src / prev");
+  c10::cuda::CUDAGuard g(ids.device());
+  b200::forward_tokens_launch(ids.data_ptr<int32_t>(), src.data_ptr<int32_t>(), prev.data_ptr<int32_t>(),
+                              (int)ids.numel(), cur_stream(ids));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void sample(const Tensor& logits, const Tensor& temperature, const Tensor& top_k, const Tensor& top_p,
             const Tensor& min_p, const Tensor& seeds, const Tensor& offsets, Tensor& out,
             const optional<Tensor>& logprob) {
@@ -1225,6 +1236,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("window"), py::arg("scale"), py::arg("max_q_len"), py::arg("status"), py::arg("causal"),
         py::arg("q_paged"), py::arg("softcap") = 0.0);
   m.def("argmax", &argmax);
+  m.def("forward_tokens", &forward_tokens);
   m.def("sample", &sample);
   m.def("symm_malloc", &symm_malloc);
   m.def("symm_free", &symm_free);

@@ -392,6 +392,7 @@ void dit_qk_rope_launch(const void* qkv, int64_t ld, int rows, int heads, const 
 
 // ---------------- sampling ----------------
 void argmax_launch(const float* logits, int64_t ld, int64_t B, int64_t V, int32_t* out, cudaStream_t st);
+void forward_tokens_launch(int32_t* ids, const int32_t* src, const int32_t* prev, int n, cudaStream_t st);
 
 struct SampleArgs {
   const float* logits;  // [B, V]

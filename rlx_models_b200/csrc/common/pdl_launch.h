@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdlib>
+#include <map>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 
@@ -17,6 +19,34 @@ inline bool pdl_enabled() {
     v = (e != nullptr && e[0] == '0') ? 0 : 1;
   }
   return v == 1;
+}
+
+// Raise a kernel's dynamic shared-memory limit on the current device, once per
+// (kernel, device): the attribute belongs to each device's context, so a
+// process that drives several GPUs sets it on every one. Thread-safe; a failed
+// call throws instead of surfacing later as a launch error.
+inline std::mutex& smem_attr_mutex() {
+  static std::mutex m;
+  return m;
+}
+inline std::map<std::pair<const void*, int>, size_t>& smem_attr_done() {
+  static std::map<std::pair<const void*, int>, size_t> m;
+  return m;
+}
+template <typename... KArgs>
+inline void ensure_smem(void (*kern)(KArgs...), size_t bytes) {
+  if (bytes <= 48 * 1024) return;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) throw std::runtime_error("b200: cudaGetDevice failed");
+  std::lock_guard<std::mutex> lk(smem_attr_mutex());
+  auto key = std::make_pair(reinterpret_cast<const void*>(kern), dev);
+  auto& done = smem_attr_done();
+  auto it = done.find(key);
+  if (it != done.end() && it->second >= bytes) return;
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("b200: cannot raise the shared-memory limit: ") + cudaGetErrorString(e));
+  done[key] = bytes;
 }
 
 template <typename... KArgs, typename... Args>

@@ -22,11 +22,8 @@ template <int BN, int EPI, bool A_MN = false, bool B_MN = false>
 static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid, cudaStream_t st,
                      int device) {
   auto kern = gemm_bf16_kernel<BN, EPI, A_MN, B_MN>;
-  static uint64_t attr_done = 0;  // one bit per device
-  if (!(attr_done & (1ull << device))) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg<BN>::SMEM_BYTES);
-    attr_done |= (1ull << device);
-  }
+  (void)device;
+  ensure_smem(kern, Cfg<BN>::SMEM_BYTES);
   launch_pdl(kern, dim3(grid), dim3(kThreads), Cfg<BN>::SMEM_BYTES, st, ta, tb, p);
 }
 

@@ -627,7 +627,7 @@ static void moe_gemm_go(const MoeGemmArgs& a, const moe::MoeParams& p, int grid,
   using namespace moe;
   CUtensorMap tx = make_tmap_2d(a.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a.rows, a.K, a.K, BT, kBK);
   auto k = moe_gemm_kernel<BT, EPI>;
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, MoeCfg<BT>::kSmem);
+  ensure_smem(k, MoeCfg<BT>::kSmem);
   launch_pdl(k, dim3(grid), dim3(kThreads), MoeCfg<BT>::kSmem, st, tx, p);
 }
 

@@ -18,6 +18,15 @@
 //   2. the remaining token budget goes to prefill chunks: first sequences
 //      whose prompt is partially computed, then new admissions (FIFO) while
 //      the sequence limit and free blocks allow.
+// Overlapped (asynchronous) scheduling: when schedule() is given a `tok_src`
+// buffer, every sampled row appends a placeholder token to its sequence at
+// once, so step n+1 can be scheduled and launched while step n still runs on
+// the GPU. A decode row whose input is such a placeholder gets tok_src[t] =
+// the logit row of the previous step that produces it (the device copies the
+// token from the previous step's sampler output); update() later replaces
+// placeholders, oldest first, by the sampled values. A sequence whose
+// placeholders already reach max_new_tokens is not scheduled again; one that
+// stops on EOS / a stop id discards the row that was scheduled behind it.
 // Prefix caching: every full block is keyed by a chained 64-bit hash of its
 // tokens; freed blocks that carry a hash stay reusable (LRU) until the pool
 // needs them, and an admitted prompt skips its longest cached block prefix.
@@ -28,6 +37,7 @@
 #include <deque>
 #include <list>
 #include <memory>
+#include <optional>
 #include <stdexcept>
 #include <unordered_map>
 #include <vector>
@@ -148,7 +158,11 @@ struct Seq {
   int status = WAITING;
   int finish_reason = 0;  // 1 length, 2 stop token, 3 aborted
   int num_cached_prompt = 0;
+  int pending = 0;        // trailing placeholder tokens whose values the device has not returned yet
+  int pending_row = -1;   // logit row (of the step that made it) of the newest placeholder
+  bool length_done = false;  // placeholders reach max_new_tokens: finishes when they resolve
   int generated() const { return (int)tokens.size() - prompt_len; }
+  int resolved_generated() const { return (int)tokens.size() - pending - prompt_len; }
 };
 
 class Scheduler {
@@ -193,7 +207,13 @@ class Scheduler {
   // counts; the per-row sequence ids to sample are written to `sample_ids`.
   py::dict schedule(torch::Tensor input_ids, torch::Tensor positions, torch::Tensor slots,
                     torch::Tensor dec_tables, torch::Tensor dec_ctx, torch::Tensor pre_tables, torch::Tensor pre_ctx,
-                    torch::Tensor pre_cu, torch::Tensor logit_rows, torch::Tensor sample_ids) {
+                    torch::Tensor pre_cu, torch::Tensor logit_rows, torch::Tensor sample_ids,
+                    std::optional<torch::Tensor> tok_src_opt, bool overlap) {
+    const bool has_src = tok_src_opt.has_value() && tok_src_opt->numel() > 0;
+    if (overlap && !has_src) throw std::invalid_argument("scheduler: overlapped scheduling needs tok_src");
+    int32_t* tsrc = has_src ? tok_src_opt->data_ptr<int32_t>() : nullptr;
+    if (has_src && tok_src_opt->numel() < input_ids.numel())
+      throw std::invalid_argument("scheduler: tok_src must hold as many rows as input_ids");
     int32_t* ids = input_ids.data_ptr<int32_t>();
     int32_t* pos = positions.data_ptr<int32_t>();
     int64_t* slt = slots.data_ptr<int64_t>();
@@ -215,7 +235,8 @@ class Scheduler {
     // 1. decode tokens for running sequences past their prompt
     std::vector<int64_t> decoders;
     for (int64_t id : running_) {
-      if (is_decode(*seqs_[id])) decoders.push_back(id);
+      const Seq& s = *seqs_[id];
+      if (is_decode(s) && !s.length_done) decoders.push_back(id);
     }
     for (size_t i = 0; i < decoders.size(); ++i) {
       Seq& s = *seqs_[decoders[i]];
@@ -229,11 +250,17 @@ class Scheduler {
       step_decode_.push_back(s.id);
       ++tokens;
     }
+    // a sequence preempted while the loop above allocated for a later one drops out
+    step_decode_.erase(std::remove_if(step_decode_.begin(), step_decode_.end(),
+                                      [&](int64_t id) { return seqs_[id]->status != RUNNING; }),
+                       step_decode_.end());
+    tokens = (int)step_decode_.size();
     // 2. prefill chunks (continuing sequences first, then admissions)
     std::vector<int64_t> cand;
     for (int64_t id : running_) {
       Seq& s = *seqs_[id];
-      if (s.status == RUNNING && !is_decode(s) && s.num_computed < prefill_limit(s)) cand.push_back(id);
+      if (s.status == RUNNING && !is_decode(s) && s.pending == 0 && s.num_computed < prefill_limit(s))
+        cand.push_back(id);
     }
     std::vector<int> chunk_len;
     for (int64_t id : cand) {
@@ -251,6 +278,7 @@ class Scheduler {
     while (!waiting_.empty() && tokens < budget_ && (int)running_.size() < max_num_seqs_ &&
            (int64_t)(step_decode_.size() + step_prefill_.size()) < cap_seq) {
       Seq& s = *seqs_[waiting_.front()];
+      if (s.pending > 0) break;  // preempted with a token still in flight: re-admit once it resolves
       // prefix cache lookup over full prompt blocks (leave >= 1 token to compute)
       if (s.blocks.empty()) {
         uint64_t h = 0;
@@ -294,7 +322,9 @@ class Scheduler {
     for (size_t i = 0; i < step_decode_.size(); ++i) {
       Seq& s = *seqs_[step_decode_[i]];
       const int p = s.num_computed;
-      ids[t] = s.tokens[p];
+      const bool placeholder = p >= (int)s.tokens.size() - s.pending;
+      ids[t] = placeholder ? 0 : s.tokens[p];
+      if (tsrc) tsrc[t] = placeholder ? s.pending_row : -1;
       pos[t] = p;
       slt[t] = (int64_t)s.blocks[p / kBlock] * kBlock + p % kBlock;
       for (int b = 0; b < W; ++b) dtab[i * W + b] = b < (int)s.blocks.size() ? s.blocks[b] : 0;
@@ -312,6 +342,7 @@ class Scheduler {
       for (int j = 0; j < n; ++j) {
         const int p = s.num_computed + j;
         ids[t] = s.tokens[p];
+        if (tsrc) tsrc[t] = -1;
         pos[t] = p;
         slt[t] = (int64_t)s.blocks[p / kBlock] * kBlock + p % kBlock;
         ++t;
@@ -332,6 +363,16 @@ class Scheduler {
       Seq& s = *seqs_[step_prefill_[i]];
       s.num_computed += chunk_len[i];
       publish_full_blocks(s);
+    }
+    if (overlap) {
+      // every sampled row appends a placeholder now, so the next step can be scheduled before this one returns
+      for (int i = 0; i < r; ++i) {
+        Seq& s = *seqs_[sids[i]];
+        s.tokens.push_back(0);
+        ++s.pending;
+        s.pending_row = i;
+        if (s.generated() >= s.max_new_tokens) s.length_done = true;
+      }
     }
     py::dict d;
     d["num_tokens"] = t;
@@ -358,16 +399,23 @@ class Scheduler {
       auto it = seqs_.find(seq_ids[i]);
       if (it == seqs_.end()) continue;
       Seq& s = *it->second;
-      if (s.status != RUNNING) continue;
-      s.tokens.push_back(toks[i]);
+      if (s.status == FINISHED) continue;  // (a sequence preempted with a token in flight still resolves it)
+      if (s.pending > 0) {  // resolve the oldest placeholder
+        s.tokens[s.tokens.size() - s.pending] = toks[i];
+        --s.pending;
+      } else {
+        s.tokens.push_back(toks[i]);
+      }
       int reason = 0;
-      if (s.generated() >= s.max_new_tokens) reason = 1;
+      if (s.resolved_generated() >= s.max_new_tokens) reason = 1;
       if (!s.ignore_eos) {
         if (eos >= 0 && toks[i] == eos) reason = 2;
         for (int32_t st : s.stop_ids)
           if (toks[i] == st) reason = 2;
       }
       if (reason) {
+        s.tokens.resize(s.tokens.size() - s.pending);  // rows scheduled behind a stop are discarded
+        s.pending = 0;
         finish(s, reason);
         done.push_back(s.id);
       }
@@ -483,7 +531,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("num_waiting", &Scheduler::num_waiting)
       .def("num_running", &Scheduler::num_running)
       .def("num_free_blocks", &Scheduler::num_free_blocks)
-      .def("schedule", &Scheduler::schedule)
+      .def("schedule", &Scheduler::schedule, py::arg("input_ids"), py::arg("positions"), py::arg("slots"),
+           py::arg("dec_tables"), py::arg("dec_ctx"), py::arg("pre_tables"), py::arg("pre_ctx"), py::arg("pre_cu"),
+           py::arg("logit_rows"), py::arg("sample_ids"), py::arg("tok_src") = py::none(),
+           py::arg("overlap") = false)
       .def("step_seq_ids", &Scheduler::step_seq_ids)
       .def("update", &Scheduler::update)
       .def("output_tokens", &Scheduler::output_tokens)

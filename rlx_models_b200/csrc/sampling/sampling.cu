@@ -311,6 +311,27 @@ void argmax_launch(const float* logits, int64_t ld, int64_t B, int64_t V, int32_
   launch_pdl(smp::argmax_kernel, dim3((unsigned)B), dim3(smp::kThreads), 0, st, logits, ld, V, out);
 }
 
+namespace smp {
+// Overlapped scheduling: a decode row whose input token was still being
+// sampled when its step was scheduled names the logit row of the previous
+// step (src >= 0); copy that row's sampled id from the previous step's output.
+__global__ void forward_tokens_kernel(int32_t* __restrict__ ids, const int32_t* __restrict__ src,
+                                      const int32_t* __restrict__ prev, int n) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t < n) {
+    const int r = src[t];
+    if (r >= 0) ids[t] = prev[r];
+  }
+}
+}  // namespace smp
+
+void forward_tokens_launch(int32_t* ids, const int32_t* src, const int32_t* prev, int n, cudaStream_t st) {
+  if (n == 0) return;
+  launch_pdl(smp::forward_tokens_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, ids, src, prev, n);
+}
+
 void sample_launch(const SampleArgs& a, cudaStream_t st) {
   if (a.B == 0) return;
   launch_pdl(smp::sample_kernel, dim3((unsigned)a.B), dim3(smp::kThreads), 0, st, a);

@@ -296,6 +296,15 @@ def argmax(logits: torch.Tensor, *, out: torch.Tensor | None = None) -> torch.Te
     return out
 
 
+def forward_tokens(ids: torch.Tensor, src: torch.Tensor, prev: torch.Tensor) -> torch.Tensor:
+    """In place: ``ids[t] = prev[src[t]]`` where ``src[t] >= 0`` (int32). Decode
+    rows scheduled before the previous step's tokens reached the host take
+    their input token from that step's sampler output on the device."""
+    _count(1)
+    ext().forward_tokens(ids, src, prev)
+    return ids
+
+
 def sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, *, out=None, logprob=None):
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)

@@ -14,12 +14,26 @@ src/batch.rs:262-360):
 4. only the sampled token ids come back to the host; the scheduler appends
    them and retires finished sequences.
 
+Overlapped scheduling (``EngineConfig.async_scheduling``, the default): step
+n+1 is scheduled and launched before step n's tokens are read back. The
+scheduler appends a placeholder for every sampled row; decode rows fed by a
+placeholder carry the previous step's logit row in ``tok_src`` and a small
+kernel (``ops.forward_tokens``, the first launch of every step) copies the
+sampled ids on the device. Host staging and the token read-back buffers are
+double-buffered by step parity; the host waits for step n's event only after
+step n+1 is queued, so scheduling, staging and Python bookkeeping run while
+the GPU computes. Requests that need the host between steps (penalties,
+host-side logit processors) and pipeline stages fall back to the synchronous
+loop.
+
 Every launch in a step is one of this package's kernels (GEMM, attention,
 norm/RoPE, sampling) except for small torch copies/index ops.
 """
 from __future__ import annotations
 
+import collections
 import dataclasses
+import json
 
 import time
 from dataclasses import dataclass, field
@@ -93,6 +107,11 @@ class EngineConfig:
     # long-context decode over retrieved KV blocks, e.g. {"topk_blocks": 64,
     # "window_blocks": 16, "sink_blocks": 1} (runtime/kv_retrieval.py); None = full attention
     kv_retrieval: dict | None = None
+    # schedule / launch step n+1 before step n's tokens come back (see module docstring)
+    async_scheduling: bool = True
+    # per-step metrics as JSON lines (step kind, tokens, batch occupancy, KV blocks in use,
+    # host launch / wait time, device time); None = off. ``LLMEngine.step_log`` keeps the last 4096.
+    metrics_path: str | None = None
 
 
 @dataclass
@@ -112,6 +131,7 @@ class RequestState:
     rng: object = None                  # XTC coin flips
     mirostat_mu: float | None = None
     mirostat_lp2: object = None
+    n_sched: int = 0                    # sampled rows scheduled so far (the sampler's stream offset)
 
 
 @dataclass
@@ -164,15 +184,24 @@ class LLMEngine:
         T, S, W = cfg.max_batched_tokens, cfg.max_num_seqs, self.max_blocks_per_seq
         pin = dict(pin_memory=True)
         i32, i64 = torch.int32, torch.int64
-        self.h = dict(
-            input_ids=torch.zeros(T, dtype=i32, **pin), positions=torch.zeros(T, dtype=i32, **pin),
-            slots=torch.zeros(T, dtype=i64, **pin), dec_tables=torch.zeros(S, W, dtype=i32, **pin),
-            dec_ctx=torch.zeros(S, dtype=i32, **pin), pre_tables=torch.zeros(S, W, dtype=i32, **pin),
-            pre_ctx=torch.zeros(S, dtype=i32, **pin), pre_cu=torch.zeros(S + 1, dtype=i32, **pin),
-            logit_rows=torch.zeros(T, dtype=i64, **pin), sample_ids=torch.zeros(T, dtype=i64, **pin),
-            seq_slots=torch.full((S,), -1, dtype=i32, **pin))
+
+        def staging():
+            return dict(
+                input_ids=torch.zeros(T, dtype=i32, **pin), positions=torch.zeros(T, dtype=i32, **pin),
+                slots=torch.zeros(T, dtype=i64, **pin), dec_tables=torch.zeros(S, W, dtype=i32, **pin),
+                dec_ctx=torch.zeros(S, dtype=i32, **pin), pre_tables=torch.zeros(S, W, dtype=i32, **pin),
+                pre_ctx=torch.zeros(S, dtype=i32, **pin), pre_cu=torch.zeros(S + 1, dtype=i32, **pin),
+                logit_rows=torch.zeros(T, dtype=i64, **pin), sample_ids=torch.zeros(T, dtype=i64, **pin),
+                seq_slots=torch.full((S,), -1, dtype=i32, **pin), tok_src=torch.full((T,), -1, dtype=i32, **pin))
+
+        # host staging, double-buffered by step parity: step n+1 is written while
+        # step n's host->device copies may still be queued
+        self._hs = [staging(), staging()]
+        self._hb = 0
+        self.h = self._hs[0]
         dev = self.device
         self.d = {k: torch.zeros_like(v, device=dev) for k, v in self.h.items() if k != "sample_ids"}
+        self.d["tok_src"].fill_(-1)
         # per-row sampling parameters (host pinned -> device)
         self.hp = dict(temp=torch.zeros(T, **pin), top_k=torch.zeros(T, dtype=i32, **pin),
                        top_p=torch.ones(T, **pin), min_p=torch.zeros(T, **pin),
@@ -180,12 +209,21 @@ class LLMEngine:
         self.dp = {k: torch.zeros_like(v, device=dev) for k, v in self.hp.items()}
         self.tok_out = torch.zeros(T, dtype=i32, device=dev)
         self.logprob_out = torch.zeros(T, dtype=torch.float32, device=dev)
-        self.tok_host = torch.zeros(T, dtype=i32, pin_memory=True)
+        self._tok_hosts = [torch.zeros(T, dtype=i32, pin_memory=True) for _ in range(2)]
+        self._lp_hosts = [torch.zeros(T, dtype=torch.float32, pin_memory=True) for _ in range(2)]
+        self.tok_host = self._tok_hosts[0]
         self.requests: dict[int, RequestState] = {}
+        self._n_nongreedy = 0   # active requests that sample or want logprobs
+        self._n_host_rows = 0   # active requests that need the host between steps (penalties, processors)
+        self._inflight = None
         self.graphs: dict[int, tuple] = {}
         self._graph_pool = None
-        self.stats = dict(steps=0, graph_steps=0, eager_steps=0, tokens=0, h2d_bytes=0, d2h_bytes=0)
+        self.stats = dict(steps=0, graph_steps=0, eager_steps=0, tokens=0, h2d_bytes=0, d2h_bytes=0,
+                          overlapped_steps=0)
         self.copy_stream = torch.cuda.current_stream(dev)
+        self.step_log = collections.deque(maxlen=4096)
+        self._metrics_f = open(cfg.metrics_path, "a") if cfg.metrics_path else None
+        self._nblocks = nb
 
     # -- requests --------------------------------------------------------------
     def add_request(self, prompt: list[int], params: SamplingParams | None = None) -> int:
@@ -198,12 +236,26 @@ class LLMEngine:
             if params.repetition_penalty != 1.0 or params.dry_multiplier > 0:
                 st.prompt = list(map(int, prompt))
         self.requests[sid] = st
+        self._track(st, +1)
         return sid
+
+    def _track(self, st: RequestState, d: int):
+        p = st.params
+        if p.temperature > 0 or p.logprobs:
+            self._n_nongreedy += d
+        if st.out_counts is not None:
+            self._n_host_rows += d
+
+    def _retire(self, sid: int) -> RequestState | None:
+        st = self.requests.pop(sid, None)
+        if st is not None:
+            self._track(st, -1)
+        self._free_slot(sid)
+        return st
 
     def abort(self, sid: int):
         self.sched.abort(sid)
-        self.requests.pop(sid, None)
-        self._free_slot(sid)
+        self._retire(sid)
 
     def _free_slot(self, sid: int):
         if self.stateful and sid in self.slot_of:
@@ -221,25 +273,32 @@ class LLMEngine:
         return len(ids)
 
     def has_unfinished(self) -> bool:
-        return self.sched.has_work()
+        return self.sched.has_work() or self._inflight is not None
 
     # -- model step ------------------------------------------------------------
     def _params_rows(self, sids: list[int]) -> bool:
-        """Fill per-row sampling params; returns True if every row is greedy without logprobs."""
-        greedy = True
+        """Advance each row's sampler offset and, unless every active request is
+        greedy without logprobs (returns True then), fill the per-row sampling
+        parameters with one pinned write per field."""
+        reqs = self.requests
+        sts = [reqs[sid] for sid in sids]
+        offs = [st.n_sched for st in sts]
+        for st in sts:
+            st.n_sched += 1
+        if self._n_nongreedy == 0:
+            return True
+        ps = [st.params for st in sts]
+        if not any(p.temperature > 0 or p.logprobs for p in ps):
+            return True
+        R = len(sids)
         hp = self.hp
-        for r, sid in enumerate(sids):
-            st = self.requests[sid]
-            p = st.params
-            hp["temp"][r] = p.temperature
-            hp["top_k"][r] = p.top_k
-            hp["top_p"][r] = p.top_p
-            hp["min_p"][r] = p.min_p
-            hp["seed"][r] = p.seed * 1000003 + sid
-            hp["offset"][r] = len(st.tokens)
-            if p.temperature > 0 or p.logprobs:
-                greedy = False
-        return greedy
+        hp["temp"][:R] = torch.tensor([p.temperature for p in ps], dtype=torch.float32)
+        hp["top_k"][:R] = torch.tensor([p.top_k for p in ps], dtype=torch.int32)
+        hp["top_p"][:R] = torch.tensor([p.top_p for p in ps], dtype=torch.float32)
+        hp["min_p"][:R] = torch.tensor([p.min_p for p in ps], dtype=torch.float32)
+        hp["seed"][:R] = torch.tensor([p.seed * 1000003 + sid for p, sid in zip(ps, sids)], dtype=torch.int64)
+        hp["offset"][:R] = torch.tensor(offs, dtype=torch.int64)
+        return False
 
     def _penalty_rows(self, sids: list[int]):
         """Per-row penalty tables for ops.apply_penalties (None when no row of
@@ -301,7 +360,9 @@ class LLMEngine:
         d = self.d
         self._copy_in(dict(input_ids=T, positions=T, slots=T, dec_tables=nd, dec_ctx=nd, pre_tables=npf,
                            pre_ctx=npf, pre_cu=npf + 1 if npf else 0, logit_rows=R,
-                           seq_slots=nd + npf if self.stateful else 0))
+                           seq_slots=nd + npf if self.stateful else 0, tok_src=nd))
+        if nd:  # decode inputs still being sampled by the previous step
+            ops.forward_tokens(d["input_ids"][:nd], d["tok_src"][:nd], self.tok_out)
         fb = ForwardBatch(
             input_ids=d["input_ids"][:T], positions=d["positions"][:T], slots=d["slots"][:T], num_decode=nd,
             dec_block_tables=d["dec_tables"][:nd] if nd else None, dec_ctx_lens=d["dec_ctx"][:nd] if nd else None,
@@ -318,6 +379,8 @@ class LLMEngine:
         return None
 
     def _pad_decode_rows(self, nd: int, B: int):
+        if nd == B:
+            return
         h = self.h
         db = self.dummy_block
         h["input_ids"][nd:B] = 0
@@ -325,6 +388,7 @@ class LLMEngine:
         h["slots"][nd:B] = db * BLOCK_SIZE
         h["dec_tables"][nd:B] = db
         h["dec_ctx"][nd:B] = 1
+        h["tok_src"][nd:B] = -1
         h["seq_slots"][nd:B] = -1  # no state slot: the recurrent kernels skip these rows
 
     def _capture(self, B: int, greedy: bool):
@@ -334,7 +398,13 @@ class LLMEngine:
                           logit_rows=None, seq_slots=d["seq_slots"][:B] if self.stateful else None)
         # warm up (allocations, kernel attributes) outside the graph on dummy
         # rows written straight into the device buffers: the host staging
-        # buffers may already hold the step being scheduled.
+        # buffers may already hold the step being scheduled. A step may be in
+        # flight (overlapped scheduling): wait for it so its device inputs are
+        # not overwritten under it.
+        torch.cuda.synchronize(self.device)
+        saved = {k: d[k][:B].clone() for k in ("input_ids", "positions", "slots", "dec_tables", "dec_ctx",
+                                               "seq_slots", "tok_src")}
+        saved_tok = self.tok_out.clone()
         db = self.dummy_block
         d["input_ids"][:B].zero_()
         d["positions"][:B].zero_()
@@ -342,10 +412,12 @@ class LLMEngine:
         d["dec_tables"][:B].fill_(db)
         d["dec_ctx"][:B].fill_(1)
         d["seq_slots"][:B].fill_(-1)
+        d["tok_src"][:B].fill_(-1)
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             for _ in range(2):
+                ops.forward_tokens(d["input_ids"][:B], d["tok_src"][:B], self.tok_out)
                 logits = self.model.forward(fb, self.kv)
                 self._sample(logits, B, greedy)
         torch.cuda.current_stream(self.device).wait_stream(s)
@@ -355,10 +427,15 @@ class LLMEngine:
             self._graph_pool = torch.cuda.graph_pool_handle()
         n0 = ops.launch_count()
         with torch.cuda.graph(g, pool=self._graph_pool):
+            ops.forward_tokens(d["input_ids"][:B], d["tok_src"][:B], self.tok_out)
             logits = self.model.forward(fb, self.kv)
             out = self._sample(logits, B, greedy)
         n_launch = ops.launch_count() - n0
         ops._count(-n_launch)  # capture does not execute; replays are counted
+        for k, v in saved.items():
+            d[k][:B].copy_(v)
+        self.tok_out.copy_(saved_tok)
+        torch.cuda.synchronize(self.device)
         self.graphs[(B, greedy)] = (g, out, n_launch)
         return g, out, n_launch
 
@@ -369,38 +446,66 @@ class LLMEngine:
                 self._capture(B, greedy)
 
     def step(self) -> list[RequestOutput]:
+        """One engine iteration. With overlapped scheduling this launches the
+        next step and returns the requests finished by the previous one."""
         with nvtx("engine.step"):
-            return self._step()
+            if self._can_overlap():
+                inf = self._launch(overlap=True)
+                outs = self._finish(self._inflight) if self._inflight is not None else []
+                self._inflight = inf
+                return outs
+            outs = []
+            if self._inflight is not None:  # leave overlapped mode: drain the step in flight first
+                outs = self._finish(self._inflight)
+                self._inflight = None
+            inf = self._launch(overlap=False)
+            if inf is not None:
+                outs += self._finish(inf)
+            return outs
 
-    def _step(self) -> list[RequestOutput]:
-        h = self.h
+    def _can_overlap(self) -> bool:
+        return (self.cfg.async_scheduling and self._n_host_rows == 0 and not hasattr(self.model, "share_tokens"))
+
+    def _launch(self, overlap: bool):
+        """Schedule one step and queue it on the GPU (tokens read back
+        asynchronously into the pinned buffer of this step's parity)."""
+        t0 = time.perf_counter()
+        hb = self._hb
+        h = self.h = self._hs[hb]
         info = self.sched.schedule(h["input_ids"], h["positions"], h["slots"], h["dec_tables"], h["dec_ctx"],
-                                   h["pre_tables"], h["pre_ctx"], h["pre_cu"], h["logit_rows"], h["sample_ids"])
+                                   h["pre_tables"], h["pre_ctx"], h["pre_cu"], h["logit_rows"], h["sample_ids"],
+                                   h["tok_src"], overlap)
         T, nd, npf = info["num_tokens"], info["num_decode"], info["num_prefill"]
         R, max_q = info["num_logits"], info["max_q_len"]
         self.stats["steps"] += 1
         if T == 0:
-            return []
+            return None
         sids = h["sample_ids"][:R].tolist()
         self._step_sids = sids
         if self.stateful:
             self._assign_slots()
         greedy = self._params_rows(sids)
-        pen = self._penalty_rows(sids)
+        pen = None if overlap else self._penalty_rows(sids)
         B = self._bucket(nd) if (npf == 0 and self.cfg.cuda_graphs and not hasattr(self.model, "share_tokens")
                                  and pen is None) else None
+        stream = torch.cuda.current_stream(self.device)
+        timing = self._metrics_f is not None
+        ev0 = torch.cuda.Event(enable_timing=True) if timing else None
+        if ev0 is not None:
+            ev0.record(stream)
         if B is not None:
             key = (B, greedy)
             if key not in self.graphs:
                 self._capture(B, greedy)
             g, out, n_launch = self.graphs[key]
             self._pad_decode_rows(nd, B)
-            self._copy_in(dict(input_ids=B, positions=B, slots=B, dec_tables=B, dec_ctx=B,
+            self._copy_in(dict(input_ids=B, positions=B, slots=B, dec_tables=B, dec_ctx=B, tok_src=B,
                                seq_slots=B if self.stateful else 0))
             g.replay()
             ops._count(n_launch)
             toks = out[:nd]
             self.stats["graph_steps"] += 1
+            kind = "graph"
         else:
             logits = self._eager_forward(T, nd, npf, max_q, R)
             if logits is None:  # a non-final pipeline stage: tokens come from the last stage
@@ -411,13 +516,41 @@ class LLMEngine:
                 self.model.share_tokens(self.tok_out[:R])
                 toks = self.tok_out[:R]
             self.stats["eager_steps"] += 1
-        self.tok_host[:R].copy_(toks[:R])
+            kind = "eager"
+        th = self._tok_hosts[hb]
+        th[:R].copy_(toks[:R], non_blocking=True)
         self.stats["d2h_bytes"] += 4 * R
-        tl = self.tok_host[:R].tolist()
-        lps = self.logprob_out[:R].tolist() if not greedy else None
+        if not greedy:
+            self._lp_hosts[hb][:R].copy_(self.logprob_out[:R], non_blocking=True)
+            self.stats["d2h_bytes"] += 4 * R
+        ev = torch.cuda.Event(enable_timing=timing)
+        ev.record(stream)
+        if overlap:
+            self.stats["overlapped_steps"] += 1
+        self._hb ^= 1
+        rec = None
+        if timing:
+            rec = dict(step=self.stats["steps"], kind=kind, tokens=T, decode=nd, prefill=npf, logits=R,
+                       batch=B or T, running=self.sched.num_running(), waiting=self.sched.num_waiting(),
+                       kv_blocks_used=self._nblocks - self.sched.num_free_blocks(), kv_blocks=self._nblocks,
+                       overlap=overlap, host_launch_ms=round((time.perf_counter() - t0) * 1e3, 3))
+        return dict(sids=sids, R=R, greedy=greedy, hb=hb, ev=ev, ev0=ev0, rec=rec)
+
+    def _finish(self, inf) -> list[RequestOutput]:
+        """Wait for a launched step's tokens and hand them to the scheduler and
+        the request states; returns the requests that finished."""
+        t0 = time.perf_counter()
+        inf["ev"].synchronize()
+        t1 = time.perf_counter()
+        R, sids = inf["R"], inf["sids"]
+        tl = self._tok_hosts[inf["hb"]][:R].tolist()
+        lps = self._lp_hosts[inf["hb"]][:R].tolist() if not inf["greedy"] else None
         now = time.perf_counter()
+        reqs = self.requests
         for r, sid in enumerate(sids):
-            st = self.requests[sid]
+            st = reqs.get(sid)
+            if st is None:  # finished (stop token) while this row was in flight: discarded
+                continue
             st.tokens.append(tl[r])
             if st.out_counts is not None:
                 st.out_counts[tl[r]] = st.out_counts.get(tl[r], 0) + 1
@@ -433,8 +566,9 @@ class LLMEngine:
         done = self.sched.update(sids, tl, int(self.cfg.eos_token_id))
         outs = []
         for sid in done:
-            st = self.requests.pop(sid)
-            self._free_slot(sid)
+            st = self._retire(sid)
+            if st is None:
+                continue
             st.finish = now
             reason = _REASONS.get(self.sched.finish_reason(sid), "length")
             cached = self.sched.num_cached_prompt_tokens(sid)
@@ -443,6 +577,14 @@ class LLMEngine:
             tpot = (st.finish - st.first_token) / max(1, n - 1)
             outs.append(RequestOutput(sid, st.prompt_len, st.tokens, reason, st.first_token - st.arrival, tpot,
                                       st.finish - st.arrival, cached, st.logprobs or None))
+        rec = inf["rec"]
+        if rec is not None:
+            rec["device_ms"] = round(inf["ev0"].elapsed_time(inf["ev"]), 3)
+            rec["host_wait_ms"] = round((t1 - t0) * 1e3, 3)
+            rec["host_finish_ms"] = round((time.perf_counter() - t1) * 1e3, 3)
+            rec["finished"] = len(outs)
+            self.step_log.append(rec)
+            self._metrics_f.write(json.dumps(rec) + "\n")
         return outs
 
     def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None

@@ -107,22 +107,40 @@ def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model", 
         first = [None]
 
         def events():
-            toks = []
+            toks, lps = [], []
             for ev in h.events():
                 if ev[0] == "token":
                     if first[0] is None:
                         first[0] = time.perf_counter()
                         m_ttft.observe(first[0] - t0)
                     toks.append(ev[1])
+                    lps.append(ev[2] if len(ev) > 2 else None)
                     m_tok.inc()
-                    yield "token", ev[1], toks
+                    yield "token", ev[1], toks, lps
                 elif ev[0] == "error":
                     raise HTTPException(500, ev[1])
                 else:
                     out = ev[1]
                     reason = h.finish_reason or (out.finish_reason if out is not None else "stop")
-                    yield "done", reason, toks
+                    final = getattr(out, "logprobs", None) if out is not None else None
+                    if final:
+                        lps[:] = list(final[:len(toks)])
+                    yield "done", reason, toks, lps
         return events()
+
+    def logprobs_of(kind, toks, lps):
+        """OpenAI ``logprobs`` object of the sampled tokens (no alternatives):
+        completions: tokens / token_logprobs / text_offset; chat: content[]."""
+        pieces = [tokenizer.decode([t]) for t in toks]
+        vals = [None if v is None else float(v) for v in lps[:len(toks)]]
+        if kind == "chat":
+            return {"content": [{"token": p, "logprob": v, "bytes": list(p.encode("utf-8")), "top_logprobs": []}
+                                for p, v in zip(pieces, vals)]}
+        offs, o = [], 0
+        for p in pieces:
+            offs.append(o)
+            o += len(p)
+        return {"tokens": pieces, "token_logprobs": vals, "top_logprobs": None, "text_offset": offs}
 
     def text_of(toks, stop):
         s = tokenizer.decode(toks)
@@ -131,11 +149,14 @@ def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model", 
                 s = s[:s.index(st)]
         return s
 
-    def choice(kind, text, reason, idx=0, delta=False):
+    def choice(kind, text, reason, idx=0, delta=False, logprobs=None):
         if kind == "chat":
             key = "delta" if delta else "message"
-            return {"index": idx, key: ({"role": "assistant", "content": text}), "finish_reason": reason}
-        return {"index": idx, "text": text, "finish_reason": reason, "logprobs": None}
+            ch = {"index": idx, key: ({"role": "assistant", "content": text}), "finish_reason": reason}
+            if logprobs is not None:
+                ch["logprobs"] = logprobs
+            return ch
+        return {"index": idx, "text": text, "finish_reason": reason, "logprobs": logprobs}
 
     def respond(body, ids, kind):
         rid = ("chatcmpl-" if kind == "chat" else "cmpl-") + uuid.uuid4().hex[:24]
@@ -144,16 +165,18 @@ def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model", 
         stop = body.get("stop") or []
         stop = [stop] if isinstance(stop, str) else list(stop)
         evs = run(ids, body, kind, rid, created)
+        want_lp = bool(body.get("logprobs"))
         if body.get("stream"):
             def sse():
                 sent = ""
-                for typ, val, toks in evs:
+                for typ, val, toks, lps in evs:
                     if typ == "token":
                         cur = text_of(toks, stop)
                         piece, sent = cur[len(sent):], cur
-                        if piece:
+                        if piece or want_lp:
+                            lp = logprobs_of(kind, toks[-1:], lps[-1:]) if want_lp else None
                             chunk = {"id": rid, "object": obj + ".chunk", "created": created, "model": model_name,
-                                     "choices": [choice(kind, piece, None, delta=True)]}
+                                     "choices": [choice(kind, piece, None, delta=True, logprobs=lp)]}
                             yield f"data: {json.dumps(chunk)}\n\n"
                     else:
                         chunk = {"id": rid, "object": obj + ".chunk", "created": created, "model": model_name,
@@ -163,13 +186,13 @@ def create_app(runner: EngineRunner, tokenizer, model_name: str = "b200-model", 
                         yield f"data: {json.dumps(chunk)}\n\n"
                 yield "data: [DONE]\n\n"
             return StreamingResponse(sse(), media_type="text/event-stream")
-        toks, reason = [], "stop"
-        for typ, val, tk in evs:
-            toks = tk
+        toks, lps, reason = [], [], "stop"
+        for typ, val, tk, lp in evs:
+            toks, lps = tk, lp
             if typ == "done":
                 reason = val
         text = text_of(toks, stop)
-        ch = choice(kind, text, reason)
+        ch = choice(kind, text, reason, logprobs=logprobs_of(kind, toks, lps) if want_lp else None)
         tools = body.get("tools") or []
         if kind == "chat" and tools:
             # tool calls in the text: validated and sanitised against the request's tools

@@ -4,7 +4,8 @@
 ``has_unfinished`` / ``abort`` / ``requests``, i.e. ``runtime.engine.LLMEngine``)
 on one background thread, so every client's request joins the same
 continuous batch. ``submit`` returns a ``RequestHandle`` whose ``events()``
-yields ``("token", id)`` as tokens appear and finally ``("done", output)``.
+yields ``("token", id, logprob)`` as tokens appear (logprob None unless the
+request asked for log-probabilities) and finally ``("done", output)``.
 Stop strings are matched on the incrementally decoded text; a match aborts
 the request in the engine.
 
@@ -72,10 +73,10 @@ class EngineRunner:
             self._live[sid] = (h, 0)
             self.stats["requests"] += 1
 
-    def _emit(self, sid, toks, final=None):
+    def _emit(self, sid, toks, final=None, lps=None):
         h, sent = self._live[sid]
-        for t in toks[sent:]:
-            h.q.put(("token", t))
+        for i, t in enumerate(toks[sent:], start=sent):
+            h.q.put(("token", t, lps[i] if lps is not None and i < len(lps) else None))
             self.stats["tokens"] += 1
             if h.stop and self.tok is not None:
                 h.text += self.tok.decode([t])
@@ -108,8 +109,9 @@ class EngineRunner:
                 continue
             for sid in list(self._live):
                 if sid in done:
-                    self._emit(sid, done[sid].token_ids, final=done[sid])
+                    self._emit(sid, done[sid].token_ids, final=done[sid],
+                               lps=getattr(done[sid], "logprobs", None))
                 else:
                     st = self.engine.requests.get(sid)
                     if st is not None:
-                        self._emit(sid, st.tokens)
+                        self._emit(sid, st.tokens, lps=getattr(st, "logprobs", None) or None)

@@ -76,6 +76,8 @@ class LMHeadCE(torch.autograd.Function):
     def forward(ctx, x, w, targets, chunk: int = 2048, denom: float | None = None):
         T, H = x.shape
         V = w.shape[0]
+        # the trainer passes the global valid-target count as ``denom``; counting here
+        # (a device read) only happens for direct calls without it
         n_valid = int((targets >= 0).sum()) if denom is None else None
         scale = 1.0 / (denom if denom is not None else max(1, n_valid))
         total = torch.zeros((), dtype=torch.float32, device=x.device)

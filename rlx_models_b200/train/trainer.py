@@ -149,12 +149,15 @@ class Trainer:
         t0 = time.perf_counter()
         c = self.cfg
         if isinstance(batch, (tuple, list)):
+            # valid targets counted where the batch lives (no device round trip for host batches)
+            n_local = float((batch[1] >= 0).sum())
             ids, tgt = batch[0].to(self.device), batch[1].to(self.device)
         else:
+            n_local = float((batch[:, 1:] >= 0).sum())
             batch = batch.to(self.device)
             ids, tgt = batch[:, :-1].contiguous(), batch[:, 1:].contiguous()
         B_local, S = ids.shape
-        n_valid = torch.tensor([float((tgt >= 0).sum())], device=self.device)
+        n_valid = torch.tensor([n_local], device=self.device)
         if self.world > 1:
             dist.all_reduce(n_valid, group=self.group)
         global_tokens = max(1.0, float(n_valid))  # mean over the global batch's valid targets

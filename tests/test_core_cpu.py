@@ -316,3 +316,71 @@ def test_mixtral_and_qwen2_moe_configs_and_names():
     assert "model.layers.0.mlp.shared_expert_gate.weight" in w2
     lg, _ = DecoderOracle(q2, {k: v.float() for k, v in w2.items()}).forward(ids)
     assert torch.isfinite(lg).all()
+
+
+def _drive_overlap(sched, bufs, eos=-1, max_steps=10000):
+    """Overlapped scheduling with the same fake model (token = position % 97 + 1):
+    step n+1 is scheduled before step n's tokens are handed back; decode inputs
+    that are still placeholders name a row of the previous step's output, which
+    must hold exactly the token the synchronous loop would have fed."""
+    T = bufs[0].numel()
+    src = torch.full((T,), -1, dtype=torch.int32)
+    inflight, prev_out, steps = None, [], []
+    for _ in range(max_steps):
+        if not sched.has_work() and inflight is None:
+            break
+        launched = None
+        if sched.has_work():
+            info = sched.schedule(*bufs, src, True)
+            T_, R, nd = info["num_tokens"], info["num_logits"], info["num_decode"]
+            if T_:
+                ids = bufs[0][:T_].tolist()
+                srcs = src[:T_].tolist()
+                pos = bufs[1][:T_].tolist()
+                fed = [prev_out[srcs[t]] if srcs[t] >= 0 else ids[t] for t in range(T_)]
+                for t in range(nd):  # a decode input is the token sampled at the previous position
+                    assert fed[t] == (pos[t] - 1) % 97 + 1, (t, fed[t], pos[t])
+                rows = bufs[8][:R].tolist()
+                launched = (bufs[9][:R].tolist(), [pos[r] % 97 + 1 for r in rows])
+                steps.append(info)
+        if inflight is not None:
+            sched.update(inflight[0], inflight[1], eos)
+        if launched is not None:
+            prev_out = launched[1]
+        inflight = launched
+    return steps
+
+
+def test_scheduler_overlap_matches_sync():
+    from rlx_models_b200 import _runtime
+    lens = [5, 70, 33, 16, 1]
+    outs = {}
+    for mode in ("sync", "overlap"):
+        s = _runtime.Scheduler(num_blocks=200, max_num_seqs=8, max_batched_tokens=64, max_blocks_per_seq=64,
+                               prefix_caching=False, chunk_size=0)
+        bufs = _staging()
+        ids = [s.add_request([1 + (i % 90) for i in range(l)], 10, True, []) for l in lens]
+        (_drive if mode == "sync" else _drive_overlap)(s, bufs)
+        outs[mode] = [s.output_tokens(i) for i in ids]
+        assert s.stats()["free_blocks"] == 200
+    assert outs["sync"] == outs["overlap"]
+
+
+def test_scheduler_overlap_preemption_and_stop():
+    from rlx_models_b200 import _runtime
+    s = _runtime.Scheduler(6, 4, 64, 16, False, 0)
+    bufs = _staging(W=16)
+    ids = [s.add_request(list(range(1, 31)), 20, True, []) for _ in range(2)]
+    _drive_overlap(s, bufs)
+    for sid in ids:
+        assert s.output_tokens(sid) == [((29 + j) % 97) + 1 for j in range(20)]
+    assert s.stats()["preemptions"] >= 1 and s.stats()["free_blocks"] == 6
+    # stop id: the row scheduled behind the stop is discarded
+    s = _runtime.Scheduler(50, 4, 64, 16, False, 0)
+    bufs = _staging(W=16)
+    a = s.add_request([1, 2, 3], 50, False, [6])
+    b = s.add_request([1, 2, 3, 4], 5, False, [])
+    _drive_overlap(s, bufs)
+    assert s.output_tokens(a) == [3, 4, 5, 6] and s.finish_reason(a) == 2
+    assert s.output_tokens(b) == [4, 5, 6, 7, 8] and s.finish_reason(b) == 1
+    assert s.stats()["free_blocks"] == 50

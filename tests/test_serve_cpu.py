@@ -18,6 +18,7 @@ from rlx_models_b200.tokenizer import ByteTokenizer  # noqa: E402
 @dataclass
 class _St:
     tokens: list = field(default_factory=list)
+    logprobs: list = field(default_factory=list)
 
 
 @dataclass
@@ -25,6 +26,7 @@ class _Out:
     seq_id: int
     token_ids: list
     finish_reason: str
+    logprobs: list | None = None
 
 
 class FakeEngine:
@@ -57,8 +59,11 @@ class FakeEngine:
             ids, p = self.params[sid]
             t = (ids[-1] + len(st.tokens) + 1) % 256
             st.tokens.append(t)
+            if p.logprobs:
+                st.logprobs.append(-0.5 * len(st.tokens))
             if t in p.stop_token_ids or len(st.tokens) >= p.max_new_tokens:
-                done.append(_Out(sid, list(st.tokens), "stop" if t in p.stop_token_ids else "length"))
+                done.append(_Out(sid, list(st.tokens), "stop" if t in p.stop_token_ids else "length",
+                                 list(st.logprobs) if p.logprobs else None))
                 del self.requests[sid]
         return done
 
@@ -231,3 +236,23 @@ def test_transcriptions_endpoint():
         bad = c.post("/v1/audio/transcriptions", files={"file": ("a.wav", b"not audio", "audio/wav")})
         assert bad.status_code == 400
     runner.shutdown()
+
+
+def test_logprobs_completion_chat_and_stream(client):
+    c, _ = client
+    r = c.post("/v1/completions", json={"prompt": "a", "max_tokens": 3, "logprobs": 1})
+    lp = r.json()["choices"][0]["logprobs"]
+    assert lp["tokens"] == ["b", "c", "d"] and lp["token_logprobs"] == [-0.5, -1.0, -1.5]
+    assert lp["text_offset"] == [0, 1, 2]
+    r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "a"}], "max_tokens": 2,
+                                             "logprobs": True})
+    content = r.json()["choices"][0]["logprobs"]["content"]
+    assert [e["logprob"] for e in content] == [-0.5, -1.0]
+    with c.stream("POST", "/v1/completions", json={"prompt": "a", "max_tokens": 3, "stream": True,
+                                                    "logprobs": 1}) as s:
+        lines = [ln for ln in s.iter_lines() if ln]
+    chunks = [json.loads(ln[6:]) for ln in lines[:-1]]
+    got = [ch["choices"][0]["logprobs"]["token_logprobs"][0] for ch in chunks if ch["choices"][0]["logprobs"]]
+    assert len(got) == 3 and got[-1] == -1.5
+    r = c.post("/v1/completions", json={"prompt": "a", "max_tokens": 2})
+    assert r.json()["choices"][0]["logprobs"] is None

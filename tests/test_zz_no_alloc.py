@@ -82,6 +82,22 @@ def test_noalloc_matches_regular_entry_point_twice(cuda):
                                    splits=cs["splits"])
         rel = ((out.float() - ref.float()).norm() / ref.float().norm()).item()
         assert rel < 2e-2, rel
+        # and against the fp32 restatement of the same attention
+        orc = _oracle(q, kc, vc, tables, ctx, scale, sinks, cs["window"])
+        rel = ((out.float() - orc).norm() / orc.norm()).item()
+        assert rel < 2e-2, rel
+
+
+def _oracle(q, kc, vc, tables, ctx, scale, sinks, window):
+    from rlx_models_b200.ops.reference import attention, gather_paged
+    outs = []
+    for b in range(q.shape[0]):
+        L = int(ctx[b])
+        k = gather_paged(kc, tables[b], L)
+        v = gather_paged(vc, tables[b], L)
+        pos = torch.arange(L, device=q.device)
+        outs.append(attention(q[b:b + 1], k, v, pos[-1:], pos, scale, causal=True, window=window, sinks=sinks))
+    return torch.cat(outs)
 
 
 def test_noalloc_rejects_oversized_request(cuda):
