@@ -164,6 +164,8 @@ def serve(args):
     nsteps = max(1, eng.stats["steps"] - s0)
     e2e_val = sum(len(o.token_ids) for o in e2e_outs) / e2e_s
     clocks = sampler.summary()
+    if args.profile_steps > 0:
+        profile_decode(args, eng, cfg, sp, rank, dev)
     res = {
         "metric": METRIC if args.workload == "serve" else f"gpt-oss-120b-shape EP output tok/s (part of: {METRIC})",
         "value": round(value, 1), "unit": "output tok/s", "n_gpus": ws, "steps": args.steps,
@@ -195,6 +197,34 @@ def serve(args):
     return 0
 
 
+def profile_decode(args, eng, cfg, sp, rank, dev):
+    """Per-kernel device times of ``--profile-steps`` decode steps (torch profiler /
+    CUPTI, CUDA graphs off so every kernel is listed), one JSON file per rank.
+    Every rank runs the same steps, so collectives stay matched."""
+    import dataclasses
+
+    import torch
+
+    from rlx_models_b200.utils.trace import profile
+    prompts = make_prompts(args.num_requests, args.min_prompt, args.max_prompt, cfg.vocab_size, 4000)
+    for p in prompts:
+        eng.add_request(p, sp)
+    while eng.stats["graph_steps"] == 0 or eng.sched.num_waiting() > 0:
+        eng.step()
+        if eng.sched.num_waiting() == 0 and all(len(st.tokens) > 0 for st in eng.requests.values()):
+            break
+    saved = eng.cfg
+    eng.cfg = dataclasses.replace(saved, cuda_graphs=False)
+    rows = profile(eng.step, steps=args.profile_steps, warmup=2, top=40)
+    eng.cfg = saved
+    while eng.has_unfinished():
+        eng.step()
+    torch.cuda.synchronize(dev)
+    out = args.profile_out or "profile_decode"
+    with open(f"{out}.rank{rank}.json", "w") as f:
+        json.dump({"steps": args.profile_steps, "rows": rows}, f, indent=1)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -216,6 +246,9 @@ def main():
     ap.add_argument("--async-sched", type=int, default=1,
                     help="serving: 1 = schedule / launch step n+1 while step n runs (default), 0 = synchronous loop")
     ap.add_argument("--engine-metrics", default=None, help="serving: write per-step engine metrics (JSONL) here")
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="serving: after the timed passes, profile this many eager decode steps per rank")
+    ap.add_argument("--profile-out", default=None, help="serving: path prefix of the per-rank profile JSON")
     ap.add_argument("--tp-comm", default="pull", choices=["nccl", "fused", "pull"],
                     help="pull (default): decode steps read every rank's GEMM partial over NVLink in one kernel "
                          "with the residual add + RMSNorm, prefill on NCCL; nccl: NCCL all-reduce baseline; "

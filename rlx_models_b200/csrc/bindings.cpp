@@ -1061,6 +1061,76 @@ void flag_wait_probe(const Tensor& flag, int64_t target, Tensor& status, Tensor&
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void tp_argmax(const Tensor& logits, int64_t v_offset, Tensor& own_pairs, const Tensor& peer_pairs,
+               const Tensor& peer_flags, const Tensor& flags, Tensor& epoch, Tensor& cta_ctr, Tensor& out,
+               int64_t max_rows, int64_t rank, int64_t world, Tensor& status) {
+  check_cuda(logits, "logits");
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
+              "b200.tp_argmax: fp32 [R, V/world] logits");
+  TORCH_CHECK(out.scalar_type() == at::kInt && out.numel() >= logits.size(0), "b200.tp_argmax: out");
+  TORCH_CHECK(peer_pairs.scalar_type() == at::kLong && peer_pairs.numel() == world && peer_flags.numel() == world &&
+                  cta_ctr.numel() >= 2,
+              "b200.tp_argmax: peer tables / counters");
+  c10::cuda::CUDAGuard g(logits.device());
+  b200::TpArgmaxArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.ld = logits.stride(0);
+  a.V_local = (int)logits.size(1);
+  a.v_offset = (int)v_offset;
+  a.own_pairs = reinterpret_cast<unsigned long long*>(own_pairs.data_ptr());
+  a.peer_pairs = reinterpret_cast<unsigned long long* const*>(peer_pairs.data_ptr<int64_t>());
+  a.peer_flags = reinterpret_cast<unsigned* const*>(peer_flags.data_ptr<int64_t>());
+  a.flags = reinterpret_cast<const unsigned*>(flags.data_ptr<int32_t>());
+  a.epoch = reinterpret_cast<unsigned*>(epoch.data_ptr<int32_t>());
+  a.cta_ctr = reinterpret_cast<unsigned*>(cta_ctr.data_ptr<int32_t>());
+  a.out = out.data_ptr<int32_t>();
+  a.R = (int)logits.size(0);
+  a.max_rows = (int)max_rows;
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.status = status.data_ptr<int>();
+  b200::tp_argmax_launch(a, cur_stream(logits));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ar2_norm(const Tensor& peer_acc, const Tensor& peer_res, Tensor& own_res, const Tensor& peer_flags,
+              const Tensor& flags, Tensor& zero_buf, int64_t zero_rows, Tensor& h, const Tensor& norm_w, Tensor& out,
+              Tensor& epoch, Tensor& cta_ctr, int64_t rank, int64_t world, int64_t rpr, int64_t rpr_max, double eps,
+              Tensor& status) {
+  check_cuda(h, "h");
+  TORCH_CHECK(peer_acc.scalar_type() == at::kLong && peer_acc.numel() == world && peer_res.numel() == world &&
+                  peer_flags.numel() == world && flags.numel() >= 2 * world && cta_ctr.numel() >= 2,
+              "b200.ar2_norm: peer tables");
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && h.is_contiguous() && out.is_contiguous() &&
+                  zero_buf.scalar_type() == at::kFloat && zero_buf.size(0) >= zero_rows &&
+                  own_res.numel() >= 2 * rpr_max * h.size(1),
+              "b200.ar2_norm: buffers");
+  c10::cuda::CUDAGuard g(h.device());
+  b200::TwoShotNormArgs a{};
+  a.peer_acc = reinterpret_cast<const float* const*>(peer_acc.data_ptr<int64_t>());
+  a.peer_res = reinterpret_cast<const void* const*>(peer_res.data_ptr<int64_t>());
+  a.own_res = own_res.data_ptr();
+  a.peer_flags = reinterpret_cast<unsigned* const*>(peer_flags.data_ptr<int64_t>());
+  a.flags = reinterpret_cast<const unsigned*>(flags.data_ptr<int32_t>());
+  a.zero_buf = zero_buf.data_ptr<float>();
+  a.zero_rows = (int)zero_rows;
+  a.h = h.data_ptr();
+  a.norm_w = norm_w.data_ptr();
+  a.out = out.data_ptr();
+  a.epoch = reinterpret_cast<unsigned*>(epoch.data_ptr<int32_t>());
+  a.cta_ctr = reinterpret_cast<unsigned*>(cta_ctr.data_ptr<int32_t>());
+  a.M = (int)h.size(0);
+  a.H = (int)h.size(1);
+  a.world = (int)world;
+  a.rank = (int)rank;
+  a.rpr = (int)rpr;
+  a.rpr_max = (int)rpr_max;
+  a.eps = (float)eps;
+  a.status = status.data_ptr<int>();
+  b200::ar2_norm_launch(a, cur_stream(h));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void ar_pull_norm(const Tensor& peer_acc, const Tensor& peer_flags, const Tensor& flags, Tensor& zero_buf,
                   int64_t zero_rows, Tensor& h, const Tensor& norm_w, Tensor& out, Tensor& epoch, Tensor& cta_ctr,
                   int64_t rank, int64_t world, double eps, Tensor& status) {
@@ -1237,6 +1307,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("q_paged"), py::arg("softcap") = 0.0);
   m.def("argmax", &argmax);
   m.def("forward_tokens", &forward_tokens);
+  m.def("tp_argmax", &tp_argmax);
+  m.def("ar2_norm", &ar2_norm);
   m.def("sample", &sample);
   m.def("symm_malloc", &symm_malloc);
   m.def("symm_free", &symm_free);

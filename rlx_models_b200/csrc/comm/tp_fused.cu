@@ -380,3 +380,149 @@ void ar_pull_norm_launch(const PullNormArgs& a, cudaStream_t st) {
              st, a);
 }
 }  // namespace b200
+
+namespace b200 {
+namespace tpc {
+// Two-shot all-reduce + residual add + RMSNorm for decode-sized steps.
+//
+// Same inputs as ar_pull_norm (every rank's fp32 partial in its symmetric
+// slot, a replicated bf16 residual stream), but each rank reduces only the
+// rows it owns (row i belongs to rank i / rpr) and the others fetch the
+// finished rows:
+//   barrier 1  CTA 0 announces "partial ready" to every rank; the CTAs of the
+//              owned rows wait for all ranks' announcements;
+//   phase A    owned row: sum the world partials over NVLink (fp32), add the
+//              residual, RMSNorm; store the new residual row and the normalised
+//              row in this rank's result slot; the last of these CTAs
+//              announces "rows ready" to every rank (barrier 2);
+//   phase B    every CTA waits for barrier 2 and copies row i (residual and
+//              normalised) from its owner's result slot.
+// Per rank, each op moves M*H*4/world bytes of partials in and M*H*4 bytes of
+// results in over NVLink, against M*H*4*(world-1) bytes of partials for the
+// one-shot pull: the two-shot form wins once the partials outweigh the extra
+// barrier. Result slots are reused without double buffering: a rank rewrites
+// its slot in op k+1 only after every rank announced op k+1's partial, which
+// each does after its op-k kernel (and its phase-B reads) completed.
+__global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs a) {
+  __shared__ float red[kPullThreads / 32];
+  pdl_wait();
+  pdl_trigger();
+  const unsigned e = *reinterpret_cast<volatile unsigned*>(a.epoch) + 1u;
+  const int H = a.H;
+  const int i = blockIdx.x;
+  const int n_my = max(0, min(a.rpr, a.M - a.rank * a.rpr));
+  __nv_bfloat16* hbuf = reinterpret_cast<__nv_bfloat16*>(a.h);
+  __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+  __nv_bfloat16* res = reinterpret_cast<__nv_bfloat16*>(a.own_res);  // [2][rpr_max][H]
+  if (i == 0 && threadIdx.x < (unsigned)a.world) st_release_sys_u32(a.peer_flags[threadIdx.x] + a.rank, e);
+  if (i < n_my) {
+    if (threadIdx.x < (unsigned)a.world) wait_flag_geq(a.flags + threadIdx.x, e, a.status, 700 + threadIdx.x);
+    __syncthreads();
+    const int r = a.rank * a.rpr + i;
+    constexpr int kMaxChunks = 4;  // H <= 256 * 8 * 4
+    const int nch = H / (kPullThreads * 8);
+    float v[kMaxChunks][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      if (c >= nch) break;
+      const int col = (c * kPullThreads + threadIdx.x) * 8;
+      float sm[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int q = 0; q < a.world; ++q) {
+        const float4* src = reinterpret_cast<const float4*>(a.peer_acc[q] + (int64_t)r * H + col);
+        const float4 x0 = __ldcv(src), x1 = __ldcv(src + 1);
+        sm[0] += x0.x; sm[1] += x0.y; sm[2] += x0.z; sm[3] += x0.w;
+        sm[4] += x1.x; sm[5] += x1.y; sm[6] += x1.z; sm[7] += x1.w;
+      }
+      const uint4 hv = *reinterpret_cast<const uint4*>(hbuf + (int64_t)r * H + col);
+      const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        o[k] = pack_bf16x2(bf16_lo(hw[k]) + __bfloat162float(__float2bfloat16(sm[2 * k])),
+                           bf16_hi(hw[k]) + __bfloat162float(__float2bfloat16(sm[2 * k + 1])));
+        v[c][2 * k] = bf16_lo(o[k]);
+        v[c][2 * k + 1] = bf16_hi(o[k]);
+        ss += v[c][2 * k] * v[c][2 * k] + v[c][2 * k + 1] * v[c][2 * k + 1];
+      }
+      *reinterpret_cast<uint4*>(res + (int64_t)i * H + col) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < kPullThreads / 32 ? red[threadIdx.x] : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = rsqrtf(red[0] / (float)H + a.eps);
+    const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
+    __nv_bfloat16* res_out = res + (int64_t)a.rpr_max * H;
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      if (c >= nch) break;
+      const int col = (c * kPullThreads + threadIdx.x) * 8;
+      const uint4 wv = *reinterpret_cast<const uint4*>(nw + col);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        o[k] = pack_bf16x2(v[c][2 * k] * inv * bf16_lo(ww[k]), v[c][2 * k + 1] * inv * bf16_hi(ww[k]));
+      *reinterpret_cast<uint4*>(res_out + (int64_t)i * H + col) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0 && atomicAdd(a.cta_ctr, 1u) == (unsigned)n_my - 1) {
+      __threadfence_system();  // one system fence covers every rank's flag store below
+      for (int q = 0; q < a.world; ++q) st_relaxed_sys_u32(a.peer_flags[q] + a.world + a.rank, e);
+    }
+  } else if (n_my == 0 && i == 0 && threadIdx.x == 0) {
+    for (int q = 0; q < a.world; ++q) st_release_sys_u32(a.peer_flags[q] + a.world + a.rank, e);
+  }
+  // every CTA passes barrier 2 (it also orders the accumulator clearing below after
+  // every rank's phase-A reads of the previous op's partials)
+  if (threadIdx.x < (unsigned)a.world) wait_flag_geq(a.flags + a.world + threadIdx.x, e, a.status, 800 + threadIdx.x);
+  __syncthreads();
+  if (i < a.M) {
+    const int owner = i / a.rpr, j = i % a.rpr;
+    const uint4* sh = reinterpret_cast<const uint4*>(
+        reinterpret_cast<const __nv_bfloat16*>(a.peer_res[owner]) + (int64_t)j * H);
+    const uint4* so = reinterpret_cast<const uint4*>(
+        reinterpret_cast<const __nv_bfloat16*>(a.peer_res[owner]) + ((int64_t)a.rpr_max + j) * H);
+    uint4* dh = reinterpret_cast<uint4*>(hbuf + (int64_t)i * H);
+    uint4* dout = reinterpret_cast<uint4*>(out + (int64_t)i * H);
+    for (int c = threadIdx.x; c < H / 8; c += kPullThreads) {
+      dh[c] = __ldcv(sh + c);
+      dout[c] = __ldcv(so + c);
+    }
+  }
+  if (i < a.zero_rows) {
+    float4* z = reinterpret_cast<float4*>(a.zero_buf + (int64_t)i * H);
+    for (int c = threadIdx.x; c < H / 4; c += kPullThreads) z[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(a.cta_ctr + 1, 1u) == gridDim.x - 1) {
+      a.cta_ctr[0] = 0;
+      a.cta_ctr[1] = 0;
+      __threadfence();
+      *reinterpret_cast<volatile unsigned*>(a.epoch) = e;
+    }
+  }
+}
+}  // namespace tpc
+
+void ar2_norm_launch(const TwoShotNormArgs& a, cudaStream_t st) {
+  if (a.H % (tpc::kPullThreads * 8) != 0 || a.H > tpc::kPullThreads * 8 * 4)
+    throw std::runtime_error("b200.ar2_norm: hidden must be a multiple of 2048 and <= 8192");
+  if (a.rpr <= 0 || a.rpr > a.rpr_max || (int64_t)a.rpr * a.world < a.M)
+    throw std::runtime_error("b200.ar2_norm: row split does not cover the rows");
+  launch_pdl(tpc::ar2_norm_kernel, dim3(std::max(std::max(1, a.M), a.zero_rows)), dim3(tpc::kPullThreads), 0, st,
+             a);
+}
+}  // namespace b200
+

@@ -136,6 +136,44 @@ struct PullNormArgs {
 };
 void ar_pull_norm_launch(const PullNormArgs& a, cudaStream_t st);
 
+// Two-shot variant (each rank reduces the rows it owns, the others fetch them):
+// see comm/tp_fused.cu ar2_norm_kernel.
+struct TwoShotNormArgs {
+  const float* const* peer_acc;  // [world] each rank's fp32 [rows][H] partial (this op's parity)
+  const void* const* peer_res;   // [world] each rank's bf16 [2][rpr_max][H] result slot
+  void* own_res;                 // this rank's result slot
+  unsigned* const* peer_flags;   // [world] each rank's flag array [2][world]
+  const unsigned* flags;         // local flags [2][world]
+  float* zero_buf;               // own previous-parity accumulator
+  int zero_rows;
+  void* h;                       // [M][H] bf16 replicated residual (in/out)
+  const void* norm_w;
+  void* out;                     // [M][H] bf16
+  unsigned* epoch;
+  unsigned* cta_ctr;             // [2]
+  int M, H, world, rank, rpr, rpr_max;
+  float eps;
+  int* status;
+};
+void ar2_norm_launch(const TwoShotNormArgs& a, cudaStream_t st);
+
+// Vocab-parallel greedy argmax over NVLink peer memory: see comm/tp_sample.cu.
+struct TpArgmaxArgs {
+  const float* logits;                    // [R][ld] fp32, this rank's vocab shard
+  int64_t ld;
+  int V_local, v_offset;                  // shard width, first global id of the shard
+  unsigned long long* own_pairs;          // this rank's [2][max_rows] packed keys
+  unsigned long long* const* peer_pairs;  // [world] every rank's pair buffer
+  unsigned* const* peer_flags;            // [world] every rank's flag array [world]
+  const unsigned* flags;                  // local flags [world]
+  unsigned* epoch;
+  unsigned* cta_ctr;                      // [2] arrival / departure counters
+  int32_t* out;                           // [R] global token ids
+  int R, max_rows, world, rank;
+  int* status;
+};
+void tp_argmax_launch(const TpArgmaxArgs& a, cudaStream_t st);
+
 // Expert-parallel combine over NVLink + residual add + RMSNorm: see
 // comm/ep_combine.cu. Every rank routed the same tokens; token t's slot s went
 // to expert experts[t, s], held by rank experts[t, s] / e_local, whose down

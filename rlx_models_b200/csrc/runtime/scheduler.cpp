@@ -255,6 +255,10 @@ class Scheduler {
                                       [&](int64_t id) { return seqs_[id]->status != RUNNING; }),
                        step_decode_.end());
     tokens = (int)step_decode_.size();
+    // longest context first: the decode attention grid walks rows in order, so the
+    // longest (sequence, kv-head) CTAs start in the first wave and short ones fill the tail
+    std::stable_sort(step_decode_.begin(), step_decode_.end(),
+                     [&](int64_t x, int64_t y) { return seqs_[x]->num_computed > seqs_[y]->num_computed; });
     // 2. prefill chunks (continuing sequences first, then admissions)
     std::vector<int64_t> cand;
     for (int64_t id : running_) {

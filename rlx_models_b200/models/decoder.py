@@ -46,6 +46,7 @@ class ForwardBatch:
     pre_max_q: int = 0
     logit_rows: torch.Tensor | None = None        # [R] int64 rows needing logits
     seq_slots: torch.Tensor | None = None         # [Bd + Bp] int32 state slot per sequence (stateful models)
+    pre_cu_host: list | None = None               # host copy of pre_cu_q (lets a TP model split the step)
 
     @property
     def num_tokens(self) -> int:
@@ -224,9 +225,68 @@ class DecoderLM:
             gu = ops.linear_swiglu(x, L.w_gu, act=self.glu_act)
         return comm.rowpar_add_norm(gu, L.wd, h, nw)
 
+    MB_MIN_TOKENS = 1024  # smallest step split into two overlapped micro-batches under TP
+
+    def _microbatches(self, fb: ForwardBatch):
+        """Split a prefill-heavy step into two sequence-disjoint micro-batches of
+        about equal token counts (decode rows go with the first), or None."""
+        cu = fb.pre_cu_host
+        if (cu is None or len(cu) < 3 or fb.seq_slots is not None or fb.num_tokens < self.MB_MIN_TOKENS
+                or getattr(self, "retrieval", None) is not None):
+            return None
+        nd, npf = fb.num_decode, len(cu) - 1
+        half = (nd + cu[-1]) / 2
+        k = min(range(1, npf), key=lambda j: abs(nd + cu[j] - half))
+        tA = nd + cu[k]
+        if tA <= ops.ACC_MAX_M or fb.num_tokens - tA <= ops.ACC_MAX_M:
+            return None  # both halves must stay on the prefill (non-accumulating) paths
+        qA = max(cu[j + 1] - cu[j] for j in range(k))
+        qB = max(cu[j + 1] - cu[j] for j in range(k, npf))
+        a = ForwardBatch(input_ids=fb.input_ids[:tA], positions=fb.positions[:tA], slots=fb.slots[:tA],
+                         num_decode=nd, dec_block_tables=fb.dec_block_tables, dec_ctx_lens=fb.dec_ctx_lens,
+                         pre_block_tables=fb.pre_block_tables[:k], pre_ctx_lens=fb.pre_ctx_lens[:k],
+                         pre_cu_q=fb.pre_cu_q[:k + 1], pre_max_q=qA)
+        b = ForwardBatch(input_ids=fb.input_ids[tA:], positions=fb.positions[tA:], slots=fb.slots[tA:],
+                         num_decode=0, pre_block_tables=fb.pre_block_tables[k:], pre_ctx_lens=fb.pre_ctx_lens[k:],
+                         pre_cu_q=fb.pre_cu_q[k:] - cu[k], pre_max_q=qB)
+        return a, b
+
+    def _forward_overlapped(self, a: ForwardBatch, b: ForwardBatch, kv, comm, comm_b) -> torch.Tensor:
+        """Tensor-parallel prefill as two micro-batches on two streams with one
+        communicator (process group) each: while one micro-batch's row-parallel
+        all-reduce crosses NVLink, the other's GEMMs and attention run, layer by
+        layer. The halves touch disjoint sequences (KV pages), so they need no
+        ordering between them; each stream uses its own scratch set."""
+        from ..ops._ext import scratch_slot
+        main = torch.cuda.current_stream(self.device)
+        side = getattr(self, "_side_stream", None)
+        if side is None:
+            side = self._side_stream = torch.cuda.Stream(self.device)
+        side.wait_stream(main)
+        n = len(self.layers)
+        ha = comm.embed(a.input_ids, self.embed)
+        xa = comm.norm_in(ha, self.layers[0].ln1)
+        with torch.cuda.stream(side), scratch_slot(1):
+            hb = comm_b.embed(b.input_ids, self.embed)
+            xb = comm_b.norm_in(hb, self.layers[0].ln1)
+        for i, L in enumerate(self.layers):
+            nw = self.layers[i + 1].ln1 if i + 1 < n else self.norm
+            with nvtx(f"layer{i}.mb0"):
+                xa = self._layer(i, L, xa, ha, a, kv, comm, nw)
+            with torch.cuda.stream(side), scratch_slot(1), nvtx(f"layer{i}.mb1"):
+                xb = self._layer(i, L, xb, hb, b, kv, comm_b, nw)
+        main.wait_stream(side)
+        xb.record_stream(main)
+        return torch.cat([xa, xb])
+
     def forward_hidden(self, fb: ForwardBatch, kv: PagedKVCache) -> torch.Tensor:
         """Returns the final-normed hidden states of every token ([T, H])."""
         comm = self.comm or LocalComm(self.cfg.rms_norm_eps)
+        comm_b = getattr(comm, "microbatch_comm", None)
+        if comm_b is not None and not inspecting():
+            mbs = self._microbatches(fb)
+            if mbs is not None:
+                return self._forward_overlapped(mbs[0], mbs[1], kv, comm, comm_b)
         h = comm.embed(fb.input_ids, self.embed)
         if self.cfg.embedding_multiplier != 1.0:
             h.mul_(self.cfg.embedding_multiplier)

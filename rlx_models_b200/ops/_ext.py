@@ -95,8 +95,28 @@ def launch_count() -> int:
     return _LAUNCHES[0]
 
 
-_scratch: dict[int, DeviceScratch] = {}
+_scratch: dict[tuple[int, int], DeviceScratch] = {}
 _lock = threading.Lock()
+_slot = threading.local()
+
+
+class scratch_slot:
+    """Context manager: kernels launched inside use scratch set ``i`` of the
+    device. Work queued on two streams at once (e.g. two prefill micro-batches
+    overlapping one's collective with the other's GEMMs) must use different
+    slots, since split-K workspaces and semaphores are per set."""
+
+    def __init__(self, i: int):
+        self.i = int(i)
+
+    def __enter__(self):
+        self.prev = getattr(_slot, "i", 0)
+        _slot.i = self.i
+        return self
+
+    def __exit__(self, *exc):
+        _slot.i = self.prev
+        return False
 
 
 def scratch(device: torch.device | int | None = None) -> DeviceScratch:
@@ -105,15 +125,25 @@ def scratch(device: torch.device | int | None = None) -> DeviceScratch:
     idx = device.index if isinstance(device, torch.device) else int(device)
     if idx is None:
         idx = torch.cuda.current_device()
-    s = _scratch.get(idx)
+    key = (idx, getattr(_slot, "i", 0))
+    s = _scratch.get(key)
     if s is None:
         with _lock:
-            s = _scratch.get(idx)
+            s = _scratch.get(key)
             if s is None:
                 s = DeviceScratch(torch.device("cuda", idx))
-                _scratch[idx] = s
+                _scratch[key] = s
     return s
 
 
 def check_errors(device=None):
-    scratch(device).check()
+    if device is None:
+        device = torch.cuda.current_device()
+    idx = device.index if isinstance(device, torch.device) else int(device)
+    if idx is None:
+        idx = torch.cuda.current_device()
+    for (d, _), s in list(_scratch.items()):
+        if d == idx:
+            s.check()
+    if (idx, 0) not in _scratch:
+        scratch(device).check()

@@ -42,8 +42,11 @@ def main():
     w = (torch.randn(H, K, device=dev, generator=g) * 0.02).bfloat16()
     nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
     res = {}
-    for kind in ("nccl", "fused", "pull"):
-        comm = make_tp_comm(kind, rank, world, dev, 1e-6, max_tokens=max(M, 128), hidden=H)
+    variants = [("nccl", "nccl", {}), ("fused", "fused", {})]
+    if M <= 128:  # the pull communicator's decode path, one-shot and two-shot
+        variants += [("pull", "pull", {"two_shot": "off"}), ("pull2", "pull", {"two_shot": "on"})]
+    for label, kind, kw in variants:
+        comm = make_tp_comm(kind, rank, world, dev, 1e-6, max_tokens=max(M, 128), hidden=H, **kw)
         ids = torch.zeros(M, dtype=torch.int32, device=dev)
         table = torch.randn(8, H, device=dev).bfloat16()
         h = comm.embed(ids, table)
@@ -81,7 +84,7 @@ def main():
         torch.cuda.synchronize(dev)
         t = torch.tensor([e0.elapsed_time(e1) / args.iters * 1e3], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        res[kind] = round(float(t), 2)
+        res[label] = round(float(t), 2)
         ops.check_errors(dev)
         if args.graph:
             del gr

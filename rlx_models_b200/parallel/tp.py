@@ -37,6 +37,9 @@ class NcclTPComm:
     def __init__(self, rank: int, world: int, device: torch.device, eps: float = 1e-6, group=None):
         self.rank, self.world, self.device, self.eps = rank, world, device, eps
         self.group = group
+        # second communicator on its own process group for overlapped prefill
+        # micro-batches (models.decoder.DecoderLM._forward_overlapped); None = off
+        self.microbatch_comm = None
 
     def embed(self, ids, table):
         return ops.embedding(ids, table)
@@ -78,15 +81,27 @@ class NcclTPComm:
         return out
 
 
-def make_tp_comm(kind: str, rank: int, world: int, device, eps: float = 1e-6, **kw):
+def make_tp_comm(kind: str, rank: int, world: int, device, eps: float = 1e-6, prefill_overlap: bool | None = None,
+                 **kw):
+    """``prefill_overlap`` (default: on unless B200_TP_PREFILL_OVERLAP=0) gives the
+    NCCL and pull communicators a second NCCL process group, so large prefill
+    steps run as two micro-batches whose all-reduces overlap each other's compute."""
     if world == 1:
         return None
     if kind == "nccl":
-        return NcclTPComm(rank, world, device, eps)
-    if kind == "fused":
+        comm = NcclTPComm(rank, world, device, eps)
+    elif kind == "fused":
         from .fused_tp import FusedTPComm
         return FusedTPComm(rank, world, device, eps, **kw)
-    if kind == "pull":
+    elif kind == "pull":
         from .pull_tp import PullTPComm
-        return PullTPComm(rank, world, device, eps, **kw)
-    raise ValueError(kind)
+        comm = PullTPComm(rank, world, device, eps, **kw)
+    else:
+        raise ValueError(kind)
+    if prefill_overlap is None:
+        import os
+        prefill_overlap = os.environ.get("B200_TP_PREFILL_OVERLAP", "1") != "0"
+    if prefill_overlap:
+        g2 = dist.new_group(list(range(world)))
+        comm.microbatch_comm = NcclTPComm(rank, world, device, eps, group=g2)
+    return comm

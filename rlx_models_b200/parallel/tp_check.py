@@ -2,12 +2,25 @@
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 -m rlx_models_b200.parallel.tp_check
 
-Builds the same seeded decoder at TP=N with each communicator (NCCL baseline
-and the fused NVLink path) and compares, on every rank, the prefill logits
-with a TP=1 copy of the model on the same GPU, then compares greedy
-generations through the engine (CUDA graphs on) with the TP=1 engine.
-Prints one JSON line per communicator from rank 0 and exits non-zero on a
-mismatch.
+Builds the same seeded decoder at TP=N with each communicator (NCCL baseline,
+the fused NVLink push path, the pull all-reduce in its one-shot and two-shot
+forms) and compares, on every rank, against a TP=1 copy of the model on the
+same GPU:
+
+* prefill logits of one 70-token prompt,
+* decode-step logits: 20 prompts prefilled into the paged cache, then one
+  decode step of 20 rows (the row count that selects the two-shot reduction
+  from 4 ranks up), relative error of the gathered vocab-parallel logits,
+* the vocab-parallel greedy choice (peer-memory argmax) against the argmax of
+  the gathered logits,
+* a 1500-token prefill step of three sequences, which the TP model runs as two
+  micro-batches overlapping each other's all-reduces (NCCL and pull
+  communicators), against the TP=1 logits,
+* greedy generations through the engine (CUDA graphs on): first tokens equal,
+  and the decode steps' logits above stand for the rest.
+
+Prints one JSON line per communicator from rank 0 (with the measured errors)
+and exits non-zero on a mismatch.
 """
 from __future__ import annotations
 
@@ -56,13 +69,90 @@ def main():
                             pre_cu_q=torch.tensor([0, T], dtype=torch.int32, device=dev), pre_max_q=T)
 
     ref_logits = ref.forward(fb(), ref.make_kv_cache(nb))
+
+    # decode-step batch: 20 prompts prefilled, then one decode token each
+    dp = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in
+          (3, 17, 40, 9, 64, 1, 25, 31, 16, 15, 50, 2, 33, 8, 47, 12, 5, 60, 21, 29)]
+    B = len(dp)
+    lens = [len(p) for p in dp]
+    nbs = [(n + 1 + 15) // 16 for n in lens]
+    maxb = max(nbs)
+    offs = [sum(nbs[:i]) for i in range(B)]
+    tables = torch.zeros(B, maxb, dtype=torch.int32)
+    for i in range(B):
+        tables[i, :nbs[i]] = torch.arange(offs[i], offs[i] + nbs[i], dtype=torch.int32)
+    tables = tables.to(dev)
+
+    def slot_of(i, p):
+        return (offs[i] + p // 16) * 16 + p % 16
+
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    pre = ForwardBatch(
+        input_ids=torch.tensor([t for p in dp for t in p], dtype=torch.int32, device=dev),
+        positions=torch.tensor([j for n in lens for j in range(n)], dtype=torch.int32, device=dev),
+        slots=torch.tensor([slot_of(i, j) for i, n in enumerate(lens) for j in range(n)], dtype=torch.int64,
+                           device=dev),
+        num_decode=0, pre_block_tables=tables, pre_ctx_lens=torch.tensor(lens, dtype=torch.int32, device=dev),
+        pre_cu_q=torch.tensor(cu, dtype=torch.int32, device=dev), pre_max_q=max(lens),
+        logit_rows=torch.tensor(cu[1:], dtype=torch.int64, device=dev) - 1)
+
+    def dec(next_ids):
+        return ForwardBatch(input_ids=next_ids, positions=torch.tensor(lens, dtype=torch.int32, device=dev),
+                            slots=torch.tensor([slot_of(i, n) for i, n in enumerate(lens)], dtype=torch.int64,
+                                               device=dev), num_decode=B, dec_block_tables=tables,
+                            dec_ctx_lens=torch.tensor([n + 1 for n in lens], dtype=torch.int32, device=dev))
+
+    nblk = sum(nbs)
+    kv_ref = ref.make_kv_cache(nblk)
+    next_ids = ops.argmax(ref.forward(pre, kv_ref))
+    ref_dec = ref.forward(dec(next_ids), kv_ref)
+
+    # a large prefill step (3 sequences, 1500 tokens) that the TP model runs as two
+    # overlapped micro-batches (pre_cu_host given), against the TP=1 logits
+    big = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (700, 300, 500)]
+    blens = [len(p) for p in big]
+    bnb = [(n + 15) // 16 for n in blens]
+    boff = [sum(bnb[:i]) for i in range(len(big))]
+    btab = torch.zeros(len(big), max(bnb), dtype=torch.int32)
+    for i in range(len(big)):
+        btab[i, :bnb[i]] = torch.arange(boff[i], boff[i] + bnb[i], dtype=torch.int32)
+    bcu = [0]
+    for n in blens:
+        bcu.append(bcu[-1] + n)
+
+    def bigfb():
+        return ForwardBatch(
+            input_ids=torch.tensor([t for p in big for t in p], dtype=torch.int32, device=dev),
+            positions=torch.tensor([j for n in blens for j in range(n)], dtype=torch.int32, device=dev),
+            slots=torch.tensor([(boff[i] + j // 16) * 16 + j % 16 for i, n in enumerate(blens) for j in range(n)],
+                               dtype=torch.int64, device=dev),
+            num_decode=0, pre_block_tables=btab.to(dev),
+            pre_ctx_lens=torch.tensor(blens, dtype=torch.int32, device=dev),
+            pre_cu_q=torch.tensor(bcu, dtype=torch.int32, device=dev), pre_max_q=max(blens),
+            logit_rows=torch.tensor(bcu[1:], dtype=torch.int64, device=dev) - 1, pre_cu_host=list(bcu))
+
+    ref_big = ref.forward(bigfb(), ref.make_kv_cache(sum(bnb)))
     ok_all = True
-    for kind in ("nccl", "fused", "pull"):
-        comm = make_tp_comm(kind, rank, world, dev, cfg.rms_norm_eps, max_tokens=512, hidden=cfg.hidden_size)
+    kinds = [("nccl", {}), ("fused", {}), ("pull", {"two_shot": "off"}), ("pull", {"two_shot": "on"})]
+    for kind, kw in kinds:
+        comm = make_tp_comm(kind, rank, world, dev, cfg.rms_norm_eps, max_tokens=512, hidden=cfg.hidden_size, **kw)
+        name = kind + ("" if not kw else ("-two-shot" if kw["two_shot"] == "on" else "-one-shot"))
         m = DecoderLM(cfg, w, device=dev, tp_rank=rank, tp_size=world, comm=comm)
         lg_local = m.forward(fb(), m.make_kv_cache(nb))
         lg = comm.gather_logits(lg_local)
         rel = ((lg - ref_logits).norm() / ref_logits.norm()).item()
+        kv_m = m.make_kv_cache(nblk)
+        m.forward(pre, kv_m)
+        dl_local = m.forward(dec(next_ids), kv_m)
+        dl = comm.gather_logits(dl_local)
+        rel_dec = ((dl - ref_dec).norm() / ref_dec.norm()).item()
+        pick = comm.greedy(dl_local, torch.empty(B, dtype=torch.int32, device=dev))
+        greedy_ok = bool(torch.equal(pick.long(), dl.argmax(1)))
+        bl = comm.gather_logits(m.forward(bigfb(), m.make_kv_cache(sum(bnb))))
+        rel_big = ((bl - ref_big).norm() / ref_big.norm()).item()
+        overlapped = getattr(comm, "microbatch_comm", None) is not None
         eng = LLMEngine(m, EngineConfig(**ecfg))
         toks = [o.token_ids for o in eng.generate(prompts, sp)]
         agree = sum(a == b for a, b in zip(toks, ref_tokens))
@@ -74,12 +164,15 @@ def main():
                      zip(toks, ref_tokens)) / sum(len(a) for a in ref_tokens)
         ops.check_errors(dev)
         eng.graphs.clear()
-        ok = rel < 2e-2 and first == len(prompts) and prefix >= 0.5
+        ok = rel < 2e-2 and rel_dec < 2e-2 and rel_big < 2e-2 and greedy_ok and first == len(prompts)
         ok_all &= ok
         t = torch.tensor([1.0 if ok else 0.0], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MIN)
         if rank == 0:
-            print(json.dumps({"comm": kind, "world": world, "logits_rel_err": rel, "seqs_equal": agree, "first_tokens_equal": first, "prefix_agreement": round(prefix, 3),
+            print(json.dumps({"comm": name, "world": world, "logits_rel_err": rel, "decode_logits_rel_err": rel_dec,
+                              "big_prefill_rel_err": rel_big, "prefill_overlapped": overlapped,
+                              "greedy_matches_gathered_argmax": greedy_ok, "seqs_equal": agree,
+                              "first_tokens_equal": first, "prefix_agreement": round(prefix, 3),
                               "seqs": len(prompts), "graph_steps": eng.stats["graph_steps"],
                               "ok_all_ranks": bool(t.item() == 1.0)}), flush=True)
         torch.cuda.synchronize(dev)

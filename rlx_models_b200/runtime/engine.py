@@ -369,7 +369,8 @@ class LLMEngine:
             pre_block_tables=d["pre_tables"][:npf] if npf else None,
             pre_ctx_lens=d["pre_ctx"][:npf] if npf else None, pre_cu_q=d["pre_cu"][:npf + 1] if npf else None,
             pre_max_q=max_q, logit_rows=d["logit_rows"][:R],
-            seq_slots=d["seq_slots"][:nd + npf] if self.stateful else None)
+            seq_slots=d["seq_slots"][:nd + npf] if self.stateful else None,
+            pre_cu_host=self.h["pre_cu"][:npf + 1].tolist() if npf else None)
         return self.model.forward(fb, self.kv)
 
     def _bucket(self, n: int) -> int | None:

@@ -1,5 +1,7 @@
-"""Multi-GPU checks through torchrun (skipped with fewer than 2 GPUs):
-tensor-parallel and pipeline-parallel generations equal the single-GPU ones."""
+"""Multi-GPU checks through torchrun (each skipped with fewer GPUs than ranks):
+tensor-parallel prefill / decode logits and generations, pipeline, FLUX
+sequence-parallel, expert-parallel and FSDP paths against their single-GPU
+counterparts, at 2 ranks and (where the box has them) 4 and 8."""
 import os
 import subprocess
 import sys
@@ -27,8 +29,10 @@ def test_pipeline_parallel_two_stages():
     assert '"match": true' in out
 
 
-def test_tensor_parallel_two_ranks():
-    _torchrun("rlx_models_b200.parallel.tp_check", 2)
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_tensor_parallel(n):
+    out = _torchrun("rlx_models_b200.parallel.tp_check", n)
+    assert '"ok_all_ranks": false' not in out and out.count('"ok_all_ranks": true') == 4
 
 
 def test_flux_sequence_parallel_two_ranks():
