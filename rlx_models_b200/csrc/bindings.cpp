@@ -1061,6 +1061,134 @@ void flag_wait_probe(const Tensor& flag, int64_t target, Tensor& status, Tensor&
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// -- training elementwise kernels (train/train_fused.cu) ---------------------
+static void check_bf16_contig(const Tensor& t, const char* what) {
+  check_cuda(t, what);
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16 && t.is_contiguous(), "b200: ", what, " must be contiguous bf16");
+}
+
+void rmsnorm_train_fwd(const Tensor& x, const Tensor& w, Tensor& y, Tensor& rstd, double eps) {
+  check_bf16_contig(x, "x");
+  check_bf16_contig(w, "w");
+  const int64_t H = x.size(-1), rows = x.numel() / H;
+  TORCH_CHECK(y.numel() == x.numel() && y.is_contiguous() && rstd.scalar_type() == at::kFloat && rstd.numel() >= rows,
+              "b200.rmsnorm_train_fwd: outputs");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::rmsnorm_train_fwd_launch(x.data_ptr(), w.data_ptr(), y.data_ptr(), rstd.data_ptr<float>(), (int)rows, (int)H,
+                                 (float)eps, x.get_device(), cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rmsnorm_train_bwd(const Tensor& dy, const Tensor& x, const Tensor& w, const Tensor& rstd, Tensor& dx,
+                       Tensor& dw) {
+  check_bf16_contig(dy, "dy");
+  check_bf16_contig(x, "x");
+  check_bf16_contig(w, "w");
+  const int64_t H = x.size(-1), rows = x.numel() / H;
+  TORCH_CHECK(dw.scalar_type() == at::kFloat && dw.numel() == H && dx.numel() == x.numel() && dx.is_contiguous() &&
+                  dy.numel() == x.numel(),
+              "b200.rmsnorm_train_bwd: fp32 dw [H], dx like x");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::rmsnorm_train_bwd_launch(dy.data_ptr(), x.data_ptr(), w.data_ptr(), rstd.data_ptr<float>(), dx.data_ptr(),
+                                 dw.data_ptr<float>(), (int)rows, (int)H, x.get_device(), cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static b200::QKNormRopeArgs qknr_args(const Tensor& qkv, const optional<Tensor>& qn, const optional<Tensor>& kn,
+                                      const Tensor& cos, const Tensor& sin, int64_t S, int64_t Hq, int64_t Hkv,
+                                      double eps) {
+  check_bf16_contig(qkv, "qkv");
+  TORCH_CHECK(cos.scalar_type() == at::kBFloat16 && sin.scalar_type() == at::kBFloat16 && cos.size(-1) == 128 &&
+                  cos.is_contiguous() && sin.is_contiguous() && cos.size(0) >= S,
+              "b200.qk_norm_rope: bf16 [S, 128] tables");
+  TORCH_CHECK(qkv.size(-1) == (Hq + 2 * Hkv) * 128, "b200.qk_norm_rope: qkv width");
+  b200::QKNormRopeArgs a{};
+  a.qkv = qkv.data_ptr();
+  a.q_norm = opt_ptr(qn);
+  a.k_norm = opt_ptr(kn);
+  a.cos = cos.data_ptr();
+  a.sin = sin.data_ptr();
+  a.positions = nullptr;
+  a.D = 128;
+  a.Hq = (int)Hq;
+  a.Hkv = (int)Hkv;
+  a.T = (int)(qkv.numel() / ((Hq + 2 * Hkv) * 128));
+  a.S = (int)S;
+  a.eps = (float)eps;
+  return a;
+}
+
+void qk_norm_rope_fwd(const Tensor& qkv, const optional<Tensor>& qn, const optional<Tensor>& kn, const Tensor& cos,
+                      const Tensor& sin, int64_t S, int64_t Hq, int64_t Hkv, double eps, Tensor& q, Tensor& k,
+                      Tensor& v, Tensor& rstd_q, Tensor& rstd_k) {
+  auto a = qknr_args(qkv, qn, kn, cos, sin, S, Hq, Hkv, eps);
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && q.numel() == (int64_t)a.T * Hq * 128 &&
+                  k.numel() == (int64_t)a.T * Hkv * 128 && v.numel() == k.numel() && rstd_q.numel() >= a.T * Hq &&
+                  rstd_k.numel() >= a.T * Hkv,
+              "b200.qk_norm_rope_fwd: outputs");
+  a.q = q.data_ptr();
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.rstd_q = rstd_q.data_ptr<float>();
+  a.rstd_k = rstd_k.data_ptr<float>();
+  c10::cuda::CUDAGuard g(qkv.device());
+  b200::qk_norm_rope_fwd_launch(a, qkv.get_device(), cur_stream(qkv));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void qk_norm_rope_bwd(const Tensor& qkv, const optional<Tensor>& qn, const optional<Tensor>& kn, const Tensor& cos,
+                      const Tensor& sin, int64_t S, int64_t Hq, int64_t Hkv, const Tensor& rstd_q,
+                      const Tensor& rstd_k, const Tensor& dq, const Tensor& dk, const Tensor& dv, Tensor& dqkv,
+                      const optional<Tensor>& dw_q, const optional<Tensor>& dw_k) {
+  auto a = qknr_args(qkv, qn, kn, cos, sin, S, Hq, Hkv, 1e-6);
+  TORCH_CHECK(dq.is_contiguous() && dk.is_contiguous() && dv.is_contiguous() && dqkv.is_contiguous() &&
+                  dqkv.numel() == qkv.numel() && dq.numel() == (int64_t)a.T * Hq * 128,
+              "b200.qk_norm_rope_bwd: contiguous gradients");
+  a.rstd_q = const_cast<float*>(rstd_q.data_ptr<float>());
+  a.rstd_k = const_cast<float*>(rstd_k.data_ptr<float>());
+  a.dq = dq.data_ptr();
+  a.dk = dk.data_ptr();
+  a.dv = dv.data_ptr();
+  a.dqkv = dqkv.data_ptr();
+  a.dw_q = dw_q.has_value() && dw_q->defined() ? dw_q->data_ptr<float>() : nullptr;
+  a.dw_k = dw_k.has_value() && dw_k->defined() ? dw_k->data_ptr<float>() : nullptr;
+  c10::cuda::CUDAGuard g(qkv.device());
+  b200::qk_norm_rope_bwd_launch(a, qkv.get_device(), cur_stream(qkv));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void swiglu_train_fwd(const Tensor& gu, Tensor& h) {
+  check_bf16_contig(gu, "gate_up");
+  const int64_t I = gu.size(-1) / 2, T = gu.numel() / gu.size(-1);
+  TORCH_CHECK(h.numel() == T * I && h.is_contiguous(), "b200.swiglu_train_fwd: h");
+  c10::cuda::CUDAGuard g(gu.device());
+  b200::swiglu_train_fwd_launch(gu.data_ptr(), h.data_ptr(), T, (int)I, gu.get_device(), cur_stream(gu));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void swiglu_train_bwd(const Tensor& dh, const Tensor& gu, Tensor& dgu) {
+  check_bf16_contig(gu, "gate_up");
+  check_bf16_contig(dh, "dh");
+  const int64_t I = gu.size(-1) / 2, T = gu.numel() / gu.size(-1);
+  TORCH_CHECK(dgu.numel() == gu.numel() && dgu.is_contiguous() && dh.numel() == T * I,
+              "b200.swiglu_train_bwd: shapes");
+  c10::cuda::CUDAGuard g(gu.device());
+  b200::swiglu_train_bwd_launch(dh.data_ptr(), gu.data_ptr(), dgu.data_ptr(), T, (int)I, gu.get_device(),
+                                cur_stream(gu));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void scale_by(Tensor& t, const Tensor& g) {
+  check_cuda(t, "t");
+  TORCH_CHECK(t.is_contiguous() && (t.scalar_type() == at::kFloat || t.scalar_type() == at::kBFloat16) &&
+                  g.scalar_type() == at::kFloat && g.numel() == 1 && g.is_cuda(),
+              "b200.scale_by: contiguous fp32/bf16 tensor, fp32 device scalar");
+  c10::cuda::CUDAGuard gd(t.device());
+  b200::scale_by_launch(t.data_ptr(), t.scalar_type() == at::kFloat, t.numel(), g.data_ptr<float>(), t.get_device(),
+                        cur_stream(t));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void tp_argmax(const Tensor& logits, int64_t v_offset, Tensor& own_pairs, const Tensor& peer_pairs,
                const Tensor& peer_flags, const Tensor& flags, Tensor& epoch, Tensor& cta_ctr, Tensor& out,
                int64_t max_rows, int64_t rank, int64_t world, Tensor& status) {
@@ -1309,6 +1437,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward_tokens", &forward_tokens);
   m.def("tp_argmax", &tp_argmax);
   m.def("ar2_norm", &ar2_norm);
+  m.def("rmsnorm_train_fwd", &rmsnorm_train_fwd);
+  m.def("rmsnorm_train_bwd", &rmsnorm_train_bwd);
+  m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("swiglu_train_fwd", &swiglu_train_fwd);
+  m.def("swiglu_train_bwd", &swiglu_train_bwd);
+  m.def("scale_by", &scale_by);
   m.def("sample", &sample);
   m.def("symm_malloc", &symm_malloc);
   m.def("symm_free", &symm_free);

@@ -157,6 +157,39 @@ struct TwoShotNormArgs {
 };
 void ar2_norm_launch(const TwoShotNormArgs& a, cudaStream_t st);
 
+// Training-path elementwise kernels (forward + backward): see train/train_fused.cu.
+struct QKNormRopeArgs {
+  const void* qkv;           // [T][(Hq + 2 Hkv) * D] bf16 GEMM output
+  const void* q_norm;        // [D] bf16 or null (no QK-norm)
+  const void* k_norm;
+  const void* cos;           // [S][D] bf16 rotary tables (halves duplicated)
+  const void* sin;
+  const int32_t* positions;  // [T] or null: position = t % S
+  void* q;                   // [T][Hq][D]  forward outputs
+  void* k;                   // [T][Hkv][D]
+  void* v;                   // [T][Hkv][D]
+  float* rstd_q;             // [T][Hq] saved for backward
+  float* rstd_k;             // [T][Hkv]
+  const void* dq;            // backward inputs [T][H][D]
+  const void* dk;
+  const void* dv;
+  void* dqkv;                // backward output, layout of qkv
+  float* dw_q;               // [D] fp32 weight-gradient accumulators (or null)
+  float* dw_k;
+  int T, S, Hq, Hkv, D;
+  float eps;
+};
+void rmsnorm_train_fwd_launch(const void* x, const void* w, void* y, float* rstd, int rows, int H, float eps,
+                              int device, cudaStream_t st);
+void rmsnorm_train_bwd_launch(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw,
+                              int rows, int H, int device, cudaStream_t st);
+void qk_norm_rope_fwd_launch(const QKNormRopeArgs& a, int device, cudaStream_t st);
+void qk_norm_rope_bwd_launch(const QKNormRopeArgs& a, int device, cudaStream_t st);
+void swiglu_train_fwd_launch(const void* gu, void* h, int64_t T, int I, int device, cudaStream_t st);
+void swiglu_train_bwd_launch(const void* dh, const void* gu, void* dgu, int64_t T, int I, int device,
+                             cudaStream_t st);
+void scale_by_launch(void* t, bool is_f32, int64_t n, const float* g, int device, cudaStream_t st);
+
 // Vocab-parallel greedy argmax over NVLink peer memory: see comm/tp_sample.cu.
 struct TpArgmaxArgs {
   const float* logits;                    // [R][ld] fp32, this rank's vocab shard

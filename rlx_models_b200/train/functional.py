@@ -66,6 +66,30 @@ def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return LinearFn.apply(x, w)
 
 
+class LinearResidualFn(torch.autograd.Function):
+    """y = residual + x @ w.T with the residual add in the GEMM epilogue; the
+    residual's gradient is the output gradient itself."""
+
+    @staticmethod
+    def forward(ctx, x, w, residual):
+        ctx.save_for_backward(x, w)
+        x2 = x.reshape(-1, x.shape[-1])
+        y = ops.matmul(x2, w.t(), static_b=False, residual=residual.reshape(-1, w.shape[0]).contiguous())
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, gy):
+        dx, dw = LinearFn.backward(ctx, gy)
+        return dx, dw, gy
+
+
+def linear_residual(x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+    """``residual + x @ w.T`` (one GEMM with the add fused on CUDA)."""
+    if _cuda(x):
+        return LinearResidualFn.apply(x, w, residual)
+    return residual + LinearFn.apply(x, w)
+
+
 class LMHeadCE(torch.autograd.Function):
     """Mean next-token cross-entropy of ``x @ w.T`` without materialising all
     logits: per chunk of rows, fp32 logits on the GEMM, one kernel for loss +
@@ -113,6 +137,14 @@ class LMHeadCE(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g):
         dx, dw = ctx.saved_tensors
+        if _cuda(dx):
+            # gradients were formed in forward: scale them in place by the incoming
+            # loss gradient, read on the device (the kernels return at once when it is 1)
+            gf = g.detach().float().reshape(1).contiguous()
+            ops._count(2)
+            ops.ext().scale_by(dx, gf)
+            ops.ext().scale_by(dw, gf)
+            return dx, dw, None, None, None
         return dx * g.to(dx.dtype), dw * g, None, None, None
 
 
@@ -120,11 +152,123 @@ def lm_head_ce(x, w, targets, chunk: int = 2048, denom: float | None = None):
     return LMHeadCE.apply(x, w, targets, chunk, denom)
 
 
-def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    """HF RMSNorm semantics (normalise in fp32, cast, scale)."""
+def _rmsnorm_ref(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     xf = x.float()
     y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
     return w * y.to(x.dtype)
+
+
+class RMSNormFn(torch.autograd.Function):
+    """RMSNorm on the training kernels (``csrc/train/train_fused.cu``): forward
+    saves the per-row rstd; backward gives dx and the fp32 weight gradient."""
+
+    @staticmethod
+    def forward(ctx, x, w, eps: float):
+        xc = x.contiguous()
+        y = torch.empty_like(xc)
+        rows = xc.numel() // xc.shape[-1]
+        rstd = torch.empty(rows, dtype=torch.float32, device=x.device)
+        ops._count(1)
+        ops.ext().rmsnorm_train_fwd(xc, w.contiguous(), y, rstd, float(eps))
+        ctx.save_for_backward(xc, w, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w, rstd = ctx.saved_tensors
+        dx = torch.empty_like(x)
+        dw = torch.zeros(w.shape, dtype=torch.float32, device=w.device)
+        ops._count(1)
+        ops.ext().rmsnorm_train_bwd(dy.contiguous(), x, w.contiguous(), rstd, dx, dw)
+        return dx, dw, None
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """HF RMSNorm semantics (normalise in fp32, cast, scale); this package's
+    kernels on CUDA for bf16 hidden sizes that are multiples of 2048."""
+    if _cuda(x) and x.dtype == torch.bfloat16 and x.shape[-1] % 2048 == 0 and x.shape[-1] <= 8192:
+        return RMSNormFn.apply(x, w, eps)
+    return _rmsnorm_ref(x, w, eps)
+
+
+class QKNormRopeFn(torch.autograd.Function):
+    """q|k|v GEMM output [B, S, (Hq + 2 Hkv) * D] -> per-head RMSNorm of q and k
+    (when norm weights are given) and rotary embedding, as q [B, S, Hq, D],
+    k / v [B, S, Hkv, D]; one kernel each way (``csrc/train/train_fused.cu``)."""
+
+    @staticmethod
+    def forward(ctx, qkv, qn, kn, cos, sin, Hq: int, Hkv: int, eps: float):
+        B, S, _ = qkv.shape
+        D = 128
+        qkv = qkv.contiguous()
+        dev = qkv.device
+        q = torch.empty(B, S, Hq, D, dtype=qkv.dtype, device=dev)
+        k = torch.empty(B, S, Hkv, D, dtype=qkv.dtype, device=dev)
+        v = torch.empty(B, S, Hkv, D, dtype=qkv.dtype, device=dev)
+        rq = torch.empty(B * S * Hq, dtype=torch.float32, device=dev)
+        rk = torch.empty(B * S * Hkv, dtype=torch.float32, device=dev)
+        ops._count(1)
+        ops.ext().qk_norm_rope_fwd(qkv, qn, kn, cos, sin, S, Hq, Hkv, float(eps), q, k, v, rq, rk)
+        empty = torch.empty(0, device=dev)
+        ctx.save_for_backward(qkv, qn if qn is not None else empty, kn if kn is not None else empty, cos, sin, rq, rk)
+        ctx.meta = (S, Hq, Hkv, qn is not None)
+        return q, k, v
+
+    @staticmethod
+    def backward(ctx, dq, dk, dv):
+        qkv, qn, kn, cos, sin, rq, rk = ctx.saved_tensors
+        S, Hq, Hkv, normed = ctx.meta
+        dqkv = torch.empty_like(qkv)
+        dwq = torch.zeros(128, dtype=torch.float32, device=qkv.device) if normed else None
+        dwk = torch.zeros(128, dtype=torch.float32, device=qkv.device) if normed else None
+        ops._count(1)
+        ops.ext().qk_norm_rope_bwd(qkv, qn if normed else None, kn if normed else None, cos, sin, S, Hq, Hkv, rq, rk,
+                                   dq.contiguous(), dk.contiguous(), dv.contiguous(), dqkv, dwq, dwk)
+        return dqkv, dwq, dwk, None, None, None, None, None
+
+
+def qk_norm_rope(qkv, qn, kn, cos, sin, Hq: int, Hkv: int, D: int, eps: float):
+    """Split the fused q|k|v projection, QK-norm (if ``qn``) and rotate; returns q, k, v [B, S, H, D]."""
+    B, S, _ = qkv.shape
+    if _cuda(qkv) and qkv.dtype == torch.bfloat16 and D == 128 and cos.shape[-1] == D:
+        return QKNormRopeFn.apply(qkv, qn, kn, cos.contiguous(), sin.contiguous(), Hq, Hkv, eps)
+    q, k, v = torch.split(qkv, [Hq * D, Hkv * D, Hkv * D], -1)
+    q = q.reshape(B, S, Hq, D)
+    k = k.reshape(B, S, Hkv, D)
+    v = v.reshape(B, S, Hkv, D)
+    if qn is not None:
+        q = _rmsnorm_ref(q, qn, eps)
+        k = _rmsnorm_ref(k, kn, eps)
+    return rope(q, cos, sin), rope(k, cos, sin), v
+
+
+class SwiGLUFn(torch.autograd.Function):
+    """[..., 2I] = [gate | up] -> silu(gate) * up, one kernel each way."""
+
+    @staticmethod
+    def forward(ctx, gu):
+        gu = gu.contiguous()
+        h = torch.empty(*gu.shape[:-1], gu.shape[-1] // 2, dtype=gu.dtype, device=gu.device)
+        ops._count(1)
+        ops.ext().swiglu_train_fwd(gu, h)
+        ctx.save_for_backward(gu)
+        return h
+
+    @staticmethod
+    def backward(ctx, dh):
+        (gu,) = ctx.saved_tensors
+        dgu = torch.empty_like(gu)
+        ops._count(1)
+        ops.ext().swiglu_train_bwd(dh.contiguous(), gu, dgu)
+        return dgu
+
+
+def swiglu(gu: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up over the [gate | up] halves of the last dimension."""
+    if _cuda(gu) and gu.dtype == torch.bfloat16 and (gu.shape[-1] // 2) % 8 == 0:
+        return SwiGLUFn.apply(gu)
+    g, u = gu.chunk(2, dim=-1)
+    return torch.nn.functional.silu(g) * u
 
 
 def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:

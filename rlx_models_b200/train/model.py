@@ -109,26 +109,20 @@ class TrainableDecoder:
         if self.lora is not None:
             lp = self.lora.params()
             lin = lambda t, x, w: self.lora.linear(lp, i, t, x, w)
+            lin_res = lambda t, x, w, r: r + lin(t, x, w)
         else:
             lin = lambda t, x, w: TF.linear(x, w)
+            lin_res = lambda t, x, w, r: TF.linear_residual(x, w, r)  # residual add in the GEMM epilogue
         a = TF.rmsnorm(h, ln1, c.rms_norm_eps)
         qkv = lin("qkv", a, wqkv)
-        q, k, v = torch.split(qkv, [c.q_size, c.kv_size, c.kv_size], -1)
-        q = q.reshape(B, S, c.num_attention_heads, c.head_dim)
-        k = k.reshape(B, S, c.num_key_value_heads, c.head_dim)
-        v = v.reshape(B, S, c.num_key_value_heads, c.head_dim)
-        if qn is not None:
-            q = TF.rmsnorm(q, qn, c.rms_norm_eps)
-            k = TF.rmsnorm(k, kn, c.rms_norm_eps)
         cos, sin = self.cos[:S], self.sin[:S]
-        q, k = TF.rope(q, cos, sin), TF.rope(k, cos, sin)
+        q, k, v = TF.qk_norm_rope(qkv, qn, kn, cos, sin, c.num_attention_heads, c.num_key_value_heads, c.head_dim,
+                                  c.rms_norm_eps)
         o = TF.attention(q, k, v, causal=True).reshape(B, S, c.q_size)
-        h = h + lin("o", o, wo)
+        h = lin_res("o", o, wo, h)
         m = TF.rmsnorm(h, ln2, c.rms_norm_eps)
         gu = lin("gate_up", m, wgu)
-        g, u = gu.chunk(2, dim=-1)
-        h = h + lin("down", F.silu(g) * u, wd)
-        return h
+        return lin_res("down", TF.swiglu(gu), wd, h)
 
     def loss(self, ids: torch.Tensor, targets: torch.Tensor, denom: float | None = None) -> torch.Tensor:
         """Summed CE over valid targets divided by ``denom`` (default: this
