@@ -336,6 +336,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const float inv = L > 0.f ? f / L : 0.f;
       const int t = tok0 + tok;
+      if (a.lse != nullptr && a.sinks == nullptr && row_ok && !a.q_paged)  // training: log2-sum-exp2 of the scaled row
+        a.lse[(int64_t)(q0 + t) * a.Hq + head] = L > 0.f ? m_used + __log2f(L) : -INFINITY;
       const int64_t orow = a.q_paged ? (int64_t)btab[min(t >> 4, max_page - 1)] * 16 + (t & 15) : (int64_t)(q0 + t);
       __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) +
                            orow * (a.out_ld ? a.out_ld : (int64_t)a.Hq * kD) + (int64_t)head * kD;

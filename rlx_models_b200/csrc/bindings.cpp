@@ -1178,6 +1178,61 @@ void swiglu_train_bwd(const Tensor& dh, const Tensor& gu, Tensor& dgu) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Causal training attention over dense [B * S, H, D] rows: forward on the tcgen05
+// kernel with the per-row log2-sum-exp2 saved, backward in train/attn_bwd.cu.
+void attn_train_fwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& block_tables,
+                    const Tensor& ctx_lens, const Tensor& cu_q, int64_t S, double scale, Tensor& out, Tensor& lse,
+                    Tensor& status) {
+  c10::cuda::CUDAGuard g(q.device());
+  auto a = attn_args(q, k, v, block_tables, ctx_lens, out, c10::nullopt, 0, scale, status);
+  TORCH_CHECK(k.dim() == 3 && lse.scalar_type() == at::kFloat && lse.numel() == q.size(0) * q.size(1),
+              "b200.attn_train_fwd: dense k/v [T, Hkv, D], fp32 lse [T, Hq]");
+  a.cu_q = cu_q.data_ptr<int32_t>();
+  a.max_q_len = (int)S;
+  a.causal = 1;
+  a.q_rows = q.size(0);
+  a.kv_dense = 1;
+  a.kv_rows = k.size(0);
+  a.lse = lse.data_ptr<float>();
+  TORCH_CHECK(b200::fmha_supported(a), "b200.attn_train_fwd: needs the tcgen05 attention (head_dim 128, G <= 8)");
+  b200::prefill_attention_launch(a, cur_stream(q));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void attn_train_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& dout,
+                    const Tensor& lse, Tensor& delta, Tensor& dq_acc, Tensor& dq, Tensor& dk, Tensor& dv, int64_t B,
+                    int64_t S, double scale) {
+  for (const Tensor* t : std::initializer_list<const Tensor*>{&q, &k, &v, &o, &dout, &dq, &dk, &dv})
+    check_bf16_contig(*t, "attention tensor");
+  TORCH_CHECK(q.dim() == 3 && q.size(2) == 128 && k.size(2) == 128 && q.size(0) == B * S && k.size(0) == B * S &&
+                  o.sizes() == q.sizes() && dout.sizes() == q.sizes() && dq.sizes() == q.sizes() &&
+                  dk.sizes() == k.sizes() && dv.sizes() == k.sizes(),
+              "b200.attn_train_bwd: shapes");
+  TORCH_CHECK(lse.numel() == q.size(0) * q.size(1) && delta.numel() == lse.numel() &&
+                  dq_acc.numel() == q.numel() && dq_acc.scalar_type() == at::kFloat,
+              "b200.attn_train_bwd: fp32 lse / delta / dq accumulator");
+  c10::cuda::CUDAGuard g(q.device());
+  b200::AttnBwdArgs a{};
+  a.q = q.data_ptr();
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.o = o.data_ptr();
+  a.dout = dout.data_ptr();
+  a.lse = lse.data_ptr<float>();
+  a.delta = delta.data_ptr<float>();
+  a.dq_acc = dq_acc.data_ptr<float>();
+  a.dq = dq.data_ptr();
+  a.dk = dk.data_ptr();
+  a.dv = dv.data_ptr();
+  a.B = (int)B;
+  a.S = (int)S;
+  a.Hq = (int)q.size(1);
+  a.Hkv = (int)k.size(1);
+  a.scale = (float)scale;
+  b200::attn_bwd_launch(a, q.get_device(), cur_stream(q));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void scale_by(Tensor& t, const Tensor& g) {
   check_cuda(t, "t");
   TORCH_CHECK(t.is_contiguous() && (t.scalar_type() == at::kFloat || t.scalar_type() == at::kBFloat16) &&
@@ -1444,6 +1499,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_train_fwd", &swiglu_train_fwd);
   m.def("swiglu_train_bwd", &swiglu_train_bwd);
   m.def("scale_by", &scale_by);
+  m.def("attn_train_fwd", &attn_train_fwd);
+  m.def("attn_train_bwd", &attn_train_bwd);
   m.def("sample", &sample);
   m.def("symm_malloc", &symm_malloc);
   m.def("symm_free", &symm_free);

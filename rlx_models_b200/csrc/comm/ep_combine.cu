@@ -65,7 +65,7 @@ __global__ void ep_combine_norm_kernel(EpCombineArgs a) {
       const int q = ex / a.e_local;
       const uint4* row = nullptr;
       if (ex >= 0 && q < a.world) {
-        const int pos = __ldcv(a.peer_inv[q] + (int64_t)t * a.k + s);  // peer memory: no stale L1 lines
+        const int pos = __ldcg(a.peer_inv[q] + (int64_t)t * a.k + s);  // peer memory through L2 only
         if (pos >= 0)
           row = reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.peer_rows[q]) +
                                                (int64_t)pos * H);
@@ -84,7 +84,7 @@ __global__ void ep_combine_norm_kernel(EpCombineArgs a) {
       uint4 rv[kMaxK];
 #pragma unroll
       for (int s = 0; s < kMaxK; ++s)  // issue every slot's load before summing
-        if (s < a.k && s_row[s] != nullptr) rv[s] = __ldcv(s_row[s] + vi);
+        if (s < a.k && s_row[s] != nullptr) rv[s] = __ldcg(s_row[s] + vi);
 #pragma unroll
       for (int s = 0; s < kMaxK; ++s) {
         if (s >= a.k || s_row[s] == nullptr) continue;

@@ -288,6 +288,33 @@ namespace tpc {
 // this op's barrier, hence finished the previous op), so the next GEMM can
 // accumulate into it. One barrier per op; no NCCL call.
 constexpr int kPullThreads = 256;
+constexpr int kMaxWorld = 8;
+
+// s[0..8) = sum over the world ranks of the 8 fp32 values at element offset
+// `off` of each rank's partial (peer memory). Every rank's two 16-byte loads
+// are issued before any is consumed, so the NVLink round trips overlap
+// instead of running one after another. Plain L2 (.cg) loads: the data was
+// published before the flag this kernel acquired, and is never cached in L1.
+__device__ __forceinline__ void sum_peer_rows(const float* const* peer, int world, int64_t off, float (&s)[8]) {
+  float4 x[kMaxWorld][2];
+#pragma unroll
+  for (int q = 0; q < kMaxWorld; ++q) {
+    if (q < world) {
+      const float4* src = reinterpret_cast<const float4*>(peer[q] + off);
+      x[q][0] = __ldcg(src);
+      x[q][1] = __ldcg(src + 1);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < 8; ++k) s[k] = 0.f;
+#pragma unroll
+  for (int q = 0; q < kMaxWorld; ++q) {
+    if (q < world) {
+      s[0] += x[q][0].x; s[1] += x[q][0].y; s[2] += x[q][0].z; s[3] += x[q][0].w;
+      s[4] += x[q][1].x; s[5] += x[q][1].y; s[6] += x[q][1].z; s[7] += x[q][1].w;
+    }
+  }
+}
 
 __global__ void __launch_bounds__(kPullThreads) ar_pull_norm_kernel(PullNormArgs a) {
   __shared__ float red[kPullThreads / 32];
@@ -312,13 +339,8 @@ __global__ void __launch_bounds__(kPullThreads) ar_pull_norm_kernel(PullNormArgs
     for (int c = 0; c < kMaxChunks; ++c) {
       if (c >= nch) break;
       const int col = (c * kPullThreads + threadIdx.x) * 8;
-      float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int q = 0; q < a.world; ++q) {
-        const float4* src = reinterpret_cast<const float4*>(a.peer_acc[q] + (int64_t)r * H + col);
-        const float4 x0 = __ldcv(src), x1 = __ldcv(src + 1);  // peer memory: bypass stale cache lines
-        s[0] += x0.x; s[1] += x0.y; s[2] += x0.z; s[3] += x0.w;
-        s[4] += x1.x; s[5] += x1.y; s[6] += x1.z; s[7] += x1.w;
-      }
+      float s[8];
+      sum_peer_rows(a.peer_acc, a.world, (int64_t)r * H + col, s);
       const uint4 hv = *reinterpret_cast<const uint4*>(hbuf + (int64_t)r * H + col);
       const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
       uint32_t o[4];
@@ -374,6 +396,7 @@ __global__ void __launch_bounds__(kPullThreads) ar_pull_norm_kernel(PullNormArgs
 }  // namespace tpc
 
 void ar_pull_norm_launch(const PullNormArgs& a, cudaStream_t st) {
+  if (a.world > tpc::kMaxWorld) throw std::runtime_error("b200.ar_pull_norm: at most 8 ranks");
   if (a.H % (tpc::kPullThreads * 8) != 0 || a.H > tpc::kPullThreads * 8 * 4)
     throw std::runtime_error("b200.ar_pull_norm: hidden must be a multiple of 2048 and <= 8192");
   launch_pdl(tpc::ar_pull_norm_kernel, dim3(std::max(std::max(1, a.M), a.zero_rows)), dim3(tpc::kPullThreads), 0,
@@ -427,13 +450,8 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
     for (int c = 0; c < kMaxChunks; ++c) {
       if (c >= nch) break;
       const int col = (c * kPullThreads + threadIdx.x) * 8;
-      float sm[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int q = 0; q < a.world; ++q) {
-        const float4* src = reinterpret_cast<const float4*>(a.peer_acc[q] + (int64_t)r * H + col);
-        const float4 x0 = __ldcv(src), x1 = __ldcv(src + 1);
-        sm[0] += x0.x; sm[1] += x0.y; sm[2] += x0.z; sm[3] += x0.w;
-        sm[4] += x1.x; sm[5] += x1.y; sm[6] += x1.z; sm[7] += x1.w;
-      }
+      float sm[8];
+      sum_peer_rows(a.peer_acc, a.world, (int64_t)r * H + col, sm);
       const uint4 hv = *reinterpret_cast<const uint4*>(hbuf + (int64_t)r * H + col);
       const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
       uint32_t o[4];
@@ -494,9 +512,23 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
         reinterpret_cast<const __nv_bfloat16*>(a.peer_res[owner]) + ((int64_t)a.rpr_max + j) * H);
     uint4* dh = reinterpret_cast<uint4*>(hbuf + (int64_t)i * H);
     uint4* dout = reinterpret_cast<uint4*>(out + (int64_t)i * H);
-    for (int c = threadIdx.x; c < H / 8; c += kPullThreads) {
-      dh[c] = __ldcv(sh + c);
-      dout[c] = __ldcv(so + c);
+    constexpr int kMaxIt = 4;  // H <= 256 * 8 * 4: every load of the row is issued before any store
+    uint4 vh[kMaxIt], vo[kMaxIt];
+#pragma unroll
+    for (int it = 0; it < kMaxIt; ++it) {
+      const int c = it * kPullThreads + threadIdx.x;
+      if (c < H / 8) {
+        vh[it] = __ldcg(sh + c);
+        vo[it] = __ldcg(so + c);
+      }
+    }
+#pragma unroll
+    for (int it = 0; it < kMaxIt; ++it) {
+      const int c = it * kPullThreads + threadIdx.x;
+      if (c < H / 8) {
+        dh[c] = vh[it];
+        dout[c] = vo[it];
+      }
     }
   }
   if (i < a.zero_rows) {
@@ -517,6 +549,7 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
 }  // namespace tpc
 
 void ar2_norm_launch(const TwoShotNormArgs& a, cudaStream_t st) {
+  if (a.world > tpc::kMaxWorld) throw std::runtime_error("b200.ar2_norm: at most 8 ranks");
   if (a.H % (tpc::kPullThreads * 8) != 0 || a.H > tpc::kPullThreads * 8 * 4)
     throw std::runtime_error("b200.ar2_norm: hidden must be a multiple of 2048 and <= 8192");
   if (a.rpr <= 0 || a.rpr > a.rpr_max || (int64_t)a.rpr * a.world < a.M)

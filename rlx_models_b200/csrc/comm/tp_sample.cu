@@ -69,11 +69,13 @@ __global__ void __launch_bounds__(kThreads) tp_argmax_kernel(TpArgmaxArgs a) {
   if (threadIdx.x < (unsigned)a.world) wait_flag_geq(a.flags + threadIdx.x, e, a.status, 600 + threadIdx.x);
   __syncthreads();
   if (threadIdx.x == 0) {
-    unsigned long long b = 0ull;
-    for (int q = 0; q < a.world; ++q) {
-      const unsigned long long k = __ldcv(a.peer_pairs[q] + (int64_t)par * a.max_rows + row);
-      b = k > b ? k : b;
-    }
+    unsigned long long kq[8], b = 0ull;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)  // every rank's key requested before any is compared
+      if (q < a.world) kq[q] = __ldcg(a.peer_pairs[q] + (int64_t)par * a.max_rows + row);
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (q < a.world) b = kq[q] > b ? kq[q] : b;
     a.out[row] = (int32_t)(0xFFFFFFFFu - (uint32_t)(b & 0xFFFFFFFFull));
     __threadfence();
     // the last CTA to finish resets the arrival counter and publishes the epoch
@@ -91,6 +93,7 @@ __global__ void __launch_bounds__(kThreads) tp_argmax_kernel(TpArgmaxArgs a) {
 void tp_argmax_launch(const TpArgmaxArgs& a, cudaStream_t st) {
   if (a.R <= 0) return;
   if (a.R > a.max_rows) throw std::runtime_error("b200.tp_argmax: more rows than the pair buffers hold");
+  if (a.world > 8) throw std::runtime_error("b200.tp_argmax: at most 8 ranks");
   launch_pdl(tps::tp_argmax_kernel, dim3((unsigned)a.R), dim3(tps::kThreads), 0, st, a);
 }
 

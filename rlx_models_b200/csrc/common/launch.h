@@ -294,6 +294,8 @@ struct AttnArgs {
   int64_t q_rows = 0;        // prefill: rows of q (bounds of its TMA map)
   int kv_dense = 0;          // prefill: k/v row-major [kv_rows, Hkv, D] (pages = 16 consecutive rows)
   int64_t kv_rows = 0;
+  float* lse = nullptr;      // prefill (tcgen05 kernel, no sinks): per (row, head) log2-sum-exp2 of the
+                             // scaled scores, [q_rows][Hq], for the attention backward
   float* ws;                 // decode split workspace
   int64_t ws_elems;
   int* status;
@@ -305,6 +307,25 @@ void prefill_attention_launch(const AttnArgs& a, cudaStream_t st);
 // prefill_attention_launch when supported (B200_ATTN_LEGACY=1 forces the mma.sync kernel)
 bool fmha_supported(const AttnArgs& a);
 void fmha_launch(const AttnArgs& a, cudaStream_t st);
+
+// Attention backward for training (causal, dense [T, H, D] rows, head_dim 128):
+// see train/attn_bwd.cu.
+struct AttnBwdArgs {
+  const void* q;      // [T][Hq][D] bf16
+  const void* k;      // [T][Hkv][D]
+  const void* v;
+  const void* o;      // forward output [T][Hq][D]
+  const void* dout;   // [T][Hq][D]
+  const float* lse;   // [T][Hq] log2 units (forward)
+  float* delta;       // [T][Hq] scratch: rowsum(dO * O)
+  float* dq_acc;      // [T][Hq][D] fp32 scratch (zeroed by the prep kernel)
+  void* dq;           // [T][Hq][D] bf16
+  void* dk;           // [T][Hkv][D]
+  void* dv;
+  int B, S, Hq, Hkv;
+  float scale;
+};
+void attn_bwd_launch(const AttnBwdArgs& a, int device, cudaStream_t st);
 
 // ---------------- linear attention (Gated DeltaNet) ----------------
 struct GdnDecodeArgs {

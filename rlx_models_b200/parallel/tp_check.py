@@ -137,7 +137,8 @@ def main():
     ok_all = True
     kinds = [("nccl", {}), ("fused", {}), ("pull", {"two_shot": "off"}), ("pull", {"two_shot": "on"})]
     for kind, kw in kinds:
-        comm = make_tp_comm(kind, rank, world, dev, cfg.rms_norm_eps, max_tokens=512, hidden=cfg.hidden_size, **kw)
+        comm = make_tp_comm(kind, rank, world, dev, cfg.rms_norm_eps, max_tokens=2048, hidden=cfg.hidden_size,
+                             **kw)
         name = kind + ("" if not kw else ("-two-shot" if kw["two_shot"] == "on" else "-one-shot"))
         m = DecoderLM(cfg, w, device=dev, tp_rank=rank, tp_size=world, comm=comm)
         lg_local = m.forward(fb(), m.make_kv_cache(nb))

@@ -71,14 +71,39 @@ class FlatGroup:
         self.frozen = False  # frozen groups are gathered without autograd (no weight gradients)
         self.push_table = None  # GradPush: int64 [world] device addresses of every rank's grad shard
         self.gathered = (0, 0)  # [start, end) byte range of the live gathered bf16 params
+        self._prefetched = None  # (full params, event) of an all-gather started by prefetch()
 
     # -- collective helpers ---------------------------------------------------
     def _gloo(self) -> bool:
         return self.device.type == "cpu"
 
+    def prefetch(self):
+        """Start this group's parameter all-gather on the communication stream,
+        so it overlaps the compute queued after this call (the layer before it
+        in forward, or after it in the backward recompute); ``all_gather``
+        then waits for it instead of issuing its own."""
+        if self.world == 1 or self._gloo() or self._prefetched is not None:
+            return
+        cur = torch.cuda.current_stream(self.device)
+        s = _comm_stream(self.device)
+        s.wait_stream(cur)  # the shard is final (optimizer of the previous step done)
+        with torch.cuda.stream(s):
+            full = torch.empty(self.padded, dtype=self.param.dtype, device=self.device)
+            dist.all_gather_into_tensor(full, self.param, group=self.group)
+            ev = torch.cuda.Event()
+            ev.record(s)
+        self._prefetched = (full, ev)
+
     def all_gather(self) -> torch.Tensor:
         if self.world == 1:
             return self.param
+        if self._prefetched is not None:
+            full, ev = self._prefetched
+            self._prefetched = None
+            cur = torch.cuda.current_stream(self.device)
+            cur.wait_event(ev)
+            full.record_stream(cur)
+            return full
         if self._gloo():  # CPU test path (gloo has no *_into_tensor collectives)
             parts = [torch.empty_like(self.param) for _ in range(self.world)]
             dist.all_gather(parts, self.param, group=self.group)
@@ -117,6 +142,16 @@ class FlatGroup:
     def named_full(self) -> dict[str, torch.Tensor]:
         full = self.full_fp32()
         return {n: full[o:o + k].view(s) for n, o, k, s in zip(self.names, self.offsets, self.numels, self.shapes)}
+
+
+_COMM_STREAMS: dict = {}
+
+
+def _comm_stream(device: torch.device) -> "torch.cuda.Stream":
+    s = _COMM_STREAMS.get(device)
+    if s is None:
+        s = _COMM_STREAMS[device] = torch.cuda.Stream(device)
+    return s
 
 
 class GradPush:

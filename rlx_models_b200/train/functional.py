@@ -11,6 +11,8 @@ external autodiff crate; here autograd drives our kernels.
 """
 from __future__ import annotations
 
+import math
+
 import torch
 
 from .. import ops
@@ -282,8 +284,74 @@ def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
     return x * cos[None, :, None, :] + rot * sin[None, :, None, :]
 
 
+_ATTN_META: dict = {}
+
+
+def _attn_meta(B: int, S: int, dev):
+    """Block tables / lengths / query offsets that view dense [B * S, H, D] K/V
+    rows as 16-row pages of B sequences, for the tcgen05 attention kernel."""
+    key = (B, S, dev)
+    m = _ATTN_META.get(key)
+    if m is None:
+        nb = S // 16
+        tables = (torch.arange(B, dtype=torch.int32)[:, None] * nb + torch.arange(nb, dtype=torch.int32)[None, :])
+        m = _ATTN_META[key] = (tables.to(dev).contiguous(), torch.full((B,), S, dtype=torch.int32, device=dev),
+                               (torch.arange(B + 1, dtype=torch.int32) * S).to(dev))
+    return m
+
+
+class AttentionFn(torch.autograd.Function):
+    """Causal GQA attention on this package's kernels: the tcgen05 forward (it
+    also saves each row's log-sum-exp) and the flash-style backward
+    (``csrc/train/attn_bwd.cu``). q [B, S, Hq, 128], k / v [B, S, Hkv, 128]."""
+
+    @staticmethod
+    def forward(ctx, q, k, v):
+        B, S, Hq, D = q.shape
+        Hkv = k.shape[2]
+        q3 = q.reshape(B * S, Hq, D).contiguous()
+        k3 = k.reshape(B * S, Hkv, D).contiguous()
+        v3 = v.reshape(B * S, Hkv, D).contiguous()
+        out = torch.empty_like(q3)
+        lse = torch.empty(B * S, Hq, dtype=torch.float32, device=q.device)
+        tables, lens, cu = _attn_meta(B, S, q.device)
+        scale = 1.0 / math.sqrt(D)
+        s = ops.scratch(q.device)
+        ops._count(1)
+        ops.ext().attn_train_fwd(q3, k3, v3, tables, lens, cu, S, scale, out, lse, s.status)
+        ctx.save_for_backward(q3, k3, v3, out, lse)
+        ctx.meta = (B, S, scale)
+        return out.view(B, S, Hq, D)
+
+    @staticmethod
+    def backward(ctx, do):
+        q3, k3, v3, out, lse = ctx.saved_tensors
+        B, S, scale = ctx.meta
+        dq = torch.empty_like(q3)
+        dk = torch.empty_like(k3)
+        dv = torch.empty_like(v3)
+        delta = torch.empty_like(lse)
+        dq_acc = torch.empty(q3.shape, dtype=torch.float32, device=q3.device)
+        ops._count(3)
+        ops.ext().attn_train_bwd(q3, k3, v3, out, do.reshape(q3.shape).contiguous(), lse, delta, dq_acc, dq, dk, dv,
+                                 B, S, scale)
+        shp_q, shp_k = (B, S) + tuple(q3.shape[1:]), (B, S) + tuple(k3.shape[1:])
+        return dq.view(shp_q), dk.view(shp_k), dv.view(shp_k)
+
+
+def _kernel_attention_ok(q, k) -> bool:
+    B, S, Hq, D = q.shape
+    G = Hq // k.shape[2]
+    return (q.is_cuda and q.dtype == torch.bfloat16 and D == 128 and S % 64 == 0 and Hq % k.shape[2] == 0
+            and G <= 8 and (G & (G - 1)) == 0)
+
+
 def attention(q, k, v, causal: bool = True):
-    """q [B, S, Hq, D], k/v [B, S, Hkv, D] -> [B, S, Hq, D] (GQA)."""
+    """q [B, S, Hq, D], k/v [B, S, Hkv, D] -> [B, S, Hq, D] (GQA). On CUDA,
+    causal attention with head_dim 128 and S a multiple of 64 runs on this
+    package's forward / backward kernels."""
+    if causal and _kernel_attention_ok(q, k):
+        return AttentionFn.apply(q, k, v)
     qt, kt, vt = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
     if not q.is_cuda:
         g = q.shape[2] // k.shape[2]

@@ -94,9 +94,18 @@ class TrainableDecoder:
     def num_params(self) -> int:
         return sum(g.numel for g in self.groups)
 
+    def _prefetch_next(self, i: int):
+        """Overlap the next layer's parameter all-gather with this layer: i + 1
+        in forward order, i - 1 in the backward recompute (descending order)."""
+        last, self._last_layer = getattr(self, "_last_layer", None), i
+        nxt = i - 1 if (last is not None and last == i + 1) else i + 1
+        if 0 <= nxt < len(self.layers) and not self.layers[nxt].frozen:
+            self.layers[nxt].prefetch()
+
     def _layer(self, h: torch.Tensor, i: int) -> torch.Tensor:
         c = self.cfg
         w = gather_params(self.layers[i])
+        self._prefetch_next(i)
         if c.qk_norm:
             ln1, wqkv, qn, kn, wo, ln2, wgu, wd = w
         else:
