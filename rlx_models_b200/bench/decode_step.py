@@ -7,6 +7,14 @@ times ``iters`` replays of the captured decode graph with CUDA events (device
 time per step), and reports the weight + KV bytes per step and the achieved
 fraction of measured HBM bandwidth. With ``--replays N`` it only replays N
 times (for an ncu launch list of one step).
+
+``--tp-emulate N`` builds rank 0 of an N-way tensor-parallel model on this one
+GPU with no communicator (every row-parallel reduction is local): the step
+then times exactly the compute a TP=N rank does per decode step (its weight
+and KV shards, its kernels and launches), so a multi-GPU step time minus this
+one is the cost of the collectives. ``--breakdown K`` adds a per-kernel table
+of K eager steps (torch profiler; run with B200_PDL=0 so kernel durations do
+not include waiting for their predecessor).
 """
 from __future__ import annotations
 
@@ -24,6 +32,8 @@ def main():
     ap.add_argument("--ctx", type=int, default=1400)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--replays", type=int, default=0)
+    ap.add_argument("--tp-emulate", type=int, default=1)
+    ap.add_argument("--breakdown", type=int, default=0)
     args = ap.parse_args()
     from .. import ops
     from ..api import load
@@ -36,7 +46,8 @@ def main():
     cfg = preset(args.model)
     ecfg = EngineConfig(max_num_seqs=max(64, args.batch), max_batched_tokens=8192, max_model_len=args.ctx + 64,
                         kv_memory_gb=40, prefix_caching=False)
-    llm = load(args.model, device=dev, engine_config=ecfg, config=cfg)
+    tp = args.tp_emulate
+    llm = load(args.model, device=dev, engine_config=ecfg, config=cfg, tp_rank=0, tp_size=tp, comm=None)
     eng = llm.engine
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, cfg.vocab_size, (args.ctx,), generator=g).tolist() for _ in range(args.batch)]
@@ -69,12 +80,26 @@ def main():
     torch.cuda.synchronize(dev)
     ms = ev[0].elapsed_time(ev[1]) / args.iters
     ops.check_errors(dev)
+    breakdown = None
+    if args.breakdown:
+        import dataclasses
+        from ..utils.trace import profile
+        eng.cfg = dataclasses.replace(eng.cfg, cuda_graphs=False)
+        breakdown = profile(eng.step, steps=args.breakdown, warmup=1, top=16)
     nparam = cfg.num_params()
-    wbytes = 2 * nparam - (2 * cfg.vocab_size * cfg.hidden_size)  # embedding rows are gathered, not streamed
-    kv_bytes = 2 * 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_dim * args.batch * (args.ctx + 1)
+    wbytes = (2 * nparam - (2 * cfg.vocab_size * cfg.hidden_size)) / tp  # embedding rows are gathered
+    kv_bytes = 2 * 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_dim * args.batch * (args.ctx + 1) / tp
     hbm, _, src = peaks()
     ach = (wbytes + kv_bytes) / (ms * 1e-3) / 1e12
-    print(json.dumps({"model": args.model, "batch": key[0], "ctx": args.ctx, "ms_per_step": round(ms, 3),
+    if breakdown is not None:
+        for r in breakdown:
+            r["us_per_step"] = round(r["device_us_total"] / args.breakdown, 1)
+            r["calls_per_step"] = r["calls"] // args.breakdown
+            r["name"] = r["name"][:80]
+            for k in ("device_us_total", "calls"):
+                r.pop(k)
+    print(json.dumps({"model": args.model, "tp_emulate": tp, "breakdown": breakdown,
+                      "batch": key[0], "ctx": args.ctx, "ms_per_step": round(ms, 3),
                       "launches_per_step": n_launch, "weight_gb": round(wbytes / 1e9, 2),
                       "kv_gb": round(kv_bytes / 1e9, 2), "achieved_tbs": round(ach, 2),
                       "frac_hbm": round(ach / hbm, 3), "peak_source": src}))
