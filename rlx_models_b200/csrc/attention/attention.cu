@@ -19,6 +19,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <stdexcept>
 
 #include "../common/b200.cuh"
@@ -79,7 +80,7 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
     last_page = a.max_blocks;
   }
   const int npages = max(0, last_page - first_page);
-  const int pps = (npages + nsplit - 1) / nsplit;
+  const int pps = a.chunk_pages > 0 ? a.chunk_pages : (npages + nsplit - 1) / nsplit;
   const int p0 = first_page + split * pps;
   const int p1 = min(last_page, p0 + pps);
   const int my_pages = max(0, p1 - p0);
@@ -563,12 +564,21 @@ int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
   CUtensorMap tv = make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
   int splits = a.splits;
   const int sms = num_sms(a.device);
+  AttnArgs args = a;
   if (splits <= 0) {
-    const int ctas = a.B * a.Hkv;
-    // split the KV range only when (sequence, kv-head) pairs leave SMs idle: measured on B200 at Hkv 8,
-    // ctx 1400, one split beats two at 256 pairs (42.4 vs 48.3 us) and at 512 (79.4 vs 90.8 us)
-    splits = std::max(1, std::min(16, (3 * sms + ctas - 1) / ctas));
-    if (ctas >= sms) splits = 1;
+    // Fixed-size chunks instead of equal parts: a CTA per (sequence, kv head, chunk of pages), so
+    // long sequences become several CTAs of the same size as everyone else's and the last wave
+    // is short (equal parts keep the longest sequence's CTA as long as its whole context). The
+    // chunk shrinks as (sequence, kv-head) pairs get fewer than the ~3 resident CTAs per SM, so
+    // small batches / high tensor parallelism still fill the machine. Chunks past a sequence's end
+    // exit at once; the merge kernel skips their empty partials.
+    const int pairs = a.B * a.Hkv, slots = 3 * sms;
+    int chunk = pairs >= slots ? 32 : pairs * 2 >= slots ? 16 : pairs * 4 >= slots ? 8 : 4;
+    if (const char* e = std::getenv("B200_DECODE_CHUNK")) chunk = std::max(1, std::atoi(e));
+    while (chunk < a.max_blocks && (int64_t)a.B * a.Hq * ((a.max_blocks + chunk - 1) / chunk) * (a.D + 2) > a.ws_elems)
+      chunk *= 2;
+    splits = (a.max_blocks + chunk - 1) / chunk;
+    args.chunk_pages = splits > 1 ? chunk : 0;
   }
   if (splits > 1 && a.ws_elems < (int64_t)a.B * a.Hq * splits * (a.D + 2))
     throw std::runtime_error("b200.decode_attention: split workspace too small");
@@ -577,20 +587,20 @@ int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
     constexpr int NST = 4;
     auto k = decode_attn_kernel<256, NST>;
     ensure_smem(k, DecCfg<256, NST>::SMEM);
-    launch_pdl(k, grid, dim3(160), DecCfg<256, NST>::SMEM, st, tk, tv, a);
-    if (splits > 1) launch_pdl(decode_merge_kernel<256>, dim3(a.B * a.Hq), dim3(256), 0, st, a, splits);
+    launch_pdl(k, grid, dim3(160), DecCfg<256, NST>::SMEM, st, tk, tv, args);
+    if (splits > 1) launch_pdl(decode_merge_kernel<256>, dim3(a.B * a.Hq), dim3(256), 0, st, args, splits);
   } else if (a.D == 128) {
     constexpr int NST = 8;
     auto k = decode_attn_kernel<128, NST>;
     ensure_smem(k, DecCfg<128, NST>::SMEM);
-    launch_pdl(k, grid, dim3(160), DecCfg<128, NST>::SMEM, st, tk, tv, a);
-    if (splits > 1) launch_pdl(decode_merge_kernel<128>, dim3(a.B * a.Hq), dim3(128), 0, st, a, splits);
+    launch_pdl(k, grid, dim3(160), DecCfg<128, NST>::SMEM, st, tk, tv, args);
+    if (splits > 1) launch_pdl(decode_merge_kernel<128>, dim3(a.B * a.Hq), dim3(128), 0, st, args, splits);
   } else {
     constexpr int NST = 8;
     auto k = decode_attn_kernel<64, NST>;
     ensure_smem(k, DecCfg<64, NST>::SMEM);
-    launch_pdl(k, grid, dim3(160), DecCfg<64, NST>::SMEM, st, tk, tv, a);
-    if (splits > 1) launch_pdl(decode_merge_kernel<64>, dim3(a.B * a.Hq), dim3(64), 0, st, a, splits);
+    launch_pdl(k, grid, dim3(160), DecCfg<64, NST>::SMEM, st, tk, tv, args);
+    if (splits > 1) launch_pdl(decode_merge_kernel<64>, dim3(a.B * a.Hq), dim3(64), 0, st, args, splits);
   }
   return splits > 1 ? 2 : 1;
 }

@@ -288,6 +288,9 @@ struct AttnArgs {
   float softcap = 0.f;       // > 0: scores = softcap * tanh(scale * q.k / softcap) (Gemma-2)
   int max_q_len;             // prefill: max query length per sequence
   int splits;                // decode: KV splits (0 = auto)
+  int chunk_pages = 0;       // decode: > 0 cuts every sequence's pages into chunks of this many pages
+                             // (split s takes chunk s; empty chunks write an empty partial), 0 = splits
+                             // equal parts of each sequence
   int causal = 1;            // prefill: 0 = every query sees the whole context (DiT joint attention)
   int q_paged = 0;           // prefill: query / output row of token t = block_tables[b][t / 16] * 16 + t % 16
   int64_t out_ld = 0;        // prefill: output row stride in elements (0 = Hq * D)

@@ -20,6 +20,71 @@ import torch
 import torch.distributed as dist
 
 
+def _graph_us(fn, iters, dev):
+    """Device time per call of ``fn`` replayed ``iters`` times in one CUDA graph (max over ranks)."""
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(iters):
+            fn()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    t = torch.tensor([e0.elapsed_time(e1) / iters * 1e3], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    del g
+    return round(float(t), 2)
+
+
+def kernel_breakdown(args, rank, world, dev, x, w, nw, M, H):
+    """Decode row-parallel op split into its kernels, each graph-timed alone:
+    the local accumulate GEMM, the one-shot and two-shot reduction kernels
+    (their accumulator already filled), and a bare cross-rank flag barrier."""
+    from .. import ops
+    from ..ops._ext import ext, scratch
+    from .pull_tp import PullTPComm
+    out = {}
+    comm = PullTPComm(rank, world, dev, 1e-6, hidden=H, two_shot="off")
+    h = torch.zeros(M, H, device=dev, dtype=torch.bfloat16)
+    o = torch.empty_like(h)
+    s = scratch(dev)
+    out["gemm_acc"] = _graph_us(lambda: ops.linear_acc(x, w, acc=comm.acc[0, :M]), args.iters, dev)
+
+    def pull():
+        ext().ar_pull_norm(comm.peer_acc[0], comm.peer_flags, comm.flags, comm.acc[1], comm.ROWS, h, nw, o,
+                           comm.ctr[0:1], comm.ctr[1:2], rank, world, 1e-6, s.status)
+
+    def two_shot():
+        rpr = (M + world - 1) // world
+        ext().ar2_norm(comm.peer_acc[0], comm.peer_res, comm.res, comm.peer_flags2, comm.flags2, comm.acc[1],
+                       comm.ROWS, h, nw, o, comm.ctr2[0:1], comm.ctr2[1:3], rank, world, rpr, comm.rpr_max, 1e-6,
+                       s.status)
+
+    out["ar_pull_norm"] = _graph_us(pull, args.iters, dev)
+    out["ar2_norm"] = _graph_us(two_shot, args.iters, dev)
+    from ..train.fsdp import FlatGroup, GradPush
+    fg = FlatGroup("b", [("t", torch.zeros(1024))], rank, world, dev)
+    gp = GradPush([fg], rank, world, dev)
+    out["flag_barrier"] = _graph_us(gp.barrier, args.iters, dev)
+    logits = torch.randn(64, 151936 // world, device=dev)
+    picked = torch.empty(64, dtype=torch.int32, device=dev)
+    out["greedy_argmax_v19k_r64"] = _graph_us(lambda: comm.argmax(logits, picked), args.iters, dev)
+    ops.check_errors(dev)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    gp.close()
+    comm.close()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--M", type=int, default=64)
@@ -92,6 +157,8 @@ def main():
         dist.barrier()
         if hasattr(comm, "close"):
             comm.close()
+    if M <= 128:
+        res["pull_kernels_us"] = kernel_breakdown(args, rank, world, dev, x, w, nw, M, H)
     # per-kernel breakdown of the fused op (eager, events between launches)
     from ..ops._ext import ext, scratch
     comm = make_tp_comm("fused", rank, world, dev, 1e-6, max_tokens=max(M, 128), hidden=H)
