@@ -138,12 +138,27 @@ def cmd_train(a):
     return train_from_jsonl(a)
 
 
+def cmd_scan(a):
+    """List (or resolve) locally cached checkpoints: weights/discover.py."""
+    from .weights.discover import resolve, scan
+    if a.resolve:
+        p = resolve(a.query or "")
+        print(p or "")
+        return 0 if p else 1
+    for h in scan(query=a.query):
+        print(f"{h.source:9s} {h.fmt:12s} {h.name}  ->  {h.path}")
+    return 0
+
+
 def main(argv=None):
     argv = list(sys.argv[1:] if argv is None else argv)
     if argv and argv[0] == "bench":
         return cmd_bench(argv[1:])
     ap = argparse.ArgumentParser(prog="python -m rlx_models_b200")
     sub = ap.add_subparsers(dest="cmd", required=True)
+    p = sub.add_parser("scan", help="list weights found in local caches (LM Studio, Ollama, HF, RLX_WEIGHTS_*)")
+    p.add_argument("query", nargs="?", default=None)
+    p.add_argument("--resolve", action="store_true", help="print only the path a query resolves to")
     p = sub.add_parser("inspect")
     p.add_argument("path")
     p.add_argument("--tensors", action="store_true")
@@ -186,7 +201,7 @@ def main(argv=None):
     p.add_argument("--out", default=None)
     p.add_argument("--lora-rank", type=int, default=0)
     a = ap.parse_args(argv)
-    return {"inspect": cmd_inspect, "run": cmd_run, "serve": cmd_serve, "train": cmd_train,
+    return {"scan": cmd_scan, "inspect": cmd_inspect, "run": cmd_run, "serve": cmd_serve, "train": cmd_train,
             "profile": cmd_profile}[a.cmd](a)
 
 

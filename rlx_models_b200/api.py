@@ -65,6 +65,9 @@ def resolve_model_path(model: str) -> str | None:
     if os.path.isfile(model) and model.lower().endswith(".rlxp"):  # packed model: unpack once into the cache
         from .weights.assets import materialize
         return materialize(model)
+    if model.startswith("ollama:") or model.startswith("local:"):  # discovery queries (weights/discover.py)
+        from .weights.discover import resolve
+        return resolve(model.split(":", 1)[1] if model.startswith("local:") else model)
     if "/" in model:
         name, _, rev = parse_model_ref(model)
         root = os.environ.get("HF_HUB_CACHE") or os.path.join(
@@ -76,6 +79,11 @@ def resolve_model_path(model: str) -> str | None:
                 return os.path.join(d, rev)
             if snaps:
                 return os.path.join(d, snaps[-1])
+    from . import config as _C
+    if not any(model == k or model.startswith(k) for k in _C.PRESETS):
+        # not a named random-init shape: look in other tools' caches (LM Studio, Ollama, HF, ...)
+        from .weights.discover import resolve
+        return resolve(model)
     return None
 
 

@@ -566,19 +566,21 @@ int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
   const int sms = num_sms(a.device);
   AttnArgs args = a;
   if (splits <= 0) {
-    // Fixed-size chunks instead of equal parts: a CTA per (sequence, kv head, chunk of pages), so
-    // long sequences become several CTAs of the same size as everyone else's and the last wave
-    // is short (equal parts keep the longest sequence's CTA as long as its whole context). The
-    // chunk shrinks as (sequence, kv-head) pairs get fewer than the ~3 resident CTAs per SM, so
-    // small batches / high tensor parallelism still fill the machine. Chunks past a sequence's end
-    // exit at once; the merge kernel skips their empty partials.
-    const int pairs = a.B * a.Hkv, slots = 3 * sms;
-    int chunk = pairs >= slots ? 32 : pairs * 2 >= slots ? 16 : pairs * 4 >= slots ? 8 : 4;
-    if (const char* e = std::getenv("B200_DECODE_CHUNK")) chunk = std::max(1, std::atoi(e));
-    while (chunk < a.max_blocks && (int64_t)a.B * a.Hq * ((a.max_blocks + chunk - 1) / chunk) * (a.D + 2) > a.ws_elems)
-      chunk *= 2;
-    splits = (a.max_blocks + chunk - 1) / chunk;
-    args.chunk_pages = splits > 1 ? chunk : 0;
+    const int ctas = a.B * a.Hkv;
+    // split the KV range only when (sequence, kv-head) pairs leave SMs idle: measured on B200 at Hkv 8,
+    // ctx 1400, one split beats two at 256 pairs (42.4 vs 48.3 us) and at 512 (79.4 vs 90.8 us); fixed
+    // 32-page chunks per CTA (B200_DECODE_CHUNK) measured slower still (6.87 vs 6.23 ms per Qwen3-8B
+    // decode step at batch 64): the extra partials and the merge cost more than the shorter tail saves
+    splits = std::max(1, std::min(16, (3 * sms + ctas - 1) / ctas));
+    if (ctas >= sms) splits = 1;
+    if (const char* e = std::getenv("B200_DECODE_CHUNK")) {
+      int chunk = std::max(1, std::atoi(e));
+      while (chunk < a.max_blocks &&
+             (int64_t)a.B * a.Hq * ((a.max_blocks + chunk - 1) / chunk) * (a.D + 2) > a.ws_elems)
+        chunk *= 2;
+      splits = (a.max_blocks + chunk - 1) / chunk;
+      args.chunk_pages = splits > 1 ? chunk : 0;
+    }
   }
   if (splits > 1 && a.ws_elems < (int64_t)a.B * a.Hq * splits * (a.D + 2))
     throw std::runtime_error("b200.decode_attention: split workspace too small");

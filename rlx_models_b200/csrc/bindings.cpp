@@ -1233,6 +1233,23 @@ void attn_train_bwd(const Tensor& q, const Tensor& k, const Tensor& v, const Ten
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void instance_norm(const Tensor& x, const optional<Tensor>& gamma, const optional<Tensor>& beta, Tensor& y,
+                   int64_t active, double eps) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.dim() == 3 && x.is_contiguous() && y.is_contiguous() && y.sizes() == x.sizes() &&
+                  y.scalar_type() == x.scalar_type() &&
+                  (x.scalar_type() == at::kFloat || x.scalar_type() == at::kBFloat16),
+              "b200.instance_norm: contiguous fp32 / bf16 [N, C, T]");
+  for (const optional<Tensor>* t : {&gamma, &beta})
+    if (t->has_value() && (*t)->defined())
+      TORCH_CHECK((*t)->scalar_type() == at::kFloat && (*t)->numel() == x.size(1), "b200.instance_norm: fp32 [C]");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::instance_norm_launch(x.data_ptr(), static_cast<const float*>(opt_ptr(gamma)),
+                             static_cast<const float*>(opt_ptr(beta)), y.data_ptr(), x.size(0), (int)x.size(1),
+                             x.size(2), active, (float)eps, x.scalar_type() == at::kBFloat16, cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void scale_by(Tensor& t, const Tensor& g) {
   check_cuda(t, "t");
   TORCH_CHECK(t.is_contiguous() && (t.scalar_type() == at::kFloat || t.scalar_type() == at::kBFloat16) &&
@@ -1499,6 +1516,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_train_fwd", &swiglu_train_fwd);
   m.def("swiglu_train_bwd", &swiglu_train_bwd);
   m.def("scale_by", &scale_by);
+  m.def("instance_norm", &instance_norm);
   m.def("attn_train_fwd", &attn_train_fwd);
   m.def("attn_train_bwd", &attn_train_bwd);
   m.def("sample", &sample);

@@ -190,6 +190,10 @@ void swiglu_train_bwd_launch(const void* dh, const void* gu, void* dgu, int64_t 
                              cudaStream_t st);
 void scale_by_launch(void* t, bool is_f32, int64_t n, const float* g, int device, cudaStream_t st);
 
+// Instance norm over time with an active prefix (Kitten TTS): see audio/instance_norm.cu.
+void instance_norm_launch(const void* x, const float* gamma, const float* beta, void* y, int64_t N, int C,
+                          int64_t T, int64_t active, float eps, bool bf16, cudaStream_t st);
+
 // Vocab-parallel greedy argmax over NVLink peer memory: see comm/tp_sample.cu.
 struct TpArgmaxArgs {
   const float* logits;                    // [R][ld] fp32, this rank's vocab shard

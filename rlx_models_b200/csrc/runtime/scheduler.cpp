@@ -129,6 +129,13 @@ class BlockManager {
     return b;
   }
 
+  // Cached block of a hash without taking a reference (-1 if absent).
+  int peek_cached(uint64_t h) const {
+    if (!prefix_caching_) return -1;
+    auto it = cached_.find(h);
+    return it == cached_.end() ? -1 : it->second;
+  }
+
   int64_t hits = 0, queries = 0;
 
  private:
@@ -427,6 +434,45 @@ class Scheduler {
     return done;
   }
 
+  // Prompt-cache persistence. prefix_blocks: the cached blocks holding the
+  // longest full-block prefix of `tokens` (block ids in order; stops at the first
+  // block that is not cached). import_prefix: allocate blocks for the full-block
+  // prefix of `tokens`, register their hashes and leave them free-but-cached
+  // (LRU), so a later request with that prefix reuses them; returns the block ids
+  // whose contents the caller must fill (blocks already cached are skipped and
+  // returned as -1).
+  std::vector<int32_t> prefix_blocks(const std::vector<int32_t>& tokens) const {
+    std::vector<int32_t> out;
+    uint64_t h = 0;
+    const int full = (int)tokens.size() / kBlock;
+    for (int b = 0; b < full; ++b) {
+      h = block_hash(h, tokens.data() + b * kBlock);
+      const int blk = bm_.peek_cached(h);
+      if (blk < 0) break;
+      out.push_back(blk);
+    }
+    return out;
+  }
+
+  std::vector<int32_t> import_prefix(const std::vector<int32_t>& tokens) {
+    std::vector<int32_t> out;
+    uint64_t h = 0;
+    const int full = (int)tokens.size() / kBlock;
+    for (int b = 0; b < full; ++b) {
+      h = block_hash(h, tokens.data() + b * kBlock);
+      if (bm_.peek_cached(h) >= 0) {
+        out.push_back(-1);
+        continue;
+      }
+      const int blk = bm_.allocate();
+      if (blk < 0) break;
+      bm_.publish(blk, h);
+      bm_.release(blk);  // ref 0 with a hash: reusable cached block (LRU)
+      out.push_back(blk);
+    }
+    return out;
+  }
+
   std::vector<int32_t> output_tokens(int64_t id) const {
     const Seq& s = *seqs_.at(id);
     return std::vector<int32_t>(s.tokens.begin() + s.prompt_len, s.tokens.end());
@@ -542,6 +588,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
       .def("step_seq_ids", &Scheduler::step_seq_ids)
       .def("update", &Scheduler::update)
       .def("output_tokens", &Scheduler::output_tokens)
+      .def("prefix_blocks", &Scheduler::prefix_blocks)
+      .def("import_prefix", &Scheduler::import_prefix)
       .def("finish_reason", &Scheduler::finish_reason)
       .def("num_cached_prompt_tokens", &Scheduler::num_cached_prompt_tokens)
       .def("release", &Scheduler::release)

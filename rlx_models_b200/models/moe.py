@@ -132,6 +132,11 @@ class MoEDecoderLM(DecoderLM):
         self._moe_comm = comm
         super().__init__(cfg, weights, device=device, tp_rank=0, tp_size=1, comm=None)
         self.combiner = None
+        if ep_size > 1 and not (dist.is_available() and dist.is_initialized()):
+            # one rank of an EP model built without a process group (single-GPU timing of a
+            # rank's share: bench/decode_step.py --tp-emulate): only its own experts contribute
+            ep_combine = "local"
+        self._ep_local_only = ep_combine == "local"
         if ep_combine == "fused":
             from ..parallel.ep import EPCombiner
             n_moe = sum(cfg.is_moe_layer(i) for i in range(cfg.num_hidden_layers))
@@ -310,7 +315,7 @@ class MoEDecoderLM(DecoderLM):
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
         ext().moe_combine(dn, inv, k, out, False)
         ops._count(1)
-        if self.ep_size > 1:
+        if self.ep_size > 1 and not self._ep_local_only:
             dist.all_reduce(out)
         return ops.rmsnorm(out, norm_w, c.rms_norm_eps, residual=h, residual_out=h)  # h += moe; norm
 

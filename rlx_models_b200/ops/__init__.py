@@ -305,6 +305,17 @@ def forward_tokens(ids: torch.Tensor, src: torch.Tensor, prev: torch.Tensor) -> 
     return ids
 
 
+def instance_norm(x: torch.Tensor, gamma: torch.Tensor | None = None, beta: torch.Tensor | None = None, *,
+                  active: int = 0, eps: float = 1e-5) -> torch.Tensor:
+    """Instance norm of x [N, C, T] (fp32 / bf16) over time: statistics of the
+    first ``active`` steps (all when 0), applied to every step, then per-channel
+    affine ``gamma`` / ``beta`` (fp32 [C])."""
+    y = torch.empty_like(x)
+    _count(1)
+    ext().instance_norm(x.contiguous(), gamma, beta, y, int(active), float(eps))
+    return y
+
+
 def sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, *, out=None, logprob=None):
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)

@@ -76,3 +76,17 @@ def gather_paged(cache: torch.Tensor, block_table: torch.Tensor, length: int) ->
     nblk = (length + 15) // 16
     pages = cache[block_table[:nblk].long()]  # [nblk, Hkv, 16, D]
     return pages.permute(0, 2, 1, 3).reshape(nblk * 16, cache.shape[1], cache.shape[3])[:length]
+
+
+def instance_norm(x: torch.Tensor, gamma=None, beta=None, active: int = 0, eps: float = 1e-5) -> torch.Tensor:
+    """fp32 instance norm over the last axis with statistics of the first ``active`` steps."""
+    xf = x.float()
+    a = active if 0 < active <= x.shape[-1] else x.shape[-1]
+    mean = xf[..., :a].mean(-1, keepdim=True)
+    var = xf[..., :a].var(-1, unbiased=False, keepdim=True)
+    y = (xf - mean) * torch.rsqrt(var + eps)
+    if gamma is not None:
+        y = y * gamma.float()[None, :, None]
+    if beta is not None:
+        y = y + beta.float()[None, :, None]
+    return y

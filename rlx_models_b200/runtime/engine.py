@@ -588,6 +588,19 @@ class LLMEngine:
             self._metrics_f.write(json.dumps(rec) + "\n")
         return outs
 
+    def save_prompt_cache(self, path: str, tokens: list[int]) -> int:
+        """Persist the cached KV of ``tokens``' longest cached prefix (full 16-token
+        blocks) with a model fingerprint; returns the tokens saved. See runtime/prompt_cache.py."""
+        from .prompt_cache import save_prompt
+        torch.cuda.synchronize(self.device)
+        return save_prompt(self, path, tokens)
+
+    def load_prompt_cache(self, path: str) -> int:
+        """Restore a saved prompt prefix into the prefix cache (0 if the file is
+        from another model); later requests starting with it skip those tokens."""
+        from .prompt_cache import load_prompt
+        return load_prompt(self, path)
+
     def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None
                  ) -> list[RequestOutput]:
         if not isinstance(params, list):

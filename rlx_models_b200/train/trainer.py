@@ -52,6 +52,9 @@ class TrainConfig:
     # quantisation-aware training: linear weights are fake-quantised to this
     # format in the forward pass (quant/calib.py FORMATS), gradients straight-through
     qat: str | None = None
+    # "adamw", or "muon": orthogonalized Nesterov momentum for 2-D weights, AdamW for the rest (train/muon.py)
+    optimizer: str = "adamw"
+    muon_momentum: float = 0.95
 
     def lr_at(self, step: int) -> float:
         if self.warmup_steps and step < self.warmup_steps:
@@ -247,6 +250,10 @@ class Trainer:
 
     def _adamw(self, g: FlatGroup, lr: float):
         c = self.cfg
+        if c.optimizer == "muon" and self.lora is None:
+            from .muon import muon_step
+            muon_step(self, g, lr)
+            return
         if g.master.is_cuda:
             ops.ext().adamw(g.master, g.grad, g.exp_avg, g.exp_avg_sq, g.param, lr, c.betas[0], c.betas[1], c.eps,
                             c.weight_decay, self.step_num, self._coef, 1.0)

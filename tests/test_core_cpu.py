@@ -384,3 +384,23 @@ def test_scheduler_overlap_preemption_and_stop():
     assert s.output_tokens(a) == [3, 4, 5, 6] and s.finish_reason(a) == 2
     assert s.output_tokens(b) == [4, 5, 6, 7, 8] and s.finish_reason(b) == 1
     assert s.stats()["free_blocks"] == 50
+
+
+def test_scheduler_prefix_export_import():
+    """prefix_blocks finds a prompt's cached blocks; import_prefix registers blocks
+    that a fresh scheduler then reuses for a request with that prefix."""
+    from rlx_models_b200 import _runtime
+    s = _runtime.Scheduler(100, 4, 256, 32, True, 0)
+    bufs = _staging(W=32)
+    prompt = list(range(100, 150))  # 3 full blocks + 2 tokens
+    s.add_request(prompt, 2, True, [])
+    _drive(s, bufs)
+    assert len(s.prefix_blocks(prompt)) == 3
+    assert s.prefix_blocks([7] * 40) == []
+    s2 = _runtime.Scheduler(100, 4, 256, 32, True, 0)
+    blocks = s2.import_prefix(prompt)
+    assert len(blocks) == 3 and all(b >= 0 for b in blocks)
+    assert s2.import_prefix(prompt) == [-1, -1, -1]  # already cached: nothing to fill
+    sid = s2.add_request(prompt + [1, 2, 3], 2, True, [])
+    info = s2.schedule(*_staging(W=32))
+    assert s2.num_cached_prompt_tokens(sid) == 48 and info["num_tokens"] == 53 - 48

@@ -366,3 +366,17 @@ def test_geglu_epilogues(cuda):
         assert rel_err(ops.linear_swiglu(x, w_gu, act=1), r) < 1e-2
         if M <= ops.ACC_MAX_M:
             assert rel_err(ops.swiglu_acc(ops.linear_acc(x, w_gu), act=1), r) < 1e-2
+
+
+@pytest.mark.parametrize("dtype,active", [(torch.float32, 0), (torch.float32, 700), (torch.bfloat16, 333)])
+def test_instance_norm_vs_fp32(cuda, dtype, active):
+    from rlx_models_b200 import ops
+    from rlx_models_b200.ops import reference as R
+    g = torch.Generator(device=cuda).manual_seed(0)
+    x = (torch.randn(3, 20, 1000, device=cuda, generator=g) * 3 + 1).to(dtype)
+    gamma = torch.randn(20, device=cuda, generator=g)
+    beta = torch.randn(20, device=cuda, generator=g)
+    y = ops.instance_norm(x, gamma, beta, active=active)
+    ref = R.instance_norm(x, gamma, beta, active=active)
+    rel = ((y.float() - ref).norm() / ref.norm()).item()
+    assert rel < (1e-5 if dtype == torch.float32 else 1e-2), rel

@@ -152,3 +152,29 @@ def test_chunked_prefill_logits(tiny_model):
     parts = [run(kv, lo, min(T, lo + 48)) for lo in range(0, T, 48)]
     chunked = torch.cat(parts)
     assert rel(chunked.cpu(), full.cpu()) < 2e-2
+
+
+def test_prompt_cache_save_load_roundtrip(cuda, tmp_path):
+    """A prompt's cached KV saved by one engine and loaded into a fresh one is
+    reused (no recompute of those tokens) and gives the same greedy output; a
+    file from another model is refused."""
+    from rlx_models_b200 import config as C
+    from rlx_models_b200.models.decoder import DecoderLM
+    from rlx_models_b200.runtime.engine import EngineConfig, LLMEngine, SamplingParams
+    from rlx_models_b200.weights.init import random_weights
+    cfg = C.tiny(num_hidden_layers=2, hidden_size=2048, intermediate_size=2048, num_attention_heads=16,
+                 num_key_value_heads=8, head_dim=128, vocab_size=4096)
+    m = DecoderLM(cfg, random_weights(cfg, seed=1, device=cuda), device=cuda)
+    prompt = torch.randint(0, cfg.vocab_size, (70,), generator=torch.Generator().manual_seed(0)).tolist()
+    sp = SamplingParams(max_new_tokens=6, ignore_eos=True)
+    ecfg = EngineConfig(max_num_seqs=8, max_batched_tokens=256, max_model_len=256, num_blocks=64)
+    e1 = LLMEngine(m, ecfg)
+    ref = e1.generate([prompt], sp)[0].token_ids
+    path = str(tmp_path / "p.safetensors")
+    assert e1.save_prompt_cache(path, prompt) == 64
+    e2 = LLMEngine(m, ecfg)
+    assert e2.load_prompt_cache(path) == 64
+    out = e2.generate([prompt], sp)[0]
+    assert out.cached_prompt_tokens == 64 and out.token_ids == ref
+    other = DecoderLM(cfg, random_weights(cfg, seed=2, device=cuda), device=cuda)
+    assert LLMEngine(other, ecfg).load_prompt_cache(path) == 0

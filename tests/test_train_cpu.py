@@ -98,3 +98,55 @@ def test_hf_export_roundtrip(tmp_path):
     assert set(wm.keys()) == set(sd)
     assert torch.allclose(wm.peek("model.layers.1.mlp.up_proj.weight").float(),
                           sd["model.layers.1.mlp.up_proj.weight"].bfloat16().float())
+
+
+def test_newton_schulz_orthogonalizes():
+    from rlx_models_b200.train.muon import newton_schulz5
+    g = torch.randn(48, 96, generator=torch.Generator().manual_seed(0))
+    o = newton_schulz5(g)
+    sv = torch.linalg.svdvals(o)
+    assert sv.min() > 0.5 and sv.max() < 1.3  # singular values pushed toward 1 (the method's band)
+    # same left / right singular vectors as G: O is close to U V^T
+    u, _, vh = torch.linalg.svd(g, full_matrices=False)
+    assert ((o - u @ vh).norm() / (u @ vh).norm()) < 0.35
+
+
+def _muon_worker(rank, world, port, out_dir, steps):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = _cfg()
+    t = Trainer(cfg, TrainConfig(lr=1e-2, micro_batch=1, param_dtype="float32", optimizer="muon"),
+                random_weights(cfg, 0), rank=rank, world=world, device="cpu")
+    losses = []
+    for s in range(steps):
+        b = _batch(s)
+        per = b.shape[0] // world
+        losses.append(t.step(b[rank * per:(rank + 1) * per]).loss)
+    sd = t.model.hf_state_dict()
+    if rank == 0:
+        torch.save({"losses": losses, "sd": sd}, os.path.join(out_dir, "res.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_muon_sharded_matches_single_process_and_learns():
+    cfg = _cfg()
+    t = Trainer(cfg, TrainConfig(lr=1e-2, micro_batch=2, param_dtype="float32", optimizer="muon"),
+                random_weights(cfg, 0), device="cpu")
+    losses = [t.step(_batch(s)).loss for s in range(3)]
+    ref_sd = t.model.hf_state_dict()
+    t2 = Trainer(cfg, TrainConfig(lr=1e-2, micro_batch=2, param_dtype="float32", optimizer="muon"),
+                 random_weights(cfg, 0), device="cpu")
+    fixed = _batch(5)
+    l0 = t2.step(fixed).loss
+    for _ in range(6):
+        l1 = t2.step(fixed).loss
+    assert l1 < l0  # overfits one batch
+    with tempfile.TemporaryDirectory() as d:
+        port = 29650 + os.getpid() % 300
+        mp.spawn(_muon_worker, args=(2, port, d, 3), nprocs=2, join=True)
+        res = torch.load(os.path.join(d, "res.pt"))
+        for a, b in zip(res["losses"], losses):
+            assert abs(a - b) < 1e-4 * max(1.0, abs(b))
+        for k, v in ref_sd.items():
+            assert torch.allclose(res["sd"][k], v, atol=5e-5, rtol=1e-4), k
