@@ -420,7 +420,7 @@ void qkv_rope(const Tensor& qkv, const optional<Tensor>& q_norm, const optional<
               const Tensor& positions, const optional<Tensor>& slots, const Tensor& inv_freq, double rope_scale,
               Tensor& q_out, const optional<Tensor>& k_cache, const optional<Tensor>& v_cache,
               const optional<Tensor>& k_out, const optional<Tensor>& v_out, int64_t Hq, int64_t Hkv, int64_t D,
-              double eps, int64_t rot_dim) {
+              double eps, int64_t rot_dim, const optional<Tensor>& bias) {
   check_cuda(qkv, "qkv");
   if (rot_dim <= 0) rot_dim = D;
   TORCH_CHECK(rot_dim <= D && rot_dim % (2 * (D / 32)) == 0, "b200.qkv_rope: rot_dim must be <= head_dim and a "
@@ -441,6 +441,12 @@ void qkv_rope(const Tensor& qkv, const optional<Tensor>& q_norm, const optional<
   b200::QkvRopeArgs a{};
   a.qkv = qkv.data_ptr();
   if (qkv.scalar_type() == at::kFloat) a.qkv_f32 = qkv.data_ptr<float>();
+  if (bias.has_value() && bias->defined()) {
+    TORCH_CHECK(qkv.scalar_type() == at::kFloat && bias->scalar_type() == at::kBFloat16 &&
+                    bias->numel() == qkv.size(1),
+                "b200.qkv_rope: bias applies to the fp32 accumulate input, bf16 [(Hq + 2 Hkv) * D]");
+    a.bias = bias->data_ptr();
+  }
   a.ld_qkv = qkv.stride(0);
   a.q_norm = opt_ptr(q_norm);
   a.k_norm = opt_ptr(k_norm);
@@ -727,14 +733,15 @@ void rs_norm_ag(const optional<Tensor>& recv, const optional<Tensor>& racc, Tens
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void add_rmsnorm_acc(Tensor& acc, Tensor& h, const Tensor& w, Tensor& out, double eps) {
+void add_rmsnorm_acc(Tensor& acc, Tensor& h, const Tensor& w, Tensor& out, double eps,
+                     const optional<Tensor>& bias) {
   check_cuda(acc, "acc");
   TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && h.is_contiguous() &&
                   h.scalar_type() == at::kBFloat16 && acc.sizes() == h.sizes() && h.size(1) % 8 == 0,
               "b200.add_rmsnorm_acc: shapes");
   c10::cuda::CUDAGuard g(acc.device());
   b200::add_rmsnorm_acc_launch(acc.data_ptr<float>(), h.data_ptr(), w.data_ptr(), out.data_ptr(), out.stride(0),
-                               h.size(0), h.size(1), (float)eps, cur_stream(acc));
+                               h.size(0), h.size(1), (float)eps, cur_stream(acc), opt_ptr(bias));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -268,10 +268,12 @@ struct QkvRopeArgs {
   int64_t T;
   int Hq, Hkv, D;
   float eps;
+  const void* bias = nullptr;  // [(Hq + 2 Hkv) * D] bf16 added to the fp32 sums (accumulate-mode input only)
 };
 void qkv_rope_launch(const QkvRopeArgs& a, cudaStream_t st);
+// bias ([H] bf16, may be null) is added to the fp32 sums before the residual add
 void add_rmsnorm_acc_launch(float* acc, void* h, const void* w, void* out, int64_t ldo, int64_t T, int64_t H,
-                            float eps, cudaStream_t st);
+                            float eps, cudaStream_t st, const void* bias = nullptr);
 void swiglu_acc_launch(float* acc, void* out, int64_t T, int64_t I, int act, cudaStream_t st);
 
 // ---------------- attention ----------------

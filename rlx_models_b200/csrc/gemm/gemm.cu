@@ -89,7 +89,10 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
     for (int s = 1; s <= max_sp; ++s) {
       const int kts = (p.k_tiles + s - 1) / s;
       const int waves = (tiles * s + sms - 1) / sms;
-      const double cost = (double)waves * kts + (s > 1 ? (epi == gemm::EPI_ACC ? 0.5 : 6.0) * s : 0.0);
+      // a handful of output tiles (a router, a small head) would otherwise stream the whole K
+      // on a few SMs: there the partial-tile round trip is cheap next to the serial k loop
+      const double per_split = epi == gemm::EPI_ACC ? 0.5 : (tiles <= 8 ? 1.0 : 6.0);
+      const double cost = (double)waves * kts + (s > 1 ? per_split * s : 0.0);
       if (cost < best - 1e-9) {
         best = cost;
         sp = s;

@@ -144,9 +144,12 @@ __global__ void qkv_rope_kernel(QkvRopeArgs a) {
     // accumulate-only GEMM output: round the fp32 sum to bf16 (as the bf16
     // GEMM epilogue would) and zero it for the next use
     float* src = a.qkv_f32 + t * a.ld_qkv + (int64_t)h * D;
+    const __nv_bfloat16* bb =
+        a.bias != nullptr ? reinterpret_cast<const __nv_bfloat16*>(a.bias) + (int64_t)h * D + lane * E : nullptr;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
-      x[e] = __bfloat162float(__float2bfloat16(__ldcg(src + lane * E + e)));
+      const float bv = bb != nullptr ? __bfloat162float(bb[e]) : 0.f;  // the bf16 epilogue adds the bias
+      x[e] = __bfloat162float(__float2bfloat16(__ldcg(src + lane * E + e) + bv));
       __stcg(src + lane * E + e, 0.f);
     }
   } else {
@@ -239,7 +242,7 @@ void qkv_rope_launch(const QkvRopeArgs& a, cudaStream_t st) {
 template <int VPT>
 __global__ void add_rmsnorm_acc_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ h,
                                        const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out,
-                                       int64_t ldo, int H, float eps) {
+                                       int64_t ldo, int H, float eps, const __nv_bfloat16* __restrict__ bias) {
   __shared__ float red[32];
   pdl_wait();
   pdl_trigger();
@@ -255,7 +258,16 @@ __global__ void add_rmsnorm_acc_kernel(float* __restrict__ acc, __nv_bfloat16* _
     const float4 a0 = __ldcg(ap), a1 = __ldcg(ap + 1);
     __stcg(ap, make_float4(0.f, 0.f, 0.f, 0.f));
     __stcg(ap + 1, make_float4(0.f, 0.f, 0.f, 0.f));
-    const float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    float av[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    if (bias != nullptr) {
+      const uint4 bv = *reinterpret_cast<const uint4*>(bias + vi * 8);
+      const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        av[2 * q] += bf16_lo(bw[q]);
+        av[2 * q + 1] += bf16_hi(bw[q]);
+      }
+    }
     uint4* hp = reinterpret_cast<uint4*>(h + row * (int64_t)H + vi * 8);
     const uint4 hv = *hp;
     const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
@@ -301,7 +313,7 @@ __global__ void add_rmsnorm_acc_kernel(float* __restrict__ acc, __nv_bfloat16* _
 }
 
 void add_rmsnorm_acc_launch(float* acc, void* h, const void* w, void* out, int64_t ldo, int64_t T, int64_t H,
-                            float eps, cudaStream_t st) {
+                            float eps, cudaStream_t st, const void* bias) {
   if (T == 0) return;
   const int nv = (int)(H / 8);
   const int threads = std::min(1024, (nv + 31) / 32 * 32);
@@ -309,9 +321,12 @@ void add_rmsnorm_acc_launch(float* acc, void* h, const void* w, void* out, int64
   auto hb = reinterpret_cast<__nv_bfloat16*>(h);
   auto wb = reinterpret_cast<const __nv_bfloat16*>(w);
   auto ob = reinterpret_cast<__nv_bfloat16*>(out);
-  if (vpt <= 1) launch_pdl(add_rmsnorm_acc_kernel<1>, dim3((unsigned)T), dim3(threads), 0, st, acc, hb, wb, ob, ldo, (int)H, eps);
-  else if (vpt <= 2) launch_pdl(add_rmsnorm_acc_kernel<2>, dim3((unsigned)T), dim3(threads), 0, st, acc, hb, wb, ob, ldo, (int)H, eps);
-  else if (vpt <= 4) launch_pdl(add_rmsnorm_acc_kernel<4>, dim3((unsigned)T), dim3(threads), 0, st, acc, hb, wb, ob, ldo, (int)H, eps);
+  if (vpt <= 1) launch_pdl(add_rmsnorm_acc_kernel<1>, dim3((unsigned)T), dim3(threads), 0, st, acc, hb, wb, ob, ldo, (int)H, eps,
+                                    reinterpret_cast<const __nv_bfloat16*>(bias));
+  else if (vpt <= 2) launch_pdl(add_rmsnorm_acc_kernel<2>, dim3((unsigned)T), dim3(threads), 0, st, acc, hb, wb, ob, ldo, (int)H, eps,
+                                    reinterpret_cast<const __nv_bfloat16*>(bias));
+  else if (vpt <= 4) launch_pdl(add_rmsnorm_acc_kernel<4>, dim3((unsigned)T), dim3(threads), 0, st, acc, hb, wb, ob, ldo, (int)H, eps,
+                                    reinterpret_cast<const __nv_bfloat16*>(bias));
   else throw std::runtime_error("b200.add_rmsnorm_acc: hidden size too large");
 }
 

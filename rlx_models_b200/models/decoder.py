@@ -181,15 +181,16 @@ class DecoderLM:
     def _attention(self, i: int, L: LayerWeights, x: torch.Tensor, fb: ForwardBatch, kv: PagedKVCache):
         T = x.shape[0]
         kc, vc = kv.layer(i)
-        if T <= ops.ACC_MAX_M and L.bqkv is None:
-            qkv = ops.linear_acc(x, L.wqkv)  # fp32 sums, consumed (and zeroed) by qkv_rope
+        acc = T <= ops.ACC_MAX_M
+        if acc:
+            qkv = ops.linear_acc(x, L.wqkv)  # fp32 sums, consumed (and zeroed) by qkv_rope, which adds the bias
         else:
             qkv = ops.linear(x, L.wqkv, bias=L.bqkv)
         q = ops.qkv_rope(qkv, num_q_heads=self.hq, num_kv_heads=self.hkv, head_dim=self.D,
                          positions=fb.positions, inv_freq=L.inv_freq, rope_scale=L.rope_mult,
                          rot_dim=self.cfg.rotary_dim,
                          q_norm=L.q_norm, k_norm=L.k_norm, eps=self.cfg.rms_norm_eps, slots=fb.slots,
-                         k_cache=kc, v_cache=vc)
+                         k_cache=kc, v_cache=vc, bias=L.bqkv if acc else None)
         o = torch.empty_like(q)
         nd = fb.num_decode
         retrieval = getattr(self, "retrieval", None)
@@ -333,7 +334,7 @@ class LocalComm:
 
         Decode-sized batches: accumulate-only GEMM + one add+RMSNorm kernel that
         consumes the fp32 sums; larger batches: residual add in the GEMM epilogue."""
-        if x.shape[0] <= ops.ACC_MAX_M and bias is None:
-            return ops.add_rmsnorm_acc(ops.linear_acc(x, w), h, norm_w, self.eps)
+        if x.shape[0] <= ops.ACC_MAX_M:
+            return ops.add_rmsnorm_acc(ops.linear_acc(x, w), h, norm_w, self.eps, bias=bias)
         ops.linear(x, w, bias=bias, residual=h, out=h)
         return ops.rmsnorm(h, norm_w, self.eps)

@@ -326,8 +326,11 @@ class MoEDecoderLM(DecoderLM):
         n = len(self.layers)
         for i, L in enumerate(self.layers):
             a = self._attention(i, L, x, fb, kv)
-            ops.linear(a, L.wo, bias=L.bo, residual=h, out=h)  # h += o_proj (+ bias)
-            x = ops.rmsnorm(h, L.ln2, c.rms_norm_eps)
+            if a.shape[0] <= ops.ACC_MAX_M:  # decode: accumulate-only GEMM, bias + residual + norm in one kernel
+                x = ops.add_rmsnorm_acc(ops.linear_acc(a, L.wo), h, L.ln2, c.rms_norm_eps, bias=L.bo)
+            else:
+                ops.linear(a, L.wo, bias=L.bo, residual=h, out=h)  # h += o_proj (+ bias)
+                x = ops.rmsnorm(h, L.ln2, c.rms_norm_eps)
             nw = self.layers[i + 1].ln1 if i + 1 < n else self.norm
             if self.moe[i] is None:  # dense layer
                 ops.linear(ops.linear_swiglu(x, L.w_gu), L.wd, residual=h, out=h)

@@ -125,12 +125,12 @@ def linear_acc(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor | None = None
 
 
 def add_rmsnorm_acc(acc: torch.Tensor, h: torch.Tensor, w: torch.Tensor, eps: float,
-                    out: torch.Tensor | None = None) -> torch.Tensor:
-    """h = bf16(h + bf16(acc)); returns rmsnorm(h) * w; zeroes acc."""
+                    out: torch.Tensor | None = None, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """h = bf16(h + bf16(acc (+ bias))); returns rmsnorm(h) * w; zeroes acc."""
     if out is None:
         out = torch.empty_like(h)
     _count(1)
-    ext().add_rmsnorm_acc(acc, h, w, out, float(eps))
+    ext().add_rmsnorm_acc(acc, h, w, out, float(eps), bias)
     return out
 
 
@@ -250,15 +250,16 @@ def qkv_rope(qkv: torch.Tensor, *, num_q_heads: int, num_kv_heads: int, head_dim
              slots: torch.Tensor | None = None, k_cache: torch.Tensor | None = None,
              v_cache: torch.Tensor | None = None, q_out: torch.Tensor | None = None,
              k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None,
-             rot_dim: int = 0) -> torch.Tensor:
+             rot_dim: int = 0, bias: torch.Tensor | None = None) -> torch.Tensor:
     """QK RMSNorm + RoPE on the fused qkv projection; K/V written to the paged cache.
-    ``rot_dim`` (0 = head_dim): rotate only the first rot_dim dims of each head."""
+    ``rot_dim`` (0 = head_dim): rotate only the first rot_dim dims of each head.
+    ``bias`` (bf16) is added to an fp32 accumulate-mode ``qkv`` before rounding."""
     T = qkv.shape[0]
     if q_out is None:
         q_out = torch.empty(T, num_q_heads, head_dim, dtype=torch.bfloat16, device=qkv.device)
     _count(1)
     ext().qkv_rope(qkv, q_norm, k_norm, positions, slots, inv_freq, float(rope_scale), q_out, k_cache,
-                   v_cache, k_out, v_out, num_q_heads, num_kv_heads, head_dim, float(eps), int(rot_dim))
+                   v_cache, k_out, v_out, num_q_heads, num_kv_heads, head_dim, float(eps), int(rot_dim), bias)
     return q_out
 
 

@@ -79,7 +79,7 @@ def load_prompt(engine, path: str) -> int:
         tokens = f.get("tokens").tolist()
         blocks = engine.sched.import_prefix(tokens)
         kv = engine.kv
-        k, v = f.get("k"), f.get("v")
+        k, v = f.get("k").clone(), f.get("v").clone()  # copies: the file's mapping closes below
         fill = [(i, b) for i, b in enumerate(blocks) if b >= 0]
         if fill:
             src = torch.tensor([i for i, _ in fill], dtype=torch.long)
