@@ -82,6 +82,8 @@ class DecoderLM:
             self.local_rope = (li.to(self.device), lm)
         if c.sandwich_norm and tp_size > 1:
             raise NotImplementedError("sandwich-norm (Gemma-2/3) decoders run with tp_size 1")
+        if c.qk_norm_full and tp_size > 1:
+            raise NotImplementedError("full-width QK-norm (MiniMax-M2) needs every head of a token: tp_size 1")
         self._load(weights)
 
     # -- weights ---------------------------------------------------------------
@@ -181,15 +183,21 @@ class DecoderLM:
     def _attention(self, i: int, L: LayerWeights, x: torch.Tensor, fb: ForwardBatch, kv: PagedKVCache):
         T = x.shape[0]
         kc, vc = kv.layer(i)
-        acc = T <= ops.ACC_MAX_M
+        full = self.cfg.qk_norm_full
+        acc = T <= ops.ACC_MAX_M and not full
         if acc:
             qkv = ops.linear_acc(x, L.wqkv)  # fp32 sums, consumed (and zeroed) by qkv_rope, which adds the bias
         else:
             qkv = ops.linear(x, L.wqkv, bias=L.bqkv)
+        if full:  # MiniMax-M2: one RMSNorm over all q heads (and all k heads) of a token, in place
+            qd, kd = self.hq * self.D, self.hkv * self.D
+            ops.rmsnorm(qkv[:, :qd], L.q_norm, self.cfg.rms_norm_eps, out=qkv[:, :qd])
+            ops.rmsnorm(qkv[:, qd:qd + kd], L.k_norm, self.cfg.rms_norm_eps, out=qkv[:, qd:qd + kd])
         q = ops.qkv_rope(qkv, num_q_heads=self.hq, num_kv_heads=self.hkv, head_dim=self.D,
                          positions=fb.positions, inv_freq=L.inv_freq, rope_scale=L.rope_mult,
                          rot_dim=self.cfg.rotary_dim,
-                         q_norm=L.q_norm, k_norm=L.k_norm, eps=self.cfg.rms_norm_eps, slots=fb.slots,
+                         q_norm=None if full else L.q_norm, k_norm=None if full else L.k_norm,
+                         eps=self.cfg.rms_norm_eps, slots=fb.slots,
                          k_cache=kc, v_cache=vc, bias=L.bqkv if acc else None)
         o = torch.empty_like(q)
         nd = fb.num_decode

@@ -155,9 +155,6 @@ class MoEDecoderLM(DecoderLM):
     # -- weights ----------------------------------------------------------------
     def _load(self, w):
         c, dev, bf = self.cfg, self.device, torch.bfloat16
-        if c.qk_norm_full:
-            raise NotImplementedError(f"{c.model_type}: the full-width QK-norm runs in the fp32 oracle "
-                                      "(models.oracle.Oracle); the served MoE path normalises per head")
         if c.model_type in ("mixtral", "minimax_m2"):  # block_sparse_moe.* names -> the canonical MoE names
             from ..weights.aliases import CanonicalView
             w = CanonicalView(w, c.model_type)

@@ -42,9 +42,10 @@ def decoder_tensor_specs(cfg: DecoderConfig) -> list[TensorSpec]:
         if cfg.sandwich_norm:
             specs += [TensorSpec(p + "pre_feedforward_layernorm.weight", (H,), "norm"),
                       TensorSpec(p + "post_feedforward_layernorm.weight", (H,), "norm")]
-        if cfg.qk_norm:
-            specs += [TensorSpec(p + "self_attn.q_norm.weight", (D,), "norm"),
-                      TensorSpec(p + "self_attn.k_norm.weight", (D,), "norm")]
+        if cfg.qk_norm:  # per head (D), or over all heads of the token (MiniMax-M2)
+            qn, kn = (q, kv) if cfg.qk_norm_full else (D, D)
+            specs += [TensorSpec(p + "self_attn.q_norm.weight", (qn,), "norm"),
+                      TensorSpec(p + "self_attn.k_norm.weight", (kn,), "norm")]
         if cfg.attention_bias:
             specs += [TensorSpec(p + "self_attn.q_proj.bias", (q,), "bias"),
                       TensorSpec(p + "self_attn.k_proj.bias", (kv,), "bias"),

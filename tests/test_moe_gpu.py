@@ -183,3 +183,39 @@ def test_mixtral_qwen2_moe_vs_oracle(cuda, family):
     row = ((lg.cpu().float() - ref).norm(dim=-1) / ref.norm(dim=-1))
     assert row.median() < 2e-2, row
     assert (row > 0.1).float().mean() <= 0.1, row
+
+
+def test_minimax_m2_vs_oracle(cuda):
+    """MiniMax-M2 on the GPU: full-width QK-norm (one RMSNorm over all heads of
+    a token, in place on the bf16 q|k|v projection), partial RoPE, sigmoid
+    routing with the correction bias; oracle on the same MXFP4-rounded experts."""
+    from rlx_models_b200.config import DecoderConfig
+    from rlx_models_b200.models.decoder import ForwardBatch
+    from rlx_models_b200.quant.mxfp4 import mxfp4_roundtrip
+    cfg = DecoderConfig.from_hf_dict(dict(model_type="minimax_m2", vocab_size=512, hidden_size=256,
+                                          intermediate_size=128, num_hidden_layers=2, num_attention_heads=4,
+                                          num_key_value_heads=2, head_dim=64, num_local_experts=8,
+                                          num_experts_per_tok=2, rotary_dim=32, rms_norm_eps=1e-6,
+                                          max_position_embeddings=256))
+    assert cfg.qk_norm_full and cfg.rotary_dim == 32
+    w = random_weights(cfg, seed=8, dtype=torch.bfloat16)
+    for k in list(w):
+        if ".mlp.experts." in k:
+            w[k] = mxfp4_roundtrip(w[k].float()).bfloat16()
+        if k.endswith("e_score_correction_bias"):
+            w[k] = torch.randn(w[k].shape, generator=torch.Generator().manual_seed(5)) * 0.5
+    model = MoEDecoderLM(cfg, w, device=cuda)
+    oracle = DecoderOracle(cfg, {k: v.float() for k, v in w.items()})
+    for T in (37, 5):  # prefill-sized and decode-sized batches
+        ids = torch.randint(0, cfg.vocab_size, (T,), generator=torch.Generator().manual_seed(T))
+        nb = (T + 15) // 16
+        fb = ForwardBatch(input_ids=ids.int().to(cuda), positions=torch.arange(T, dtype=torch.int32, device=cuda),
+                          slots=torch.arange(T, dtype=torch.int64, device=cuda), num_decode=0,
+                          pre_block_tables=torch.arange(nb, dtype=torch.int32, device=cuda).view(1, -1),
+                          pre_ctx_lens=torch.tensor([T], dtype=torch.int32, device=cuda),
+                          pre_cu_q=torch.tensor([0, T], dtype=torch.int32, device=cuda), pre_max_q=T)
+        lg = model.forward(fb, model.make_kv_cache(nb))
+        ref, _ = oracle.forward(ids)
+        row = ((lg.cpu().float() - ref).norm(dim=-1) / ref.norm(dim=-1))
+        assert row.median() < 2e-2, row
+        assert (row > 0.1).float().mean() <= 0.2, row
