@@ -25,6 +25,38 @@ import os
 import torch
 
 
+def resident_weight_bytes(model) -> int:
+    """Bytes of every distinct CUDA tensor reachable from ``model``'s
+    attributes (the weights as stored: bf16, packed MXFP4 blocks + scales),
+    except an untied input embedding, of which a decode step reads only the
+    batch's rows."""
+    seen, total = set(), 0
+    skip = set()
+    emb, head = getattr(model, "embed", None), getattr(model, "lm_head", None)
+    if torch.is_tensor(emb) and not (torch.is_tensor(head) and head.data_ptr() == emb.data_ptr()):
+        skip.add(emb.data_ptr())
+    stack, visited = [model], set()
+    while stack:
+        o = stack.pop()
+        if id(o) in visited:
+            continue
+        visited.add(id(o))
+        if torch.is_tensor(o):
+            if o.is_cuda and o.data_ptr() not in seen and o.data_ptr() not in skip:
+                seen.add(o.data_ptr())
+                total += o.untyped_storage().nbytes()
+        elif isinstance(o, (list, tuple)):
+            stack.extend(o)
+        elif isinstance(o, dict):
+            stack.extend(o.values())
+        elif not isinstance(o, type) and type(o).__module__.startswith("rlx_models_b200"):
+            if hasattr(o, "__dict__"):
+                stack.extend(vars(o).values())
+            for c in type(o).__mro__:
+                stack.extend(getattr(o, n, None) for n in getattr(c, "__slots__", ()))
+    return total
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="qwen3-8b")
@@ -86,8 +118,9 @@ def main():
         from ..utils.trace import profile
         eng.cfg = dataclasses.replace(eng.cfg, cuda_graphs=False)
         breakdown = profile(eng.step, steps=args.breakdown, warmup=1, top=16)
-    nparam = cfg.num_params()
-    wbytes = (2 * nparam - (2 * cfg.vocab_size * cfg.hidden_size)) / tp  # embedding rows are gathered
+    # weights as stored on this rank (bf16, packed MXFP4 experts); for an MoE every
+    # expert counts, an upper bound once a step routes to fewer than all of them
+    wbytes = resident_weight_bytes(llm.engine.model)
     kv_bytes = 2 * 2 * cfg.num_hidden_layers * cfg.num_key_value_heads * cfg.head_dim * args.batch * (args.ctx + 1) / tp
     hbm, _, src = peaks()
     ach = (wbytes + kv_bytes) / (ms * 1e-3) / 1e12

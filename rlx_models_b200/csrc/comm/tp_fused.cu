@@ -144,9 +144,9 @@ __global__ void __launch_bounds__(kRsThreads) rs_norm_ag_kernel(RsNormAgArgs a) 
       for (int q = 0; q < a.world; ++q) *reinterpret_cast<uint4*>(pg[q] + grow + col) = ov;
     }
   }
-  __threadfence_system();
-  __syncthreads();
+  __syncthreads();  // the CTA's gather stores, then one system fence (cumulative) per CTA
   if (threadIdx.x == 0) {
+    __threadfence_system();
     const unsigned old = atomicAdd(a.cta_ctr, 1u);
     if (old == gridDim.x - 1) {
       __threadfence_system();
@@ -491,8 +491,10 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
         o[k] = pack_bf16x2(v[c][2 * k] * inv * bf16_lo(ww[k]), v[c][2 * k + 1] * inv * bf16_hi(ww[k]));
       *reinterpret_cast<uint4*>(res_out + (int64_t)i * H + col) = make_uint4(o[0], o[1], o[2], o[3]);
     }
-    __threadfence_system();
+    // every thread's result stores are ordered before thread 0's system fence by
+    // the barrier (fence cumulativity), so one fence per CTA publishes them
     __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
     if (threadIdx.x == 0 && atomicAdd(a.cta_ctr, 1u) == (unsigned)n_my - 1) {
       __threadfence_system();  // one system fence covers every rank's flag store below
       for (int q = 0; q < a.world; ++q) st_relaxed_sys_u32(a.peer_flags[q] + a.world + a.rank, e);

@@ -41,12 +41,36 @@ __global__ void __launch_bounds__(kThreads) tp_argmax_kernel(TpArgmaxArgs a) {
   const int row = blockIdx.x;
   const float* x = a.logits + (int64_t)row * a.ld;
   unsigned long long best = 0ull;
-  for (int i = threadIdx.x; i < a.V_local; i += kThreads) {
-    const float v = x[i];
-    if (v != v) continue;  // NaN never wins
+  auto consider = [&](float v, int i) {
+    if (v != v) return;  // NaN never wins
     const unsigned long long k =
         ((unsigned long long)ord_f32(v) << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)(a.v_offset + i));
     best = k > best ? k : best;
+  };
+  if ((a.ld & 3) == 0 && (reinterpret_cast<uintptr_t>(a.logits) & 15) == 0) {
+    // 16-byte loads, kUnroll of them in flight per thread before any compare
+    constexpr int kUnroll = 4;
+    const int nv = a.V_local >> 2;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (int base = threadIdx.x; base < nv; base += kThreads * kUnroll) {
+      float4 v[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (base + u * kThreads < nv) v[u] = __ldg(x4 + base + u * kThreads);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int j = base + u * kThreads;
+        if (j < nv) {
+          consider(v[u].x, 4 * j);
+          consider(v[u].y, 4 * j + 1);
+          consider(v[u].z, 4 * j + 2);
+          consider(v[u].w, 4 * j + 3);
+        }
+      }
+    }
+    for (int i = (nv << 2) + threadIdx.x; i < a.V_local; i += kThreads) consider(x[i], i);
+  } else {
+    for (int i = threadIdx.x; i < a.V_local; i += kThreads) consider(x[i], i);
   }
   for (int o = 16; o > 0; o >>= 1) {
     const unsigned long long ob = __shfl_xor_sync(0xffffffffu, best, o);

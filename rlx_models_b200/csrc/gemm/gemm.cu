@@ -100,14 +100,15 @@ void linear_launch(const LinearArgs& a, cudaStream_t st) {
     }
   }
   sp = std::max(1, std::min(sp, p.k_tiles));
-  if (sp > 1 && epi != gemm::EPI_ACC && (int64_t)tiles * gemm::kBM * BN > a.ws_elems) sp = 1;
+  if (sp > 1 && epi != gemm::EPI_ACC)  // one fp32 partial slice per split must fit the workspace
+    sp = (int)std::max<int64_t>(1, std::min<int64_t>(sp, a.ws_elems / ((int64_t)tiles * gemm::kBM * BN)));
   if (dit_epi) sp = 1;  // the activation / gate must see the full sum
   p.kt_per_split = (p.k_tiles + sp - 1) / sp;
   p.splits = (p.k_tiles + p.kt_per_split - 1) / p.kt_per_split;
   p.num_units = tiles * p.splits;
   if (epi == gemm::EPI_ACC && !sw) throw std::runtime_error("b200.linear: accumulate mode needs swap-AB (M <= 128)");
   if (p.splits > 1 && epi != gemm::EPI_ACC) {
-    if (a.ws_elems < (int64_t)tiles * gemm::kBM * BN || a.ws == nullptr)
+    if (a.ws_elems < (int64_t)p.splits * tiles * gemm::kBM * BN || a.ws == nullptr)
       throw std::runtime_error("b200.linear: split-K accumulator too small");
     if (a.sem_elems < tiles || a.sem == nullptr) throw std::runtime_error("b200.linear: semaphore buffer too small");
   }
@@ -203,11 +204,12 @@ void gemm_launch(const GemmArgs& a, cudaStream_t st) {
     }
   }
   sp = std::max(1, std::min(sp, p.k_tiles));
-  if (sp > 1 && (int64_t)tiles * gemm::kBM * BN > a.ws_elems) sp = 1;
+  if (sp > 1) sp = (int)std::max<int64_t>(1, std::min<int64_t>(sp, a.ws_elems / ((int64_t)tiles * gemm::kBM * BN)));
   p.kt_per_split = (p.k_tiles + sp - 1) / sp;
   p.splits = (p.k_tiles + p.kt_per_split - 1) / p.kt_per_split;
   p.num_units = tiles * p.splits;
-  if (p.splits > 1 && (a.ws == nullptr || a.sem == nullptr || a.sem_elems < tiles))
+  if (p.splits > 1 && (a.ws == nullptr || a.sem == nullptr || a.sem_elems < tiles ||
+                       a.ws_elems < (int64_t)p.splits * tiles * gemm::kBM * BN))
     throw std::runtime_error("b200.gemm: split-K buffers too small");
   p.C = a.c;
   p.ldc_i = a.ldc;

@@ -18,11 +18,12 @@
 //   warps 2..5  epilogue: tcgen05.ld 32x32b from TMEM -> registers -> fused
 //               epilogue -> global, overlapping the next tile's MMAs.
 //
-// Split-K (used for skinny decode GEMMs so that all SMs stream weights): each
-// split adds its fp32 partial tile into a per-tile L2 accumulator with vector
-// red.global.add; the last split of a tile (per-tile semaphore) reads the sum
-// once, zeroes the accumulator, runs the real epilogue and resets the
-// semaphore, so the next launch (or graph replay) starts from zero.
+// Split-K (used for skinny GEMMs so that all SMs stream weights): each split
+// stores its fp32 partial tile into its own workspace slice (L2); the last
+// split of a tile (per-tile semaphore) sums the slices in split order, runs the
+// real epilogue and resets the semaphore. The fixed order keeps the result
+// independent of which split finished first (eager and graph-replayed runs,
+// and repeated runs, give the same bits).
 #pragma once
 
 #include "../common/b200.cuh"
@@ -545,7 +546,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t t_row = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
       const int i = m_tile * kBM + row;
       const int jt = n_tile * BN;
-      // fp32 accumulator of this tile in L2 (split-K); zero between uses
+      // split-K: each split's fp32 partial of this tile in its own workspace slice
+      // [split][tile][kBM][BN]; the last split to arrive sums the slices in split
+      // order, so the result does not depend on which split finished first
+      const int64_t slice = (int64_t)(p.num_m * p.num_n) * (kBM * BN);
       float* acc_row = p.ws + (int64_t)tile * (kBM * BN) + (int64_t)row * BN;
 
       if (EPI == EPI_ACC) {
@@ -584,8 +588,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       if (p.splits > 1) {
-        // Add this split's partial into the shared fp32 tile (fire-and-forget
-        // vector reductions in L2), release TMEM, then count arrivals.
+        // Store this split's partial into its slice (L2), release TMEM, then
+        // count arrivals.
+        float* my_row = acc_row + ks * slice;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -593,8 +598,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_wait_ld();
 #pragma unroll
           for (int q = 0; q < 8; ++q)
-            red_add_v4(acc_row + c * 32 + q * 4, __uint_as_float(r[q * 4]), __uint_as_float(r[q * 4 + 1]),
-                       __uint_as_float(r[q * 4 + 2]), __uint_as_float(r[q * 4 + 3]));
+            __stcg(reinterpret_cast<float4*>(my_row + c * 32) + q,
+                   make_float4(__uint_as_float(r[q * 4]), __uint_as_float(r[q * 4 + 1]),
+                               __uint_as_float(r[q * 4 + 2]), __uint_as_float(r[q * 4 + 3])));
         }
         tc_fence_before();
         __syncwarp();
@@ -614,16 +620,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Fetch 32 accumulator columns [c*32, c*32+32) of this thread's row.
       auto fetch = [&](int c, float (&v)[32]) {
         if (p.splits > 1) {
-          float4 w[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) w[q] = __ldcg(reinterpret_cast<const float4*>(acc_row + c * 32) + q);
+          for (int t = 0; t < 32; ++t) v[t] = 0.f;
+#pragma unroll 1
+          for (int sp = 0; sp < p.splits; ++sp) {
+            float4 w[8];
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            v[q * 4] = w[q].x;
-            v[q * 4 + 1] = w[q].y;
-            v[q * 4 + 2] = w[q].z;
-            v[q * 4 + 3] = w[q].w;
-            __stcg(reinterpret_cast<float4*>(acc_row + c * 32) + q, make_float4(0.f, 0.f, 0.f, 0.f));
+            for (int q = 0; q < 8; ++q) w[q] = __ldcg(reinterpret_cast<const float4*>(acc_row + sp * slice + c * 32) + q);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              v[q * 4] += w[q].x;
+              v[q * 4 + 1] += w[q].y;
+              v[q * 4 + 2] += w[q].z;
+              v[q * 4 + 3] += w[q].w;
+            }
           }
         } else {
           uint32_t r[32];
