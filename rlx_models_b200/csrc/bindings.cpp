@@ -1268,16 +1268,15 @@ void scale_by(Tensor& t, const Tensor& g) {
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void tp_argmax(const Tensor& logits, int64_t v_offset, Tensor& own_pairs, const Tensor& peer_pairs,
-               const Tensor& peer_flags, const Tensor& flags, Tensor& epoch, Tensor& cta_ctr, Tensor& out,
-               int64_t max_rows, int64_t rank, int64_t world, Tensor& status) {
+void tp_argmax(const Tensor& logits, int64_t v_offset, Tensor& own_pairs, const Tensor& peer_pairs, Tensor& epoch,
+               Tensor& cta_ctr, Tensor& out, int64_t max_rows, int64_t rank, int64_t world, Tensor& status) {
   check_cuda(logits, "logits");
   TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
               "b200.tp_argmax: fp32 [R, V/world] logits");
   TORCH_CHECK(out.scalar_type() == at::kInt && out.numel() >= logits.size(0), "b200.tp_argmax: out");
-  TORCH_CHECK(peer_pairs.scalar_type() == at::kLong && peer_pairs.numel() == world && peer_flags.numel() == world &&
-                  cta_ctr.numel() >= 2,
-              "b200.tp_argmax: peer tables / counters");
+  TORCH_CHECK(peer_pairs.scalar_type() == at::kLong && peer_pairs.numel() == world && cta_ctr.numel() >= 1 &&
+                  own_pairs.numel() >= 2 * max_rows * world,
+              "b200.tp_argmax: key buffers / peer table / counter");
   c10::cuda::CUDAGuard g(logits.device());
   b200::TpArgmaxArgs a{};
   a.logits = logits.data_ptr<float>();
@@ -1286,8 +1285,6 @@ void tp_argmax(const Tensor& logits, int64_t v_offset, Tensor& own_pairs, const 
   a.v_offset = (int)v_offset;
   a.own_pairs = reinterpret_cast<unsigned long long*>(own_pairs.data_ptr());
   a.peer_pairs = reinterpret_cast<unsigned long long* const*>(peer_pairs.data_ptr<int64_t>());
-  a.peer_flags = reinterpret_cast<unsigned* const*>(peer_flags.data_ptr<int64_t>());
-  a.flags = reinterpret_cast<const unsigned*>(flags.data_ptr<int32_t>());
   a.epoch = reinterpret_cast<unsigned*>(epoch.data_ptr<int32_t>());
   a.cta_ctr = reinterpret_cast<unsigned*>(cta_ctr.data_ptr<int32_t>());
   a.out = out.data_ptr<int32_t>();

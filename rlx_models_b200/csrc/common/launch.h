@@ -199,12 +199,10 @@ struct TpArgmaxArgs {
   const float* logits;                    // [R][ld] fp32, this rank's vocab shard
   int64_t ld;
   int V_local, v_offset;                  // shard width, first global id of the shard
-  unsigned long long* own_pairs;          // this rank's [2][max_rows] packed keys
-  unsigned long long* const* peer_pairs;  // [world] every rank's pair buffer
-  unsigned* const* peer_flags;            // [world] every rank's flag array [world]
-  const unsigned* flags;                  // local flags [world]
+  unsigned long long* own_pairs;          // this rank's [2][max_rows][world] tagged keys
+  unsigned long long* const* peer_pairs;  // [world] every rank's key buffer
   unsigned* epoch;
-  unsigned* cta_ctr;                      // [2] arrival / departure counters
+  unsigned* cta_ctr;                      // [1] departure counter
   int32_t* out;                           // [R] global token ids
   int R, max_rows, world, rank;
   int* status;

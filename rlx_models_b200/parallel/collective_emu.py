@@ -9,7 +9,9 @@ the peer tables points at a separate buffer in this GPU's memory (the same
 number of bytes the real rank reads from its peers, but from local HBM / L2
 instead of over NVLink), and every flag the kernel waits on is set before the
 launch, so no launch waits for another (the kernels' own flag stores go to a
-separate dummy array). What this measures is the kernel's own cost - its
+separate dummy array; the argmax, whose keys carry their op's tag, gets the
+other ranks' keys written before each launch, a small fill kernel that the
+graph timing includes). What this measures is the kernel's own cost - its
 loads, reduction, norm and stores - with the NVLink transfer and the
 cross-rank skew taken out; the multi-rank timing (``comm_bench``) adds them
 back. Each op runs ``--iters`` plain launches (ncu) and, with ``--time``,
@@ -75,15 +77,19 @@ def build(op: str, world: int, M: int, H: int, dev, vocab: int = 151936, k: int 
     if op == "argmax":
         R, Vl, max_rows = M, vocab // world, 256
         logits = torch.randn(R, Vl, device=dev, generator=g)
-        pairs = [torch.zeros(2, max_rows, dtype=torch.int64, device=dev) for _ in range(world)]
-        peer_pairs = _ptrs(pairs, dev)
-        ctr = torch.zeros(3, dtype=torch.int32, device=dev)
+        keys = torch.zeros(2, max_rows, world, dtype=torch.int64, device=dev)
+        peer_keys = _ptrs([keys] * world, dev)
+        ctr = torch.zeros(2, dtype=torch.int32, device=dev)
         picked = torch.empty(R, dtype=torch.int32, device=dev)
-        keep.update(logits=logits, pairs=pairs, peer_pairs=peer_pairs, ctr=ctr, picked=picked)
+        keep.update(logits=logits, keys=keys, peer_keys=peer_keys, ctr=ctr, picked=picked)
 
         def launch():
-            ext().tp_argmax(logits, rank * Vl, pairs[rank], peer_pairs, peer_flags, flags, ctr[0:1], ctr[1:3], picked,
-                            max_rows, rank, world, s.status)
+            # the other ranks' keys of this op: value bits 0 (lose to any real value) and this
+            # op's tag, computed on the device from the epoch counter (so graph replays stay valid)
+            e = ctr[0:1].long() + 1
+            keys.index_copy_(0, e & 1, (1 + e % 8191).view(1, 1, 1).expand(1, max_rows, world).contiguous())
+            ext().tp_argmax(logits, rank * Vl, keys, peer_keys, ctr[0:1], ctr[1:2], picked, max_rows, rank, world,
+                            s.status)
         return launch, (world - 1) * R * 8, keep
     if op == "combine":
         T = M

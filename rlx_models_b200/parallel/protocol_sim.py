@@ -2,7 +2,8 @@
 
 The peer-memory kernels (``csrc/comm/tp_fused.cu`` ``ar_pull_norm`` /
 ``ar2_norm``, ``csrc/comm/tp_sample.cu`` ``tp_argmax``) synchronise ranks with
-epoch flags and reuse their buffers without host involvement. Their
+epoch flags (or, for the argmax, keys that carry their op's tag) and reuse
+their buffers without host involvement. Their
 correctness rests on ordering arguments ("a rank rewrites this slot only after
 every peer passed the next barrier, which it does after finishing its reads").
 This module replays each protocol step by step on the host:
@@ -249,37 +250,39 @@ def tp_decode_ops(world: int, M: int, n_ops: int, seed: int, rows: int = 8, mode
 # vocab-parallel greedy argmax
 # ---------------------------------------------------------------------------
 
-def tp_argmax_ops(world: int, R: int, n_ops: int, seed: int) -> int:
-    """``tp_argmax_kernel``: pair buffers double-buffered by epoch parity, one flag barrier."""
+def tp_argmax_ops(world: int, R: int, n_ops: int, seed: int, buffers: int = 2) -> int:
+    """``tp_argmax_kernel``: every rank pushes row r's tagged key into slot
+    [parity][r][rank] of every rank, then polls its own slots [parity][r][q]
+    until each holds a key, reads and clears them. A writer must never find an
+    unread key in a slot, and a reader must only ever find this op's key.
+    ``buffers=1`` models a single-buffered variant (for the negative test)."""
     sim = Sim(world, seed)
     for q in range(world):
         m = sim.mem(q)
-        m["pairs"] = [[None] * R for _ in range(2)]
-        m["flags"] = [0] * world
-        m["ctr"] = dict(epoch=0, arr=0, dep=0)
+        m["keys"] = [[[None] * world for _ in range(R)] for _ in range(2)]
+        m["ctr"] = dict(epoch=0, dep=0)
 
     def kernel(rank, op):
         def cta(row):
             def g():
                 m = sim.mem(rank)
                 e = m["ctr"]["epoch"] + 1
-                par = e & 1
+                par = e % buffers
                 _check(e == op, f"rank {rank}: epoch {e} for op {op}")
-                m["pairs"][par][row] = op
-                yield
-                m["ctr"]["arr"] += 1
-                if m["ctr"]["arr"] == R:
-                    for q in range(world):
-                        sim.mem(q)["flags"][rank] = e
-                        yield
-                yield Wait(lambda: all(f >= e for f in m["flags"]))
                 for q in range(world):
-                    v = sim.mem(q)["pairs"][par][row]
-                    _check(v == op, f"rank {rank} op {op}: read rank {q} pairs[{par}][{row}] = {v}")
+                    slot = sim.mem(q)["keys"][par][row]
+                    _check(slot[rank] is None,
+                           f"rank {rank} op {op}: rank {q} slot [{par}][{row}][{rank}] still holds op {slot[rank]}")
+                    slot[rank] = op
+                    yield
+                for q in range(world):
+                    yield Wait(lambda q=q: m["keys"][par][row][q] is not None)
+                    v = m["keys"][par][row][q]
+                    _check(v == op, f"rank {rank} op {op}: slot [{par}][{row}][{q}] holds op {v}")
+                    m["keys"][par][row][q] = None
                     yield
                 m["ctr"]["dep"] += 1
                 if m["ctr"]["dep"] == R:
-                    m["ctr"]["arr"] = 0
                     m["ctr"]["dep"] = 0
                     m["ctr"]["epoch"] = e
             return g

@@ -40,24 +40,21 @@ from .tp import NcclTPComm
 
 class PeerArgmax:
     """Vocab-parallel greedy choice in one kernel over NVLink peer memory
-    (``csrc/comm/tp_sample.cu``): local shard argmax, packed (value, index)
-    keys exchanged through a symmetric buffer, one flag barrier; every rank
-    gets the global argmax (lowest index on ties). Replaces the local argmax +
-    NCCL all-gather + selection of the baseline communicator."""
+    (``csrc/comm/tp_sample.cu``): local shard argmax packed into a key that
+    carries its op's tag, pushed into every rank's key buffer, polled by tag
+    (no flags, no fences); every rank gets the global argmax (lowest index on
+    ties). Replaces the local argmax + NCCL all-gather + selection of the
+    baseline communicator."""
 
     def __init__(self, rank: int, world: int, device, max_rows: int = 256, group=None):
         self.rank, self.world, self.max_rows = rank, world, max_rows
         lay = Layout()
-        o_pairs = lay.add("pairs", (2, max_rows), torch.int64)
-        o_flags = lay.add("flags", (world,), torch.int32)
+        o_keys = lay.add("keys", (2, max_rows, world), torch.int64)
         self.heap = SymmetricHeap(lay.nbytes, device, group)
-        self.pairs = self.heap.view(o_pairs, (2, max_rows), torch.int64)
-        self.pairs.zero_()
-        self.flags = self.heap.view(o_flags, (world,), torch.int32)
-        self.flags.zero_()
-        self.peer_pairs = self.heap.peer_ptr_table(o_pairs)
-        self.peer_flags = self.heap.peer_ptr_table(o_flags)
-        self.ctr = torch.zeros(3, dtype=torch.int32, device=device)  # [epoch, arrivals, departures]
+        self.keys = self.heap.view(o_keys, (2, max_rows, world), torch.int64)
+        self.keys.zero_()
+        self.peer_keys = self.heap.peer_ptr_table(o_keys)
+        self.ctr = torch.zeros(2, dtype=torch.int32, device=device)  # [epoch, departures]
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
 
@@ -66,9 +63,8 @@ class PeerArgmax:
         if R > self.max_rows:
             raise ValueError(f"PeerArgmax: {R} rows > {self.max_rows}")
         ops._count(1)
-        ext().tp_argmax(logits_local, self.rank * Vl, self.pairs, self.peer_pairs, self.peer_flags, self.flags,
-                        self.ctr[0:1], self.ctr[1:3], out, self.max_rows, self.rank, self.world,
-                        scratch(logits_local.device).status)
+        ext().tp_argmax(logits_local, self.rank * Vl, self.keys, self.peer_keys, self.ctr[0:1], self.ctr[1:2], out,
+                        self.max_rows, self.rank, self.world, scratch(logits_local.device).status)
         return out
 
     def close(self):

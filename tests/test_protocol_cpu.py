@@ -20,6 +20,18 @@ def test_tp_argmax_protocol(world, R):
         ps.tp_argmax_ops(world, R, n_ops=5, seed=seed)
 
 
+def test_emulator_catches_single_buffered_argmax_keys():
+    """With one key buffer a fast rank's next op pushes its key into a slot
+    whose previous key a slow peer has not read yet."""
+    caught = 0
+    for seed in range(40):
+        try:
+            ps.tp_argmax_ops(4, 2, n_ops=6, seed=seed, buffers=1)
+        except ps.ProtocolError:
+            caught += 1
+    assert caught > 0
+
+
 def test_emulator_catches_single_buffered_accumulator(monkeypatch):
     """Accumulating every op into the same parity (no double buffering) lets a
     fast rank's next GEMM overwrite a partial a slow peer is still reading."""
