@@ -287,7 +287,11 @@ namespace tpc {
 // parity accumulator, which every rank has finished reading (they all passed
 // this op's barrier, hence finished the previous op), so the next GEMM can
 // accumulate into it. One barrier per op; no NCCL call.
-constexpr int kPullThreads = 256;
+// Threads per CTA: one 8-column chunk of the row per thread up to 512 threads
+// (H = 4096: every peer load of a thread is issued in one round), 512 threads
+// with 2-4 chunks above that.
+constexpr int kPullThreads = 512;
+__host__ __device__ constexpr int pull_threads(int H) { return H / 8 < kPullThreads ? H / 8 : kPullThreads; }
 constexpr int kMaxWorld = 8;
 
 // s[0..8) = sum over the world ranks of the 8 fp32 values at element offset
@@ -331,14 +335,14 @@ __global__ void __launch_bounds__(kPullThreads) ar_pull_norm_kernel(PullNormArgs
     __nv_bfloat16* hbuf = reinterpret_cast<__nv_bfloat16*>(a.h);
     const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
-    constexpr int kMaxChunks = 4;  // H <= 256 * 8 * 4
-    const int nch = H / (kPullThreads * 8);
+    constexpr int kMaxChunks = 4;  // H <= 512 * 8 * 4
+    const int nch = H / ((int)blockDim.x * 8);
     float v[kMaxChunks][8];
     float ss = 0.f;
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
       if (c >= nch) break;
-      const int col = (c * kPullThreads + threadIdx.x) * 8;
+      const int col = (c * (int)blockDim.x + threadIdx.x) * 8;
       float s[8];
       sum_peer_rows(a.peer_acc, a.world, (int64_t)r * H + col, s);
       const uint4 hv = *reinterpret_cast<const uint4*>(hbuf + (int64_t)r * H + col);
@@ -359,7 +363,7 @@ __global__ void __launch_bounds__(kPullThreads) ar_pull_norm_kernel(PullNormArgs
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
     if (threadIdx.x < 32) {
-      float t = threadIdx.x < kPullThreads / 32 ? red[threadIdx.x] : 0.f;
+      float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
       if (threadIdx.x == 0) red[0] = t;
@@ -369,7 +373,7 @@ __global__ void __launch_bounds__(kPullThreads) ar_pull_norm_kernel(PullNormArgs
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
       if (c >= nch) break;
-      const int col = (c * kPullThreads + threadIdx.x) * 8;
+      const int col = (c * (int)blockDim.x + threadIdx.x) * 8;
       const uint4 wv = *reinterpret_cast<const uint4*>(nw + col);
       const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
       uint32_t o[4];
@@ -381,7 +385,7 @@ __global__ void __launch_bounds__(kPullThreads) ar_pull_norm_kernel(PullNormArgs
   }
   if (r < a.zero_rows) {
     float4* z = reinterpret_cast<float4*>(a.zero_buf + (int64_t)r * H);
-    for (int i = threadIdx.x; i < H / 4; i += kPullThreads) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = threadIdx.x; i < H / 4; i += blockDim.x) z[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   // the last CTA publishes this op's epoch for the next op
   __syncthreads();
@@ -397,10 +401,10 @@ __global__ void __launch_bounds__(kPullThreads) ar_pull_norm_kernel(PullNormArgs
 
 void ar_pull_norm_launch(const PullNormArgs& a, cudaStream_t st) {
   if (a.world > tpc::kMaxWorld) throw std::runtime_error("b200.ar_pull_norm: at most 8 ranks");
-  if (a.H % (tpc::kPullThreads * 8) != 0 || a.H > tpc::kPullThreads * 8 * 4)
-    throw std::runtime_error("b200.ar_pull_norm: hidden must be a multiple of 2048 and <= 8192");
-  launch_pdl(tpc::ar_pull_norm_kernel, dim3(std::max(std::max(1, a.M), a.zero_rows)), dim3(tpc::kPullThreads), 0,
-             st, a);
+  const int nt = tpc::pull_threads(a.H);
+  if (a.H % 256 != 0 || a.H % (nt * 8) != 0 || a.H > nt * 8 * 4)
+    throw std::runtime_error("b200.ar_pull_norm: hidden must be a multiple of 256 and <= 16384");
+  launch_pdl(tpc::ar_pull_norm_kernel, dim3(std::max(std::max(1, a.M), a.zero_rows)), dim3(nt), 0, st, a);
 }
 }  // namespace b200
 
@@ -442,14 +446,14 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
     if (threadIdx.x < (unsigned)a.world) wait_flag_geq(a.flags + threadIdx.x, e, a.status, 700 + threadIdx.x);
     __syncthreads();
     const int r = a.rank * a.rpr + i;
-    constexpr int kMaxChunks = 4;  // H <= 256 * 8 * 4
-    const int nch = H / (kPullThreads * 8);
+    constexpr int kMaxChunks = 4;  // H <= 512 * 8 * 4
+    const int nch = H / ((int)blockDim.x * 8);
     float v[kMaxChunks][8];
     float ss = 0.f;
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
       if (c >= nch) break;
-      const int col = (c * kPullThreads + threadIdx.x) * 8;
+      const int col = (c * (int)blockDim.x + threadIdx.x) * 8;
       float sm[8];
       sum_peer_rows(a.peer_acc, a.world, (int64_t)r * H + col, sm);
       const uint4 hv = *reinterpret_cast<const uint4*>(hbuf + (int64_t)r * H + col);
@@ -470,7 +474,7 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
     if (threadIdx.x < 32) {
-      float t = threadIdx.x < kPullThreads / 32 ? red[threadIdx.x] : 0.f;
+      float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
       if (threadIdx.x == 0) red[0] = t;
@@ -482,7 +486,7 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
 #pragma unroll
     for (int c = 0; c < kMaxChunks; ++c) {
       if (c >= nch) break;
-      const int col = (c * kPullThreads + threadIdx.x) * 8;
+      const int col = (c * (int)blockDim.x + threadIdx.x) * 8;
       const uint4 wv = *reinterpret_cast<const uint4*>(nw + col);
       const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
       uint32_t o[4];
@@ -514,11 +518,11 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
         reinterpret_cast<const __nv_bfloat16*>(a.peer_res[owner]) + ((int64_t)a.rpr_max + j) * H);
     uint4* dh = reinterpret_cast<uint4*>(hbuf + (int64_t)i * H);
     uint4* dout = reinterpret_cast<uint4*>(out + (int64_t)i * H);
-    constexpr int kMaxIt = 4;  // H <= 256 * 8 * 4: every load of the row is issued before any store
+    constexpr int kMaxIt = 4;  // H <= 512 * 8 * 4: every load of the row is issued before any store
     uint4 vh[kMaxIt], vo[kMaxIt];
 #pragma unroll
     for (int it = 0; it < kMaxIt; ++it) {
-      const int c = it * kPullThreads + threadIdx.x;
+      const int c = it * (int)blockDim.x + threadIdx.x;
       if (c < H / 8) {
         vh[it] = __ldcg(sh + c);
         vo[it] = __ldcg(so + c);
@@ -526,7 +530,7 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
     }
 #pragma unroll
     for (int it = 0; it < kMaxIt; ++it) {
-      const int c = it * kPullThreads + threadIdx.x;
+      const int c = it * (int)blockDim.x + threadIdx.x;
       if (c < H / 8) {
         dh[c] = vh[it];
         dout[c] = vo[it];
@@ -535,7 +539,7 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
   }
   if (i < a.zero_rows) {
     float4* z = reinterpret_cast<float4*>(a.zero_buf + (int64_t)i * H);
-    for (int c = threadIdx.x; c < H / 4; c += kPullThreads) z[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int c = threadIdx.x; c < H / 4; c += blockDim.x) z[c] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -552,12 +556,12 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
 
 void ar2_norm_launch(const TwoShotNormArgs& a, cudaStream_t st) {
   if (a.world > tpc::kMaxWorld) throw std::runtime_error("b200.ar2_norm: at most 8 ranks");
-  if (a.H % (tpc::kPullThreads * 8) != 0 || a.H > tpc::kPullThreads * 8 * 4)
-    throw std::runtime_error("b200.ar2_norm: hidden must be a multiple of 2048 and <= 8192");
+  const int nt = tpc::pull_threads(a.H);
+  if (a.H % 256 != 0 || a.H % (nt * 8) != 0 || a.H > nt * 8 * 4)
+    throw std::runtime_error("b200.ar2_norm: hidden must be a multiple of 256 and <= 16384");
   if (a.rpr <= 0 || a.rpr > a.rpr_max || (int64_t)a.rpr * a.world < a.M)
     throw std::runtime_error("b200.ar2_norm: row split does not cover the rows");
-  launch_pdl(tpc::ar2_norm_kernel, dim3(std::max(std::max(1, a.M), a.zero_rows)), dim3(tpc::kPullThreads), 0, st,
-             a);
+  launch_pdl(tpc::ar2_norm_kernel, dim3(std::max(std::max(1, a.M), a.zero_rows)), dim3(nt), 0, st, a);
 }
 }  // namespace b200
 
