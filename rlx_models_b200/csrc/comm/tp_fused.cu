@@ -416,20 +416,27 @@ namespace tpc {
 // slot, a replicated bf16 residual stream), but each rank reduces only the
 // rows it owns (row i belongs to rank i / rpr) and the others fetch the
 // finished rows:
-//   barrier 1  CTA 0 announces "partial ready" to every rank; the CTAs of the
-//              owned rows wait for all ranks' announcements;
-//   phase A    owned row: sum the world partials over NVLink (fp32), add the
-//              residual, RMSNorm; store the new residual row and the normalised
-//              row in this rank's result slot; the last of these CTAs
+//   barrier 1  CTA 0 announces "partial ready" to every rank; the phase-A CTAs
+//              wait for all ranks' announcements;
+//   phase A    work item = (owned row, 512-column slice), spread over the CTAs so
+//              the remote reads of the owned rows use many SMs: sum the
+//              world partials of the slice over NVLink (fp32), add the
+//              residual, store the new residual slice (bf16) and the slice's
+//              sum of squares in this rank's result slot; the last item
 //              announces "rows ready" to every rank (barrier 2);
-//   phase B    every CTA waits for barrier 2 and copies row i (residual and
-//              normalised) from its owner's result slot.
-// Per rank, each op moves M*H*4/world bytes of partials in and M*H*4 bytes of
-// results in over NVLink, against M*H*4*(world-1) bytes of partials for the
-// one-shot pull: the two-shot form wins once the partials outweigh the extra
-// barrier. Result slots are reused without double buffering: a rank rewrites
-// its slot in op k+1 only after every rank announced op k+1's partial, which
-// each does after its op-k kernel (and its phase-B reads) completed.
+//   phase B    every CTA waits for barrier 2, copies row i's new residual and
+//              its per-slice sums of squares from the owner, and applies the
+//              RMSNorm itself (the owner never writes a normalised row).
+// Per rank, each op moves M*H*4/world bytes of partials and M*H*2 bytes of
+// residual rows in over NVLink, against M*H*4*(world-1) bytes of partials for
+// the one-shot pull. Result slots are reused without double buffering: a rank
+// rewrites its slot in op k+1 only after every rank announced op k+1's
+// partial, which each does after its op-k kernel (and its phase-B reads)
+// completed. One system fence per phase-A CTA (after a CTA barrier, so it
+// covers every thread's stores) and one before the barrier-2 flags.
+constexpr int kSliceCols = 512;              // phase-A item width
+constexpr int kSliceThreads = kSliceCols / 8;  // 64 threads, 8 columns each
+
 __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs a) {
   __shared__ float red[kPullThreads / 32];
   pdl_wait();
@@ -437,71 +444,57 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
   const unsigned e = *reinterpret_cast<volatile unsigned*>(a.epoch) + 1u;
   const int H = a.H;
   const int i = blockIdx.x;
+  const int S = H / kSliceCols;
   const int n_my = max(0, min(a.rpr, a.M - a.rank * a.rpr));
+  const int n_items = n_my * S;
   __nv_bfloat16* hbuf = reinterpret_cast<__nv_bfloat16*>(a.h);
   __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
-  __nv_bfloat16* res = reinterpret_cast<__nv_bfloat16*>(a.own_res);  // [2][rpr_max][H]
+  __nv_bfloat16* res = reinterpret_cast<__nv_bfloat16*>(a.own_res);  // [rpr_max][H] new residual rows
+  float* ssq = reinterpret_cast<float*>(res + (int64_t)a.rpr_max * H);  // [rpr_max][S] slice sums of squares
   if (i == 0 && threadIdx.x < (unsigned)a.world) st_release_sys_u32(a.peer_flags[threadIdx.x] + a.rank, e);
-  if (i < n_my) {
+  if (i < n_items) {
     if (threadIdx.x < (unsigned)a.world) wait_flag_geq(a.flags + threadIdx.x, e, a.status, 700 + threadIdx.x);
     __syncthreads();
-    const int r = a.rank * a.rpr + i;
-    constexpr int kMaxChunks = 4;  // H <= 512 * 8 * 4
-    const int nch = H / ((int)blockDim.x * 8);
-    float v[kMaxChunks][8];
-    float ss = 0.f;
+    // items i, i + grid, ...: the grid stays within one CTA per SM, so every CTA
+    // (all of which wait at barrier 2 below) is resident at once
+    for (int item = i; item < n_items; item += gridDim.x) {
+      const int li = item / S, sl = item % S;
+      const int r = a.rank * a.rpr + li;
+      float ss = 0.f;
+      if (threadIdx.x < (unsigned)kSliceThreads) {
+        const int col = sl * kSliceCols + threadIdx.x * 8;
+        float sm[8];
+        sum_peer_rows(a.peer_acc, a.world, (int64_t)r * H + col, sm);
+        const uint4 hv = *reinterpret_cast<const uint4*>(hbuf + (int64_t)r * H + col);
+        const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
+        uint32_t o[4];
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-      if (c >= nch) break;
-      const int col = (c * (int)blockDim.x + threadIdx.x) * 8;
-      float sm[8];
-      sum_peer_rows(a.peer_acc, a.world, (int64_t)r * H + col, sm);
-      const uint4 hv = *reinterpret_cast<const uint4*>(hbuf + (int64_t)r * H + col);
-      const uint32_t hw[4] = {hv.x, hv.y, hv.z, hv.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        o[k] = pack_bf16x2(bf16_lo(hw[k]) + __bfloat162float(__float2bfloat16(sm[2 * k])),
-                           bf16_hi(hw[k]) + __bfloat162float(__float2bfloat16(sm[2 * k + 1])));
-        v[c][2 * k] = bf16_lo(o[k]);
-        v[c][2 * k + 1] = bf16_hi(o[k]);
-        ss += v[c][2 * k] * v[c][2 * k] + v[c][2 * k + 1] * v[c][2 * k + 1];
+        for (int k = 0; k < 4; ++k) {
+          o[k] = pack_bf16x2(bf16_lo(hw[k]) + __bfloat162float(__float2bfloat16(sm[2 * k])),
+                             bf16_hi(hw[k]) + __bfloat162float(__float2bfloat16(sm[2 * k + 1])));
+          const float lo = bf16_lo(o[k]), hi = bf16_hi(o[k]);
+          ss += lo * lo + hi * hi;
+        }
+        *reinterpret_cast<uint4*>(res + (int64_t)li * H + col) = make_uint4(o[0], o[1], o[2], o[3]);
       }
-      *reinterpret_cast<uint4*>(res + (int64_t)i * H + col) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-      float t = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      if ((threadIdx.x & 31) == 0 && threadIdx.x < (unsigned)kSliceThreads) red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float t = 0.f;
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-      if (threadIdx.x == 0) red[0] = t;
-    }
-    __syncthreads();
-    const float inv = rsqrtf(red[0] / (float)H + a.eps);
-    const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
-    __nv_bfloat16* res_out = res + (int64_t)a.rpr_max * H;
-#pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
-      if (c >= nch) break;
-      const int col = (c * (int)blockDim.x + threadIdx.x) * 8;
-      const uint4 wv = *reinterpret_cast<const uint4*>(nw + col);
-      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        o[k] = pack_bf16x2(v[c][2 * k] * inv * bf16_lo(ww[k]), v[c][2 * k + 1] * inv * bf16_hi(ww[k]));
-      *reinterpret_cast<uint4*>(res_out + (int64_t)i * H + col) = make_uint4(o[0], o[1], o[2], o[3]);
-    }
-    // every thread's result stores are ordered before thread 0's system fence by
-    // the barrier (fence cumulativity), so one fence per CTA publishes them
-    __syncthreads();
-    if (threadIdx.x == 0) __threadfence_system();
-    if (threadIdx.x == 0 && atomicAdd(a.cta_ctr, 1u) == (unsigned)n_my - 1) {
-      __threadfence_system();  // one system fence covers every rank's flag store below
-      for (int q = 0; q < a.world; ++q) st_relaxed_sys_u32(a.peer_flags[q] + a.world + a.rank, e);
+        for (int w = 0; w < kSliceThreads / 32; ++w) t += red[w];
+        ssq[li * S + sl] = t;
+        // every thread's stores are ordered before this fence by the barrier above
+        // (fence cumulativity): one system fence per item publishes the slice
+        __threadfence_system();
+        if (atomicAdd(a.cta_ctr, 1u) == (unsigned)n_items - 1) {
+          __threadfence_system();  // one system fence covers every rank's flag store below
+          for (int q = 0; q < a.world; ++q) st_relaxed_sys_u32(a.peer_flags[q] + a.world + a.rank, e);
+        }
+      }
+      __syncthreads();  // red[] is reused by the next item
     }
   } else if (n_my == 0 && i == 0 && threadIdx.x == 0) {
     for (int q = 0; q < a.world; ++q) st_release_sys_u32(a.peer_flags[q] + a.world + a.rank, e);
@@ -512,28 +505,40 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
   __syncthreads();
   if (i < a.M) {
     const int owner = i / a.rpr, j = i % a.rpr;
-    const uint4* sh = reinterpret_cast<const uint4*>(
-        reinterpret_cast<const __nv_bfloat16*>(a.peer_res[owner]) + (int64_t)j * H);
-    const uint4* so = reinterpret_cast<const uint4*>(
-        reinterpret_cast<const __nv_bfloat16*>(a.peer_res[owner]) + ((int64_t)a.rpr_max + j) * H);
-    uint4* dh = reinterpret_cast<uint4*>(hbuf + (int64_t)i * H);
-    uint4* dout = reinterpret_cast<uint4*>(out + (int64_t)i * H);
+    const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(a.peer_res[owner]);
+    const uint4* sh = reinterpret_cast<const uint4*>(src + (int64_t)j * H);
+    const float* sq = reinterpret_cast<const float*>(src + (int64_t)a.rpr_max * H) + j * S;
     constexpr int kMaxIt = 4;  // H <= 512 * 8 * 4: every load of the row is issued before any store
-    uint4 vh[kMaxIt], vo[kMaxIt];
+    uint4 vh[kMaxIt];
 #pragma unroll
     for (int it = 0; it < kMaxIt; ++it) {
       const int c = it * (int)blockDim.x + threadIdx.x;
-      if (c < H / 8) {
-        vh[it] = __ldcg(sh + c);
-        vo[it] = __ldcg(so + c);
-      }
+      if (c < H / 8) vh[it] = __ldcg(sh + c);
     }
+    if (threadIdx.x < 32) {
+      float t = threadIdx.x < (unsigned)S ? __ldcg(sq + threadIdx.x) : 0.f;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+      if (threadIdx.x == 0) red[0] = t;
+    }
+    __syncthreads();
+    const float inv = rsqrtf(red[0] / (float)H + a.eps);
+    const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
+    uint4* dh = reinterpret_cast<uint4*>(hbuf + (int64_t)i * H);
+    uint4* dout = reinterpret_cast<uint4*>(out + (int64_t)i * H);
 #pragma unroll
     for (int it = 0; it < kMaxIt; ++it) {
       const int c = it * (int)blockDim.x + threadIdx.x;
       if (c < H / 8) {
         dh[c] = vh[it];
-        dout[c] = vo[it];
+        const uint4 wv = *reinterpret_cast<const uint4*>(nw + c * 8);
+        const uint32_t hw[4] = {vh[it].x, vh[it].y, vh[it].z, vh[it].w};
+        const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          o[k] = pack_bf16x2(bf16_lo(hw[k]) * inv * bf16_lo(ww[k]), bf16_hi(hw[k]) * inv * bf16_hi(ww[k]));
+        dout[c] = make_uint4(o[0], o[1], o[2], o[3]);
       }
     }
   }
@@ -557,11 +562,15 @@ __global__ void __launch_bounds__(kPullThreads) ar2_norm_kernel(TwoShotNormArgs 
 void ar2_norm_launch(const TwoShotNormArgs& a, cudaStream_t st) {
   if (a.world > tpc::kMaxWorld) throw std::runtime_error("b200.ar2_norm: at most 8 ranks");
   const int nt = tpc::pull_threads(a.H);
-  if (a.H % 256 != 0 || a.H % (nt * 8) != 0 || a.H > nt * 8 * 4)
-    throw std::runtime_error("b200.ar2_norm: hidden must be a multiple of 256 and <= 16384");
+  if (a.H % tpc::kSliceCols != 0 || a.H % (nt * 8) != 0 || a.H > nt * 8 * 4 || a.H / tpc::kSliceCols > 32)
+    throw std::runtime_error("b200.ar2_norm: hidden must be a multiple of 512 and <= 16384");
   if (a.rpr <= 0 || a.rpr > a.rpr_max || (int64_t)a.rpr * a.world < a.M)
     throw std::runtime_error("b200.ar2_norm: row split does not cover the rows");
-  launch_pdl(tpc::ar2_norm_kernel, dim3(std::max(std::max(1, a.M), a.zero_rows)), dim3(nt), 0, st, a);
+  // every CTA waits at barrier 2, which the phase-A CTAs release: the grid (at most
+  // 128 CTAs, one per SM at this block size) must be resident at once
+  const int grid = std::max(std::max(1, a.M), a.zero_rows);
+  if (grid > 128) throw std::runtime_error("b200.ar2_norm: at most 128 rows per op");
+  launch_pdl(tpc::ar2_norm_kernel, dim3(grid), dim3(nt), 0, st, a);
 }
 }  // namespace b200
 

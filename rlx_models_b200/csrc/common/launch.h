@@ -140,7 +140,8 @@ void ar_pull_norm_launch(const PullNormArgs& a, cudaStream_t st);
 // see comm/tp_fused.cu ar2_norm_kernel.
 struct TwoShotNormArgs {
   const float* const* peer_acc;  // [world] each rank's fp32 [rows][H] partial (this op's parity)
-  const void* const* peer_res;   // [world] each rank's bf16 [2][rpr_max][H] result slot
+  const void* const* peer_res;   // [world] each rank's result slot: bf16 [rpr_max][H] new residual rows,
+                                 // then fp32 [rpr_max][H / 512] slice sums of squares (within 2*rpr_max*H bf16)
   void* own_res;                 // this rank's result slot
   unsigned* const* peer_flags;   // [world] each rank's flag array [2][world]
   const unsigned* flags;         // local flags [2][world]

@@ -8,8 +8,8 @@ captured here as ONE rank of a ``--world``-rank job on one GPU: every entry of
 the peer tables points at a separate buffer in this GPU's memory (the same
 number of bytes the real rank reads from its peers, but from local HBM / L2
 instead of over NVLink), and every flag the kernel waits on is set before the
-launch, so no launch waits for another (the kernels' own flag stores go to a
-separate dummy array; the argmax, whose keys carry their op's tag, gets the
+launch, so no launch waits for another (the flag stores meant for other ranks
+go to a dummy array, the ones for this rank to its real flags; the argmax, whose keys carry their op's tag, gets the
 other ranks' keys written before each launch, a small fill kernel that the
 graph timing includes). What this measures is the kernel's own cost - its
 loads, reduction, norm and stores - with the NVLink transfer and the
@@ -40,9 +40,14 @@ def build(op: str, world: int, M: int, H: int, dev, vocab: int = 151936, k: int 
     s = scratch(dev)
     g = torch.Generator(device=dev).manual_seed(0)
     rank = 0
+    # the other ranks' flags preset; this rank's own entries are raised by the kernel
+    # itself (its flag stores to "rank 0" land in the real flag array), so a kernel
+    # that waits on its own CTAs (the two-shot reduction's barrier 2) still orders them
     flags = torch.full((2 * world,), FLAG_SET, dtype=torch.int32, device=dev)
+    flags[rank] = 0
+    flags[world + rank] = 0
     dummy = torch.zeros(2 * world, dtype=torch.int32, device=dev)
-    peer_flags = _ptrs([dummy] * world, dev)
+    peer_flags = _ptrs([flags if q == rank else dummy for q in range(world)], dev)
     h = (torch.randn(M, H, device=dev, generator=g) * 0.1).bfloat16()
     nw = torch.ones(H, device=dev, dtype=torch.bfloat16)
     out = torch.empty_like(h)
@@ -64,6 +69,7 @@ def build(op: str, world: int, M: int, H: int, dev, vocab: int = 151936, k: int 
             return launch, (world - 1) * M * H * 4, keep
         rpr_max = (rows + world - 1) // world
         rpr = (M + world - 1) // world
+        # result slots: [rpr_max][H] bf16 residual rows, then fp32 slice sums of squares
         res = [torch.zeros(2, rpr_max, H, device=dev, dtype=torch.bfloat16) for _ in range(world)]
         peer_res = _ptrs(res, dev)
         ctr2 = torch.zeros(3, dtype=torch.int32, device=dev)
@@ -72,8 +78,9 @@ def build(op: str, world: int, M: int, H: int, dev, vocab: int = 151936, k: int 
         def launch():
             ext().ar2_norm(peer_acc, peer_res, res[rank], peer_flags, flags, zero, rows, h, nw, out, ctr2[0:1],
                            ctr2[1:3], rank, world, rpr, rpr_max, 1e-6, s.status)
-        # reduce-scatter reads (fp32, own rows from every peer) + all-gather reads (bf16 result rows)
-        return launch, (world - 1) * rpr * H * 4 + (world - 1) * rpr * H * 2, keep
+        # reduce-scatter reads (fp32, owned rows from every peer) + gather reads (bf16 residual rows
+        # of the rows other ranks own, plus their slice sums of squares)
+        return launch, (world - 1) * rpr * H * 4 + (world - 1) * rpr * (H * 2 + H // 512 * 4), keep
     if op == "argmax":
         R, Vl, max_rows = M, vocab // world, 256
         logits = torch.randn(R, Vl, device=dev, generator=g)

@@ -126,7 +126,7 @@ def setup_tp(sim: Sim, rows: int):
         m = sim.mem(q)
         m["acc"] = [[ZERO] * rows for _ in range(2)]
         m["flags"] = [0] * W
-        m["res"] = [None] * rpr_max
+        m["res"] = {}  # (owned row, slice) -> op that wrote it
         m["flags2"] = [[0] * W for _ in range(2)]
         m["out"] = [None] * rows
         m["ctr1"] = dict(epoch=0, dep=0)
@@ -177,11 +177,14 @@ def ar_pull(sim: Sim, rank: int, op: int, par: int, M: int, rows: int):
     sim.launch(rank, f"pull{op}", [cta(i) for i in range(grid)])
 
 
-def ar2(sim: Sim, rank: int, op: int, par: int, M: int, rows: int):
-    """ar2_norm_kernel: owned rows reduced after barrier 1, copied by everyone after barrier 2."""
+def ar2(sim: Sim, rank: int, op: int, par: int, M: int, rows: int, slices: int = 2):
+    """ar2_norm_kernel: (owned row, column slice) items reduced after barrier 1 by
+    CTAs i, i + grid, ...; every row (residual slices + slice sums of squares)
+    copied from its owner by everyone after barrier 2."""
     W = sim.world
     rpr = -(-M // W)
     n_my = max(0, min(rpr, M - rank * rpr))
+    n_items = n_my * slices
     grid = max(M, rows)
 
     def cta(i):
@@ -192,20 +195,22 @@ def ar2(sim: Sim, rank: int, op: int, par: int, M: int, rows: int):
                 for q in range(W):
                     sim.mem(q)["flags2"][0][rank] = e
                     yield
-            if i < n_my:
+            if i < n_items:
                 yield Wait(lambda: all(f >= e for f in m["flags2"][0]))
-                row = rank * rpr + i
-                for q in range(W):
-                    v = sim.mem(q)["acc"][par][row]
-                    _check(v == op, f"rank {rank} op {op}: reduced rank {q} acc[{par}][{row}] = {v}")
-                    yield
-                m["res"][i] = op
-                yield
-                m["ctr2"]["arr"] += 1
-                if m["ctr2"]["arr"] == n_my:
+                for item in range(i, n_items, grid):
+                    li, sl = divmod(item, slices)
+                    row = rank * rpr + li
                     for q in range(W):
-                        sim.mem(q)["flags2"][1][rank] = e
+                        v = sim.mem(q)["acc"][par][row]
+                        _check(v == op, f"rank {rank} op {op}: reduced rank {q} acc[{par}][{row}] = {v}")
                         yield
+                    m["res"][(li, sl)] = op
+                    yield
+                    m["ctr2"]["arr"] += 1
+                    if m["ctr2"]["arr"] == n_items:
+                        for q in range(W):
+                            sim.mem(q)["flags2"][1][rank] = e
+                            yield
             elif n_my == 0 and i == 0:
                 for q in range(W):
                     sim.mem(q)["flags2"][1][rank] = e
@@ -213,8 +218,10 @@ def ar2(sim: Sim, rank: int, op: int, par: int, M: int, rows: int):
             yield Wait(lambda: all(f >= e for f in m["flags2"][1]))
             if i < M:
                 owner, j = i // rpr, i % rpr
-                v = sim.mem(owner)["res"][j]
-                _check(v == op, f"rank {rank} op {op}: copied row {i} from rank {owner} res[{j}] = {v}")
+                for sl in range(slices):
+                    v = sim.mem(owner)["res"].get((j, sl))
+                    _check(v == op, f"rank {rank} op {op}: copied row {i} slice {sl} from rank {owner} = {v}")
+                    yield
                 m["out"][i] = op
             if i < rows:
                 m["acc"][par ^ 1][i] = ZERO

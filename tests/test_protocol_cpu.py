@@ -98,7 +98,7 @@ def test_emulator_catches_missing_second_barrier(monkeypatch):
                     m["res"][i] = op
                 if i < M:
                     owner, j = i // rpr, i % rpr
-                    v = sim.mem(owner)["res"][j]
+                    v = sim.mem(owner)["res"].get(j)
                     ps._check(v == op, f"rank {rank} op {op}: copied {v}")
                 yield
                 m["ctr2"]["dep"] += 1
