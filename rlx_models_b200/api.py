@@ -397,6 +397,9 @@ class ImageEmbedder:
     def pixels(self, images) -> torch.Tensor:
         from .utils import preprocess as P
         c = self.encoder.cfg
+        if not hasattr(c, "family"):  # DINOv2: shortest edge 256, centre crop 224, ImageNet statistics
+            return torch.stack([P.preprocess_image(im, size=256, crop=224, mean=P.IMAGENET_MEAN, std=P.IMAGENET_STD)
+                                for im in images])
         if c.family == "siglip":
             return torch.stack([P.preprocess_image(im, size=(c.image_size, c.image_size), crop=None, mean=P.HALF,
                                                    std=P.HALF) for im in images])
@@ -410,15 +413,19 @@ class ImageEmbedder:
 
 
 def load_image_embedder(model: str, *, device: str | torch.device = "cuda") -> ImageEmbedder:
-    """CLIP / SigLIP checkpoint (vision model alone or the full dual encoder;
-    local dir / offline HF id) -> ``ImageEmbedder``."""
+    """CLIP / SigLIP checkpoint (vision model alone or the full dual encoder) or
+    a DINOv2 backbone (with or without registers; local dir / offline HF id)
+    -> ``ImageEmbedder``."""
     import json
-    from .models.vit import VisionConfig, VisionEncoder
+    from .models.vit import Dinov2Config, Dinov2Encoder, VisionConfig, VisionEncoder
     path = resolve_model_path(model)
     if path is None:
         raise FileNotFoundError(f"no local vision checkpoint for {model!r}")
     with open(os.path.join(path, "config.json")) as f:
-        cfg = VisionConfig.from_dict(json.load(f))
+        raw = json.load(f)
+    if raw.get("model_type") in ("dinov2", "dinov2_with_registers"):
+        return ImageEmbedder(Dinov2Encoder(Dinov2Config.from_dict(raw), WeightMap.from_dir(path), device=device))
+    cfg = VisionConfig.from_dict(raw)
     return ImageEmbedder(VisionEncoder(cfg, WeightMap.from_dir(path), device=device))
 
 

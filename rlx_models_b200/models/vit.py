@@ -1,6 +1,6 @@
 """Vision transformers for image embeddings: the CLIP and SigLIP vision towers
 (HF ``vision_model.*`` names, standalone or inside the full CLIP / SigLIP
-checkpoints).
+checkpoints) and the DINOv2 self-supervised backbone (``Dinov2Encoder``).
 
     patches  = patchify(pixels) @ W_patch^T (+ bias)      (the stride-p conv as a GEMM)
     tokens   = [CLS] + patches (CLIP) | patches (SigLIP), + position embeddings
@@ -139,4 +139,130 @@ class VisionEncoder:
         checkpoint has visual_projection), otherwise the pooled output."""
         _, pooled = self(pixels)
         e = _linear(pooled, self.proj).float() if self.proj is not None else pooled.float()
+        return F.normalize(e, dim=-1) if normalize else e
+
+
+# ---------------------------------------------------------------------------
+# DINOv2 (with or without register tokens)
+# ---------------------------------------------------------------------------
+
+@dataclass
+class Dinov2Config:
+    hidden_size: int = 768
+    num_hidden_layers: int = 12
+    num_attention_heads: int = 12
+    mlp_ratio: float = 4.0
+    image_size: int = 518
+    patch_size: int = 14
+    layer_norm_eps: float = 1e-6
+    use_swiglu_ffn: bool = False
+    num_register_tokens: int = 0
+    hidden_act: str = "gelu"
+    # the with-registers release resizes position grids with the antialiased bicubic
+    # filter (a = -0.5), the original one with plain bicubic (a = -0.75)
+    antialias: bool = False
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "Dinov2Config":
+        kw = {k: d[k] for k in cls.__dataclass_fields__ if k in d}
+        kw.setdefault("antialias", d.get("model_type") == "dinov2_with_registers")
+        return cls(**kw)
+
+
+class Dinov2Encoder:
+    """DINOv2 ViT: [CLS] + register tokens + patch tokens, position embeddings
+    on CLS and patches (bicubically resized to the image's patch grid when it
+    differs from the pretraining grid), pre-norm blocks with learned per-channel
+    layer scales on both residual branches (GELU MLP, or SwiGLU for the giant
+    variants), final LayerNorm; pooled output = the normalised CLS token.
+    Checkpoint names: ``embeddings.*``, ``encoder.layer.{i}.*``, ``layernorm.*``
+    (an optional ``dinov2.`` prefix is accepted).
+
+    Reference: the reference's vision crates (crates/rlx-dinov2); the
+    transformers Dinov2Model / Dinov2WithRegistersModel are the CPU oracles."""
+
+    def __init__(self, cfg: Dinov2Config, weights, device="cpu", dtype: torch.dtype | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else torch.float32)
+        names = list(weights.keys()) if hasattr(weights, "keys") else list(weights)
+        pre = "dinov2." if any(n.startswith("dinov2.") for n in names) else ""
+        get = (lambda n: weights.take(pre + n)) if hasattr(weights, "take") else (lambda n: weights[pre + n])
+        has = lambda n: (pre + n) in weights  # noqa: E731
+        dv = lambda t: t.to(self.device, self.dtype).contiguous()  # noqa: E731
+        ln = lambda p: (dv(get(p + ".weight")), dv(get(p + ".bias")))  # noqa: E731
+        lin = lambda p: (dv(get(p + ".weight")), dv(get(p + ".bias")))  # noqa: E731
+        H = cfg.hidden_size
+        e = "embeddings."
+        self.w_patch = dv(get(e + "patch_embeddings.projection.weight").reshape(H, -1))
+        self.b_patch = dv(get(e + "patch_embeddings.projection.bias"))
+        self.cls = dv(get(e + "cls_token").reshape(1, 1, H))
+        self.regs = dv(get(e + "register_tokens")) if has(e + "register_tokens") else None
+        self.pos = get(e + "position_embeddings").float().to(self.device)  # [1, 1 + g*g, H], resized per image grid
+        self.layers = []
+        for i in range(cfg.num_hidden_layers):
+            p = f"encoder.layer.{i}."
+            a = p + "attention."
+            mlp = dict(w_in=lin(p + "mlp.weights_in"), w_out=lin(p + "mlp.weights_out")) if cfg.use_swiglu_ffn \
+                else dict(fc1=lin(p + "mlp.fc1"), fc2=lin(p + "mlp.fc2"))
+            self.layers.append(dict(
+                ln1=ln(p + "norm1"), ln2=ln(p + "norm2"),
+                qkv=dv(torch.cat([get(a + f"attention.{n}.weight") for n in ("query", "key", "value")], 0)),
+                qkv_b=dv(torch.cat([get(a + f"attention.{n}.bias") for n in ("query", "key", "value")], 0)),
+                o=lin(a + "output.dense"),
+                ls1=dv(get(p + "layer_scale1.lambda1")), ls2=dv(get(p + "layer_scale2.lambda1")), **mlp))
+        self.norm = ln("layernorm")
+
+    def _ln(self, x, p):
+        return F.layer_norm(x.float(), (x.shape[-1],), p[0].float(), p[1].float(),
+                            self.cfg.layer_norm_eps).to(x.dtype)
+
+    def _pos(self, gh: int, gw: int) -> torch.Tensor:
+        n = self.pos.shape[1] - 1
+        if gh * gw == n and gh == gw:
+            return self.pos
+        g = int(round(n ** 0.5))
+        H = self.pos.shape[-1]
+        grid = self.pos[:, 1:].reshape(1, g, g, H).permute(0, 3, 1, 2)
+        grid = F.interpolate(grid, size=(gh, gw), mode="bicubic", align_corners=False, antialias=self.cfg.antialias)
+        return torch.cat([self.pos[:, :1], grid.permute(0, 2, 3, 1).reshape(1, gh * gw, H)], 1)
+
+    def _mlp(self, x, ly):
+        if "w_in" in ly:
+            a, b = _linear(x, *ly["w_in"]).float().chunk(2, -1)
+            return _linear((F.silu(a) * b).to(x.dtype), *ly["w_out"])
+        h = _linear(x, *ly["fc1"]).float()
+        h = F.gelu(h, approximate="tanh" if self.cfg.hidden_act == "gelu_pytorch_tanh" else "none")
+        return _linear(h.to(x.dtype), *ly["fc2"])
+
+    @torch.no_grad()
+    def __call__(self, pixels: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """pixels [B, 3, h, w] (preprocessed; h, w multiples of the patch size) ->
+        (last hidden [B, 1 + registers + patches, H], pooled CLS [B, H])."""
+        from ..utils.preprocess import patchify
+        c = self.cfg
+        pixels = pixels.to(self.device, torch.float32)
+        B, _, h, w = pixels.shape
+        H, nh = c.hidden_size, c.num_attention_heads
+        gh, gw = h // c.patch_size, w // c.patch_size
+        rows = torch.stack([patchify(p, c.patch_size) for p in pixels]).to(self.dtype)
+        x = _linear(rows, self.w_patch, self.b_patch)
+        x = torch.cat([self.cls.expand(B, 1, H), x], 1)
+        x = (x.float() + self._pos(gh, gw)).to(self.dtype)
+        if self.regs is not None:
+            x = torch.cat([x[:, :1], self.regs.expand(B, -1, H), x[:, 1:]], 1)
+        for ly in self.layers:
+            q, k, v = _linear(self._ln(x, ly["ln1"]), ly["qkv"], ly["qkv_b"]).split(H, -1)
+            D = H // nh
+            q, k, v = (t.reshape(B, -1, nh, D).transpose(1, 2) for t in (q, k, v))
+            att = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(B, -1, H)
+            x = x + _linear(att, *ly["o"]) * ly["ls1"]
+            x = x + self._mlp(self._ln(x, ly["ln2"]), ly) * ly["ls2"]
+        x = self._ln(x, self.norm)
+        return x, x[:, 0]
+
+    def embed(self, pixels: torch.Tensor, normalize: bool = True) -> torch.Tensor:
+        """[B, H] fp32 image embeddings (the normalised CLS token)."""
+        _, pooled = self(pixels)
+        e = pooled.float()
         return F.normalize(e, dim=-1) if normalize else e

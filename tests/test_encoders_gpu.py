@@ -1,5 +1,5 @@
 """Encoder families on the GPU (bf16 GEMMs) against their CPU fp32 paths:
-NomicBERT text embeddings and CLIP image embeddings."""
+NomicBERT text embeddings, CLIP and DINOv2 image embeddings."""
 import math
 
 import numpy as np
@@ -51,4 +51,23 @@ def test_clip_vision_gpu_matches_cpu(cuda):
                       for _ in range(2)])
     ref = VisionEncoder(cfg, sd).embed(px)
     got = VisionEncoder(cfg, sd, device=cuda).embed(px)
+    assert _cos(got, ref).min() > 0.999
+
+
+@pytest.mark.parametrize("registers", [False, True])
+def test_dinov2_gpu_matches_cpu(cuda, registers):
+    import transformers as T
+    from rlx_models_b200.models.vit import Dinov2Config, Dinov2Encoder
+    kw = dict(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, image_size=56, patch_size=14)
+    if registers:
+        hc = T.Dinov2WithRegistersConfig(num_register_tokens=4, **kw)
+        m = T.Dinov2WithRegistersModel(hc)
+    else:
+        hc = T.Dinov2Config(**kw)
+        m = T.Dinov2Model(hc)
+    sd = {k: v.detach() for k, v in _rand(m).state_dict().items()}
+    cfg = Dinov2Config.from_dict(hc.to_dict())
+    px = torch.randn(2, 3, 112, 112, generator=torch.Generator().manual_seed(2))
+    ref = Dinov2Encoder(cfg, sd).embed(px)
+    got = Dinov2Encoder(cfg, sd, device=cuda).embed(px)
     assert _cos(got, ref).min() > 0.999

@@ -104,3 +104,59 @@ def test_clip_dual_encoder_matches_transformers(tmp_path):
         ref = m(input_ids=ids, pixel_values=px).logits_per_image
     got = clip.model.logits_per_image(px, ids)
     assert (got - ref).abs().max() < 1e-3
+
+
+def _dinov2_case(registers: bool, swiglu: bool, size: int):
+    import transformers as T
+    from rlx_models_b200.models.vit import Dinov2Config, Dinov2Encoder
+    kw = dict(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, image_size=28, patch_size=7,
+              use_swiglu_ffn=swiglu, layerscale_value=0.5)
+    if registers:
+        hc = T.Dinov2WithRegistersConfig(num_register_tokens=3, **kw)
+        m = _rand(T.Dinov2WithRegistersModel(hc))
+    else:
+        hc = T.Dinov2Config(**kw)
+        m = _rand(T.Dinov2Model(hc))
+    torch.manual_seed(1)
+    px = torch.randn(2, 3, size, size)
+    with torch.no_grad():
+        ref = m(pixel_values=px)
+    enc = Dinov2Encoder(Dinov2Config.from_dict(hc.to_dict()), {k: v.detach() for k, v in m.state_dict().items()})
+    last, pooled = enc(px)
+    assert last.shape == ref.last_hidden_state.shape
+    assert (last - ref.last_hidden_state).abs().max() < 2e-4
+    assert (pooled - ref.pooler_output).abs().max() < 2e-4
+
+
+def test_dinov2_matches_transformers():
+    _dinov2_case(registers=False, swiglu=False, size=28)
+
+
+def test_dinov2_interpolated_positions_and_swiglu():
+    _dinov2_case(registers=False, swiglu=True, size=42)
+
+
+def test_dinov2_with_registers_matches_transformers():
+    _dinov2_case(registers=True, swiglu=False, size=35)
+
+
+def test_load_image_embedder_dinov2(tmp_path):
+    import json
+    from PIL import Image
+    import transformers as T
+    from rlx_models_b200.api import load_image_embedder
+    from rlx_models_b200.weights.safetensors_io import save_file
+    hc = T.Dinov2Config(hidden_size=64, num_hidden_layers=1, num_attention_heads=4, image_size=56, patch_size=14)
+    m = _rand(T.Dinov2Model(hc))
+    d = tmp_path / "dino"
+    d.mkdir()
+    (d / "config.json").write_text(json.dumps(hc.to_dict()))
+    save_file({k: v.detach().contiguous() for k, v in m.state_dict().items()}, str(d / "model.safetensors"))
+    img = Image.fromarray(np.random.default_rng(4).integers(0, 256, (300, 260, 3), dtype=np.uint8))
+    e = load_image_embedder(str(d), device="cpu").embed(img)
+    px = T.BitImageProcessor(size={"shortest_edge": 256}, crop_size={"height": 224, "width": 224},
+                             image_mean=[0.485, 0.456, 0.406], image_std=[0.229, 0.224, 0.225])(
+        img, return_tensors="pt")["pixel_values"]
+    with torch.no_grad():
+        r = torch.nn.functional.normalize(m(pixel_values=px).pooler_output, dim=-1)
+    assert (e - r).abs().max() < 2e-2
