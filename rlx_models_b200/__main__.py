@@ -57,11 +57,31 @@ def cmd_inspect(a):
     return 0
 
 
+def _run_config(a):
+    """The --config file's RunConfig (or an empty one); applies its knob
+    overrides and prints the knob table with --show-knobs."""
+    from . import settings
+    rc = settings.load_run_config(a.config) if getattr(a, "config", None) else settings.RunConfig()
+    rc.apply_kernel_overrides()
+    if getattr(a, "show_knobs", False):
+        print(settings.describe(), file=sys.stderr)
+    return rc
+
+
+def _explicit(a, ap_defaults: dict, mapping: dict) -> dict:
+    """EngineConfig / TrainConfig fields given explicitly on the command line
+    (values that differ from the parser defaults), as keyword arguments."""
+    return {field: getattr(a, dest) for dest, field in mapping.items() if getattr(a, dest) != ap_defaults.get(dest)}
+
+
 def cmd_run(a):
     from .api import load
-    from .runtime.engine import EngineConfig, SamplingParams
-    llm = load(a.model, engine_config=EngineConfig(max_num_seqs=8, max_model_len=a.max_model_len,
-                                                   kv_memory_gb=a.kv_gb))
+    from .runtime.engine import SamplingParams
+    rc = _run_config(a)
+    base = {"max_num_seqs": 8, "max_model_len": a.max_model_len, "kv_memory_gb": a.kv_gb}
+    cli = _explicit(a, a._defaults, {"max_model_len": "max_model_len", "kv_gb": "kv_memory_gb"})
+    llm = load(a.model or rc.model, engine_config=rc.engine_config(**{**{k: v for k, v in base.items()
+                                                                         if k not in rc.serve}, **cli}))
     tok = llm.tokenizer
     if a.ids:
         ids = [int(x) for x in a.ids.split(",")]
@@ -82,10 +102,14 @@ def cmd_run(a):
 
 def cmd_serve(a):
     from .api import load
-    from .runtime.engine import EngineConfig
     from .serve.openai_server import serve
-    llm = load(a.model, engine_config=EngineConfig(max_num_seqs=a.max_num_seqs, max_model_len=a.max_model_len,
-                                                   kv_memory_gb=a.kv_gb))
+    rc = _run_config(a)
+    base = {"max_num_seqs": a.max_num_seqs, "max_model_len": a.max_model_len, "kv_memory_gb": a.kv_gb}
+    cli = _explicit(a, a._defaults, {"max_num_seqs": "max_num_seqs", "max_model_len": "max_model_len",
+                                     "kv_gb": "kv_memory_gb"})
+    model = a.model or rc.model
+    llm = load(model, engine_config=rc.engine_config(**{**{k: v for k, v in base.items() if k not in rc.serve},
+                                                        **cli}))
     embedder = None
     if a.embed_model:  # an encoder checkpoint behind /v1/embeddings
         from .api import load_embedder
@@ -94,7 +118,7 @@ def cmd_serve(a):
     if a.asr_model:  # a Whisper checkpoint behind /v1/audio/transcriptions
         from .api import load_transcriber
         transcriber = load_transcriber(a.asr_model)
-    serve(llm, a.host, a.port, model_name=a.model, embedder=embedder, transcriber=transcriber)
+    serve(llm, a.host, a.port, model_name=model, embedder=embedder, transcriber=transcriber)
     return 0
 
 
@@ -135,7 +159,17 @@ def cmd_bench(rest):
 
 def cmd_train(a):
     from .train.data import train_from_jsonl
+    a.run_config = _run_config(a)
+    a.model = a.model or a.run_config.model
     return train_from_jsonl(a)
+
+
+def cmd_knobs(a):
+    """Print every environment knob with its value and where it came from."""
+    _run_config(a)
+    from . import settings
+    print(settings.describe())
+    return 0
 
 
 def cmd_scan(a):
@@ -165,7 +199,9 @@ def main(argv=None):
     p.add_argument("--limit", type=int, default=100000)
     for name in ("run", "serve"):
         p = sub.add_parser(name)
-        p.add_argument("--model", required=True)
+        p.add_argument("--model", default=None, help="model id, preset or path (or the config file's 'model')")
+        p.add_argument("--config", default=None, help="YAML / JSON run config (settings.RunConfig)")
+        p.add_argument("--show-knobs", action="store_true", help="print the knob table at startup")
         p.add_argument("--max-model-len", type=int, default=4096)
         p.add_argument("--kv-gb", type=float, default=8.0)
         if name == "run":
@@ -191,8 +227,12 @@ def main(argv=None):
     p.add_argument("--kv-gb", type=float, default=4.0)
     p.add_argument("--graphs", action="store_true", help="keep decode CUDA graphs (kernels then appear per graph)")
     p.add_argument("--trace", default="b200_trace.json")
+    p = sub.add_parser("knobs", help="print the environment knobs and their values")
+    p.add_argument("--config", default=None)
     p = sub.add_parser("train")
-    p.add_argument("--model", required=True)
+    p.add_argument("--model", default=None)
+    p.add_argument("--config", default=None, help="YAML / JSON run config (its 'train' section)")
+    p.add_argument("--show-knobs", action="store_true")
     p.add_argument("--data", required=True, help="JSONL with 'text', 'prompt'/'completion' or 'input_ids'")
     p.add_argument("--steps", type=int, default=100)
     p.add_argument("--seq-len", type=int, default=2048)
@@ -201,8 +241,17 @@ def main(argv=None):
     p.add_argument("--out", default=None)
     p.add_argument("--lora-rank", type=int, default=0)
     a = ap.parse_args(argv)
+    if a.cmd in ("run", "serve", "train"):
+        a._defaults = {act.dest: act.default for act in sub.choices[a.cmd]._actions}
+    if a.cmd in ("run", "serve", "train") and not (a.model or (a.config and _peek_model(a.config))):
+        ap.error(f"{a.cmd}: --model (or a --config file with 'model') is required")
     return {"scan": cmd_scan, "inspect": cmd_inspect, "run": cmd_run, "serve": cmd_serve, "train": cmd_train,
-            "profile": cmd_profile}[a.cmd](a)
+            "profile": cmd_profile, "knobs": cmd_knobs}[a.cmd](a)
+
+
+def _peek_model(path: str):
+    from . import settings
+    return settings.load_run_config(path).model
 
 
 if __name__ == "__main__":

@@ -27,7 +27,6 @@ Megatron split this implements.
 """
 from __future__ import annotations
 
-import os
 
 import torch
 import torch.distributed as dist
@@ -81,7 +80,8 @@ class PullTPComm(NcclTPComm):
         self.H = hidden
         # "auto": two-shot from 8 ranks and 16 rows (at 4 ranks the one-shot pull measured
         # 28.3 vs 34.0 us per GEMM + reduction at 64 rows; at 8, 48.7 vs 41.5); "on" / "off" force it
-        self.two_shot = two_shot or os.environ.get("B200_TP_TWO_SHOT", "auto")
+        from .. import settings
+        self.two_shot = two_shot or settings.get("B200_TP_TWO_SHOT")
         self.rpr_max = (self.ROWS + world - 1) // world
         lay = Layout()
         self.o_acc = lay.add("acc", (2, self.ROWS, hidden), torch.float32)

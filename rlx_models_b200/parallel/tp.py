@@ -99,8 +99,8 @@ def make_tp_comm(kind: str, rank: int, world: int, device, eps: float = 1e-6, pr
     else:
         raise ValueError(kind)
     if prefill_overlap is None:
-        import os
-        prefill_overlap = os.environ.get("B200_TP_PREFILL_OVERLAP", "1") != "0"
+        from .. import settings
+        prefill_overlap = settings.get("B200_TP_PREFILL_OVERLAP")
     if prefill_overlap:
         g2 = dist.new_group(list(range(world)))
         comm.microbatch_comm = NcclTPComm(rank, world, device, eps, group=g2)

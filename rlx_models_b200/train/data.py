@@ -122,8 +122,17 @@ def train_from_jsonl(a) -> int:
         weights = RandomWeights(cfg, 0, dev)
     tok = load_tokenizer(path)
     ds = SFTDataset(read_jsonl(a.data), tok, a.seq_len)
-    tcfg = TrainConfig(lr=a.lr, total_steps=a.steps, micro_batch=max(1, a.batch // 4), lora_rank=a.lora_rank,
-                       param_dtype="bfloat16" if dev.type == "cuda" else "float32")
+    base = dict(lr=a.lr, total_steps=a.steps, micro_batch=max(1, a.batch // 4), lora_rank=a.lora_rank,
+                param_dtype="bfloat16" if dev.type == "cuda" else "float32")
+    rc = getattr(a, "run_config", None)
+    if rc is not None and rc.train:
+        # the config file's train section over the parser defaults; explicit flags win
+        dflt = getattr(a, "_defaults", {})
+        explicit = {f: getattr(a, d) for d, f in (("lr", "lr"), ("steps", "total_steps"), ("lora_rank", "lora_rank"))
+                    if getattr(a, d) != dflt.get(d)}
+        tcfg = rc.train_config(**{**{k: v for k, v in base.items() if k not in rc.train}, **explicit})
+    else:
+        tcfg = TrainConfig(**base)
     tr = Trainer(cfg, tcfg, weights, rank=rank, world=world, device=dev)
     it = ds.batches(a.batch, rank, world)
     for _ in range(a.steps):

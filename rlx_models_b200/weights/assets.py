@@ -126,7 +126,8 @@ def materialize(source, directory: str | None = None) -> str:
     if isinstance(s, DirSource) and directory is None:
         return s.path
     if directory is None:
-        root = os.environ.get("RLX_B200_ASSET_CACHE", os.path.expanduser("~/.cache/rlx_models_b200/assets"))
+        from .. import settings
+        root = os.path.expanduser(settings.get("RLX_B200_ASSET_CACHE"))
         if isinstance(s, PackSource):
             key = s.digest
         else:
