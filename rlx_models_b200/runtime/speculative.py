@@ -86,9 +86,27 @@ class _Seq:
         return out
 
 
+_STATE_ATTRS = ("conv", "rec", "ssm")  # per-slot recurrent state tensors [layers, slots, ...] of hybrid caches
+
+
+def _snapshot(kv, slot: int = 0) -> dict:
+    return {a: getattr(kv, a)[:, slot].clone() for a in _STATE_ATTRS if hasattr(kv, a)}
+
+
+def _restore(kv, snap: dict, slot: int = 0) -> None:
+    for a, t in snap.items():
+        getattr(kv, a)[:, slot].copy_(t)
+
+
 class SpeculativeDecoder:
     def __init__(self, target, draft=None, k: int = 4, max_len: int = 4096, ngram: int = 3, draft_head=None,
                  head_window: int = 16):
+        if draft is not None and getattr(draft, "stateful", False) and draft is not target:
+            raise NotImplementedError("a recurrent-state draft model cannot roll back rejected tokens")
+        # recurrent-state targets (linear attention / SSM layers): the verify pass advances the
+        # state over every proposal, so a partial acceptance restores the state saved before it
+        # and re-runs the accepted tokens (attention KV rolls back by position as before)
+        self.stateful = bool(getattr(target, "stateful", False))
         self.target = _Seq(target, max_len)
         self.draft = _Seq(draft, max_len) if draft is not None else None
         self.head, self.head_window = draft_head, head_window
@@ -99,7 +117,8 @@ class SpeculativeDecoder:
         """Learned draft head over the target's features of the last positions."""
         last = len(seq) - 2  # feature that produced the newest token
         a = max(0, last - self.head_window + 1)
-        return self.head.propose(self.target.hidden[a:last + 1], seq[a + 1:last + 2], k)
+        kw = {"pos0": a + 1} if getattr(self.head, "uses_positions", False) else {}  # RoPE'd heads (MTP)
+        return self.head.propose(self.target.hidden[a:last + 1], seq[a + 1:last + 2], k, **kw)
 
     # -- proposers ---------------------------------------------------------------
     def _propose_draft(self, seq: list[int], k: int) -> list[int]:
@@ -144,11 +163,15 @@ class SpeculativeDecoder:
                 props = self._propose_lookup(seq, k)
             # verify: the last accepted token (not yet in the target cache) + proposals
             start = len(seq) - 1
+            snap = _snapshot(t.kv) if self.stateful and props else None
             lv = t.run([seq[-1]] + props, start, keep)
             tgt = lv.argmax(-1).tolist()
             n_acc = 0
             while n_acc < len(props) and props[n_acc] == tgt[n_acc]:
                 n_acc += 1
+            if snap is not None and n_acc < len(props):
+                _restore(t.kv, snap)
+                t.run([seq[-1]] + props[:n_acc], start, keep)
             new = props[:n_acc] + [tgt[n_acc]]
             self.stats.target_passes += 1
             self.stats.proposed += len(props)
