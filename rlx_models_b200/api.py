@@ -469,3 +469,61 @@ def load_clip(model: str, *, device: str | torch.device = "cuda") -> CLIP:
         from transformers import AutoTokenizer
         tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
     return CLIP(CLIPDualEncoder(cfg, WeightMap.from_dir(path), device=device), tok)
+
+
+class VLM:
+    """A vision-language model (``models/llava.py``) plus its serving engine:
+    prompts are token ids whose image placeholder runs (one placeholder per
+    image token, as the model's processor expands them) receive the images'
+    projected features."""
+
+    def __init__(self, vlm, engine_config: EngineConfig | None = None, tokenizer=None):
+        import dataclasses
+        self.vlm = vlm
+        ec = dataclasses.replace(engine_config or EngineConfig(), prefix_caching=False)
+        self.engine = LLMEngine(vlm.lm, ec)
+        self.tokenizer = tokenizer
+
+    @property
+    def image_tokens(self) -> int:
+        """Placeholders per image."""
+        c = self.vlm.cfg.vision
+        n = (c.image_size // c.patch_size) ** 2
+        return n + (1 if self.vlm.cfg.vision_feature_select_strategy == "full" else 0)
+
+    def pixels(self, images) -> torch.Tensor:
+        return ImageEmbedder(self.vlm.vision).pixels(list(images))
+
+    def generate(self, prompts: list[list[int]], images: list, params: SamplingParams | None = None
+                 ) -> list[RequestOutput]:
+        """``images[i]``: the images of prompt i (paths, PIL images, HWC uint8
+        arrays, or a preprocessed [n, 3, S, S] tensor), in placeholder order."""
+        mm = []
+        for ids, ims in zip(prompts, images):
+            if ims is None or len(ims) == 0:
+                mm.append(None)
+                continue
+            px = ims if torch.is_tensor(ims) else self.pixels(ims)
+            mm.append(self.vlm.mm_segments(list(ids), px))
+        return self.engine.generate([list(p) for p in prompts], params, mm)
+
+
+def load_vlm(model: str, *, device: str | torch.device = "cuda", engine_config: EngineConfig | None = None) -> VLM:
+    """LLaVA-form vision-language checkpoint (local dir / offline HF id) -> ``VLM``."""
+    import json
+    from .models.llava import LlavaConfig, LlavaVLM
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        raw = json.load(f)
+    if raw.get("model_type") not in ("llava",):
+        raise NotImplementedError(f"vision-language model_type {raw.get('model_type')!r}")
+    vlm = LlavaVLM(LlavaConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
+    tok = None
+    try:
+        from .tokenizer import load_tokenizer
+        tok = load_tokenizer(path)
+    except Exception:
+        pass
+    return VLM(vlm, engine_config, tok)

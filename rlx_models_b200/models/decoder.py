@@ -47,6 +47,8 @@ class ForwardBatch:
     logit_rows: torch.Tensor | None = None        # [R] int64 rows needing logits
     seq_slots: torch.Tensor | None = None         # [Bd + Bp] int32 state slot per sequence (stateful models)
     pre_cu_host: list | None = None               # host copy of pre_cu_q (lets a TP model split the step)
+    mm_rows: torch.Tensor | None = None           # [n] int64 token rows whose input embedding is replaced
+    mm_embeds: torch.Tensor | None = None         # [n, H] their embeddings (image tokens of a VLM)
 
     @property
     def num_tokens(self) -> int:
@@ -292,13 +294,15 @@ class DecoderLM:
         """Returns the final-normed hidden states of every token ([T, H])."""
         comm = self.comm or LocalComm(self.cfg.rms_norm_eps)
         comm_b = getattr(comm, "microbatch_comm", None)
-        if comm_b is not None and not inspecting():
+        if comm_b is not None and not inspecting() and fb.mm_rows is None:
             mbs = self._microbatches(fb)
             if mbs is not None:
                 return self._forward_overlapped(mbs[0], mbs[1], kv, comm, comm_b)
         h = comm.embed(fb.input_ids, self.embed)
         if self.cfg.embedding_multiplier != 1.0:
             h.mul_(self.cfg.embedding_multiplier)
+        if fb.mm_rows is not None:
+            h.index_copy_(0, fb.mm_rows, fb.mm_embeds.to(h.dtype))
         x = comm.norm_in(h, self.layers[0].ln1)
         n = len(self.layers)
         for i, L in enumerate(self.layers):

@@ -179,9 +179,10 @@ class DecoderOracle:
         return out
 
     @torch.no_grad()
-    def forward(self, ids: torch.Tensor, kv: OracleKV | None = None) -> tuple[torch.Tensor, OracleKV]:
-        """ids: [T] new tokens continuing ``kv``. Returns fp32 logits [T, V]."""
-        h, kv = self.forward_hidden(ids, kv)
+    def forward(self, ids: torch.Tensor, kv: OracleKV | None = None, mm=None) -> tuple[torch.Tensor, OracleKV]:
+        """ids: [T] new tokens continuing ``kv``; ``mm`` = (rows, embeds) replaces the
+        input embeddings of those rows (image tokens). Returns fp32 logits [T, V]."""
+        h, kv = self.forward_hidden(ids, kv, mm)
         c = self.cfg
         head = self.W("model.embed_tokens.weight") if c.tie_word_embeddings else self.W("lm_head.weight")
         logits = h @ head.T / c.logits_scaling
@@ -190,7 +191,7 @@ class DecoderOracle:
         return logits, kv
 
     @torch.no_grad()
-    def forward_hidden(self, ids: torch.Tensor, kv: OracleKV | None = None) -> tuple[torch.Tensor, OracleKV]:
+    def forward_hidden(self, ids: torch.Tensor, kv: OracleKV | None = None, mm=None) -> tuple[torch.Tensor, OracleKV]:
         """Final-normed hidden states [T, H] (the embedding models' last_hidden_state)."""
         c = self.cfg
         if kv is None:
@@ -198,6 +199,9 @@ class DecoderOracle:
         start = kv.length
         pos = torch.arange(start, start + ids.shape[0], device=self.device)
         h = self.W("model.embed_tokens.weight")[ids.to(self.device).long()] * c.embedding_multiplier
+        if mm is not None:
+            rows, emb = mm
+            h = h.index_copy(0, rows.to(self.device).long(), emb.to(self.device, h.dtype))
         rm = c.residual_multiplier
         eps = c.rms_norm_eps
         for i in range(c.num_hidden_layers):

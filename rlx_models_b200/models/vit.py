@@ -102,9 +102,7 @@ class VisionEncoder:
         q, k, v = (t.reshape(B, -1, nh, D).transpose(1, 2) for t in (q, k, v))
         return F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(B, Lq, H)
 
-    @torch.no_grad()
-    def __call__(self, pixels: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """pixels [B, 3, S, S] (preprocessed) -> (last hidden [B, L, H], pooled [B, H])."""
+    def _blocks(self, pixels: torch.Tensor, n_blocks: int) -> torch.Tensor:
         from ..utils.preprocess import patchify
         c = self.cfg
         pixels = pixels.to(self.device, torch.float32)
@@ -117,10 +115,29 @@ class VisionEncoder:
         x = x + self.pos[None, :x.shape[1]]
         if self.pre_ln is not None:
             x = self._ln(x, self.pre_ln)
-        for ly in self.layers:
+        for ly in self.layers[:n_blocks]:
             q, k, v = _linear(self._ln(x, ly["ln1"]), ly["qkv"], ly["qkv_b"]).split(H, -1)
             x = x + _linear(self._attend(q, k, v, nh), *ly["o"])
             x = x + _linear(self._act(_linear(self._ln(x, ly["ln2"]), *ly["fc1"])).to(x.dtype), *ly["fc2"])
+        return x
+
+    @torch.no_grad()
+    def hidden_at(self, pixels: torch.Tensor, layer: int) -> torch.Tensor:
+        """Hidden states after ``layer`` blocks (HF ``hidden_states[layer]``; negative
+        counts from the end: -1 = the last block's output, before any post-norm)."""
+        n = len(self.layers)
+        k = layer if layer >= 0 else n + 1 + layer
+        if not 0 <= k <= n:
+            raise ValueError(f"layer {layer} outside 0..{n}")
+        return self._blocks(pixels, k)
+
+    @torch.no_grad()
+    def __call__(self, pixels: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """pixels [B, 3, S, S] (preprocessed) -> (last hidden [B, L, H], pooled [B, H])."""
+        c = self.cfg
+        H, nh = c.hidden_size, c.num_attention_heads
+        x = self._blocks(pixels, len(self.layers))
+        B = x.shape[0]
         if c.family == "clip":
             return x, self._ln(x[:, 0], self.post_ln)
         x = self._ln(x, self.post_ln)

@@ -132,6 +132,7 @@ class RequestState:
     mirostat_mu: float | None = None
     mirostat_lp2: object = None
     n_sched: int = 0                    # sampled rows scheduled so far (the sampler's stream offset)
+    mm: list | None = None              # [(first prompt position, [n, H] input embeddings)] (images)
 
 
 @dataclass
@@ -215,6 +216,7 @@ class LLMEngine:
         self.requests: dict[int, RequestState] = {}
         self._n_nongreedy = 0   # active requests that sample or want logprobs
         self._n_host_rows = 0   # active requests that need the host between steps (penalties, processors)
+        self._n_mm = 0          # active requests with input embeddings (images)
         self._inflight = None
         self.graphs: dict[int, tuple] = {}
         self._graph_pool = None
@@ -226,11 +228,24 @@ class LLMEngine:
         self._nblocks = nb
 
     # -- requests --------------------------------------------------------------
-    def add_request(self, prompt: list[int], params: SamplingParams | None = None) -> int:
+    def add_request(self, prompt: list[int], params: SamplingParams | None = None, mm: list | None = None) -> int:
+        """Queue a request. ``mm``: [(position, embeds [n, H])] input embeddings that
+        replace the token embeddings of prompt positions position .. position + n - 1
+        (image tokens of a vision-language model)."""
         params = params or SamplingParams()
+        if mm:
+            if self.cfg.prefix_caching:
+                raise ValueError("requests with input embeddings need prefix_caching=False "
+                                 "(equal placeholder ids would share cached KV across images)")
+            for p0, e in mm:
+                if p0 < 0 or p0 + e.shape[0] > len(prompt):
+                    raise ValueError(f"embeddings at {p0}..{p0 + e.shape[0]} outside the {len(prompt)}-token prompt")
         sid = self.sched.add_request(list(map(int, prompt)), int(params.max_new_tokens), bool(params.ignore_eos),
                                      list(params.stop_token_ids))
         st = RequestState(sid, len(prompt), params, time.perf_counter())
+        if mm:
+            st.mm = [(int(p0), e.to(self.device)) for p0, e in mm]
+            self._n_mm += 1
         if params.penalised or params.processed:
             st.out_counts = {}
             if params.repetition_penalty != 1.0 or params.dry_multiplier > 0:
@@ -250,6 +265,9 @@ class LLMEngine:
         st = self.requests.pop(sid, None)
         if st is not None:
             self._track(st, -1)
+            if st.mm is not None:
+                st.mm = None
+                self._n_mm -= 1
         self._free_slot(sid)
         return st
 
@@ -371,7 +389,30 @@ class LLMEngine:
             pre_max_q=max_q, logit_rows=d["logit_rows"][:R],
             seq_slots=d["seq_slots"][:nd + npf] if self.stateful else None,
             pre_cu_host=self.h["pre_cu"][:npf + 1].tolist() if npf else None)
+        if npf and self._n_mm:
+            fb.mm_rows, fb.mm_embeds = self._mm_rows(nd, npf)
         return self.model.forward(fb, self.kv)
+
+    def _mm_rows(self, nd: int, npf: int):
+        """Rows of this step's prefill tokens whose input embeddings a request
+        supplies (images), and those embeddings; (None, None) when there are none."""
+        sids = self.sched.step_seq_ids()[nd:nd + npf]
+        cu, ctx = self.h["pre_cu"][:npf + 1].tolist(), self.h["pre_ctx"][:npf].tolist()
+        rows, embs = [], []
+        for j, sid in enumerate(sids):
+            st = self.requests.get(sid)
+            if st is None or st.mm is None:
+                continue
+            n = cu[j + 1] - cu[j]
+            p_lo = ctx[j] - n  # prompt position of this chunk's first row
+            for p0, e in st.mm:
+                a, b = max(p0, p_lo), min(p0 + e.shape[0], ctx[j])
+                if a < b:
+                    rows.append(torch.arange(nd + cu[j] + a - p_lo, nd + cu[j] + b - p_lo))
+                    embs.append(e[a - p0:b - p0])
+        if not rows:
+            return None, None
+        return torch.cat(rows).to(self.device), torch.cat(embs)
 
     def _bucket(self, n: int) -> int | None:
         for b in self.cfg.graph_batch_sizes:
@@ -601,11 +642,14 @@ class LLMEngine:
         from .prompt_cache import load_prompt
         return load_prompt(self, path)
 
-    def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None
-                 ) -> list[RequestOutput]:
+    def generate(self, prompts: list[list[int]], params: SamplingParams | list[SamplingParams] | None = None,
+                 mm: list | None = None) -> list[RequestOutput]:
+        """Run requests to completion; ``mm[i]`` (optional) is request i's input
+        embeddings (see ``add_request``)."""
         if not isinstance(params, list):
             params = [params or SamplingParams()] * len(prompts)
-        ids = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
+        mm = mm or [None] * len(prompts)
+        ids = [self.add_request(p, sp, m) for p, sp, m in zip(prompts, params, mm)]
         order = {sid: i for i, sid in enumerate(ids)}
         results: list[RequestOutput | None] = [None] * len(ids)
         while self.has_unfinished():
