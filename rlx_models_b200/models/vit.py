@@ -27,6 +27,19 @@ import torch.nn.functional as F
 from .flux_text import _linear
 
 
+def _pad_k(w: torch.Tensor) -> torch.Tensor:
+    """Zero-pad a patch-embedding weight's input dim to a multiple of 8 (the GEMM's
+    16-byte row rule; a 14-pixel patch has 3 * 14 * 14 = 588 inputs)."""
+    k = w.shape[1]
+    return w if k % 8 == 0 else F.pad(w, (0, 8 - k % 8))
+
+
+def _patch_rows(pixels: torch.Tensor, patch: int, k_padded: int, dtype) -> torch.Tensor:
+    from ..utils.preprocess import patchify
+    rows = torch.stack([patchify(p, patch) for p in pixels]).to(dtype)
+    return rows if rows.shape[-1] == k_padded else F.pad(rows, (0, k_padded - rows.shape[-1]))
+
+
 @dataclass
 class VisionConfig:
     family: str = "clip"  # "clip" | "siglip"
@@ -60,7 +73,7 @@ class VisionEncoder:
         v = "vision_model."
         e = v + "embeddings."
         H = cfg.hidden_size
-        self.w_patch = dv(get(e + "patch_embedding.weight").reshape(H, -1))
+        self.w_patch = _pad_k(dv(get(e + "patch_embedding.weight").reshape(H, -1)))
         self.b_patch = dv(get(e + "patch_embedding.bias")) if has(e + "patch_embedding.bias") else None
         self.cls = dv(get(e + "class_embedding")) if has(e + "class_embedding") else None
         self.pos = dv(get(e + "position_embedding.weight"))
@@ -103,13 +116,11 @@ class VisionEncoder:
         return F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(B, Lq, H)
 
     def _blocks(self, pixels: torch.Tensor, n_blocks: int) -> torch.Tensor:
-        from ..utils.preprocess import patchify
         c = self.cfg
         pixels = pixels.to(self.device, torch.float32)
         B = pixels.shape[0]
         H, nh = c.hidden_size, c.num_attention_heads
-        rows = torch.stack([patchify(p, c.patch_size) for p in pixels]).to(self.dtype)
-        x = _linear(rows, self.w_patch, self.b_patch)
+        x = _linear(_patch_rows(pixels, c.patch_size, self.w_patch.shape[1], self.dtype), self.w_patch, self.b_patch)
         if self.cls is not None:
             x = torch.cat([self.cls.expand(B, 1, H), x], 1)
         x = x + self.pos[None, :x.shape[1]]
@@ -211,7 +222,7 @@ class Dinov2Encoder:
         lin = lambda p: (dv(get(p + ".weight")), dv(get(p + ".bias")))  # noqa: E731
         H = cfg.hidden_size
         e = "embeddings."
-        self.w_patch = dv(get(e + "patch_embeddings.projection.weight").reshape(H, -1))
+        self.w_patch = _pad_k(dv(get(e + "patch_embeddings.projection.weight").reshape(H, -1)))
         self.b_patch = dv(get(e + "patch_embeddings.projection.bias"))
         self.cls = dv(get(e + "cls_token").reshape(1, 1, H))
         self.regs = dv(get(e + "register_tokens")) if has(e + "register_tokens") else None
@@ -256,14 +267,12 @@ class Dinov2Encoder:
     def __call__(self, pixels: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
         """pixels [B, 3, h, w] (preprocessed; h, w multiples of the patch size) ->
         (last hidden [B, 1 + registers + patches, H], pooled CLS [B, H])."""
-        from ..utils.preprocess import patchify
         c = self.cfg
         pixels = pixels.to(self.device, torch.float32)
         B, _, h, w = pixels.shape
         H, nh = c.hidden_size, c.num_attention_heads
         gh, gw = h // c.patch_size, w // c.patch_size
-        rows = torch.stack([patchify(p, c.patch_size) for p in pixels]).to(self.dtype)
-        x = _linear(rows, self.w_patch, self.b_patch)
+        x = _linear(_patch_rows(pixels, c.patch_size, self.w_patch.shape[1], self.dtype), self.w_patch, self.b_patch)
         x = torch.cat([self.cls.expand(B, 1, H), x], 1)
         x = (x.float() + self._pos(gh, gw)).to(self.dtype)
         if self.regs is not None:
