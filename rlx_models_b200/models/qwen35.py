@@ -370,6 +370,7 @@ class Qwen35Oracle:
         self.cfg, self.device, self.chunk = cfg, torch.device(device), chunk
         self.w = CanonicalSource(weights, cfg)
         self.inv, self.mult = rope_inv_freq(cfg.rotary_dim, cfg.rope_theta, None, cfg.max_position_embeddings)
+        self.inv = self.inv.to(self.device)
 
     def _t(self, n):
         return self.w[n].to(self.device, torch.float32)
