@@ -102,6 +102,17 @@ class DecoderConfig:
     routed_scaling_factor: float = 1.0
     n_shared_experts: int = 0
     first_k_dense_replace: int = 0
+    moe_layers: list | None = None  # explicit MoE layer indices (Llama-4 interleaves dense / MoE)
+    # Llama-4 axes: per-layer RoPE on / off (1 / 0; NoPE layers every 4th), RoPE on interleaved
+    # pairs, weightless RMS norm of q and k after RoPE on the RoPE layers, chunked attention on
+    # the RoPE layers, query temperature on the NoPE layers
+    rope_layers: list | None = None
+    rope_interleaved: bool = False
+    qk_l2_norm: bool = False
+    attention_chunk_size: int = 0
+    attn_temperature_tuning: bool = False
+    floor_scale: float = 8192.0
+    attn_scale: float = 0.1
     expert_quant: str = "bf16"  # "bf16" | "mxfp4"
     torch_dtype: str = "bfloat16"
     extra: dict = field(default_factory=dict)
@@ -123,7 +134,12 @@ class DecoderConfig:
         return self.num_experts > 0
 
     def is_moe_layer(self, i: int) -> bool:
+        if self.moe_layers is not None:
+            return self.is_moe and i in self.moe_layers
         return self.is_moe and i >= self.first_k_dense_replace
+
+    def uses_rope(self, i: int) -> bool:
+        return self.rope_layers is None or bool(self.rope_layers[i])
 
     def layer_window(self, i: int) -> int:
         if self.layer_types is not None and self.sliding_window:
@@ -178,6 +194,29 @@ class DecoderConfig:
                 kw[k] = dflt
             if d.get("rotary_dim") and not d.get("partial_rotary_factor"):
                 kw["partial_rotary_factor"] = d["rotary_dim"] / kw.get("head_dim", d.get("head_dim", 128))
+        elif mt in ("llama4_text", "llama4"):  # Llama-4 (text): iRoPE + top-1 sigmoid experts + shared expert
+            kw["model_type"] = "llama4_text"
+            kw["qk_norm"] = False
+            kw["qk_l2_norm"] = bool(d.get("use_qk_norm", True))
+            kw.setdefault("rms_norm_eps", d.get("rms_norm_eps", 1e-5))
+            kw["num_experts"] = d.get("num_local_experts", 16)
+            kw["num_experts_per_tok"] = d.get("num_experts_per_tok", 1)
+            kw["moe_intermediate_size"] = d.get("intermediate_size", 8192)
+            kw["intermediate_size"] = d.get("intermediate_size_mlp", d.get("intermediate_size", 8192))
+            kw["router_scoring"] = "llama4"
+            kw["n_shared_experts"] = 1
+            n = d["num_hidden_layers"]
+            step = int(d.get("interleave_moe_layer_step", 1))
+            kw["moe_layers"] = list(d["moe_layers"]) if d.get("moe_layers") is not None else \
+                list(range(step - 1, n, step))
+            every = int(d.get("no_rope_layer_interval", 4))
+            kw["rope_layers"] = list(d["no_rope_layers"]) if d.get("no_rope_layers") else \
+                [int((i + 1) % every != 0) for i in range(n)]
+            kw["rope_interleaved"] = True
+            kw["attention_chunk_size"] = int(d.get("attention_chunk_size") or 0)
+            kw["attn_temperature_tuning"] = bool(d.get("attn_temperature_tuning", True))
+            kw["floor_scale"] = float(d.get("floor_scale", 8192))
+            kw["attn_scale"] = float(d.get("attn_scale", 0.1))
         elif mt == "qwen2_moe":
             kw["qk_norm"] = False
             kw["attention_bias"] = True

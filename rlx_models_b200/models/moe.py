@@ -124,6 +124,8 @@ class MoEDecoderLM(DecoderLM):
         tokens; larger steps, and "nccl", sum per-rank partials with an NCCL
         all-reduce."""
         assert cfg.is_moe
+        if cfg.router_scoring == "llama4" and cfg.num_experts_per_tok != 1:
+            raise NotImplementedError("Llama-4 routing scales the expert input: top-1 only on the GPU path")
         self.ep_rank, self.ep_size = ep_rank, ep_size
         assert cfg.num_experts % ep_size == 0
         self.e_local = cfg.num_experts // ep_size
@@ -144,6 +146,13 @@ class MoEDecoderLM(DecoderLM):
                                        top_k=cfg.num_experts_per_tok, e_local=self.e_local,
                                        max_tokens=combine_max_tokens, num_layers=n_moe,
                                        eps=cfg.rms_norm_eps)
+        if cfg.rope_layers is not None:
+            # Llama-4: chunked attention on the RoPE layers and the NoPE layers' query
+            # temperature both start at position min(chunk, floor_scale); below it the
+            # layers are plain causal attention, which is what the kernels here run
+            lim = [v for v in (cfg.attention_chunk_size, int(cfg.floor_scale) if cfg.attn_temperature_tuning else 0)
+                   if v > 0]
+            self.max_context = min(lim) if lim else None
         self._route_spec = None
         if cfg.router_scoring == "sigmoid":  # DeepSeek-style group-limited routing (glm4_moe)
             from types import SimpleNamespace
@@ -158,6 +167,9 @@ class MoEDecoderLM(DecoderLM):
         if c.model_type in ("mixtral", "minimax_m2"):  # block_sparse_moe.* names -> the canonical MoE names
             from ..weights.aliases import CanonicalView
             w = CanonicalView(w, c.model_type)
+        elif c.model_type == "llama4_text":  # feed_forward.* names, fused expert banks
+            from ..weights.aliases import Llama4View
+            w = Llama4View(w)
 
         def g(name):
             return self._get(w, name)
@@ -177,11 +189,21 @@ class MoEDecoderLM(DecoderLM):
             L.ln1 = dv(g(p + "input_layernorm.weight"))
             L.ln2 = dv(g(p + "post_attention_layernorm.weight"))
             L.wqkv = dv(torch.cat([g(p + f"self_attn.{n}_proj.weight").to(dev) for n in "qkv"], 0))
+            if c.rope_interleaved:
+                # RoPE on interleaved pairs (2j, 2j+1) == half-split RoPE on q / k rows reordered
+                # [0, 2, .., D-2, 1, 3, .., D-1] per head (attention scores are unchanged)
+                perm = torch.cat([torch.arange(0, D, 2), torch.arange(1, D, 2)]).to(dev)
+                nq, nk = c.num_attention_heads, c.num_key_value_heads
+                rows = torch.cat([(h * D + perm) for h in range(nq + nk)] +
+                                 [torch.arange((nq + nk) * D, L.wqkv.shape[0], device=dev)])
+                L.wqkv = L.wqkv.index_select(0, rows).contiguous()
             L.bqkv = dv(torch.cat([g(p + f"self_attn.{n}_proj.bias").to(dev) for n in "qkv"])) \
                 if c.attention_bias else None
             if c.qk_norm:
                 L.q_norm = dv(g(p + "self_attn.q_norm.weight"))
                 L.k_norm = dv(g(p + "self_attn.k_norm.weight"))
+            elif c.qk_l2_norm and c.uses_rope(i):  # weightless RMS norm (it commutes with the rotation)
+                L.q_norm = L.k_norm = torch.ones(D, dtype=bf, device=dev)
             else:
                 L.q_norm = L.k_norm = None
             L.wo = dv(g(p + "self_attn.o_proj.weight"))
@@ -192,6 +214,8 @@ class MoEDecoderLM(DecoderLM):
             L.sinks = g(p + "self_attn.sinks").to(dev, torch.float32).contiguous() if c.attn_sinks else None
             L.window = c.layer_window(i)
             L.inv_freq, L.rope_mult = self.inv_freq, self.rope_mult
+            if not c.uses_rope(i):  # Llama-4 NoPE layer: zero frequencies rotate nothing
+                L.inv_freq = torch.zeros_like(self.inv_freq)
             L.ln_post_attn = L.ln_post_ffn = None
             self.layers.append(L)
             if not c.is_moe_layer(i):  # dense layer of a mostly-MoE model (glm4_moe's first layers)
@@ -266,10 +290,17 @@ class MoEDecoderLM(DecoderLM):
         k = c.num_experts_per_tok
         E_l = self.e_local
         dev = x.device
+        x_in = x
         if self._route_spec is not None:
             from .deepseek import route
             idx, wts = route(self._route_spec, x.float() @ M.router_w.t(), M.router_corr)
             experts, weights = idx.to(torch.int32).contiguous(), wts.contiguous()
+        elif c.router_scoring == "llama4":  # top-1 on the logits; the expert sees x * sigmoid(logit)
+            logits = ops.linear(x, M.router_w, out_dtype=torch.float32)
+            topv, topi = logits.topk(k, -1)
+            experts = topi.to(torch.int32).contiguous()
+            weights = torch.ones_like(topv)
+            x_in = (x.float() * torch.sigmoid(topv)).to(x.dtype)
         else:
             logits = ops.linear(x, M.router_w, bias=M.router_b, out_dtype=torch.float32)
             experts = torch.empty(T, k, dtype=torch.int32, device=dev)
@@ -288,7 +319,7 @@ class MoEDecoderLM(DecoderLM):
             dn, inv = self.combiner.slots(n)  # symmetric slots the peers read
         ext().moe_align(experts, E_l, self.e_lo, E_l, bt, meta, tiles, perm, inv, cursor)
         a = torch.empty(n, H, dtype=torch.float16, device=dev)  # grouped GEMM operands are f16
-        ext().moe_gather(x, perm, meta, E_l, k, a)
+        ext().moe_gather(x_in, perm, meta, E_l, k, a)
         I = c.moe_intermediate_size
         s = scratch(dev)
         gu = torch.empty(n, I, dtype=torch.float16, device=dev)

@@ -43,7 +43,9 @@ class DecoderOracle:
     def __init__(self, cfg: DecoderConfig, weights: dict[str, torch.Tensor], device="cpu"):
         self.cfg = cfg
         self.device = torch.device(device)
-        from ..weights.aliases import FusedSplitView, canonical_name
+        from ..weights.aliases import FusedSplitView, Llama4View, canonical_name
+        if cfg.model_type == "llama4_text":  # feed_forward.* names, fused expert banks
+            weights = Llama4View(weights).as_dict()
         if FusedSplitView.needed(weights):  # Phi-3 fused qkv / gate_up
             v = FusedSplitView(weights, cfg.q_size, cfg.kv_size, cfg.intermediate_size)
             weights = {k: v[k] for k in v.keys()}
@@ -104,8 +106,20 @@ class DecoderOracle:
             k = R.rmsnorm(k, self.N(p + "k_norm.weight"), c.rms_norm_eps)
         inv, mult = (self.local_rope if self.local_rope is not None and c.layer_window(i) > 0
                      else (self.inv_freq, self.rope_mult))
-        q = R.rope(q, pos, inv, mult)
-        k = R.rope(k, pos, inv, mult)
+        chunk = 0
+        if c.rope_layers is not None and not c.uses_rope(i):  # Llama-4 NoPE layer
+            if c.attn_temperature_tuning:  # query temperature grows with log(position / floor_scale)
+                q = q * (torch.log1p(torch.floor((pos.float() + 1.0) / c.floor_scale)) * c.attn_scale + 1.0)[:, None, None]
+        elif c.rope_interleaved:
+            q = R.rope_interleaved(q, pos, inv, mult)
+            k = R.rope_interleaved(k, pos, inv, mult)
+            chunk = c.attention_chunk_size
+        else:
+            q = R.rope(q, pos, inv, mult)
+            k = R.rope(k, pos, inv, mult)
+        if c.qk_l2_norm and c.uses_rope(i):  # weightless RMS norm after RoPE (Llama-4)
+            q = q * torch.rsqrt(q.pow(2).mean(-1, keepdim=True) + c.rms_norm_eps)
+            k = k * torch.rsqrt(k.pow(2).mean(-1, keepdim=True) + c.rms_norm_eps)
         if kv.k[i] is None:
             kv.k[i], kv.v[i] = k, v
         else:
@@ -114,7 +128,7 @@ class DecoderOracle:
         kpos = torch.arange(kv.k[i].shape[0], device=x.device)
         sinks = self.W(p + "sinks") if c.attn_sinks else None
         o = R.attention(q, kv.k[i], kv.v[i], pos, kpos, c.attention_multiplier or 1.0 / math.sqrt(c.head_dim),
-                        causal=c.causal, window=c.layer_window(i), sinks=sinks, softcap=c.attn_softcap)
+                        causal=c.causal, window=c.layer_window(i), sinks=sinks, softcap=c.attn_softcap, chunk=chunk)
         y = self._mm(o.reshape(T, -1), p + "o_proj.weight")
         if (p + "o_proj.bias") in self.w:
             y = y + self.W(p + "o_proj.bias")
@@ -147,6 +161,20 @@ class DecoderOracle:
                 out += probs[:, slot:slot + 1] * y
             return out
         logits = x @ self.W(p + "gate.weight").T
+        if c.router_scoring == "llama4":  # top-k on logits; each expert sees x * sigmoid(its logit)
+            topv, topi = logits.topk(c.num_experts_per_tok, dim=-1)
+            sc = torch.sigmoid(topv)
+            out = torch.zeros_like(x)
+            for t in range(x.shape[0]):
+                for s in range(c.num_experts_per_tok):
+                    pe = p + f"experts.{int(topi[t, s])}."
+                    xs = x[t] * sc[t, s]
+                    g = xs @ self.W(pe + "gate_proj.weight").T
+                    u = xs @ self.W(pe + "up_proj.weight").T
+                    out[t] += (F.silu(g) * u) @ self.W(pe + "down_proj.weight").T
+            ps = p + "shared_experts."
+            return out + (F.silu(x @ self.W(ps + "gate_proj.weight").T) * (x @ self.W(ps + "up_proj.weight").T)) \
+                @ self.W(ps + "down_proj.weight").T
         if c.router_scoring == "sigmoid":  # glm4_moe: DeepSeek's group-limited sigmoid routing
             from types import SimpleNamespace
             from .deepseek import route

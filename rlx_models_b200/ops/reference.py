@@ -38,15 +38,27 @@ def rope(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor, scale
     return xf * cos[:, None, :] + rot * sin[:, None, :]
 
 
+def rope_interleaved(x: torch.Tensor, positions: torch.Tensor, inv_freq: torch.Tensor,
+                     scale: float = 1.0) -> torch.Tensor:
+    """Rotary embedding on interleaved pairs (x[2i], x[2i+1]) rotated by
+    positions * inv_freq[i] (Llama-4 / GPT-J layout). x: [T, H, D]."""
+    xf = x.float()
+    a, b = xf[..., 0::2], xf[..., 1::2]
+    ang = positions.float()[:, None] * inv_freq.float().to(x.device)[None, :]
+    cos, sin = (ang.cos() * scale)[:, None, :], (ang.sin() * scale)[:, None, :]
+    return torch.stack([a * cos - b * sin, a * sin + b * cos], -1).flatten(-2)
+
+
 def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     return F.silu(gate.float()) * up.float()
 
 
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Tensor, k_pos: torch.Tensor,
               scale: float, causal: bool = True, window: int = 0, sinks: torch.Tensor | None = None,
-              softcap: float = 0.0) -> torch.Tensor:
+              softcap: float = 0.0, chunk: int = 0) -> torch.Tensor:
     """Dense GQA attention. q: [Tq, Hq, D], k/v: [Tk, Hkv, D]; returns [Tq, Hq, D] fp32.
-    ``softcap`` > 0: scaled scores become softcap * tanh(s / softcap)."""
+    ``softcap`` > 0: scaled scores become softcap * tanh(s / softcap); ``chunk`` > 0:
+    a query sees only keys of its own ``chunk``-token block (chunked attention)."""
     Hq, Hkv = q.shape[1], k.shape[1]
     G = Hq // Hkv
     kf = k.float().repeat_interleave(G, dim=1)
@@ -57,6 +69,8 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_pos: torch.Te
     mask = torch.ones(q.shape[0], k.shape[0], dtype=torch.bool, device=q.device)
     if causal:
         mask &= k_pos[None, :] <= q_pos[:, None]
+    if chunk > 0:
+        mask &= (k_pos[None, :] // chunk) == (q_pos[:, None] // chunk)
     if window > 0:
         mask &= k_pos[None, :] > (q_pos[:, None] - window)
         if not causal:  # a bidirectional window: |q - k| < window

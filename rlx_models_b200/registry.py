@@ -56,7 +56,7 @@ def _dense(cfg, weights, device, tp_rank, tp_size, comm):
     return DecoderLM(cfg, weights, device=device, tp_rank=tp_rank, tp_size=tp_size, comm=comm)
 
 
-@register("gpt_oss", "qwen3_moe", "mixtral", "qwen2_moe", "glm4_moe", "minimax_m2")
+@register("gpt_oss", "qwen3_moe", "mixtral", "qwen2_moe", "glm4_moe", "minimax_m2", "llama4_text")
 def _moe(cfg, weights, device, tp_rank, tp_size, comm):
     from .models.moe import MoEDecoderLM
     return MoEDecoderLM(cfg, weights, device=device, ep_rank=tp_rank, ep_size=tp_size, comm=comm)

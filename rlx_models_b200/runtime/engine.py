@@ -159,6 +159,10 @@ class LLMEngine:
         self.cfg = cfg = config or EngineConfig()
         self.device = model.device
         mc = model.cfg
+        lim = getattr(model, "max_context", None)
+        if lim and cfg.max_model_len > lim:
+            raise ValueError(f"{type(model).__name__}: max_model_len {cfg.max_model_len} > {lim}, the context this "
+                             "model's kernels run exactly (e.g. Llama-4's chunked attention starts there)")
         self.max_blocks_per_seq = (cfg.max_model_len + BLOCK_SIZE - 1) // BLOCK_SIZE
         nb = cfg.num_blocks
         if nb <= 0:

@@ -4,6 +4,8 @@ the canonical layout the builders read (Qwen3-MoE style MoE names).
 Mixtral and MiniMax-M2: ``block_sparse_moe.gate`` is the router, ``block_sparse_moe.experts.{e}.w1 / w3 / w2``
 are gate / up / down. ``canonical_name`` maps a checkpoint name to the
 canonical one; ``CanonicalView`` presents a weight source under canonical names.
+Llama-4 (``Llama4View``) also changes tensor layouts: fused expert banks are
+split into per-expert matrices.
 """
 from __future__ import annotations
 
@@ -134,3 +136,81 @@ class ModelPrefixView:
 
     def __getitem__(self, name):
         return self.take(name)
+
+
+class Llama4View:
+    """Llama-4 text weights under the canonical MoE names.
+
+    ``feed_forward.`` -> ``mlp.``; the router ``feed_forward.router`` ->
+    ``mlp.gate``; the always-on shared expert ``feed_forward.shared_expert`` ->
+    ``mlp.shared_experts`` (ungated); the fused expert banks
+    ``feed_forward.experts.gate_up_proj`` [E, H, 2I] (gate = the first I
+    columns) and ``feed_forward.experts.down_proj`` [E, I, H] -> per-expert
+    ``mlp.experts.{e}.gate_proj / up_proj / down_proj.weight`` ([I, H], [I, H],
+    [H, I]). The multimodal release's ``language_model.`` prefix is dropped
+    (its vision tower is not part of the text model)."""
+
+    def __init__(self, weights):
+        self.w = weights
+        # peek: a fused bank is read once per expert
+        self.get = (lambda k: weights.peek(k)) if hasattr(weights, "peek") else (lambda k: weights[k])
+        self.map: dict[str, tuple] = {}
+        for n in list(weights.keys()):
+            c = n
+            for pre in ("language_model.", "model.language_model."):
+                if c.startswith(pre):
+                    c = c[len(pre):]
+                    if not c.startswith(("model.", "lm_head")):
+                        c = "model." + c
+            if c.startswith(("vision_model.", "multi_modal_projector.", "model.vision_model.",
+                             "model.multi_modal_projector.")):
+                continue
+            c = c.replace(".feed_forward.router.", ".mlp.gate.").replace(".feed_forward.shared_expert.",
+                                                                         ".mlp.shared_experts.")
+            c = c.replace(".feed_forward.", ".mlp.")
+            if c.endswith(".mlp.experts.gate_up_proj"):
+                pre = c[: -len("gate_up_proj")]
+                for e in range(self._n_experts(n)):
+                    self.map[pre + f"{e}.gate_proj.weight"] = (n, e, "gate")
+                    self.map[pre + f"{e}.up_proj.weight"] = (n, e, "up")
+            elif c.endswith(".mlp.experts.down_proj"):
+                pre = c[: -len("down_proj")]
+                for e in range(self._n_experts(n)):
+                    self.map[pre + f"{e}.down_proj.weight"] = (n, e, "down")
+            else:
+                self.map[c] = (n, None, None)
+        self._bank: dict[str, object] = {}
+
+    def _n_experts(self, n) -> int:
+        return int(self.w.shape(n)[0]) if hasattr(self.w, "shape") else int(self.w[n].shape[0])
+
+    def keys(self):
+        return list(self.map)
+
+    def __contains__(self, name):
+        return name in self.map
+
+    def _bank_of(self, n):
+        if n not in self._bank:
+            self._bank = {n: self.get(n)}  # one fused bank resident at a time
+        return self._bank[n]
+
+    def take(self, name, **kw):
+        n, e, part = self.map[name]
+        if e is None:
+            t = self.get(n)
+        else:
+            b = self._bank_of(n)[e]
+            if part == "down":
+                t = b.t()
+            else:
+                inter = b.shape[1] // 2
+                t = (b[:, :inter] if part == "gate" else b[:, inter:]).t()
+        dt, dev = kw.get("dtype"), kw.get("device")
+        return t if dt is None and dev is None else t.to(device=dev, dtype=dt)
+
+    def __getitem__(self, name):
+        return self.take(name)
+
+    def as_dict(self) -> dict:
+        return {k: self.take(k).contiguous() for k in self.map}

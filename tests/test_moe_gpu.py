@@ -2,6 +2,8 @@
 MXFP4 GEMM against a dequantized fp32 reference, and the full model against
 the fp32 oracle (sinks, sliding window beyond its length, YaRN, biases)."""
 
+import math
+
 import pytest
 import torch
 
@@ -208,6 +210,65 @@ def test_minimax_m2_vs_oracle(cuda):
     oracle = DecoderOracle(cfg, {k: v.float() for k, v in w.items()})
     for T in (37, 5):  # prefill-sized and decode-sized batches
         ids = torch.randint(0, cfg.vocab_size, (T,), generator=torch.Generator().manual_seed(T))
+        nb = (T + 15) // 16
+        fb = ForwardBatch(input_ids=ids.int().to(cuda), positions=torch.arange(T, dtype=torch.int32, device=cuda),
+                          slots=torch.arange(T, dtype=torch.int64, device=cuda), num_decode=0,
+                          pre_block_tables=torch.arange(nb, dtype=torch.int32, device=cuda).view(1, -1),
+                          pre_ctx_lens=torch.tensor([T], dtype=torch.int32, device=cuda),
+                          pre_cu_q=torch.tensor([0, T], dtype=torch.int32, device=cuda), pre_max_q=T)
+        lg = model.forward(fb, model.make_kv_cache(nb))
+        ref, _ = oracle.forward(ids)
+        row = ((lg.cpu().float() - ref).norm(dim=-1) / ref.norm(dim=-1))
+        assert row.median() < 2e-2, row
+        assert (row > 0.1).float().mean() <= 0.2, row
+
+
+def test_llama4_text_vs_oracle(cuda):
+    """Llama-4 text on the GPU: q / k rows reordered so the half-split RoPE kernel
+    rotates the interleaved pairs, weightless QK norm on the RoPE layers, zero
+    frequencies on the NoPE layer, top-1 sigmoid routing that scales the expert
+    input, shared expert, dense / MoE interleave, checkpoint names with fused
+    expert banks; against the oracle (HF semantics) on MXFP4-rounded experts,
+    below the context where chunking and the query temperature start."""
+    from rlx_models_b200.config import DecoderConfig
+    from rlx_models_b200.models.decoder import ForwardBatch
+    from rlx_models_b200.quant.mxfp4 import mxfp4_roundtrip
+    hf = dict(model_type="llama4_text", vocab_size=512, hidden_size=256, intermediate_size=128,
+              intermediate_size_mlp=384, num_hidden_layers=4, num_attention_heads=4, num_key_value_heads=2,
+              head_dim=64, num_local_experts=8, num_experts_per_tok=1, interleave_moe_layer_step=2,
+              attention_chunk_size=128, floor_scale=128, rms_norm_eps=1e-5, max_position_embeddings=256)
+    cfg = DecoderConfig.from_hf_dict(hf)
+    g = torch.Generator().manual_seed(4)
+    H, I, E = 256, 128, 8
+    r = lambda *s, f=1.0: (torch.randn(*s, generator=g) * f / math.sqrt(s[-1])).bfloat16()  # noqa: E731
+    w = {"model.embed_tokens.weight": torch.randn(512, H, generator=g).bfloat16(),
+         "model.norm.weight": (1 + 0.1 * torch.randn(H, generator=g)).bfloat16(), "lm_head.weight": r(512, H)}
+    for i in range(4):
+        p = f"model.layers.{i}."
+        w[p + "input_layernorm.weight"] = (1 + 0.1 * torch.randn(H, generator=g)).bfloat16()
+        w[p + "post_attention_layernorm.weight"] = (1 + 0.1 * torch.randn(H, generator=g)).bfloat16()
+        for n, o in (("q", 256), ("k", 128), ("v", 128)):
+            w[p + f"self_attn.{n}_proj.weight"] = r(o, H)
+        w[p + "self_attn.o_proj.weight"] = r(H, 256)
+        f = p + "feed_forward."
+        if i in cfg.moe_layers:
+            w[f + "router.weight"] = r(E, H, f=4.0)
+            gu = torch.randn(E, H, 2 * I, generator=g) / math.sqrt(H)
+            dn = torch.randn(E, I, H, generator=g) / math.sqrt(I)
+            # experts as the MXFP4 rounding the GPU path stores (per output row, along the input)
+            gu = torch.stack([mxfp4_roundtrip(gu[e].t().contiguous()).t() for e in range(E)])
+            dn = torch.stack([mxfp4_roundtrip(dn[e].t().contiguous()).t() for e in range(E)])
+            w[f + "experts.gate_up_proj"], w[f + "experts.down_proj"] = gu.bfloat16(), dn.bfloat16()
+            for n, (o, ii) in (("gate", (I, H)), ("up", (I, H)), ("down", (H, I))):
+                w[f + f"shared_expert.{n}_proj.weight"] = r(o, ii)
+        else:
+            for n, (o, ii) in (("gate", (384, H)), ("up", (384, H)), ("down", (H, 384))):
+                w[f + f"{n}_proj.weight"] = r(o, ii)
+    model = MoEDecoderLM(cfg, w, device=cuda)
+    assert model.max_context == 128
+    oracle = DecoderOracle(cfg, {k: v.float() for k, v in w.items()})
+    for T in (45, 6):
+        ids = torch.randint(0, 512, (T,), generator=torch.Generator().manual_seed(T))
         nb = (T + 15) // 16
         fb = ForwardBatch(input_ids=ids.int().to(cuda), positions=torch.arange(T, dtype=torch.int32, device=cuda),
                           slots=torch.arange(T, dtype=torch.int64, device=cuda), num_decode=0,
