@@ -230,19 +230,24 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
 
 def load_transcriber(model: str, *, device: str | torch.device = "cuda", language: str | None = "en",
                      task: str = "transcribe"):
-    """Whisper checkpoint (local dir / offline HF id) -> object with
-    ``transcribe(audio, sample_rate)``."""
+    """Whisper or Parakeet-CTC checkpoint (local dir / offline HF id) -> object
+    with ``transcribe(audio, sample_rate)``."""
+    import json
     from .models.whisper import SpeechToText, WhisperConfig, WhisperModel
     path = resolve_model_path(model)
     if path is None:
-        raise FileNotFoundError(f"no local Whisper checkpoint for {model!r}")
+        raise FileNotFoundError(f"no local speech checkpoint for {model!r}")
     with open(os.path.join(path, "config.json")) as f:
-        import json
-        cfg = WhisperConfig.from_dict(json.load(f))
+        raw = json.load(f)
     tok = None
     if any(os.path.exists(os.path.join(path, f)) for f in ("tokenizer.json", "tokenizer_config.json", "vocab.json")):
         from transformers import AutoTokenizer
         tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+    if raw.get("model_type") == "parakeet_ctc":
+        from .models.parakeet import ParakeetConfig, ParakeetCTC, ParakeetTranscriber
+        return ParakeetTranscriber(ParakeetCTC(ParakeetConfig.from_dict(raw), WeightMap.from_dir(path), device=device),
+                                   tok)
+    cfg = WhisperConfig.from_dict(raw)
     return SpeechToText(WhisperModel(cfg, WeightMap.from_dir(path), device=device), tok, language, task)
 
 

@@ -1,5 +1,5 @@
 """Encoder families on the GPU (bf16 GEMMs) against their CPU fp32 paths:
-NomicBERT text embeddings, CLIP and DINOv2 image embeddings."""
+NomicBERT text embeddings, CLIP and DINOv2 image embeddings, Parakeet CTC logits."""
 import math
 
 import numpy as np
@@ -71,3 +71,18 @@ def test_dinov2_gpu_matches_cpu(cuda, registers):
     ref = Dinov2Encoder(cfg, sd).embed(px)
     got = Dinov2Encoder(cfg, sd, device=cuda).embed(px)
     assert _cos(got, ref).min() > 0.999
+
+
+def test_parakeet_ctc_gpu_matches_cpu(cuda):
+    import transformers as T
+    from rlx_models_b200.models.parakeet import ParakeetConfig, ParakeetCTC
+    enc = dict(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, intermediate_size=512,
+               conv_kernel_size=9, subsampling_factor=8, subsampling_conv_channels=32, num_mel_bins=80)
+    hc = T.ParakeetCTCConfig(encoder_config=enc, vocab_size=129, pad_token_id=128)
+    sd = {k: v.detach() for k, v in _rand(T.ParakeetForCTC(hc)).state_dict().items()}
+    cfg = ParakeetConfig.from_dict(hc.to_dict())
+    feats = torch.randn(2, 200, 80, generator=torch.Generator().manual_seed(3))
+    ref, _ = ParakeetCTC(cfg, sd).logits(feats, torch.tensor([200, 150]))
+    got, n = ParakeetCTC(cfg, sd, device=cuda).logits(feats, torch.tensor([200, 150]))
+    assert _cos(got[0], ref[0]).min() > 0.995
+    assert _cos(got[1, :int(n[1])], ref[1, :int(n[1])]).min() > 0.995
