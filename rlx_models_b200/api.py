@@ -216,6 +216,9 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
             weights = MLXWeights(path, device=device)
         else:
             weights = WeightMap.from_dir(path)
+            from .weights.aliases import LanguageModelView
+            if getattr(cfg, "model_type", "") != "llama4_text" and LanguageModelView.applies(weights):
+                weights = LanguageModelView(weights)  # the text model of a multimodal checkpoint
         try:
             from .tokenizer import load_tokenizer
             tok = load_tokenizer(path)

@@ -160,6 +160,15 @@ class DecoderConfig:
     def from_hf_dict(cls, raw: dict) -> "DecoderConfig":
         d = legacy_rope_keys(merge_text_config(raw))
         mt = d.get("model_type", "qwen3")
+        if mt in ("qwen3_vl", "qwen3_vl_text", "qwen3_vl_moe", "qwen3_vl_moe_text"):
+            # Qwen3-VL's language model is Qwen3 (dense or MoE); for text its interleaved
+            # multimodal RoPE (three equal position ids) is the plain 1-D RoPE
+            mt = "qwen3_moe" if "moe" in mt else "qwen3"
+            d = dict(d, model_type=mt)
+            if d.get("num_experts") is None and d.get("num_local_experts") is not None:
+                d["num_experts"] = d["num_local_experts"]  # the MoE config's serialised name
+            if isinstance(d.get("rope_scaling"), dict) and d["rope_scaling"].get("rope_type", "default") == "default":
+                d["rope_scaling"] = None
         kw: dict[str, Any] = {}
         fields = {f.name for f in dataclasses.fields(cls)}
         for k in fields:

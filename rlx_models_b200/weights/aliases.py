@@ -214,3 +214,62 @@ class Llama4View:
 
     def as_dict(self) -> dict:
         return {k: self.take(k).contiguous() for k in self.map}
+
+
+class LanguageModelView:
+    """The text model inside a multimodal checkpoint, under the decoder's names:
+    ``model.language_model.X`` -> ``model.X`` (the vision tower ``model.visual.*``
+    and any projector are left out; ``lm_head`` stays), and transformers'
+    fused expert banks ``mlp.experts.gate_up_proj`` [E, 2I, H] /
+    ``mlp.experts.down_proj`` [E, H, I] seen as per-expert matrices."""
+
+    _DROP = ("model.visual.", "visual.", "model.vision_tower.", "vision_tower.", "model.multi_modal_projector.",
+             "multi_modal_projector.", "mtp.")
+
+    def __init__(self, weights):
+        self.w = weights
+        self.get = (lambda k: weights.peek(k)) if hasattr(weights, "peek") else (lambda k: weights[k])
+        self.map: dict[str, tuple] = {}
+        for n in list(weights.keys()):
+            if n.startswith(self._DROP):
+                continue
+            c = n.replace("model.language_model.", "model.", 1)
+            if c.endswith("mlp.experts.gate_up_proj"):
+                pre = c[: -len("gate_up_proj")]
+                for e in range(self._dim0(n)):
+                    self.map[pre + f"{e}.gate_proj.weight"] = (n, e, "gate")
+                    self.map[pre + f"{e}.up_proj.weight"] = (n, e, "up")
+            elif c.endswith("mlp.experts.down_proj"):
+                pre = c[: -len("down_proj")]
+                for e in range(self._dim0(n)):
+                    self.map[pre + f"{e}.down_proj.weight"] = (n, e, "down")
+            else:
+                self.map[c] = (n, None, None)
+
+    def _dim0(self, n) -> int:
+        return int(self.w.shape(n)[0]) if hasattr(self.w, "shape") else int(self.w[n].shape[0])
+
+    @staticmethod
+    def applies(weights) -> bool:
+        return any(k.startswith("model.language_model.") for k in weights.keys())
+
+    def keys(self):
+        return list(self.map)
+
+    def __contains__(self, name):
+        return name in self.map
+
+    def take(self, name, **kw):
+        n, e, part = self.map[name]
+        t = self.get(n) if e is None else self.get(n)[e]
+        if part in ("gate", "up"):
+            inter = t.shape[0] // 2
+            t = t[:inter] if part == "gate" else t[inter:]
+        dt, dev = kw.get("dtype"), kw.get("device")
+        return t if dt is None and dev is None else t.to(device=dev, dtype=dt)
+
+    def __getitem__(self, name):
+        return self.take(name)
+
+    def as_dict(self) -> dict:
+        return {k: self.take(k).contiguous() for k in self.map}

@@ -134,3 +134,43 @@ def test_gemma_vs_oracle(cuda, family, D):
     lg2, _ = oracle.forward(torch.tensor(ids + toks[:-1]))
     for t, r in zip(toks, lg2[len(ids) - 1:]):
         assert r[t] >= r.max() - 0.05 * (r.max() - r.min())
+
+
+def test_qwen3_vl_text_checkpoint_loads_and_serves(cuda, tmp_path):
+    """A Qwen3-VL checkpoint (the text model under ``model.language_model.``, a
+    vision tower beside it) loads through ``api.load`` as its Qwen3 language model
+    and serves text; first generated tokens against the oracle."""
+    import json
+    import math
+    import transformers as T
+    from rlx_models_b200.api import load
+    from rlx_models_b200.runtime.engine import EngineConfig, SamplingParams
+    from rlx_models_b200.weights.aliases import LanguageModelView
+    from rlx_models_b200.weights.safetensors_io import save_file
+    tc = dict(vocab_size=512, hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+              num_key_value_heads=2, head_dim=64, tie_word_embeddings=False,
+              rope_parameters={"rope_type": "default", "rope_theta": 1e6, "mrope_section": [8, 12, 12],
+                               "mrope_interleaved": True})
+    vc = dict(depth=1, hidden_size=32, intermediate_size=64, num_heads=2, out_hidden_size=256,
+              deepstack_visual_indexes=[0])
+    cfg = T.Qwen3VLConfig(text_config=tc, vision_config=vc)
+    m = T.Qwen3VLForConditionalGeneration(cfg)
+    torch.manual_seed(0)
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if p.dim() >= 2:
+                p.normal_(0, 1 / math.sqrt(p.shape[-1]))
+            else:
+                p.normal_(1.0 if n.endswith("norm.weight") else 0.0, 0.1)
+    sd = {k: v.detach().bfloat16().contiguous() for k, v in m.state_dict().items()}
+    d = tmp_path / "q3vl"
+    d.mkdir()
+    (d / "config.json").write_text(json.dumps(cfg.to_dict()))
+    save_file(sd, str(d / "model.safetensors"))
+    llm = load(str(d), device=cuda, engine_config=EngineConfig(max_num_seqs=2, max_model_len=128, num_blocks=32))
+    prompt = torch.randint(0, 500, (30,), generator=torch.Generator().manual_seed(3)).tolist()
+    out = llm.generate(prompt, SamplingParams(max_new_tokens=4, ignore_eos=True))[0].token_ids
+    oracle = DecoderOracle(llm.config, {k: v.float() for k, v in LanguageModelView(sd).as_dict().items()})
+    lg, _ = oracle.forward(torch.tensor(prompt + out[:-1]))
+    for t, r in zip(out, lg[len(prompt) - 1:]):
+        assert r[t] >= r.max() - 0.05 * (r.max() - r.min())
