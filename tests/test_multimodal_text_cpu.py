@@ -1,6 +1,6 @@
-"""Qwen3-VL (dense and MoE) text path: the language model of the multimodal
-checkpoint (``model.language_model.*``, fused expert banks) through the
-decoder's config and names, against transformers on text-only input."""
+"""Text paths of multimodal checkpoints (Qwen3-VL dense and MoE, Gemma-3):
+the language model (``model.language_model.*``, fused expert banks) through
+the decoder's config and names, against transformers on text-only input."""
 import math
 
 import pytest
@@ -47,3 +47,23 @@ def test_qwen3_vl_text_matches_transformers(moe):
     o = DecoderOracle(dc, LanguageModelView(sd).as_dict())
     lg, _ = o.forward(ids[0])
     assert (lg - ref).abs().max() < 1e-3, (lg - ref).abs().max()
+
+
+def test_gemma3_multimodal_text_matches_transformers():
+    import transformers as T
+    from rlx_models_b200.config import DecoderConfig
+    from rlx_models_b200.models.oracle import DecoderOracle
+    from rlx_models_b200.weights.aliases import LanguageModelView
+    tc = dict(vocab_size=300, hidden_size=64, intermediate_size=96, num_hidden_layers=2, num_attention_heads=4,
+              num_key_value_heads=2, head_dim=16, sliding_window=8)
+    vc = dict(hidden_size=32, intermediate_size=64, num_hidden_layers=1, num_attention_heads=2, image_size=28,
+              patch_size=14)
+    cfg = T.Gemma3Config(text_config=tc, vision_config=vc, mm_tokens_per_image=4, image_token_index=299)
+    m = _rand(T.Gemma3ForConditionalGeneration(cfg))
+    ids = torch.randint(0, 290, (1, 19), generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        ref = m(input_ids=ids).logits[0]
+    sd = {k: v.detach() for k, v in m.state_dict().items()}
+    o = DecoderOracle(DecoderConfig.from_hf_dict(cfg.to_dict()), LanguageModelView(sd).as_dict())
+    lg, _ = o.forward(ids[0])
+    assert (lg - ref).abs().max() < 1e-3
