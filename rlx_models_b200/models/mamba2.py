@@ -40,7 +40,7 @@ import torch.nn.functional as F
 from ..ops import rope_inv_freq
 from ..runtime.kv_cache import BLOCK_SIZE, PagedKVCache
 
-SSM_TYPES = ("mamba2", "bamba")
+SSM_TYPES = ("mamba2", "bamba", "nemotron_h")
 
 
 @dataclass
@@ -103,6 +103,12 @@ class SSMConfig:
 
     def is_moe(self, i: int) -> bool:
         return bool(self.layer_types) and self.layer_types[i] == "moe"
+
+    def is_mlp(self, i: int) -> bool:
+        return bool(self.layer_types) and self.layer_types[i] == "mlp"
+
+    def is_mamba(self, i: int) -> bool:
+        return not (self.is_attention(i) or self.is_moe(i) or self.is_mlp(i))
 
     @property
     def rotary_dim(self) -> int:
@@ -351,6 +357,9 @@ class SSMOracle:
             x = self._rms(h, p + bn + ".weight")
             if c.is_moe(i):
                 h = h + self._moe(p + mix, x)
+            elif c.is_mlp(i):  # Nemotron-H squared-ReLU MLP block
+                m = p + mix
+                h = h + torch.relu(x @ self._t(m + "up_proj.weight").t()).square() @ self._t(m + "down_proj.weight").t()
             elif c.is_attention(i):
                 a, D, nh, nkv = p + ("mixer." if c.model_type == "nemotron_h" else "self_attn."), c.attn_head_dim, c.num_attention_heads, c.num_key_value_heads
                 q = (x @ self._t(a + "q_proj.weight").t()).view(S, nh, D)
@@ -387,7 +396,7 @@ class SSMCache:
 
     def __init__(self, cfg: SSMConfig, num_blocks: int, num_slots: int, device):
         n_attn = len(cfg.attn_layer_indices)
-        n_ssm = cfg.num_hidden_layers - n_attn
+        n_ssm = sum(cfg.is_mamba(i) for i in range(cfg.num_hidden_layers))
         hkv, D = (cfg.num_key_value_heads, cfg.attn_head_dim) if n_attn else (1, 64)
         self.paged = PagedKVCache(max(1, n_attn), num_blocks if n_attn else 1, hkv, D, device)
         self.k, self.v = self.paged.k, self.paged.v
@@ -401,9 +410,30 @@ class SSMCache:
         return self.paged.layer(i)
 
 
+class _BackboneNames:
+    """A weight source with ``model.*`` names seen under ``backbone.*``."""
+
+    def __init__(self, weights):
+        self.w = weights
+        self.map = {("backbone." + k[6:] if k.startswith("model.") else k): k for k in weights.keys()}
+
+    def keys(self):
+        return list(self.map)
+
+    def __contains__(self, name):
+        return name in self.map
+
+    def take(self, name, **kw):
+        n = self.map[name]
+        return self.w.take(n, **kw) if hasattr(self.w, "take") else self.w[n]
+
+    def __getitem__(self, name):
+        return self.take(name)
+
+
 class _Layer:
     __slots__ = ("ln1", "ln2", "w_gu", "wd", "wo", "attn", "idx", "wqkv", "w_in", "conv_w", "conv_b", "A_log",
-                 "dt_bias", "Dp", "norm_w")
+                 "dt_bias", "Dp", "norm_w", "kind", "up", "moe")
 
 
 class SSMHybridLM:
@@ -416,10 +446,16 @@ class SSMHybridLM:
         self.hkv = c.num_key_value_heads or 1
         self.D = c.attn_head_dim or 64
         if c.attn_layer_indices:
-            inv, self.rope_mult = rope_inv_freq(c.rotary_dim, c.rope_theta, None, c.max_position_embeddings)
+            if c.rotary_dim:
+                inv, self.rope_mult = rope_inv_freq(c.rotary_dim, c.rope_theta, None, c.max_position_embeddings)
+            else:  # NoPE attention (Nemotron-H): zero frequencies rotate nothing
+                inv, self.rope_mult = torch.zeros(c.attn_head_dim // 2), 1.0
             self.inv_freq = inv.to(dev)
             self.scale = c.attn_head_dim ** -0.5
+        if c.model_type == "nemotron_h" and "backbone.embeddings.weight" not in weights:
+            weights = _BackboneNames(weights)  # transformers' ``model.`` names -> the releases' ``backbone.``
         get = _getter(weights)
+        self._weights = weights
         emb, fin, lay, bn, mix = _names(c)
 
         def g(n):
@@ -446,8 +482,14 @@ class SSMHybridLM:
                 L.w_gu = dv(ops.interleave_gate_up(g(f + "gate_proj.weight"), g(f + "up_proj.weight")))
                 L.wd = dv(g(f + "down_proj.weight"))
             L.attn = c.is_attention(i)
-            if L.attn:
-                a = p + "self_attn."
+            L.kind = "attention" if L.attn else ("moe" if c.is_moe(i) else ("mlp" if c.is_mlp(i) else "mamba"))
+            L.moe = None
+            if L.kind == "mlp":  # Nemotron-H squared-ReLU MLP: h += relu(x W_up)^2 W_down
+                L.up, L.wo = dv(g(p + mix + "up_proj.weight")), dv(g(p + mix + "down_proj.weight"))
+            elif L.kind == "moe":
+                L.moe = self._load_moe(g, dv, p + mix)
+            elif L.attn:
+                a = p + ("mixer." if c.model_type == "nemotron_h" else "self_attn.")
                 L.idx, n_attn = n_attn, n_attn + 1
                 L.wqkv = dv(torch.cat([g(a + "q_proj.weight"), g(a + "k_proj.weight"), g(a + "v_proj.weight")], 0))
                 L.wo = dv(g(a + "o_proj.weight"))
@@ -462,6 +504,52 @@ class SSMHybridLM:
                 L.wo = dv(g(m + "out_proj.weight"))
             self.layers.append(L)
         self.n_attn = n_attn
+
+    def _load_moe(self, g, dv, m: str):
+        """Nemotron-H MoE block: router + correction bias, squared-ReLU experts packed
+        for the grouped MXFP4 GEMM with the gate rows set to the up rows (its epilogue
+        computes u * g * sigmoid(alpha g); with g = u and a huge alpha that is
+        relu(u) * u = relu(u)^2), latent projections, squared-ReLU shared expert."""
+        from types import SimpleNamespace
+        from .moe import pack_experts
+        c = self.cfg
+        dev = self.device
+        E = c.n_routed_experts
+
+        def bank(which):  # per-expert matrices from a fused [E, out, in] bank or per-expert tensors
+            fused = m + f"experts.{which}"
+            if fused in self._weights:
+                b = g(fused).float()
+                return [b[e] for e in range(E)]
+            return [g(m + f"experts.{e}.{which}.weight").float() for e in range(E)]
+        ups, downs = bank("up_proj"), bank("down_proj")
+        gu_w, gu_exp, dn_w, dn_exp = pack_experts(ups, ups, downs)
+        del ups, downs
+        s = m + "shared_experts."
+        return SimpleNamespace(
+            router=g(m + "gate.weight").to(dev, torch.float32).contiguous(),
+            corr=g(m + "gate.e_score_correction_bias").to(dev, torch.float32),
+            gu_w=gu_w, gu_exp=gu_exp, dn_w=dn_w, dn_exp=dn_exp,
+            fc1=dv(g(m + "fc1_latent_proj.weight")) if (m + "fc1_latent_proj.weight") in self._weights else None,
+            fc2=dv(g(m + "fc2_latent_proj.weight")) if (m + "fc2_latent_proj.weight") in self._weights else None,
+            sh_up=dv(g(s + "up_proj.weight")), sh_down=dv(g(s + "down_proj.weight")),
+            spec=SimpleNamespace(scoring_func="sigmoid", topk_method="noaux_tc", n_group=c.n_group,
+                                 topk_group=c.topk_group, num_experts_per_tok=c.num_experts_per_tok,
+                                 norm_topk_prob=c.norm_topk_prob, routed_scaling_factor=c.routed_scaling_factor))
+
+    def _moe(self, M, x: torch.Tensor) -> torch.Tensor:
+        from .. import ops
+        from .deepseek import route
+        from .moe import routed_experts
+        idx, wts = route(M.spec, x.float() @ M.router.t(), M.corr)
+        xl = ops.linear(x, M.fc1) if M.fc1 is not None else x
+        out = routed_experts(xl.contiguous(), idx.to(torch.int32).contiguous(), wts.float().contiguous(), M.gu_w,
+                             M.gu_exp, M.dn_w, M.dn_exp, self.cfg.n_routed_experts,
+                             self.cfg.moe_intermediate_size, alpha=1e30)
+        if M.fc2 is not None:
+            out = ops.linear(out, M.fc2)
+        sh = torch.relu(ops.linear(x, M.sh_up).float()).square().to(x.dtype)
+        return out + ops.linear(sh, M.sh_down)
 
     def make_kv_cache(self, num_blocks: int, num_slots: int = 8) -> SSMCache:
         return SSMCache(self.cfg, num_blocks, num_slots, self.device)
@@ -523,7 +611,7 @@ class SSMHybridLM:
                 kv.conv[L.idx, slot, (start + n) & 1] = new_win
                 kv.ssm[L.idx, slot] = S
                 y[a:b] = yy.to(torch.bfloat16)
-        return gated_norm(y, proj[:, :I], L.norm_w, c.rms_norm_eps).to(torch.bfloat16)
+        return gated_norm(y, proj[:, :I], L.norm_w, c.rms_norm_eps, c.norm_groups).to(torch.bfloat16)
 
     def forward_hidden(self, fb, kv: SSMCache) -> torch.Tensor:
         from .. import ops
@@ -538,8 +626,14 @@ class SSMHybridLM:
         x = ops.rmsnorm(h, self.layers[0].ln1, c.rms_norm_eps)
         n = len(self.layers)
         for i, L in enumerate(self.layers):
-            a = self._attention(L, x, fb, kv) if L.attn else self._ssm(L, x, fb, kv, slots)
             nw = self.layers[i + 1].ln1 if i + 1 < n else self.norm
+            if L.kind == "moe":  # h += moe(x); x = rmsnorm(h) for the next block
+                x = ops.rmsnorm(self._moe(L.moe, x), nw, c.rms_norm_eps, residual=h, residual_out=h)
+                continue
+            if L.kind == "mlp":
+                a = torch.relu(ops.linear(x, L.up).float()).square().to(x.dtype)
+            else:
+                a = self._attention(L, x, fb, kv) if L.attn else self._ssm(L, x, fb, kv, slots)
             if L.w_gu is None:
                 x = comm.rowpar_add_norm(a, L.wo, h, nw)
                 continue

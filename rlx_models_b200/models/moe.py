@@ -69,10 +69,12 @@ def pack_experts(gates, ups, downs):
 
 
 def routed_experts(x: torch.Tensor, experts: torch.Tensor, weights: torch.Tensor, gu_w, gu_exp, dn_w, dn_exp,
-                   num_experts: int, inter: int) -> torch.Tensor:
+                   num_experts: int, inter: int, alpha: float = 1.0) -> torch.Tensor:
     """sum_s weights[t, s] * expert_{experts[t, s]}(x[t]) on the grouped MXFP4
-    GEMM (SwiGLU experts, no biases, every expert local): align -> gather ->
-    gate/up GEMM with SwiGLU -> down GEMM scaled by the router weight -> combine."""
+    GEMM (no biases, every expert local): align -> gather -> gate/up GEMM with
+    the u * g * sigmoid(alpha g) epilogue (SwiGLU at alpha = 1; relu(u)^2 for
+    experts packed with gate = up and a huge alpha) -> down GEMM scaled by the
+    router weight -> combine."""
     T, H = x.shape
     k = experts.shape[1]
     E = num_experts
@@ -89,7 +91,8 @@ def routed_experts(x: torch.Tensor, experts: torch.Tensor, weights: torch.Tensor
     ext().moe_gather(x, perm, meta, E, k, xa)
     s = scratch(dev)
     gu = torch.empty(n, inter, dtype=torch.float16, device=dev)
-    ext().moe_gemm(xa, gu_w, gu_exp, 2 * inter, None, None, perm, meta, tiles, gu, True, 1e30, 1.0, bt, s.status, 0.0)
+    ext().moe_gemm(xa, gu_w, gu_exp, 2 * inter, None, None, perm, meta, tiles, gu, True, 1e30, float(alpha), bt,
+                   s.status, 0.0)
     dn = torch.empty(n, H, dtype=torch.bfloat16, device=dev)
     ext().moe_gemm(gu, dn_w, dn_exp, H, None, weights.reshape(-1), perm, meta, tiles, dn, False, 0.0, 0.0, bt,
                    s.status)

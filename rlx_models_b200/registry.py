@@ -78,7 +78,7 @@ def _qwen35(cfg, weights, device, tp_rank, tp_size, comm):
     return Qwen35LM(cfg, weights, device=device)
 
 
-@register("mamba2", "bamba")
+@register("mamba2", "bamba", "nemotron_h")
 def _ssm(cfg, weights, device, tp_rank, tp_size, comm):
     from .models.mamba2 import SSMHybridLM
     if tp_size != 1:

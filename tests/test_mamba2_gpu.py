@@ -75,3 +75,53 @@ def test_ssm_model_and_engine_vs_oracle(cuda, family):
         for t, r in zip(toks, oracle.logits(p + toks[:-1])[len(p) - 1:]):
             assert r[t] >= r.max() - 0.05 * (r.max() - r.min())
     assert [o.token_ids for o in llm.generate(prompts, sp)] == singles
+
+
+@pytest.mark.parametrize("latent", [None, 128])
+def test_nemotron_h_moe_model_and_engine_vs_oracle(cuda, latent):
+    """Nemotron-H on the GPU: Mamba-2, NoPE attention and MoE blocks; the
+    squared-ReLU experts run on the grouped MXFP4 GEMM (gate rows = up rows,
+    relu(u) * u epilogue), optionally inside the latent projections; oracle on
+    the same MXFP4-rounded experts."""
+    import math
+    from transformers import NemotronHConfig, NemotronHForCausalLM
+    from rlx_models_b200.api import LLM
+    from rlx_models_b200.quant.mxfp4 import mxfp4_roundtrip
+    from rlx_models_b200.runtime.engine import EngineConfig, SamplingParams
+    d = dict(vocab_size=512, hidden_size=256, layers_block_type=["mamba", "moe", "attention", "moe", "mamba"],
+             num_attention_heads=4, num_key_value_heads=2, head_dim=64, mamba_num_heads=8, mamba_head_dim=64,
+             ssm_state_size=128, n_groups=2, conv_kernel=4, expand=2, n_routed_experts=8, num_experts_per_tok=2,
+             moe_intermediate_size=128, moe_shared_expert_intermediate_size=128, moe_latent_size=latent, n_group=2,
+             topk_group=1, routed_scaling_factor=2.0, norm_topk_prob=True, chunk_size=16, tie_word_embeddings=False)
+    torch.manual_seed(0)
+    m = NemotronHForCausalLM(NemotronHConfig(**d)).eval()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if p.dim() >= 2 and "conv1d" not in n:
+                p.normal_(0, 1 / math.sqrt(p.shape[-1]))
+            elif n.endswith("norm.weight"):
+                p.normal_(1.0, 0.2)
+        for mod in m.modules():
+            if hasattr(mod, "e_score_correction_bias"):
+                mod.e_score_correction_bias.normal_(0, 0.2)
+    w = {}
+    for k, v in m.state_dict().items():
+        v = v.detach().float()
+        if ".experts." in k:  # the MXFP4 rounding the grouped GEMM stores (along each row's input dim)
+            v = torch.stack([mxfp4_roundtrip(e.contiguous()) for e in v]) if v.dim() == 3 else mxfp4_roundtrip(v)
+        w[k] = v.bfloat16()
+    cfg = SSMConfig.from_dict(m.config.to_dict())
+    llm = LLM(SSMHybridLM(cfg, w, device=cuda), EngineConfig(max_num_seqs=4, max_model_len=256, num_blocks=64,
+                                                             chunk_size=40))
+    oracle = SSMOracle(cfg, {k: v.float() for k, v in w.items()})
+    g = torch.Generator().manual_seed(5)
+    ids = torch.randint(0, 512, (61,), generator=g).tolist()
+    lg = llm.logits(ids).float().cpu()
+    ref = oracle.logits(ids)
+    row = (lg - ref).norm(dim=-1) / ref.norm(dim=-1)
+    assert row.median() < 3e-2 and (row > 0.1).float().mean() <= 0.1, row
+    prompts = [torch.randint(0, 512, (n,), generator=g).tolist() for n in (7, 95)]
+    sp = SamplingParams(max_new_tokens=6, ignore_eos=True)
+    for p, o in zip(prompts, llm.generate(prompts, sp)):
+        for t, r in zip(o.token_ids, oracle.logits(p + o.token_ids[:-1])[len(p) - 1:]):
+            assert r[t] >= r.max() - 0.05 * (r.max() - r.min())

@@ -51,3 +51,34 @@ def test_grouped_gated_norm():
     assert SSMConfig.from_dict({"model_type": "nemotron_h", "hidden_size": 64, "num_attention_heads": 4,
                                 "hybrid_override_pattern": "M*ME"}).layer_types == ["mamba", "attention", "mamba",
                                                                                      "moe"]
+
+
+def test_nemotron_h_mlp_block():
+    """Squared-ReLU MLP blocks ("-" in the hybrid pattern of the dense Nemotron-H
+    releases): h += relu(rmsnorm(h) W_up)^2 W_down, the formula of transformers'
+    NemotronHMLP with mlp_hidden_act relu2."""
+    from transformers import NemotronHConfig
+    from transformers.models.nemotron_h.modeling_nemotron_h import NemotronHMLP
+    cfg = SSMConfig.from_dict(dict(model_type="nemotron_h", vocab_size=64, hidden_size=32,
+                                   hybrid_override_pattern="-", num_attention_heads=4, num_key_value_heads=2,
+                                   head_dim=8, mamba_num_heads=4, mamba_head_dim=8, ssm_state_size=8,
+                                   tie_word_embeddings=False))
+    assert cfg.is_mlp(0) and not cfg.is_mamba(0)
+    mlp = NemotronHMLP(NemotronHConfig(hidden_size=32, intermediate_size=48, mlp_hidden_act="relu2")).eval()
+    g = torch.Generator().manual_seed(0)
+    w = {"backbone.embeddings.weight": torch.randn(64, 32, generator=g),
+         "backbone.norm_f.weight": torch.rand(32, generator=g) + 0.5,
+         "backbone.layers.0.norm.weight": torch.rand(32, generator=g) + 0.5,
+         "backbone.layers.0.mixer.up_proj.weight": mlp.up_proj.weight.detach(),
+         "backbone.layers.0.mixer.down_proj.weight": mlp.down_proj.weight.detach(),
+         "lm_head.weight": torch.randn(64, 32, generator=g)}
+    ids = torch.randint(0, 64, (9,), generator=g)
+    got = SSMOracle(cfg, w).logits(ids)
+
+    def rms(x, wt):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + cfg.rms_norm_eps) * wt
+    h = w["backbone.embeddings.weight"][ids]
+    with torch.no_grad():
+        h = h + mlp(rms(h, w["backbone.layers.0.norm.weight"]))
+    ref = rms(h, w["backbone.norm_f.weight"]) @ w["lm_head.weight"].t()
+    assert (got - ref).abs().max() < 1e-4
