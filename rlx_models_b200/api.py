@@ -422,10 +422,10 @@ class ImageEmbedder:
 
 def load_image_embedder(model: str, *, device: str | torch.device = "cuda") -> ImageEmbedder:
     """CLIP / SigLIP checkpoint (vision model alone or the full dual encoder) or
-    a DINOv2 backbone (with or without registers; local dir / offline HF id)
-    -> ``ImageEmbedder``."""
+    a DINOv2 (with or without registers) / DINOv3 backbone (local dir / offline
+    HF id) -> ``ImageEmbedder``."""
     import json
-    from .models.vit import Dinov2Config, Dinov2Encoder, VisionConfig, VisionEncoder
+    from .models.vit import Dinov2Config, Dinov2Encoder, Dinov3Config, Dinov3Encoder, VisionConfig, VisionEncoder
     path = resolve_model_path(model)
     if path is None:
         raise FileNotFoundError(f"no local vision checkpoint for {model!r}")
@@ -433,6 +433,8 @@ def load_image_embedder(model: str, *, device: str | torch.device = "cuda") -> I
         raw = json.load(f)
     if raw.get("model_type") in ("dinov2", "dinov2_with_registers"):
         return ImageEmbedder(Dinov2Encoder(Dinov2Config.from_dict(raw), WeightMap.from_dir(path), device=device))
+    if raw.get("model_type") == "dinov3_vit":
+        return ImageEmbedder(Dinov3Encoder(Dinov3Config.from_dict(raw), WeightMap.from_dir(path), device=device))
     cfg = VisionConfig.from_dict(raw)
     return ImageEmbedder(VisionEncoder(cfg, WeightMap.from_dir(path), device=device))
 

@@ -1,6 +1,7 @@
 """Vision transformers for image embeddings: the CLIP and SigLIP vision towers
 (HF ``vision_model.*`` names, standalone or inside the full CLIP / SigLIP
-checkpoints) and the DINOv2 self-supervised backbone (``Dinov2Encoder``).
+checkpoints) and the DINOv2 / DINOv3 self-supervised backbones
+(``Dinov2Encoder``, ``Dinov3Encoder``).
 
     patches  = patchify(pixels) @ W_patch^T (+ bias)      (the stride-p conv as a GEMM)
     tokens   = [CLS] + patches (CLIP) | patches (SigLIP), + position embeddings
@@ -19,6 +20,7 @@ models are the CPU oracles.
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import torch
@@ -289,6 +291,131 @@ class Dinov2Encoder:
 
     def embed(self, pixels: torch.Tensor, normalize: bool = True) -> torch.Tensor:
         """[B, H] fp32 image embeddings (the normalised CLS token)."""
+        _, pooled = self(pixels)
+        e = pooled.float()
+        return F.normalize(e, dim=-1) if normalize else e
+
+
+# ---------------------------------------------------------------------------
+# DINOv3 (2-D axial RoPE on the patch tokens, register tokens, LayerScale)
+# ---------------------------------------------------------------------------
+
+@dataclass
+class Dinov3Config:
+    hidden_size: int = 384
+    intermediate_size: int = 1536
+    num_hidden_layers: int = 12
+    num_attention_heads: int = 6
+    patch_size: int = 16
+    image_size: int = 224
+    layer_norm_eps: float = 1e-5
+    rope_theta: float = 100.0
+    num_register_tokens: int = 0
+    use_gated_mlp: bool = False
+    hidden_act: str = "gelu"
+
+    @classmethod
+    def from_dict(cls, d: dict) -> "Dinov3Config":
+        return cls(**{k: d[k] for k in cls.__dataclass_fields__ if k in d})
+
+
+class Dinov3Encoder:
+    """DINOv3 ViT: [CLS] + register tokens + patch tokens (no absolute position
+    embedding); in every block, q and k of the patch tokens are rotated by a 2-D
+    axial RoPE whose angles are 2 pi * (patch-centre coordinate in [-1, 1]) *
+    theta^(-4j / head_dim), the y frequencies then the x frequencies, repeated
+    for the two halves of the head (half-split rotation); pre-norm blocks with
+    LayerScale on both branches (GELU MLP, or a gated one), final LayerNorm,
+    CLS pooling. Checkpoint names: ``embeddings.*``, ``model.layer.{i}.*``
+    (or ``layer.{i}.*``), ``norm.*``.
+
+    Reference: crates/rlx-dinov3; transformers' DINOv3ViTModel is the CPU oracle."""
+
+    def __init__(self, cfg: Dinov3Config, weights, device="cpu", dtype: torch.dtype | None = None):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else torch.float32)
+        get = (lambda n: weights.take(n)) if hasattr(weights, "take") else (lambda n: weights[n])
+        has = lambda n: n in weights  # noqa: E731
+        dv = lambda t: t.to(self.device, self.dtype).contiguous()  # noqa: E731
+        H = cfg.hidden_size
+        e = "embeddings."
+        self.w_patch = _pad_k(dv(get(e + "patch_embeddings.weight").reshape(H, -1)))
+        self.b_patch = dv(get(e + "patch_embeddings.bias"))
+        self.cls = dv(get(e + "cls_token").reshape(1, 1, H))
+        self.regs = dv(get(e + "register_tokens")) if has(e + "register_tokens") and cfg.num_register_tokens else None
+        lp = "model.layer." if has("model.layer.0.norm1.weight") else "layer."
+        ln = lambda p: (dv(get(p + ".weight")), dv(get(p + ".bias")))  # noqa: E731
+        opt = lambda n: dv(get(n)) if has(n) else None  # noqa: E731
+        self.layers = []
+        for i in range(cfg.num_hidden_layers):
+            p = lp + f"{i}."
+            a = p + "attention."
+            zero = torch.zeros(H)
+            qkv_b = torch.cat([get(a + f"{n}_proj.bias") if has(a + f"{n}_proj.bias") else zero for n in "qkv"])
+            mlp = {n: (dv(get(p + f"mlp.{n}_proj.weight")), opt(p + f"mlp.{n}_proj.bias"))
+                   for n in (("gate", "up", "down") if cfg.use_gated_mlp else ("up", "down"))}
+            self.layers.append(dict(
+                ln1=ln(p + "norm1"), ln2=ln(p + "norm2"),
+                qkv=dv(torch.cat([get(a + f"{n}_proj.weight") for n in "qkv"], 0)), qkv_b=dv(qkv_b),
+                o=(dv(get(a + "o_proj.weight")), opt(a + "o_proj.bias")),
+                ls1=dv(get(p + "layer_scale1.lambda1")), ls2=dv(get(p + "layer_scale2.lambda1")), mlp=mlp))
+        self.norm = ln("norm")
+        D = H // cfg.num_attention_heads
+        self.inv = 1.0 / cfg.rope_theta ** torch.arange(0, 1, 4 / D, dtype=torch.float32)  # [D / 4]
+
+    def _ln(self, x, p):
+        return F.layer_norm(x.float(), (x.shape[-1],), p[0].float(), p[1].float(),
+                            self.cfg.layer_norm_eps).to(x.dtype)
+
+    def _act(self, x):
+        a = self.cfg.hidden_act
+        return F.gelu(x) if a == "gelu" else (F.silu(x) if a in ("silu", "swish") else F.gelu(x, approximate="tanh"))
+
+    def _rope(self, gh: int, gw: int):
+        ch = (torch.arange(0.5, gh) / gh) * 2 - 1
+        cw = (torch.arange(0.5, gw) / gw) * 2 - 1
+        coords = torch.stack(torch.meshgrid(ch, cw, indexing="ij"), -1).reshape(-1, 2)  # [P, (y, x)]
+        ang = (2 * math.pi * coords[:, :, None] * self.inv[None, None, :]).reshape(coords.shape[0], -1).repeat(1, 2)
+        return ang.cos().to(self.device), ang.sin().to(self.device)
+
+    @torch.no_grad()
+    def __call__(self, pixels: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """pixels [B, 3, h, w] (preprocessed; multiples of the patch size) ->
+        (last hidden [B, 1 + registers + patches, H], pooled CLS [B, H])."""
+        c = self.cfg
+        pixels = pixels.to(self.device, torch.float32)
+        B, _, h, w = pixels.shape
+        H, nh = c.hidden_size, c.num_attention_heads
+        D = H // nh
+        gh, gw = h // c.patch_size, w // c.patch_size
+        x = _linear(_patch_rows(pixels, c.patch_size, self.w_patch.shape[1], self.dtype), self.w_patch, self.b_patch)
+        parts = [self.cls.expand(B, 1, H)] + ([self.regs.expand(B, -1, H)] if self.regs is not None else []) + [x]
+        x = torch.cat(parts, 1)
+        n_pre = x.shape[1] - gh * gw
+        cos, sin = self._rope(gh, gw)
+
+        def rot(t):  # [B, nh, L, D]: rotate the patch tokens only
+            pre, pt = t[:, :, :n_pre], t[:, :, n_pre:].float()
+            half = D // 2
+            r = torch.cat([-pt[..., half:], pt[..., :half]], -1)
+            return torch.cat([pre, (pt * cos + r * sin).to(t.dtype)], 2)
+        for ly in self.layers:
+            q, k, v = _linear(self._ln(x, ly["ln1"]), ly["qkv"], ly["qkv_b"]).split(H, -1)
+            q, k, v = (t.reshape(B, -1, nh, D).transpose(1, 2) for t in (q, k, v))
+            att = F.scaled_dot_product_attention(rot(q), rot(k), v).transpose(1, 2).reshape(B, -1, H)
+            x = x + _linear(att, *ly["o"]) * ly["ls1"]
+            y = self._ln(x, ly["ln2"])
+            m = ly["mlp"]
+            if "gate" in m:
+                hdn = (self._act(_linear(y, *m["gate"]).float()) * _linear(y, *m["up"]).float()).to(y.dtype)
+            else:
+                hdn = self._act(_linear(y, *m["up"]).float()).to(y.dtype)
+            x = x + _linear(hdn, *m["down"]) * ly["ls2"]
+        x = self._ln(x, self.norm)
+        return x, x[:, 0]
+
+    def embed(self, pixels: torch.Tensor, normalize: bool = True) -> torch.Tensor:
         _, pooled = self(pixels)
         e = pooled.float()
         return F.normalize(e, dim=-1) if normalize else e

@@ -86,3 +86,16 @@ def test_parakeet_ctc_gpu_matches_cpu(cuda):
     got, n = ParakeetCTC(cfg, sd, device=cuda).logits(feats, torch.tensor([200, 150]))
     assert _cos(got[0], ref[0]).min() > 0.995
     assert _cos(got[1, :int(n[1])], ref[1, :int(n[1])]).min() > 0.995
+
+
+def test_dinov3_gpu_matches_cpu(cuda):
+    import transformers as T
+    from rlx_models_b200.models.vit import Dinov3Config, Dinov3Encoder
+    hc = T.DINOv3ViTConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=2, num_attention_heads=4,
+                           image_size=64, patch_size=16, num_register_tokens=4, use_gated_mlp=True, hidden_act="silu")
+    sd = {k: v.detach() for k, v in _rand(T.DINOv3ViTModel(hc)).state_dict().items() if v.numel()}
+    cfg = Dinov3Config.from_dict(hc.to_dict())
+    px = torch.randn(2, 3, 96, 96, generator=torch.Generator().manual_seed(2))
+    ref = Dinov3Encoder(cfg, sd).embed(px)
+    got = Dinov3Encoder(cfg, sd, device=cuda).embed(px)
+    assert _cos(got, ref).min() > 0.999

@@ -4,6 +4,7 @@ package's own image preprocessing."""
 import math
 
 import numpy as np
+import pytest
 import torch
 
 
@@ -11,6 +12,8 @@ def _rand(m):
     torch.manual_seed(0)
     with torch.no_grad():
         for n, p in m.named_parameters():
+            if p.numel() == 0:
+                continue
             if p.dim() >= 2:
                 p.normal_(0, 1 / math.sqrt(p[0].numel()))
             else:
@@ -160,3 +163,21 @@ def test_load_image_embedder_dinov2(tmp_path):
     with torch.no_grad():
         r = torch.nn.functional.normalize(m(pixel_values=px).pooler_output, dim=-1)
     assert (e - r).abs().max() < 2e-2
+
+
+@pytest.mark.parametrize("gated,regs,size", [(False, 0, 28), (True, 2, 42)])
+def test_dinov3_matches_transformers(gated, regs, size):
+    import transformers as T
+    from rlx_models_b200.models.vit import Dinov3Config, Dinov3Encoder
+    hc = T.DINOv3ViTConfig(hidden_size=64, intermediate_size=96, num_hidden_layers=2, num_attention_heads=4,
+                           image_size=28, patch_size=7, num_register_tokens=regs, use_gated_mlp=gated,
+                           hidden_act="silu" if gated else "gelu", layerscale_value=0.5)
+    m = _rand(T.DINOv3ViTModel(hc))
+    px = torch.randn(2, 3, size, size, generator=torch.Generator().manual_seed(3))
+    with torch.no_grad():
+        ref = m(pixel_values=px)
+    enc = Dinov3Encoder(Dinov3Config.from_dict(hc.to_dict()), {k: v.detach() for k, v in m.state_dict().items()})
+    last, pooled = enc(px)
+    assert last.shape == ref.last_hidden_state.shape
+    assert (last - ref.last_hidden_state).abs().max() < 2e-4
+    assert (pooled - ref.pooler_output).abs().max() < 2e-4
