@@ -233,8 +233,8 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
 
 def load_transcriber(model: str, *, device: str | torch.device = "cuda", language: str | None = "en",
                      task: str = "transcribe"):
-    """Whisper or Parakeet-CTC checkpoint (local dir / offline HF id) -> object
-    with ``transcribe(audio, sample_rate)``."""
+    """Whisper, Moonshine or Parakeet-CTC checkpoint (local dir / offline HF id)
+    -> object with ``transcribe(audio, sample_rate)``."""
     import json
     from .models.whisper import SpeechToText, WhisperConfig, WhisperModel
     path = resolve_model_path(model)
@@ -246,6 +246,10 @@ def load_transcriber(model: str, *, device: str | torch.device = "cuda", languag
     if any(os.path.exists(os.path.join(path, f)) for f in ("tokenizer.json", "tokenizer_config.json", "vocab.json")):
         from transformers import AutoTokenizer
         tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+    if raw.get("model_type") == "moonshine":
+        from .models.moonshine import MoonshineConfig, MoonshineModel, MoonshineTranscriber
+        return MoonshineTranscriber(MoonshineModel(MoonshineConfig.from_dict(raw), WeightMap.from_dir(path),
+                                                   device=device), tok)
     if raw.get("model_type") == "parakeet_ctc":
         from .models.parakeet import ParakeetConfig, ParakeetCTC, ParakeetTranscriber
         return ParakeetTranscriber(ParakeetCTC(ParakeetConfig.from_dict(raw), WeightMap.from_dir(path), device=device),

@@ -1,5 +1,5 @@
 """Encoder families on the GPU (bf16 GEMMs) against their CPU fp32 paths:
-NomicBERT text embeddings, CLIP and DINOv2 image embeddings, Parakeet CTC logits."""
+NomicBERT text embeddings, CLIP and DINOv2 image embeddings, Parakeet CTC logits, Moonshine decoder logits."""
 import math
 
 import numpy as np
@@ -99,3 +99,19 @@ def test_dinov3_gpu_matches_cpu(cuda):
     ref = Dinov3Encoder(cfg, sd).embed(px)
     got = Dinov3Encoder(cfg, sd, device=cuda).embed(px)
     assert _cos(got, ref).min() > 0.999
+
+
+def test_moonshine_gpu_matches_cpu(cuda):
+    import transformers as T
+    from rlx_models_b200.models.moonshine import MoonshineConfig, MoonshineModel
+    hc = T.MoonshineConfig(vocab_size=256, hidden_size=256, intermediate_size=512, encoder_num_hidden_layers=2,
+                           decoder_num_hidden_layers=2, encoder_num_attention_heads=4, decoder_num_attention_heads=4,
+                           encoder_num_key_value_heads=4, decoder_num_key_value_heads=4)
+    sd = {k: v.detach() for k, v in _rand(T.MoonshineForConditionalGeneration(hc)).state_dict().items()}
+    cfg = MoonshineConfig.from_dict(hc.to_dict())
+    audio = torch.randn(1, 32000, generator=torch.Generator().manual_seed(4)) * 0.3
+    ids = torch.tensor([[1, 7, 19, 200, 42]])
+    ref_m, got_m = MoonshineModel(cfg, sd), MoonshineModel(cfg, sd, device=cuda)
+    ref = ref_m.decode_step(ids, 0, [None] * 2, ref_m._cross_kv(ref_m.encode(audio)))
+    got = got_m.decode_step(ids, 0, [None] * 2, got_m._cross_kv(got_m.encode(audio)))
+    assert _cos(got[0], ref[0]).min() > 0.995
