@@ -258,6 +258,22 @@ def load_transcriber(model: str, *, device: str | torch.device = "cuda", languag
     return SpeechToText(WhisperModel(cfg, WeightMap.from_dir(path), device=device), tok, language, task)
 
 
+def load_codec(model: str, *, device: str | torch.device = "cuda"):
+    """Neural audio codec checkpoint (local dir / offline HF id; DAC in
+    transformers' or the original Descript layout) -> object with
+    ``encode(pcm) -> codes``, ``decode(codes) -> pcm`` and ``roundtrip``."""
+    import json
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local codec checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        raw = json.load(f)
+    if raw.get("model_type", "dac") == "dac":
+        from .models.dac import DacConfig, DacModel
+        return DacModel(DacConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
+    raise NotImplementedError(f"codec model_type {raw.get('model_type')!r}")
+
+
 class Embedder:
     """Sentence embeddings from an encoder checkpoint (BERT family)."""
 

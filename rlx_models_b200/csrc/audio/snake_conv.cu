@@ -1,0 +1,148 @@
+// Channels-last 1-D convolutions of the DAC-style codecs as GEMMs on the
+// tcgen05 linear, with the elementwise work fused into the operand producers.
+//
+// snake_im2col: x [B, T, C] bf16 -> cols [B * T_out, Kp] bf16,
+//     cols[(b, t), j * C + c] = snake(x[b, t * stride - pad + j * dil, c])   (0 outside [0, T))
+//     snake(v) = v + sin(alpha[c] * v)^2 / (alpha[c] + 1e-9)                 (identity when alpha is null)
+//   and zeros in columns [k * C, Kp) (Kp = k * C rounded up to 8, the GEMM's
+//   16-byte row rule). A convolution is then cols @ W'^T with
+//   W'[o, j * C + c] = W[o, c, j]; the snake that precedes every DAC conv costs
+//   no extra pass over the activations.
+//
+// convt_fold: the transposed convolution (kernel k = m * stride) as a GEMM
+//   Y = x @ W'' ([B * T_in, k * C_out] fp32, W''[j * C_out + o, c] = W[c, o, j])
+//   followed by this overlap-add, fused with the bias and the output crop:
+//     y[b, u, o] = bias[o] + sum_{q < m} Y[b, t - q, (q * stride + r) * C_out + o]
+//     with v = u + pad, t = v / stride, r = v % stride, over 0 <= t - q < T_in.
+//
+// Reference: the reference's DAC layers (crates/rlx-dac/src/ops.rs:3-40 snake,
+// ops.rs:159-220 transposed convolution as one sgemm plus a scatter,
+// crates/rlx-dac/src/layers.rs:7-60 weight-normalised convolutions).
+#include <cuda_bf16.h>
+
+#include <cstdint>
+#include <stdexcept>
+
+#include "../common/b200.cuh"
+#include "../common/launch.h"
+#include "../common/pdl_launch.h"
+
+namespace b200 {
+namespace snake {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ float snake_f(float v, float a) {
+  const float s = sinf(a * v);
+  return v + s * s / (a + 1e-9f);
+}
+
+// C % 8 == 0: one thread per 8 channels of one (row, tap), 16-byte loads and stores.
+__global__ void __launch_bounds__(kThreads) im2col_vec_kernel(const __nv_bfloat16* __restrict__ x,
+                                                              const float* __restrict__ alpha,
+                                                              __nv_bfloat16* __restrict__ cols, int64_t rows,
+                                                              int T, int T_out, int C, int k, int stride, int pad,
+                                                              int dil) {
+  pdl_wait();
+  pdl_trigger();
+  const int cv = C / 8;
+  const int64_t n = rows * k * cv;
+  for (int64_t i = blockIdx.x * (int64_t)kThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kThreads) {
+    const int c8 = (int)(i % cv);
+    const int64_t rj = i / cv;
+    const int j = (int)(rj % k);
+    const int64_t row = rj / k;
+    const int b = (int)(row / T_out), t = (int)(row % T_out);
+    const int ts = t * stride - pad + j * dil;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (ts >= 0 && ts < T) {
+      v = *reinterpret_cast<const uint4*>(x + ((int64_t)b * T + ts) * C + c8 * 8);
+      if (alpha != nullptr) {
+        __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) e[q] = __float2bfloat16(snake_f(__bfloat162float(e[q]), alpha[c8 * 8 + q]));
+      }
+    }
+    *reinterpret_cast<uint4*>(cols + row * (int64_t)k * C + (int64_t)j * C + c8 * 8) = v;
+  }
+}
+
+// Any C (the stem's single input channel): one thread per output element,
+// including the zero padding columns.
+__global__ void __launch_bounds__(kThreads) im2col_scalar_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                 const float* __restrict__ alpha,
+                                                                 __nv_bfloat16* __restrict__ cols, int64_t rows,
+                                                                 int Kp, int T, int T_out, int C, int k, int stride,
+                                                                 int pad, int dil) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t n = rows * Kp;
+  for (int64_t i = blockIdx.x * (int64_t)kThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kThreads) {
+    const int col = (int)(i % Kp);
+    const int64_t row = i / Kp;
+    float v = 0.f;
+    if (col < k * C) {
+      const int j = col / C, c = col % C;
+      const int b = (int)(row / T_out), t = (int)(row % T_out);
+      const int ts = t * stride - pad + j * dil;
+      if (ts >= 0 && ts < T) {
+        v = __bfloat162float(x[((int64_t)b * T + ts) * C + c]);
+        if (alpha != nullptr) v = snake_f(v, alpha[c]);
+      }
+    }
+    cols[i] = __float2bfloat16(v);
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) convt_fold_kernel(const float* __restrict__ Y, const float* __restrict__ bias,
+                                                              __nv_bfloat16* __restrict__ y, int64_t n, int T_in,
+                                                              int T_out, int C_out, int stride, int m, int pad) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t ycols = (int64_t)m * stride * C_out;
+  for (int64_t i = blockIdx.x * (int64_t)kThreads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kThreads) {
+    const int o = (int)(i % C_out);
+    const int64_t bu = i / C_out;
+    const int u = (int)(bu % T_out), b = (int)(bu / T_out);
+    const int v = u + pad, t = v / stride, r = v % stride;
+    float acc = bias != nullptr ? bias[o] : 0.f;
+    for (int q = 0; q < m; ++q) {
+      const int ti = t - q;
+      if (ti >= 0 && ti < T_in) acc += Y[((int64_t)b * T_in + ti) * ycols + (int64_t)(q * stride + r) * C_out + o];
+    }
+    y[i] = __float2bfloat16(acc);
+  }
+}
+
+inline unsigned grid_for(int64_t n) {
+  const int64_t want = (n + kThreads - 1) / kThreads;
+  return (unsigned)(want < 148 * 16 ? (want > 0 ? want : 1) : 148 * 16);
+}
+
+}  // namespace snake
+
+void snake_im2col_launch(const void* x, const float* alpha, void* cols, int B, int T, int T_out, int C, int Kp, int k,
+                         int stride, int pad, int dil, cudaStream_t st) {
+  const int64_t rows = (int64_t)B * T_out;
+  if (rows == 0) return;
+  auto* xp = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto* cp = reinterpret_cast<__nv_bfloat16*>(cols);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(cols)) & 15u) == 0;
+  if (C % 8 == 0 && Kp == k * C && aligned) {
+    launch_pdl(snake::im2col_vec_kernel, dim3(snake::grid_for(rows * k * (C / 8))), dim3(snake::kThreads), 0, st, xp,
+               alpha, cp, rows, T, T_out, C, k, stride, pad, dil);
+  } else {
+    launch_pdl(snake::im2col_scalar_kernel, dim3(snake::grid_for(rows * Kp)), dim3(snake::kThreads), 0, st, xp, alpha,
+               cp, rows, Kp, T, T_out, C, k, stride, pad, dil);
+  }
+}
+
+void convt_fold_launch(const float* Y, const float* bias, void* y, int B, int T_in, int T_out, int C_out, int stride,
+                       int m, int pad, cudaStream_t st) {
+  const int64_t n = (int64_t)B * T_out * C_out;
+  if (n == 0) return;
+  launch_pdl(snake::convt_fold_kernel, dim3(snake::grid_for(n)), dim3(snake::kThreads), 0, st, Y, bias,
+             reinterpret_cast<__nv_bfloat16*>(y), n, T_in, T_out, C_out, stride, m, pad);
+}
+
+}  // namespace b200

@@ -1257,6 +1257,49 @@ void instance_norm(const Tensor& x, const optional<Tensor>& gamma, const optiona
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+void snake_im2col(const Tensor& x, const optional<Tensor>& alpha, Tensor& cols, int64_t k, int64_t stride, int64_t pad,
+                  int64_t dil) {
+  check_cuda(x, "x");
+  TORCH_CHECK(x.dim() == 3 && x.is_contiguous() && x.scalar_type() == at::kBFloat16,
+              "b200.snake_im2col: contiguous bf16 x [B, T, C]");
+  const int64_t B = x.size(0), T = x.size(1), C = x.size(2);
+  TORCH_CHECK(k >= 1 && stride >= 1 && dil >= 1 && pad >= 0, "b200.snake_im2col: bad geometry");
+  const int64_t T_out = (T + 2 * pad - dil * (k - 1) - 1) / stride + 1;
+  const int64_t Kp = (k * C + 7) / 8 * 8;
+  TORCH_CHECK(T_out >= 1 && cols.is_contiguous() && cols.scalar_type() == at::kBFloat16 && cols.dim() == 2 &&
+                  cols.size(0) == B * T_out && cols.size(1) == Kp,
+              "b200.snake_im2col: cols must be contiguous bf16 [B * T_out, round_up(k * C, 8)]");
+  TORCH_CHECK(B * T <= INT32_MAX && B * T_out <= INT32_MAX && Kp <= INT32_MAX, "b200.snake_im2col: too large");
+  if (alpha.has_value() && alpha->defined())
+    TORCH_CHECK(alpha->scalar_type() == at::kFloat && alpha->is_contiguous() && alpha->numel() == C,
+                "b200.snake_im2col: alpha fp32 [C]");
+  c10::cuda::CUDAGuard g(x.device());
+  b200::snake_im2col_launch(x.data_ptr(), static_cast<const float*>(opt_ptr(alpha)), cols.data_ptr(), (int)B, (int)T,
+                            (int)T_out, (int)C, (int)Kp, (int)k, (int)stride, (int)pad, (int)dil, cur_stream(x));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void convt_fold(const Tensor& Y, const optional<Tensor>& bias, Tensor& y, int64_t stride, int64_t pad) {
+  check_cuda(Y, "Y");
+  TORCH_CHECK(Y.dim() == 3 && Y.is_contiguous() && Y.scalar_type() == at::kFloat,
+              "b200.convt_fold: contiguous fp32 Y [B, T_in, k * C_out]");
+  TORCH_CHECK(y.dim() == 3 && y.is_contiguous() && y.scalar_type() == at::kBFloat16 && y.size(0) == Y.size(0),
+              "b200.convt_fold: contiguous bf16 y [B, T_out, C_out]");
+  const int64_t C_out = y.size(2);
+  TORCH_CHECK(stride >= 1 && pad >= 0 && C_out > 0 && Y.size(2) % (stride * C_out) == 0,
+              "b200.convt_fold: kernel size must be a multiple of the stride");
+  const int64_t m = Y.size(2) / (stride * C_out);
+  TORCH_CHECK(y.size(1) == (Y.size(1) - 1) * stride + m * stride - 2 * pad, "b200.convt_fold: T_out mismatch");
+  if (bias.has_value() && bias->defined())
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->is_contiguous() && bias->numel() == C_out,
+                "b200.convt_fold: bias fp32 [C_out]");
+  c10::cuda::CUDAGuard g(Y.device());
+  b200::convt_fold_launch(Y.data_ptr<float>(), static_cast<const float*>(opt_ptr(bias)), y.data_ptr(),
+                          (int)Y.size(0), (int)Y.size(1), (int)y.size(1), (int)C_out, (int)stride, (int)m, (int)pad,
+                          cur_stream(Y));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void scale_by(Tensor& t, const Tensor& g) {
   check_cuda(t, "t");
   TORCH_CHECK(t.is_contiguous() && (t.scalar_type() == at::kFloat || t.scalar_type() == at::kBFloat16) &&
@@ -1521,6 +1564,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_train_bwd", &swiglu_train_bwd);
   m.def("scale_by", &scale_by);
   m.def("instance_norm", &instance_norm);
+  m.def("snake_im2col", &snake_im2col);
+  m.def("convt_fold", &convt_fold);
   m.def("attn_train_fwd", &attn_train_fwd);
   m.def("attn_train_bwd", &attn_train_bwd);
   m.def("sample", &sample);

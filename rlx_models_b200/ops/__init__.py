@@ -317,6 +317,32 @@ def instance_norm(x: torch.Tensor, gamma: torch.Tensor | None = None, beta: torc
     return y
 
 
+def snake_im2col(x: torch.Tensor, alpha: torch.Tensor | None, k: int, *, stride: int = 1, pad: int = 0,
+                 dil: int = 1) -> torch.Tensor:
+    """Channels-last im2col with the Snake activation fused in: x [B, T, C] bf16
+    -> [B * T_out, round_up(k * C, 8)] bf16, column ``j * C + c`` of row
+    ``(b, t)`` = snake(x[b, t * stride - pad + j * dil, c]) (zero outside the
+    signal and in the padding columns); ``alpha`` fp32 [C] or None (no snake)."""
+    B, T, C = x.shape
+    T_out = (T + 2 * pad - dil * (k - 1) - 1) // stride + 1
+    cols = torch.empty(B * T_out, (k * C + 7) // 8 * 8, dtype=torch.bfloat16, device=x.device)
+    _count(1)
+    ext().snake_im2col(x.contiguous(), alpha, cols, int(k), int(stride), int(pad), int(dil))
+    return cols
+
+
+def convt_fold(Y: torch.Tensor, bias: torch.Tensor | None, c_out: int, *, stride: int, pad: int) -> torch.Tensor:
+    """Overlap-add of a transposed convolution computed as a GEMM: Y [B, T_in,
+    k * C_out] fp32 (column ``j * C_out + o`` = tap j of output channel o) ->
+    y [B, (T_in - 1) * stride + k - 2 * pad, C_out] bf16, plus ``bias`` fp32 [C_out]."""
+    B, T_in, kc = Y.shape
+    k = kc // c_out
+    y = torch.empty(B, (T_in - 1) * stride + k - 2 * pad, c_out, dtype=torch.bfloat16, device=Y.device)
+    _count(1)
+    ext().convt_fold(Y.contiguous(), bias, y, int(stride), int(pad))
+    return y
+
+
 def sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, *, out=None, logprob=None):
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)

@@ -92,6 +92,41 @@ def gather_paged(cache: torch.Tensor, block_table: torch.Tensor, length: int) ->
     return pages.permute(0, 2, 1, 3).reshape(nblk * 16, cache.shape[1], cache.shape[3])[:length]
 
 
+def snake(x: torch.Tensor, alpha: torch.Tensor) -> torch.Tensor:
+    """fp32 Snake activation over the last (channel) axis: x + sin(a x)^2 / (a + 1e-9)."""
+    xf, a = x.float(), alpha.float()
+    return xf + torch.sin(a * xf).pow(2) / (a + 1e-9)
+
+
+def snake_im2col(x: torch.Tensor, alpha, k: int, stride: int = 1, pad: int = 0, dil: int = 1) -> torch.Tensor:
+    """fp32 channels-last im2col of x [B, T, C] (Snake first when ``alpha`` is
+    given): [B * T_out, round_up(k * C, 8)], column j * C + c of row (b, t) =
+    x[b, t * stride - pad + j * dil, c], zero outside the signal and in the
+    padding columns."""
+    B, T, C = x.shape
+    xs = snake(x, alpha) if alpha is not None else x.float()
+    xp = torch.nn.functional.pad(xs, (0, 0, pad, pad + dil * (k - 1) + stride))
+    T_out = (T + 2 * pad - dil * (k - 1) - 1) // stride + 1
+    t = torch.arange(T_out, device=x.device)[:, None] * stride + torch.arange(k, device=x.device)[None, :] * dil
+    cols = xp[:, t].reshape(B * T_out, k * C)        # [B, T_out, k, C] -> rows
+    kp = (k * C + 7) // 8 * 8
+    return cols if kp == k * C else torch.nn.functional.pad(cols, (0, kp - k * C))
+
+
+def convt_fold(Y: torch.Tensor, bias, c_out: int, stride: int, pad: int) -> torch.Tensor:
+    """fp32 overlap-add of a transposed convolution computed as a GEMM: Y [B,
+    T_in, k * C_out] (column j * C_out + o = tap j of output o) -> [B, (T_in - 1)
+    * stride + k - 2 * pad, C_out] (+ bias)."""
+    B, T_in, kc = Y.shape
+    k = kc // c_out
+    full = torch.zeros(B, (T_in - 1) * stride + k, c_out, dtype=torch.float32, device=Y.device)
+    Yr = Y.float().reshape(B, T_in, k, c_out)
+    for j in range(k):
+        full[:, j:j + (T_in - 1) * stride + 1:stride] += Yr[:, :, j]
+    out = full[:, pad:full.shape[1] - pad]
+    return out + bias.float() if bias is not None else out
+
+
 def instance_norm(x: torch.Tensor, gamma=None, beta=None, active: int = 0, eps: float = 1e-5) -> torch.Tensor:
     """fp32 instance norm over the last axis with statistics of the first ``active`` steps."""
     xf = x.float()
