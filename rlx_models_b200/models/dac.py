@@ -308,9 +308,9 @@ def random_weights(cfg: DacConfig, seed: int = 0, weight_norm: bool = False) -> 
     g = torch.Generator().manual_seed(seed)
     w = {}
 
-    def conv(name, o, c, k, transposed=False):
+    def conv(name, o, c, k, transposed=False, gain=1.0):
         shape = (c, o, k) if transposed else (o, c, k)
-        t = torch.randn(*shape, generator=g) / math.sqrt(c * k)
+        t = gain * torch.randn(*shape, generator=g) / math.sqrt(c * k)
         if weight_norm:
             w[name + ".weight_v"] = t
             w[name + ".weight_g"] = t.reshape(t.shape[0], -1).norm(dim=1).reshape(-1, 1, 1) * (
@@ -326,7 +326,7 @@ def random_weights(cfg: DacConfig, seed: int = 0, weight_norm: bool = False) -> 
         snake(p + "snake1", c)
         conv(p + "conv1", c, c, 7)
         snake(p + "snake2", c)
-        conv(p + "conv2", c, c, 1)
+        conv(p + "conv2", c, c, 1, gain=0.3)       # small residual branches, as in trained codecs
 
     d = cfg.encoder_hidden_size
     conv("encoder.conv1", d, 1, 7)
