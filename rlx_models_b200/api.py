@@ -259,9 +259,10 @@ def load_transcriber(model: str, *, device: str | torch.device = "cuda", languag
 
 
 def load_codec(model: str, *, device: str | torch.device = "cuda"):
-    """Neural audio codec checkpoint (local dir / offline HF id; DAC in
-    transformers' or the original Descript layout) -> object with
-    ``encode(pcm) -> codes``, ``decode(codes) -> pcm`` and ``roundtrip``."""
+    """Neural audio codec checkpoint (local dir / offline HF id): DAC (transformers'
+    or the original Descript layout; ``encode(pcm) -> codes``, ``decode(codes)
+    -> pcm``, ``roundtrip``) or EnCodec (``encode(pcm, bandwidth) -> (codes,
+    scales, pad)``, ``decode(codes, scales, pad)``, the transformers layout)."""
     import json
     path = resolve_model_path(model)
     if path is None:
@@ -271,6 +272,9 @@ def load_codec(model: str, *, device: str | torch.device = "cuda"):
     if raw.get("model_type", "dac") == "dac":
         from .models.dac import DacConfig, DacModel
         return DacModel(DacConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
+    if raw.get("model_type") == "encodec":
+        from .models.encodec import EncodecConfig, EncodecModel
+        return EncodecModel(EncodecConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
     raise NotImplementedError(f"codec model_type {raw.get('model_type')!r}")
 
 

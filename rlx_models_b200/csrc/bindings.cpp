@@ -1257,46 +1257,69 @@ void instance_norm(const Tensor& x, const optional<Tensor>& gamma, const optiona
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void snake_im2col(const Tensor& x, const optional<Tensor>& alpha, Tensor& cols, int64_t k, int64_t stride, int64_t pad,
-                  int64_t dil) {
+void act_im2col(const Tensor& x, const optional<Tensor>& alpha, Tensor& cols, int64_t k, int64_t stride, int64_t pad_l,
+                int64_t pad_r, int64_t dil, int64_t act, bool reflect) {
   check_cuda(x, "x");
   TORCH_CHECK(x.dim() == 3 && x.is_contiguous() && x.scalar_type() == at::kBFloat16,
-              "b200.snake_im2col: contiguous bf16 x [B, T, C]");
+              "b200.act_im2col: contiguous bf16 x [B, T, C]");
   const int64_t B = x.size(0), T = x.size(1), C = x.size(2);
-  TORCH_CHECK(k >= 1 && stride >= 1 && dil >= 1 && pad >= 0, "b200.snake_im2col: bad geometry");
-  const int64_t T_out = (T + 2 * pad - dil * (k - 1) - 1) / stride + 1;
+  TORCH_CHECK(k >= 1 && stride >= 1 && dil >= 1 && pad_l >= 0 && pad_r >= 0 && act >= 0 && act <= 2,
+              "b200.act_im2col: bad geometry");
+  TORCH_CHECK(!reflect || (pad_l < T && pad_r < T), "b200.act_im2col: reflection needs padding < T");
+  const int64_t T_out = (T + pad_l + pad_r - dil * (k - 1) - 1) / stride + 1;
   const int64_t Kp = (k * C + 7) / 8 * 8;
   TORCH_CHECK(T_out >= 1 && cols.is_contiguous() && cols.scalar_type() == at::kBFloat16 && cols.dim() == 2 &&
                   cols.size(0) == B * T_out && cols.size(1) == Kp,
-              "b200.snake_im2col: cols must be contiguous bf16 [B * T_out, round_up(k * C, 8)]");
-  TORCH_CHECK(B * T <= INT32_MAX && B * T_out <= INT32_MAX && Kp <= INT32_MAX, "b200.snake_im2col: too large");
+              "b200.act_im2col: cols must be contiguous bf16 [B * T_out, round_up(k * C, 8)]");
+  TORCH_CHECK(B * T <= INT32_MAX && B * T_out <= INT32_MAX && Kp <= INT32_MAX, "b200.act_im2col: too large");
+  TORCH_CHECK(act != 1 || (alpha.has_value() && alpha->defined()), "b200.act_im2col: snake needs alpha");
   if (alpha.has_value() && alpha->defined())
-    TORCH_CHECK(alpha->scalar_type() == at::kFloat && alpha->is_contiguous() && alpha->numel() == C,
-                "b200.snake_im2col: alpha fp32 [C]");
+    TORCH_CHECK(alpha->scalar_type() == at::kFloat && alpha->is_contiguous() && alpha->numel() == C &&
+                    alpha->device() == x.device(),
+                "b200.act_im2col: alpha fp32 [C] on the device of x");
   c10::cuda::CUDAGuard g(x.device());
-  b200::snake_im2col_launch(x.data_ptr(), static_cast<const float*>(opt_ptr(alpha)), cols.data_ptr(), (int)B, (int)T,
-                            (int)T_out, (int)C, (int)Kp, (int)k, (int)stride, (int)pad, (int)dil, cur_stream(x));
+  b200::act_im2col_launch(x.data_ptr(), static_cast<const float*>(opt_ptr(alpha)), cols.data_ptr(), (int)B, (int)T,
+                          (int)T_out, (int)C, (int)Kp, (int)k, (int)stride, (int)pad_l, (int)dil, (int)act, reflect,
+                          cur_stream(x));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void convt_fold(const Tensor& Y, const optional<Tensor>& bias, Tensor& y, int64_t stride, int64_t pad) {
+void convt_fold(const Tensor& Y, const optional<Tensor>& bias, Tensor& y, int64_t stride, int64_t pad_l, int64_t pad_r) {
   check_cuda(Y, "Y");
   TORCH_CHECK(Y.dim() == 3 && Y.is_contiguous() && Y.scalar_type() == at::kFloat,
               "b200.convt_fold: contiguous fp32 Y [B, T_in, k * C_out]");
   TORCH_CHECK(y.dim() == 3 && y.is_contiguous() && y.scalar_type() == at::kBFloat16 && y.size(0) == Y.size(0),
               "b200.convt_fold: contiguous bf16 y [B, T_out, C_out]");
   const int64_t C_out = y.size(2);
-  TORCH_CHECK(stride >= 1 && pad >= 0 && C_out > 0 && Y.size(2) % (stride * C_out) == 0,
+  TORCH_CHECK(stride >= 1 && pad_l >= 0 && pad_r >= 0 && C_out > 0 && Y.size(2) % (stride * C_out) == 0,
               "b200.convt_fold: kernel size must be a multiple of the stride");
   const int64_t m = Y.size(2) / (stride * C_out);
-  TORCH_CHECK(y.size(1) == (Y.size(1) - 1) * stride + m * stride - 2 * pad, "b200.convt_fold: T_out mismatch");
+  TORCH_CHECK(y.size(1) == (Y.size(1) - 1) * stride + m * stride - pad_l - pad_r, "b200.convt_fold: T_out mismatch");
   if (bias.has_value() && bias->defined())
-    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->is_contiguous() && bias->numel() == C_out,
-                "b200.convt_fold: bias fp32 [C_out]");
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->is_contiguous() && bias->numel() == C_out &&
+                    bias->device() == Y.device(),
+                "b200.convt_fold: bias fp32 [C_out] on the device of Y");
   c10::cuda::CUDAGuard g(Y.device());
   b200::convt_fold_launch(Y.data_ptr<float>(), static_cast<const float*>(opt_ptr(bias)), y.data_ptr(),
-                          (int)Y.size(0), (int)Y.size(1), (int)y.size(1), (int)C_out, (int)stride, (int)m, (int)pad,
+                          (int)Y.size(0), (int)Y.size(1), (int)y.size(1), (int)C_out, (int)stride, (int)m, (int)pad_l,
                           cur_stream(Y));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void lstm_cell(const Tensor& G, Tensor& c, Tensor& h, Tensor& y) {
+  check_cuda(G, "G");
+  TORCH_CHECK(G.dim() == 2 && G.is_contiguous() && G.scalar_type() == at::kFloat && G.size(1) % 4 == 0,
+              "b200.lstm_cell: contiguous fp32 G [B, 4H]");
+  const int64_t B = G.size(0), H = G.size(1) / 4;
+  TORCH_CHECK(c.is_contiguous() && c.scalar_type() == at::kFloat && c.numel() == B * H && c.device() == G.device(),
+              "b200.lstm_cell: fp32 c [B, H]");
+  for (const Tensor* t : {&h, &y})
+    TORCH_CHECK(t->is_contiguous() && t->scalar_type() == at::kBFloat16 && t->numel() == B * H &&
+                    t->device() == G.device(),
+                "b200.lstm_cell: bf16 h / y [B, H]");
+  c10::cuda::CUDAGuard g(G.device());
+  b200::lstm_cell_launch(G.data_ptr<float>(), c.data_ptr<float>(), h.data_ptr(), y.data_ptr(), (int)B, (int)H,
+                         cur_stream(G));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1564,7 +1587,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_train_bwd", &swiglu_train_bwd);
   m.def("scale_by", &scale_by);
   m.def("instance_norm", &instance_norm);
-  m.def("snake_im2col", &snake_im2col);
+  m.def("act_im2col", &act_im2col);
+  m.def("lstm_cell", &lstm_cell);
   m.def("convt_fold", &convt_fold);
   m.def("attn_train_fwd", &attn_train_fwd);
   m.def("attn_train_bwd", &attn_train_bwd);

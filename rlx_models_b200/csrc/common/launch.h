@@ -195,12 +195,13 @@ void scale_by_launch(void* t, bool is_f32, int64_t n, const float* g, int device
 void instance_norm_launch(const void* x, const float* gamma, const float* beta, void* y, int64_t N, int C,
                           int64_t T, int64_t active, float eps, bool bf16, cudaStream_t st);
 
-// Channels-last convolutions of the audio codecs (snake-fused im2col, transposed-conv overlap-add): see
-// audio/snake_conv.cu.
-void snake_im2col_launch(const void* x, const float* alpha, void* cols, int B, int T, int T_out, int C, int Kp, int k,
-                         int stride, int pad, int dil, cudaStream_t st);
+// Channels-last convolutions of the audio codecs (activation-fused im2col, transposed-conv overlap-add) and the
+// LSTM cell: see audio/codec_conv.cu. act: 0 none, 1 snake (alpha [C]), 2 ELU.
+void act_im2col_launch(const void* x, const float* alpha, void* cols, int B, int T, int T_out, int C, int Kp, int k,
+                       int stride, int pad_l, int dil, int act, bool reflect, cudaStream_t st);
 void convt_fold_launch(const float* Y, const float* bias, void* y, int B, int T_in, int T_out, int C_out, int stride,
-                       int m, int pad, cudaStream_t st);
+                       int m, int pad_l, cudaStream_t st);
+void lstm_cell_launch(const float* G, float* c, void* h, void* y, int B, int H, cudaStream_t st);
 
 // Vocab-parallel greedy argmax over NVLink peer memory: see comm/tp_sample.cu.
 struct TpArgmaxArgs {

@@ -11,7 +11,7 @@ residual vector quantiser, 16 / 24 / 44.1 kHz mono.
     snake(x) = x + sin(alpha x)^2 / (alpha + 1e-9), alpha per channel
 
 Every convolution runs channels-last ([B, T, C]) as a GEMM on the tcgen05
-linear: ``ops.snake_im2col`` builds the operand with the preceding Snake fused
+linear: ``ops.act_im2col`` builds the operand with the preceding Snake fused
 in, a 1x1 conv is a plain linear (the residual add rides in its epilogue), and
 the transposed convolutions are one GEMM into fp32 taps followed by
 ``ops.convt_fold`` (overlap-add, bias and crop in one pass). Weight
@@ -37,7 +37,7 @@ from dataclasses import dataclass, field
 import torch
 import torch.nn.functional as F
 
-from ..ops import reference as R
+from .codec_common import ConvRunner, GemmConv, fold_weight_norm
 
 
 @dataclass
@@ -109,68 +109,29 @@ def _descript_name(name: str, n_enc: int, n_dec: int) -> str:
 
 
 def fold_weights(weights, cfg: DacConfig) -> dict:
-    """Plain fp32 tensors under transformers' names, weight norm folded:
-    w = g * v / ||v|| (norm over every axis but the first)."""
+    """Plain fp32 tensors under transformers' names, weight norm folded."""
     get = (lambda k: weights.take(k)) if hasattr(weights, "take") else (lambda k: weights[k])
     keys = list(weights.keys())
     descript = any(k.startswith("decoder.model.") for k in keys)
-    raw = {}
-    for k in keys:
-        n = _descript_name(k, len(cfg.downsampling_ratios), len(cfg.upsampling_ratios)) if descript else k
-        n = n.replace("parametrizations.weight.original0", "weight_g").replace(
-            "parametrizations.weight.original1", "weight_v")
-        raw[n] = get(k).float()
-    out = {}
-    for n, t in raw.items():
-        if n.endswith(".weight_g"):
-            base = n[:-len(".weight_g")]
-            v = raw[base + ".weight_v"]
-            norm = v.reshape(v.shape[0], -1).norm(dim=1).reshape(-1, *([1] * (v.dim() - 1)))
-            out[base + ".weight"] = t * v / norm
-        elif not n.endswith(".weight_v"):
-            out[n] = t
-    return out
-
-
-class _Conv:
-    """One convolution prepared as a GEMM operand: ``w`` [N_pad, round_up(k * C, 8)]
-    (column j * C + c = tap j of input channel c; transposed convs: row j * O + o)."""
-
-    def __init__(self, W: torch.Tensor, b: torch.Tensor | None, transposed: bool, dt, dev):
-        if transposed:
-            C, O, k = W.shape
-            w = W.permute(2, 1, 0).reshape(k * O, C)
-        else:
-            O, C, k = W.shape
-            w = W.permute(0, 2, 1).reshape(O, k * C)
-            w = F.pad(w, (0, (-w.shape[1]) % 8))
-            w = F.pad(w, (0, 0, 0, (-O) % 8))           # output rows to a multiple of 8
-        self.k, self.C, self.O, self.transposed = k, C, O, transposed
-        self.w = w.to(dev, dt).contiguous()
-        bp = None if b is None else (b if transposed else F.pad(b, (0, (-O) % 8)))
-        self.b = None if bp is None else bp.to(dev, dt).contiguous()   # GEMM epilogue bias (bf16 on the GPU)
-        self.b32 = None if b is None else b.to(dev, torch.float32).contiguous()
+    ne, nd = len(cfg.downsampling_ratios), len(cfg.upsampling_ratios)
+    return fold_weight_norm({(_descript_name(k, ne, nd) if descript else k): get(k) for k in keys})
 
 
 class DacModel:
     def __init__(self, cfg: DacConfig, weights, device="cpu"):
         self.cfg = cfg
-        self.device = torch.device(device)
-        self.fast = self.device.type == "cuda"
-        self.dtype = torch.bfloat16 if self.fast else torch.float32
-        if self.fast:
-            from .. import ops
-            self.ops = ops
+        self.run = ConvRunner(device)
+        self.device, self.dtype = self.run.device, self.run.dtype
         w = fold_weights(weights, cfg)
         dt, dev = self.dtype, self.device
-        self.convs: dict[str, _Conv] = {}
+        self.convs: dict[str, GemmConv] = {}
         self.alpha: dict[str, torch.Tensor] = {}
         for n, t in w.items():
             if n.endswith(".alpha"):
                 self.alpha[n[:-len(".alpha")]] = t.reshape(-1).to(dev, torch.float32).contiguous()
             elif n.endswith(".weight") and (n.startswith("encoder.") or n.startswith("decoder.")):
                 base = n[:-len(".weight")]
-                self.convs[base] = _Conv(t, w.get(base + ".bias"), base.endswith("conv_t1"), dt, dev)
+                self.convs[base] = GemmConv(t, w.get(base + ".bias"), base.endswith("conv_t1"), dt, dev)
         f32 = lambda t: t.to(dev, torch.float32).contiguous()  # noqa: E731
         self.quant = []
         for i in range(cfg.n_codebooks):
@@ -185,35 +146,13 @@ class DacModel:
     def _conv(self, x: torch.Tensor, name: str, snake: str | None = None, stride: int = 1, pad: int = 0,
               dil: int = 1, residual: torch.Tensor | None = None) -> torch.Tensor:
         """x [B, T, C] -> [B, T_out, O] of conv ``name`` after the Snake ``snake``."""
-        L = self.convs[name]
-        a = self.alpha[snake] if snake is not None else None
-        B = x.shape[0]
-        if self.fast:
-            cols = self.ops.snake_im2col(x, a, L.k, stride=stride, pad=pad, dil=dil)
-            res = None if residual is None else residual.reshape(-1, L.O)
-            y = self.ops.linear(cols, L.w, bias=L.b, residual=res)
-        else:
-            cols = R.snake_im2col(x, a, L.k, stride, pad, dil)
-            y = cols @ L.w.t()
-            if L.b is not None:
-                y = y + L.b
-            if residual is not None:
-                y = y + residual.reshape(-1, L.O)
-        if y.shape[1] != L.O:
-            y = y[:, :L.O]
-        return y.reshape(B, -1, L.O)
+        return self.run.conv(x, self.convs[name], act="snake" if snake is not None else None,
+                             alpha=self.alpha[snake] if snake is not None else None, stride=stride, pad=pad,
+                             dil=dil, residual=residual)
 
     def _conv_t(self, x: torch.Tensor, name: str, snake: str, stride: int) -> torch.Tensor:
-        L = self.convs[name]
-        a = self.alpha[snake]
-        B, T, _ = x.shape
-        pad = math.ceil(stride / 2)
-        if self.fast:
-            cols = self.ops.snake_im2col(x, a, 1)
-            Y = self.ops.linear(cols, L.w, out_dtype=torch.float32)
-            return self.ops.convt_fold(Y.view(B, T, -1), L.b32, L.O, stride=stride, pad=pad)
-        Y = R.snake(x, a).reshape(B * T, -1) @ L.w.t()
-        return R.convt_fold(Y.view(B, T, -1), L.b32, L.O, stride, pad)
+        return self.run.conv_t(x, self.convs[name], stride=stride, pad=math.ceil(stride / 2), act="snake",
+                               alpha=self.alpha[snake])
 
     def _res(self, x: torch.Tensor, p: str, dil: int) -> torch.Tensor:
         h = self._conv(x, p + "conv1", p + "snake1", pad=3 * dil, dil=dil)

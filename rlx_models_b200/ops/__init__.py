@@ -317,30 +317,49 @@ def instance_norm(x: torch.Tensor, gamma: torch.Tensor | None = None, beta: torc
     return y
 
 
-def snake_im2col(x: torch.Tensor, alpha: torch.Tensor | None, k: int, *, stride: int = 1, pad: int = 0,
-                 dil: int = 1) -> torch.Tensor:
-    """Channels-last im2col with the Snake activation fused in: x [B, T, C] bf16
-    -> [B * T_out, round_up(k * C, 8)] bf16, column ``j * C + c`` of row
-    ``(b, t)`` = snake(x[b, t * stride - pad + j * dil, c]) (zero outside the
-    signal and in the padding columns); ``alpha`` fp32 [C] or None (no snake)."""
+_ACTS = {None: 0, "snake": 1, "elu": 2}
+
+
+def act_im2col(x: torch.Tensor, k: int, *, stride: int = 1, pad: int = 0, pad_right: int | None = None,
+               dil: int = 1, act: str | None = None, alpha: torch.Tensor | None = None,
+               reflect: bool = False) -> torch.Tensor:
+    """Channels-last im2col with the preceding activation fused in: x [B, T, C]
+    bf16 -> [B * T_out, round_up(k * C, 8)] bf16, column ``j * C + c`` of row
+    ``(b, t)`` = act(x[b, t * stride - pad + j * dil, c]); positions outside the
+    signal read zero, or the reflected sample when ``reflect``. ``act``: None,
+    "snake" (``alpha`` fp32 [C]) or "elu"; padding columns are zero."""
     B, T, C = x.shape
-    T_out = (T + 2 * pad - dil * (k - 1) - 1) // stride + 1
+    pr = pad if pad_right is None else pad_right
+    T_out = (T + pad + pr - dil * (k - 1) - 1) // stride + 1
     cols = torch.empty(B * T_out, (k * C + 7) // 8 * 8, dtype=torch.bfloat16, device=x.device)
     _count(1)
-    ext().snake_im2col(x.contiguous(), alpha, cols, int(k), int(stride), int(pad), int(dil))
+    ext().act_im2col(x.contiguous(), alpha, cols, int(k), int(stride), int(pad), int(pr), int(dil), _ACTS[act],
+                     bool(reflect))
     return cols
 
 
-def convt_fold(Y: torch.Tensor, bias: torch.Tensor | None, c_out: int, *, stride: int, pad: int) -> torch.Tensor:
+def convt_fold(Y: torch.Tensor, bias: torch.Tensor | None, c_out: int, *, stride: int, pad: int,
+               pad_right: int | None = None) -> torch.Tensor:
     """Overlap-add of a transposed convolution computed as a GEMM: Y [B, T_in,
     k * C_out] fp32 (column ``j * C_out + o`` = tap j of output channel o) ->
-    y [B, (T_in - 1) * stride + k - 2 * pad, C_out] bf16, plus ``bias`` fp32 [C_out]."""
+    y [B, (T_in - 1) * stride + k - pad - pad_right, C_out] bf16 (the full
+    output with ``pad`` samples cut on the left and ``pad_right`` on the right),
+    plus ``bias`` fp32 [C_out]."""
     B, T_in, kc = Y.shape
     k = kc // c_out
-    y = torch.empty(B, (T_in - 1) * stride + k - 2 * pad, c_out, dtype=torch.bfloat16, device=Y.device)
+    pr = pad if pad_right is None else pad_right
+    y = torch.empty(B, (T_in - 1) * stride + k - pad - pr, c_out, dtype=torch.bfloat16, device=Y.device)
     _count(1)
-    ext().convt_fold(Y.contiguous(), bias, y, int(stride), int(pad))
+    ext().convt_fold(Y.contiguous(), bias, y, int(stride), int(pad), int(pr))
     return y
+
+
+def lstm_cell(G: torch.Tensor, c: torch.Tensor, h: torch.Tensor, y: torch.Tensor) -> None:
+    """One LSTM step from accumulated gate pre-activations G [B, 4H] fp32
+    (order i, f, g, o): updates c [B, H] fp32 in place and writes
+    h = sig(o) tanh(c) in bf16 to ``h`` and ``y``."""
+    _count(1)
+    ext().lstm_cell(G, c, h, y)
 
 
 def sample(logits, temperature, top_k, top_p, min_p, seeds, offsets, *, out=None, logprob=None):

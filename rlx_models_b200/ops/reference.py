@@ -98,33 +98,49 @@ def snake(x: torch.Tensor, alpha: torch.Tensor) -> torch.Tensor:
     return xf + torch.sin(a * xf).pow(2) / (a + 1e-9)
 
 
-def snake_im2col(x: torch.Tensor, alpha, k: int, stride: int = 1, pad: int = 0, dil: int = 1) -> torch.Tensor:
-    """fp32 channels-last im2col of x [B, T, C] (Snake first when ``alpha`` is
-    given): [B * T_out, round_up(k * C, 8)], column j * C + c of row (b, t) =
-    x[b, t * stride - pad + j * dil, c], zero outside the signal and in the
+def act_im2col(x: torch.Tensor, k: int, stride: int = 1, pad: int = 0, pad_right: int | None = None, dil: int = 1,
+               act: str | None = None, alpha=None, reflect: bool = False) -> torch.Tensor:
+    """fp32 channels-last im2col of x [B, T, C] with the activation applied
+    first (None, "snake" with ``alpha``, "elu"): [B * T_out, round_up(k * C, 8)],
+    column j * C + c of row (b, t) = act(x)[b, t * stride - pad + j * dil, c];
+    outside the signal zero, or the reflected sample when ``reflect``; zero
     padding columns."""
     B, T, C = x.shape
-    xs = snake(x, alpha) if alpha is not None else x.float()
-    xp = torch.nn.functional.pad(xs, (0, 0, pad, pad + dil * (k - 1) + stride))
-    T_out = (T + 2 * pad - dil * (k - 1) - 1) // stride + 1
+    pr = pad if pad_right is None else pad_right
+    xs = snake(x, alpha) if act == "snake" else (torch.nn.functional.elu(x.float()) if act == "elu" else x.float())
+    if reflect:
+        xp = torch.nn.functional.pad(xs.transpose(1, 2), (pad, pr), mode="reflect").transpose(1, 2)
+    else:
+        xp = torch.nn.functional.pad(xs, (0, 0, pad, pr))
+    T_out = (T + pad + pr - dil * (k - 1) - 1) // stride + 1
     t = torch.arange(T_out, device=x.device)[:, None] * stride + torch.arange(k, device=x.device)[None, :] * dil
     cols = xp[:, t].reshape(B * T_out, k * C)        # [B, T_out, k, C] -> rows
     kp = (k * C + 7) // 8 * 8
     return cols if kp == k * C else torch.nn.functional.pad(cols, (0, kp - k * C))
 
 
-def convt_fold(Y: torch.Tensor, bias, c_out: int, stride: int, pad: int) -> torch.Tensor:
+def convt_fold(Y: torch.Tensor, bias, c_out: int, stride: int, pad: int, pad_right: int | None = None) -> torch.Tensor:
     """fp32 overlap-add of a transposed convolution computed as a GEMM: Y [B,
-    T_in, k * C_out] (column j * C_out + o = tap j of output o) -> [B, (T_in - 1)
-    * stride + k - 2 * pad, C_out] (+ bias)."""
+    T_in, k * C_out] (column j * C_out + o = tap j of output o) -> the full
+    output [B, (T_in - 1) * stride + k, C_out] (+ bias) with ``pad`` samples cut
+    on the left and ``pad_right`` (default ``pad``) on the right."""
     B, T_in, kc = Y.shape
     k = kc // c_out
+    pr = pad if pad_right is None else pad_right
     full = torch.zeros(B, (T_in - 1) * stride + k, c_out, dtype=torch.float32, device=Y.device)
     Yr = Y.float().reshape(B, T_in, k, c_out)
     for j in range(k):
         full[:, j:j + (T_in - 1) * stride + 1:stride] += Yr[:, :, j]
-    out = full[:, pad:full.shape[1] - pad]
+    out = full[:, pad:full.shape[1] - pr]
     return out + bias.float() if bias is not None else out
+
+
+def lstm_cell(G: torch.Tensor, c: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 LSTM step from gate pre-activations G [B, 4H] (order i, f, g, o)
+    -> (h, c)."""
+    i, f, g, o = G.float().chunk(4, -1)
+    c = torch.sigmoid(f) * c + torch.sigmoid(i) * torch.tanh(g)
+    return torch.sigmoid(o) * torch.tanh(c), c
 
 
 def instance_norm(x: torch.Tensor, gamma=None, beta=None, active: int = 0, eps: float = 1e-5) -> torch.Tensor:

@@ -28,28 +28,50 @@ def _hf(w, weight_norm=False):
     return hm
 
 
-@pytest.mark.parametrize("k,s,p,d", [(7, 1, 3, 1), (7, 1, 9, 3), (4, 2, 1, 1), (10, 5, 3, 1), (3, 1, 1, 1)])
-def test_snake_im2col_is_conv1d(k, s, p, d):
+@pytest.mark.parametrize("k,s,p,pr,d", [(7, 1, 3, 3, 1), (7, 1, 9, 9, 3), (4, 2, 1, 1, 1), (10, 5, 3, 3, 1),
+                                        (3, 1, 1, 1, 1), (7, 1, 6, 0, 1), (4, 2, 2, 3, 1)])
+@pytest.mark.parametrize("act", [None, "snake", "elu"])
+@pytest.mark.parametrize("reflect", [False, True])
+def test_act_im2col_is_conv1d(k, s, p, pr, d, act, reflect):
     torch.manual_seed(0)
     B, T, C, O = 2, 37, 5, 6
     x, a = torch.randn(B, T, C), torch.rand(C) + 0.5
     W, b = torch.randn(O, C, k), torch.randn(O)
-    ref = F.conv1d(R.snake(x, a).transpose(1, 2), W, b, stride=s, padding=p, dilation=d).transpose(1, 2)
-    cols = R.snake_im2col(x, a, k, s, p, d)
+    xa = R.snake(x, a) if act == "snake" else (F.elu(x) if act == "elu" else x)
+    xp = F.pad(xa.transpose(1, 2), (p, pr), mode="reflect" if reflect else "constant")
+    ref = F.conv1d(xp, W, b, stride=s, dilation=d).transpose(1, 2)
+    cols = R.act_im2col(x, k, s, p, pr, d, act, a, reflect)
     assert cols.shape[1] % 8 == 0
     Wg = F.pad(W.permute(0, 2, 1).reshape(O, k * C), (0, cols.shape[1] - k * C))
     torch.testing.assert_close((cols @ Wg.t() + b).reshape(B, -1, O), ref, atol=1e-4, rtol=1e-4)
 
 
-@pytest.mark.parametrize("s", [2, 5, 8])
-def test_convt_fold_is_conv_transpose(s):
+@pytest.mark.parametrize("s,p,pr", [(2, 1, 1), (5, 3, 3), (8, 4, 4), (4, 0, 4), (5, 1, 4)])
+def test_convt_fold_is_conv_transpose(s, p, pr):
     torch.manual_seed(0)
     B, T, C, O = 2, 11, 8, 6
-    k, p = 2 * s, math.ceil(s / 2)
+    k = 2 * s
     x, W, b = torch.randn(B, T, C), torch.randn(C, O, k), torch.randn(O)
-    ref = F.conv_transpose1d(x.transpose(1, 2), W, b, stride=s, padding=p).transpose(1, 2)
+    full = F.conv_transpose1d(x.transpose(1, 2), W, b, stride=s).transpose(1, 2)
+    ref = full[:, p:full.shape[1] - pr]
     Y = (x.reshape(-1, C) @ W.permute(2, 1, 0).reshape(k * O, C).t()).reshape(B, T, k * O)
-    torch.testing.assert_close(R.convt_fold(Y, b, O, s, p), ref, atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(R.convt_fold(Y, b, O, s, p, pr), ref, atol=1e-4, rtol=1e-4)
+
+
+def test_lstm_cell_is_torch_lstm():
+    torch.manual_seed(0)
+    T, B, H = 9, 3, 16
+    lstm = torch.nn.LSTM(H, H, 1)
+    x = torch.randn(T, B, H)
+    with torch.no_grad():
+        ref = lstm(x)[0]
+        G = x @ lstm.weight_ih_l0.t() + lstm.bias_ih_l0 + lstm.bias_hh_l0
+        h, c = torch.zeros(B, H), torch.zeros(B, H)
+        out = []
+        for t in range(T):
+            h, c = R.lstm_cell(G[t] + h @ lstm.weight_hh_l0.t(), c)
+            out.append(h)
+    torch.testing.assert_close(torch.stack(out), ref, atol=1e-5, rtol=1e-5)
 
 
 def test_dac_matches_transformers():
