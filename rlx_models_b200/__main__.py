@@ -79,7 +79,8 @@ def cmd_run(a):
     from .runtime.engine import SamplingParams
     rc = _run_config(a)
     base = {"max_num_seqs": 8, "max_model_len": a.max_model_len, "kv_memory_gb": a.kv_gb}
-    cli = _explicit(a, a._defaults, {"max_model_len": "max_model_len", "kv_gb": "kv_memory_gb"})
+    cli = _explicit(a, a._defaults, {"max_model_len": "max_model_len", "kv_gb": "kv_memory_gb",
+                                     "kv_cache_dtype": "kv_cache_dtype"})
     llm = load(a.model or rc.model, engine_config=rc.engine_config(**{**{k: v for k, v in base.items()
                                                                          if k not in rc.serve}, **cli}))
     tok = llm.tokenizer
@@ -106,7 +107,7 @@ def cmd_serve(a):
     rc = _run_config(a)
     base = {"max_num_seqs": a.max_num_seqs, "max_model_len": a.max_model_len, "kv_memory_gb": a.kv_gb}
     cli = _explicit(a, a._defaults, {"max_num_seqs": "max_num_seqs", "max_model_len": "max_model_len",
-                                     "kv_gb": "kv_memory_gb"})
+                                     "kv_gb": "kv_memory_gb", "kv_cache_dtype": "kv_cache_dtype"})
     model = a.model or rc.model
     llm = load(model, engine_config=rc.engine_config(**{**{k: v for k, v in base.items() if k not in rc.serve},
                                                         **cli}))
@@ -204,6 +205,8 @@ def main(argv=None):
         p.add_argument("--show-knobs", action="store_true", help="print the knob table at startup")
         p.add_argument("--max-model-len", type=int, default=4096)
         p.add_argument("--kv-gb", type=float, default=8.0)
+        p.add_argument("--kv-cache-dtype", default="bf16", choices=["bf16", "fp8"],
+                       help="fp8: e4m3 KV pages (half the cache bytes; the decode kernel reads them directly)")
         if name == "run":
             p.add_argument("--prompt", default="Hello")
             p.add_argument("--ids", default=None, help="comma-separated token ids instead of --prompt")

@@ -117,6 +117,31 @@ def wgrad(args, dev, timer, tf, hbm):
     ops.check_errors(dev)
 
 
+def decode_attn_rows(args, cfg, dev, timer, hbm, rows, write=True):
+    """Decode attention over bf16 and float8 e4m3 pages (batch 64 at 1400 and
+    2300 tokens of context; the pages spread over a cache larger than L2)."""
+    Hq, Hkv, D = cfg.num_attention_heads // args.tp, cfg.num_key_value_heads // args.tp, cfg.head_dim
+    for dt, esize in ((torch.bfloat16, 2), (torch.float8_e4m3fn, 1)):
+        for (B, ctx) in ((64, 1400), (64, 2300)):
+            nbps = (ctx + 15) // 16
+            NB = B * nbps + 1
+            kc = torch.randn(NB, Hkv, 16, D, device=dev).to(dt)
+            vc = torch.randn(NB, Hkv, 16, D, device=dev).to(dt)
+            tables = torch.randperm(NB - 1, device=dev)[:B * nbps].view(B, nbps).int()
+            ctxs = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+            q = torch.randn(B, Hq, D, device=dev).bfloat16()
+            out = torch.empty_like(q)
+            t = timer(lambda: ops.decode_attention(q, kc, vc, tables, ctxs, scale=1 / math.sqrt(D), out=out),
+                      args.reps)
+            byts = 2.0 * B * ctx * Hkv * D * esize
+            rows.append(dict(op="decode_attn" if esize == 2 else "decode_attn_fp8", B=B, ctx=ctx,
+                             us=round(t * 1e6, 1), tbs=round(byts / t / 1e12, 2),
+                             frac_hbm=round(byts / t / 1e12 / hbm, 3)))
+            print(json.dumps(rows[-1]), flush=True)
+    if write and args.json:
+        json.dump({"peaks": {"hbm_tbs": hbm}, "rows": rows}, open(args.json, "w"), indent=1)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="qwen3-8b")
@@ -137,6 +162,8 @@ def main():
     rows = []
     if args.only in ("wgrad", "wgrad_push"):
         return wgrad(args, dev, timer, tf, hbm)
+    if args.only == "decode_attn":
+        return decode_attn_rows(args, cfg, dev, timer, hbm, rows)
     if args.only:
         for name, m, n, k, mode in gemm_rows(cfg, args.tp, args.M):
             if name != args.only:
@@ -177,21 +204,8 @@ def main():
                              vs_cublas=round(tc / t, 2)))
             print(json.dumps(rows[-1]), flush=True)
     # attention: decode batch 64 at ~1400 context; prefill 8 x 1024
+    decode_attn_rows(args, cfg, dev, timer, hbm, rows, write=False)
     Hq, Hkv, D = cfg.num_attention_heads // args.tp, cfg.num_key_value_heads // args.tp, cfg.head_dim
-    for (B, ctx) in ((64, 1400), (64, 2300)):
-        nbps = (ctx + 15) // 16
-        NB = B * nbps + 1
-        kc = torch.randn(NB, Hkv, 16, D, device=dev).bfloat16()
-        vc = torch.randn_like(kc)
-        tables = torch.randperm(NB - 1, device=dev)[:B * nbps].view(B, nbps).int()
-        ctxs = torch.full((B,), ctx, dtype=torch.int32, device=dev)
-        q = torch.randn(B, Hq, D, device=dev).bfloat16()
-        out = torch.empty_like(q)
-        t = timer(lambda: ops.decode_attention(q, kc, vc, tables, ctxs, scale=1 / math.sqrt(D), out=out), args.reps)
-        byts = 2.0 * B * ctx * Hkv * D * 2
-        rows.append(dict(op="decode_attn", B=B, ctx=ctx, us=round(t * 1e6, 1), tbs=round(byts / t / 1e12, 2),
-                         frac_hbm=round(byts / t / 1e12 / hbm, 3)))
-        print(json.dumps(rows[-1]), flush=True)
     B, L = 8, 1024
     nbps = L // 16
     NB = B * nbps + 1

@@ -17,10 +17,13 @@
 // decode). The reference re-uploads host KV per step; here the KV is always
 // device resident in pages.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include <algorithm>
 #include <cstdlib>
 #include <stdexcept>
+#include <type_traits>
 
 #include "../common/b200.cuh"
 #include "../common/launch.h"
@@ -42,23 +45,58 @@ __device__ __forceinline__ float score_log2(float s, const AttnArgs& a, float sc
 // Decode: grid (B * Hkv, splits), 4 compute warps + 1 TMA producer warp.
 // Warp w consumes pages w, w+4, ... of this split from an NST-deep ring.
 // ---------------------------------------------------------------------------
-template <int D, int NST>
+// F8: pages hold float8 e4m3 ([16, D] bytes, one unswizzled TMA box); each
+// compute warp widens its page into a private bf16 staging tile in the 128-byte
+// swizzled layout the bf16 path reads, then releases the ring slot at once.
+template <int D, int NST, bool F8 = false>
 struct DecCfg {
-  static constexpr int PAGE_BYTES = 16 * D * 2;
+  static constexpr int PAGE_BYTES = 16 * D * (F8 ? 1 : 2);
   static constexpr int STAGE_BYTES = 2 * PAGE_BYTES;  // K page + V page
   static constexpr int MERGE_BYTES = 4 * 16 * (D + 2) * 4;
   static constexpr int RING_BYTES = NST * STAGE_BYTES;
-  static constexpr int SMEM = 1024 + (RING_BYTES > MERGE_BYTES ? RING_BYTES : MERGE_BYTES) + 2 * NST * 8 + 64;
+  static constexpr int RING_OR_MERGE = RING_BYTES > MERGE_BYTES ? RING_BYTES : MERGE_BYTES;
+  static constexpr int BF16_PAGE = 16 * D * 2;
+  static constexpr int STAGING_BYTES = F8 ? 4 * 2 * BF16_PAGE : 0;  // per compute warp: K and V in bf16
+  static constexpr int SMEM = 1024 + RING_OR_MERGE + STAGING_BYTES + 2 * NST * 8 + 64;
 };
 
-template <int D, int NST>
+// 16 e4m3 values -> 16 bf16 (exact: e4m3 values are representable in bf16).
+__device__ __forceinline__ void fp8x16_to_bf16(const uint4 raw, uint4& lo, uint4& hi) {
+  const __nv_fp8x2_storage_t* p = reinterpret_cast<const __nv_fp8x2_storage_t*>(&raw);
+  uint32_t w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(p[i], __NV_E4M3);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+    const __nv_bfloat162 b = __floats2bfloat162_rn(f.x, f.y);
+    w[i] = *reinterpret_cast<const uint32_t*>(&b);
+  }
+  lo = make_uint4(w[0], w[1], w[2], w[3]);
+  hi = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+// One [16, D] e4m3 page (row-major bytes) -> bf16 in the swizzled page layout.
+template <int D>
+__device__ __forceinline__ void widen_page(const uint8_t* src, uint8_t* dst, int lane) {
+#pragma unroll
+  for (int c = lane; c < D; c += 32) {
+    const int row = c / (D / 16), col = (c % (D / 16)) * 16;
+    uint4 lo, hi;
+    fp8x16_to_bf16(*reinterpret_cast<const uint4*>(src + row * D + col), lo, hi);
+    *reinterpret_cast<uint4*>(dst + sw128_off(row, col, 16)) = lo;
+    *reinterpret_cast<uint4*>(dst + sw128_off(row, col + 8, 16)) = hi;
+  }
+}
+
+template <int D, int NST, bool F8 = false>
 __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant__ CUtensorMap tmK,
                                                           const __grid_constant__ CUtensorMap tmV, AttnArgs a) {
-  using Cf = DecCfg<D, NST>;
+  using Cf = DecCfg<D, NST, F8>;
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-  const int ring_or_merge = Cf::RING_BYTES > Cf::MERGE_BYTES ? Cf::RING_BYTES : Cf::MERGE_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring_or_merge);
+  const int ring_or_merge = Cf::RING_OR_MERGE;
+  uint8_t* staging = smem + ring_or_merge;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring_or_merge + Cf::STAGING_BYTES);
   uint64_t* empty = full + NST;
 
   pdl_wait();
@@ -113,10 +151,15 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
         const int row = (blk * a.Hkv + hkv) * 16;
         uint8_t* st = smem + s * Cf::STAGE_BYTES;
         mbar_arrive_expect_tx(&full[s], Cf::STAGE_BYTES);
+        if constexpr (F8) {
+          tma_load_2d(st, &tmK, &full[s], 0, row);
+          tma_load_2d(st + Cf::PAGE_BYTES, &tmV, &full[s], 0, row);
+        } else {
 #pragma unroll
-        for (int bx = 0; bx < D / 64; ++bx) {
-          tma_load_2d(st + bx * 2048, &tmK, &full[s], bx * 64, row);
-          tma_load_2d(st + Cf::PAGE_BYTES + bx * 2048, &tmV, &full[s], bx * 64, row);
+          for (int bx = 0; bx < D / 64; ++bx) {
+            tma_load_2d(st + bx * 2048, &tmK, &full[s], bx * 64, row);
+            tma_load_2d(st + Cf::PAGE_BYTES + bx * 2048, &tmV, &full[s], bx * 64, row);
+          }
         }
         if (++s == NST) {
           s = 0;
@@ -145,8 +188,19 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
       s = j % NST;
       ph = (j / NST) & 1;
       if (!mbar_wait(&full[s], ph, a.status, kErrTimeoutFull)) break;
-      const uint32_t kb = smem_u32(smem + s * Cf::STAGE_BYTES);
-      const uint32_t vb = kb + Cf::PAGE_BYTES;
+      uint32_t kb, vb;
+      if constexpr (F8) {
+        uint8_t* mine = staging + warp * 2 * Cf::BF16_PAGE;
+        widen_page<D>(smem + s * Cf::STAGE_BYTES, mine, lane);
+        widen_page<D>(smem + s * Cf::STAGE_BYTES + Cf::PAGE_BYTES, mine + Cf::BF16_PAGE, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);  // the ring slot is free once widened
+        kb = smem_u32(mine);
+        vb = kb + Cf::BF16_PAGE;
+      } else {
+        kb = smem_u32(smem + s * Cf::STAGE_BYTES);
+        vb = kb + Cf::PAGE_BYTES;
+      }
       float sc[2][4];
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
@@ -169,7 +223,8 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
         for (int h = 0; h < 4; ++h) {
           const int tk = base_tok + nt * 8 + 2 * t4 + (h & 1);
           const bool ok = tk < ctx && tk >= first_tok;
-          sc[nt][h] = ok ? score_log2(sc[nt][h], a, scale_log2) : kNegInf;
+          const float raw = F8 ? sc[nt][h] * a.k_scale : sc[nt][h];
+          sc[nt][h] = ok ? score_log2(raw, a, scale_log2) : kNegInf;
           mx[h >> 1] = fmaxf(mx[h >> 1], sc[nt][h]);
         }
 #pragma unroll
@@ -218,7 +273,7 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
         mma_bf16_16816(o[dp * 2 + 1], pa, b2, b3);
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
+      if (!F8 && lane == 0) mbar_arrive(&empty[s]);
     }
     // finish row sums inside the quad
 #pragma unroll
@@ -262,6 +317,7 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
       L += sm_ml[(w * 16 + r) * 2 + 1] * f;
       O += sm_o[(w * 16 + r) * D + d] * f;
     }
+    if (F8) O *= a.v_scale;
     const int head = hkv * G + r;
     if (nsplit == 1) {
       if (a.sinks != nullptr) {
@@ -560,8 +616,14 @@ int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
   if (G > 16 || a.Hq % a.Hkv != 0) throw std::runtime_error("b200.decode_attention: G must divide and be <= 16");
   if (a.D != 256 && a.D != 128 && a.D != 64) throw std::runtime_error("b200.decode_attention: D must be 64, 128 or 256");
   const int64_t rows = a.num_blocks * a.Hkv * 16;
-  CUtensorMap tk = make_tmap_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
-  CUtensorMap tv = make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
+  const bool f8 = a.kv_fp8 != 0;
+  // e4m3 pages: one unswizzled [16, D]-byte box per page (D <= 256 bytes per row)
+  CUtensorMap tk = f8 ? make_tmap_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, a.D, a.D, 16, a.D,
+                                     CU_TENSOR_MAP_SWIZZLE_NONE)
+                      : make_tmap_2d(a.k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
+  CUtensorMap tv = f8 ? make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rows, a.D, a.D, 16, a.D,
+                                     CU_TENSOR_MAP_SWIZZLE_NONE)
+                      : make_tmap_2d(a.v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, a.D, a.D, 16, 64);
   int splits = a.splits;
   const int sms = num_sms(a.device);
   AttnArgs args = a;
@@ -585,26 +647,82 @@ int decode_attention_launch(const AttnArgs& a, cudaStream_t st) {
   if (splits > 1 && a.ws_elems < (int64_t)a.B * a.Hq * splits * (a.D + 2))
     throw std::runtime_error("b200.decode_attention: split workspace too small");
   dim3 grid(a.B * a.Hkv, splits);
+  auto run = [&](auto dtag, auto ntag, auto ftag) {
+    constexpr int Dv = decltype(dtag)::value, NST = decltype(ntag)::value;
+    constexpr bool F8 = decltype(ftag)::value;
+    auto k = decode_attn_kernel<Dv, NST, F8>;
+    ensure_smem(k, DecCfg<Dv, NST, F8>::SMEM);
+    launch_pdl(k, grid, dim3(160), DecCfg<Dv, NST, F8>::SMEM, st, tk, tv, args);
+    if (splits > 1) launch_pdl(decode_merge_kernel<Dv>, dim3(a.B * a.Hq), dim3(Dv), 0, st, args, splits);
+  };
+  using I256 = std::integral_constant<int, 256>;
+  using I128 = std::integral_constant<int, 128>;
+  using I64 = std::integral_constant<int, 64>;
+  using N4 = std::integral_constant<int, 4>;
+  using N8 = std::integral_constant<int, 8>;
   if (a.D == 256) {
-    constexpr int NST = 4;
-    auto k = decode_attn_kernel<256, NST>;
-    ensure_smem(k, DecCfg<256, NST>::SMEM);
-    launch_pdl(k, grid, dim3(160), DecCfg<256, NST>::SMEM, st, tk, tv, args);
-    if (splits > 1) launch_pdl(decode_merge_kernel<256>, dim3(a.B * a.Hq), dim3(256), 0, st, args, splits);
+    if (f8) run(I256{}, N4{}, std::true_type{}); else run(I256{}, N4{}, std::false_type{});
   } else if (a.D == 128) {
-    constexpr int NST = 8;
-    auto k = decode_attn_kernel<128, NST>;
-    ensure_smem(k, DecCfg<128, NST>::SMEM);
-    launch_pdl(k, grid, dim3(160), DecCfg<128, NST>::SMEM, st, tk, tv, args);
-    if (splits > 1) launch_pdl(decode_merge_kernel<128>, dim3(a.B * a.Hq), dim3(128), 0, st, args, splits);
+    if (f8) run(I128{}, N8{}, std::true_type{}); else run(I128{}, N8{}, std::false_type{});
   } else {
-    constexpr int NST = 8;
-    auto k = decode_attn_kernel<64, NST>;
-    ensure_smem(k, DecCfg<64, NST>::SMEM);
-    launch_pdl(k, grid, dim3(160), DecCfg<64, NST>::SMEM, st, tk, tv, args);
-    if (splits > 1) launch_pdl(decode_merge_kernel<64>, dim3(a.B * a.Hq), dim3(64), 0, st, args, splits);
+    if (f8) run(I64{}, N8{}, std::true_type{}); else run(I64{}, N8{}, std::false_type{});
   }
   return splits > 1 ? 2 : 1;
+}
+
+namespace attn {
+// One CTA per (sequence, page): all kv heads of the page, K and V, e4m3 -> bf16.
+__global__ void __launch_bounds__(256) kv_dequant_pages_kernel(const uint8_t* __restrict__ k8,
+                                                               const uint8_t* __restrict__ v8,
+                                                               const int32_t* __restrict__ tables,
+                                                               const int32_t* __restrict__ ctx_lens, int max_blocks,
+                                                               int64_t page_bytes, float ks, float vs,
+                                                               __nv_bfloat16* __restrict__ k_out,
+                                                               __nv_bfloat16* __restrict__ v_out) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x / max_blocks, p = blockIdx.x % max_blocks;
+  if (p * 16 >= ctx_lens[b]) return;
+  const int64_t src = (int64_t)tables[(int64_t)b * max_blocks + p] * page_bytes;
+  const int64_t dst = (int64_t)blockIdx.x * page_bytes;
+  for (int64_t i = threadIdx.x * 16; i < page_bytes; i += 256 * 16) {
+    uint4 lo, hi;
+    fp8x16_to_bf16(*reinterpret_cast<const uint4*>(k8 + src + i), lo, hi);
+    if (ks != 1.f) {
+      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&lo);
+      __nv_bfloat16* f = reinterpret_cast<__nv_bfloat16*>(&hi);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        e[q] = __float2bfloat16(__bfloat162float(e[q]) * ks);
+        f[q] = __float2bfloat16(__bfloat162float(f[q]) * ks);
+      }
+    }
+    *reinterpret_cast<uint4*>(k_out + dst + i) = lo;
+    *reinterpret_cast<uint4*>(k_out + dst + i + 8) = hi;
+    fp8x16_to_bf16(*reinterpret_cast<const uint4*>(v8 + src + i), lo, hi);
+    if (vs != 1.f) {
+      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&lo);
+      __nv_bfloat16* f = reinterpret_cast<__nv_bfloat16*>(&hi);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        e[q] = __float2bfloat16(__bfloat162float(e[q]) * vs);
+        f[q] = __float2bfloat16(__bfloat162float(f[q]) * vs);
+      }
+    }
+    *reinterpret_cast<uint4*>(v_out + dst + i) = lo;
+    *reinterpret_cast<uint4*>(v_out + dst + i + 8) = hi;
+  }
+}
+}  // namespace attn
+
+void kv_dequant_pages_launch(const void* k8, const void* v8, const int32_t* block_tables, const int32_t* ctx_lens,
+                             int B, int max_blocks, int Hkv, int D, float k_scale, float v_scale, void* k_out,
+                             void* v_out, cudaStream_t st) {
+  if (B == 0 || max_blocks == 0) return;
+  launch_pdl(attn::kv_dequant_pages_kernel, dim3((unsigned)(B * max_blocks)), dim3(256), 0, st,
+             reinterpret_cast<const uint8_t*>(k8), reinterpret_cast<const uint8_t*>(v8), block_tables, ctx_lens,
+             max_blocks, (int64_t)Hkv * 16 * D, k_scale, v_scale, reinterpret_cast<__nv_bfloat16*>(k_out),
+             reinterpret_cast<__nv_bfloat16*>(v_out));
 }
 
 void prefill_attention_launch(const AttnArgs& a, cudaStream_t st) {

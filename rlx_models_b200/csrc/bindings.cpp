@@ -420,7 +420,7 @@ void qkv_rope(const Tensor& qkv, const optional<Tensor>& q_norm, const optional<
               const Tensor& positions, const optional<Tensor>& slots, const Tensor& inv_freq, double rope_scale,
               Tensor& q_out, const optional<Tensor>& k_cache, const optional<Tensor>& v_cache,
               const optional<Tensor>& k_out, const optional<Tensor>& v_out, int64_t Hq, int64_t Hkv, int64_t D,
-              double eps, int64_t rot_dim, const optional<Tensor>& bias) {
+              double eps, int64_t rot_dim, const optional<Tensor>& bias, double k_scale, double v_scale) {
   check_cuda(qkv, "qkv");
   if (rot_dim <= 0) rot_dim = D;
   TORCH_CHECK(rot_dim <= D && rot_dim % (2 * (D / 32)) == 0, "b200.qkv_rope: rot_dim must be <= head_dim and a "
@@ -458,6 +458,18 @@ void qkv_rope(const Tensor& qkv, const optional<Tensor>& q_norm, const optional<
   a.q_out = q_out.data_ptr();
   a.k_cache = const_cast<void*>(opt_ptr(k_cache));
   a.v_cache = const_cast<void*>(opt_ptr(v_cache));
+  if (k_cache.has_value() && k_cache->defined()) {
+    const auto kt = k_cache->scalar_type();
+    TORCH_CHECK((kt == at::kBFloat16 || kt == at::kFloat8_e4m3fn) && v_cache.has_value() &&
+                    v_cache->scalar_type() == kt,
+                "b200.qkv_rope: caches bf16 or float8_e4m3fn, both the same");
+    if (kt == at::kFloat8_e4m3fn) {
+      TORCH_CHECK(k_scale > 0 && v_scale > 0, "b200.qkv_rope: fp8 cache scales must be > 0");
+      a.kv_fp8 = 1;
+      a.k_inv_scale = (float)(1.0 / k_scale);
+      a.v_inv_scale = (float)(1.0 / v_scale);
+    }
+  }
   a.k_out = const_cast<void*>(opt_ptr(k_out));
   a.v_out = const_cast<void*>(opt_ptr(v_out));
   a.T = qkv.size(0);
@@ -491,7 +503,11 @@ static b200::AttnArgs attn_args(const Tensor& q, const Tensor& k_cache, const Te
               "b200.attention: out [Tq, Hq, D] (or a row-strided [Tq, Hq * D] view for prefill)");
   if (sinks.has_value() && sinks->defined())
     TORCH_CHECK(sinks->scalar_type() == at::kFloat && sinks->numel() == q.size(1), "b200.attention: sinks f32 [Hq]");
+  TORCH_CHECK((k_cache.scalar_type() == at::kBFloat16 || k_cache.scalar_type() == at::kFloat8_e4m3fn) &&
+                  v_cache.scalar_type() == k_cache.scalar_type(),
+              "b200.attention: caches bf16 or float8_e4m3fn, both the same");
   b200::AttnArgs a{};
+  a.kv_fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn ? 1 : 0;
   a.q = q.data_ptr();
   a.k_cache = k_cache.data_ptr();
   a.v_cache = v_cache.data_ptr();
@@ -514,10 +530,13 @@ static b200::AttnArgs attn_args(const Tensor& q, const Tensor& k_cache, const Te
 
 int64_t decode_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_cache, const Tensor& block_tables,
                          const Tensor& ctx_lens, Tensor& out, const optional<Tensor>& sinks, int64_t window,
-                         double scale, int64_t splits, Tensor& ws, Tensor& status, double softcap) {
+                         double scale, int64_t splits, Tensor& ws, Tensor& status, double softcap, double k_scale,
+                         double v_scale) {
   c10::cuda::CUDAGuard g(q.device());
   auto a = attn_args(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, window, scale, status);
   a.softcap = (float)softcap;
+  a.k_scale = (float)k_scale;
+  a.v_scale = (float)v_scale;
   TORCH_CHECK(q.size(0) == block_tables.size(0), "b200.decode_attention: one query per sequence");
   a.cu_q = nullptr;
   a.splits = (int)splits;
@@ -534,6 +553,7 @@ void prefill_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_c
                        double softcap) {
   c10::cuda::CUDAGuard g(q.device());
   auto a = attn_args(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, window, scale, status);
+  TORCH_CHECK(!a.kv_fp8, "b200.prefill: fp8 pages are read through kv_dequant_pages (bf16 copies)");
   a.softcap = (float)softcap;
   TORCH_CHECK(cu_q.scalar_type() == at::kInt && cu_q.numel() == block_tables.size(0) + 1, "b200.prefill: cu_q");
   a.cu_q = cu_q.data_ptr<int32_t>();
@@ -551,6 +571,28 @@ void prefill_attention(const Tensor& q, const Tensor& k_cache, const Tensor& v_c
     a.out_ld = out.stride(0);
   }
   b200::prefill_attention_launch(a, cur_stream(q));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void kv_dequant_pages(const Tensor& k8, const Tensor& v8, const Tensor& block_tables, const Tensor& ctx_lens,
+                      double k_scale, double v_scale, Tensor& k_out, Tensor& v_out) {
+  check_cuda(k8, "k8");
+  TORCH_CHECK(k8.scalar_type() == at::kFloat8_e4m3fn && v8.scalar_type() == at::kFloat8_e4m3fn && k8.dim() == 4 &&
+                  k8.is_contiguous() && v8.is_contiguous() && v8.sizes() == k8.sizes() && k8.size(2) == 16,
+              "b200.kv_dequant_pages: float8_e4m3fn pages [NB, Hkv, 16, D]");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.dim() == 2 && block_tables.is_contiguous() &&
+                  ctx_lens.scalar_type() == at::kInt && ctx_lens.numel() == block_tables.size(0),
+              "b200.kv_dequant_pages: int32 tables [B, max_blocks] and ctx_lens [B]");
+  const int64_t B = block_tables.size(0), mb = block_tables.size(1), Hkv = k8.size(1), D = k8.size(3);
+  TORCH_CHECK(D % 16 == 0, "b200.kv_dequant_pages: D % 16");
+  for (const Tensor* t : {&k_out, &v_out})
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->is_contiguous() && t->dim() == 4 && t->size(0) >= B * mb &&
+                    t->size(1) == Hkv && t->size(2) == 16 && t->size(3) == D && t->device() == k8.device(),
+                "b200.kv_dequant_pages: bf16 outputs [>= B * max_blocks, Hkv, 16, D]");
+  c10::cuda::CUDAGuard g(k8.device());
+  b200::kv_dequant_pages_launch(k8.data_ptr(), v8.data_ptr(), block_tables.data_ptr<int32_t>(),
+                                ctx_lens.data_ptr<int32_t>(), (int)B, (int)mb, (int)Hkv, (int)D, (float)k_scale,
+                                (float)v_scale, k_out.data_ptr(), v_out.data_ptr(), cur_stream(k8));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -1570,7 +1612,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_rope", &qkv_rope);
   m.def("decode_attention", &decode_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("block_tables"), py::arg("ctx_lens"), py::arg("out"), py::arg("sinks"), py::arg("window"),
-        py::arg("scale"), py::arg("splits"), py::arg("ws"), py::arg("status"), py::arg("softcap") = 0.0);
+        py::arg("scale"), py::arg("splits"), py::arg("ws"), py::arg("status"), py::arg("softcap") = 0.0,
+        py::arg("k_scale") = 1.0, py::arg("v_scale") = 1.0);
   m.def("prefill_attention", &prefill_attention, py::arg("q"), py::arg("k_cache"), py::arg("v_cache"),
         py::arg("block_tables"), py::arg("ctx_lens"), py::arg("cu_q"), py::arg("out"), py::arg("sinks"),
         py::arg("window"), py::arg("scale"), py::arg("max_q_len"), py::arg("status"), py::arg("causal"),
@@ -1587,6 +1630,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("swiglu_train_bwd", &swiglu_train_bwd);
   m.def("scale_by", &scale_by);
   m.def("instance_norm", &instance_norm);
+  m.def("kv_dequant_pages", &kv_dequant_pages);
   m.def("act_im2col", &act_im2col);
   m.def("lstm_cell", &lstm_cell);
   m.def("convt_fold", &convt_fold);

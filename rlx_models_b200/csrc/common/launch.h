@@ -276,6 +276,8 @@ struct QkvRopeArgs {
   int Hq, Hkv, D;
   float eps;
   const void* bias = nullptr;  // [(Hq + 2 Hkv) * D] bf16 added to the fp32 sums (accumulate-mode input only)
+  int kv_fp8 = 0;              // caches hold float8 e4m3: stored value = saturate(x / scale)
+  float k_inv_scale = 1.f, v_inv_scale = 1.f;
 };
 void qkv_rope_launch(const QkvRopeArgs& a, cudaStream_t st);
 // bias ([H] bf16, may be null) is added to the fp32 sums before the residual add
@@ -316,8 +318,15 @@ struct AttnArgs {
   int64_t ws_elems;
   int* status;
   int device;
+  int kv_fp8 = 0;            // decode: pages hold float8 e4m3 (K = k_scale * stored, V = v_scale * stored)
+  float k_scale = 1.f, v_scale = 1.f;
 };
 int decode_attention_launch(const AttnArgs& a, cudaStream_t st);  // returns #launches
+// float8 e4m3 pages of the sequences in a prefill batch -> bf16 pages at block b * max_blocks + p
+// (pages at or past ceil(ctx_lens[b] / 16) are skipped): see attention/attention.cu.
+void kv_dequant_pages_launch(const void* k8, const void* v8, const int32_t* block_tables, const int32_t* ctx_lens,
+                             int B, int max_blocks, int Hkv, int D, float k_scale, float v_scale, void* k_out,
+                             void* v_out, cudaStream_t st);
 void prefill_attention_launch(const AttnArgs& a, cudaStream_t st);
 // tcgen05 flash attention (head_dim 128, G <= 8 query heads per kv head); used by
 // prefill_attention_launch when supported (B200_ATTN_LEGACY=1 forces the mma.sync kernel)

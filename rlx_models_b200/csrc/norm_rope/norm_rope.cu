@@ -13,6 +13,7 @@
 // `per_head_rms`); RoPE rotates (x[i], x[i+half]) pairs
 // (standard_decoder.rs:411,705; rlx-qwen3 src/generator.rs:4486).
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 
 #include "../common/b200.cuh"
 #include "../common/launch.h"
@@ -216,10 +217,18 @@ __global__ void qkv_rope_kernel(QkvRopeArgs a) {
     const int64_t slot = a.slots[t];
     if (slot >= 0) {
       const int64_t blk = slot >> 4, off = slot & 15;
-      __nv_bfloat16* cache = reinterpret_cast<__nv_bfloat16*>(is_k ? a.k_cache : a.v_cache);
-      __nv_bfloat16* dst = cache + ((blk * a.Hkv + kh) * 16 + off) * D;
+      const int64_t at = ((blk * a.Hkv + kh) * 16 + off) * D;
+      if (a.kv_fp8) {
+        // the bf16-rounded value, scaled, to e4m3 with saturation (what the bf16 cache would hold)
+        __nv_fp8_e4m3* dst = reinterpret_cast<__nv_fp8_e4m3*>(is_k ? a.k_cache : a.v_cache) + at;
+        const float inv = is_k ? a.k_inv_scale : a.v_inv_scale;
 #pragma unroll
-      for (int e = 0; e < E; ++e) dst[lane * E + e] = __float2bfloat16(x[e]);
+        for (int e = 0; e < E; ++e) dst[lane * E + e] = __nv_fp8_e4m3(__bfloat162float(__float2bfloat16(x[e])) * inv);
+      } else {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(is_k ? a.k_cache : a.v_cache) + at;
+#pragma unroll
+        for (int e = 0; e < E; ++e) dst[lane * E + e] = __float2bfloat16(x[e]);
+      }
     }
   }
 }

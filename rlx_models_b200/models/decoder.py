@@ -178,8 +178,25 @@ class DecoderLM:
             raise NotImplementedError("KV retrieval is for full-attention layers without sinks")
         self.retrieval = KVRetrieval(self.cfg.num_hidden_layers, num_blocks, self.hkv, self.D, self.device, **kw)
 
+    kv_dtype = torch.bfloat16       # or torch.float8_e4m3fn (set_kv_cache_dtype)
+    kv_scales = (1.0, 1.0)
+
+    def set_kv_cache_dtype(self, dtype: str, scales: tuple = (1.0, 1.0)) -> None:
+        """"bf16" or "fp8" (e4m3 pages holding value / scale; scales (k, v))."""
+        if dtype not in ("bf16", "fp8"):
+            raise ValueError(f"kv cache dtype {dtype!r}: 'bf16' or 'fp8'")
+        if dtype == "fp8" and getattr(self, "retrieval", None) is not None:
+            raise NotImplementedError("KV retrieval reads bf16 pages")
+        self.kv_dtype = torch.float8_e4m3fn if dtype == "fp8" else torch.bfloat16
+        self.kv_scales = (float(scales[0]), float(scales[1]))
+
+    def kv_bytes_per_block(self) -> int:
+        return PagedKVCache.bytes_per_block(self.cfg.num_hidden_layers, self.hkv, self.D,
+                                            1 if self.kv_dtype == torch.float8_e4m3fn else 2)
+
     def make_kv_cache(self, num_blocks: int) -> PagedKVCache:
-        return PagedKVCache(self.cfg.num_hidden_layers, num_blocks, self.hkv, self.D, self.device)
+        return PagedKVCache(self.cfg.num_hidden_layers, num_blocks, self.hkv, self.D, self.device,
+                            dtype=self.kv_dtype, scales=self.kv_scales)
 
     # -- forward ---------------------------------------------------------------
     def _attention(self, i: int, L: LayerWeights, x: torch.Tensor, fb: ForwardBatch, kv: PagedKVCache):
@@ -195,12 +212,14 @@ class DecoderLM:
             qd, kd = self.hq * self.D, self.hkv * self.D
             ops.rmsnorm(qkv[:, :qd], L.q_norm, self.cfg.rms_norm_eps, out=qkv[:, :qd])
             ops.rmsnorm(qkv[:, qd:qd + kd], L.k_norm, self.cfg.rms_norm_eps, out=qkv[:, qd:qd + kd])
+        f8 = kc.dtype == torch.float8_e4m3fn
+        sc = kv.scales if f8 else (1.0, 1.0)
         q = ops.qkv_rope(qkv, num_q_heads=self.hq, num_kv_heads=self.hkv, head_dim=self.D,
                          positions=fb.positions, inv_freq=L.inv_freq, rope_scale=L.rope_mult,
                          rot_dim=self.cfg.rotary_dim,
                          q_norm=None if full else L.q_norm, k_norm=None if full else L.k_norm,
                          eps=self.cfg.rms_norm_eps, slots=fb.slots,
-                         k_cache=kc, v_cache=vc, bias=L.bqkv if acc else None)
+                         k_cache=kc, v_cache=vc, bias=L.bqkv if acc else None, kv_scales=sc)
         o = torch.empty_like(q)
         nd = fb.num_decode
         retrieval = getattr(self, "retrieval", None)
@@ -211,9 +230,13 @@ class DecoderLM:
             if retrieval is not None:
                 tables, ctx = retrieval.select(i, q[:nd], tables, ctx)
             ops.decode_attention(q[:nd], kc, vc, tables, ctx, scale=self.scale,
-                                 sinks=L.sinks, window=L.window, out=o[:nd], softcap=self.cfg.attn_softcap)
+                                 sinks=L.sinks, window=L.window, out=o[:nd], softcap=self.cfg.attn_softcap,
+                                 kv_scales=sc)
         if T > nd:
-            ops.prefill_attention(q[nd:], kc, vc, fb.pre_block_tables, fb.pre_ctx_lens, fb.pre_cu_q,
+            pk, pv, ptab = kc, vc, fb.pre_block_tables
+            if f8:  # prefill reads bf16 copies of its sequences' pages (after this step's writes)
+                pk, pv, ptab = ops.kv_dequant_pages(kc, vc, fb.pre_block_tables, fb.pre_ctx_lens, sc)
+            ops.prefill_attention(q[nd:], pk, pv, ptab, fb.pre_ctx_lens, fb.pre_cu_q,
                                   fb.pre_max_q, scale=self.scale, sinks=L.sinks, window=L.window, out=o[nd:],
                                   softcap=self.cfg.attn_softcap, causal=self.cfg.causal)
         return o.view(T, self.hq * self.D)

@@ -250,29 +250,57 @@ def qkv_rope(qkv: torch.Tensor, *, num_q_heads: int, num_kv_heads: int, head_dim
              slots: torch.Tensor | None = None, k_cache: torch.Tensor | None = None,
              v_cache: torch.Tensor | None = None, q_out: torch.Tensor | None = None,
              k_out: torch.Tensor | None = None, v_out: torch.Tensor | None = None,
-             rot_dim: int = 0, bias: torch.Tensor | None = None) -> torch.Tensor:
+             rot_dim: int = 0, bias: torch.Tensor | None = None, kv_scales: tuple = (1.0, 1.0)) -> torch.Tensor:
     """QK RMSNorm + RoPE on the fused qkv projection; K/V written to the paged cache.
     ``rot_dim`` (0 = head_dim): rotate only the first rot_dim dims of each head.
-    ``bias`` (bf16) is added to an fp32 accumulate-mode ``qkv`` before rounding."""
+    ``bias`` (bf16) is added to an fp32 accumulate-mode ``qkv`` before rounding.
+    float8_e4m3fn caches store saturate(value / scale) with ``kv_scales`` = (k, v)."""
     T = qkv.shape[0]
     if q_out is None:
         q_out = torch.empty(T, num_q_heads, head_dim, dtype=torch.bfloat16, device=qkv.device)
     _count(1)
     ext().qkv_rope(qkv, q_norm, k_norm, positions, slots, inv_freq, float(rope_scale), q_out, k_cache,
-                   v_cache, k_out, v_out, num_q_heads, num_kv_heads, head_dim, float(eps), int(rot_dim), bias)
+                   v_cache, k_out, v_out, num_q_heads, num_kv_heads, head_dim, float(eps), int(rot_dim), bias,
+                   float(kv_scales[0]), float(kv_scales[1]))
     return q_out
 
 
 def decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, *, scale, sinks=None, window=0,
-                     splits=0, out=None, softcap=0.0):
+                     splits=0, out=None, softcap=0.0, kv_scales=(1.0, 1.0)):
     """Paged decode attention (one query per sequence); ``softcap`` > 0 caps
     the scaled scores at softcap * tanh(s / softcap)."""
     if out is None:
         out = torch.empty_like(q)
     s = scratch(q.device)
     _count(ext().decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, out, sinks, int(window), float(scale),
-                           int(splits), s.attn_ws, s.status, float(softcap)))
+                           int(splits), s.attn_ws, s.status, float(softcap), float(kv_scales[0]),
+                           float(kv_scales[1])))
     return out
+
+
+_DEQ_CACHE: dict = {}
+
+
+def kv_dequant_pages(k_cache, v_cache, block_tables, ctx_lens, kv_scales=(1.0, 1.0)):
+    """bf16 copies of the float8_e4m3fn pages a prefill batch reads: page p of
+    sequence b goes to block b * max_blocks + p of the returned [B * max_blocks,
+    Hkv, 16, D] caches, whose block table is returned with them (an arange).
+    The buffers are reused across calls on a device (grown as needed)."""
+    B, mb = block_tables.shape
+    _, Hkv, _, D = k_cache.shape
+    key = (k_cache.device, Hkv, D)
+    st = _DEQ_CACHE.get(key)
+    n = B * mb
+    if st is None or st[0].shape[0] < n:
+        cap = max(n, 2 * st[0].shape[0]) if st is not None else n
+        st = _DEQ_CACHE[key] = (torch.empty(cap, Hkv, 16, D, dtype=torch.bfloat16, device=k_cache.device),
+                                torch.empty(cap, Hkv, 16, D, dtype=torch.bfloat16, device=k_cache.device),
+                                torch.arange(cap, dtype=torch.int32, device=k_cache.device))
+    kb, vb, ar = st
+    _count(1)
+    ext().kv_dequant_pages(k_cache, v_cache, block_tables, ctx_lens, float(kv_scales[0]), float(kv_scales[1]),
+                           kb, vb)
+    return kb, vb, ar[:n].view(B, mb)
 
 
 def prefill_attention(q, k_cache, v_cache, block_tables, ctx_lens, cu_q, max_q_len, *, scale, sinks=None,

@@ -107,6 +107,10 @@ class EngineConfig:
     # long-context decode over retrieved KV blocks, e.g. {"topk_blocks": 64,
     # "window_blocks": 16, "sink_blocks": 1} (runtime/kv_retrieval.py); None = full attention
     kv_retrieval: dict | None = None
+    # "bf16", or "fp8": float8 e4m3 pages holding value / scale with scales (k, v) (the
+    # decode kernel reads them directly; prefill reads bf16 copies of its pages)
+    kv_cache_dtype: str = "bf16"
+    kv_cache_scales: tuple = (1.0, 1.0)
     # schedule / launch step n+1 before step n's tokens come back (see module docstring)
     async_scheduling: bool = True
     # per-step metrics as JSON lines (step kind, tokens, batch occupancy, KV blocks in use,
@@ -164,6 +168,10 @@ class LLMEngine:
             raise ValueError(f"{type(model).__name__}: max_model_len {cfg.max_model_len} > {lim}, the context this "
                              "model's kernels run exactly (e.g. Llama-4's chunked attention starts there)")
         self.max_blocks_per_seq = (cfg.max_model_len + BLOCK_SIZE - 1) // BLOCK_SIZE
+        if cfg.kv_cache_dtype != "bf16" or hasattr(model, "set_kv_cache_dtype"):
+            if not hasattr(model, "set_kv_cache_dtype"):
+                raise NotImplementedError(f"{type(model).__name__}: kv_cache_dtype {cfg.kv_cache_dtype!r}")
+            model.set_kv_cache_dtype(cfg.kv_cache_dtype, cfg.kv_cache_scales)
         nb = cfg.num_blocks
         if nb <= 0:
             per = (model.kv_bytes_per_block() if hasattr(model, "kv_bytes_per_block")

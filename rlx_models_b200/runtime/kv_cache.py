@@ -17,8 +17,16 @@ BLOCK_SIZE = 16
 
 
 class PagedKVCache:
+    """``dtype`` bf16, or torch.float8_e4m3fn: pages then hold saturate(x / s)
+    with the per-cache ``scales`` = (s_k, s_v), halving the cache's bytes and
+    the decode kernel's reads (prefill reads bf16 copies of its pages)."""
+
     def __init__(self, num_layers: int, num_blocks: int, num_kv_heads: int, head_dim: int,
-                 device: torch.device | str = "cuda", dtype: torch.dtype = torch.bfloat16):
+                 device: torch.device | str = "cuda", dtype: torch.dtype = torch.bfloat16,
+                 scales: tuple = (1.0, 1.0)):
+        if dtype not in (torch.bfloat16, torch.float8_e4m3fn):
+            raise ValueError(f"KV cache dtype {dtype}: bf16 or float8_e4m3fn")
+        self.dtype, self.scales = dtype, (float(scales[0]), float(scales[1]))
         self.num_layers = num_layers
         self.num_blocks = num_blocks
         self.num_kv_heads = num_kv_heads

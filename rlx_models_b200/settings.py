@@ -186,7 +186,7 @@ def run_config_from_dict(d: dict) -> RunConfig:
     _check_keys("serve", serve, EngineConfig)
     train = dict(d.get("train") or {})
     _check_keys("train", train, TrainConfig)
-    for k in ("betas", "lora_targets", "graph_batch_sizes"):
+    for k in ("betas", "lora_targets", "graph_batch_sizes", "kv_cache_scales"):
         for sec in (serve, train):
             if k in sec and isinstance(sec[k], list):
                 sec[k] = tuple(sec[k])
