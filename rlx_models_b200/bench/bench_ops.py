@@ -121,7 +121,10 @@ def decode_attn_rows(args, cfg, dev, timer, hbm, rows, write=True):
     """Decode attention over bf16 and float8 e4m3 pages (batch 64 at 1400 and
     2300 tokens of context; the pages spread over a cache larger than L2)."""
     Hq, Hkv, D = cfg.num_attention_heads // args.tp, cfg.num_key_value_heads // args.tp, cfg.head_dim
-    for dt, esize in ((torch.bfloat16, 2), (torch.float8_e4m3fn, 1)):
+    for dt, esize, splits in ((torch.bfloat16, 2, 0), (torch.float8_e4m3fn, 1, 0), (torch.float8_e4m3fn, 1, 2),
+                              (torch.float8_e4m3fn, 1, 3)):
+        if splits and args.only != "decode_attn":
+            continue
         for (B, ctx) in ((64, 1400), (64, 2300)):
             nbps = (ctx + 15) // 16
             NB = B * nbps + 1
@@ -131,10 +134,10 @@ def decode_attn_rows(args, cfg, dev, timer, hbm, rows, write=True):
             ctxs = torch.full((B,), ctx, dtype=torch.int32, device=dev)
             q = torch.randn(B, Hq, D, device=dev).bfloat16()
             out = torch.empty_like(q)
-            t = timer(lambda: ops.decode_attention(q, kc, vc, tables, ctxs, scale=1 / math.sqrt(D), out=out),
-                      args.reps)
+            t = timer(lambda: ops.decode_attention(q, kc, vc, tables, ctxs, scale=1 / math.sqrt(D), out=out,
+                                                   splits=splits), args.reps)
             byts = 2.0 * B * ctx * Hkv * D * esize
-            rows.append(dict(op="decode_attn" if esize == 2 else "decode_attn_fp8", B=B, ctx=ctx,
+            rows.append(dict(op="decode_attn" if esize == 2 else "decode_attn_fp8", B=B, ctx=ctx, splits=splits,
                              us=round(t * 1e6, 1), tbs=round(byts / t / 1e12, 2),
                              frac_hbm=round(byts / t / 1e12 / hbm, 3)))
             print(json.dumps(rows[-1]), flush=True)

@@ -46,7 +46,7 @@ __device__ __forceinline__ float score_log2(float s, const AttnArgs& a, float sc
 // Warp w consumes pages w, w+4, ... of this split from an NST-deep ring.
 // ---------------------------------------------------------------------------
 // F8: pages hold float8 e4m3 ([16, D] bytes, one unswizzled TMA box); each
-// compute warp widens its page into a private bf16 staging tile in the 128-byte
+// compute warp widens its page into a private f16 staging tile in the 128-byte
 // swizzled layout the bf16 path reads, then releases the ring slot at once.
 template <int D, int NST, bool F8 = false>
 struct DecCfg {
@@ -59,6 +59,45 @@ struct DecCfg {
   static constexpr int STAGING_BYTES = F8 ? 4 * 2 * BF16_PAGE : 0;  // per compute warp: K and V in bf16
   static constexpr int SMEM = 1024 + RING_OR_MERGE + STAGING_BYTES + 2 * NST * 8 + 64;
 };
+
+// fp8 pages are widened to f16 (one cvt per two values; e4m3 is exact in f16)
+// and the F8 kernel runs its MMAs in f16 (Q converted once, P packed as f16).
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <bool F8>
+__device__ __forceinline__ void mma16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  if constexpr (F8) mma_f16_16816(d, a, b0, b1);
+  else mma_bf16_16816(d, a, b0, b1);
+}
+
+template <bool F8>
+__device__ __forceinline__ uint32_t pack16(float a, float b) {
+  if constexpr (F8) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+  } else {
+    return pack_bf16x2(a, b);
+  }
+}
+
+// 16 e4m3 values -> 16 f16.
+__device__ __forceinline__ void fp8x16_to_f16(const uint4 raw, uint4& lo, uint4& hi) {
+  const __nv_fp8x2_storage_t* p = reinterpret_cast<const __nv_fp8x2_storage_t*>(&raw);
+  uint32_t w[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(p[i], __NV_E4M3);
+    w[i] = *reinterpret_cast<const uint32_t*>(&hr);
+  }
+  lo = make_uint4(w[0], w[1], w[2], w[3]);
+  hi = make_uint4(w[4], w[5], w[6], w[7]);
+}
 
 // 16 e4m3 values -> 16 bf16 (exact: e4m3 values are representable in bf16).
 __device__ __forceinline__ void fp8x16_to_bf16(const uint4 raw, uint4& lo, uint4& hi) {
@@ -75,16 +114,25 @@ __device__ __forceinline__ void fp8x16_to_bf16(const uint4 raw, uint4& lo, uint4
   hi = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
-// One [16, D] e4m3 page (row-major bytes) -> bf16 in the swizzled page layout.
+// One [16, D] e4m3 page (row-major bytes) -> f16 in the swizzled page layout.
+// Work item = (row, 64-column box), 4 lanes of 16 values each; the two items
+// of an 8-lane group are rows r and r + 1 with boxes of opposite parity (D >=
+// 128; for D = 64 the rows alternate 64-byte halves), so each group's 16-byte
+// reads cover all 32 banks and its swizzled writes land on disjoint chunks.
 template <int D>
 __device__ __forceinline__ void widen_page(const uint8_t* src, uint8_t* dst, int lane) {
+  constexpr int NB = D / 64;
+  const int h = (lane >> 2) & 1, cq = lane & 3, g = lane >> 3;
 #pragma unroll
-  for (int c = lane; c < D; c += 32) {
-    const int row = c / (D / 16), col = (c % (D / 16)) * 16;
+  for (int it = 0; it < 2 * NB; ++it) {
+    const int P = it * 4 + g;                 // pair of items, 0 .. 8 * NB - 1
+    const int r = 2 * (P & 7) + h;
+    const int bx = NB >= 2 ? ((P >> 3) ^ h) : 0;
+    const int col = bx * 64 + cq * 16;
     uint4 lo, hi;
-    fp8x16_to_bf16(*reinterpret_cast<const uint4*>(src + row * D + col), lo, hi);
-    *reinterpret_cast<uint4*>(dst + sw128_off(row, col, 16)) = lo;
-    *reinterpret_cast<uint4*>(dst + sw128_off(row, col + 8, 16)) = hi;
+    fp8x16_to_f16(*reinterpret_cast<const uint4*>(src + r * D + col), lo, hi);
+    *reinterpret_cast<uint4*>(dst + sw128_off(r, col, 16)) = lo;
+    *reinterpret_cast<uint4*>(dst + sw128_off(r, col + 8, 16)) = hi;
   }
 }
 
@@ -178,7 +226,12 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
       for (int h = 0; h < 4; ++h) {
         const int r = g + ((h & 1) ? 8 : 0);
         const int c = ks * 16 + 2 * t4 + ((h & 2) ? 8 : 0);
-        qa[ks][h] = (r < G) ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)r * D + c) : 0u;
+        uint32_t v = (r < G) ? *reinterpret_cast<const uint32_t*>(qb + (int64_t)r * D + c) : 0u;
+        if constexpr (F8) {  // the F8 kernel multiplies in f16
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+          v = pack16<true>(f.x, f.y);
+        }
+        qa[ks][h] = v;
       }
     }
     int s = warp % NST;
@@ -211,8 +264,8 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
         const int d0 = ks * 16 + (mi & 1) * 8;
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4(kb + sw128_off(tok, d0, 16), b0, b1, b2, b3);
-        mma_bf16_16816(sc[0], qa[ks], b0, b1);
-        mma_bf16_16816(sc[1], qa[ks], b2, b3);
+        mma16<F8>(sc[0], qa[ks], b0, b1);
+        mma16<F8>(sc[1], qa[ks], b2, b3);
       }
       // mask + online softmax (rows g and g+8)
       const int base_tok = (p0 + j) * 16;
@@ -251,10 +304,10 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
             p[nt][h] = (mm == kNegInf) ? 0.f : exp2f(sc[nt][h] - mm);
             l_r[h >> 1] += p[nt][h];
           }
-        pa[0] = pack_bf16x2(p[0][0], p[0][1]);
-        pa[1] = pack_bf16x2(p[0][2], p[0][3]);
-        pa[2] = pack_bf16x2(p[1][0], p[1][1]);
-        pa[3] = pack_bf16x2(p[1][2], p[1][3]);
+        pa[0] = pack16<F8>(p[0][0], p[0][1]);
+        pa[1] = pack16<F8>(p[0][2], p[0][3]);
+        pa[2] = pack16<F8>(p[1][0], p[1][1]);
+        pa[3] = pack16<F8>(p[1][2], p[1][3]);
       }
 #pragma unroll
       for (int dn = 0; dn < D / 8; ++dn) {
@@ -269,8 +322,8 @@ __global__ void __launch_bounds__(160) decode_attn_kernel(const __grid_constant_
         const int d0 = (dp * 2 + (mi >> 1)) * 8;
         uint32_t b0, b1, b2, b3;
         ldmatrix_x4_trans(vb + sw128_off(tok, d0, 16), b0, b1, b2, b3);
-        mma_bf16_16816(o[dp * 2], pa, b0, b1);
-        mma_bf16_16816(o[dp * 2 + 1], pa, b2, b3);
+        mma16<F8>(o[dp * 2], pa, b0, b1);
+        mma16<F8>(o[dp * 2 + 1], pa, b2, b3);
       }
       __syncwarp();
       if (!F8 && lane == 0) mbar_arrive(&empty[s]);
