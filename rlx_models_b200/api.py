@@ -278,6 +278,69 @@ def load_codec(model: str, *, device: str | torch.device = "cuda"):
     raise NotImplementedError(f"codec model_type {raw.get('model_type')!r}")
 
 
+class Segmenter:
+    """Segment Anything: an image and point / box prompts (in the image's own
+    pixel coordinates) -> boolean masks at the image's size and IoU scores.
+    ``set_image`` keeps the encoder output for further prompts on the same image."""
+
+    MEAN, STD = (0.485, 0.456, 0.406), (0.229, 0.224, 0.225)
+
+    def __init__(self, model):
+        self.model = model
+        self.size = model.cfg.vision.image_size
+        self._emb = None
+        self._sizes = None
+
+    def preprocess(self, image):
+        """Longest edge to the model's input size (bilinear), ImageNet
+        normalisation, zero padding to a square at the bottom / right."""
+        from PIL import Image
+
+        from .utils.preprocess import load_image, normalize, to_tensor
+        img = load_image(image)
+        w, h = img.size
+        s = self.size / max(h, w)
+        nh, nw = int(h * s + 0.5), int(w * s + 0.5)
+        t = normalize(to_tensor(img.resize((nw, nh), resample=Image.BILINEAR)), self.MEAN, self.STD)
+        t = torch.nn.functional.pad(t, (0, self.size - nw, 0, self.size - nh))
+        return t[None], (h, w), (nh, nw)
+
+    def set_image(self, image) -> None:
+        px, orig, resized = self.preprocess(image)
+        self._emb = self.model.image_embeddings(px)
+        self._sizes = (orig, resized)
+
+    def segment(self, image=None, points=None, labels=None, boxes=None, multimask: bool = True):
+        """points [P, n, 2] (x, y) with labels [P, n] (1 foreground, 0
+        background), and / or boxes [P, 4] (x0, y0, x1, y1) -> (masks [P, k, H, W]
+        bool, iou [P, k]); k = 3 with ``multimask`` else 1."""
+        from .models.sam import upscale_masks
+        if image is not None:
+            self.set_image(image)
+        if self._emb is None:
+            raise ValueError("no image: pass one or call set_image first")
+        (h, w), (nh, nw) = self._sizes
+        scale = torch.tensor([nw / w, nh / h])
+        pts = None if points is None else (torch.as_tensor(points, dtype=torch.float32) * scale)[None]
+        lab = None if labels is None else torch.as_tensor(labels)[None]
+        bx = None if boxes is None else (torch.as_tensor(boxes, dtype=torch.float32).view(-1, 2, 2) * scale).view(1, -1, 4)
+        masks, iou = self.model.segment(points=pts, labels=lab, boxes=bx, image_embeddings=self._emb,
+                                        multimask=multimask)
+        return upscale_masks(masks[0].cpu(), (h, w), (nh, nw), self.size), iou[0].cpu()
+
+
+def load_segmenter(model: str, *, device: str | torch.device = "cuda") -> Segmenter:
+    """SAM checkpoint (transformers' SamModel layout; local dir / offline HF id) -> ``Segmenter``."""
+    import json
+    from .models.sam import SamConfig, SamModel
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local SAM checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        raw = json.load(f)
+    return Segmenter(SamModel(SamConfig.from_dict(raw), WeightMap.from_dir(path), device=device))
+
+
 class Embedder:
     """Sentence embeddings from an encoder checkpoint (BERT family)."""
 
