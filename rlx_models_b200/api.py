@@ -233,7 +233,7 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
 
 def load_transcriber(model: str, *, device: str | torch.device = "cuda", language: str | None = "en",
                      task: str = "transcribe"):
-    """Whisper, Moonshine or Parakeet-CTC checkpoint (local dir / offline HF id)
+    """Whisper, Moonshine, Parakeet-CTC or wav2vec 2.0 CTC checkpoint (local dir / offline HF id)
     -> object with ``transcribe(audio, sample_rate)``."""
     import json
     from .models.whisper import SpeechToText, WhisperConfig, WhisperModel
@@ -250,6 +250,10 @@ def load_transcriber(model: str, *, device: str | torch.device = "cuda", languag
         from .models.moonshine import MoonshineConfig, MoonshineModel, MoonshineTranscriber
         return MoonshineTranscriber(MoonshineModel(MoonshineConfig.from_dict(raw), WeightMap.from_dir(path),
                                                    device=device), tok)
+    if raw.get("model_type") in ("wav2vec2", "wav2vec2-ctc"):
+        from .models.wav2vec2 import Wav2Vec2Config, Wav2Vec2CTC, Wav2Vec2Transcriber
+        return Wav2Vec2Transcriber(Wav2Vec2CTC(Wav2Vec2Config.from_dict(raw), WeightMap.from_dir(path), device=device),
+                                   tok, normalize=raw.get("do_normalize", True))
     if raw.get("model_type") == "parakeet_ctc":
         from .models.parakeet import ParakeetConfig, ParakeetCTC, ParakeetTranscriber
         return ParakeetTranscriber(ParakeetCTC(ParakeetConfig.from_dict(raw), WeightMap.from_dir(path), device=device),

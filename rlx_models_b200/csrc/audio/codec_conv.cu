@@ -1,10 +1,12 @@
-// Channels-last 1-D convolutions of the neural audio codecs (DAC, EnCodec) as
+// Channels-last 1-D convolutions of the neural audio codecs (DAC, EnCodec) and
+// audio front ends (wav2vec 2.0) as
 // GEMMs on the tcgen05 linear, with the elementwise work fused into the operand
 // producers, plus the LSTM cell of EnCodec's recurrent layers.
 //
 // act_im2col: x [B, T, C] bf16 -> cols [B * T_out, Kp] bf16,
 //     cols[(b, t), j * C + c] = act(x[b, idx(t * stride - pad_l + j * dil), c])
 //     act: none | snake(v) = v + sin(alpha[c] v)^2 / (alpha[c] + 1e-9) | elu(v) = v > 0 ? v : exp(v) - 1
+//          | gelu(v) = v / 2 (1 + erf(v / sqrt 2))
 //     idx(s) = s inside [0, T); outside, zero padding (the column is 0) or
 //              reflection (-s on the left, 2 (T - 1) - s on the right)
 //   and zeros in columns [k * C, Kp) (Kp = k * C rounded up to 8, the GEMM's
@@ -42,7 +44,7 @@ namespace codec {
 
 constexpr int kThreads = 256;
 
-enum Act { kNone = 0, kSnake = 1, kElu = 2 };
+enum Act { kNone = 0, kSnake = 1, kElu = 2, kGelu = 3 };
 
 __device__ __forceinline__ float act_f(float v, int act, const float* alpha, int c) {
   if (act == kSnake) {
@@ -51,6 +53,7 @@ __device__ __forceinline__ float act_f(float v, int act, const float* alpha, int
     return v + s * s / (a + 1e-9f);
   }
   if (act == kElu) return v > 0.f ? v : expm1f(v);
+  if (act == kGelu) return 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
   return v;
 }
 

@@ -1305,7 +1305,7 @@ void act_im2col(const Tensor& x, const optional<Tensor>& alpha, Tensor& cols, in
   TORCH_CHECK(x.dim() == 3 && x.is_contiguous() && x.scalar_type() == at::kBFloat16,
               "b200.act_im2col: contiguous bf16 x [B, T, C]");
   const int64_t B = x.size(0), T = x.size(1), C = x.size(2);
-  TORCH_CHECK(k >= 1 && stride >= 1 && dil >= 1 && pad_l >= 0 && pad_r >= 0 && act >= 0 && act <= 2,
+  TORCH_CHECK(k >= 1 && stride >= 1 && dil >= 1 && pad_l >= 0 && pad_r >= 0 && act >= 0 && act <= 3,
               "b200.act_im2col: bad geometry");
   TORCH_CHECK(!reflect || (pad_l < T && pad_r < T), "b200.act_im2col: reflection needs padding < T");
   const int64_t T_out = (T + pad_l + pad_r - dil * (k - 1) - 1) / stride + 1;

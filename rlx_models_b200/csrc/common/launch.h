@@ -196,7 +196,7 @@ void instance_norm_launch(const void* x, const float* gamma, const float* beta, 
                           int64_t T, int64_t active, float eps, bool bf16, cudaStream_t st);
 
 // Channels-last convolutions of the audio codecs (activation-fused im2col, transposed-conv overlap-add) and the
-// LSTM cell: see audio/codec_conv.cu. act: 0 none, 1 snake (alpha [C]), 2 ELU.
+// LSTM cell: see audio/codec_conv.cu. act: 0 none, 1 snake (alpha [C]), 2 ELU, 3 GELU (erf).
 void act_im2col_launch(const void* x, const float* alpha, void* cols, int B, int T, int T_out, int C, int Kp, int k,
                        int stride, int pad_l, int dil, int act, bool reflect, cudaStream_t st);
 void convt_fold_launch(const float* Y, const float* bias, void* y, int B, int T_in, int T_out, int C_out, int stride,

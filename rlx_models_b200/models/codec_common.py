@@ -24,9 +24,10 @@ from ..ops import reference as R
 
 
 def fold_weight_norm(named: dict) -> dict:
-    """fp32 tensors with weight normalisation folded, w = g * v / ||v|| (norm
-    over every axis but the first), from either serialisation: ``X.weight_g`` /
-    ``X.weight_v`` or ``X.parametrizations.weight.original0`` / ``original1``."""
+    """fp32 tensors with weight normalisation folded, w = g * v / ||v|| (the
+    norm over every axis but the one ``g`` keeps: the first, or e.g. the kernel
+    axis of wav2vec2's positional conv), from either serialisation:
+    ``X.weight_g`` / ``X.weight_v`` or ``X.parametrizations.weight.original0`` / ``original1``."""
     raw = {}
     for k, t in named.items():
         n = k.replace("parametrizations.weight.original0", "weight_g").replace(
@@ -37,7 +38,9 @@ def fold_weight_norm(named: dict) -> dict:
         if n.endswith(".weight_g"):
             base = n[:-len(".weight_g")]
             v = raw[base + ".weight_v"]
-            norm = v.reshape(v.shape[0], -1).norm(dim=1).reshape(-1, *([1] * (v.dim() - 1)))
+            keep = [d for d in range(v.dim()) if t.dim() == v.dim() and t.shape[d] != 1] or [0]
+            axes = [d for d in range(v.dim()) if d not in keep]
+            norm = v.pow(2).sum(dim=axes, keepdim=True).sqrt() if axes else v.abs()
             out[base + ".weight"] = t * v / norm
         elif not n.endswith(".weight_v"):
             out[n] = t

@@ -345,7 +345,7 @@ def instance_norm(x: torch.Tensor, gamma: torch.Tensor | None = None, beta: torc
     return y
 
 
-_ACTS = {None: 0, "snake": 1, "elu": 2}
+_ACTS = {None: 0, "snake": 1, "elu": 2, "gelu": 3}
 
 
 def act_im2col(x: torch.Tensor, k: int, *, stride: int = 1, pad: int = 0, pad_right: int | None = None,
@@ -355,7 +355,7 @@ def act_im2col(x: torch.Tensor, k: int, *, stride: int = 1, pad: int = 0, pad_ri
     bf16 -> [B * T_out, round_up(k * C, 8)] bf16, column ``j * C + c`` of row
     ``(b, t)`` = act(x[b, t * stride - pad + j * dil, c]); positions outside the
     signal read zero, or the reflected sample when ``reflect``. ``act``: None,
-    "snake" (``alpha`` fp32 [C]) or "elu"; padding columns are zero."""
+    "snake" (``alpha`` fp32 [C]), "elu" or "gelu" (erf); padding columns are zero."""
     B, T, C = x.shape
     pr = pad if pad_right is None else pad_right
     T_out = (T + pad + pr - dil * (k - 1) - 1) // stride + 1

@@ -101,13 +101,14 @@ def snake(x: torch.Tensor, alpha: torch.Tensor) -> torch.Tensor:
 def act_im2col(x: torch.Tensor, k: int, stride: int = 1, pad: int = 0, pad_right: int | None = None, dil: int = 1,
                act: str | None = None, alpha=None, reflect: bool = False) -> torch.Tensor:
     """fp32 channels-last im2col of x [B, T, C] with the activation applied
-    first (None, "snake" with ``alpha``, "elu"): [B * T_out, round_up(k * C, 8)],
+    first (None, "snake" with ``alpha``, "elu", "gelu"): [B * T_out, round_up(k * C, 8)],
     column j * C + c of row (b, t) = act(x)[b, t * stride - pad + j * dil, c];
     outside the signal zero, or the reflected sample when ``reflect``; zero
     padding columns."""
     B, T, C = x.shape
     pr = pad if pad_right is None else pad_right
-    xs = snake(x, alpha) if act == "snake" else (torch.nn.functional.elu(x.float()) if act == "elu" else x.float())
+    acts = {"snake": lambda t: snake(t, alpha), "elu": torch.nn.functional.elu, "gelu": torch.nn.functional.gelu}
+    xs = acts[act](x.float()) if act is not None else x.float()
     if reflect:
         xp = torch.nn.functional.pad(xs.transpose(1, 2), (pad, pr), mode="reflect").transpose(1, 2)
     else:

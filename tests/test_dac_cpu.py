@@ -30,14 +30,14 @@ def _hf(w, weight_norm=False):
 
 @pytest.mark.parametrize("k,s,p,pr,d", [(7, 1, 3, 3, 1), (7, 1, 9, 9, 3), (4, 2, 1, 1, 1), (10, 5, 3, 3, 1),
                                         (3, 1, 1, 1, 1), (7, 1, 6, 0, 1), (4, 2, 2, 3, 1)])
-@pytest.mark.parametrize("act", [None, "snake", "elu"])
+@pytest.mark.parametrize("act", [None, "snake", "elu", "gelu"])
 @pytest.mark.parametrize("reflect", [False, True])
 def test_act_im2col_is_conv1d(k, s, p, pr, d, act, reflect):
     torch.manual_seed(0)
     B, T, C, O = 2, 37, 5, 6
     x, a = torch.randn(B, T, C), torch.rand(C) + 0.5
     W, b = torch.randn(O, C, k), torch.randn(O)
-    xa = R.snake(x, a) if act == "snake" else (F.elu(x) if act == "elu" else x)
+    xa = {"snake": lambda t: R.snake(t, a), "elu": F.elu, "gelu": F.gelu, None: lambda t: t}[act](x)
     xp = F.pad(xa.transpose(1, 2), (p, pr), mode="reflect" if reflect else "constant")
     ref = F.conv1d(xp, W, b, stride=s, dilation=d).transpose(1, 2)
     cols = R.act_im2col(x, k, s, p, pr, d, act, a, reflect)

@@ -16,7 +16,7 @@ pytestmark = pytest.mark.gpu
 @pytest.mark.parametrize("C,k,s,p,pr,d", [(16, 7, 1, 3, 3, 1), (16, 7, 1, 27, 27, 9), (32, 4, 2, 1, 1, 1),
                                            (24, 10, 5, 3, 3, 1), (1, 7, 1, 3, 3, 1), (3, 3, 1, 1, 1, 1),
                                            (64, 1, 1, 0, 0, 1), (16, 7, 1, 6, 0, 1), (8, 16, 8, 4, 5, 1)])
-@pytest.mark.parametrize("act", [None, "snake", "elu"])
+@pytest.mark.parametrize("act", [None, "snake", "elu", "gelu"])
 @pytest.mark.parametrize("reflect", [False, True])
 def test_act_im2col(C, k, s, p, pr, d, act, reflect):
     from rlx_models_b200 import ops
