@@ -345,6 +345,44 @@ def load_segmenter(model: str, *, device: str | torch.device = "cuda") -> Segmen
     return Segmenter(SamModel(SamConfig.from_dict(raw), WeightMap.from_dir(path), device=device))
 
 
+class Translator:
+    """Many-to-many translation (NLLB-200 / M2M-100): ``translate(texts,
+    src_lang, tgt_lang)`` with the checkpoint's tokenizer (language codes as
+    the tokenizer names them, e.g. "eng_Latn" / "fra_Latn" for NLLB)."""
+
+    def __init__(self, model, tokenizer=None):
+        self.model, self.tokenizer = model, tokenizer
+
+    def translate(self, texts, src_lang: str, tgt_lang: str, max_new_tokens: int = 128) -> list:
+        if self.tokenizer is None:
+            raise ValueError("no tokenizer next to the checkpoint; use model.generate on token ids")
+        single = isinstance(texts, str)
+        texts = [texts] if single else list(texts)
+        self.tokenizer.src_lang = src_lang
+        enc = self.tokenizer(texts, return_tensors="pt", padding=True)
+        ids = self.model.generate(enc["input_ids"], forced_bos=self.tokenizer.convert_tokens_to_ids(tgt_lang),
+                                  max_new_tokens=max_new_tokens)
+        out = [self.tokenizer.decode(x, skip_special_tokens=True) for x in ids]
+        return out[0] if single else out
+
+
+def load_translator(model: str, *, device: str | torch.device = "cuda") -> Translator:
+    """NLLB / M2M-100 checkpoint (local dir / offline HF id) -> ``Translator``."""
+    import json
+    from .models.nllb import NllbConfig, NllbTranslator
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local translation checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        raw = json.load(f)
+    tok = None
+    if any(os.path.exists(os.path.join(path, f)) for f in ("tokenizer.json", "sentencepiece.bpe.model",
+                                                            "tokenizer_config.json")):
+        from transformers import AutoTokenizer
+        tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+    return Translator(NllbTranslator(NllbConfig.from_dict(raw), WeightMap.from_dir(path), device=device), tok)
+
+
 class Embedder:
     """Sentence embeddings from an encoder checkpoint (BERT family)."""
 
