@@ -266,7 +266,8 @@ def load_codec(model: str, *, device: str | torch.device = "cuda"):
     """Neural audio codec checkpoint (local dir / offline HF id): DAC (transformers'
     or the original Descript layout; ``encode(pcm) -> codes``, ``decode(codes)
     -> pcm``, ``roundtrip``) or EnCodec (``encode(pcm, bandwidth) -> (codes,
-    scales, pad)``, ``decode(codes, scales, pad)``, the transformers layout)."""
+    scales, pad)``, ``decode(codes, scales, pad)``, the transformers layout) or Mimi
+    (``encode(pcm, num_quantizers) -> codes``, ``decode(codes)``)."""
     import json
     path = resolve_model_path(model)
     if path is None:
@@ -276,6 +277,9 @@ def load_codec(model: str, *, device: str | torch.device = "cuda"):
     if raw.get("model_type", "dac") == "dac":
         from .models.dac import DacConfig, DacModel
         return DacModel(DacConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
+    if raw.get("model_type") == "mimi":
+        from .models.mimi import MimiConfig, MimiModel
+        return MimiModel(MimiConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
     if raw.get("model_type") == "encodec":
         from .models.encodec import EncodecConfig, EncodecModel
         return EncodecModel(EncodecConfig.from_dict(raw), WeightMap.from_dir(path), device=device)

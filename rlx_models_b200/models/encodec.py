@@ -112,18 +112,22 @@ class _Layer:
     res_dil: int = 1
 
 
-def _layout(cfg: EncodecConfig) -> tuple[list[_Layer], list[_Layer]]:
-    """The transformers module lists (``encoder.layers.N`` / ``decoder.layers.N``)."""
+def _layout(cfg: EncodecConfig, lstm: bool = True) -> tuple[list[_Layer], list[_Layer]]:
+    """The transformers module lists (``encoder.layers.N`` / ``decoder.layers.N``);
+    ``lstm=False``: the SEANet stacks without their LSTMs (Mimi)."""
     enc = [_Layer("conv", "encoder.layers.0", k=cfg.kernel_size)]
     for r in reversed(cfg.upsampling_ratios):
         for j in range(cfg.num_residual_layers):
             enc.append(_Layer("res", f"encoder.layers.{len(enc)}", res_dil=cfg.dilation_growth_rate ** j))
         enc.append(_Layer("elu", f"encoder.layers.{len(enc)}"))
         enc.append(_Layer("conv", f"encoder.layers.{len(enc)}", k=2 * r, stride=r))
-    enc.append(_Layer("lstm", f"encoder.layers.{len(enc)}"))
+    if lstm:
+        enc.append(_Layer("lstm", f"encoder.layers.{len(enc)}"))
     enc.append(_Layer("elu", f"encoder.layers.{len(enc)}"))
     enc.append(_Layer("conv", f"encoder.layers.{len(enc)}", k=cfg.last_kernel_size))
-    dec = [_Layer("conv", "decoder.layers.0", k=cfg.kernel_size), _Layer("lstm", "decoder.layers.1")]
+    dec = [_Layer("conv", "decoder.layers.0", k=cfg.kernel_size)]
+    if lstm:
+        dec.append(_Layer("lstm", "decoder.layers.1"))
     for r in cfg.upsampling_ratios:
         dec.append(_Layer("elu", f"decoder.layers.{len(dec)}"))
         dec.append(_Layer("convt", f"decoder.layers.{len(dec)}", k=2 * r, stride=r))
@@ -135,16 +139,20 @@ def _layout(cfg: EncodecConfig) -> tuple[list[_Layer], list[_Layer]]:
 
 
 class EncodecModel:
-    def __init__(self, cfg: EncodecConfig, weights, device="cpu"):
+    """``seanet_only``: load just the SEANet convolution stacks (no LSTM, no
+    quantiser) for codecs built around them (Mimi)."""
+
+    def __init__(self, cfg: EncodecConfig, weights, device="cpu", seanet_only: bool = False):
         self.cfg = cfg
         self.run = ConvRunner(device)
         self.device, self.dtype = self.run.device, self.run.dtype
         get = (lambda k: weights.take(k)) if hasattr(weights, "take") else (lambda k: weights[k])
-        w = fold_weight_norm({k: get(k) for k in weights.keys()})
+        keys = [k for k in weights.keys() if not seanet_only or k.startswith(("encoder.layers.", "decoder.layers."))]
+        w = fold_weight_norm({k: get(k) for k in keys})
         dt, dev = self.dtype, self.device
         self.convs: dict[str, GemmConv] = {}
         self.norms: dict[str, tuple] = {}
-        self.enc, self.dec = _layout(cfg)
+        self.enc, self.dec = _layout(cfg, lstm=not seanet_only)
         transposed = {L.name for L in self.dec if L.kind == "convt"}
         for n, t in w.items():
             if n.endswith(".conv.weight"):
@@ -160,6 +168,8 @@ class EncodecModel:
                      w[f"{L.name}.lstm.weight_hh_l{i}"].to(dev, dt).contiguous(),
                      (w[f"{L.name}.lstm.bias_ih_l{i}"] + w[f"{L.name}.lstm.bias_hh_l{i}"]).to(dev).contiguous())
                     for i in range(cfg.num_lstm_layers)]
+        if seanet_only:
+            return
         self.books = [w[f"quantizer.layers.{i}.codebook.embed"].to(dev).contiguous()
                       for i in range(cfg.num_quantizers)]
         self.book_sq = [b.pow(2).sum(1) for b in self.books]
