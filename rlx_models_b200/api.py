@@ -387,6 +387,19 @@ def load_translator(model: str, *, device: str | torch.device = "cuda") -> Trans
     return Translator(NllbTranslator(NllbConfig.from_dict(raw), WeightMap.from_dir(path), device=device), tok)
 
 
+def load_forecaster(model: str, *, device: str | torch.device = "cuda"):
+    """TimesFM checkpoint (transformers' TimesFmModelForPrediction layout; local
+    dir / offline HF id) -> model with ``forecast(series, freq, horizon, ...)``."""
+    import json
+    from .models.timesfm import TimesFm, TimesFmConfig
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local forecasting checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        raw = json.load(f)
+    return TimesFm(TimesFmConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
+
+
 class Embedder:
     """Sentence embeddings from an encoder checkpoint (BERT family)."""
 
