@@ -400,6 +400,38 @@ def load_forecaster(model: str, *, device: str | torch.device = "cuda"):
     return TimesFm(TimesFmConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
 
 
+class SpeechGenerator:
+    """Text to speech with CSM: ``speak(text, speaker=0)`` formats the prompt
+    as the checkpoint's processor does ("[speaker]text"), generates Mimi frames
+    greedily and decodes them to 24 kHz audio."""
+
+    def __init__(self, model, tokenizer=None):
+        self.model, self.tokenizer = model, tokenizer
+
+    def speak(self, text: str, speaker: int = 0, max_frames: int = 125) -> torch.Tensor:
+        if self.tokenizer is None:
+            raise ValueError("no tokenizer next to the checkpoint; use model.speak on token ids")
+        ids = self.tokenizer(f"[{speaker}]{text}", return_tensors="pt")["input_ids"][0]
+        return self.model.speak(ids, max_frames=max_frames)
+
+
+def load_speech_generator(model: str, *, device: str | torch.device = "cuda") -> SpeechGenerator:
+    """CSM checkpoint (transformers' CsmForConditionalGeneration layout, Mimi codec
+    included; local dir / offline HF id) -> ``SpeechGenerator``."""
+    import json
+    from .models.csm import CsmConfig, CsmModel
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local speech-generation checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        raw = json.load(f)
+    tok = None
+    if any(os.path.exists(os.path.join(path, f)) for f in ("tokenizer.json", "tokenizer_config.json")):
+        from transformers import AutoTokenizer
+        tok = AutoTokenizer.from_pretrained(path, local_files_only=True)
+    return SpeechGenerator(CsmModel(CsmConfig.from_dict(raw), WeightMap.from_dir(path), device=device), tok)
+
+
 class Embedder:
     """Sentence embeddings from an encoder checkpoint (BERT family)."""
 
