@@ -696,6 +696,61 @@ class VLM:
         return self.engine.generate([list(p) for p in prompts], params, mm)
 
 
+class AudioLLM:
+    """An audio LLM (Voxtral: ``models/voxtral.py``) plus its serving engine:
+    prompts are token ids with one audio placeholder per audio token; each
+    prompt's audio (16 kHz PCM, or log-mel windows [n, n_mels, frames]) fills
+    its placeholders in order."""
+
+    def __init__(self, model, engine_config: EngineConfig | None = None, tokenizer=None):
+        import dataclasses
+        self.model = model
+        ec = dataclasses.replace(engine_config or EngineConfig(), prefix_caching=False)
+        self.engine = LLMEngine(model.lm, ec)
+        self.tokenizer = tokenizer
+
+    def features(self, audio) -> torch.Tensor:
+        """16 kHz PCM -> log-mel windows of 30 s [n, n_mels, 3000]."""
+        from .models.whisper import CHUNK_SECONDS, SAMPLE_RATE, log_mel
+        a = torch.as_tensor(audio, dtype=torch.float32).flatten()
+        n = SAMPLE_RATE * CHUNK_SECONDS
+        wins = [a[i:i + n] for i in range(0, max(1, a.numel()), n)]
+        return torch.stack([log_mel(w, self.model.cfg.audio.num_mel_bins) for w in wins])
+
+    def generate(self, prompts: list[list[int]], audio: list, params: SamplingParams | None = None
+                 ) -> list[RequestOutput]:
+        mm = []
+        for ids, a in zip(prompts, audio):
+            if a is None:
+                mm.append(None)
+                continue
+            mel = a if torch.is_tensor(a) and a.dim() == 3 else self.features(a)
+            mm.append(self.model.mm_segments(list(ids), mel))
+        return self.engine.generate([list(p) for p in prompts], params, mm)
+
+
+def load_audio_llm(model: str, *, device: str | torch.device = "cuda",
+                   engine_config: EngineConfig | None = None) -> AudioLLM:
+    """Voxtral checkpoint (local dir / offline HF id) -> ``AudioLLM``."""
+    import json
+    from .models.voxtral import VoxtralConfig, VoxtralModel
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        raw = json.load(f)
+    if raw.get("model_type") != "voxtral":
+        raise NotImplementedError(f"audio LLM model_type {raw.get('model_type')!r}")
+    m = VoxtralModel(VoxtralConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
+    tok = None
+    try:
+        from .tokenizer import load_tokenizer
+        tok = load_tokenizer(path)
+    except Exception:
+        pass
+    return AudioLLM(m, engine_config, tok)
+
+
 def load_vlm(model: str, *, device: str | torch.device = "cuda", engine_config: EngineConfig | None = None) -> VLM:
     """LLaVA-form vision-language checkpoint (local dir / offline HF id) -> ``VLM``."""
     import json

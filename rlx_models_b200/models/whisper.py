@@ -119,7 +119,10 @@ def sinusoids(length: int, channels: int, max_timescale: float = 10000.0) -> tor
 # ---------------------------------------------------------------------------
 
 class WhisperModel:
-    def __init__(self, cfg: WhisperConfig, weights, device="cpu", dtype: torch.dtype | None = None):
+    """``encoder_only``: load just the audio encoder (audio LLMs that reuse it)."""
+
+    def __init__(self, cfg: WhisperConfig, weights, device="cpu", dtype: torch.dtype | None = None,
+                 encoder_only: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype or (torch.bfloat16 if self.device.type == "cuda" else torch.float32)
@@ -149,6 +152,8 @@ class WhisperModel:
                          ln2=ln(e + f"layers.{i}.final_layer_norm"), **mlp(e + f"layers.{i}."))
                     for i in range(cfg.encoder_layers)]
         self.enc_ln = ln(e + "layer_norm")
+        if encoder_only:
+            return
         self.tok = dv(get(d + "embed_tokens.weight"))
         self.dec_pos = dv(get(d + "embed_positions.weight"))
         self.dec = [dict(ln1=ln(d + f"layers.{i}.self_attn_layer_norm"), att=attn(d + f"layers.{i}.self_attn."),
