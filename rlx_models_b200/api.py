@@ -432,6 +432,20 @@ def load_speech_generator(model: str, *, device: str | torch.device = "cuda") ->
     return SpeechGenerator(CsmModel(CsmConfig.from_dict(raw), WeightMap.from_dir(path), device=device), tok)
 
 
+def load_video_model(model: str, *, device: str | torch.device = "cuda"):
+    """V-JEPA 2 checkpoint (encoder alone or with the attentive-probe classifier;
+    local dir / offline HF id) -> model with ``features(video)`` and, for
+    classifiers, ``classify(video)`` (video [B, T, 3, H, W], preprocessed)."""
+    import json
+    from .models.vjepa2 import VJEPA2, VJEPA2Config
+    path = resolve_model_path(model)
+    if path is None:
+        raise FileNotFoundError(f"no local video checkpoint for {model!r}")
+    with open(os.path.join(path, "config.json")) as f:
+        raw = json.load(f)
+    return VJEPA2(VJEPA2Config.from_dict(raw), WeightMap.from_dir(path), device=device)
+
+
 class Embedder:
     """Sentence embeddings from an encoder checkpoint (BERT family)."""
 
