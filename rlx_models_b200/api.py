@@ -609,6 +609,8 @@ class ImageEmbedder:
         """Paths, PIL images or HWC uint8 arrays -> [N, D] fp32 embeddings."""
         if not isinstance(images, (list, tuple)):
             images = [images]
+        if hasattr(self.encoder, "embed_images"):  # SigLIP 2: NaFlex patches at each image's aspect ratio
+            return self.encoder.embed_images(list(images), normalize=normalize)
         return self.encoder.embed(self.pixels(images), normalize=normalize)
 
 
@@ -625,6 +627,9 @@ def load_image_embedder(model: str, *, device: str | torch.device = "cuda") -> I
         raw = json.load(f)
     if raw.get("model_type") in ("dinov2", "dinov2_with_registers"):
         return ImageEmbedder(Dinov2Encoder(Dinov2Config.from_dict(raw), WeightMap.from_dir(path), device=device))
+    if raw.get("model_type") in ("siglip2", "siglip2_vision_model"):
+        from .models.vit import Siglip2Encoder
+        return ImageEmbedder(Siglip2Encoder(VisionConfig.from_dict(raw), WeightMap.from_dir(path), device=device))
     if raw.get("model_type") == "dinov3_vit":
         return ImageEmbedder(Dinov3Encoder(Dinov3Config.from_dict(raw), WeightMap.from_dir(path), device=device))
     cfg = VisionConfig.from_dict(raw)

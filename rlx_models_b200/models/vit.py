@@ -419,3 +419,107 @@ class Dinov3Encoder:
         _, pooled = self(pixels)
         e = pooled.float()
         return F.normalize(e, dim=-1) if normalize else e
+
+
+# ---------------------------------------------------------------------------
+# SigLIP 2 (NaFlex: native aspect ratio, variable patch count)
+# ---------------------------------------------------------------------------
+
+def naflex_size(height: int, width: int, patch: int, max_patches: int) -> tuple[int, int]:
+    """Largest resize of (height, width), each side a multiple of the patch,
+    with at most ``max_patches`` patches (the scale found by bisection, as the
+    SigLIP 2 processor does)."""
+    def side(scale, n):
+        return max(patch, int(math.ceil(n * scale / patch) * patch))
+    lo, hi = 1e-6, 100.0
+    while hi - lo >= 1e-5:
+        s = (lo + hi) / 2
+        if (side(s, height) / patch) * (side(s, width) / patch) <= max_patches:
+            lo = s
+        else:
+            hi = s
+    return side(lo, height), side(lo, width)
+
+
+class Siglip2Encoder(VisionEncoder):
+    """SigLIP 2 vision tower over NaFlex inputs: patches [B, L, p * p * C]
+    (row-major patches, channel-last inside each), their grid shapes [B, 2] and
+    a validity mask [B, L]. The learned square position table is resized
+    (bilinear, antialiased) to each image's grid; padded patches are masked as
+    keys in every block and in the attention-pooling head.
+
+    Reference: crates/rlx-siglip2 (SigLIP 2 image tower); transformers'
+    Siglip2VisionModel is the CPU oracle."""
+
+    def _positions(self, shapes: torch.Tensor, L: int) -> torch.Tensor:
+        n = self.pos.shape[0]
+        side = int(round(math.sqrt(n)))
+        table = self.pos.float().reshape(side, side, -1).permute(2, 0, 1)[None]
+        out = torch.empty(len(shapes), L, table.shape[1], device=self.device)
+        for i, (h, w) in enumerate(shapes.tolist()):
+            r = F.interpolate(table, size=(h, w), mode="bilinear", align_corners=False, antialias=True)
+            r = r.reshape(table.shape[1], h * w).t()
+            out[i, :h * w] = r
+            out[i, h * w:] = r[0]
+        return out
+
+    def _attend_masked(self, q, k, v, nh, mask):
+        B, Lq, H = q.shape
+        D = H // nh
+        q, k, v = (t.reshape(B, -1, nh, D).transpose(1, 2) for t in (q, k, v))
+        return F.scaled_dot_product_attention(q, k, v, attn_mask=mask).transpose(1, 2).reshape(B, Lq, H)
+
+    @torch.no_grad()
+    def forward_patches(self, patches: torch.Tensor, shapes: torch.Tensor, valid: torch.Tensor):
+        """-> (last hidden [B, L, H] after the post-norm, pooled [B, H] or None)."""
+        c = self.cfg
+        H, nh = c.hidden_size, c.num_attention_heads
+        B, L, K = patches.shape
+        rows = patches.to(self.device, self.dtype).reshape(B * L, K)
+        if rows.shape[1] != self.w_patch.shape[1]:
+            rows = F.pad(rows, (0, self.w_patch.shape[1] - rows.shape[1]))
+        x = _linear(rows.contiguous(), self.w_patch, self.b_patch).view(B, L, H)
+        x = (x.float() + self._positions(shapes, L)).to(self.dtype)
+        valid = valid.to(self.device).bool()
+        mask = valid[:, None, None, :]
+        for ly in self.layers:
+            q, k, v = _linear(self._ln(x, ly["ln1"]), ly["qkv"], ly["qkv_b"]).split(H, -1)
+            x = x + _linear(self._attend_masked(q, k, v, nh, mask), *ly["o"])
+            x = x + _linear(self._act(_linear(self._ln(x, ly["ln2"]), *ly["fc1"])).to(x.dtype), *ly["fc2"])
+        x = self._ln(x, self.post_ln)
+        if self.head is None:
+            return x, None
+        hd = self.head
+        wq, wk, wv = hd["in_w"].split(H, 0)
+        bq, bk, bv = hd["in_b"].split(H, 0)
+        probe = hd["probe"].expand(B, 1, H)
+        h = _linear(self._attend_masked(_linear(probe, wq, bq), _linear(x, wk, bk), _linear(x, wv, bv), nh, mask),
+                    *hd["o"])
+        h = h + _linear(self._act(_linear(self._ln(h, hd["ln"]), *hd["fc1"])).to(h.dtype), *hd["fc2"])
+        return x, h[:, 0]
+
+    def patchify(self, images, max_patches: int = 256, mean=(0.5, 0.5, 0.5), std=(0.5, 0.5, 0.5)):
+        """Images -> (patches [B, max_patches, p * p * 3], shapes [B, 2], valid [B, max_patches]):
+        NaFlex resize (bilinear), rescale to [0, 1], normalise, row-major patches."""
+        from PIL import Image
+
+        from ..utils.preprocess import load_image, normalize, to_tensor
+        p = self.cfg.patch_size
+        out, shapes, valid = [], [], []
+        for im in images:
+            im = load_image(im)
+            w0, h0 = im.size
+            th, tw = naflex_size(h0, w0, p, max_patches)
+            t = normalize(to_tensor(im.resize((tw, th), resample=Image.BILINEAR)), mean, std)    # [3, th, tw]
+            gh, gw = th // p, tw // p
+            rows = t.view(3, gh, p, gw, p).permute(1, 3, 2, 4, 0).reshape(gh * gw, p * p * 3)
+            out.append(F.pad(rows, (0, 0, 0, max_patches - rows.shape[0])))
+            shapes.append((gh, gw))
+            valid.append(torch.arange(max_patches) < gh * gw)
+        return torch.stack(out), torch.tensor(shapes), torch.stack(valid)
+
+    def embed_images(self, images, max_patches: int = 256, normalize: bool = True) -> torch.Tensor:
+        patches, shapes, valid = self.patchify(images, max_patches)
+        _, pooled = self.forward_patches(patches, shapes, valid)
+        e = pooled.float()
+        return F.normalize(e, dim=-1) if normalize else e
