@@ -710,6 +710,9 @@ class VLM:
             if ims is None or len(ims) == 0:
                 mm.append(None)
                 continue
+            if hasattr(self.vlm, "segments_for_images"):  # NaFlex towers take the images themselves
+                mm.append(self.vlm.segments_for_images(list(ids), ims))
+                continue
             px = ims if torch.is_tensor(ims) else self.pixels(ims)
             mm.append(self.vlm.mm_segments(list(ids), px))
         return self.engine.generate([list(p) for p in prompts], params, mm)
@@ -771,7 +774,7 @@ def load_audio_llm(model: str, *, device: str | torch.device = "cuda",
 
 
 def load_vlm(model: str, *, device: str | torch.device = "cuda", engine_config: EngineConfig | None = None) -> VLM:
-    """LLaVA-form vision-language checkpoint (local dir / offline HF id) -> ``VLM``."""
+    """LLaVA-form or LFM2-VL vision-language checkpoint (local dir / offline HF id) -> ``VLM``."""
     import json
     from .models.llava import LlavaConfig, LlavaVLM
     path = resolve_model_path(model)
@@ -779,9 +782,13 @@ def load_vlm(model: str, *, device: str | torch.device = "cuda", engine_config: 
         raise FileNotFoundError(f"no local checkpoint for {model!r}")
     with open(os.path.join(path, "config.json")) as f:
         raw = json.load(f)
-    if raw.get("model_type") not in ("llava",):
+    if raw.get("model_type") == "lfm2_vl":
+        from .models.lfm2_vl import Lfm2VlConfig, Lfm2VlModel
+        vlm = Lfm2VlModel(Lfm2VlConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
+    elif raw.get("model_type") == "llava":
+        vlm = LlavaVLM(LlavaConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
+    else:
         raise NotImplementedError(f"vision-language model_type {raw.get('model_type')!r}")
-    vlm = LlavaVLM(LlavaConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
     tok = None
     try:
         from .tokenizer import load_tokenizer

@@ -182,13 +182,17 @@ class Lfm2Oracle:
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + self.cfg.norm_eps) * self._t(n)
 
     @torch.no_grad()
-    def logits(self, ids) -> torch.Tensor:
+    def logits(self, ids, mm=None) -> torch.Tensor:
+        """``mm`` = (rows, embeds): input embeddings replaced at those rows
+        (image tokens of a vision-language prompt)."""
         from ..ops import reference as R
         c = self.cfg
         ids = torch.as_tensor(ids, device=self.device).long()
         S = ids.shape[0]
         pos = torch.arange(S, device=self.device)
         h = self._t("model.embed_tokens.weight")[ids]
+        if mm is not None:
+            h = h.index_copy(0, mm[0].to(self.device).long(), mm[1].to(self.device, torch.float32))
         nh, nkv, D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
         for i in range(c.num_hidden_layers):
             p = f"model.layers.{i}."
@@ -362,6 +366,8 @@ class Lfm2LM:
             nseq = fb.num_decode + (0 if fb.pre_ctx_lens is None else fb.pre_ctx_lens.shape[0])
             slots = torch.arange(nseq, dtype=torch.int32, device=self.device)
         h = ops.embedding(fb.input_ids, self.embed)
+        if getattr(fb, "mm_rows", None) is not None:  # image tokens of a vision-language prompt
+            h.index_copy_(0, fb.mm_rows, fb.mm_embeds.to(h.dtype))
         x = ops.rmsnorm(h, self.layers[0].ln1, c.norm_eps)
         n = len(self.layers)
         for i, L in enumerate(self.layers):
