@@ -202,8 +202,11 @@ def load(model: str, *, device: str | torch.device = "cuda", tp_rank: int = 0, t
         else:
             from .models.lfm2 import Lfm2Config, is_lfm2_config
             from .models.mamba2 import SSMConfig, is_ssm_config
+            from .models.minimax import MiniMaxConfig, is_minimax_config
             if config is None and is_lfm2_config(path):  # short-conv hybrid
                 config = Lfm2Config.from_file(path)
+            elif config is None and is_minimax_config(path):  # lightning-attention hybrid
+                config = MiniMaxConfig.from_file(path)
             elif config is None and is_ssm_config(path):  # Mamba-2 (SSD) and its attention hybrids
                 config = SSMConfig.from_file(path)
             else:

@@ -94,6 +94,14 @@ def _mamba1(cfg, weights, device, tp_rank, tp_size, comm):
     return Mamba1LM(cfg, weights, device=device)
 
 
+@register("minimax")
+def _minimax(cfg, weights, device, tp_rank, tp_size, comm):
+    from .models.minimax import MiniMaxLM
+    if tp_size != 1:
+        raise NotImplementedError("MiniMax-Text-01 runs on one GPU per replica")
+    return MiniMaxLM(cfg, weights, device=device)
+
+
 @register("lfm2")
 def _lfm2(cfg, weights, device, tp_rank, tp_size, comm):
     from .models.lfm2 import Lfm2LM
@@ -121,6 +129,9 @@ def build_model(cfg: DecoderConfig, weights=None, *, device="cuda", tp_rank=0, t
         weights = random_weights(cfg, seed, device)
     elif weights is None and cfg.model_type == "lfm2":
         from .models.lfm2 import random_weights
+        weights = random_weights(cfg, seed, device)
+    elif weights is None and cfg.model_type == "minimax":
+        from .models.minimax import random_weights
         weights = random_weights(cfg, seed, device)
     elif weights is None:
         weights = RandomWeights(cfg, seed, device)
