@@ -99,9 +99,11 @@ void linear(const Tensor& x, const Tensor& w, Tensor& out, int64_t mode, const o
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void gdn_decode(const Tensor& proj, const Tensor& conv_w, const Tensor& A_log, const Tensor& dt_bias,
-                const Tensor& norm_w, Tensor& conv_state, Tensor& rec_state, const Tensor& seq_slots,
-                const Tensor& positions, Tensor& out, int64_t Hk, int64_t Hv, int64_t D, double eps) {
+static void gdn_decode_impl(const Tensor& proj, const Tensor& conv_w, const Tensor& A_log, const Tensor& dt_bias,
+                            const Tensor& norm_w, Tensor& conv_state, Tensor& rec_state, const Tensor& seq_slots,
+                            const Tensor& positions, Tensor& out, int64_t Hk, int64_t Hv, int64_t D, double eps,
+                            bool kda) {
+  const int64_t n_gate = kda ? Hv * D : Hv;  // decay logits per head (GDN) or per key channel (KDA)
   check_cuda(proj, "proj");
   const int64_t B = proj.size(0);
   TORCH_CHECK(proj.scalar_type() == at::kBFloat16 && proj.dim() == 2 && proj.stride(1) == 1, "b200.gdn_decode: proj");
@@ -109,9 +111,10 @@ void gdn_decode(const Tensor& proj, const Tensor& conv_w, const Tensor& A_log, c
   const int64_t conv_dim = conv_w.size(0), K = conv_w.size(1);
   const int64_t key_dim = Hk * D, value_dim = Hv * D;
   TORCH_CHECK(conv_dim == 2 * key_dim + value_dim, "b200.gdn_decode: conv_dim != 2 key_dim + value_dim");
-  TORCH_CHECK(proj.size(1) >= conv_dim + value_dim + 2 * Hv, "b200.gdn_decode: proj width");
+  TORCH_CHECK(!kda || Hk == Hv, "b200.kda_decode: key heads == value heads");
+  TORCH_CHECK(proj.size(1) >= conv_dim + value_dim + Hv + n_gate, "b200.gdn_decode: proj width");
   TORCH_CHECK(A_log.scalar_type() == at::kFloat && A_log.numel() == Hv && dt_bias.scalar_type() == at::kFloat &&
-                  dt_bias.numel() == Hv && norm_w.scalar_type() == at::kFloat && norm_w.numel() == D,
+                  dt_bias.numel() == n_gate && norm_w.scalar_type() == at::kFloat && norm_w.numel() == D,
               "b200.gdn_decode: A_log / dt_bias / norm_w fp32");
   TORCH_CHECK(conv_state.scalar_type() == at::kBFloat16 && conv_state.is_contiguous() && conv_state.dim() == 4 &&
                   conv_state.size(1) == 2 && conv_state.size(2) == conv_dim && conv_state.size(3) == K - 1,
@@ -148,8 +151,24 @@ void gdn_decode(const Tensor& proj, const Tensor& conv_w, const Tensor& A_log, c
   a.value_dim = (int)value_dim;
   a.num_slots = conv_state.size(0);
   a.eps = (float)eps;
+  a.kda = kda ? 1 : 0;
   b200::gdn_decode_launch(a, cur_stream(proj));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gdn_decode(const Tensor& proj, const Tensor& conv_w, const Tensor& A_log, const Tensor& dt_bias,
+                const Tensor& norm_w, Tensor& conv_state, Tensor& rec_state, const Tensor& seq_slots,
+                const Tensor& positions, Tensor& out, int64_t Hk, int64_t Hv, int64_t D, double eps) {
+  gdn_decode_impl(proj, conv_w, A_log, dt_bias, norm_w, conv_state, rec_state, seq_slots, positions, out, Hk, Hv, D,
+                  eps, false);
+}
+
+// Kimi Delta Attention decode step: proj rows [q k v (3 Hv D) | z (Hv D) | b (Hv) | a (Hv D)], dt_bias [Hv D].
+void kda_decode(const Tensor& proj, const Tensor& conv_w, const Tensor& A_log, const Tensor& dt_bias,
+                const Tensor& norm_w, Tensor& conv_state, Tensor& rec_state, const Tensor& seq_slots,
+                const Tensor& positions, Tensor& out, int64_t H, int64_t D, double eps) {
+  gdn_decode_impl(proj, conv_w, A_log, dt_bias, norm_w, conv_state, rec_state, seq_slots, positions, out, H, H, D,
+                  eps, true);
 }
 
 void shortconv_decode(const Tensor& proj, const Tensor& w, const optional<Tensor>& bias, Tensor& conv_state,
@@ -1578,6 +1597,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gate_r2") = 1, py::arg("gate_off") = 0, py::arg("glu_act") = 0);
   m.def("gemm", &gemm);
   m.def("gdn_decode", &gdn_decode);
+  m.def("kda_decode", &kda_decode);
   m.def("shortconv_decode", &shortconv_decode);
   m.def("ssd_decode", &ssd_decode);
   m.def("kv_select", &kv_select);

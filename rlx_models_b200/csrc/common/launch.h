@@ -369,6 +369,7 @@ struct GdnDecodeArgs {
   int conv_dim, key_dim, value_dim;
   int64_t num_slots;
   float eps;
+  int kda;  // 1: per-channel decay (a: Hv*D logits, dt_bias [Hv*D]) and a sigmoid output gate
 };
 void gdn_decode_launch(const GdnDecodeArgs& a, cudaStream_t st);
 

@@ -18,6 +18,14 @@
 //
 // Reference behaviour: transformers qwen3_5 Qwen3_5GatedDeltaNet (recurrent
 // path) and the family in crates/rlx-qwen35.
+//
+// The KDA instantiation (Kimi Delta Attention: Kimi-Linear, Ling 3) differs in
+// two places: the log decay is per key channel, g_i = -exp(A_log) *
+// softplus(a_i + dt_bias_i) with a the Hv*D logits at the end of the row, so
+// the state update scales row i of S by exp(g_i); and the output gate is
+// sigmoid(z) instead of silu(z). Key and value heads are the same heads.
+// Reference behaviour: crates/rlx-models-core/src/standard_decoder.rs
+// build_kimi_kda (lines 11527-11680).
 #include <cuda_bf16.h>
 
 #include <cstdint>
@@ -68,9 +76,9 @@ __device__ __forceinline__ float conv_step(const GdnDecodeArgs& a, const __nv_bf
   return rbf(silu(acc));  // the conv output is a bf16 activation
 }
 
-template <int D>
+template <int D, bool KDA>
 __global__ void __launch_bounds__(D) gdn_decode_kernel(GdnDecodeArgs a) {
-  __shared__ float qs[D], ks[D];
+  __shared__ float qs[D], ks[D], gs[KDA ? D : 1];
   __shared__ float red[D / 32];
   pdl_wait();
   pdl_trigger();
@@ -96,10 +104,19 @@ __global__ void __launch_bounds__(D) gdn_decode_kernel(GdnDecodeArgs a) {
   ks[t] = k * kn;
   const float zb = bf(row[a.conv_dim + hv * D + t]);
   const float bb = bf(row[a.conv_dim + a.value_dim + hv]);
-  const float ab = bf(row[a.conv_dim + a.value_dim + a.Hv + hv]);
-  const float xa = ab + a.dt_bias[hv];
-  const float softplus = xa > 20.f ? xa : log1pf(__expf(xa));
-  const float decay = __expf(-__expf(a.A_log[hv]) * softplus);
+  float decay;
+  if constexpr (KDA) {  // per key channel: this thread computes channel t's decay for the whole CTA
+    const float ab = bf(row[a.conv_dim + a.value_dim + a.Hv + hv * D + t]);
+    const float xa = ab + a.dt_bias[hv * D + t];
+    const float softplus = xa > 20.f ? xa : log1pf(__expf(xa));
+    gs[t] = __expf(-__expf(a.A_log[hv]) * softplus);
+    decay = 1.f;
+  } else {
+    const float ab = bf(row[a.conv_dim + a.value_dim + a.Hv + hv]);
+    const float xa = ab + a.dt_bias[hv];
+    const float softplus = xa > 20.f ? xa : log1pf(__expf(xa));
+    decay = __expf(-__expf(a.A_log[hv]) * softplus);
+  }
   const float beta = 1.f / (1.f + __expf(-bb));
   __syncthreads();
 
@@ -108,7 +125,7 @@ __global__ void __launch_bounds__(D) gdn_decode_kernel(GdnDecodeArgs a) {
   float kv = 0.f;
 #pragma unroll
   for (int i = 0; i < D; ++i) {
-    s[i] = S[(int64_t)i * D] * decay;
+    s[i] = S[(int64_t)i * D] * (KDA ? gs[i] : decay);
     kv += s[i] * ks[i];
   }
   const float u = beta * (v - kv);
@@ -121,7 +138,8 @@ __global__ void __launch_bounds__(D) gdn_decode_kernel(GdnDecodeArgs a) {
   }
   o = rbf(o);
   const float inv = rsqrtf(block_sum<D>(o * o, red) / (float)D + a.eps);
-  *out = __float2bfloat16(rbf(o * inv) * a.norm_w[t] * silu(zb));
+  const float gate = KDA ? 1.f / (1.f + __expf(-zb)) : silu(zb);
+  *out = __float2bfloat16(rbf(o * inv) * a.norm_w[t] * gate);
 }
 
 }  // namespace gdn
@@ -131,8 +149,11 @@ void gdn_decode_launch(const GdnDecodeArgs& a, cudaStream_t st) {
   if (a.K < 2 || a.K > gdn::kMaxK) throw std::runtime_error("b200.gdn_decode: conv kernel 2..8");
   if (a.Hv % a.Hk != 0) throw std::runtime_error("b200.gdn_decode: value heads must be a multiple of key heads");
   dim3 grid(a.B, a.Hv);
-  if (a.D == 128) launch_pdl(gdn::gdn_decode_kernel<128>, grid, dim3(128), 0, st, a);
-  else if (a.D == 64) launch_pdl(gdn::gdn_decode_kernel<64>, grid, dim3(64), 0, st, a);
+  if (a.kda && a.Hk != a.Hv) throw std::runtime_error("b200.kda_decode: key heads == value heads");
+  if (a.D == 128 && a.kda) launch_pdl(gdn::gdn_decode_kernel<128, true>, grid, dim3(128), 0, st, a);
+  else if (a.D == 64 && a.kda) launch_pdl(gdn::gdn_decode_kernel<64, true>, grid, dim3(64), 0, st, a);
+  else if (a.D == 128) launch_pdl(gdn::gdn_decode_kernel<128, false>, grid, dim3(128), 0, st, a);
+  else if (a.D == 64) launch_pdl(gdn::gdn_decode_kernel<64, false>, grid, dim3(64), 0, st, a);
   else throw std::runtime_error("b200.gdn_decode: head dims 64 or 128 (key == value)");
 }
 
