@@ -790,6 +790,9 @@ def load_vlm(model: str, *, device: str | torch.device = "cuda", engine_config: 
         vlm = Lfm2VlModel(Lfm2VlConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
     elif raw.get("model_type") == "llava":
         vlm = LlavaVLM(LlavaConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
+    elif raw.get("model_type") == "mistral3":  # Pixtral tower at native image sizes
+        from .models.pixtral import Mistral3Config, Mistral3VLM
+        vlm = Mistral3VLM(Mistral3Config.from_dict(raw), WeightMap.from_dir(path), device=device)
     else:
         raise NotImplementedError(f"vision-language model_type {raw.get('model_type')!r}")
     tok = None
