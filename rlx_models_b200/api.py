@@ -735,7 +735,10 @@ class AudioLLM:
         self.tokenizer = tokenizer
 
     def features(self, audio) -> torch.Tensor:
-        """16 kHz PCM -> log-mel windows of 30 s [n, n_mels, 3000]."""
+        """16 kHz PCM -> log-mel windows of 30 s [n, n_mels, 3000] (Voxtral); the
+        24 kHz waveform itself for models whose encoders take raw audio (VibeVoice-ASR)."""
+        if getattr(self.model, "takes_waveform", False):
+            return torch.as_tensor(audio, dtype=torch.float32).reshape(1, -1)
         from .models.whisper import CHUNK_SECONDS, SAMPLE_RATE, log_mel
         a = torch.as_tensor(audio, dtype=torch.float32).flatten()
         n = SAMPLE_RATE * CHUNK_SECONDS
@@ -764,9 +767,13 @@ def load_audio_llm(model: str, *, device: str | torch.device = "cuda",
         raise FileNotFoundError(f"no local checkpoint for {model!r}")
     with open(os.path.join(path, "config.json")) as f:
         raw = json.load(f)
-    if raw.get("model_type") != "voxtral":
+    if raw.get("model_type") == "vibevoice_asr":
+        from .models.vibevoice import VibeVoiceAsr, VibeVoiceAsrConfig
+        m = VibeVoiceAsr(VibeVoiceAsrConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
+    elif raw.get("model_type") != "voxtral":
         raise NotImplementedError(f"audio LLM model_type {raw.get('model_type')!r}")
-    m = VoxtralModel(VoxtralConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
+    else:
+        m = VoxtralModel(VoxtralConfig.from_dict(raw), WeightMap.from_dir(path), device=device)
     tok = None
     try:
         from .tokenizer import load_tokenizer
