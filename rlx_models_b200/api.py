@@ -257,6 +257,9 @@ def load_transcriber(model: str, *, device: str | torch.device = "cuda", languag
         from .models.wav2vec2 import Wav2Vec2Config, Wav2Vec2CTC, Wav2Vec2Transcriber
         return Wav2Vec2Transcriber(Wav2Vec2CTC(Wav2Vec2Config.from_dict(raw), WeightMap.from_dir(path), device=device),
                                    tok, normalize=raw.get("do_normalize", True))
+    if raw.get("model_type") == "wav2vec2-bert":
+        from .models.w2v_bert import W2vBertConfig, W2vBertCTC, W2vBertTranscriber
+        return W2vBertTranscriber(W2vBertCTC(W2vBertConfig.from_dict(raw), WeightMap.from_dir(path), device=device), tok)
     if raw.get("model_type") == "parakeet_ctc":
         from .models.parakeet import ParakeetConfig, ParakeetCTC, ParakeetTranscriber
         return ParakeetTranscriber(ParakeetCTC(ParakeetConfig.from_dict(raw), WeightMap.from_dir(path), device=device),

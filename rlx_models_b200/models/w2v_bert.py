@@ -58,6 +58,38 @@ class W2vBertConfig:
         return c
 
 
+def _kaldi_mel_bank(n_mels: int, n_fft: int, sr: int, f_min: float = 20.0) -> torch.Tensor:
+    """[n_fft // 2 + 1, n_mels] triangles laid out evenly on Kaldi's mel scale
+    1127 ln(1 + f / 700) and evaluated there (no area normalisation)."""
+    mel = lambda f: 1127.0 * torch.log1p(torch.as_tensor(f, dtype=torch.float64) / 700.0)  # noqa: E731
+    edges = torch.linspace(float(mel(f_min)), float(mel(sr / 2)), n_mels + 2, dtype=torch.float64)
+    m = mel(torch.linspace(0, sr / 2, n_fft // 2 + 1, dtype=torch.float64))[:, None]
+    lo, c, hi = edges[None, :-2], edges[None, 1:-1], edges[None, 2:]
+    return torch.clamp(torch.minimum((m - lo) / (c - lo), (hi - m) / (hi - c)), min=0.0)
+
+
+def fbank_features(audio, sample_rate: int = 16000, n_mels: int = 80, stride: int = 2) -> torch.Tensor:
+    """The w2v-BERT / SeamlessM4T input features of one clip: Kaldi-style log mel
+    filterbank (16-bit scale, 25 ms Povey windows every 10 ms, DC offset removed,
+    pre-emphasis 0.97, 512-point power spectrum, 80 Kaldi-mel triangles from
+    20 Hz, log with a floor of 2^-23), normalised per mel bin (mean, unbiased
+    variance + 1e-7), and ``stride`` consecutive frames stacked per row ->
+    [frames // stride, n_mels * stride] fp32."""
+    x = torch.as_tensor(audio, dtype=torch.float64).flatten() * 2.0 ** 15
+    flen, hop, nfft = 400, 160, 512
+    n = 1 + (x.numel() - flen) // hop
+    fr = x.unfold(0, flen, hop)[:n].clone()
+    fr -= fr.mean(-1, keepdim=True)
+    fr[:, 1:] -= 0.97 * fr[:, :-1].clone()
+    fr[:, 0] *= 1 - 0.97
+    win = torch.hann_window(flen, periodic=False, dtype=torch.float64).pow(0.85)
+    spec = torch.fft.rfft(fr * win, n=nfft).abs().pow(2)
+    feats = torch.log(torch.clamp(spec @ _kaldi_mel_bank(n_mels, nfft, sample_rate), min=1.192092955078125e-07))
+    feats = (feats - feats.mean(0, keepdim=True)) / torch.sqrt(feats.var(0, unbiased=True, keepdim=True) + 1e-7)
+    T = feats.shape[0] - feats.shape[0] % stride
+    return feats[:T].reshape(T // stride, n_mels * stride).float()
+
+
 def _act(name, x):
     if name in ("swish", "silu"):
         return F.silu(x)
@@ -166,3 +198,21 @@ class W2vBertCTC:
                 out.append(t)
             prev = t
         return out
+
+
+class W2vBertTranscriber:
+    """``transcribe(audio, sample_rate)``: mono 16 kHz, filterbank features,
+    greedy CTC, tokenizer decode (token ids when there is no tokenizer)."""
+
+    def __init__(self, model: W2vBertCTC, tokenizer=None):
+        self.model, self.tokenizer = model, tokenizer
+
+    def transcribe(self, audio, sample_rate: int = 16000):
+        a = torch.as_tensor(audio, dtype=torch.float32)
+        if a.dim() > 1:
+            a = a.mean(-1)
+        if sample_rate != 16000:
+            a = F.interpolate(a[None, None], scale_factor=16000 / sample_rate, mode="linear",
+                              align_corners=False)[0, 0]
+        ids = self.model.transcribe_ids(fbank_features(a))
+        return self.tokenizer.decode(ids) if self.tokenizer is not None else ids

@@ -39,3 +39,28 @@ def test_w2v_bert_ctc_matches_transformers(pos):
     best = out.logits[0].argmax(-1).tolist()
     ref = [t for i, t in enumerate(best) if t != 0 and (i == 0 or t != best[i - 1])]
     assert ids == ref
+
+
+def test_fbank_features_match_seamless_extractor():
+    import numpy as np
+    import transformers as T
+    from rlx_models_b200.models.w2v_bert import fbank_features
+    fe = T.SeamlessM4TFeatureExtractor()
+    a = (0.1 * torch.randn(16000 + 1234, generator=torch.Generator().manual_seed(4))).numpy().astype(np.float32)
+    ref = torch.from_numpy(fe(a, sampling_rate=16000, return_tensors="np")["input_features"][0])
+    got = fbank_features(a)
+    assert got.shape == ref.shape, (got.shape, ref.shape)
+    assert (got - ref).abs().max() < 2e-3, (got - ref).abs().max()
+
+
+def test_transcriber_runs_end_to_end():
+    from rlx_models_b200.models.w2v_bert import W2vBertConfig, W2vBertCTC, W2vBertTranscriber
+    import transformers as T
+    hcfg = T.Wav2Vec2BertConfig(hidden_size=32, num_hidden_layers=1, num_attention_heads=4, intermediate_size=48,
+                                feature_projection_input_dim=160, conv_depthwise_kernel_size=5, vocab_size=24,
+                                pad_token_id=0, add_adapter=False)
+    m = _rand(T.Wav2Vec2BertForCTC(hcfg))
+    sd = {k: v.detach() for k, v in m.state_dict().items()}
+    tr = W2vBertTranscriber(W2vBertCTC(W2vBertConfig.from_dict(hcfg.to_dict()), sd))
+    ids = tr.transcribe(0.1 * torch.randn(8000, generator=torch.Generator().manual_seed(5)), sample_rate=8000)
+    assert isinstance(ids, list) and all(0 < t < 24 for t in ids)
